@@ -1,0 +1,369 @@
+"""Headline benchmark: training tokens/s of the Qwen3-0.6B-shaped dense DDP config.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+For N > 1 the driver launches one rank per GPU with torch.distributed.run.
+Config: 28 layers, hidden 1024, 16 q / 8 kv heads,
+head_dim 128, SwiGLU 3072, QK-norm, RoPE 1e6, vocab 151936, tied embeddings,
+bf16 compute with fp32 master weights and AdamW state, seq 4096, micro-batch 8
+per GPU (weak scaling: global batch 8*N), fused linear-CE chunk 4096, AdamW
+(0.9, 0.95) wd 0.1, clip 1.0, WSD schedule. Data: synthetic Zipf(1.1) token ids
+with EOS every U[512, 4096] tokens; random-init weights.
+
+``value``: device-timed (CUDA events on the launching stream, barrier +
+synchronize on both sides, max over ranks) tokens/s of the full training step
+(forward, backward, grad all-reduce, clip, AdamW, zero_grad, scheduler) with the
+step's batch already resident on the device. ``e2e``: the same step through
+the public ``Trainer.train_step`` API, including the pinned host-to-device copy
+of every step's batch and a device-to-host read of the loss. Activations are
+gigabytes per step, far larger than the 126 MB L2, so no flush is needed.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+METRIC = "train tokens/sec, 8×B200 device-timed max-over-ranks, 1/2/4/8 GPU vs ref NCCL"
+MODEL_CFG = {"num_layers": 28, "num_heads": 16, "num_kv_heads": 8, "emb_dim": 1024,
+             "head_dim": 128, "vocab_size": 151936, "ffn_dim": 3072}
+MICRO, SEQ = 8, 4096
+BASELINE_VALUE = None  # BASELINE.json "published" is empty: no number to divide by
+
+
+def train_config(n_gpus: int, reducer: str = "nccl") -> dict:
+    return {
+        "model": {"name": "qwen3_dense", "config": dict(MODEL_CFG)},
+        "mesh": {"dp": n_gpus},
+        "parallelism": "ddp",
+        "ddp": {"bucket_mb": 25, "reducer": reducer},
+        "optimizer": {"name": "adamw",
+                      "config": {"lr": 3e-4, "weight_decay": 0.1, "betas": [0.9, 0.95], "fused": True},
+                      "max_norm": 1.0,
+                      "scheduler": {"type": "wsd", "warmup_ratio": 0.001, "decay_ratio": 0.1,
+                                    "total_steps": 1000}},
+        "objective": {"name": "AR", "config": {"ignore_index": -100, "fused_linear_ce": True,
+                                               "ce_chunk_size": 4096}},
+        "data": {"synthetic": {"kind": "zipf", "s": 1.1, "min_doc": 512, "max_doc": 4096},
+                 "global_batch_size": MICRO * n_gpus, "micro_batch_size": MICRO, "seq_len": SEQ,
+                 "seed": 42},
+        "checkpointing": {"save_steps": 10**9, "resume": None},
+        "seed": 0,
+        "run_name": "bench",
+    }
+
+
+# ------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi sampling (every 200 ms) of this rank's GPU during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def gather_clocks(c: dict, device) -> dict:
+    if not (dist.is_initialized() and dist.get_world_size() > 1):
+        return c
+    objs = [None] * dist.get_world_size()
+    dist.all_gather_object(objs, c)
+    sms = [o["sm_mhz"] for o in objs if o and o.get("sm_mhz")]
+    reasons = sorted({r for o in objs if o for r in o.get("reasons", [])})
+    return {"sm_mhz": statistics.median(sms) if sms else None,
+            "sm_max_mhz": max((o["sm_max_mhz"] or 0) for o in objs if o) or None,
+            "reasons": reasons, "per_rank_sm_mhz": sms}
+
+
+# ------------------------------------------------------------------------ timing
+def timed_loop(step_fn, steps: int, warmup: int, device) -> float:
+    """ms per step: CUDA events on the current stream, barrier+sync both sides, max over ranks."""
+    for _ in range(warmup):
+        step_fn()
+    torch.cuda.synchronize()
+    if dist.is_initialized():
+        dist.barrier()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        step_fn()
+    end.record()
+    torch.cuda.synchronize()
+    if dist.is_initialized():
+        dist.barrier()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / steps
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+class ResidentBatches:
+    """Serves one device-resident batch forever (the kernel-only timing input)."""
+
+    def __init__(self, batch):
+        self.batch = batch
+
+    def __next__(self):
+        return self.batch
+
+    def loader_state_dict(self):
+        return {}
+
+
+# --------------------------------------------------------------------- our arm
+def run_ours(args, rank, local_rank, world, device) -> dict:
+    from pluggy_b200.ops import _ext
+    from pluggy_b200.train.trainer import Trainer
+    from pluggy_b200.utils.launch_count import count_launches
+
+    reducer = os.environ.get("PLG_DDP_REDUCER", "nccl")
+    trainer = Trainer(train_config(world, reducer), rank=rank, local_rank=local_rank,
+                      world_size=world, benchmark=True)
+    # kernel-only arm: the batch is already on the device
+    batch = next(trainer.prefetcher)
+    real_prefetcher = trainer.prefetcher
+    trainer.prefetcher = ResidentBatches(batch)
+
+    def step():
+        trainer._train_step()
+
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        ms = timed_loop(step, args.steps, args.warmup, device)
+    _ext.check_status(device)
+    with count_launches() as cnt:
+        step()
+    torch.cuda.synchronize()
+    launches = cnt.count * args.steps
+
+    # end-to-end arm through the public Trainer.train_step (H2D of every batch + loss read)
+    trainer.prefetcher = real_prefetcher
+    h2d = MICRO * SEQ * 8  # int64 ids; labels are the same host tensor (copied once)
+    d2h = 4
+
+    def e2e_step():
+        metrics, _ = trainer.train_step()
+        metrics["loss"].item()
+
+    e2e_ms = timed_loop(e2e_step, max(1, args.steps // 2), 1, device)
+    _ext.check_status(device)
+    tokens = MICRO * SEQ * world
+    return {
+        "value": tokens / (ms / 1e3), "ms_per_step": ms, "clocks": clk.summary(),
+        "gpu_launches": launches,
+        "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "api": "pluggy_b200.train.trainer.Trainer.train_step"},
+        "peak_mem_gib": torch.cuda.max_memory_allocated() / 2**30,
+    }
+
+
+# --------------------------------------------------------------- reference arm
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def run_reference(args, rank, local_rank, world, device) -> dict:
+    """The unmodified reference package (baseline/_ref) through its own Trainer.train_step."""
+    import types
+
+    if not os.path.isdir(os.path.join(REF_DIR, "pluggy")):
+        return {"unavailable": "reference not installed in baseline/_ref"}
+    sys.path.insert(0, REF_DIR)
+    for name in list(sys.modules):
+        if name == "pluggy" or name.startswith("pluggy."):
+            del sys.modules[name]
+    # the reference's model registry imports two modules missing from its tree
+    for mod, cls in (("pluggy.models.grokathon_model.grokathon_model", "GrokathonModel"),
+                     ("pluggy.models.hybrid_test.hybrid_test", "HybridTest")):
+        parent = mod.rsplit(".", 1)[0]
+        sys.modules.setdefault(parent, types.ModuleType(parent))
+        m = types.ModuleType(mod)
+        setattr(m, cls, type(cls, (), {}))
+        sys.modules[mod] = m
+    import pluggy.train.trainer as ref_trainer_mod
+    from pluggy.core.mesh import Mesh
+    from pluggy.dataloader.prefetcher import CUDAPrefetcher
+    from pluggy.models.builder import build_model
+    from pluggy.objectives.builder import build_objective
+    from pluggy.optimizer.builder import build_optimizer, build_scheduler
+    from pluggy.parallelism.data_parallel import DDP
+
+    from pluggy_b200.dataloader.synthetic import SyntheticBatches, SyntheticZipfRows
+
+    cfg = train_config(world)
+    cfg["model"]["config"].pop("ffn_dim")
+    cfg["model"]["config"]["ffn_dim"] = MODEL_CFG["ffn_dim"]
+    T = ref_trainer_mod.Trainer
+    tr = object.__new__(T)  # the reference __init__ needs a network tokenizer and dataset
+    tr.config, tr.rank, tr.world_size, tr.benchmark = cfg, rank, world, True
+    tr.device = device
+    tr.mesh = Mesh(cfg["mesh"])
+    tr.dp_size = tr.mesh.size("dp")
+    torch.manual_seed(0)
+    tr.model = build_model("qwen3_dense", cfg["model"]["config"])
+    tr.model.to(device)
+    tr.model.init_weights()
+    tr._parallelize(tr.model)
+    tr._compile(tr.model)
+    torch.manual_seed(1 + tr.mesh.coordinate("dp"))
+    tr.objective = build_objective("AR", cfg["objective"]["config"])
+    tr.optimizer = build_optimizer(tr.model, "adamw", cfg["optimizer"]["config"])
+    tr.scheduler = build_scheduler(tr.optimizer, cfg["optimizer"]["scheduler"])
+    tr.max_norm = 1.0
+    tr.global_batch_size = cfg["data"]["global_batch_size"]
+    tr.micro_batch_size = MICRO
+    tr.microbatches_per_step = 1
+    tr.wandb_run = None
+    src = SyntheticZipfRows(vocab_size=MODEL_CFG["vocab_size"], seq_len=SEQ, seed=42,
+                            dp_rank=tr.mesh.coordinate("dp"))
+    tr.prefetcher = CUDAPrefetcher(SyntheticBatches(src, MICRO, pin=True), device)
+    assert isinstance(tr.dp, DDP)
+    batch = next(tr.prefetcher)
+    real = tr.prefetcher
+    tr.prefetcher = ResidentBatches(batch)
+    raw_step = T.train_step.__wrapped__ if hasattr(T.train_step, "__wrapped__") else None
+
+    def step():
+        if raw_step is not None:
+            raw_step(tr)
+        else:
+            tr.train_step()
+
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        ms = timed_loop(step, args.steps, args.warmup, device)
+    tr.prefetcher = real
+
+    def e2e_step():
+        metrics, _ = tr.train_step()
+        metrics["loss"].item()
+
+    e2e_ms = timed_loop(e2e_step, max(1, args.steps // 2), 1, device)
+    tokens = MICRO * SEQ * world
+    return {"value": tokens / (ms / 1e3), "ms_per_step": ms, "clocks": clk.summary(),
+            "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": MICRO * SEQ * 8 * 2, "d2h_bytes_per_step": 4,
+                    "api": "pluggy.train.trainer.Trainer.train_step"},
+            "peak_mem_gib": torch.cuda.max_memory_allocated() / 2**30}
+
+
+# ------------------------------------------------------------------------ main
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    args = p.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torch.distributed.run")
+    if not torch.cuda.is_available():
+        line = {"metric": METRIC, "impl": args.impl, "unavailable": "no CUDA device"}
+        print(json.dumps(line))
+        return
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29512")
+    os.environ.setdefault("RANK", "0")
+    os.environ.setdefault("WORLD_SIZE", "1")
+    dist.init_process_group("nccl", timeout=timedelta(minutes=5), device_id=device)
+    try:
+        if args.impl == "reference":
+            res = run_reference(args, rank, local_rank, world, device)
+        else:
+            res = run_ours(args, rank, local_rank, world, device)
+        clocks = gather_clocks(res.get("clocks", {}), device) if "clocks" in res else None
+        if rank == 0:
+            if "unavailable" in res:
+                print(json.dumps({"metric": METRIC, "impl": args.impl, "unavailable": res["unavailable"]}))
+                return
+            line = {
+                "metric": METRIC, "value": res["value"], "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
+                "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": (res["value"] / BASELINE_VALUE) if BASELINE_VALUE else None,
+                "dtype": "bf16", "data": "synthetic (Zipf(1.1) ids, EOS every U[512,4096]; random init)",
+                "config": {"model": "qwen3-0.6B-shaped (28L, d1024, 16q/8kv x128, ffn 3072, V151936, tied)",
+                           "global_batch": MICRO * world, "seq_len": SEQ, "parallelism": f"dp{world}",
+                           "micro_batch_per_gpu": MICRO, "l2": "inputs larger than L2 (GBs of activations)"},
+                "clocks": clocks, "e2e": res.get("e2e"),
+                "peak_mem_gib": res.get("peak_mem_gib"),
+            }
+            if args.impl == "reference":
+                line["impl"] = "reference"
+            else:
+                line["gpu_launches"] = res.get("gpu_launches")
+            print(json.dumps(line))
+    finally:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,339 @@
+// torch bindings for the pluggy_b200 sm_100a kernels (module pluggy_b200._C).
+//
+// Thin adapters: validate dtypes/devices/contiguity, pass raw pointers and the
+// current CUDA stream to the launchers in ops.h. No computation happens here.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "ops.h"
+
+namespace {
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check_cuda(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+}
+
+bool is_f32(const at::Tensor& t) { return t.scalar_type() == at::kFloat; }
+bool is_bf16(const at::Tensor& t) { return t.scalar_type() == at::kBFloat16; }
+
+int* status_ptr(const c10::optional<at::Tensor>& s) {
+  if (!s.has_value()) return nullptr;
+  TORCH_CHECK(s->scalar_type() == at::kInt, "status must be int32");
+  return s->data_ptr<int>();
+}
+
+// C = alpha * op(A) op(B)^T (+ beta * D).
+// a: [M,K] (a_mn_major=false) or [K,M] (true); b: [N,K] or [K,N]; c: [M,N]
+void gemm(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool b_mn_major, at::Tensor& c,
+          const c10::optional<at::Tensor>& d, double alpha, double beta, int64_t splits, int64_t bn,
+          const c10::optional<at::Tensor>& status) {
+  check_cuda(a, "a");
+  check_cuda(b, "b");
+  check_cuda(c, "c");
+  TORCH_CHECK(is_bf16(a) && is_bf16(b), "gemm operands must be bf16");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && c.dim() == 2, "gemm takes 2-D tensors");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && c.stride(1) == 1, "gemm needs unit inner stride");
+  TORCH_CHECK(is_bf16(c) || is_f32(c), "gemm output must be bf16 or fp32");
+  const c10::cuda::CUDAGuard guard(a.device());
+  plg::GemmProblem p;
+  p.M = static_cast<int>(a_mn_major ? a.size(1) : a.size(0));
+  p.K = static_cast<int>(a_mn_major ? a.size(0) : a.size(1));
+  p.N = static_cast<int>(b_mn_major ? b.size(1) : b.size(0));
+  const int kb = static_cast<int>(b_mn_major ? b.size(0) : b.size(1));
+  TORCH_CHECK(kb == p.K, "gemm: K mismatch (", p.K, " vs ", kb, ")");
+  TORCH_CHECK(c.size(0) == p.M && c.size(1) == p.N, "gemm: C must be [M, N]");
+  p.A = a.data_ptr();
+  p.lda = a.stride(0);
+  p.a_mn_major = a_mn_major;
+  p.B = b.data_ptr();
+  p.ldb = b.stride(0);
+  p.b_mn_major = b_mn_major;
+  p.C = c.data_ptr();
+  p.ldc = c.stride(0);
+  p.c_fp32 = is_f32(c);
+  if (d.has_value() && beta != 0.0) {
+    check_cuda(*d, "d");
+    TORCH_CHECK(d->dim() == 2 && d->size(0) == p.M && d->size(1) == p.N && d->stride(1) == 1,
+                "gemm: D must be [M, N] with unit inner stride");
+    TORCH_CHECK(is_bf16(*d) || is_f32(*d), "gemm: D must be bf16 or fp32");
+    p.D = d->data_ptr();
+    p.ldd = d->stride(0);
+    p.d_fp32 = is_f32(*d);
+  }
+  p.alpha = static_cast<float>(alpha);
+  p.beta = static_cast<float>(beta);
+  p.splits = static_cast<int>(splits);
+  p.allow_split = splits != 1;
+  p.bn = static_cast<int>(bn);
+  p.status = status_ptr(status);
+  plg::gemm_bf16(p, cur_stream());
+}
+
+void rmsnorm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& w, at::Tensor& y,
+                 const c10::optional<at::Tensor>& rstd, double eps) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.is_contiguous() && y.is_contiguous(), "rmsnorm tensors must be contiguous");
+  const int D = static_cast<int>(x.size(-1));
+  const long long rows = x.numel() / D;
+  const float* wp = nullptr;
+  if (w.has_value()) {
+    TORCH_CHECK(is_f32(*w) && w->numel() == D, "rmsnorm weight must be fp32 [D]");
+    wp = w->data_ptr<float>();
+  }
+  float* rp = rstd.has_value() ? rstd->data_ptr<float>() : nullptr;
+  const c10::cuda::CUDAGuard guard(x.device());
+  plg::rmsnorm_fwd(x.data_ptr(), is_f32(x), wp, y.data_ptr(), is_f32(y), rp, rows, D,
+                   static_cast<float>(eps), cur_stream());
+}
+
+void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const c10::optional<at::Tensor>& w,
+                 const at::Tensor& rstd, const c10::optional<at::Tensor>& dres,
+                 const c10::optional<at::Tensor>& dx_f32, const c10::optional<at::Tensor>& dx_bf16,
+                 const c10::optional<at::Tensor>& dw_partial) {
+  check_cuda(dy, "dy");
+  TORCH_CHECK(dy.is_contiguous() && x.is_contiguous(), "rmsnorm_bwd tensors must be contiguous");
+  const int D = static_cast<int>(x.size(-1));
+  const long long rows = x.numel() / D;
+  const float* wp = w.has_value() ? w->data_ptr<float>() : nullptr;
+  const float* rp = dres.has_value() ? dres->data_ptr<float>() : nullptr;
+  float* dxf = dx_f32.has_value() ? dx_f32->data_ptr<float>() : nullptr;
+  void* dxb = dx_bf16.has_value() ? dx_bf16->data_ptr() : nullptr;
+  float* dwp = dw_partial.has_value() ? dw_partial->data_ptr<float>() : nullptr;
+  const int blocks = dw_partial.has_value() ? static_cast<int>(dw_partial->size(0)) : 592;
+  const c10::cuda::CUDAGuard guard(x.device());
+  plg::rmsnorm_bwd(dy.data_ptr(), is_f32(dy), x.data_ptr(), is_f32(x), wp,
+                   rstd.data_ptr<float>(), rp, dxf, dxb, dwp, blocks, rows, D, cur_stream());
+}
+
+plg::QkRopeArgs qk_args(const at::Tensor& qkv, at::Tensor& q, at::Tensor& k, at::Tensor& rstd,
+                        const c10::optional<at::Tensor>& wq, const c10::optional<at::Tensor>& wk,
+                        const at::Tensor& inv_freq, const c10::optional<at::Tensor>& positions,
+                        int64_t S, int64_t Hq, int64_t Hk, int64_t d, int64_t rot_dim, double eps,
+                        int64_t k_offset) {
+  plg::QkRopeArgs a{};
+  a.qkv = qkv.data_ptr();
+  a.ld_qkv = qkv.stride(0);
+  a.q = q.data_ptr();
+  a.k = k.data_ptr();
+  a.rstd = rstd.data_ptr<float>();
+  a.wq = wq.has_value() ? wq->data_ptr<float>() : nullptr;
+  a.wk = wk.has_value() ? wk->data_ptr<float>() : nullptr;
+  a.norm_q = wq.has_value();
+  a.norm_k = wk.has_value();
+  a.inv_freq = inv_freq.data_ptr<float>();
+  a.positions = positions.has_value() ? positions->data_ptr<int32_t>() : nullptr;
+  a.T = qkv.size(0);
+  a.S = static_cast<int>(S);
+  a.Hq = static_cast<int>(Hq);
+  a.Hk = static_cast<int>(Hk);
+  a.d = static_cast<int>(d);
+  a.rot_dim = static_cast<int>(rot_dim);
+  a.eps = static_cast<float>(eps);
+  a.k_offset = static_cast<int>(k_offset);
+  return a;
+}
+
+void qk_norm_rope_fwd(const at::Tensor& qkv, at::Tensor& q, at::Tensor& k, at::Tensor& rstd,
+                      const c10::optional<at::Tensor>& wq, const c10::optional<at::Tensor>& wk,
+                      const at::Tensor& inv_freq, const c10::optional<at::Tensor>& positions,
+                      int64_t S, int64_t Hq, int64_t Hk, int64_t d, int64_t rot_dim, double eps,
+                      int64_t k_offset) {
+  check_cuda(qkv, "qkv");
+  TORCH_CHECK(is_bf16(qkv) && qkv.dim() == 2 && qkv.stride(1) == 1, "qkv must be bf16 [T, W]");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  auto a = qk_args(qkv, q, k, rstd, wq, wk, inv_freq, positions, S, Hq, Hk, d, rot_dim, eps, k_offset);
+  plg::qk_norm_rope_fwd(a, cur_stream());
+}
+
+void qk_norm_rope_bwd(const at::Tensor& qkv, at::Tensor& rstd, const c10::optional<at::Tensor>& wq,
+                      const c10::optional<at::Tensor>& wk, const at::Tensor& inv_freq,
+                      const c10::optional<at::Tensor>& positions, int64_t S, int64_t Hq, int64_t Hk,
+                      int64_t d, int64_t rot_dim, double eps, int64_t k_offset,
+                      const at::Tensor& dq, const at::Tensor& dk, at::Tensor& dqkv,
+                      const c10::optional<at::Tensor>& dwq_partial,
+                      const c10::optional<at::Tensor>& dwk_partial, int64_t blocks) {
+  check_cuda(qkv, "qkv");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  at::Tensor q_dummy = dq, k_dummy = dk;
+  auto a = qk_args(qkv, q_dummy, k_dummy, rstd, wq, wk, inv_freq, positions, S, Hq, Hk, d, rot_dim,
+                   eps, k_offset);
+  plg::qk_norm_rope_bwd(a, dq.data_ptr(), dk.data_ptr(), dqkv.data_ptr(), dqkv.stride(0),
+                        dwq_partial.has_value() ? dwq_partial->data_ptr<float>() : nullptr,
+                        dwk_partial.has_value() ? dwk_partial->data_ptr<float>() : nullptr,
+                        static_cast<int>(blocks), cur_stream());
+}
+
+void glu_fwd(const at::Tensor& gu, at::Tensor& out, int64_t kind) {
+  check_cuda(gu, "gu");
+  TORCH_CHECK(is_bf16(gu) && gu.stride(-1) == 1, "glu input must be bf16");
+  const int F = static_cast<int>(out.size(-1));
+  const long long rows = out.numel() / F;
+  const c10::cuda::CUDAGuard guard(gu.device());
+  plg::glu_fwd(gu.data_ptr(), gu.stride(-2), out.data_ptr(), rows, F, static_cast<int>(kind),
+               cur_stream());
+}
+
+void glu_bwd(const at::Tensor& gu, const at::Tensor& dout, at::Tensor& dgu, int64_t kind) {
+  check_cuda(gu, "gu");
+  TORCH_CHECK(dout.is_contiguous() && dgu.stride(-2) == gu.stride(-2), "glu_bwd layout");
+  const int F = static_cast<int>(dout.size(-1));
+  const long long rows = dout.numel() / F;
+  const c10::cuda::CUDAGuard guard(gu.device());
+  plg::glu_bwd(gu.data_ptr(), gu.stride(-2), dout.data_ptr(), dgu.data_ptr(), rows, F,
+               static_cast<int>(kind), cur_stream());
+}
+
+void cast_f32_bf16(const at::Tensor& x, at::Tensor& y) {
+  check_cuda(x, "x");
+  TORCH_CHECK(is_f32(x) && is_bf16(y) && x.is_contiguous() && y.is_contiguous() &&
+                  x.numel() == y.numel(),
+              "cast_f32_bf16 layout");
+  const c10::cuda::CUDAGuard guard(x.device());
+  plg::cast_f32_bf16(x.data_ptr<float>(), y.data_ptr(), x.numel(), cur_stream());
+}
+
+void embedding_fwd(const at::Tensor& ids, const at::Tensor& w, at::Tensor& out, double scale) {
+  check_cuda(ids, "ids");
+  TORCH_CHECK(ids.scalar_type() == at::kLong && is_f32(w) && is_f32(out), "embedding dtypes");
+  TORCH_CHECK(ids.is_contiguous() && w.is_contiguous() && out.is_contiguous(), "embedding layout");
+  const c10::cuda::CUDAGuard guard(ids.device());
+  plg::embedding_fwd(ids.data_ptr<int64_t>(), w.data_ptr<float>(), out.data_ptr<float>(),
+                     ids.numel(), static_cast<int>(w.size(1)), static_cast<float>(scale),
+                     cur_stream());
+}
+
+void embedding_bwd(const at::Tensor& ids, const at::Tensor& dout, at::Tensor& dw, double scale) {
+  check_cuda(ids, "ids");
+  TORCH_CHECK(dout.is_contiguous() && dw.is_contiguous() && is_f32(dout) && is_f32(dw),
+              "embedding_bwd layout");
+  const c10::cuda::CUDAGuard guard(ids.device());
+  plg::embedding_bwd(ids.data_ptr<int64_t>(), dout.data_ptr<float>(), dw.data_ptr<float>(),
+                     ids.numel(), static_cast<int>(dw.size(1)), static_cast<float>(scale),
+                     cur_stream());
+}
+
+void softcap(const at::Tensor& x, at::Tensor& y, double cap) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.is_contiguous() && y.is_contiguous() && x.scalar_type() == y.scalar_type(),
+              "softcap layout");
+  TORCH_CHECK(is_bf16(x) || is_f32(x), "softcap dtype");
+  const c10::cuda::CUDAGuard guard(x.device());
+  plg::softcap_fwd(x.data_ptr(), y.data_ptr(), x.numel(), static_cast<float>(cap), is_bf16(x),
+                   cur_stream());
+}
+
+void ce_rows(at::Tensor& logits, const at::Tensor& labels, int64_t ignore_index, double grad_scale,
+             double softcap, const c10::optional<at::Tensor>& lse, at::Tensor& loss_sum,
+             const c10::optional<at::Tensor>& n_valid) {
+  check_cuda(logits, "logits");
+  TORCH_CHECK(is_bf16(logits) && logits.dim() == 2 && logits.stride(1) == 1, "ce logits layout");
+  TORCH_CHECK(labels.scalar_type() == at::kLong && labels.is_contiguous(), "ce labels");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  plg::ce_rows(logits.data_ptr(), logits.stride(0), labels.data_ptr<int64_t>(), logits.size(0),
+               static_cast<int>(logits.size(1)), static_cast<int>(ignore_index),
+               static_cast<float>(grad_scale), static_cast<float>(softcap),
+               lse.has_value() ? lse->data_ptr<float>() : nullptr, loss_sum.data_ptr<float>(),
+               n_valid.has_value() ? n_valid->data_ptr<int>() : nullptr, cur_stream());
+}
+
+void multi_sumsq(const at::Tensor& table, int64_t ntensors, int64_t total_chunks, at::Tensor& out) {
+  const c10::cuda::CUDAGuard guard(out.device());
+  plg::multi_sumsq(table.data_ptr<int64_t>(), static_cast<int>(ntensors), total_chunks,
+                   out.data_ptr<float>(), cur_stream());
+}
+
+void multi_scale(const at::Tensor& table, int64_t ntensors, int64_t total_chunks,
+                 const at::Tensor& coef) {
+  const c10::cuda::CUDAGuard guard(coef.device());
+  plg::multi_scale(table.data_ptr<int64_t>(), static_cast<int>(ntensors), total_chunks,
+                   coef.data_ptr<float>(), cur_stream());
+}
+
+void adamw_multi(const at::Tensor& table, int64_t ntensors, int64_t total_chunks, double lr,
+                 double beta1, double beta2, double eps, double wd, double bc1, double bc2,
+                 const c10::optional<at::Tensor>& grad_scale) {
+  const c10::cuda::CUDAGuard guard(table.device());
+  plg::adamw_multi(table.data_ptr<int64_t>(), static_cast<int>(ntensors), total_chunks,
+                   static_cast<float>(lr), static_cast<float>(beta1), static_cast<float>(beta2),
+                   static_cast<float>(eps), static_cast<float>(wd), static_cast<float>(bc1),
+                   static_cast<float>(bc2),
+                   grad_scale.has_value() ? grad_scale->data_ptr<float>() : nullptr, cur_stream());
+}
+
+plg::AttnArgs attn_args(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                        at::Tensor& o, at::Tensor& lse, double scale, bool causal, int64_t window,
+                        const c10::optional<at::Tensor>& status) {
+  // q: [B, S, Hq, d], k/v: [B, S, Hk, d] with unit inner stride and head stride d
+  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "attention takes [B, S, H, d]");
+  TORCH_CHECK(is_bf16(q) && is_bf16(k) && is_bf16(v) && is_bf16(o), "attention is bf16");
+  for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&q, &k, &v, &o}) {
+    TORCH_CHECK(t->stride(3) == 1 && t->stride(2) == t->size(3), "attention: heads must be packed");
+    TORCH_CHECK(t->stride(0) == t->stride(1) * t->size(1), "attention: batch stride = S * row");
+  }
+  plg::AttnArgs a{};
+  a.q = q.data_ptr(); a.k = k.data_ptr(); a.v = v.data_ptr(); a.o = o.data_ptr();
+  a.q_row = q.stride(1); a.k_row = k.stride(1); a.v_row = v.stride(1); a.o_row = o.stride(1);
+  a.lse = lse.data_ptr<float>();
+  a.B = static_cast<int>(q.size(0)); a.S = static_cast<int>(q.size(1));
+  a.Hq = static_cast<int>(q.size(2)); a.Hk = static_cast<int>(k.size(2));
+  a.d = static_cast<int>(q.size(3));
+  a.scale = static_cast<float>(scale);
+  a.causal = causal ? 1 : 0;
+  a.window = static_cast<int>(window);
+  a.status = status_ptr(status);
+  return a;
+}
+
+void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o,
+              at::Tensor& lse, double scale, bool causal, int64_t window,
+              const c10::optional<at::Tensor>& status) {
+  check_cuda(q, "q");
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto a = attn_args(q, k, v, o, lse, scale, causal, window, status);
+  plg::attn_fwd(a, cur_stream());
+}
+
+void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o,
+              at::Tensor& lse, const at::Tensor& dout, at::Tensor& dq, at::Tensor& dk,
+              at::Tensor& dv, at::Tensor& dq_acc, at::Tensor& delta, double scale, bool causal,
+              int64_t window, const c10::optional<at::Tensor>& status) {
+  check_cuda(q, "q");
+  const c10::cuda::CUDAGuard guard(q.device());
+  plg::AttnBwdArgs b{};
+  b.f = attn_args(q, k, v, o, lse, scale, causal, window, status);
+  TORCH_CHECK(dout.stride(3) == 1 && dq.stride(3) == 1 && dk.stride(3) == 1 && dv.stride(3) == 1,
+              "attention grads need unit inner stride");
+  b.dout = dout.data_ptr(); b.do_row = dout.stride(1);
+  b.dq = dq.data_ptr(); b.dk = dk.data_ptr(); b.dv = dv.data_ptr();
+  b.dq_row = dq.stride(1); b.dk_row = dk.stride(1); b.dv_row = dv.stride(1);
+  TORCH_CHECK(is_f32(dq_acc) && dq_acc.is_contiguous() && is_f32(delta), "attention workspaces");
+  b.dq_acc = dq_acc.data_ptr<float>();
+  b.delta = delta.data_ptr<float>();
+  plg::attn_bwd(b, cur_stream());
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "pluggy_b200 sm_100a kernels";
+  m.def("gemm", &gemm);
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd);
+  m.def("qk_norm_rope_bwd", &qk_norm_rope_bwd);
+  m.def("glu_fwd", &glu_fwd);
+  m.def("glu_bwd", &glu_bwd);
+  m.def("cast_f32_bf16", &cast_f32_bf16);
+  m.def("embedding_fwd", &embedding_fwd);
+  m.def("embedding_bwd", &embedding_bwd);
+  m.def("softcap", &softcap);
+  m.def("ce_rows", &ce_rows);
+  m.def("multi_sumsq", &multi_sumsq);
+  m.def("multi_scale", &multi_scale);
+  m.def("adamw_multi", &adamw_multi);
+  m.def("attn_fwd", &attn_fwd);
+  m.def("attn_bwd", &attn_bwd);
+}

@@ -1,0 +1,493 @@
+// Persistent bf16 GEMM on the sm_100a 5th-generation tensor cores.
+//
+//   C[M,N] = alpha * sum_k A(m,k) * B(n,k)  (+ beta * D[M,N])
+//
+// A is K-major ([M,K] row-major) or M-major ([K,M] row-major); B likewise
+// ([N,K] or [K,N]). These three combinations cover a linear layer:
+//   forward  y  = x  W^T : A K-major (x [T,K]),  B K-major (W [N,K])
+//   dgrad    dx = dy W   : A K-major (dy [T,N]), B N-major (W [N,K] read as [K=N,N=K])
+//   wgrad    dW = dy^T x : A M-major (dy [T,N]), B N-major (x [T,K])
+// Replaces the reference's cuBLAS calls behind nn.Linear under autocast
+// (pluggy/models/qwen3/qwen3.py:94-97,207-215; pluggy/loss/fused_linear_ce.py:31-58).
+//
+// Structure (one CTA per SM, grid-stride over output tiles):
+//   warp 0      TMA producer: per k-block, one elected thread waits for a free
+//               smem stage and issues the A and B tile loads (128-byte swizzle,
+//               no multicast) onto the stage's mbarrier.
+//   warp 1      allocates TMEM (2 accumulators x BN fp32 columns), then one
+//               thread issues tcgen05.mma 128xBNx16 per 16-wide k step and
+//               commits each stage back to the producer and each finished tile
+//               to the epilogue.
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes
+//               32*(w%4)..+31 = tile rows), optional alpha/beta*D, convert,
+//               store; split-K partial sums are added with vector fp32 atomics.
+// The epilogue of tile i overlaps the main loop of tile i+1 (double-buffered
+// accumulator). Every wait is bounded (common.cuh).
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <stdexcept>
+#include <string>
+
+#include "common.cuh"
+#include "ops.h"
+
+namespace plg {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
+constexpr int kThreads = 192;
+
+struct Args {
+  int M, N, K;
+  void* C;
+  long long ldc;
+  const void* D;
+  long long ldd;
+  float alpha, beta;
+  int c_fp32, d_fp32;
+  int splits;        // >1: fp32 atomic accumulation into C
+  int m_tiles, n_tiles, k_blocks;
+  int raster_m;      // 1: m-tiles vary fastest
+  int* status;
+};
+
+template <int BN>
+struct Cfg {
+  static constexpr int kStages = (BN == 256) ? 4 : 6;
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BN;  // 256 or 512: a power of two
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                Args args) {
+  using C_ = Cfg<BN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment for the 128-byte swizzle atoms
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* tiles = smem;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C_::kStages * C_::kStageBytes);
+  uint64_t* full_bar = bar;                       // [kStages]
+  uint64_t* empty_bar = bar + C_::kStages;        // [kStages]
+  uint64_t* accf_bar = bar + 2 * C_::kStages;     // [2]
+  uint64_t* acce_bar = bar + 2 * C_::kStages + 2; // [2]
+  uint64_t* done_bar = bar + 2 * C_::kStages + 4;  // [1]
+  uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(bar + 2 * C_::kStages + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_smem + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C_::kStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf_bar[b], 1);
+      mbar_init(&acce_bar[b], 4);  // one arrival per epilogue warp
+    }
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_base_smem, C_::kTmemCols);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_smem;
+
+  const int total_tiles = args.m_tiles * args.n_tiles;
+  const int total_work = total_tiles * args.splits;
+  const int kb_per_split = (args.k_blocks + args.splits - 1) / args.splits;
+
+  auto decode = [&](int w, int& mt, int& nt, int& kb0, int& kb1) {
+    int tile = w / args.splits;
+    int sp = w - tile * args.splits;
+    if (args.raster_m) {
+      mt = tile % args.m_tiles;
+      nt = tile / args.m_tiles;
+    } else {
+      nt = tile % args.n_tiles;
+      mt = tile / args.n_tiles;
+    }
+    kb0 = sp * kb_per_split;
+    kb1 = min(args.k_blocks, kb0 + kb_per_split);
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      uint32_t issued_mask = 0, parity_mask = 0;  // per stage: issued, and the phase parity
+      for (int w = blockIdx.x; w < total_work && ok; w += gridDim.x) {
+        int mt, nt, kb0, kb1;
+        decode(w, mt, nt, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, abort_flag)) {
+            record_status(args.status, kTimeoutSmemEmpty);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          uint8_t* sA = tiles + stage * C_::kStageBytes;
+          uint8_t* sB = sA + C_::kABytes;
+          mbar_arrive_expect_tx(&full_bar[stage], C_::kStageBytes);
+          const int k0 = kb * BK;
+          if (A_MN) {
+            // [K, M] row-major: boxes of 64 m x 64 k, one per 64-wide m chunk
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j)
+              tma_load_2d(sA + j * (BK * 128), &tmA, &full_bar[stage], mt * BM + j * 64, k0);
+          } else {
+            tma_load_2d(sA, &tmA, &full_bar[stage], k0, mt * BM);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sB + j * (BK * 128), &tmB, &full_bar[stage], nt * BN + j * 64, k0);
+          } else {
+            tma_load_2d(sB, &tmB, &full_bar[stage], k0, nt * BN);
+          }
+          issued_mask |= 1u << stage;
+          parity_mask = (parity_mask & ~(1u << stage)) | (phase << stage);
+          if (++stage == C_::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // unwind: wait (bounded) until every load this thread issued has landed
+        // so no bulk copy is still writing into smem when the CTA exits.
+        for (int s = 0; s < C_::kStages; ++s) {
+          if ((issued_mask >> s) & 1u) {
+            if (!mbar_wait_bounded(&full_bar[s], (parity_mask >> s) & 1u, nullptr))
+              record_status(args.status, kTimeoutDrain);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------------- MMA
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16_f32(BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < total_work && ok; w += gridDim.x, ++local) {
+        int mt, nt, kb0, kb1;
+        decode(w, mt, nt, kb0, kb1);
+        const int buf = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait_bounded(&acce_bar[buf], acc_phase ^ 1u, abort_flag)) {
+          record_status(args.status, kTimeoutAccEmpty);
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait_bounded(&full_bar[stage], phase, abort_flag)) {
+            record_status(args.status, kTimeoutTmaFull);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sA = smem_u32(tiles + stage * C_::kStageBytes);
+          const uint32_t sB = sA + C_::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            uint64_t da, db;
+            if (A_MN) da = make_smem_desc(sA + kk * 2048, BK * 128, 1024, kLayoutSW128);
+            else da = make_smem_desc(sA + kk * 32, 16, 1024, kLayoutSW128);
+            if (B_MN) db = make_smem_desc(sB + kk * 2048, BK * 128, 1024, kLayoutSW128);
+            else db = make_smem_desc(sB + kk * 32, 16, 1024, kLayoutSW128);
+            tc_mma_ss(d_tmem, da, db, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty_bar[stage]);  // frees the smem stage when these MMAs finish
+          if (++stage == C_::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&accf_bar[buf]);  // accumulator ready for the epilogue
+      }
+      // every issued MMA must finish before TMEM is released
+      tc_commit(done_bar);
+      if (!mbar_wait_bounded(done_bar, 0, nullptr)) record_status(args.status, kTimeoutDrain);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row_in_tile = q * 32 + lane;
+    int local = 0;
+    for (int w = blockIdx.x; w < total_work; w += gridDim.x, ++local) {
+      int mt, nt, kb0, kb1;
+      decode(w, mt, nt, kb0, kb1);
+      const int buf = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait_bounded(&accf_bar[buf], acc_phase, abort_flag)) {
+        record_status(args.status, kTimeoutAccFull);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const long long row = (long long)mt * BM + row_in_tile;
+      const bool row_ok = row < args.M;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        __syncwarp();
+        tmem_ld_32x32b_x32(t_row + c * 32, r);
+        tmem_ld_wait();
+        const int col0 = nt * BN + c * 32;
+        if (!row_ok || col0 >= args.N) continue;
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * args.alpha;
+        const bool full = col0 + 32 <= args.N;
+        if (args.D != nullptr && args.beta != 0.f && kb0 == 0) {
+          if (args.d_fp32) {
+            const float* dp = reinterpret_cast<const float*>(args.D) + row * args.ldd + col0;
+            if (full) {
+#pragma unroll
+              for (int i = 0; i < 32; i += 4) {
+                float4 d4 = *reinterpret_cast<const float4*>(dp + i);
+                v[i] += args.beta * d4.x; v[i + 1] += args.beta * d4.y;
+                v[i + 2] += args.beta * d4.z; v[i + 3] += args.beta * d4.w;
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (col0 + i < args.N) v[i] += args.beta * dp[i];
+            }
+          } else {
+            const __nv_bfloat16* dp =
+                reinterpret_cast<const __nv_bfloat16*>(args.D) + row * args.ldd + col0;
+            if (full) {
+#pragma unroll
+              for (int i = 0; i < 32; i += 8) {
+                uint4 u = *reinterpret_cast<const uint4*>(dp + i);
+                float2 f0 = unpack_bf16x2(u.x), f1 = unpack_bf16x2(u.y);
+                float2 f2 = unpack_bf16x2(u.z), f3 = unpack_bf16x2(u.w);
+                v[i] += args.beta * f0.x; v[i + 1] += args.beta * f0.y;
+                v[i + 2] += args.beta * f1.x; v[i + 3] += args.beta * f1.y;
+                v[i + 4] += args.beta * f2.x; v[i + 5] += args.beta * f2.y;
+                v[i + 6] += args.beta * f3.x; v[i + 7] += args.beta * f3.y;
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (col0 + i < args.N) v[i] += args.beta * __bfloat162float(dp[i]);
+            }
+          }
+        }
+        if (args.c_fp32) {
+          float* cp = reinterpret_cast<float*>(args.C) + row * args.ldc + col0;
+          if (args.splits > 1) {
+            if (full) {
+#pragma unroll
+              for (int i = 0; i < 32; i += 4)
+                atomicAdd(reinterpret_cast<float4*>(cp + i),
+                          make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (col0 + i < args.N) atomicAdd(cp + i, v[i]);
+            }
+          } else if (full) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              *reinterpret_cast<float4*>(cp + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (col0 + i < args.N) cp[i] = v[i];
+          }
+        } else {
+          __nv_bfloat16* cp = reinterpret_cast<__nv_bfloat16*>(args.C) + row * args.ldc + col0;
+          if (full) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              uint4 u;
+              u.x = pack_bf16x2(v[i], v[i + 1]);
+              u.y = pack_bf16x2(v[i + 2], v[i + 3]);
+              u.z = pack_bf16x2(v[i + 4], v[i + 5]);
+              u.w = pack_bf16x2(v[i + 6], v[i + 7]);
+              *reinterpret_cast<uint4*>(cp + i) = u;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (col0 + i < args.N) cp[i] = __float2bfloat16(v[i]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce_bar[buf]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C_::kTmemCols);
+  }
+}
+
+// --------------------------------------------------------------------------
+// host side
+// --------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    PLG_CUDA_CHECK(cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000,
+                                                    cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || p == nullptr)
+      throw std::runtime_error("cuTensorMapEncodeTiled entry point not found");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix with leading dim `ld`
+// (elements); box = box_cols x box_rows; 128-byte swizzle.
+static CUtensorMap make_map_2d(const void* base, long long rows, long long cols, long long ld,
+                               int box_cols, int box_rows) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base),
+                               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw std::runtime_error("cuTensorMapEncodeTiled failed with code " + std::to_string(r));
+  return m;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev;
+    PLG_CUDA_CHECK(cudaGetDevice(&dev));
+    PLG_CUDA_CHECK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+  }
+  return n;
+}
+
+template <int BN, bool A_MN, bool B_MN>
+static void launch(const GemmProblem& p, cudaStream_t stream) {
+  using C_ = Cfg<BN>;
+  // A map
+  CUtensorMap ta = A_MN ? make_map_2d(p.A, p.K, p.M, p.lda, 64, BK)
+                        : make_map_2d(p.A, p.M, p.K, p.lda, BK, BM);
+  CUtensorMap tb = B_MN ? make_map_2d(p.B, p.K, p.N, p.ldb, 64, BK)
+                        : make_map_2d(p.B, p.N, p.K, p.ldb, BK, BN);
+  Args a;
+  a.M = p.M; a.N = p.N; a.K = p.K;
+  a.C = p.C; a.ldc = p.ldc; a.D = p.D; a.ldd = p.ldd;
+  a.alpha = p.alpha; a.beta = p.beta;
+  a.c_fp32 = p.c_fp32; a.d_fp32 = p.d_fp32;
+  a.m_tiles = (p.M + BM - 1) / BM;
+  a.n_tiles = (p.N + BN - 1) / BN;
+  a.k_blocks = (p.K + BK - 1) / BK;
+  a.status = p.status;
+  const int sms = num_sms();
+  const int tiles = a.m_tiles * a.n_tiles;
+  int splits = p.splits;
+  if (splits <= 0) {
+    splits = 1;
+    if (p.c_fp32 && p.allow_split) {
+      // split K until there is about one wave of work, keeping >= 8 k-blocks per split
+      while (tiles * splits * 2 <= sms * 2 && a.k_blocks / (splits * 2) >= 8) splits *= 2;
+      if (tiles * splits < sms && a.k_blocks / (splits * 2) >= 8) splits *= 2;
+    }
+  }
+  if (splits > a.k_blocks) splits = a.k_blocks;
+  if (splits < 1) splits = 1;
+  // every split must own at least one k-block
+  while (splits > 1 && (splits - 1) * ((a.k_blocks + splits - 1) / splits) >= a.k_blocks) --splits;
+  a.splits = splits;
+  if (splits > 1) {
+    // partial sums are atomically added into C: C must start from its base value
+    const bool accumulate_into_c = (p.D == p.C && p.beta == 1.f);
+    if (accumulate_into_c) {
+      a.D = nullptr;
+    } else {
+      if (p.D == p.C) throw std::invalid_argument("gemm: split-K with D == C needs beta == 1");
+      PLG_CUDA_CHECK(cudaMemsetAsync(p.C, 0, sizeof(float) * (size_t)p.ldc * (size_t)(p.M - 1) +
+                                                 sizeof(float) * (size_t)p.N, stream));
+    }
+  }
+  // raster: walk along the operand that is re-read from L2 less
+  a.raster_m = (static_cast<long long>(p.N) > static_cast<long long>(p.M)) ? 1 : 0;
+  const int work = tiles * splits;
+  const int grid = work < sms ? work : sms;
+  auto kern = gemm_kernel<BN, A_MN, B_MN>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    PLG_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        C_::kSmemBytes));
+    attr_set = true;
+  }
+  kern<<<grid, kThreads, C_::kSmemBytes, stream>>>(ta, tb, a);
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace gemm
+
+void gemm_bf16(const GemmProblem& p, cudaStream_t stream) {
+  using namespace gemm;
+  if (p.M <= 0 || p.N <= 0 || p.K <= 0) return;
+  if ((p.lda % 8) || (p.ldb % 8)) throw std::invalid_argument("gemm: lda/ldb must be multiples of 8");
+  if ((reinterpret_cast<uintptr_t>(p.A) | reinterpret_cast<uintptr_t>(p.B)) & 15)
+    throw std::invalid_argument("gemm: A/B must be 16-byte aligned");
+  if (p.ldc % (p.c_fp32 ? 4 : 8)) throw std::invalid_argument("gemm: ldc must keep rows 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(p.C) & 15) throw std::invalid_argument("gemm: C must be 16-byte aligned");
+  if (p.splits > 1 && !p.c_fp32) throw std::invalid_argument("gemm: split-K needs an fp32 output");
+  const bool wide = p.N >= 256 && p.bn != 128;
+#define PLG_GEMM_CASE(BN_, AM, BMJ) \
+  if (p.a_mn_major == AM && p.b_mn_major == BMJ) return launch<BN_, AM, BMJ>(p, stream);
+  if (wide) {
+    PLG_GEMM_CASE(256, false, false)
+    PLG_GEMM_CASE(256, false, true)
+    PLG_GEMM_CASE(256, true, true)
+    PLG_GEMM_CASE(256, true, false)
+  } else {
+    PLG_GEMM_CASE(128, false, false)
+    PLG_GEMM_CASE(128, false, true)
+    PLG_GEMM_CASE(128, true, true)
+    PLG_GEMM_CASE(128, true, false)
+  }
+#undef PLG_GEMM_CASE
+}
+
+}  // namespace plg

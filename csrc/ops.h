@@ -1,0 +1,129 @@
+// Host-side launcher API of the pluggy_b200 sm_100a kernels.
+//
+// The .cu files implement these with raw pointers and a cudaStream_t so they
+// compile without the torch headers; bindings.cpp adapts torch tensors to them.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace plg {
+
+// ---------------------------------------------------------------- GEMM (tcgen05)
+struct GemmProblem {
+  int M = 0, N = 0, K = 0;
+  const void* A = nullptr;  // bf16
+  long long lda = 0;
+  bool a_mn_major = false;  // false: A is [M,K] row-major; true: A is [K,M] row-major
+  const void* B = nullptr;  // bf16
+  long long ldb = 0;
+  bool b_mn_major = false;  // false: B is [N,K] row-major; true: B is [K,N] row-major
+  void* C = nullptr;        // [M, N] row-major, bf16 or fp32
+  long long ldc = 0;
+  bool c_fp32 = false;
+  const void* D = nullptr;  // optional addend [M, N] (may alias C)
+  long long ldd = 0;
+  bool d_fp32 = false;
+  float alpha = 1.f, beta = 0.f;
+  int splits = 0;           // 0: automatic split-K for fp32 outputs (when allow_split)
+  bool allow_split = true;
+  int bn = 0;               // 0 automatic, else 128 or 256
+  int* status = nullptr;    // device status word (bounded waits)
+};
+void gemm_bf16(const GemmProblem& p, cudaStream_t stream);
+
+// ---------------------------------------------------------------- normalisation
+// y = x * rsqrt(mean(x^2) + eps) * w  (rows x D), x fp32 or bf16, w fp32 or null,
+// y bf16 (and/or fp32), rstd fp32 [rows]
+void rmsnorm_fwd(const void* x, bool x_fp32, const float* w, void* y, bool y_fp32, float* rstd,
+                 long long rows, int D, float eps, cudaStream_t stream);
+// dx = (w*dy - y_hat * mean(w*dy*y_hat)) * rstd (+ dres); dw partial sums into dw_partial
+// [blocks, D] (reduced by the caller); dx written as fp32 (dx_f32) and/or bf16 (dx_bf16)
+void rmsnorm_bwd(const void* dy, bool dy_fp32, const void* x, bool x_fp32, const float* w,
+                 const float* rstd, const float* dres, float* dx_f32, void* dx_bf16,
+                 float* dw_partial, int dw_blocks, long long rows, int D, cudaStream_t stream);
+
+// QK-norm + RoPE on a packed projection [T, (Hq + 2*Hk) * d] (q | k | v):
+// per head RMSNorm with weights wq/wk (d), then rotate-half RoPE with the
+// angle pos * inv_freq[i]; writes q [T, Hq, d], k [T, Hk, d] (bf16) and rstd
+// [T, Hq + Hk]. pos = t % S (packed rows) or positions[t] when given.
+// rot_dim <= d: only the first rot_dim channels rotate (partial RoPE).
+struct QkRopeArgs {
+  const void* qkv; long long ld_qkv;
+  void* q; void* k; float* rstd;
+  const float* wq; const float* wk;
+  const float* inv_freq; const int32_t* positions;
+  long long T; int S; int Hq; int Hk; int d; int rot_dim; float eps;
+  int norm_q; int norm_k;  // 0 skips the norm (Llama)
+  int k_offset; int v_offset;  // column offsets (in heads*d units) of k and v within a row
+  int full_width_norm;     // OLMo: q/k normalised over all heads' channels jointly
+};
+void qk_norm_rope_fwd(const QkRopeArgs& a, cudaStream_t stream);
+// backward: dq [T,Hq,d], dk [T,Hk,d] -> dqkv (q and k parts) ; dwq/dwk partials
+void qk_norm_rope_bwd(const QkRopeArgs& a, const void* dq, const void* dk, void* dqkv,
+                      long long ld_dqkv, float* dwq_partial, float* dwk_partial, int dw_blocks,
+                      cudaStream_t stream);
+
+// ---------------------------------------------------------------- elementwise
+// act = silu(g) * u  (kind 0) or gelu_tanh(g) * u (kind 1); gu is [T, 2F] with
+// g = gu[:, :F], u = gu[:, F:] (ld_gu >= 2F)
+void glu_fwd(const void* gu, long long ld_gu, void* out, long long rows, int F, int kind,
+             cudaStream_t stream);
+void glu_bwd(const void* gu, long long ld_gu, const void* dout, void* dgu, long long rows, int F,
+             int kind, cudaStream_t stream);
+void cast_f32_bf16(const float* x, void* y, long long n, cudaStream_t stream);
+void cast_bf16_f32(const void* x, float* y, long long n, cudaStream_t stream);
+void embedding_fwd(const int64_t* ids, const float* w, float* out_f32, long long T, int D,
+                   float scale, cudaStream_t stream);
+// dw[ids[t]] += scale * dout[t]  (fp32 atomics)
+void embedding_bwd(const int64_t* ids, const float* dout, float* dw, long long T, int D,
+                   float scale, cudaStream_t stream);
+// y = cap * tanh(x / cap)
+void softcap_fwd(const void* x, void* y, long long n, float cap, bool bf16, cudaStream_t stream);
+
+// ---------------------------------------------------------------- cross entropy
+// Per row of bf16 logits [rows, V]: lse, loss = lse - logit[label] (0 for
+// ignored rows), and in place: logits <- (softmax - onehot) * grad_scale.
+// loss_sum accumulates sum of row losses (fp32 atomic). softcap > 0 applies
+// cap*tanh(x/cap) first (its derivative folded into the gradient).
+void ce_rows(void* logits, long long ld, const int64_t* labels, long long rows, int V,
+             int ignore_index, float grad_scale, float softcap, float* lse_out, float* loss_sum,
+             int* n_valid, cudaStream_t stream);
+
+// ---------------------------------------------------------------- optimizer
+struct TensorRef { void* p; long long n; };
+// one launch over every tensor: sum of squares (fp32) into out[0]
+void multi_sumsq(const int64_t* table, int ntensors, long long total_chunks, float* out,
+                 cudaStream_t stream);
+void multi_scale(const int64_t* table, int ntensors, long long total_chunks, const float* coef,
+                 cudaStream_t stream);
+// table rows: [param f32*, grad f32*, m f32*, v f32*, shadow bf16* (or 0), numel, chunk_start]
+void adamw_multi(const int64_t* table, int ntensors, long long total_chunks, float lr, float beta1,
+                 float beta2, float eps, float weight_decay, float bc1, float bc2,
+                 const float* grad_scale, cudaStream_t stream);
+constexpr int kOptChunk = 65536;
+
+// ---------------------------------------------------------------- attention
+struct AttnArgs {
+  const void* q; const void* k; const void* v;  // bf16 [B, S, H, d] with row strides
+  long long q_row, k_row, v_row;                 // elements between consecutive tokens
+  void* o; long long o_row;                      // bf16 [B, S, Hq, d]
+  float* lse;                                    // fp32 [B, Hq, S] (natural log)
+  int B, S, Hq, Hk, d;
+  float scale;
+  int causal;
+  int window;                                    // > 0: keys k with q - k < window only
+  int* status;
+};
+void attn_fwd(const AttnArgs& a, cudaStream_t stream);
+struct AttnBwdArgs {
+  AttnArgs f;
+  const void* dout; long long do_row;
+  void* dq; void* dk; void* dv;                  // bf16, same layouts as q, k, v
+  long long dq_row, dk_row, dv_row;
+  float* dq_acc;                                 // fp32 workspace [B, S, Hq, d]
+  float* delta;                                  // fp32 workspace [B, Hq, S]
+};
+void attn_bwd(const AttnBwdArgs& a, cudaStream_t stream);
+
+}  // namespace plg

@@ -1,0 +1,523 @@
+// Memory-bound sm_100a kernels: GLU activations, casts, embedding, softcap,
+// cross-entropy rows, and the multi-tensor optimizer / grad-norm kernels.
+//
+// Parity:
+//   glu          pluggy/kernels/swiglu.py:14-21 (silu(g)*u, gelu_tanh(g)*u)
+//   embedding    nn.Embedding in pluggy/models/qwen3/qwen3.py:318 (+ Gemma's sqrt(d) scale)
+//   softcap      pluggy/kernels/softcap.py:13-33
+//   ce_rows      the per-chunk math of pluggy/loss/fused_linear_ce.py:31-58
+//                (lse, target gather, softmax - onehot masked by ignore_index)
+//   adamw/sumsq  torch.optim.AdamW(fused=True) and pluggy/core/grad_helper.py:8-34
+#include <stdexcept>
+
+#include "common.cuh"
+#include "ops.h"
+
+namespace plg {
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float silu(float x) { return x / (1.f + exp2f(-x * kLog2e)); }
+
+// tanh-approximated GELU and its derivative (Hendrycks & Gimpel 2016, eq. for
+// the tanh form): g(x) = 0.5 x (1 + tanh(k0 (x + k1 x^3))), k0 = sqrt(2/pi), k1 = 0.044715
+__device__ __forceinline__ void gelu_tanh(float x, float& y, float& dy) {
+  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+  const float inner = k0 * (x + k1 * x * x * x);
+  const float t = tanhf(inner);
+  y = 0.5f * x * (1.f + t);
+  dy = 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * k0 * (1.f + 3.f * k1 * x * x);
+}
+
+__global__ void glu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, long long ld,
+                               __nv_bfloat16* __restrict__ out, long long rows, int F, int kind) {
+  const long long n2 = rows * (F / 2);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n2;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / (F / 2);
+    const int c = static_cast<int>(i - r * (F / 2)) * 2;
+    const float2 g = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(gu + r * ld + c));
+    const float2 u = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(gu + r * ld + F + c));
+    float a0, a1;
+    if (kind == 0) {
+      a0 = silu(g.x) * u.x;
+      a1 = silu(g.y) * u.y;
+    } else {
+      float y0, y1, d0, d1;
+      gelu_tanh(g.x, y0, d0);
+      gelu_tanh(g.y, y1, d1);
+      a0 = y0 * u.x;
+      a1 = y1 * u.y;
+    }
+    *reinterpret_cast<uint32_t*>(out + r * F + c) = pack_bf16x2(a0, a1);
+  }
+}
+
+__global__ void glu_bwd_kernel(const __nv_bfloat16* __restrict__ gu, long long ld,
+                               const __nv_bfloat16* __restrict__ dout,
+                               __nv_bfloat16* __restrict__ dgu, long long rows, int F, int kind) {
+  const long long n2 = rows * (F / 2);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n2;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / (F / 2);
+    const int c = static_cast<int>(i - r * (F / 2)) * 2;
+    const float2 g = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(gu + r * ld + c));
+    const float2 u = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(gu + r * ld + F + c));
+    const float2 d = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(dout + r * F + c));
+    float dg0, dg1, du0, du1;
+    if (kind == 0) {
+      const float s0 = 1.f / (1.f + exp2f(-g.x * kLog2e));
+      const float s1 = 1.f / (1.f + exp2f(-g.y * kLog2e));
+      du0 = d.x * g.x * s0;
+      du1 = d.y * g.y * s1;
+      dg0 = d.x * u.x * s0 * (1.f + g.x * (1.f - s0));
+      dg1 = d.y * u.y * s1 * (1.f + g.y * (1.f - s1));
+    } else {
+      float y0, y1, e0, e1;
+      gelu_tanh(g.x, y0, e0);
+      gelu_tanh(g.y, y1, e1);
+      du0 = d.x * y0;
+      du1 = d.y * y1;
+      dg0 = d.x * u.x * e0;
+      dg1 = d.y * u.y * e1;
+    }
+    *reinterpret_cast<uint32_t*>(dgu + r * ld + c) = pack_bf16x2(dg0, dg1);
+    *reinterpret_cast<uint32_t*>(dgu + r * ld + F + c) = pack_bf16x2(du0, du1);
+  }
+}
+
+__global__ void cast_f32_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y,
+                                     long long n) {
+  const long long n4 = n / 4;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
+       i += (long long)gridDim.x * blockDim.x) {
+    float4 v = reinterpret_cast<const float4*>(x)[i];
+    uint2 o;
+    o.x = pack_bf16x2(v.x, v.y);
+    o.y = pack_bf16x2(v.z, v.w);
+    reinterpret_cast<uint2*>(y)[i] = o;
+  }
+  for (long long i = n4 * 4 + blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    y[i] = __float2bfloat16(x[i]);
+}
+
+__global__ void cast_bf16_f32_kernel(const __nv_bfloat16* __restrict__ x, float* __restrict__ y,
+                                     long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    y[i] = __bfloat162float(x[i]);
+}
+
+__global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const float* __restrict__ w,
+                                     float* __restrict__ out, long long T, int D, float scale) {
+  const long long t = blockIdx.x;
+  if (t >= T) return;
+  const float4* src = reinterpret_cast<const float4*>(w + ids[t] * (long long)D);
+  float4* dst = reinterpret_cast<float4*>(out + t * D);
+  for (int i = threadIdx.x; i < D / 4; i += blockDim.x) {
+    float4 v = src[i];
+    v.x *= scale; v.y *= scale; v.z *= scale; v.w *= scale;
+    dst[i] = v;
+  }
+}
+
+__global__ void embedding_bwd_kernel(const int64_t* __restrict__ ids,
+                                     const float* __restrict__ dout, float* __restrict__ dw,
+                                     long long T, int D, float scale) {
+  const long long t = blockIdx.x;
+  if (t >= T) return;
+  float* dst = dw + ids[t] * (long long)D;
+  const float* src = dout + t * D;
+  for (int i = threadIdx.x * 4; i < D; i += blockDim.x * 4) {
+    float4 v = *reinterpret_cast<const float4*>(src + i);
+    atomicAdd(reinterpret_cast<float4*>(dst + i),
+              make_float4(v.x * scale, v.y * scale, v.z * scale, v.w * scale));
+  }
+}
+
+template <typename T>
+__global__ void softcap_kernel(const T* __restrict__ x, T* __restrict__ y, long long n, float cap) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const float v = static_cast<float>(x[i]);
+    y[i] = static_cast<T>(cap * tanhf(v / cap));
+  }
+}
+
+// ------------------------------------------------------------ cross entropy
+// One CTA per row of bf16 logits. Pass 1: online max / sum of exp (8 bf16 per
+// 16-byte load). Pass 2: gradient (softmax - onehot) * scale written in place.
+constexpr int kCeThreads = 512;
+
+__global__ void __launch_bounds__(kCeThreads) ce_rows_kernel(
+    __nv_bfloat16* __restrict__ logits, long long ld, const int64_t* __restrict__ labels, int V,
+    int ignore_index, float grad_scale, float softcap, float* __restrict__ lse_out,
+    float* __restrict__ loss_sum, int* __restrict__ n_valid) {
+  const long long row = blockIdx.x;
+  __nv_bfloat16* x = logits + row * ld;
+  const int64_t lab = labels[row];
+  const bool valid = lab != ignore_index;
+  const bool cap = softcap > 0.f;
+  __shared__ float s_m[kCeThreads / 32], s_s[kCeThreads / 32];
+  float m = -INFINITY, s = 0.f;
+  const int nvec = V / 8;
+  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
+    uint4 u = reinterpret_cast<const uint4*>(x)[i];
+    float f[8];
+    float2 t;
+    t = unpack_bf16x2(u.x); f[0] = t.x; f[1] = t.y;
+    t = unpack_bf16x2(u.y); f[2] = t.x; f[3] = t.y;
+    t = unpack_bf16x2(u.z); f[4] = t.x; f[5] = t.y;
+    t = unpack_bf16x2(u.w); f[6] = t.x; f[7] = t.y;
+    float lm = m;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (cap) f[j] = softcap * tanhf(f[j] / softcap);
+      lm = fmaxf(lm, f[j]);
+    }
+    float acc = s * exp2f((m - lm) * kLog2e);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc += exp2f((f[j] - lm) * kLog2e);
+    m = lm;
+    s = acc;
+  }
+  for (int i = nvec * 8 + threadIdx.x; i < V; i += blockDim.x) {
+    float f = __bfloat162float(x[i]);
+    if (cap) f = softcap * tanhf(f / softcap);
+    const float lm = fmaxf(m, f);
+    s = s * exp2f((m - lm) * kLog2e) + exp2f((f - lm) * kLog2e);
+    m = lm;
+  }
+  // block reduction of (m, s)
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, m, o);
+    const float os = __shfl_xor_sync(0xffffffffu, s, o);
+    const float nm = fmaxf(m, om);
+    s = (m == -INFINITY ? 0.f : s * exp2f((m - nm) * kLog2e)) +
+        (om == -INFINITY ? 0.f : os * exp2f((om - nm) * kLog2e));
+    m = nm;
+  }
+  if (lane == 0) { s_m[warp] = m; s_s[warp] = s; }
+  __syncthreads();
+  if (warp == 0) {
+    m = lane < kCeThreads / 32 ? s_m[lane] : -INFINITY;
+    s = lane < kCeThreads / 32 ? s_s[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float om = __shfl_xor_sync(0xffffffffu, m, o);
+      const float os = __shfl_xor_sync(0xffffffffu, s, o);
+      const float nm = fmaxf(m, om);
+      s = (m == -INFINITY ? 0.f : s * exp2f((m - nm) * kLog2e)) +
+          (om == -INFINITY ? 0.f : os * exp2f((om - nm) * kLog2e));
+      m = nm;
+    }
+    if (lane == 0) { s_m[0] = m; s_s[0] = s; }
+  }
+  __syncthreads();
+  const float lse = s_m[0] + logf(s_s[0]);
+  if (threadIdx.x == 0) {
+    if (lse_out) lse_out[row] = lse;
+    if (valid) {
+      float tgt = __bfloat162float(x[lab]);
+      if (cap) tgt = softcap * tanhf(tgt / softcap);
+      atomicAdd(loss_sum, lse - tgt);
+      if (n_valid) atomicAdd(n_valid, 1);
+    }
+  }
+  __syncthreads();  // the target logit is read before pass 2 overwrites it
+  // pass 2: gradient in place
+  const float gs = valid ? grad_scale : 0.f;
+  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
+    uint4 u = reinterpret_cast<uint4*>(x)[i];
+    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 t = unpack_bf16x2(w[j]);
+      float a = t.x, b = t.y;
+      float ca = 1.f, cb = 1.f;
+      if (cap) {
+        const float ta = tanhf(a / softcap), tb = tanhf(b / softcap);
+        a = softcap * ta; b = softcap * tb;
+        ca = 1.f - ta * ta; cb = 1.f - tb * tb;
+      }
+      float pa = exp2f((a - lse) * kLog2e), pb = exp2f((b - lse) * kLog2e);
+      const int c = i * 8 + j * 2;
+      if (c == lab) pa -= 1.f;
+      if (c + 1 == lab) pb -= 1.f;
+      w[j] = pack_bf16x2(pa * gs * ca, pb * gs * cb);
+    }
+    reinterpret_cast<uint4*>(x)[i] = u;
+  }
+  for (int i = nvec * 8 + threadIdx.x; i < V; i += blockDim.x) {
+    float a = __bfloat162float(x[i]);
+    float ca = 1.f;
+    if (cap) {
+      const float ta = tanhf(a / softcap);
+      a = softcap * ta;
+      ca = 1.f - ta * ta;
+    }
+    float p = exp2f((a - lse) * kLog2e);
+    if (i == lab) p -= 1.f;
+    x[i] = __float2bfloat16(p * gs * ca);
+  }
+}
+
+// ------------------------------------------------------------ multi-tensor
+// table row (int64): [p0, p1, p2, p3, p4, numel, chunk_start]; chunk_start is
+// the global index of the tensor's first kOptChunk-element chunk.
+constexpr int kRow = 7;
+
+__device__ __forceinline__ int find_tensor(const int64_t* table, int ntensors, long long chunk) {
+  int lo = 0, hi = ntensors - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (table[mid * kRow + 6] <= chunk) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+__global__ void multi_sumsq_kernel(const int64_t* __restrict__ table, int ntensors,
+                                   long long total_chunks, float* __restrict__ partial) {
+  __shared__ float s_red[32];
+  for (long long ch = blockIdx.x; ch < total_chunks; ch += gridDim.x) {
+    const int ti = find_tensor(table, ntensors, ch);
+    const float* g = reinterpret_cast<const float*>(table[ti * kRow + 0]);
+    const long long n = table[ti * kRow + 5];
+    const long long off = (ch - table[ti * kRow + 6]) * kOptChunk;
+    const long long end = min(n, off + kOptChunk);
+    float acc = 0.f;
+    if ((reinterpret_cast<uintptr_t>(g + off) & 15) == 0) {
+      const long long n4 = (end - off) / 4;
+      const float4* g4 = reinterpret_cast<const float4*>(g + off);
+      for (long long i = threadIdx.x; i < n4; i += blockDim.x) {
+        float4 v = g4[i];
+        acc += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      }
+      for (long long i = off + n4 * 4 + threadIdx.x; i < end; i += blockDim.x) acc += g[i] * g[i];
+    } else {
+      for (long long i = off + threadIdx.x; i < end; i += blockDim.x) acc += g[i] * g[i];
+    }
+    acc = warp_sum(acc);
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float v = threadIdx.x < (blockDim.x >> 5) ? s_red[threadIdx.x] : 0.f;
+      v = warp_sum(v);
+      if (threadIdx.x == 0) partial[ch] = v;
+    }
+    __syncthreads();
+  }
+}
+
+// deterministic final reduction of the per-chunk partials (one block)
+__global__ void reduce_partials_kernel(const float* __restrict__ partial, long long n,
+                                       float* __restrict__ out) {
+  __shared__ double s_red[32];
+  double acc = 0.0;
+  for (long long i = threadIdx.x; i < n; i += blockDim.x) acc += partial[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    double v = threadIdx.x < (blockDim.x >> 5) ? s_red[threadIdx.x] : 0.0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (threadIdx.x == 0) out[0] = static_cast<float>(v);
+  }
+}
+
+__global__ void multi_scale_kernel(const int64_t* __restrict__ table, int ntensors,
+                                   long long total_chunks, const float* __restrict__ coef) {
+  const float c = *coef;
+  for (long long ch = blockIdx.x; ch < total_chunks; ch += gridDim.x) {
+    const int ti = find_tensor(table, ntensors, ch);
+    float* g = reinterpret_cast<float*>(table[ti * kRow + 0]);
+    const long long n = table[ti * kRow + 5];
+    const long long off = (ch - table[ti * kRow + 6]) * kOptChunk;
+    const long long end = min(n, off + kOptChunk);
+    for (long long i = off + threadIdx.x; i < end; i += blockDim.x) g[i] *= c;
+  }
+}
+
+__global__ void __launch_bounds__(512) adamw_kernel(const int64_t* __restrict__ table,
+                                                    int ntensors, long long total_chunks,
+                                                    float lr, float b1, float b2, float eps,
+                                                    float wd, float bc1, float bc2,
+                                                    const float* __restrict__ gscale) {
+  const float scale = gscale ? *gscale : 1.f;
+  const float step = lr / bc1;
+  const float rbc2 = rsqrtf(bc2);
+  const float decay = 1.f - lr * wd;
+  for (long long ch = blockIdx.x; ch < total_chunks; ch += gridDim.x) {
+    const int ti = find_tensor(table, ntensors, ch);
+    const int64_t* r = table + ti * kRow;
+    float* p = reinterpret_cast<float*>(r[0]);
+    const float* g = reinterpret_cast<const float*>(r[1]);
+    float* m = reinterpret_cast<float*>(r[2]);
+    float* v = reinterpret_cast<float*>(r[3]);
+    __nv_bfloat16* sh = reinterpret_cast<__nv_bfloat16*>(r[4]);
+    const long long n = r[5];
+    const long long off = (ch - r[6]) * kOptChunk;
+    const long long end = min(n, off + kOptChunk);
+    const bool vec = ((reinterpret_cast<uintptr_t>(p + off) | reinterpret_cast<uintptr_t>(g + off) |
+                       reinterpret_cast<uintptr_t>(m + off) | reinterpret_cast<uintptr_t>(v + off)) &
+                      15) == 0 &&
+                     (sh == nullptr || (reinterpret_cast<uintptr_t>(sh + off) & 7) == 0);
+    long long i0 = off;
+    if (vec) {
+      const long long n4 = (end - off) / 4;
+      for (long long i = threadIdx.x; i < n4; i += blockDim.x) {
+        const long long e = off + i * 4;
+        float4 pp = *reinterpret_cast<float4*>(p + e);
+        float4 gg = *reinterpret_cast<const float4*>(g + e);
+        float4 mm = *reinterpret_cast<float4*>(m + e);
+        float4 vv = *reinterpret_cast<float4*>(v + e);
+        float* P = &pp.x; float* G = &gg.x; float* M = &mm.x; float* W = &vv.x;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float gj = G[j] * scale;
+          P[j] *= decay;
+          M[j] += (1.f - b1) * (gj - M[j]);
+          W[j] = b2 * W[j] + (1.f - b2) * gj * gj;
+          P[j] -= step * M[j] / (sqrtf(W[j]) * rbc2 + eps);
+        }
+        *reinterpret_cast<float4*>(p + e) = pp;
+        *reinterpret_cast<float4*>(m + e) = mm;
+        *reinterpret_cast<float4*>(v + e) = vv;
+        if (sh) {
+          uint2 o;
+          o.x = pack_bf16x2(pp.x, pp.y);
+          o.y = pack_bf16x2(pp.z, pp.w);
+          *reinterpret_cast<uint2*>(sh + e) = o;
+        }
+      }
+      i0 = off + n4 * 4;
+    }
+    for (long long e = i0 + threadIdx.x; e < end; e += blockDim.x) {
+      const float gj = g[e] * scale;
+      float pj = p[e] * decay;
+      float mj = m[e] + (1.f - b1) * (gj - m[e]);
+      float vj = b2 * v[e] + (1.f - b2) * gj * gj;
+      pj -= step * mj / (sqrtf(vj) * rbc2 + eps);
+      p[e] = pj; m[e] = mj; v[e] = vj;
+      if (sh) sh[e] = __float2bfloat16(pj);
+    }
+  }
+}
+
+int grid_for(long long work, int per_block) {
+  long long b = (work + per_block - 1) / per_block;
+  if (b > 148 * 16) b = 148 * 16;
+  if (b < 1) b = 1;
+  return static_cast<int>(b);
+}
+
+}  // namespace
+
+void glu_fwd(const void* gu, long long ld_gu, void* out, long long rows, int F, int kind,
+             cudaStream_t st) {
+  if (rows <= 0) return;
+  if (F % 2) throw std::invalid_argument("glu: F must be even");
+  glu_fwd_kernel<<<grid_for(rows * F / 2, 256), 256, 0, st>>>(
+      reinterpret_cast<const __nv_bfloat16*>(gu), ld_gu, reinterpret_cast<__nv_bfloat16*>(out),
+      rows, F, kind);
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+void glu_bwd(const void* gu, long long ld_gu, const void* dout, void* dgu, long long rows, int F,
+             int kind, cudaStream_t st) {
+  if (rows <= 0) return;
+  glu_bwd_kernel<<<grid_for(rows * F / 2, 256), 256, 0, st>>>(
+      reinterpret_cast<const __nv_bfloat16*>(gu), ld_gu,
+      reinterpret_cast<const __nv_bfloat16*>(dout), reinterpret_cast<__nv_bfloat16*>(dgu), rows,
+      F, kind);
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+void cast_f32_bf16(const float* x, void* y, long long n, cudaStream_t st) {
+  if (n <= 0) return;
+  cast_f32_bf16_kernel<<<grid_for(n / 4 + 1, 256), 256, 0, st>>>(
+      x, reinterpret_cast<__nv_bfloat16*>(y), n);
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+void cast_bf16_f32(const void* x, float* y, long long n, cudaStream_t st) {
+  if (n <= 0) return;
+  cast_bf16_f32_kernel<<<grid_for(n, 256), 256, 0, st>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x), y, n);
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+void embedding_fwd(const int64_t* ids, const float* w, float* out, long long T, int D, float scale,
+                   cudaStream_t st) {
+  if (T <= 0) return;
+  if (D % 4) throw std::invalid_argument("embedding: D must be a multiple of 4");
+  embedding_fwd_kernel<<<T, 256, 0, st>>>(ids, w, out, T, D, scale);
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+void embedding_bwd(const int64_t* ids, const float* dout, float* dw, long long T, int D,
+                   float scale, cudaStream_t st) {
+  if (T <= 0) return;
+  embedding_bwd_kernel<<<T, 256, 0, st>>>(ids, dout, dw, T, D, scale);
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+void softcap_fwd(const void* x, void* y, long long n, float cap, bool bf16, cudaStream_t st) {
+  if (n <= 0) return;
+  if (bf16)
+    softcap_kernel<__nv_bfloat16><<<grid_for(n, 256), 256, 0, st>>>(
+        reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<__nv_bfloat16*>(y), n, cap);
+  else
+    softcap_kernel<float><<<grid_for(n, 256), 256, 0, st>>>(
+        reinterpret_cast<const float*>(x), reinterpret_cast<float*>(y), n, cap);
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+void ce_rows(void* logits, long long ld, const int64_t* labels, long long rows, int V,
+             int ignore_index, float grad_scale, float softcap, float* lse_out, float* loss_sum,
+             int* n_valid, cudaStream_t st) {
+  if (rows <= 0) return;
+  if ((ld % 8) || (reinterpret_cast<uintptr_t>(logits) & 15))
+    throw std::invalid_argument("ce_rows: logits rows must be 16-byte aligned");
+  ce_rows_kernel<<<rows, kCeThreads, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(logits), ld, labels,
+                                              V, ignore_index, grad_scale, softcap, lse_out,
+                                              loss_sum, n_valid);
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+void multi_sumsq(const int64_t* table, int ntensors, long long total_chunks, float* out,
+                 cudaStream_t st) {
+  // out: [1 + total_chunks]; out[0] receives the total, out[1:] the partials
+  if (total_chunks <= 0) return;
+  multi_sumsq_kernel<<<grid_for(total_chunks, 1), 512, 0, st>>>(table, ntensors, total_chunks,
+                                                                out + 1);
+  reduce_partials_kernel<<<1, 1024, 0, st>>>(out + 1, total_chunks, out);
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+void multi_scale(const int64_t* table, int ntensors, long long total_chunks, const float* coef,
+                 cudaStream_t st) {
+  if (total_chunks <= 0) return;
+  multi_scale_kernel<<<grid_for(total_chunks, 1), 512, 0, st>>>(table, ntensors, total_chunks,
+                                                                coef);
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+void adamw_multi(const int64_t* table, int ntensors, long long total_chunks, float lr, float beta1,
+                 float beta2, float eps, float weight_decay, float bc1, float bc2,
+                 const float* grad_scale, cudaStream_t st) {
+  if (total_chunks <= 0) return;
+  adamw_kernel<<<grid_for(total_chunks, 1), 512, 0, st>>>(table, ntensors, total_chunks, lr, beta1,
+                                                         beta2, eps, weight_decay, bc1, bc2,
+                                                         grad_scale);
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace plg

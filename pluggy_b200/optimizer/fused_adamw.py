@@ -1,0 +1,109 @@
+"""AdamW whose CUDA step is one sm_100a multi-tensor kernel launch.
+
+Parity: the reference builds ``torch.optim.AdamW(..., fused=True)``
+(``pluggy/optimizer/builder.py:20-46``, config ``optimizer.config.fused``).
+This class IS a ``torch.optim.AdamW`` (same param groups, same ``state_dict``
+keys ``step/exp_avg/exp_avg_sq``), so checkpoints move between the two
+frameworks unchanged. Only ``step()`` differs:
+
+* CUDA params: ``pluggy_b200.ops.optim.adamw_step`` updates every param of a
+  group in ONE launch (a device table of tensor pointers, grid-stride over
+  fixed-size chunks). It optionally multiplies grads by a device-resident clip
+  coefficient (so clipping costs no extra pass and no host sync) and can write a
+  bf16 copy of each updated param into a registered shadow tensor (the bf16
+  weights the GEMMs read), replacing a separate cast pass.
+* CPU params: the exact AdamW math in eager torch (oracle / gloo tests).
+
+Math (decoupled weight decay, PyTorch's formulation):
+``p -= lr*wd*p; m = b1*m + (1-b1)*g; v = b2*v + (1-b2)*g^2;
+p -= lr/bc1 * m / (sqrt(v)/sqrt(bc2) + eps)``.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+
+class FusedAdamW(torch.optim.AdamW):
+    def __init__(self, params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=1e-2,
+                 fused: bool | None = None, foreach: bool | None = None, **kw):
+        betas = tuple(betas)
+        super().__init__(params, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay,
+                         foreach=False, fused=False, **kw)
+        self.use_kernel = True if fused is None else bool(fused)
+        self._grad_scale: torch.Tensor | None = None
+        self._shadows: dict[int, torch.Tensor] = {}
+
+    # ------------------------------------------------------------------ hooks
+    def set_grad_scale(self, coef: torch.Tensor | None) -> None:
+        """Multiply grads by ``coef`` (0-d fp32 device tensor) inside the next step."""
+        self._grad_scale = coef
+
+    def register_bf16_shadow(self, param: torch.Tensor, shadow: torch.Tensor) -> None:
+        """After each step, write ``param`` cast to bf16 into ``shadow`` (same numel)."""
+        assert shadow.numel() == param.numel() and shadow.dtype == torch.bfloat16
+        self._shadows[id(param)] = shadow
+
+    def clear_bf16_shadows(self) -> None:
+        self._shadows.clear()
+
+    # ------------------------------------------------------------------- step
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        scale = self._grad_scale
+        self._grad_scale = None
+        for group in self.param_groups:
+            params = [p for p in group["params"] if p.grad is not None]
+            if not params:
+                continue
+            lr = group["lr"]
+            lr = float(lr) if not torch.is_tensor(lr) else float(lr.item())
+            b1, b2 = group["betas"]
+            wd, eps = group["weight_decay"], group["eps"]
+            # lazily create state in the torch.optim.AdamW layout
+            for p in params:
+                st = self.state[p]
+                if len(st) == 0:
+                    st["step"] = torch.tensor(0.0, dtype=torch.float32)
+                    st["exp_avg"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+                    st["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+            # group params by step count (normally one bucket)
+            by_step: dict[float, list] = {}
+            for p in params:
+                st = self.state[p]
+                st["step"] += 1
+                by_step.setdefault(float(st["step"]), []).append(p)
+            for step, ps in by_step.items():
+                bc1 = 1 - b1 ** step
+                bc2 = 1 - b2 ** step
+                if ps[0].is_cuda and self.use_kernel:
+                    from pluggy_b200.ops import optim as _optim
+
+                    _optim.adamw_step(
+                        ps, [p.grad for p in ps], [self.state[p]["exp_avg"] for p in ps],
+                        [self.state[p]["exp_avg_sq"] for p in ps],
+                        [self._shadows.get(id(p)) for p in ps],
+                        lr=lr, beta1=b1, beta2=b2, eps=eps, weight_decay=wd,
+                        bias_correction1=bc1, bias_correction2=bc2, grad_scale=scale)
+                    # the kernel wrote through raw pointers: tell autograd (and the bf16
+                    # weight caches keyed on the version counter) that params changed
+                    torch.autograd.graph.increment_version(ps)
+                else:
+                    for p in ps:
+                        g = p.grad if scale is None else p.grad * scale
+                        st = self.state[p]
+                        p.mul_(1 - lr * wd)
+                        st["exp_avg"].lerp_(g, 1 - b1)
+                        st["exp_avg_sq"].mul_(b2).addcmul_(g, g, value=1 - b2)
+                        denom = (st["exp_avg_sq"].sqrt() / math.sqrt(bc2)).add_(eps)
+                        p.addcdiv_(st["exp_avg"], denom, value=-lr / bc1)
+                        sh = self._shadows.get(id(p))
+                        if sh is not None:
+                            sh.copy_(p.view_as(sh))
+        return loss

@@ -1,0 +1,130 @@
+"""Data parallel: replicas in lockstep by averaging grads over the ``dp`` axis.
+
+Parity: reference ``pluggy/parallelism/data_parallel.py:69-147``:
+
+* parameters and buffers are broadcast from coordinate 0 at construction;
+* grads are bucketed in reverse ``parameters()`` order (~backward completion
+  order) with a size cap (``bucket_mb``, default 25) and a dtype break; a
+  multi-param bucket owns one flat buffer whose views become ``.grad``, and a
+  param at or above the cap is its own bucket reduced in place;
+* ``register_post_accumulate_grad_hook`` counts each bucket down and launches
+  its average as soon as it is full, overlapping the rest of backward;
+* ``requires_sync = False`` turns the hooks off for no_sync accumulation;
+* ``sync()`` asserts that every bucket launched, then waits.
+
+B200 design: the reduction behind ``_launch`` is pluggable. ``reducer="nccl"``
+is the reference path (``all_reduce(op="avg")`` via NCCL). ``reducer="fused"``
+(CUDA, dp>1) hands each bucket to ``pluggy_b200.comm.fused_ddp.BucketReducer``:
+the bucket is copied into a symmetric (peer-mapped) buffer on a side stream and
+one sm_100a kernel reads every peer's copy over NVLink, sums, scales by 1/N and
+writes the result back into the grad views, accumulating the sum of squares of
+the reduced grads for the clip on the way. Both paths leave exactly the same
+``.grad`` contract for clip and optimizer.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from pluggy_b200.core.collective import MeshLike, all_reduce, broadcast
+
+
+class _Bucket:
+    __slots__ = ("params", "pending", "flat", "views", "index")
+
+    def __init__(self, params: list[nn.Parameter], index: int):
+        self.params = params
+        self.pending = len(params)
+        self.index = index
+        self.flat = None
+        self.views = None
+        if len(params) > 1:
+            numel = sum(p.numel() for p in params)
+            self.flat = torch.empty(numel, dtype=params[0].dtype, device=params[0].device)
+            self.views, off = [], 0
+            for p in params:
+                self.views.append(self.flat[off: off + p.numel()].view_as(p))
+                off += p.numel()
+
+    def grad_tensor(self) -> torch.Tensor:
+        return self.params[0].grad if self.flat is None else self.flat
+
+
+class DDP:
+    def __init__(self, model: nn.Module, mesh: MeshLike, dim: str = "dp", bucket_mb: float = 25,
+                 reducer: str = "nccl"):
+        self.mesh = mesh
+        self.dim = dim
+        self.group_size = mesh.size(dim)
+        self.requires_sync = True
+        self._works: list = []
+        self.reducer_name = reducer
+        self._fused = None
+        if self.group_size == 1:
+            return
+        for t in [*model.parameters(), *model.buffers()]:
+            broadcast(t.detach(), mesh, dim, src=0)
+        params = [p for p in model.parameters() if p.requires_grad]
+        params.reverse()
+        self._buckets = self._build_buckets(params, int(bucket_mb * 1024 * 1024))
+        self._bucket_of = {p: b for b in self._buckets for p in b.params}
+        if reducer == "fused":
+            from pluggy_b200.comm.fused_ddp import BucketReducer
+
+            self._fused = BucketReducer(mesh, dim, self._buckets)
+        elif reducer != "nccl":
+            raise ValueError(f"unknown DDP reducer {reducer!r}: expected 'nccl' or 'fused'")
+        for p in params:
+            p.register_post_accumulate_grad_hook(self._on_grad_ready)
+
+    @staticmethod
+    def _build_buckets(params: list[nn.Parameter], cap: int) -> list[_Bucket]:
+        buckets, run, run_bytes = [], [], 0
+        for p in params:
+            nbytes = p.numel() * p.element_size()
+            if run and (run_bytes + nbytes > cap or p.dtype != run[0].dtype):
+                buckets.append(_Bucket(run, len(buckets)))
+                run, run_bytes = [], 0
+            run.append(p)
+            run_bytes += nbytes
+        if run:
+            buckets.append(_Bucket(run, len(buckets)))
+        return buckets
+
+    @property
+    def buckets(self) -> list[_Bucket]:
+        return getattr(self, "_buckets", [])
+
+    def _on_grad_ready(self, param: nn.Parameter) -> None:
+        if not self.requires_sync:
+            return
+        b = self._bucket_of[param]
+        b.pending -= 1
+        if b.pending == 0:
+            self._launch(b)
+
+    def _launch(self, b: _Bucket) -> None:
+        b.pending = len(b.params)
+        if b.flat is not None:
+            torch._foreach_copy_(b.views, [p.grad for p in b.params])
+            for p, v in zip(b.params, b.views, strict=True):
+                p.grad = v
+        if self._fused is not None:
+            self._works.append(self._fused.launch(b))
+            return
+        _, work = all_reduce(b.grad_tensor(), self.mesh, self.dim, "avg", async_op=True)
+        self._works.append(work)
+
+    def sync(self) -> None:
+        if self.group_size == 1:
+            return
+        assert len(self._works) == len(self._buckets), (
+            f"only {len(self._works)}/{len(self._buckets)} grad buckets launched -- a param got "
+            "no grad this backward, or requires_sync was still False on the last microbatch"
+        )
+        for w in self._works:
+            w.wait()
+        self._works.clear()
+        if self._fused is not None:
+            self._fused.finish()

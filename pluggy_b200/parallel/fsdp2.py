@@ -1,0 +1,258 @@
+"""FSDP2: per-parameter ``Shard(0)`` of params, grads and optimizer state.
+
+Parity: reference ``pluggy/parallelism/fsdp2.py:75-261``:
+
+* units = one per ``model.blocks[i]`` plus a root unit (embedding, head, final
+  norm) that stays gathered after forward because the fused linear-CE reads
+  ``lm_head.weight`` after ``forward`` returns;
+* pre-forward hook gathers the unit, post-forward hook frees the full storage
+  (``resize_(0)``, so a use-after-reshard fails loudly), pre-backward hook
+  re-gathers;
+* the post-accumulate-grad hook reduce-scatters (avg) each full grad into an
+  fp32 shard accumulator every microbatch; once a unit's last grad has
+  arrived its params point back at their shards;
+* ``sync()`` publishes the shard grads as ``p.grad``; the optimizer and the
+  clip (``shard_dims=("dp",)``) see only shards.
+
+B200 differences (same observable contract):
+
+* every shard of a unit lives in ONE flat fp32 buffer and every gather of a
+  unit is one coalesced collective (one NCCL group) instead of a synchronous
+  call per parameter;
+* on CUDA the gathers run on a dedicated comm stream and the NEXT unit is
+  prefetched while the current one computes (forward: i+1, backward: i-1);
+  the compute stream waits on an event only when it needs the weights;
+* grad reduce-scatters are also issued on the comm stream and coalesced per
+  unit once the unit's last grad arrives;
+* ``gather="fused"`` (CUDA, dp>1) replaces NCCL with the peer-memory gather
+  kernel in ``pluggy_b200.comm`` (each CTA pulls peer shards over NVLink).
+"""
+
+from __future__ import annotations
+
+import contextlib
+
+import torch
+import torch._dynamo
+import torch.distributed as dist
+import torch.nn as nn
+
+from pluggy_b200.core.collective import MeshLike, broadcast
+
+
+class _ParamState:
+    def __init__(self, param: nn.Parameter, n: int, coord: int):
+        assert param.shape[0] % n == 0, (
+            f"param dim 0 ({param.shape[0]}) not divisible by the dp size {n} (even shards only)"
+        )
+        self.param = param
+        rows = param.shape[0] // n
+        self.shard_shape = (rows, *param.shape[1:])
+        self.shard_numel = param.numel() // n
+        self.full = torch.empty_like(param.data)
+        self.full_nbytes = self.full.untyped_storage().nbytes()
+        self.full.untyped_storage().resize_(0)
+        self._init_shard = param.data.narrow(0, coord * rows, rows).clone()
+        self.sharded: torch.Tensor | None = None
+        self.grad_shard: torch.Tensor | None = None
+
+    def alloc_full(self) -> None:
+        if self.full.untyped_storage().nbytes() != self.full_nbytes:
+            self.full.untyped_storage().resize_(self.full_nbytes)
+
+    def free_full(self) -> None:
+        self.full.untyped_storage().resize_(0)
+
+
+class _Unit:
+    def __init__(self, name: str, states: list[_ParamState], reshard_after_forward: bool):
+        self.name = name
+        self.params = states
+        self.reshard_after_forward = reshard_after_forward
+        self.n_grads = sum(1 for s in states if s.param.requires_grad)
+        self.pending = self.n_grads
+        numel = sum(s.shard_numel for s in states)
+        dev = states[0].param.device if states else torch.device("cpu")
+        dt = states[0].param.dtype if states else torch.float32
+        self.flat_shard = torch.empty(numel, dtype=dt, device=dev)
+        off = 0
+        for s in states:
+            v = self.flat_shard[off: off + s.shard_numel].view(s.shard_shape)
+            v.copy_(s._init_shard)
+            s._init_shard = None
+            s.sharded = v
+            s.param.data = v
+            off += s.shard_numel
+        self.gathered = False
+        self.gather_event = None
+        self.ready_grads: list[_ParamState] = []
+
+
+class FSDP2:
+    def __init__(self, model: nn.Module, mesh: MeshLike, dim: str = "dp", *, prefetch: bool = True):
+        self.mesh = mesh
+        self.dim = dim
+        self.group_size = mesh.size(dim)
+        self.requires_sync = True  # API parity with DDP; FSDP2 reduces every microbatch
+        if self.group_size == 1:
+            return
+        assert hasattr(model, "blocks"), "fsdp2 units are per transformer block (model.blocks)"
+        for t in [*model.parameters(), *model.buffers()]:
+            broadcast(t.detach(), mesh, dim, src=0)
+        n, coord = self.group_size, mesh.coordinate(dim)
+        block_ids = {id(p) for b in model.blocks for p in b.parameters()}
+        self._units: list[_Unit] = []
+        for i, block in enumerate(model.blocks):
+            u = _Unit(f"block{i}", [_ParamState(p, n, coord) for p in block.parameters()], True)
+            self._units.append(u)
+            self._install(block, u)
+        root = [_ParamState(p, n, coord) for p in model.parameters() if id(p) not in block_ids]
+        self._root = _Unit("root", root, False)
+        self._units.append(self._root)
+        self._install(model, self._root)
+        dev = self._root.flat_shard.device
+        self._cuda = dev.type == "cuda"
+        self._prefetch = prefetch and self._cuda
+        self._comm_stream = torch.cuda.Stream(device=dev) if self._cuda else None
+        self._block_units = self._units[:-1]
+        self._pending_work: list = []
+
+    # --------------------------------------------------------------- plumbing
+    def _install(self, module: nn.Module, unit: _Unit) -> None:
+        module.register_forward_pre_hook(lambda m, a, u=unit: self._pre_forward(u))
+        if unit.reshard_after_forward:
+            module.register_forward_hook(lambda m, a, o, u=unit: self._reshard(u))
+            module.register_full_backward_pre_hook(lambda m, g, u=unit: self._pre_backward(u))
+        for s in unit.params:
+            if s.param.requires_grad:
+                s.param.register_post_accumulate_grad_hook(
+                    lambda p, s=s, u=unit: self._on_grad_ready(s, u))
+
+    def _group(self):
+        return self.mesh.get_group(self.dim)
+
+    def _issue_gather(self, unit: _Unit) -> None:
+        """Launch the coalesced all-gather of ``unit`` (on the comm stream on CUDA)."""
+        if unit.gathered:
+            return
+        for s in unit.params:
+            s.alloc_full()
+        ctx = torch.cuda.stream(self._comm_stream) if self._cuda else contextlib.nullcontext()
+        if self._cuda:
+            self._comm_stream.wait_stream(torch.cuda.current_stream())
+        with ctx:
+            group = self._group()
+            with dist._coalescing_manager(group=group, device=unit.flat_shard.device):
+                for s in unit.params:
+                    dist.all_gather_into_tensor(s.full, s.sharded, group=group)
+            if self._cuda:
+                unit.gather_event = torch.cuda.Event()
+                unit.gather_event.record(self._comm_stream)
+                for s in unit.params:
+                    s.full.record_stream(torch.cuda.current_stream())
+        unit.gathered = True
+
+    def _use(self, unit: _Unit) -> None:
+        if unit.gather_event is not None:
+            torch.cuda.current_stream().wait_event(unit.gather_event)
+            unit.gather_event = None
+        for s in unit.params:
+            s.param.data = s.full
+
+    def _neighbor(self, unit: _Unit, step: int) -> _Unit | None:
+        if unit is self._root:
+            return self._block_units[0] if step > 0 and self._block_units else None
+        i = self._block_units.index(unit) + step
+        return self._block_units[i] if 0 <= i < len(self._block_units) else None
+
+    # ------------------------------------------------------------------ hooks
+    @torch._dynamo.disable
+    def _pre_forward(self, unit: _Unit) -> None:
+        self._issue_gather(unit)
+        self._use(unit)
+        if self._prefetch:
+            nxt = self._neighbor(unit, +1)
+            if nxt is not None:
+                self._issue_gather(nxt)
+
+    @torch._dynamo.disable
+    def _reshard(self, unit: _Unit) -> None:
+        for s in unit.params:
+            s.free_full()
+        unit.gathered = False
+
+    @torch._dynamo.disable
+    def _pre_backward(self, unit: _Unit) -> None:
+        self._issue_gather(unit)
+        self._use(unit)
+        if self._prefetch:
+            prv = self._neighbor(unit, -1)
+            if prv is not None and prv is not self._root:
+                self._issue_gather(prv)
+
+    @torch._dynamo.disable
+    def _on_grad_ready(self, s: _ParamState, unit: _Unit) -> None:
+        unit.ready_grads.append(s)
+        unit.pending -= 1
+        if unit.pending == 0:
+            unit.pending = unit.n_grads
+            self._reduce_unit(unit)
+            for st in unit.params:
+                st.param.data = st.sharded
+                st.free_full()
+            unit.gathered = False
+
+    def _reduce_unit(self, unit: _Unit) -> None:
+        """Average each full grad of ``unit`` into its fp32 shard accumulator."""
+        group = self._group()
+        n = self.group_size
+        nccl = dist.get_backend(group) == "nccl"
+        outs = []
+        grads = [s.param.grad for s in unit.ready_grads]
+        if self._cuda:
+            self._comm_stream.wait_stream(torch.cuda.current_stream())
+        ctx = torch.cuda.stream(self._comm_stream) if self._cuda else contextlib.nullcontext()
+        with ctx:
+            for s, g in zip(unit.ready_grads, grads, strict=True):
+                outs.append(torch.empty(s.shard_shape, dtype=g.dtype, device=g.device))
+            op = dist.ReduceOp.AVG if nccl else dist.ReduceOp.SUM
+            with dist._coalescing_manager(group=group, device=unit.flat_shard.device):
+                for g, o in zip(grads, outs, strict=True):
+                    dist.reduce_scatter_tensor(o, g.contiguous(), op=op, group=group)
+            for s, o in zip(unit.ready_grads, outs, strict=True):
+                if not nccl:
+                    o.div_(n)
+                if s.grad_shard is None:
+                    s.grad_shard = o
+                else:
+                    s.grad_shard.add_(o)
+            if self._cuda:
+                for g in grads:
+                    g.record_stream(self._comm_stream)
+        for s in unit.ready_grads:
+            s.param.grad = None
+        unit.ready_grads = []
+
+    def sync(self) -> None:
+        if self.group_size == 1:
+            return
+        if self._cuda:
+            torch.cuda.current_stream().wait_stream(self._comm_stream)
+        for unit in self._units:
+            assert unit.pending == unit.n_grads, (
+                f"unit {unit.name}: only {unit.n_grads - unit.pending}/{unit.n_grads} grads "
+                "arrived -- a param got no grad this backward"
+            )
+            for s in unit.params:
+                assert s.full.untyped_storage().nbytes() == 0, (
+                    f"unit {unit.name}: full param storage still allocated at sync"
+                )
+                if s.param.requires_grad:
+                    assert s.grad_shard is not None, f"unit {unit.name}: no reduced grad to publish"
+                    s.param.grad = s.grad_shard
+                    s.grad_shard = None
+
+    # ------------------------------------------------------------- inspection
+    @property
+    def units(self) -> list[_Unit]:
+        return getattr(self, "_units", [])

@@ -1,0 +1,357 @@
+"""Training orchestrator (JSON config -> model, mesh, parallelism, optimizer, data, loop).
+
+Parity: reference ``pluggy/train/trainer.py:62-538``:
+
+* phases: build -> init -> parallelize -> re-seed -> objective -> optimizer ->
+  scheduler -> dataloader -> checkpointer -> resume -> wandb -> prefetcher;
+* same seed on every rank for build/init, then ``seed + 1 + dp_coord``;
+* grad accumulation ``K = global_batch / (micro * dp)``; ``train_step`` runs
+  K-1 microbatches with ``requires_sync=False`` and the last with ``True``,
+  then ``sync`` -> clip -> ``optimizer.step`` -> ``zero_grad`` ->
+  ``scheduler.step`` -> dp-average of the loss;
+* checkpoint layout/resume rules (mesh and data sources must be unchanged);
+* the rank-0 step line ``step=.. || loss=.. || gnorm=.. || lr=.. || tps=..``
+  (byte-compatible: the web UI scrapes it) and ``peak cuda mem``;
+* optional wandb on rank 0, asserted on every rank first.
+
+B200 differences:
+
+* no torch.compile and no autocast: on CUDA the models run their fused
+  sm_100a sublayers in bf16 with fp32 master weights and an fp32 residual;
+* the grad-norm clip coefficient stays on the device and is folded into the
+  fused AdamW kernel (no extra pass over the grads, no host sync);
+* the loop also runs on CPU (gloo) for the plumbing config and the tests;
+* ``data.synthetic`` selects the offline Zipf token source (no tokenizer);
+* ``parallelism`` accepts ``ddp`` / ``fsdp2`` plus mesh axes ``tp`` (tensor +
+  sequence parallel) and ``ep`` (expert parallel); FSDP2 checkpoints are
+  written sharded with placement metadata.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+from datetime import datetime
+
+import torch
+import torch.nn as nn
+
+from pluggy_b200.checkpoint.checkpointer import Checkpointer
+from pluggy_b200.core.collective import all_reduce, barrier
+from pluggy_b200.core.grad_helper import clip_grad_norm
+from pluggy_b200.core.mesh import Mesh
+from pluggy_b200.dataloader.prefetcher import CUDAPrefetcher
+from pluggy_b200.models.builder import build_model
+from pluggy_b200.objectives.builder import build_objective
+from pluggy_b200.optimizer.builder import build_optimizer, build_scheduler
+from pluggy_b200.utils import debug_time, get_project_dir, record_time
+
+try:
+    import wandb
+
+    HAS_WANDB = True
+except ImportError:  # pragma: no cover
+    HAS_WANDB = False
+
+
+def load_json(path: str) -> dict:
+    with open(path) as f:
+        return json.load(f)
+
+
+class Trainer:
+    def __init__(self, train_config_path: str | dict, rank: int, local_rank: int, world_size: int,
+                 benchmark: bool = False, checkpoint_root: str | None = None):
+        self.config = load_json(train_config_path) if isinstance(train_config_path, str) else \
+            dict(train_config_path)
+        from pluggy_b200.train.validate import validate_config
+
+        validate_config(self.config)
+        self.rank, self.world_size, self.benchmark = rank, world_size, benchmark
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local_rank)
+            self.device = torch.device("cuda", local_rank)
+        else:
+            self.device = torch.device("cpu")
+        self.mesh = Mesh(self.config["mesh"])
+        self.dp_size = self.mesh.size("dp")
+        self.ignore_index = self.config["objective"]["config"].get("ignore_index", -100)
+        data_cfg = self.config["data"]
+        self.tokenizer = None
+        if not data_cfg.get("synthetic"):
+            from tokenizers import Tokenizer
+
+            self.tokenizer = Tokenizer.from_pretrained(data_cfg["tokenizer"])
+        self.seed = self.config.get("seed", 0)
+        torch.manual_seed(self.seed)
+
+        self.model = self._build_model()
+        self._init_weights(self.model)
+        self.model = self._parallelize(self.model)
+        torch.manual_seed(self.seed + 1 + self.mesh.coordinate("dp"))
+
+        self.objective = build_objective(self.config["objective"]["name"],
+                                         self.config["objective"]["config"])
+        opt = self.config["optimizer"]
+        self.optimizer = build_optimizer(self.model, opt["name"], opt["config"])
+        self.scheduler = build_scheduler(self.optimizer, opt["scheduler"])
+        self.num_train_steps = opt["scheduler"]["total_steps"]
+        self.max_norm = opt.get("max_norm")
+
+        self.dataloader = self._build_dataloader()
+        self.global_batch_size = data_cfg["global_batch_size"]
+        self.micro_batch_size = data_cfg["micro_batch_size"]
+        per_backward = self.micro_batch_size * self.dp_size
+        assert self.global_batch_size % per_backward == 0, (
+            f"global_batch_size {self.global_batch_size} must be divisible by micro_batch_size "
+            f"{self.micro_batch_size} x dp {self.dp_size} = {per_backward}")
+        self.microbatches_per_step = self.global_batch_size // per_backward
+
+        stamp = datetime.now().strftime("%Y-%m-%d_%H-%M-%S")
+        self.run_name = f"{self.config['run_name']}_{stamp}"
+        root = checkpoint_root or os.path.join(get_project_dir(), "checkpoints")
+        self.checkpointer = Checkpointer(os.path.join(root, self.config["run_name"]))
+        ck = self.config.get("checkpointing", {})
+        self.resume = ck.get("resume")
+        self.save_steps = ck.get("save_steps", 10**9)
+        self.resume_scheduler = ck.get("resume_scheduler", True)
+        self.resume_wandb_id = None
+        self.start_step = self._resume()
+        self._setup_wandb()
+        self.prefetcher = CUDAPrefetcher(self.dataloader, self.device)
+
+    # ---------------------------------------------------------------- building
+    def _build_model(self) -> nn.Module:
+        m = self.config["model"]
+        return build_model(m["name"], m["config"])
+
+    def _init_weights(self, model: nn.Module) -> None:
+        model.to(self.device)
+        model.init_weights()
+        init_from = self.config["model"].get("init_from_hf")
+        if init_from:
+            from pluggy_b200.models.hf_import import load_hf_weights, weight_files
+
+            if self.rank == 0:
+                weight_files(init_from)
+            if self.world_size > 1:
+                barrier()
+            n = load_hf_weights(model, init_from)
+            if self.rank == 0:
+                print(f"init_from_hf: loaded {n} tensors from {init_from}")
+
+    def _parallelize(self, model: nn.Module) -> nn.Module:
+        self.parallelism = self.config.get("parallelism", "ddp")
+        sizes = self.config["mesh"]
+        if sizes.get("tp", 1) > 1:
+            from pluggy_b200.parallel.tensor_parallel import parallelize_tp
+
+            parallelize_tp(model, self.mesh, "tp", sequence_parallel=self.config.get("tp", {}).get(
+                "sequence_parallel", True))
+        if sizes.get("ep", 1) > 1:
+            from pluggy_b200.parallel.expert_parallel import parallelize_ep
+
+            parallelize_ep(model, self.mesh, "ep")
+        if self.parallelism == "ddp":
+            from pluggy_b200.parallel.ddp import DDP
+
+            ddp_cfg = self.config.get("ddp", {})
+            self.dp = DDP(model, self.mesh, dim="dp", bucket_mb=ddp_cfg.get("bucket_mb", 25),
+                          reducer=ddp_cfg.get("reducer", "nccl"))
+        elif self.parallelism == "fsdp2":
+            from pluggy_b200.parallel.fsdp2 import FSDP2
+
+            self.dp = FSDP2(model, self.mesh, dim="dp")
+        else:
+            raise ValueError(f"unknown parallelism {self.parallelism!r}: expected 'ddp' or 'fsdp2'")
+        self.grad_shard_dims = ("dp",) if (self.parallelism == "fsdp2" and self.dp_size > 1) else ()
+        return model
+
+    def _build_dataloader(self):
+        data = self.config["data"]
+        if data.get("synthetic"):
+            from pluggy_b200.dataloader.builder import build_synthetic_loader
+
+            vocab = self.config["model"]["config"]["vocab_size"]
+            return build_synthetic_loader(data, vocab, self.mesh.coordinate("dp"),
+                                          pin=self.device.type == "cuda")
+        from pluggy_b200.dataloader.builder import build_dataloader
+
+        return build_dataloader(data, self.tokenizer, self.ignore_index, self.mesh.coordinate("dp"),
+                                self.mesh.size("dp"))
+
+    # ------------------------------------------------------------------- wandb
+    def _setup_wandb(self) -> None:
+        self.wandb_run = None
+        cfg = self.config.get("wandb", {})
+        if not cfg.get("enabled", False) or self.benchmark:
+            return
+        assert HAS_WANDB, "wandb.enabled is true in the config but wandb isn't installed"
+        if self.rank != 0:
+            return
+        self.wandb_run = wandb.init(project=cfg.get("project", "pluggy"), entity=cfg.get("entity"),
+                                    name=self.run_name, id=self.resume_wandb_id,
+                                    resume="must" if self.resume_wandb_id else None,
+                                    config=self.config)
+
+    def _log_metrics(self, metrics, step, tokens_per_step, t) -> None:
+        if self.wandb_run is None:
+            return
+        log = {"train/loss": float(metrics["loss"]), "train/grad_norm": float(metrics["grad_norm"]),
+               "train/lr": self.scheduler.get_last_lr()[0], "train/tokens": step * tokens_per_step,
+               "perf/tps": tokens_per_step / t, "perf/step_time": t}
+        if self.device.type == "cuda":
+            log["perf/peak_mem_gib"] = torch.cuda.max_memory_allocated() / 2**30
+        self.wandb_run.log(log, step=step)
+
+    # -------------------------------------------------------------- checkpoint
+    @debug_time
+    def checkpoint(self, step: int) -> None:
+        if self.parallelism == "fsdp2" and self.dp_size > 1:
+            self._checkpoint_sharded(step)
+        elif self.rank == 0:
+            self.checkpointer.save_model(self.model, step)
+        if self.rank == 0:
+            if not (self.parallelism == "fsdp2" and self.dp_size > 1):
+                self.checkpointer.save_optimizer(self.optimizer, step)
+            self.checkpointer.save_scheduler(self.scheduler, step)
+            self.checkpointer.save_trainer({"step": step, "config": self.config,
+                                            "wandb_id": self.wandb_run.id if self.wandb_run else None},
+                                           step)
+        rng = {"cpu_rng": torch.get_rng_state()}
+        if self.device.type == "cuda":
+            rng["cuda_rng"] = torch.cuda.get_rng_state(self.device)
+        self.checkpointer.save_rng(rng, step, self.rank)
+        self.checkpointer.save_dataloader_state(self.prefetcher.loader_state_dict(), step,
+                                                self.mesh.coordinate("dp"))
+        barrier()
+        if self.rank == 0:
+            self.checkpointer.mark_complete(step)
+
+    def _checkpoint_sharded(self, step: int) -> None:
+        coord, n = self.mesh.coordinate("dp"), self.dp_size
+        local = {k: v for k, v in self.model.state_dict().items()}
+        placements = {k: {"dim": 0, "coord": coord, "axis_size": n} for k in local}
+        self.checkpointer.save_sharded_model(local, placements, step, self.rank, self.world_size)
+        torch.save(self.optimizer.state_dict(),
+                   os.path.join(self.checkpointer._step_dir(step, True), f"optimizer_rank{self.rank}.pt"))
+
+    def _resume(self) -> int:
+        if self.resume is None:
+            return 0
+        if self.resume == "auto":
+            step = self.checkpointer.latest()
+            if step is None:
+                return 0
+        elif isinstance(self.resume, int):
+            step = self.checkpointer.valid_step(self.resume)
+            assert step is not None, "non valid step to resume from"
+        else:
+            raise ValueError("resume must be None, 'auto', or a completed training step")
+        state = self.checkpointer.load_trainer(step)
+        assert state["config"]["mesh"] == self.config["mesh"], (
+            f"resume across a mesh change is unsupported: checkpoint has {state['config']['mesh']}, "
+            f"config has {self.config['mesh']}")
+        from pluggy_b200.dataloader.builder import resolve_sources
+
+        def ids(cfg):
+            if cfg["data"].get("synthetic"):
+                return [("synthetic", json.dumps(cfg["data"]["synthetic"], sort_keys=True))]
+            return [(s["label"], s["config"], s["split"]) for s in resolve_sources(cfg["data"])]
+
+        assert ids(state["config"]) == ids(self.config), (
+            f"resume across a change of data sources is unsupported: checkpoint has "
+            f"{ids(state['config'])}, config has {ids(self.config)}")
+        if self.parallelism == "fsdp2" and self.dp_size > 1:
+            shard = self.checkpointer._load(step, f"model_shard_rank{self.rank}.pt")
+            self.model.load_state_dict(shard)
+            self.optimizer.load_state_dict(self.checkpointer._load(step, f"optimizer_rank{self.rank}.pt"))
+        else:
+            self.checkpointer.load_model(self.model, step)
+            self.checkpointer.load_optimizer(self.optimizer, step)
+        if self.resume_scheduler:
+            self.checkpointer.load_scheduler(self.scheduler, step)
+        else:
+            self.scheduler.last_epoch = step
+        self.checkpointer.load_dataloader(self.dataloader, step, self.mesh.coordinate("dp"))
+        rng = self.checkpointer.load_rng(step, self.rank)
+        if rng is None:
+            rng = {k: state[k] for k in ("cpu_rng", "cuda_rng") if k in state}
+        if "cpu_rng" in rng:
+            torch.set_rng_state(rng["cpu_rng"])
+        if "cuda_rng" in rng and self.device.type == "cuda":
+            torch.cuda.set_rng_state(rng["cuda_rng"], self.device)
+        self.resume_wandb_id = state.get("wandb_id")
+        return state["step"]
+
+    # -------------------------------------------------------------------- loop
+    def get_batch_prefetcher(self):
+        return next(self.prefetcher)
+
+    def micro_train_step(self) -> torch.Tensor:
+        batch = self.get_batch_prefetcher()
+        loss = self.objective.compute_loss(self.model, batch) / self.microbatches_per_step
+        loss.backward()
+        return loss.detach()
+
+    def optimizer_step(self) -> torch.Tensor:
+        """sync -> clip -> step -> zero_grad -> scheduler; returns the grad norm."""
+        self.dp.sync()
+        fused = self.device.type == "cuda" and hasattr(self.optimizer, "set_grad_scale")
+        if fused:
+            gnorm, coef = clip_grad_norm(self.model.parameters(), self.mesh, self.max_norm,
+                                         shard_dims=self.grad_shard_dims, fold_into_optimizer=True)
+            self.optimizer.set_grad_scale(coef)
+        else:
+            gnorm = clip_grad_norm(self.model.parameters(), self.mesh, self.max_norm,
+                                   shard_dims=self.grad_shard_dims)
+        self.optimizer.step()
+        self.optimizer.zero_grad()
+        self.scheduler.step()
+        return gnorm
+
+    def _train_step(self) -> dict[str, torch.Tensor]:
+        loss = torch.zeros((), device=self.device)
+        self.dp.requires_sync = False
+        for _ in range(self.microbatches_per_step - 1):
+            loss += self.micro_train_step()
+        self.dp.requires_sync = True
+        loss += self.micro_train_step()
+        gnorm = self.optimizer_step()
+        if self.dp_size > 1:
+            all_reduce(loss, self.mesh, "dp", "avg")
+        return {"loss": loss, "grad_norm": gnorm}
+
+    train_step = record_time(_train_step)
+
+    def _line(self, step, metrics, tokens_per_step, t) -> str:
+        return (f"step={step} || loss={metrics['loss']:.4f} || gnorm={metrics['grad_norm']:.3f} "
+                f"|| lr={self.scheduler.get_last_lr()[0]:.2e} || tps={tokens_per_step / t:.0f}")
+
+    @debug_time
+    def train_n_step_test(self, n_steps: int) -> None:
+        tokens_per_step = self.config["data"]["seq_len"] * self.global_batch_size
+        for step in range(n_steps):
+            metrics, t = self.train_step()
+            if self.rank == 0:
+                print(self._line(step, metrics, tokens_per_step, t))
+        self._print_peak()
+
+    def _print_peak(self) -> None:
+        if self.rank == 0 and self.device.type == "cuda":
+            print(f"peak cuda mem: {torch.cuda.max_memory_allocated() / 2**30:.2f} GiB")
+
+    def train(self) -> None:
+        tokens_per_step = self.config["data"]["seq_len"] * self.global_batch_size
+        try:
+            for step in range(self.start_step, self.num_train_steps):
+                metrics, t = self.train_step()
+                if ((step + 1) % self.save_steps == 0 and step != 0) or (step + 1) == self.num_train_steps:
+                    self.checkpoint(step + 1)
+                if self.rank == 0:
+                    self._log_metrics(metrics, step + 1, tokens_per_step, t)
+                    print(self._line(step, metrics, tokens_per_step, t))
+            self._print_peak()
+        finally:
+            if self.wandb_run is not None:
+                self.wandb_run.finish()

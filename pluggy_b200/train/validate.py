@@ -1,0 +1,83 @@
+"""Startup validation of a training config (structure + constructor signatures).
+
+The reference validates configs only inside its web server
+(``pluggy/synth/server.py:281-384``: constructor signatures are the schema) and
+its roadmap asks for a startup ``validate()``; this module is that pass, shared
+by the trainer and the web server.
+"""
+
+from __future__ import annotations
+
+import inspect
+
+REQUIRED_TOP = ("model", "mesh", "optimizer", "objective", "data", "run_name")
+
+
+class ConfigError(ValueError):
+    pass
+
+
+def kwarg_error(cls, cfg: dict, what: str) -> str | None:
+    sig = inspect.signature(cls.__init__)
+    params = {k: p for k, p in sig.parameters.items() if k != "self"}
+    if any(p.kind == p.VAR_KEYWORD for p in params.values()):
+        return None
+    unknown = sorted(set(cfg) - set(params))
+    if unknown:
+        return f"{what}: unknown argument(s) {unknown}"
+    missing = sorted(k for k, p in params.items()
+                     if p.default is p.empty and p.kind not in (p.VAR_POSITIONAL, p.VAR_KEYWORD)
+                     and k not in cfg and k != "optimizer")
+    if missing:
+        return f"{what}: missing required argument(s) {missing}"
+    return None
+
+
+def validate_config(cfg: dict) -> None:
+    errs = [f"missing top-level key {k!r}" for k in REQUIRED_TOP if k not in cfg]
+    if errs:
+        raise ConfigError("; ".join(errs))
+    from pluggy_b200.models.builder import MODEL_REGISTRY
+    from pluggy_b200.objectives.builder import OBJECTIVE_REGISTRY
+    from pluggy_b200.optimizer.builder import OPTIMIZER_REGISTRY, SCHEDULER_REGISTRY
+
+    m = cfg["model"]
+    if m.get("name") not in MODEL_REGISTRY:
+        errs.append(f"model.name {m.get('name')!r} not in {sorted(MODEL_REGISTRY)}")
+    else:
+        e = kwarg_error(MODEL_REGISTRY[m["name"]], m.get("config", {}), "model.config")
+        if e:
+            errs.append(e)
+    mesh = cfg["mesh"]
+    if not isinstance(mesh, dict) or "dp" not in mesh or any(int(v) < 1 for v in mesh.values()):
+        errs.append("mesh must map axis names (including 'dp') to positive sizes")
+    if cfg.get("parallelism", "ddp") not in ("ddp", "fsdp2"):
+        errs.append(f"parallelism must be 'ddp' or 'fsdp2', got {cfg.get('parallelism')!r}")
+    o = cfg["optimizer"]
+    if o.get("name") not in OPTIMIZER_REGISTRY:
+        errs.append(f"optimizer.name {o.get('name')!r} not in {sorted(OPTIMIZER_REGISTRY)}")
+    sch = o.get("scheduler", {})
+    if sch.get("type") not in SCHEDULER_REGISTRY:
+        errs.append(f"optimizer.scheduler.type {sch.get('type')!r} not in {sorted(SCHEDULER_REGISTRY)}")
+    else:
+        e = kwarg_error(SCHEDULER_REGISTRY[sch["type"]], {k: v for k, v in sch.items() if k != "type"},
+                        "optimizer.scheduler")
+        if e:
+            errs.append(e)
+    ob = cfg["objective"]
+    if ob.get("name") not in OBJECTIVE_REGISTRY:
+        errs.append(f"objective.name {ob.get('name')!r} not in {sorted(OBJECTIVE_REGISTRY)}")
+    else:
+        e = kwarg_error(OBJECTIVE_REGISTRY[ob["name"]], ob.get("config", {}), "objective.config")
+        if e:
+            errs.append(e)
+    d = cfg["data"]
+    for k in ("global_batch_size", "micro_batch_size", "seq_len"):
+        if not isinstance(d.get(k), int) or d[k] < 1:
+            errs.append(f"data.{k} must be a positive integer")
+    if not d.get("synthetic"):
+        for k in ("tokenizer", "eos_token", "pad_token", "num_workers", "seed"):
+            if k not in d:
+                errs.append(f"data.{k} is required for a dataset-backed run")
+    if errs:
+        raise ConfigError("; ".join(errs))

@@ -1,0 +1,321 @@
+"""Numerics of every sm_100a kernel against a plain fp32 PyTorch reference of the same op."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def rel(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / (b.norm() + 1e-12)).item()
+
+
+@pytest.fixture(autouse=True)
+def _status():
+    from pluggy_b200.ops import _ext
+
+    _ext.ext()
+    yield
+    torch.cuda.synchronize()
+    _ext.check_status()
+
+
+# ---------------------------------------------------------------------- GEMM
+GEMM_SHAPES = [(128, 256, 64), (256, 512, 128), (300, 200, 136), (1000, 384, 520), (4096, 4096, 1024),
+               (130, 1030, 72), (8192, 1024, 3072)]
+
+
+@pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
+@pytest.mark.parametrize("layout", ["fwd", "dgrad", "wgrad"])
+def test_gemm_layouts(M, N, K, layout):
+    from pluggy_b200.ops.gemm import gemm
+
+    torch.manual_seed(M + N + K)
+    A = torch.randn(M, K, device=DEV).bfloat16()
+    B = torch.randn(N, K, device=DEV).bfloat16()
+    ref = A.float() @ B.float().t()
+    if layout == "fwd":
+        out = gemm(A, B)
+    elif layout == "dgrad":  # B given as [K, N]
+        out = gemm(A, B.t().contiguous(), b_mn_major=True)
+    else:  # A given as [K, M] and B as [K, N], fp32 out
+        out = gemm(A.t().contiguous(), B.t().contiguous(), a_mn_major=True, b_mn_major=True,
+                   out_dtype=torch.float32)
+    assert rel(out, ref) < 1e-2, (layout, M, N, K, rel(out, ref))
+
+
+@pytest.mark.parametrize("bn", [128, 256])
+def test_gemm_tile_widths_and_fp32_out(bn):
+    from pluggy_b200.ops.gemm import gemm
+
+    A = torch.randn(777, 320, device=DEV).bfloat16()
+    B = torch.randn(640, 320, device=DEV).bfloat16()
+    out = gemm(A, B, out_dtype=torch.float32, bn=bn)
+    assert rel(out, A.float() @ B.float().t()) < 5e-3
+
+
+def test_gemm_residual_epilogue():
+    from pluggy_b200.ops.gemm import linear_fwd
+
+    x = torch.randn(1024, 512, device=DEV).bfloat16()
+    w = torch.randn(384, 512, device=DEV).bfloat16() * 0.05
+    r = torch.randn(1024, 384, device=DEV)
+    out = linear_fwd(x, w, out_dtype=torch.float32, residual=r)
+    assert rel(out, r + x.float() @ w.float().t()) < 5e-3
+
+
+def test_gemm_split_k_and_accumulate():
+    from pluggy_b200.ops.gemm import gemm, linear_wgrad
+
+    dy = torch.randn(16384, 256, device=DEV).bfloat16()
+    x = torch.randn(16384, 128, device=DEV).bfloat16()
+    ref = dy.float().t() @ x.float()
+    out = linear_wgrad(dy, x)  # small output, long K: split-K with fp32 atomics
+    assert rel(out, ref) < 5e-3
+    acc = torch.ones(256, 128, device=DEV)
+    linear_wgrad(dy, x, out=acc, accumulate=True)
+    assert rel(acc, ref + 1) < 5e-3
+    for s in (1, 3, 7):
+        o = gemm(dy.t().contiguous(), x.t().contiguous(), a_mn_major=True, b_mn_major=True,
+                 out_dtype=torch.float32, splits=s)
+        assert rel(o, ref) < 5e-3, s
+
+
+# ---------------------------------------------------------------- norms, rope
+@pytest.mark.parametrize("D", [128, 1024, 2560])
+@pytest.mark.parametrize("xdt", [torch.float32, torch.bfloat16])
+def test_rmsnorm_fwd_bwd(D, xdt):
+    from pluggy_b200.ops.norm import rms_norm, rms_norm_reference
+
+    x = torch.randn(333, D, device=DEV, dtype=xdt, requires_grad=True)
+    w = (1 + 0.1 * torch.randn(D, device=DEV)).requires_grad_(True)
+    y = rms_norm(x, w, 1e-6)
+    g = torch.randn_like(y)
+    (y * g).sum().backward()
+    xr = x.detach().float().requires_grad_(True)
+    wr = w.detach().clone().requires_grad_(True)
+    yr = rms_norm_reference(xr, wr, 1e-6)
+    (yr * g.float()).sum().backward()
+    tol = 1e-2 if xdt == torch.bfloat16 else 1e-5
+    assert rel(y, yr) < tol
+    assert rel(x.grad, xr.grad) < max(tol, 1e-4)
+    assert rel(w.grad, wr.grad) < 1e-3
+
+
+def _ref_qk_rope(qkv, S, Hq, Hk, d, wq, wk, inv, eps):
+    T = qkv.shape[0]
+    q = qkv[:, :Hq * d].view(T, Hq, d)
+    k = qkv[:, Hq * d:(Hq + Hk) * d].view(T, Hk, d)
+
+    def nrm(x, w):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w
+
+    q, k = nrm(q, wq), nrm(k, wk)
+    pos = (torch.arange(T, device=qkv.device) % S).float()
+    f = pos[:, None] * inv[None]
+    cos = torch.cat([f, f], -1).cos()[:, None]
+    sin = torch.cat([f, f], -1).sin()[:, None]
+
+    def rot(x):
+        h = d // 2
+        return x * cos + torch.cat([-x[..., h:], x[..., :h]], -1) * sin
+
+    return rot(q), rot(k)
+
+
+@pytest.mark.parametrize("d", [64, 128])
+def test_qk_norm_rope_fwd_bwd(d):
+    from pluggy_b200.ops.norm import qk_norm_rope_bwd, qk_norm_rope_fwd
+
+    B, S, Hq, Hk = 2, 192, 4, 2
+    T = B * S
+    W = (Hq + 2 * Hk) * d
+    qkv = torch.randn(T, W, device=DEV).bfloat16()
+    wq = 1 + 0.1 * torch.randn(d, device=DEV)
+    wk = 1 + 0.1 * torch.randn(d, device=DEV)
+    inv = 1.0 / (1e6 ** (torch.arange(0, d, 2, device=DEV).float() / d))
+    q, k, rstd = qk_norm_rope_fwd(qkv, S=S, Hq=Hq, Hk=Hk, d=d, wq=wq, wk=wk, inv_freq=inv, eps=1e-6)
+    x = qkv.float().requires_grad_(True)
+    wqr, wkr = wq.clone().requires_grad_(True), wk.clone().requires_grad_(True)
+    qr, kr = _ref_qk_rope(x, S, Hq, Hk, d, wqr, wkr, inv, 1e-6)
+    assert rel(q, qr) < 1e-2 and rel(k, kr) < 1e-2
+    gq, gk = torch.randn_like(qr), torch.randn_like(kr)
+    ((qr * gq).sum() + (kr * gk).sum()).backward()
+    dqkv = torch.zeros(T, W, device=DEV, dtype=torch.bfloat16)
+    dwq, dwk = qk_norm_rope_bwd(qkv, rstd, gq.bfloat16(), gk.bfloat16(), dqkv, S=S, Hq=Hq, Hk=Hk,
+                                d=d, wq=wq, wk=wk, inv_freq=inv, eps=1e-6)
+    assert rel(dqkv[:, :(Hq + Hk) * d], x.grad[:, :(Hq + Hk) * d]) < 2e-2
+    assert rel(dwq, wqr.grad) < 2e-2 and rel(dwk, wkr.grad) < 2e-2
+
+
+# ----------------------------------------------------------------- pointwise
+@pytest.mark.parametrize("kind", [0, 1])
+def test_glu_fwd_bwd(kind):
+    from pluggy_b200.ops.elementwise import glu_bwd, glu_fwd
+
+    gu = torch.randn(513, 2 * 384, device=DEV).bfloat16()
+    g, u = gu.float()[:, :384].requires_grad_(True), gu.float()[:, 384:].requires_grad_(True)
+    act = torch.nn.functional.silu(g) if kind == 0 else torch.nn.functional.gelu(g, approximate="tanh")
+    ref = act * u
+    out = glu_fwd(gu, kind)
+    assert rel(out, ref) < 1e-2
+    do = torch.randn_like(ref)
+    (ref * do).sum().backward()
+    dgu = glu_bwd(gu, do.bfloat16(), kind)
+    assert rel(dgu[:, :384], g.grad) < 2e-2 and rel(dgu[:, 384:], u.grad) < 2e-2
+
+
+def test_embedding_fwd_bwd():
+    from pluggy_b200.models._engine import Embedding
+
+    w = torch.randn(1000, 256, device=DEV, requires_grad=True)
+    ids = torch.randint(0, 1000, (4, 64), device=DEV)
+    out = Embedding.apply(ids, w, 1.5)
+    assert torch.allclose(out, w.detach()[ids.view(-1)] * 1.5)
+    g = torch.randn_like(out)
+    out.backward(g)
+    ref = torch.zeros_like(w).index_add_(0, ids.view(-1), g * 1.5)
+    assert rel(w.grad, ref) < 1e-6
+
+
+# ------------------------------------------------------------- fused lin-CE
+@pytest.mark.parametrize("N,chunk", [(1000, 256), (2048, 2048), (333, 4096)])
+def test_fused_linear_ce(N, chunk):
+    from pluggy_b200.ops.ce import fused_linear_cross_entropy
+
+    D, V = 256, 5000
+    h = (torch.randn(N, D, device=DEV) * 0.5).bfloat16().requires_grad_(True)
+    w = (torch.randn(V, D, device=DEV) * 0.05).requires_grad_(True)
+    lab = torch.randint(0, V, (N,), device=DEV)
+    lab[::7] = -100
+    loss = fused_linear_cross_entropy(h, w, lab, -100, chunk)
+    loss.backward()
+    hr = h.detach().float().requires_grad_(True)
+    wr = w.detach().clone().requires_grad_(True)
+    logits = hr.bfloat16().float() @ wr.bfloat16().float().t()
+    lr = torch.nn.functional.cross_entropy(logits, lab, ignore_index=-100)
+    lr.backward()
+    assert abs(loss.item() - lr.item()) < 2e-2 * max(1.0, abs(lr.item()))
+    assert rel(h.grad, hr.grad) < 3e-2
+    assert rel(w.grad, wr.grad) < 3e-2
+
+
+# ----------------------------------------------------------------- optimizer
+def test_fused_adamw_matches_torch():
+    from pluggy_b200.optimizer.fused_adamw import FusedAdamW
+
+    torch.manual_seed(0)
+    shapes = [(300, 17), (1024,), (7,), (65536 + 5,)]
+    ps = [torch.randn(s, device=DEV, requires_grad=True) for s in shapes]
+    qs = [p.detach().clone().requires_grad_(True) for p in ps]
+    a = FusedAdamW([{"params": ps[:2], "weight_decay": 0.1}, {"params": ps[2:], "weight_decay": 0.0}],
+                   lr=1e-2, betas=(0.9, 0.95), fused=True)
+    b = torch.optim.AdamW([{"params": qs[:2], "weight_decay": 0.1}, {"params": qs[2:], "weight_decay": 0.0}],
+                          lr=1e-2, betas=(0.9, 0.95))
+    for _ in range(3):
+        for p, q in zip(ps, qs):
+            g = torch.randn_like(p)
+            p.grad, q.grad = g.clone(), g.clone()
+        a.step()
+        b.step()
+    for p, q in zip(ps, qs):
+        assert rel(p, q) < 1e-6
+    sd = a.state_dict()
+    assert set(sd["state"][0]) == {"step", "exp_avg", "exp_avg_sq"}
+
+
+def test_grad_clip_kernels():
+    from pluggy_b200.core.grad_helper import clip_grad_norm
+
+    ps = [torch.nn.Parameter(torch.randn(s, device=DEV)) for s in [(100, 30), (5,), (70000,)]]
+    for p in ps:
+        p.grad = torch.randn_like(p) * 3
+    ref = torch.linalg.vector_norm(torch.stack([p.grad.norm() for p in ps]))
+    grads0 = [p.grad.clone() for p in ps]
+    total = clip_grad_norm(ps, None, 1.0)
+    assert abs(total.item() - ref.item()) / ref.item() < 1e-5
+    coef = 1.0 / (ref.item() + 1e-6)
+    for p, g in zip(ps, grads0):
+        assert rel(p.grad, g * coef) < 1e-5
+
+
+# ----------------------------------------------------------------- attention
+ATTN_CASES = [
+    # B, S, Hq, Hk, d, causal, window
+    (1, 128, 1, 1, 128, True, 0),
+    (2, 256, 4, 2, 128, True, 0),
+    (1, 384, 2, 2, 64, True, 0),
+    (2, 200, 4, 1, 128, True, 0),
+    (1, 512, 2, 1, 128, True, 160),
+    (1, 256, 2, 2, 64, False, 0),
+    (2, 1024, 16, 8, 128, True, 0),
+]
+
+
+@pytest.mark.parametrize("B,S,Hq,Hk,d,causal,window", ATTN_CASES)
+def test_attention_fwd_bwd(B, S, Hq, Hk, d, causal, window):
+    from pluggy_b200.ops.attention import attention_reference, flash_attention
+
+    torch.manual_seed(S + d)
+    q = torch.randn(B, S, Hq, d, device=DEV).bfloat16().requires_grad_(True)
+    k = torch.randn(B, S, Hk, d, device=DEV).bfloat16().requires_grad_(True)
+    v = torch.randn(B, S, Hk, d, device=DEV).bfloat16().requires_grad_(True)
+    o = flash_attention(q, k, v, causal, window)
+    qr, kr, vr = (t.detach().float().requires_grad_(True) for t in (q, k, v))
+    orf = attention_reference(qr, kr, vr, causal, window)
+    assert rel(o, orf) < 2e-2, rel(o, orf)
+    do = torch.randn_like(orf)
+    o.backward(do.bfloat16())
+    orf.backward(do)
+    assert rel(q.grad, qr.grad) < 3e-2, rel(q.grad, qr.grad)
+    assert rel(k.grad, kr.grad) < 3e-2, rel(k.grad, kr.grad)
+    assert rel(v.grad, vr.grad) < 3e-2, rel(v.grad, vr.grad)
+
+
+def test_attention_lse():
+    from pluggy_b200.ops.attention import attn_fwd
+
+    B, S, H, d = 1, 256, 2, 128
+    q = torch.randn(B, S, H, d, device=DEV).bfloat16()
+    k = torch.randn(B, S, H, d, device=DEV).bfloat16()
+    v = torch.randn(B, S, H, d, device=DEV).bfloat16()
+    _, lse = attn_fwd(q, k, v, causal=True)
+    s = (q.float().transpose(1, 2) @ k.float().transpose(1, 2).transpose(-1, -2)) / math.sqrt(d)
+    mask = torch.ones(S, S, device=DEV, dtype=torch.bool).tril()
+    ref = s.masked_fill(~mask, float("-inf")).logsumexp(-1)
+    assert (lse - ref).abs().max().item() < 2e-2
+
+
+# ------------------------------------------------------------- model, fused
+@pytest.mark.parametrize("family", ["qwen3", "llama3"])
+def test_fused_model_matches_eager(family):
+    from pluggy_b200.models.builder import build_model
+    from pluggy_b200.objectives.autoregressive import ARObjective
+
+    torch.manual_seed(0)
+    cfg = dict(num_layers=2, num_heads=4, num_kv_heads=2, emb_dim=256, head_dim=64 if family == "llama3"
+               else 128, vocab_size=2048, ffn_dim=512)
+    name = "qwen3_dense" if family == "qwen3" else "llama3_2"
+    m = build_model(name, cfg).to(DEV)
+    m.init_weights()
+    ids = torch.randint(0, 2048, (2, 256), device=DEV)
+    batch = {"input_ids": ids, "labels": ids}
+    obj = ARObjective(ce_chunk_size=128)
+    loss = obj.compute_loss(m, batch)
+    loss.backward()
+    grads = {n: p.grad.detach().clone() for n, p in m.named_parameters()}
+    m.zero_grad()
+    # eager fp32 reference path: same weights, CPU math
+    mc = build_model(name, cfg)
+    mc.load_state_dict({k: v.cpu() for k, v in m.state_dict().items()})
+    lc = obj.compute_loss(mc, {k: v.cpu() for k, v in batch.items()})
+    lc.backward()
+    assert abs(loss.item() - lc.item()) < 2e-2 * lc.item()
+    for n, p in mc.named_parameters():
+        r = rel(grads[n].cpu(), p.grad)
+        assert r < 6e-2, (n, r)
