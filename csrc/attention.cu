@@ -38,14 +38,9 @@ namespace attn {
 
 constexpr int BQ = 128;
 constexpr int BKV = 128;
-constexpr int kThreads = 192;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr int kBox = 128 * 128;  // bytes of one [128 rows x 64 bf16] swizzled box
-
-__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
-  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
-}
 
 // K-major SW128 descriptor for k-step kk (16 elements) of a [128 rows x (64*nbox)] tile
 // stored as nbox boxes of [128 rows x 64].
@@ -69,63 +64,112 @@ __device__ __forceinline__ bool key_ok(int qi, int ki, int S, int causal, int wi
 }
 
 // --------------------------------------------------------------------- forward
-template <int D>
-struct FwdCfg {
-  static constexpr int kTile = 128 * D * 2;
-  static constexpr int kQ = 0;
-  static constexpr int kK = kTile;          // 2 stages
-  static constexpr int kV = 3 * kTile;      // 2 stages
-  static constexpr int kP = 5 * kTile;      // [128 x 128] bf16
-  static constexpr int kBar = kP + 128 * 128 * 2;
-  static constexpr int kSmem = kBar + 256 + 1024;
-  static constexpr int kTmemO = 256;
-};
+// Two 128-row query tiles per CTA, one softmax warpgroup each, so that one
+// group's softmax overlaps the tensor core working on the other group:
+//   warp 0       TMA: Q tiles once, then K_t / V_t (two stages each, released
+//                separately: K after the S MMAs, V after the PV MMAs)
+//   warp 1       TMEM owner + MMA issuer, per tile t in the order
+//                PV_0(t), S_0(t+1), PV_1(t), S_1(t+1)
+//   warps 2..5   softmax group 0 (query tile 0), warps 6..9 group 1
+// S_w lives in TMEM; the softmax group overwrites it in place with P (bf16,
+// two per 32-bit column) and the PV MMA reads P straight from TMEM (A operand
+// in tensor memory), so P never touches shared memory. O_w stays in TMEM; it
+// is rescaled only when a row max grows by more than 2^8 (stale maxima keep
+// p <= 256, safe in bf16/fp32). Masks are applied only on edge tiles, without
+// branches.
+// The two query tiles are two heads of one GQA group (same keys, same range)
+// when the group size is even, else two consecutive row tiles of one head.
+constexpr int kFwdThreads = 320;
+constexpr float kRescale = 8.0f;
 
 template <int D>
-__global__ void __launch_bounds__(kThreads, 1)
+struct Fwd {
+  static constexpr int kTile = 128 * D * 2;
+  static constexpr int kQ = 0;            // Q0, Q1
+  static constexpr int kK = 2 * kTile;    // two stages
+  static constexpr int kV = 4 * kTile;    // two stages
+  static constexpr int kBar = 6 * kTile;
+  static constexpr int kSmem = kBar + 256;
+  static constexpr int kTO = 256;         // O_w at kTO + w * D
+};
+
+struct QTile {
+  int h, qt, lo, hi;
+};
+
+__device__ __forceinline__ QTile make_qtile(const AttnArgs& a, int h, int qt) {
+  QTile t;
+  t.h = h;
+  t.qt = qt;
+  const int n_kv = (a.S + BKV - 1) / BKV;
+  const int n_q = (a.S + BQ - 1) / BQ;
+  if (qt >= n_q) {
+    t.lo = 1;
+    t.hi = 0;  // empty
+    return t;
+  }
+  t.hi = a.causal ? min(qt, n_kv - 1) : n_kv - 1;
+  t.lo = 0;
+  if (a.window > 0) {
+    const int lo_key = qt * BQ - a.window + 1;
+    t.lo = lo_key > 0 ? lo_key / BKV : 0;
+  }
+  return t;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, AttnArgs a) {
-  using C = FwdCfg<D>;
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = align1024(smem_raw);
+                    const __grid_constant__ CUtensorMap tmV, AttnArgs a, int pair_heads) {
+  using C = Fwd<D>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  if (smem_u32(smem) & 1023) {
+    if (threadIdx.x == 0) record_status(a.status, kBadArgument);
+    return;
+  }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBar);
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;    // [2]
   uint64_t* v_full = bars + 3;    // [2]
-  uint64_t* kv_empty = bars + 5;  // [2]
-  uint64_t* s_full = bars + 7;    // [2]
-  uint64_t* s_free = bars + 9;    // [2]
-  uint64_t* p_full = bars + 11;
-  uint64_t* o_done = bars + 12;
-  uint64_t* mma_done = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* k_empty = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;   // [2]
+  uint64_t* s_full = bars + 9;    // [2] per group
+  uint64_t* p_full = bars + 11;   // [2] per group
+  uint64_t* o_done = bars + 13;   // [2] per group
+  uint64_t* mma_done = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = gridDim.x - 1 - blockIdx.x;  // heavy causal tiles first
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int hk = h / (a.Hq / a.Hk);
-  const int q0 = qt * BQ;
-  const int n_kv = (a.S + BKV - 1) / BKV;
-  const int j_hi = a.causal ? min(qt, n_kv - 1) : n_kv - 1;
-  int j_lo = 0;
-  if (a.window > 0) {
-    const int lo_key = q0 - a.window + 1;
-    j_lo = lo_key > 0 ? lo_key / BKV : 0;
+  const int b = blockIdx.z;
+  const int G = a.Hq / a.Hk;
+  QTile qtl[2];
+  if (pair_heads) {
+    const int qt = gridDim.x - 1 - blockIdx.x;  // heavy causal tiles first
+    qtl[0] = make_qtile(a, 2 * blockIdx.y, qt);
+    qtl[1] = make_qtile(a, 2 * blockIdx.y + 1, qt);
+  } else {
+    const int i = gridDim.x - 1 - blockIdx.x;
+    qtl[0] = make_qtile(a, blockIdx.y, 2 * i);
+    qtl[1] = make_qtile(a, blockIdx.y, 2 * i + 1);
   }
-  const int n = j_hi - j_lo + 1;
+  const int hk = qtl[0].h / G;
+  const bool live0 = qtl[0].hi >= qtl[0].lo, live1 = qtl[1].hi >= qtl[1].lo;
+  const int t_lo = live1 && (!live0 || qtl[1].lo < qtl[0].lo) ? qtl[1].lo : qtl[0].lo;
+  const int t_hi = live1 && (!live0 || qtl[1].hi > qtl[0].hi) ? qtl[1].hi : qtl[0].hi;
+  const int n = (live0 || live1) ? t_hi - t_lo + 1 : 0;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&v_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 4);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_done[i], 1);
     }
-    mbar_init(p_full, 4);
-    mbar_init(o_done, 1);
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -137,209 +181,238 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
   uint8_t* sQ = smem + C::kQ;
   uint8_t* sK = smem + C::kK;
   uint8_t* sV = smem + C::kV;
-  uint8_t* sP = smem + C::kP;
 
   if (warp == 0) {
     if (lane == 0 && n > 0) {
-      uint32_t issued = 0, par = 0;  // bit i: stage i in flight; its parity
       bool ok = true;
-      mbar_arrive_expect_tx(q_full, C::kTile);
+      uint32_t kin = 0, vin = 0, kpar = 0, vpar = 0;  // stages in flight and their parity
+      mbar_arrive_expect_tx(q_full, (live0 + live1) * C::kTile);
+      for (int w = 0; w < 2; ++w) {
+        if (w == 0 ? !live0 : !live1) continue;
 #pragma unroll
-      for (int x = 0; x < D / 64; ++x) tma_load_4d(sQ + x * kBox, &tmQ, q_full, x * 64, h, q0, b);
-      for (int t = 0; t < n && ok; ++t) {
-        const int st = t & 1;
-        if (t >= 2 && !mbar_wait_bounded(&kv_empty[st], ((t >> 1) - 1) & 1, abort_flag)) {
-          record_status(a.status, kTimeoutSmemEmpty);
-          *abort_flag = 1;
-          ok = false;
-          break;
-        }
-        const int kv0 = (j_lo + t) * BKV;
+        for (int x = 0; x < D / 64; ++x)
+          tma_load_4d(sQ + w * C::kTile + x * kBox, &tmQ, q_full, x * 64, qtl[w].h, qtl[w].qt * BQ, b);
+      }
+      for (int i = 0; i < n && ok; ++i) {
+        const int st = i & 1;
+        const uint32_t par = ((i >> 1) - 1) & 1;
+        const int kv0 = (t_lo + i) * BKV;
+        if (i >= 2 && !mbar_wait_bounded(&k_empty[st], par, abort_flag)) { ok = false; break; }
         mbar_arrive_expect_tx(&k_full[st], C::kTile);
 #pragma unroll
         for (int x = 0; x < D / 64; ++x)
           tma_load_4d(sK + st * C::kTile + x * kBox, &tmK, &k_full[st], x * 64, hk, kv0, b);
+        kin |= 1u << st;
+        kpar = (kpar & ~(1u << st)) | (((i >> 1) & 1u) << st);
+        if (i >= 2 && !mbar_wait_bounded(&v_empty[st], par, abort_flag)) { ok = false; break; }
         mbar_arrive_expect_tx(&v_full[st], C::kTile);
 #pragma unroll
         for (int x = 0; x < D / 64; ++x)
           tma_load_4d(sV + st * C::kTile + x * kBox, &tmV, &v_full[st], x * 64, hk, kv0, b);
-        issued |= 1u << st;
-        par = (par & ~(1u << st)) | (((t >> 1) & 1u) << st);
+        vin |= 1u << st;
+        vpar = (vpar & ~(1u << st)) | (((i >> 1) & 1u) << st);
       }
       if (!ok) {
+        record_status(a.status, kTimeoutSmemEmpty);
+        *abort_flag = 1;
         mbar_wait_bounded(q_full, 0, nullptr);
-        for (int st = 0; st < 2; ++st)
-          if ((issued >> st) & 1u) {
-            if (!mbar_wait_bounded(&k_full[st], (par >> st) & 1u, nullptr) ||
-                !mbar_wait_bounded(&v_full[st], (par >> st) & 1u, nullptr))
-              record_status(a.status, kTimeoutDrain);
-          }
+        for (int st = 0; st < 2; ++st) {
+          if (((kin >> st) & 1u) && !mbar_wait_bounded(&k_full[st], (kpar >> st) & 1u, nullptr))
+            record_status(a.status, kTimeoutDrain);
+          if (((vin >> st) & 1u) && !mbar_wait_bounded(&v_full[st], (vpar >> st) & 1u, nullptr))
+            record_status(a.status, kTimeoutDrain);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0 && n > 0) {
-      constexpr uint32_t idesc_s = make_idesc_bf16_f32(128, 128, false, false);
-      constexpr uint32_t idesc_o = make_idesc_bf16_f32(128, D, false, true);
-      const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP);
-      bool ok = mbar_wait_bounded(q_full, 0, abort_flag);
-      auto issue_s = [&](int t) -> bool {
-        const int st = t & 1;
-        if (!mbar_wait_bounded(&k_full[st], (t >> 1) & 1, abort_flag)) return false;
-        if (t >= 2 && !mbar_wait_bounded(&s_free[st], ((t >> 1) - 1) & 1, abort_flag)) return false;
-        tc_fence_after();
+      constexpr uint32_t id_s = make_idesc_bf16_f32(128, 128, false, false);
+      constexpr uint32_t id_o = make_idesc_bf16_f32(128, D, false, true);
+      const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV);
+      auto act = [&](int w, int t) { return t >= qtl[w].lo && t <= qtl[w].hi; };
+      auto issue_s = [&](int w, int i) {
+        const int st = i & 1;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
-          tc_mma_ss(tmem + st * 128, desc_kmajor(aQ, kk), desc_kmajor(aK + st * C::kTile, kk),
-                    idesc_s, kk > 0 ? 1u : 0u);
-        tc_commit(&s_full[st]);
-        return true;
+          tc_mma_ss(tmem + w * 128, desc_kmajor(aQ + w * C::kTile, kk),
+                    desc_kmajor(aK + st * C::kTile, kk), id_s, kk > 0 ? 1u : 0u);
+        tc_commit(&s_full[w]);
       };
-      if (ok) ok = issue_s(0);
-      for (int t = 0; t < n && ok; ++t) {
-        if (t + 1 < n && !(ok = issue_s(t + 1))) break;
-        if (!mbar_wait_bounded(p_full, t & 1, abort_flag) ||
-            !mbar_wait_bounded(&v_full[t & 1], (t >> 1) & 1, abort_flag)) {
-          ok = false;
-          break;
-        }
+      bool ok = mbar_wait_bounded(q_full, 0, abort_flag) && mbar_wait_bounded(&k_full[0], 0, abort_flag);
+      if (ok) {
         tc_fence_after();
+        for (int w = 0; w < 2; ++w)
+          if (act(w, t_lo)) issue_s(w, 0);
+        tc_commit(&k_empty[0]);
+      }
+      for (int i = 0; i < n && ok; ++i) {
+        const int t = t_lo + i, st = i & 1;
+        if (!mbar_wait_bounded(&v_full[st], (i >> 1) & 1, abort_flag)) { ok = false; break; }
+        bool k_next = false;
+        for (int w = 0; w < 2 && ok; ++w) {
+          if (act(w, t)) {
+            const int u = t - qtl[w].lo;
+            if (!mbar_wait_bounded(&p_full[w], u & 1, abort_flag)) { ok = false; break; }
+            tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk)
-          tc_mma_ss(tmem + C::kTmemO, desc_kmajor(aP, kk), desc_mnmajor(aV + (t & 1) * C::kTile, kk),
-                    idesc_o, (t > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(o_done);
-        tc_commit(&kv_empty[t & 1]);
+            for (int kk = 0; kk < BKV / 16; ++kk)
+              tc_mma_ts(tmem + C::kTO + w * D, tmem + w * 128 + kk * 8,
+                        desc_mnmajor(aV + st * C::kTile, kk), id_o, (u > 0 || kk > 0) ? 1u : 0u);
+          }
+          if (i + 1 < n && act(w, t + 1)) {
+            if (!k_next) {
+              if (!mbar_wait_bounded(&k_full[(i + 1) & 1], ((i + 1) >> 1) & 1, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              k_next = true;
+            }
+            issue_s(w, i + 1);
+          }
+        }
+        if (!ok) break;
+        tc_commit(&v_empty[st]);
+        if (i + 1 < n) tc_commit(&k_empty[(i + 1) & 1]);
       }
       if (!ok) {
         record_status(a.status, kTimeoutTmaFull);
         *abort_flag = 1;
       }
+      tc_commit(&o_done[0]);
+      tc_commit(&o_done[1]);
       tc_commit(mma_done);
       if (!mbar_wait_bounded(mma_done, 0, nullptr)) record_status(a.status, kTimeoutDrain);
     }
   } else {
-    // ------------------------------------------------------ softmax warps
+    // ------------------------------------------------------ softmax groups
+    const int w = (warp - 2) >> 2;
+    const QTile me = qtl[w];
+    const int nw = me.hi - me.lo + 1;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
+    const int q0 = me.qt * BQ;
     const int qi = q0 + r;
-    const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const uint32_t tS = lane_base + w * 128;
+    const uint32_t tO = lane_base + C::kTO + w * D;
     const float scale2 = a.scale * kLog2e;
     float m = -INFINITY, l = 0.f;
-    bool ok = n > 0;
-    for (int t = 0; t < n && ok; ++t) {
-      const int buf = t & 1;
-      if (!mbar_wait_bounded(&s_full[buf], (t >> 1) & 1, abort_flag)) {
+    bool ok = true;
+    for (int u = 0; u < nw && ok; ++u) {
+      const int t = me.lo + u;
+      if (!mbar_wait_bounded(&s_full[w], u & 1, abort_flag)) {
         record_status(a.status, kTimeoutAccFull);
         *abort_flag = 1;
         ok = false;
         break;
       }
       tc_fence_after();
-      float s[BKV];
-#pragma unroll
-      for (int c = 0; c < BKV / 32; ++c) {
-        uint32_t u[32];
-        __syncwarp();
-        tmem_ld_32x32b_x32(trow + buf * 128 + c * 32, u);
-        tmem_ld_wait();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(u[e]);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[buf]);
-
-      const int kv0 = (j_lo + t) * BKV;
-      const bool need_mask = (a.causal && kv0 + BKV - 1 > q0) || (kv0 + BKV > a.S) ||
-                             (a.window > 0 && q0 + BQ - 1 - kv0 >= a.window);
+      const int kv0 = t * BKV;
+      const bool edge = (a.causal && kv0 + BKV - 1 > q0) | (kv0 + BKV > a.S) |
+                        (a.window > 0 && q0 + BQ - 1 - kv0 >= a.window);
+      // pass 1 over the TMEM row: max of the (masked) raw scores
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < BKV; ++c) {
-        float v = s[c] * scale2;
-        if (need_mask && !key_ok(qi, kv0 + c, a.S, a.causal, a.window)) v = -INFINITY;
-        s[c] = v;
-        mx = fmaxf(mx, v);
-      }
-      const float m_new = fmaxf(m, mx);
-      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      const float alpha = exp2f(m - m_use);
-      float rs = 0.f;
+      for (int c = 0; c < BKV / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tS + c * 32, v);
+        tmem_ld_wait();
 #pragma unroll
-      for (int c = 0; c < BKV; ++c) {
-        s[c] = exp2f(s[c] - m_use);
-        rs += s[c];
+        for (int e = 0; e < 32; ++e) {
+          float x = __uint_as_float(v[e]);
+          if (edge) {
+            const int ki = kv0 + c * 32 + e;
+            const bool ok_k = (ki < a.S) & (qi < a.S) & (!a.causal | (ki <= qi)) &
+                              ((a.window <= 0) | (qi - ki < a.window));
+            x = ok_k ? x : -INFINITY;
+          }
+          mx = fmaxf(mx, x);
+        }
+      }
+      const float mx2 = mx * scale2;
+      float m_new = m;
+      if (mx2 > m + kRescale) m_new = mx2;  // also taken on the first tile (m = -inf)
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      const float alpha = (m_new == m) ? 1.f : exp2f(m - m_use);
+      // pass 2: p = exp2(s * scale2 - m), packed two bf16 per 32-bit word
+      float rs = 0.f;
+      uint32_t pk[BKV / 2];
+#pragma unroll
+      for (int c = 0; c < BKV / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tS + c * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float p0 = exp2f(fmaf(__uint_as_float(v[e]), scale2, -m_use));
+          float p1 = exp2f(fmaf(__uint_as_float(v[e + 1]), scale2, -m_use));
+          if (edge) {
+            const int ka = kv0 + c * 32 + e, kb = ka + 1;
+            const bool oa = (ka < a.S) & (qi < a.S) & (!a.causal | (ka <= qi)) &
+                            ((a.window <= 0) | (qi - ka < a.window));
+            const bool ob = (kb < a.S) & (qi < a.S) & (!a.causal | (kb <= qi)) &
+                            ((a.window <= 0) | (qi - kb < a.window));
+            p0 = oa ? p0 : 0.f;
+            p1 = ob ? p1 : 0.f;
+          }
+          rs += p0 + p1;
+          pk[c * 16 + e / 2] = pack_bf16x2(p0, p1);
+        }
       }
       l = l * alpha + rs;
       m = m_new;
-      if (t > 0) {
-        if (!mbar_wait_bounded(o_done, (t - 1) & 1, abort_flag)) {
-          record_status(a.status, kTimeoutAccFull);
-          *abort_flag = 1;
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+      tmem_st_32x32b_x32(tS, *reinterpret_cast<const uint32_t(*)[32]>(pk));
+      tmem_st_32x32b_x32(tS + 32, *reinterpret_cast<const uint32_t(*)[32]>(pk + 32));
+      if (u > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t u[32];
-            tmem_ld_32x32b_x32(trow + C::kTmemO + c * 32, u);
-            tmem_ld_wait();
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tO + c * 32, v);
+          tmem_ld_wait();
 #pragma unroll
-            for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * alpha);
-            tmem_st_32x32b_x32(trow + C::kTmemO + c * 32, u);
-          }
-          tmem_st_wait();
+          for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+          tmem_st_32x32b_x32(tO + c * 32, v);
         }
       }
-      // P (bf16) into the swizzled K-major tile, row r
-#pragma unroll
-      for (int c16 = 0; c16 < BKV / 8; ++c16) {
-        uint4 w;
-        w.x = pack_bf16x2(s[c16 * 8 + 0], s[c16 * 8 + 1]);
-        w.y = pack_bf16x2(s[c16 * 8 + 2], s[c16 * 8 + 3]);
-        w.z = pack_bf16x2(s[c16 * 8 + 4], s[c16 * 8 + 5]);
-        w.w = pack_bf16x2(s[c16 * 8 + 6], s[c16 * 8 + 7]);
-        *reinterpret_cast<uint4*>(sP + swz_off(r, c16)) = w;
-      }
-      fence_proxy_async_smem();
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(&p_full[w]);
     }
-    if (ok && mbar_wait_bounded(o_done, (n - 1) & 1, abort_flag)) {
-      tc_fence_after();
-      const float inv_l = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(a.o) +
-                            (static_cast<long long>(b) * a.S + qi) * a.o_row + h * D;
+    if (ok && nw > 0) {
+      if (mbar_wait_bounded(&o_done[w], 0, abort_flag)) {
+        tc_fence_after();
+        const float inv_l = l > 0.f ? 1.f / l : 0.f;
+        __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(a.o) +
+                              (static_cast<long long>(b) * a.S + qi) * a.o_row + me.h * D;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t u[32];
-        __syncwarp();
-        tmem_ld_32x32b_x32(trow + C::kTmemO + c * 32, u);
-        tmem_ld_wait();
-        if (qi < a.S) {
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tO + c * 32, v);
+          tmem_ld_wait();
+          if (qi < a.S) {
 #pragma unroll
-          for (int e = 0; e < 32; e += 8) {
-            uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(u[e]) * inv_l, __uint_as_float(u[e + 1]) * inv_l);
-            w.y = pack_bf16x2(__uint_as_float(u[e + 2]) * inv_l, __uint_as_float(u[e + 3]) * inv_l);
-            w.z = pack_bf16x2(__uint_as_float(u[e + 4]) * inv_l, __uint_as_float(u[e + 5]) * inv_l);
-            w.w = pack_bf16x2(__uint_as_float(u[e + 6]) * inv_l, __uint_as_float(u[e + 7]) * inv_l);
-            *reinterpret_cast<uint4*>(orow + c * 32 + e) = w;
+            for (int e = 0; e < 32; e += 8) {
+              uint4 q4;
+              q4.x = pack_bf16x2(__uint_as_float(v[e]) * inv_l, __uint_as_float(v[e + 1]) * inv_l);
+              q4.y = pack_bf16x2(__uint_as_float(v[e + 2]) * inv_l, __uint_as_float(v[e + 3]) * inv_l);
+              q4.z = pack_bf16x2(__uint_as_float(v[e + 4]) * inv_l, __uint_as_float(v[e + 5]) * inv_l);
+              q4.w = pack_bf16x2(__uint_as_float(v[e + 6]) * inv_l, __uint_as_float(v[e + 7]) * inv_l);
+              *reinterpret_cast<uint4*>(orow + c * 32 + e) = q4;
+            }
           }
         }
+        if (qi < a.S)
+          a.lse[(static_cast<long long>(b) * a.Hq + me.h) * a.S + qi] =
+              (l > 0.f) ? (m + log2f(l)) * kLn2 : -INFINITY;
+      } else {
+        record_status(a.status, kTimeoutAccFull);
+        *abort_flag = 1;
       }
-      if (qi < a.S)
-        a.lse[(static_cast<long long>(b) * a.Hq + h) * a.S + qi] =
-            (l > 0.f) ? (m + log2f(l)) * kLn2 : -INFINITY;
-    } else if (ok) {
-      record_status(a.status, kTimeoutAccFull);
-      *abort_flag = 1;
     }
   }
   __syncthreads();
@@ -350,48 +423,60 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // -------------------------------------------------------------------- backward
+// One CTA per (128-key tile, kv head, batch), looping over the q heads of the
+// GQA group and the q tiles that see the keys. Two softmax-gradient groups
+// split the 128 query columns of each tile (group w owns columns 64w..64w+63):
+//   S^T = K Q^T -> TMEM; P^T = exp2(S^T - lse) written over S^T in TMEM (bf16)
+//   dP^T = V dO^T -> TMEM; dS^T = P^T (dP^T - delta) * scale -> smem (bf16)
+//   dV += P^T dO  (A operand from TMEM),  dK += dS^T Q,  dQ_i = dS K -> TMEM
+// dV/dK accumulate in TMEM for the whole loop; dQ_i goes out through fp32
+// vector atomics. Q/dO tiles are double-buffered; lse/delta are staged in smem
+// one iteration ahead.
+constexpr int kBwdThreads = 320;
+
 template <int D>
-struct BwdCfg {
+struct Bwd {
   static constexpr int kTile = 128 * D * 2;
   static constexpr int kK = 0;
   static constexpr int kV = kTile;
-  static constexpr int kQ = 2 * kTile;
-  static constexpr int kDO = 3 * kTile;
-  static constexpr int kPt = 4 * kTile;               // [128 kv x 128 q] bf16
-  static constexpr int kDSt = kPt + 128 * 128 * 2;    // [128 kv x 128 q] bf16
-  static constexpr int kLse = kDSt + 128 * 128 * 2;   // float [2][128]
-  static constexpr int kDelta = kLse + 2 * 128 * 4;   // float [2][128]
+  static constexpr int kQ = 2 * kTile;       // two stages
+  static constexpr int kDO = 4 * kTile;      // two stages
+  static constexpr int kDS = 6 * kTile;      // [128 kv x 128 q] bf16
+  static constexpr int kLse = kDS + 128 * 128 * 2;  // float [2][128]
+  static constexpr int kDelta = kLse + 2 * 128 * 4;
   static constexpr int kBar = kDelta + 2 * 128 * 4;
-  static constexpr int kSmem = kBar + 256 + 1024;
+  static constexpr int kSmem = kBar + 256;
   static constexpr int kTS = 0, kTdP = 128, kTdV = 256, kTdK = 256 + D;
 };
 
 template <int D>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                     AttnBwdArgs g) {
-  using C = BwdCfg<D>;
+  using C = Bwd<D>;
   const AttnArgs& a = g.f;
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = align1024(smem_raw);
+  extern __shared__ __align__(1024) uint8_t smem[];
+  if (smem_u32(smem) & 1023) {
+    if (threadIdx.x == 0) record_status(a.status, kBadArgument);
+    return;
+  }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBar);
   uint64_t* kv_full = bars + 0;
-  uint64_t* qd_full = bars + 1;
-  uint64_t* qd_empty = bars + 2;
-  uint64_t* s_full = bars + 3;
-  uint64_t* s_free = bars + 4;
-  uint64_t* p_full = bars + 5;
-  uint64_t* dq_full = bars + 6;
-  uint64_t* dq_free = bars + 7;
-  uint64_t* mma_done = bars + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  uint64_t* qd_full = bars + 1;   // [2]
+  uint64_t* qd_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* p_full = bars + 6;
+  uint64_t* dq_full = bars + 7;
+  uint64_t* dq_free = bars + 8;
+  uint64_t* mma_done = bars + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* s_lse = reinterpret_cast<float*>(smem + C::kLse);
   float* s_delta = reinterpret_cast<float*>(smem + C::kDelta);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int jt = blockIdx.x;  // key tile; small j has the most causal work: scheduled first
+  const int jt = blockIdx.x;
   const int hk = blockIdx.y, b = blockIdx.z;
   const int G = a.Hq / a.Hk;
   const int kv0 = jt * BKV;
@@ -404,13 +489,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    mbar_init(qd_full, 1);
-    mbar_init(qd_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qd_full[i], 1);
+      mbar_init(&qd_empty[i], 1);
+    }
     mbar_init(s_full, 1);
-    mbar_init(s_free, 4);
-    mbar_init(p_full, 4);
+    mbar_init(p_full, 8);
     mbar_init(dq_full, 1);
-    mbar_init(dq_free, 4);
+    mbar_init(dq_free, 8);
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -426,8 +512,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sV = smem + C::kV;
   uint8_t* sQ = smem + C::kQ;
   uint8_t* sDO = smem + C::kDO;
-  uint8_t* sPt = smem + C::kPt;
-  uint8_t* sDSt = smem + C::kDSt;
+  uint8_t* sDS = smem + C::kDS;
 
   auto it_head = [&](int it) { return hk * G + it % G; };
   auto it_q0 = [&](int it) { return (i_lo + it / G) * BQ; };
@@ -435,8 +520,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     if (lane == 0 && n_it > 0) {
       bool ok = true;
-      bool q_inflight = false;
-      uint32_t q_par = 0;
+      uint32_t qin = 0, qpar = 0;
       mbar_arrive_expect_tx(kv_full, 2 * C::kTile);
 #pragma unroll
       for (int x = 0; x < D / 64; ++x) {
@@ -444,73 +528,67 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_4d(sV + x * kBox, &tmV, kv_full, x * 64, hk, kv0, b);
       }
       for (int it = 0; it < n_it && ok; ++it) {
-        if (it > 0 && !mbar_wait_bounded(qd_empty, (it - 1) & 1, abort_flag)) {
-          record_status(a.status, kTimeoutSmemEmpty);
-          *abort_flag = 1;
+        const int st = it & 1;
+        if (it >= 2 && !mbar_wait_bounded(&qd_empty[st], ((it >> 1) - 1) & 1, abort_flag)) {
           ok = false;
           break;
         }
         const int h = it_head(it), q0 = it_q0(it);
-        mbar_arrive_expect_tx(qd_full, 2 * C::kTile);
+        mbar_arrive_expect_tx(&qd_full[st], 2 * C::kTile);
 #pragma unroll
         for (int x = 0; x < D / 64; ++x) {
-          tma_load_4d(sQ + x * kBox, &tmQ, qd_full, x * 64, h, q0, b);
-          tma_load_4d(sDO + x * kBox, &tmDO, qd_full, x * 64, h, q0, b);
+          tma_load_4d(sQ + st * C::kTile + x * kBox, &tmQ, &qd_full[st], x * 64, h, q0, b);
+          tma_load_4d(sDO + st * C::kTile + x * kBox, &tmDO, &qd_full[st], x * 64, h, q0, b);
         }
-        q_inflight = true;
-        q_par = it & 1;
+        qin |= 1u << st;
+        qpar = (qpar & ~(1u << st)) | (((it >> 1) & 1u) << st);
       }
       if (!ok) {
+        record_status(a.status, kTimeoutSmemEmpty);
+        *abort_flag = 1;
         if (!mbar_wait_bounded(kv_full, 0, nullptr)) record_status(a.status, kTimeoutDrain);
-        if (q_inflight && !mbar_wait_bounded(qd_full, q_par, nullptr))
-          record_status(a.status, kTimeoutDrain);
+        for (int st = 0; st < 2; ++st)
+          if (((qin >> st) & 1u) && !mbar_wait_bounded(&qd_full[st], (qpar >> st) & 1u, nullptr))
+            record_status(a.status, kTimeoutDrain);
       }
     }
   } else if (warp == 1) {
     if (lane == 0 && n_it > 0) {
       constexpr uint32_t id_sq = make_idesc_bf16_f32(128, 128, false, false);  // S^T, dP^T
-      constexpr uint32_t id_kv = make_idesc_bf16_f32(128, D, false, true);     // dV, dK
+      constexpr uint32_t id_v = make_idesc_bf16_f32(128, D, false, true);      // dV (A in TMEM), dK
       constexpr uint32_t id_dq = make_idesc_bf16_f32(128, D, true, true);      // dQ
       const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), aDO = smem_u32(sDO);
-      const uint32_t aPt = smem_u32(sPt), aDS = smem_u32(sDSt);
+      const uint32_t aDS = smem_u32(sDS);
       bool ok = mbar_wait_bounded(kv_full, 0, abort_flag);
       for (int it = 0; it < n_it && ok; ++it) {
-        const uint32_t par = it & 1, ppar = (it - 1) & 1;
-        if (!mbar_wait_bounded(qd_full, par, abort_flag) ||
-            (it > 0 && !mbar_wait_bounded(s_free, ppar, abort_flag))) {
-          ok = false;
-          break;
-        }
+        const int st = it & 1;
+        if (!mbar_wait_bounded(&qd_full[st], (it >> 1) & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
-          tc_mma_ss(tmem + C::kTS, desc_kmajor(aK, kk), desc_kmajor(aQ, kk), id_sq, kk > 0);
-        if (it > 0 && !mbar_wait_bounded(dq_free, ppar, abort_flag)) {
-          ok = false;
-          break;
-        }
+          tc_mma_ss(tmem + C::kTS, desc_kmajor(aK, kk), desc_kmajor(aQ + st * C::kTile, kk), id_sq,
+                    kk > 0 ? 1u : 0u);
+        if (it > 0 && !mbar_wait_bounded(dq_free, (it - 1) & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
-          tc_mma_ss(tmem + C::kTdP, desc_kmajor(aV, kk), desc_kmajor(aDO, kk), id_sq, kk > 0);
+          tc_mma_ss(tmem + C::kTdP, desc_kmajor(aV, kk), desc_kmajor(aDO + st * C::kTile, kk), id_sq,
+                    kk > 0 ? 1u : 0u);
         tc_commit(s_full);
-        if (!mbar_wait_bounded(p_full, par, abort_flag)) {
-          ok = false;
-          break;
-        }
+        if (!mbar_wait_bounded(p_full, it & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk) {
-          tc_mma_ss(tmem + C::kTdV, desc_kmajor(aPt, kk), desc_mnmajor(aDO, kk), id_kv,
+          tc_mma_ts(tmem + C::kTdV, tmem + C::kTS + kk * 8, desc_mnmajor(aDO + st * C::kTile, kk), id_v,
                     (it > 0 || kk > 0) ? 1u : 0u);
-          tc_mma_ss(tmem + C::kTdK, desc_kmajor(aDS, kk), desc_mnmajor(aQ, kk), id_kv,
+          tc_mma_ss(tmem + C::kTdK, desc_kmajor(aDS, kk), desc_mnmajor(aQ + st * C::kTile, kk), id_v,
                     (it > 0 || kk > 0) ? 1u : 0u);
         }
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk)
           tc_mma_ss(tmem + C::kTdP, desc_mnmajor(aDS, kk), desc_mnmajor(aK, kk), id_dq, kk > 0);
         tc_commit(dq_full);
-        tc_commit(qd_empty);
+        tc_commit(&qd_empty[st]);
       }
       if (!ok) {
         record_status(a.status, kTimeoutTmaFull);
@@ -520,23 +598,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait_bounded(mma_done, 0, nullptr)) record_status(a.status, kTimeoutDrain);
     }
   } else {
-    // -------------------------------------------------- softmax-grad warps
+    // ---------------------------------------------- softmax-gradient groups
+    const int w = (warp - 2) >> 2;          // query columns 64w .. 64w+63
+    const int tid = threadIdx.x - 64;       // 0..255 over both groups
     const int quad = warp & 3;
-    const int r = quad * 32 + lane;  // key row (S^T, dP^T) / query row (dQ)
+    const int r = quad * 32 + lane;         // key row (S^T, dP^T, dV, dK) / query row (dQ)
     const int ki = kv0 + r;
-    const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     const float scale2 = a.scale * kLog2e;
+    // stage iteration 0's lse / delta
+    float nxt = 0.f;
+    auto fetch = [&](int it) -> float {
+      const int h = it_head(it), qrow = it_q0(it) + (tid & 127);
+      const long long li = (static_cast<long long>(b) * a.Hq + h) * a.S + qrow;
+      if (tid < 128) return qrow < a.S ? a.lse[li] * kLog2e : INFINITY;
+      return qrow < a.S ? g.delta[li] : 0.f;
+    };
+    if (n_it > 0) nxt = fetch(0);
     bool ok = true;
     for (int it = 0; it < n_it && ok; ++it) {
-      const int h = it_head(it), q0 = it_q0(it);
       const int buf = it & 1;
-      {
-        const int qrow = q0 + r;
-        const long long li = (static_cast<long long>(b) * a.Hq + h) * a.S + qrow;
-        s_lse[buf * 128 + r] = qrow < a.S ? a.lse[li] * kLog2e : INFINITY;
-        s_delta[buf * 128 + r] = qrow < a.S ? g.delta[li] : 0.f;
-      }
-      named_bar_sync(1, 128);
+      const int q0 = it_q0(it), h = it_head(it);
+      if (tid < 128) s_lse[buf * 128 + tid] = nxt;
+      else s_delta[buf * 128 + tid - 128] = nxt;
+      named_bar_sync(1, 256);
+      if (it + 1 < n_it) nxt = fetch(it + 1);
       if (!mbar_wait_bounded(s_full, it & 1, abort_flag)) {
         record_status(a.status, kTimeoutAccFull);
         *abort_flag = 1;
@@ -544,47 +630,50 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const bool need_mask = (a.causal && q0 < kv0 + BKV - 1) || (kv0 + BKV > a.S) ||
-                             (q0 + BQ > a.S) || (a.window > 0 && q0 + BQ - 1 - kv0 >= a.window);
-#pragma unroll 1
-      for (int c = 0; c < BQ / 32; ++c) {
+      const bool edge = (a.causal && q0 < kv0 + BKV - 1) | (kv0 + BKV > a.S) | (q0 + BQ > a.S) |
+                        (a.window > 0 && q0 + BQ - 1 - kv0 >= a.window);
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c0 = w * 64 + cc * 32;  // query column of this chunk
         uint32_t us[32], ud[32];
-        __syncwarp();
-        tmem_ld_32x32b_x32(trow + C::kTS + c * 32, us);
-        tmem_ld_32x32b_x32(trow + C::kTdP + c * 32, ud);
+        tmem_ld_32x32b_x32(lane_base + C::kTS + c0, us);
+        tmem_ld_32x32b_x32(lane_base + C::kTdP + c0, ud);
         tmem_ld_wait();
-        float p[32], ds[32];
+        uint32_t pp[16];
+        float ds[32];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int qc = c * 32 + e;
-          float pv = exp2f(__uint_as_float(us[e]) * scale2 - s_lse[buf * 128 + qc]);
-          if (need_mask && !key_ok(q0 + qc, ki, a.S, a.causal, a.window)) pv = 0.f;
-          p[e] = pv;
-          ds[e] = pv * (__uint_as_float(ud[e]) - s_delta[buf * 128 + qc]) * a.scale;
+        for (int e = 0; e < 32; e += 2) {
+          float p0 = exp2f(fmaf(__uint_as_float(us[e]), scale2, -s_lse[buf * 128 + c0 + e]));
+          float p1 = exp2f(fmaf(__uint_as_float(us[e + 1]), scale2, -s_lse[buf * 128 + c0 + e + 1]));
+          if (edge) {
+            const int qa = q0 + c0 + e, qb = qa + 1;
+            const bool oa = (ki < a.S) & (qa < a.S) & (!a.causal | (ki <= qa)) &
+                            ((a.window <= 0) | (qa - ki < a.window));
+            const bool ob = (ki < a.S) & (qb < a.S) & (!a.causal | (ki <= qb)) &
+                            ((a.window <= 0) | (qb - ki < a.window));
+            p0 = oa ? p0 : 0.f;
+            p1 = ob ? p1 : 0.f;
+          }
+          pp[e / 2] = pack_bf16x2(p0, p1);
+          ds[e] = p0 * (__uint_as_float(ud[e]) - s_delta[buf * 128 + c0 + e]) * a.scale;
+          ds[e + 1] = p1 * (__uint_as_float(ud[e + 1]) - s_delta[buf * 128 + c0 + e + 1]) * a.scale;
         }
+        tmem_st_32x32b_x16(lane_base + C::kTS + c0 / 2, pp);
 #pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          const int c16 = c * 4 + w;
-          uint4 pp, dd;
-          pp.x = pack_bf16x2(p[w * 8 + 0], p[w * 8 + 1]);
-          pp.y = pack_bf16x2(p[w * 8 + 2], p[w * 8 + 3]);
-          pp.z = pack_bf16x2(p[w * 8 + 4], p[w * 8 + 5]);
-          pp.w = pack_bf16x2(p[w * 8 + 6], p[w * 8 + 7]);
-          dd.x = pack_bf16x2(ds[w * 8 + 0], ds[w * 8 + 1]);
-          dd.y = pack_bf16x2(ds[w * 8 + 2], ds[w * 8 + 3]);
-          dd.z = pack_bf16x2(ds[w * 8 + 4], ds[w * 8 + 5]);
-          dd.w = pack_bf16x2(ds[w * 8 + 6], ds[w * 8 + 7]);
-          *reinterpret_cast<uint4*>(sPt + swz_off(r, c16)) = pp;
-          *reinterpret_cast<uint4*>(sDSt + swz_off(r, c16)) = dd;
+        for (int j = 0; j < 4; ++j) {
+          uint4 d4;
+          d4.x = pack_bf16x2(ds[j * 8 + 0], ds[j * 8 + 1]);
+          d4.y = pack_bf16x2(ds[j * 8 + 2], ds[j * 8 + 3]);
+          d4.z = pack_bf16x2(ds[j * 8 + 4], ds[j * 8 + 5]);
+          d4.w = pack_bf16x2(ds[j * 8 + 6], ds[j * 8 + 7]);
+          *reinterpret_cast<uint4*>(sDS + swz_off(r, c0 / 8 + j)) = d4;
         }
       }
+      tmem_st_wait();
+      fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(s_free);
-      fence_proxy_async_smem();
-      __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
-      // dQ_i readout: TMEM lane r is query row q0 + r
       if (!mbar_wait_bounded(dq_full, it & 1, abort_flag)) {
         record_status(a.status, kTimeoutAccFull);
         *abort_flag = 1;
@@ -595,62 +684,54 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int qrow = q0 + r;
       float* dqr = g.dq_acc + ((static_cast<long long>(b) * a.S + qrow) * a.Hq + h) * D;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t u[32];
-        __syncwarp();
-        tmem_ld_32x32b_x32(trow + C::kTdP + c * 32, u);
+      for (int c = w * (D / 2); c < (w + 1) * (D / 2); c += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(lane_base + C::kTdP + c, v);
         tmem_ld_wait();
         if (qrow < a.S) {
 #pragma unroll
           for (int e = 0; e < 32; e += 4)
-            atomicAdd(reinterpret_cast<float4*>(dqr + c * 32 + e),
-                      make_float4(__uint_as_float(u[e]), __uint_as_float(u[e + 1]),
-                                  __uint_as_float(u[e + 2]), __uint_as_float(u[e + 3])));
+            atomicAdd(reinterpret_cast<float4*>(dqr + c + e),
+                      make_float4(__uint_as_float(v[e]), __uint_as_float(v[e + 1]),
+                                  __uint_as_float(v[e + 2]), __uint_as_float(v[e + 3])));
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_free);
     }
-    // dK, dV for this key tile (all MMAs finished: the last dq_full was observed)
-    if (ok && n_it > 0) {
+    if (ok && ki < a.S) {
       __nv_bfloat16* dkr = reinterpret_cast<__nv_bfloat16*>(g.dk) +
                            (static_cast<long long>(b) * a.S + ki) * g.dk_row + hk * D;
       __nv_bfloat16* dvr = reinterpret_cast<__nv_bfloat16*>(g.dv) +
                            (static_cast<long long>(b) * a.S + ki) * g.dv_row + hk * D;
+      if (n_it > 0) {
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t u[32], w32[32];
-        __syncwarp();
-        tmem_ld_32x32b_x32(trow + C::kTdV + c * 32, u);
-        tmem_ld_32x32b_x32(trow + C::kTdK + c * 32, w32);
-        tmem_ld_wait();
-        if (ki < a.S) {
+        for (int c = w * (D / 2); c < (w + 1) * (D / 2); c += 32) {
+          uint32_t u[32], v[32];
+          tmem_ld_32x32b_x32(lane_base + C::kTdV + c, u);
+          tmem_ld_32x32b_x32(lane_base + C::kTdK + c, v);
+          tmem_ld_wait();
 #pragma unroll
           for (int e = 0; e < 32; e += 8) {
-            uint4 vv, kk4;
-            vv.x = pack_bf16x2(__uint_as_float(u[e]), __uint_as_float(u[e + 1]));
-            vv.y = pack_bf16x2(__uint_as_float(u[e + 2]), __uint_as_float(u[e + 3]));
-            vv.z = pack_bf16x2(__uint_as_float(u[e + 4]), __uint_as_float(u[e + 5]));
-            vv.w = pack_bf16x2(__uint_as_float(u[e + 6]), __uint_as_float(u[e + 7]));
-            kk4.x = pack_bf16x2(__uint_as_float(w32[e]), __uint_as_float(w32[e + 1]));
-            kk4.y = pack_bf16x2(__uint_as_float(w32[e + 2]), __uint_as_float(w32[e + 3]));
-            kk4.z = pack_bf16x2(__uint_as_float(w32[e + 4]), __uint_as_float(w32[e + 5]));
-            kk4.w = pack_bf16x2(__uint_as_float(w32[e + 6]), __uint_as_float(w32[e + 7]));
-            *reinterpret_cast<uint4*>(dvr + c * 32 + e) = vv;
-            *reinterpret_cast<uint4*>(dkr + c * 32 + e) = kk4;
+            uint4 a4, b4;
+            a4.x = pack_bf16x2(__uint_as_float(u[e]), __uint_as_float(u[e + 1]));
+            a4.y = pack_bf16x2(__uint_as_float(u[e + 2]), __uint_as_float(u[e + 3]));
+            a4.z = pack_bf16x2(__uint_as_float(u[e + 4]), __uint_as_float(u[e + 5]));
+            a4.w = pack_bf16x2(__uint_as_float(u[e + 6]), __uint_as_float(u[e + 7]));
+            b4.x = pack_bf16x2(__uint_as_float(v[e]), __uint_as_float(v[e + 1]));
+            b4.y = pack_bf16x2(__uint_as_float(v[e + 2]), __uint_as_float(v[e + 3]));
+            b4.z = pack_bf16x2(__uint_as_float(v[e + 4]), __uint_as_float(v[e + 5]));
+            b4.w = pack_bf16x2(__uint_as_float(v[e + 6]), __uint_as_float(v[e + 7]));
+            *reinterpret_cast<uint4*>(dvr + c + e) = a4;
+            *reinterpret_cast<uint4*>(dkr + c + e) = b4;
           }
         }
-      }
-    } else if (n_it == 0 && ki < a.S) {
-      // keys no query attends to (only possible with a window / non-causal edge cases)
-      __nv_bfloat16* dkr = reinterpret_cast<__nv_bfloat16*>(g.dk) +
-                           (static_cast<long long>(b) * a.S + ki) * g.dk_row + hk * D;
-      __nv_bfloat16* dvr = reinterpret_cast<__nv_bfloat16*>(g.dv) +
-                           (static_cast<long long>(b) * a.S + ki) * g.dv_row + hk * D;
-      for (int c = 0; c < D; ++c) {
-        dkr[c] = __float2bfloat16(0.f);
-        dvr[c] = __float2bfloat16(0.f);
+      } else {
+        for (int c = w * (D / 2); c < (w + 1) * (D / 2); ++c) {
+          dkr[c] = __float2bfloat16(0.f);
+          dvr[c] = __float2bfloat16(0.f);
+        }
       }
     }
   }
@@ -735,7 +816,7 @@ static CUtensorMap map_bshd(const void* base, int B, int S, int H, int d, long l
 
 template <int D>
 static void fwd_launch(const AttnArgs& a, cudaStream_t st) {
-  using C = FwdCfg<D>;
+  using C = Fwd<D>;
   CUtensorMap tq = map_bshd(a.q, a.B, a.S, a.Hq, D, a.q_row);
   CUtensorMap tk = map_bshd(a.k, a.B, a.S, a.Hk, D, a.k_row);
   CUtensorMap tv = map_bshd(a.v, a.B, a.S, a.Hk, D, a.v_row);
@@ -745,14 +826,17 @@ static void fwd_launch(const AttnArgs& a, cudaStream_t st) {
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
     set = true;
   }
-  dim3 grid((a.S + BQ - 1) / BQ, a.Hq, a.B);
-  attn_fwd_kernel<D><<<grid, kThreads, C::kSmem, st>>>(tq, tk, tv, a);
+  const int G = a.Hq / a.Hk;
+  const int n_q = (a.S + BQ - 1) / BQ;
+  const int pair_heads = (G % 2 == 0) ? 1 : 0;
+  dim3 grid(pair_heads ? n_q : (n_q + 1) / 2, pair_heads ? a.Hq / 2 : a.Hq, a.B);
+  attn_fwd_kernel<D><<<grid, kFwdThreads, C::kSmem, st>>>(tq, tk, tv, a, pair_heads);
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 
 template <int D>
 static void bwd_launch(const AttnBwdArgs& g, cudaStream_t st) {
-  using C = BwdCfg<D>;
+  using C = Bwd<D>;
   const AttnArgs& a = g.f;
   CUtensorMap tq = map_bshd(a.q, a.B, a.S, a.Hq, D, a.q_row);
   CUtensorMap tk = map_bshd(a.k, a.B, a.S, a.Hk, D, a.k_row);
@@ -770,7 +854,7 @@ static void bwd_launch(const AttnBwdArgs& g, cudaStream_t st) {
       reinterpret_cast<const __nv_bfloat16*>(g.dout), g.do_row, g.delta, a.B, a.S, a.Hq, D);
   PLG_CUDA_CHECK(cudaMemsetAsync(g.dq_acc, 0, sizeof(float) * rows * D, st));
   dim3 grid((a.S + BKV - 1) / BKV, a.Hk, a.B);
-  attn_bwd_kernel<D><<<grid, kThreads, C::kSmem, st>>>(tq, tk, tv, td, g);
+  attn_bwd_kernel<D><<<grid, kBwdThreads, C::kSmem, st>>>(tq, tk, tv, td, g);
   PLG_CUDA_CHECK(cudaGetLastError());
   const long long n = rows * D;
   long long blocks = (n + 255) / 256;

@@ -55,7 +55,8 @@ class RotaryEmbedding(nn.Module):
         key = (position_ids.shape[1], position_ids.device)
         hit = self._cache.get(key)
         if hit is None:
-            hit = self._cos_sin(position_ids)
+            # packed path: every row is arange(S), so one batch-1 table broadcasts to any B
+            hit = self._cos_sin(position_ids[:1])
             self._cache[key] = hit
         return hit
 
@@ -157,8 +158,9 @@ def init_decoder_weights(model: nn.Module, blocks, std: float = 0.02, out_projs=
                 mod.weight.data.mul_(s)
 
 
-def norm_eps(module: nn.RMSNorm) -> float:
-    return FP32_EPS if module.eps is None else float(module.eps)
+def norm_eps(module: nn.RMSNorm, dtype: torch.dtype = torch.float32) -> float:
+    """The eps ``nn.RMSNorm(eps=None)`` resolves to for an input of ``dtype``."""
+    return torch.finfo(dtype).eps if module.eps is None else float(module.eps)
 
 
 def scaled_init_std(d: int) -> float:

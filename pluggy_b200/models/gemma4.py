@@ -72,7 +72,7 @@ class Gemma4RotaryEmbedding(nn.Module):
             return self._cos_sin(pos)
         key = (pos.shape[1], pos.device)
         if key not in self._cache:
-            self._cache[key] = self._cos_sin(pos)
+            self._cache[key] = self._cos_sin(pos[:1])  # batch-1 table broadcasts to any B
         return self._cache[key]
 
 

@@ -104,7 +104,7 @@ class Qwen3(nn.Module):
         g = block.attention
         return _engine.AttnCfg(B=B, S=S, Hq=g.num_heads, Hk=g.num_kv_heads, d=g.head_dim,
                                eps=norm_eps(block.norm1),
-                               qk_eps=norm_eps(g.q_norm) if g.qk_norm else 1e-6,
+                               qk_eps=norm_eps(g.q_norm, torch.bfloat16) if g.qk_norm else 1e-6,
                                qk_norm=g.qk_norm)
 
     def fused_hidden(self, x: torch.Tensor) -> torch.Tensor:

@@ -210,7 +210,7 @@ class Qwen3Moe(nn.Module):
             for i, blk in enumerate(self.blocks):
                 cfg = _engine.AttnCfg(B=B, S=S, Hq=blk.gqa.num_heads, Hk=blk.gqa.num_kv_heads,
                                       d=blk.gqa.head_dim, eps=norm_eps(blk.norm1),
-                                      qk_eps=norm_eps(blk.gqa.q_norm))
+                                      qk_eps=norm_eps(blk.gqa.q_norm, torch.bfloat16))
                 h = blk.fused_forward(h, self.weight_cache, cfg, self.rope.inv_freq, i)
             self._router_logits = self._collect()
             self._update_expert_counts(self._router_logits)

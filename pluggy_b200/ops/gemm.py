@@ -26,8 +26,17 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn_major: bool = False, b_mn_maj
 
     ``a`` is [M, K] (``a_mn_major=False``) or [K, M]; ``b`` is [N, K] or [K, N].
     """
+    if a.dim() != 2 or b.dim() != 2:
+        raise ValueError(f"gemm takes 2-D operands, got {tuple(a.shape)} and {tuple(b.shape)}")
     M = a.shape[1] if a_mn_major else a.shape[0]
+    Ka = a.shape[0] if a_mn_major else a.shape[1]
     N = b.shape[1] if b_mn_major else b.shape[0]
+    Kb = b.shape[0] if b_mn_major else b.shape[1]
+    if Ka != Kb:
+        raise ValueError(f"gemm: reduction dims differ ({Ka} vs {Kb}) for a{tuple(a.shape)} "
+                         f"(mn_major={a_mn_major}) and b{tuple(b.shape)} (mn_major={b_mn_major})")
+    if out is not None and tuple(out.shape) != (M, N):
+        raise ValueError(f"gemm: out must be [{M}, {N}], got {tuple(out.shape)}")
     if not a.is_cuda:
         A = (a.t() if a_mn_major else a).float()
         B = (b.t() if b_mn_major else b).float()

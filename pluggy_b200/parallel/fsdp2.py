@@ -131,6 +131,13 @@ class FSDP2:
     def _group(self):
         return self.mesh.get_group(self.dim)
 
+    @staticmethod
+    def _coalesced(group, unit):
+        """One NCCL group launch per unit; gloo has no coalescing, so plain calls there."""
+        if dist.get_backend(group) == "nccl":
+            return dist._coalescing_manager(group=group, device=unit.flat_shard.device)
+        return contextlib.nullcontext()
+
     def _issue_gather(self, unit: _Unit) -> None:
         """Launch the coalesced all-gather of ``unit`` (on the comm stream on CUDA)."""
         if unit.gathered:
@@ -142,7 +149,7 @@ class FSDP2:
             self._comm_stream.wait_stream(torch.cuda.current_stream())
         with ctx:
             group = self._group()
-            with dist._coalescing_manager(group=group, device=unit.flat_shard.device):
+            with self._coalesced(group, unit):
                 for s in unit.params:
                     dist.all_gather_into_tensor(s.full, s.sharded, group=group)
             if self._cuda:
@@ -216,7 +223,7 @@ class FSDP2:
             for s, g in zip(unit.ready_grads, grads, strict=True):
                 outs.append(torch.empty(s.shard_shape, dtype=g.dtype, device=g.device))
             op = dist.ReduceOp.AVG if nccl else dist.ReduceOp.SUM
-            with dist._coalescing_manager(group=group, device=unit.flat_shard.device):
+            with self._coalesced(group, unit):
                 for g, o in zip(grads, outs, strict=True):
                     dist.reduce_scatter_tensor(o, g.contiguous(), op=op, group=group)
             for s, o in zip(unit.ready_grads, outs, strict=True):

@@ -26,8 +26,10 @@ def _status():
 
 
 # ---------------------------------------------------------------------- GEMM
-GEMM_SHAPES = [(128, 256, 64), (256, 512, 128), (300, 200, 136), (1000, 384, 520), (4096, 4096, 1024),
-               (130, 1030, 72), (8192, 1024, 3072)]
+# every stride must stay 16-byte aligned (multiples of 8 bf16): M, N, K % 8 == 0 where they are
+# a leading dimension; edges that are not multiples of the 128x256x64 tile are exercised
+GEMM_SHAPES = [(128, 256, 64), (256, 512, 128), (296, 200, 136), (1000, 384, 520), (4096, 4096, 1024),
+               (136, 1032, 72), (8192, 1024, 3072), (200, 1000, 8)]
 
 
 @pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
@@ -81,9 +83,19 @@ def test_gemm_split_k_and_accumulate():
     linear_wgrad(dy, x, out=acc, accumulate=True)
     assert rel(acc, ref + 1) < 5e-3
     for s in (1, 3, 7):
-        o = gemm(dy.t().contiguous(), x.t().contiguous(), a_mn_major=True, b_mn_major=True,
-                 out_dtype=torch.float32, splits=s)
+        o = gemm(dy, x, a_mn_major=True, b_mn_major=True, out_dtype=torch.float32, splits=s)
         assert rel(o, ref) < 5e-3, s
+
+
+def test_gemm_rejects_misaligned_and_mismatched():
+    from pluggy_b200.ops.gemm import gemm
+
+    a = torch.randn(64, 100, device=DEV).bfloat16()  # K = 100: rows not 16-byte aligned
+    with pytest.raises(Exception):
+        gemm(a, a)
+    x = torch.randn(64, 128, device=DEV).bfloat16()
+    with pytest.raises(ValueError):
+        gemm(x, torch.randn(64, 256, device=DEV).bfloat16())
 
 
 # ---------------------------------------------------------------- norms, rope
@@ -303,6 +315,11 @@ def test_fused_model_matches_eager(family):
     name = "qwen3_dense" if family == "qwen3" else "llama3_2"
     m = build_model(name, cfg).to(DEV)
     m.init_weights()
+    # the fused path runs q/k norms in bf16 (eps = bf16 eps, as the reference under autocast);
+    # give the fp32 oracle the same eps so both compute the same function
+    for mod in m.modules():
+        if isinstance(mod, torch.nn.RMSNorm) and mod.normalized_shape[0] == cfg["head_dim"]:
+            mod.eps = torch.finfo(torch.bfloat16).eps
     ids = torch.randint(0, 2048, (2, 256), device=DEV)
     batch = {"input_ids": ids, "labels": ids}
     obj = ARObjective(ce_chunk_size=128)
@@ -313,6 +330,9 @@ def test_fused_model_matches_eager(family):
     # eager fp32 reference path: same weights, CPU math
     mc = build_model(name, cfg)
     mc.load_state_dict({k: v.cpu() for k, v in m.state_dict().items()})
+    for mod in mc.modules():
+        if isinstance(mod, torch.nn.RMSNorm) and mod.normalized_shape[0] == cfg["head_dim"]:
+            mod.eps = torch.finfo(torch.bfloat16).eps
     lc = obj.compute_loss(mc, {k: v.cpu() for k, v in batch.items()})
     lc.backward()
     assert abs(loss.item() - lc.item()) < 2e-2 * lc.item()
