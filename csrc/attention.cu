@@ -10,13 +10,8 @@
 // so K and V may be column slices of the fused QKV projection), o [B, S, Hq, d],
 // lse [B, Hq, S] in natural log. d in {64, 128}.
 //
-// Forward, one CTA per (128-query tile, q head, batch), heavy causal tiles first:
-//   warp 0      TMA: Q once, then K_j / V_j into two stages
-//   warp 1      TMEM owner + MMA issuer: S_j = Q K_j^T into one of two S
-//               buffers (so S_{j+1} overlaps the softmax of S_j), O += P_j V_j
-//   warps 2..5  one query row per thread: online softmax in the log2 domain,
-//               P_j (bf16) written to a 128-byte-swizzled smem tile, O rescaled
-//               in TMEM when the row max grows, final O / l and LSE stored.
+// Forward: two query tiles per CTA with one softmax warpgroup each (see the
+// comment above attn_fwd_kernel); P stays in TMEM.
 // Backward, one CTA per (128-key tile, kv head, batch), looping over the q
 // heads of the GQA group and the q tiles that see the keys:
 //   S^T = K Q^T and dP^T = V dO^T into TMEM; per key row: P^T = exp2(S^T - lse),
@@ -57,6 +52,13 @@ __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t base, int kk) {
 // two swizzled boxes
 __device__ __forceinline__ uint32_t swz_off(int r, int c16) {
   return (c16 >> 3) * kBox + r * 128 + (((c16 & 7) ^ (r & 7)) << 4);
+}
+
+// Bounded wait whose outcome is the same on every lane of the warp: a lane that
+// gave up makes the whole warp give up, so the tcgen05 .sync.aligned loads and
+// stores that follow never execute on a partial warp.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, abort_flag)) != 0;
 }
 
 __device__ __forceinline__ bool key_ok(int qi, int ki, int S, int causal, int window) {
@@ -200,14 +202,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const int st = i & 1;
         const uint32_t par = ((i >> 1) - 1) & 1;
         const int kv0 = (t_lo + i) * BKV;
-        if (i >= 2 && !mbar_wait_bounded(&k_empty[st], par, abort_flag)) { ok = false; break; }
+        if (i >= 2 && !mbar_wait_bounded(&k_empty[st], par, abort_flag)) { record_status(a.status, 17); ok = false; break; }
         mbar_arrive_expect_tx(&k_full[st], C::kTile);
 #pragma unroll
         for (int x = 0; x < D / 64; ++x)
           tma_load_4d(sK + st * C::kTile + x * kBox, &tmK, &k_full[st], x * 64, hk, kv0, b);
         kin |= 1u << st;
         kpar = (kpar & ~(1u << st)) | (((i >> 1) & 1u) << st);
-        if (i >= 2 && !mbar_wait_bounded(&v_empty[st], par, abort_flag)) { ok = false; break; }
+        if (i >= 2 && !mbar_wait_bounded(&v_empty[st], par, abort_flag)) { record_status(a.status, 18); ok = false; break; }
         mbar_arrive_expect_tx(&v_full[st], C::kTile);
 #pragma unroll
         for (int x = 0; x < D / 64; ++x)
@@ -250,12 +252,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
       for (int i = 0; i < n && ok; ++i) {
         const int t = t_lo + i, st = i & 1;
-        if (!mbar_wait_bounded(&v_full[st], (i >> 1) & 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait_bounded(&v_full[st], (i >> 1) & 1, abort_flag)) { record_status(a.status, 12); ok = false; break; }
         bool k_next = false;
         for (int w = 0; w < 2 && ok; ++w) {
           if (act(w, t)) {
             const int u = t - qtl[w].lo;
-            if (!mbar_wait_bounded(&p_full[w], u & 1, abort_flag)) { ok = false; break; }
+            if (!mbar_wait_bounded(&p_full[w], u & 1, abort_flag)) { record_status(a.status, 13); ok = false; break; }
             tc_fence_after();
 #pragma unroll
             for (int kk = 0; kk < BKV / 16; ++kk)
@@ -265,6 +267,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           if (i + 1 < n && act(w, t + 1)) {
             if (!k_next) {
               if (!mbar_wait_bounded(&k_full[(i + 1) & 1], ((i + 1) >> 1) & 1, abort_flag)) {
+                record_status(a.status, 14);
                 ok = false;
                 break;
               }
@@ -304,8 +307,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     bool ok = true;
     for (int u = 0; u < nw && ok; ++u) {
       const int t = me.lo + u;
-      if (!mbar_wait_bounded(&s_full[w], u & 1, abort_flag)) {
-        record_status(a.status, kTimeoutAccFull);
+      if (!warp_wait(&s_full[w], u & 1, abort_flag)) {
+        record_status(a.status, 15);
         *abort_flag = 1;
         ok = false;
         break;
@@ -337,7 +340,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       float m_new = m;
       if (mx2 > m + kRescale) m_new = mx2;  // also taken on the first tile (m = -inf)
       const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      const float alpha = (m_new == m) ? 1.f : exp2f(m - m_use);
+      const float alpha = (m_new == m) ? 1.f : fast_exp2(m - m_use);
       // pass 2: p = exp2(s * scale2 - m), packed two bf16 per 32-bit word
       float rs = 0.f;
       uint32_t pk[BKV / 2];
@@ -348,8 +351,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         tmem_ld_wait();
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          float p0 = exp2f(fmaf(__uint_as_float(v[e]), scale2, -m_use));
-          float p1 = exp2f(fmaf(__uint_as_float(v[e + 1]), scale2, -m_use));
+          float p0 = fast_exp2(fmaf(__uint_as_float(v[e]), scale2, -m_use));
+          float p1 = fast_exp2(fmaf(__uint_as_float(v[e + 1]), scale2, -m_use));
           if (edge) {
             const int ka = kv0 + c * 32 + e, kb = ka + 1;
             const bool oa = (ka < a.S) & (qi < a.S) & (!a.causal | (ka <= qi)) &
@@ -384,7 +387,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       if (lane == 0) mbar_arrive(&p_full[w]);
     }
     if (ok && nw > 0) {
-      if (mbar_wait_bounded(&o_done[w], 0, abort_flag)) {
+      if (warp_wait(&o_done[w], 0, abort_flag)) {
         tc_fence_after();
         const float inv_l = l > 0.f ? 1.f / l : 0.f;
         __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(a.o) +
@@ -410,7 +413,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           a.lse[(static_cast<long long>(b) * a.Hq + me.h) * a.S + qi] =
               (l > 0.f) ? (m + log2f(l)) * kLn2 : -INFINITY;
       } else {
-        record_status(a.status, kTimeoutAccFull);
+        record_status(a.status, 16);
         *abort_flag = 1;
       }
     }
@@ -423,29 +426,21 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 }
 
 // -------------------------------------------------------------------- backward
-// One CTA per (128-key tile, kv head, batch), looping over the q heads of the
-// GQA group and the q tiles that see the keys. Two softmax-gradient groups
-// split the 128 query columns of each tile (group w owns columns 64w..64w+63):
-//   S^T = K Q^T -> TMEM; P^T = exp2(S^T - lse) written over S^T in TMEM (bf16)
-//   dP^T = V dO^T -> TMEM; dS^T = P^T (dP^T - delta) * scale -> smem (bf16)
-//   dV += P^T dO  (A operand from TMEM),  dK += dS^T Q,  dQ_i = dS K -> TMEM
-// dV/dK accumulate in TMEM for the whole loop; dQ_i goes out through fp32
-// vector atomics. Q/dO tiles are double-buffered; lse/delta are staged in smem
-// one iteration ahead.
-constexpr int kBwdThreads = 320;
+constexpr int kBwdThreads = 192;
 
 template <int D>
-struct Bwd {
+struct BwdCfg {
   static constexpr int kTile = 128 * D * 2;
   static constexpr int kK = 0;
   static constexpr int kV = kTile;
-  static constexpr int kQ = 2 * kTile;       // two stages
-  static constexpr int kDO = 4 * kTile;      // two stages
-  static constexpr int kDS = 6 * kTile;      // [128 kv x 128 q] bf16
-  static constexpr int kLse = kDS + 128 * 128 * 2;  // float [2][128]
-  static constexpr int kDelta = kLse + 2 * 128 * 4;
+  static constexpr int kQ = 2 * kTile;
+  static constexpr int kDO = 3 * kTile;
+  static constexpr int kPt = 4 * kTile;               // [128 kv x 128 q] bf16
+  static constexpr int kDSt = kPt + 128 * 128 * 2;    // [128 kv x 128 q] bf16
+  static constexpr int kLse = kDSt + 128 * 128 * 2;   // float [2][128]
+  static constexpr int kDelta = kLse + 2 * 128 * 4;   // float [2][128]
   static constexpr int kBar = kDelta + 2 * 128 * 4;
-  static constexpr int kSmem = kBar + 256;
+  static constexpr int kSmem = kBar + 256 + 1024;
   static constexpr int kTS = 0, kTdP = 128, kTdV = 256, kTdK = 256 + D;
 };
 
@@ -454,29 +449,29 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                     AttnBwdArgs g) {
-  using C = Bwd<D>;
+  using C = BwdCfg<D>;
   const AttnArgs& a = g.f;
-  extern __shared__ __align__(1024) uint8_t smem[];
-  if (smem_u32(smem) & 1023) {
-    if (threadIdx.x == 0) record_status(a.status, kBadArgument);
-    return;
-  }
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBar);
   uint64_t* kv_full = bars + 0;
-  uint64_t* qd_full = bars + 1;   // [2]
-  uint64_t* qd_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;
-  uint64_t* p_full = bars + 6;
-  uint64_t* dq_full = bars + 7;
-  uint64_t* dq_free = bars + 8;
-  uint64_t* mma_done = bars + 9;
+  uint64_t* qd_full = bars + 1;
+  uint64_t* qd_empty = bars + 2;
+  uint64_t* s_full = bars + 3;
+  uint64_t* s_free = bars + 4;
+  uint64_t* p_full = bars + 5;
+  uint64_t* dq_full = bars + 6;
+  uint64_t* dq_free = bars + 7;
+  uint64_t* mma_done = bars + 8;
+  uint64_t* stats_ready = bars + 9;  // lse/delta of an iteration staged in smem (4 warps)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* s_lse = reinterpret_cast<float*>(smem + C::kLse);
   float* s_delta = reinterpret_cast<float*>(smem + C::kDelta);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int jt = blockIdx.x;
+  const int jt = blockIdx.x;  // key tile; small j has the most causal work: scheduled first
   const int hk = blockIdx.y, b = blockIdx.z;
   const int G = a.Hq / a.Hk;
   const int kv0 = jt * BKV;
@@ -489,15 +484,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&qd_full[i], 1);
-      mbar_init(&qd_empty[i], 1);
-    }
+    mbar_init(qd_full, 1);
+    mbar_init(qd_empty, 1);
     mbar_init(s_full, 1);
-    mbar_init(p_full, 8);
+    mbar_init(s_free, 4);
+    mbar_init(p_full, 4);
     mbar_init(dq_full, 1);
-    mbar_init(dq_free, 8);
+    mbar_init(dq_free, 4);
     mbar_init(mma_done, 1);
+    mbar_init(stats_ready, 4);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -512,7 +507,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* sV = smem + C::kV;
   uint8_t* sQ = smem + C::kQ;
   uint8_t* sDO = smem + C::kDO;
-  uint8_t* sDS = smem + C::kDS;
+  uint8_t* sPt = smem + C::kPt;
+  uint8_t* sDSt = smem + C::kDSt;
 
   auto it_head = [&](int it) { return hk * G + it % G; };
   auto it_q0 = [&](int it) { return (i_lo + it / G) * BQ; };
@@ -520,7 +516,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   if (warp == 0) {
     if (lane == 0 && n_it > 0) {
       bool ok = true;
-      uint32_t qin = 0, qpar = 0;
+      bool q_inflight = false;
+      uint32_t q_par = 0;
       mbar_arrive_expect_tx(kv_full, 2 * C::kTile);
 #pragma unroll
       for (int x = 0; x < D / 64; ++x) {
@@ -528,67 +525,73 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tma_load_4d(sV + x * kBox, &tmV, kv_full, x * 64, hk, kv0, b);
       }
       for (int it = 0; it < n_it && ok; ++it) {
-        const int st = it & 1;
-        if (it >= 2 && !mbar_wait_bounded(&qd_empty[st], ((it >> 1) - 1) & 1, abort_flag)) {
+        if (it > 0 && !mbar_wait_bounded(qd_empty, (it - 1) & 1, abort_flag)) {
+          record_status(a.status, kTimeoutSmemEmpty);
+          *abort_flag = 1;
           ok = false;
           break;
         }
         const int h = it_head(it), q0 = it_q0(it);
-        mbar_arrive_expect_tx(&qd_full[st], 2 * C::kTile);
+        mbar_arrive_expect_tx(qd_full, 2 * C::kTile);
 #pragma unroll
         for (int x = 0; x < D / 64; ++x) {
-          tma_load_4d(sQ + st * C::kTile + x * kBox, &tmQ, &qd_full[st], x * 64, h, q0, b);
-          tma_load_4d(sDO + st * C::kTile + x * kBox, &tmDO, &qd_full[st], x * 64, h, q0, b);
+          tma_load_4d(sQ + x * kBox, &tmQ, qd_full, x * 64, h, q0, b);
+          tma_load_4d(sDO + x * kBox, &tmDO, qd_full, x * 64, h, q0, b);
         }
-        qin |= 1u << st;
-        qpar = (qpar & ~(1u << st)) | (((it >> 1) & 1u) << st);
+        q_inflight = true;
+        q_par = it & 1;
       }
       if (!ok) {
-        record_status(a.status, kTimeoutSmemEmpty);
-        *abort_flag = 1;
         if (!mbar_wait_bounded(kv_full, 0, nullptr)) record_status(a.status, kTimeoutDrain);
-        for (int st = 0; st < 2; ++st)
-          if (((qin >> st) & 1u) && !mbar_wait_bounded(&qd_full[st], (qpar >> st) & 1u, nullptr))
-            record_status(a.status, kTimeoutDrain);
+        if (q_inflight && !mbar_wait_bounded(qd_full, q_par, nullptr))
+          record_status(a.status, kTimeoutDrain);
       }
     }
   } else if (warp == 1) {
     if (lane == 0 && n_it > 0) {
       constexpr uint32_t id_sq = make_idesc_bf16_f32(128, 128, false, false);  // S^T, dP^T
-      constexpr uint32_t id_v = make_idesc_bf16_f32(128, D, false, true);      // dV (A in TMEM), dK
+      constexpr uint32_t id_kv = make_idesc_bf16_f32(128, D, false, true);     // dV, dK
       constexpr uint32_t id_dq = make_idesc_bf16_f32(128, D, true, true);      // dQ
       const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), aDO = smem_u32(sDO);
-      const uint32_t aDS = smem_u32(sDS);
+      const uint32_t aPt = smem_u32(sPt), aDS = smem_u32(sDSt);
       bool ok = mbar_wait_bounded(kv_full, 0, abort_flag);
       for (int it = 0; it < n_it && ok; ++it) {
-        const int st = it & 1;
-        if (!mbar_wait_bounded(&qd_full[st], (it >> 1) & 1, abort_flag)) { ok = false; break; }
+        const uint32_t par = it & 1, ppar = (it - 1) & 1;
+        if (!mbar_wait_bounded(qd_full, par, abort_flag) ||
+            (it > 0 && !mbar_wait_bounded(s_free, ppar, abort_flag))) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
-          tc_mma_ss(tmem + C::kTS, desc_kmajor(aK, kk), desc_kmajor(aQ + st * C::kTile, kk), id_sq,
-                    kk > 0 ? 1u : 0u);
-        if (it > 0 && !mbar_wait_bounded(dq_free, (it - 1) & 1, abort_flag)) { ok = false; break; }
+          tc_mma_ss(tmem + C::kTS, desc_kmajor(aK, kk), desc_kmajor(aQ, kk), id_sq, kk > 0);
+        if (it > 0 && !mbar_wait_bounded(dq_free, ppar, abort_flag)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
-          tc_mma_ss(tmem + C::kTdP, desc_kmajor(aV, kk), desc_kmajor(aDO + st * C::kTile, kk), id_sq,
-                    kk > 0 ? 1u : 0u);
+          tc_mma_ss(tmem + C::kTdP, desc_kmajor(aV, kk), desc_kmajor(aDO, kk), id_sq, kk > 0);
         tc_commit(s_full);
-        if (!mbar_wait_bounded(p_full, it & 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait_bounded(p_full, par, abort_flag)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk) {
-          tc_mma_ts(tmem + C::kTdV, tmem + C::kTS + kk * 8, desc_mnmajor(aDO + st * C::kTile, kk), id_v,
+          tc_mma_ss(tmem + C::kTdV, desc_kmajor(aPt, kk), desc_mnmajor(aDO, kk), id_kv,
                     (it > 0 || kk > 0) ? 1u : 0u);
-          tc_mma_ss(tmem + C::kTdK, desc_kmajor(aDS, kk), desc_mnmajor(aQ + st * C::kTile, kk), id_v,
+          tc_mma_ss(tmem + C::kTdK, desc_kmajor(aDS, kk), desc_mnmajor(aQ, kk), id_kv,
                     (it > 0 || kk > 0) ? 1u : 0u);
         }
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk)
           tc_mma_ss(tmem + C::kTdP, desc_mnmajor(aDS, kk), desc_mnmajor(aK, kk), id_dq, kk > 0);
         tc_commit(dq_full);
-        tc_commit(&qd_empty[st]);
+        tc_commit(qd_empty);
       }
       if (!ok) {
         record_status(a.status, kTimeoutTmaFull);
@@ -598,83 +601,79 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if (!mbar_wait_bounded(mma_done, 0, nullptr)) record_status(a.status, kTimeoutDrain);
     }
   } else {
-    // ---------------------------------------------- softmax-gradient groups
-    const int w = (warp - 2) >> 2;          // query columns 64w .. 64w+63
-    const int tid = threadIdx.x - 64;       // 0..255 over both groups
+    // -------------------------------------------------- softmax-grad warps
     const int quad = warp & 3;
-    const int r = quad * 32 + lane;         // key row (S^T, dP^T, dV, dK) / query row (dQ)
+    const int r = quad * 32 + lane;  // key row (S^T, dP^T) / query row (dQ)
     const int ki = kv0 + r;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     const float scale2 = a.scale * kLog2e;
-    // stage iteration 0's lse / delta
-    float nxt = 0.f;
-    auto fetch = [&](int it) -> float {
-      const int h = it_head(it), qrow = it_q0(it) + (tid & 127);
-      const long long li = (static_cast<long long>(b) * a.Hq + h) * a.S + qrow;
-      if (tid < 128) return qrow < a.S ? a.lse[li] * kLog2e : INFINITY;
-      return qrow < a.S ? g.delta[li] : 0.f;
-    };
-    if (n_it > 0) nxt = fetch(0);
     bool ok = true;
     for (int it = 0; it < n_it && ok; ++it) {
+      const int h = it_head(it), q0 = it_q0(it);
       const int buf = it & 1;
-      const int q0 = it_q0(it), h = it_head(it);
-      if (tid < 128) s_lse[buf * 128 + tid] = nxt;
-      else s_delta[buf * 128 + tid - 128] = nxt;
-      named_bar_sync(1, 256);
-      if (it + 1 < n_it) nxt = fetch(it + 1);
-      if (!mbar_wait_bounded(s_full, it & 1, abort_flag)) {
+      {
+        const int qrow = q0 + r;
+        const long long li = (static_cast<long long>(b) * a.Hq + h) * a.S + qrow;
+        s_lse[buf * 128 + r] = qrow < a.S ? a.lse[li] * kLog2e : INFINITY;
+        s_delta[buf * 128 + r] = qrow < a.S ? g.delta[li] : 0.f;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(stats_ready);
+      if (!warp_wait(stats_ready, it & 1, abort_flag)) {
+        record_status(a.status, 25);
+        *abort_flag = 1;
+        ok = false;
+        break;
+      }
+      if (!warp_wait(s_full, it & 1, abort_flag)) {
         record_status(a.status, kTimeoutAccFull);
         *abort_flag = 1;
         ok = false;
         break;
       }
       tc_fence_after();
-      const bool edge = (a.causal && q0 < kv0 + BKV - 1) | (kv0 + BKV > a.S) | (q0 + BQ > a.S) |
-                        (a.window > 0 && q0 + BQ - 1 - kv0 >= a.window);
-#pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        const int c0 = w * 64 + cc * 32;  // query column of this chunk
+      const bool need_mask = (a.causal && q0 < kv0 + BKV - 1) || (kv0 + BKV > a.S) ||
+                             (q0 + BQ > a.S) || (a.window > 0 && q0 + BQ - 1 - kv0 >= a.window);
+#pragma unroll 1
+      for (int c = 0; c < BQ / 32; ++c) {
         uint32_t us[32], ud[32];
-        tmem_ld_32x32b_x32(lane_base + C::kTS + c0, us);
-        tmem_ld_32x32b_x32(lane_base + C::kTdP + c0, ud);
+        __syncwarp();
+        tmem_ld_32x32b_x32(trow + C::kTS + c * 32, us);
+        tmem_ld_32x32b_x32(trow + C::kTdP + c * 32, ud);
         tmem_ld_wait();
-        uint32_t pp[16];
-        float ds[32];
+        float p[32], ds[32];
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float p0 = exp2f(fmaf(__uint_as_float(us[e]), scale2, -s_lse[buf * 128 + c0 + e]));
-          float p1 = exp2f(fmaf(__uint_as_float(us[e + 1]), scale2, -s_lse[buf * 128 + c0 + e + 1]));
-          if (edge) {
-            const int qa = q0 + c0 + e, qb = qa + 1;
-            const bool oa = (ki < a.S) & (qa < a.S) & (!a.causal | (ki <= qa)) &
-                            ((a.window <= 0) | (qa - ki < a.window));
-            const bool ob = (ki < a.S) & (qb < a.S) & (!a.causal | (ki <= qb)) &
-                            ((a.window <= 0) | (qb - ki < a.window));
-            p0 = oa ? p0 : 0.f;
-            p1 = ob ? p1 : 0.f;
-          }
-          pp[e / 2] = pack_bf16x2(p0, p1);
-          ds[e] = p0 * (__uint_as_float(ud[e]) - s_delta[buf * 128 + c0 + e]) * a.scale;
-          ds[e + 1] = p1 * (__uint_as_float(ud[e + 1]) - s_delta[buf * 128 + c0 + e + 1]) * a.scale;
+        for (int e = 0; e < 32; ++e) {
+          const int qc = c * 32 + e;
+          float pv = fast_exp2(__uint_as_float(us[e]) * scale2 - s_lse[buf * 128 + qc]);
+          if (need_mask && !key_ok(q0 + qc, ki, a.S, a.causal, a.window)) pv = 0.f;
+          p[e] = pv;
+          ds[e] = pv * (__uint_as_float(ud[e]) - s_delta[buf * 128 + qc]) * a.scale;
         }
-        tmem_st_32x32b_x16(lane_base + C::kTS + c0 / 2, pp);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint4 d4;
-          d4.x = pack_bf16x2(ds[j * 8 + 0], ds[j * 8 + 1]);
-          d4.y = pack_bf16x2(ds[j * 8 + 2], ds[j * 8 + 3]);
-          d4.z = pack_bf16x2(ds[j * 8 + 4], ds[j * 8 + 5]);
-          d4.w = pack_bf16x2(ds[j * 8 + 6], ds[j * 8 + 7]);
-          *reinterpret_cast<uint4*>(sDS + swz_off(r, c0 / 8 + j)) = d4;
+        for (int w = 0; w < 4; ++w) {
+          const int c16 = c * 4 + w;
+          uint4 pp, dd;
+          pp.x = pack_bf16x2(p[w * 8 + 0], p[w * 8 + 1]);
+          pp.y = pack_bf16x2(p[w * 8 + 2], p[w * 8 + 3]);
+          pp.z = pack_bf16x2(p[w * 8 + 4], p[w * 8 + 5]);
+          pp.w = pack_bf16x2(p[w * 8 + 6], p[w * 8 + 7]);
+          dd.x = pack_bf16x2(ds[w * 8 + 0], ds[w * 8 + 1]);
+          dd.y = pack_bf16x2(ds[w * 8 + 2], ds[w * 8 + 3]);
+          dd.z = pack_bf16x2(ds[w * 8 + 4], ds[w * 8 + 5]);
+          dd.w = pack_bf16x2(ds[w * 8 + 6], ds[w * 8 + 7]);
+          *reinterpret_cast<uint4*>(sPt + swz_off(r, c16)) = pp;
+          *reinterpret_cast<uint4*>(sDSt + swz_off(r, c16)) = dd;
         }
       }
-      tmem_st_wait();
-      fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
+      if (lane == 0) mbar_arrive(s_free);
+      fence_proxy_async_smem();
+      __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
-      if (!mbar_wait_bounded(dq_full, it & 1, abort_flag)) {
+      // dQ_i readout: TMEM lane r is query row q0 + r
+      if (!warp_wait(dq_full, it & 1, abort_flag)) {
         record_status(a.status, kTimeoutAccFull);
         *abort_flag = 1;
         ok = false;
@@ -684,54 +683,62 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const int qrow = q0 + r;
       float* dqr = g.dq_acc + ((static_cast<long long>(b) * a.S + qrow) * a.Hq + h) * D;
 #pragma unroll 1
-      for (int c = w * (D / 2); c < (w + 1) * (D / 2); c += 32) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(lane_base + C::kTdP + c, v);
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t u[32];
+        __syncwarp();
+        tmem_ld_32x32b_x32(trow + C::kTdP + c * 32, u);
         tmem_ld_wait();
         if (qrow < a.S) {
 #pragma unroll
           for (int e = 0; e < 32; e += 4)
-            atomicAdd(reinterpret_cast<float4*>(dqr + c + e),
-                      make_float4(__uint_as_float(v[e]), __uint_as_float(v[e + 1]),
-                                  __uint_as_float(v[e + 2]), __uint_as_float(v[e + 3])));
+            atomicAdd(reinterpret_cast<float4*>(dqr + c * 32 + e),
+                      make_float4(__uint_as_float(u[e]), __uint_as_float(u[e + 1]),
+                                  __uint_as_float(u[e + 2]), __uint_as_float(u[e + 3])));
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_free);
     }
-    if (ok && ki < a.S) {
+    // dK, dV for this key tile (all MMAs finished: the last dq_full was observed)
+    if (ok && n_it > 0) {
       __nv_bfloat16* dkr = reinterpret_cast<__nv_bfloat16*>(g.dk) +
                            (static_cast<long long>(b) * a.S + ki) * g.dk_row + hk * D;
       __nv_bfloat16* dvr = reinterpret_cast<__nv_bfloat16*>(g.dv) +
                            (static_cast<long long>(b) * a.S + ki) * g.dv_row + hk * D;
-      if (n_it > 0) {
 #pragma unroll 1
-        for (int c = w * (D / 2); c < (w + 1) * (D / 2); c += 32) {
-          uint32_t u[32], v[32];
-          tmem_ld_32x32b_x32(lane_base + C::kTdV + c, u);
-          tmem_ld_32x32b_x32(lane_base + C::kTdK + c, v);
-          tmem_ld_wait();
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t u[32], w32[32];
+        __syncwarp();
+        tmem_ld_32x32b_x32(trow + C::kTdV + c * 32, u);
+        tmem_ld_32x32b_x32(trow + C::kTdK + c * 32, w32);
+        tmem_ld_wait();
+        if (ki < a.S) {
 #pragma unroll
           for (int e = 0; e < 32; e += 8) {
-            uint4 a4, b4;
-            a4.x = pack_bf16x2(__uint_as_float(u[e]), __uint_as_float(u[e + 1]));
-            a4.y = pack_bf16x2(__uint_as_float(u[e + 2]), __uint_as_float(u[e + 3]));
-            a4.z = pack_bf16x2(__uint_as_float(u[e + 4]), __uint_as_float(u[e + 5]));
-            a4.w = pack_bf16x2(__uint_as_float(u[e + 6]), __uint_as_float(u[e + 7]));
-            b4.x = pack_bf16x2(__uint_as_float(v[e]), __uint_as_float(v[e + 1]));
-            b4.y = pack_bf16x2(__uint_as_float(v[e + 2]), __uint_as_float(v[e + 3]));
-            b4.z = pack_bf16x2(__uint_as_float(v[e + 4]), __uint_as_float(v[e + 5]));
-            b4.w = pack_bf16x2(__uint_as_float(v[e + 6]), __uint_as_float(v[e + 7]));
-            *reinterpret_cast<uint4*>(dvr + c + e) = a4;
-            *reinterpret_cast<uint4*>(dkr + c + e) = b4;
+            uint4 vv, kk4;
+            vv.x = pack_bf16x2(__uint_as_float(u[e]), __uint_as_float(u[e + 1]));
+            vv.y = pack_bf16x2(__uint_as_float(u[e + 2]), __uint_as_float(u[e + 3]));
+            vv.z = pack_bf16x2(__uint_as_float(u[e + 4]), __uint_as_float(u[e + 5]));
+            vv.w = pack_bf16x2(__uint_as_float(u[e + 6]), __uint_as_float(u[e + 7]));
+            kk4.x = pack_bf16x2(__uint_as_float(w32[e]), __uint_as_float(w32[e + 1]));
+            kk4.y = pack_bf16x2(__uint_as_float(w32[e + 2]), __uint_as_float(w32[e + 3]));
+            kk4.z = pack_bf16x2(__uint_as_float(w32[e + 4]), __uint_as_float(w32[e + 5]));
+            kk4.w = pack_bf16x2(__uint_as_float(w32[e + 6]), __uint_as_float(w32[e + 7]));
+            *reinterpret_cast<uint4*>(dvr + c * 32 + e) = vv;
+            *reinterpret_cast<uint4*>(dkr + c * 32 + e) = kk4;
           }
         }
-      } else {
-        for (int c = w * (D / 2); c < (w + 1) * (D / 2); ++c) {
-          dkr[c] = __float2bfloat16(0.f);
-          dvr[c] = __float2bfloat16(0.f);
-        }
+      }
+    } else if (n_it == 0 && ki < a.S) {
+      // keys no query attends to (only possible with a window / non-causal edge cases)
+      __nv_bfloat16* dkr = reinterpret_cast<__nv_bfloat16*>(g.dk) +
+                           (static_cast<long long>(b) * a.S + ki) * g.dk_row + hk * D;
+      __nv_bfloat16* dvr = reinterpret_cast<__nv_bfloat16*>(g.dv) +
+                           (static_cast<long long>(b) * a.S + ki) * g.dv_row + hk * D;
+      for (int c = 0; c < D; ++c) {
+        dkr[c] = __float2bfloat16(0.f);
+        dvr[c] = __float2bfloat16(0.f);
       }
     }
   }
@@ -810,7 +817,11 @@ static CUtensorMap map_bshd(const void* base, int B, int S, int H, int d, long l
                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
-    throw std::runtime_error("attention: cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+    throw std::runtime_error("attention: cuTensorMapEncodeTiled failed (" + std::to_string(r) +
+                             ") dims {" + std::to_string(d) + "," + std::to_string(H) + "," +
+                             std::to_string(S) + "," + std::to_string(B) + "} row " +
+                             std::to_string(row) + " base " +
+                             std::to_string(reinterpret_cast<uintptr_t>(base)));
   return m;
 }
 
@@ -836,7 +847,7 @@ static void fwd_launch(const AttnArgs& a, cudaStream_t st) {
 
 template <int D>
 static void bwd_launch(const AttnBwdArgs& g, cudaStream_t st) {
-  using C = Bwd<D>;
+  using C = BwdCfg<D>;
   const AttnArgs& a = g.f;
   CUtensorMap tq = map_bshd(a.q, a.B, a.S, a.Hq, D, a.q_row);
   CUtensorMap tk = map_bshd(a.k, a.B, a.S, a.Hk, D, a.k_row);

@@ -270,8 +270,10 @@ plg::AttnArgs attn_args(const at::Tensor& q, const at::Tensor& k, const at::Tens
   TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "attention takes [B, S, H, d]");
   TORCH_CHECK(is_bf16(q) && is_bf16(k) && is_bf16(v) && is_bf16(o), "attention is bf16");
   for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&q, &k, &v, &o}) {
-    TORCH_CHECK(t->stride(3) == 1 && t->stride(2) == t->size(3), "attention: heads must be packed");
-    TORCH_CHECK(t->stride(0) == t->stride(1) * t->size(1), "attention: batch stride = S * row");
+    TORCH_CHECK(t->stride(3) == 1 && (t->size(2) == 1 || t->stride(2) == t->size(3)),
+                "attention: heads must be packed");
+    TORCH_CHECK(t->size(0) == 1 || t->stride(0) == t->stride(1) * t->size(1),
+                "attention: batch stride = S * row");
   }
   plg::AttnArgs a{};
   a.q = q.data_ptr(); a.k = k.data_ptr(); a.v = v.data_ptr(); a.o = o.data_ptr();
@@ -284,6 +286,7 @@ plg::AttnArgs attn_args(const at::Tensor& q, const at::Tensor& k, const at::Tens
   a.causal = causal ? 1 : 0;
   a.window = static_cast<int>(window);
   a.status = status_ptr(status);
+  a.debug = 0;
   return a;
 }
 
@@ -306,6 +309,9 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at:
   b.f = attn_args(q, k, v, o, lse, scale, causal, window, status);
   TORCH_CHECK(dout.stride(3) == 1 && dq.stride(3) == 1 && dk.stride(3) == 1 && dv.stride(3) == 1,
               "attention grads need unit inner stride");
+  TORCH_CHECK(dout.dim() == 4 && (dout.size(2) == 1 || dout.stride(2) == dout.size(3)) &&
+                  (dout.size(0) == 1 || dout.stride(0) == dout.stride(1) * dout.size(1)),
+              "attention backward: dout must be [B, S, Hq, d] with packed heads");
   b.dout = dout.data_ptr(); b.do_row = dout.stride(1);
   b.dq = dq.data_ptr(); b.dk = dk.data_ptr(); b.dv = dv.data_ptr();
   b.dq_row = dq.stride(1); b.dk_row = dk.stride(1); b.dv_row = dv.stride(1);

@@ -61,6 +61,15 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// 2^x with the SFU's approximate base-2 exponential (ex2.approx, denormal
+// results flushed to zero): one instruction, ~2 ulp, ideal for softmax
+// numerators whose arguments are <= 0 after max subtraction.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

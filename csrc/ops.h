@@ -114,6 +114,7 @@ struct AttnArgs {
   int causal;
   int window;                                    // > 0: keys k with q - k < window only
   int* status;
+  int debug;                                     // bisection switches (0 in production)
 };
 void attn_fwd(const AttnArgs& a, cudaStream_t stream);
 struct AttnBwdArgs {

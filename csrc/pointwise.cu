@@ -18,7 +18,7 @@ namespace {
 
 constexpr float kLog2e = 1.4426950408889634f;
 
-__device__ __forceinline__ float silu(float x) { return x / (1.f + exp2f(-x * kLog2e)); }
+__device__ __forceinline__ float silu(float x) { return x / (1.f + fast_exp2(-x * kLog2e)); }
 
 // tanh-approximated GELU and its derivative (Hendrycks & Gimpel 2016, eq. for
 // the tanh form): g(x) = 0.5 x (1 + tanh(k0 (x + k1 x^3))), k0 = sqrt(2/pi), k1 = 0.044715
@@ -67,8 +67,8 @@ __global__ void glu_bwd_kernel(const __nv_bfloat16* __restrict__ gu, long long l
     const float2 d = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(dout + r * F + c));
     float dg0, dg1, du0, du1;
     if (kind == 0) {
-      const float s0 = 1.f / (1.f + exp2f(-g.x * kLog2e));
-      const float s1 = 1.f / (1.f + exp2f(-g.y * kLog2e));
+      const float s0 = 1.f / (1.f + fast_exp2(-g.x * kLog2e));
+      const float s1 = 1.f / (1.f + fast_exp2(-g.y * kLog2e));
       du0 = d.x * g.x * s0;
       du1 = d.y * g.y * s1;
       dg0 = d.x * u.x * s0 * (1.f + g.x * (1.f - s0));
@@ -177,9 +177,9 @@ __global__ void __launch_bounds__(kCeThreads) ce_rows_kernel(
       if (cap) f[j] = softcap * tanhf(f[j] / softcap);
       lm = fmaxf(lm, f[j]);
     }
-    float acc = s * exp2f((m - lm) * kLog2e);
+    float acc = s * fast_exp2((m - lm) * kLog2e);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc += exp2f((f[j] - lm) * kLog2e);
+    for (int j = 0; j < 8; ++j) acc += fast_exp2((f[j] - lm) * kLog2e);
     m = lm;
     s = acc;
   }
@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(kCeThreads) ce_rows_kernel(
     float f = __bfloat162float(x[i]);
     if (cap) f = softcap * tanhf(f / softcap);
     const float lm = fmaxf(m, f);
-    s = s * exp2f((m - lm) * kLog2e) + exp2f((f - lm) * kLog2e);
+    s = s * fast_exp2((m - lm) * kLog2e) + fast_exp2((f - lm) * kLog2e);
     m = lm;
   }
   // block reduction of (m, s)
@@ -197,8 +197,8 @@ __global__ void __launch_bounds__(kCeThreads) ce_rows_kernel(
     const float om = __shfl_xor_sync(0xffffffffu, m, o);
     const float os = __shfl_xor_sync(0xffffffffu, s, o);
     const float nm = fmaxf(m, om);
-    s = (m == -INFINITY ? 0.f : s * exp2f((m - nm) * kLog2e)) +
-        (om == -INFINITY ? 0.f : os * exp2f((om - nm) * kLog2e));
+    s = (m == -INFINITY ? 0.f : s * fast_exp2((m - nm) * kLog2e)) +
+        (om == -INFINITY ? 0.f : os * fast_exp2((om - nm) * kLog2e));
     m = nm;
   }
   if (lane == 0) { s_m[warp] = m; s_s[warp] = s; }
@@ -211,8 +211,8 @@ __global__ void __launch_bounds__(kCeThreads) ce_rows_kernel(
       const float om = __shfl_xor_sync(0xffffffffu, m, o);
       const float os = __shfl_xor_sync(0xffffffffu, s, o);
       const float nm = fmaxf(m, om);
-      s = (m == -INFINITY ? 0.f : s * exp2f((m - nm) * kLog2e)) +
-          (om == -INFINITY ? 0.f : os * exp2f((om - nm) * kLog2e));
+      s = (m == -INFINITY ? 0.f : s * fast_exp2((m - nm) * kLog2e)) +
+          (om == -INFINITY ? 0.f : os * fast_exp2((om - nm) * kLog2e));
       m = nm;
     }
     if (lane == 0) { s_m[0] = m; s_s[0] = s; }
@@ -244,7 +244,7 @@ __global__ void __launch_bounds__(kCeThreads) ce_rows_kernel(
         a = softcap * ta; b = softcap * tb;
         ca = 1.f - ta * ta; cb = 1.f - tb * tb;
       }
-      float pa = exp2f((a - lse) * kLog2e), pb = exp2f((b - lse) * kLog2e);
+      float pa = fast_exp2((a - lse) * kLog2e), pb = fast_exp2((b - lse) * kLog2e);
       const int c = i * 8 + j * 2;
       if (c == lab) pa -= 1.f;
       if (c + 1 == lab) pb -= 1.f;
@@ -260,7 +260,7 @@ __global__ void __launch_bounds__(kCeThreads) ce_rows_kernel(
       a = softcap * ta;
       ca = 1.f - ta * ta;
     }
-    float p = exp2f((a - lse) * kLog2e);
+    float p = fast_exp2((a - lse) * kLog2e);
     if (i == lab) p -= 1.f;
     x[i] = __float2bfloat16(p * gs * ca);
   }

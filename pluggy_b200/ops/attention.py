@@ -57,6 +57,7 @@ def attn_bwd(q, k, v, o, lse, do, *, causal=True, window=0, scale=None, dq=None,
     dq = torch.empty_like(q, memory_format=torch.contiguous_format) if dq is None else dq
     dk = torch.empty(k.shape, dtype=k.dtype, device=k.device) if dk is None else dk
     dv = torch.empty(v.shape, dtype=v.dtype, device=v.device) if dv is None else dv
+    do = do.contiguous()
     dq_acc = torch.empty((B, S, Hq, d), dtype=torch.float32, device=q.device)
     delta = torch.empty((B, Hq, S), dtype=torch.float32, device=q.device)
     ext().attn_bwd(q, k, v, o, lse, do, dq, dk, dv, dq_acc, delta, float(scale), bool(causal),
