@@ -119,6 +119,50 @@ __device__ __forceinline__ QTile make_qtile(const AttnArgs& a, int h, int qt) {
   return t;
 }
 
+// One softmax row of a 128-key tile, in place: v holds raw scores (fp32 bits,
+// masked entries already -inf); P, packed two bf16 per word, overwrites v[0, 64)
+// (word j is written after scores 2j and 2j+1 were consumed); m/l are
+// the running max (base 2, scaled) and sum. alpha is the factor the O row must
+// be multiplied by (1 when the max did not move by more than 2^kRescale).
+// kPoly moves one pair in four of the exponentials onto the FMA pipe
+// (exp2_poly2); it is used only on tiles without masked entries.
+template <bool kPoly>
+__device__ __forceinline__ void softmax_row(uint32_t (&v)[BKV], float scale2,
+                                            float& m, float& l, float& alpha, float& rs) {
+  float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+#pragma unroll
+  for (int e = 0; e < BKV; e += 8) {
+    m0 = fmax3(m0, __uint_as_float(v[e]), __uint_as_float(v[e + 1]));
+    m1 = fmax3(m1, __uint_as_float(v[e + 2]), __uint_as_float(v[e + 3]));
+    m2 = fmax3(m2, __uint_as_float(v[e + 4]), __uint_as_float(v[e + 5]));
+    m3 = fmax3(m3, __uint_as_float(v[e + 6]), __uint_as_float(v[e + 7]));
+  }
+  const float mx2 = fmax3(m0, m1, fmaxf(m2, m3)) * scale2;
+  float m_new = m;
+  if (mx2 > m + kRescale) m_new = mx2;  // also taken on the first tile (m = -inf)
+  const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+  alpha = (m_new == m) ? 1.f : fast_exp2(m - m_use);
+  const float nm = -m_use;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int e = 0; e < BKV; e += 2) {
+    float x0, x1, p0, p1;
+    ffma2(x0, x1, __uint_as_float(v[e]), __uint_as_float(v[e + 1]), scale2, scale2, nm, nm);
+    if (kPoly && ((e >> 1) & 3) == 3) {
+      exp2_poly2(x0, x1, p0, p1);
+    } else {
+      p0 = fast_exp2(x0);
+      p1 = fast_exp2(x1);
+    }
+    const int q = ((e >> 1) & 3) * 2;
+    fadd2(acc[q], acc[q + 1], acc[q], acc[q + 1], p0, p1);
+    v[e >> 1] = pack_bf16x2(p0, p1);
+  }
+  rs = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+  l = l * alpha + rs;
+  m = m_new;
+}
+
 template <int D>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -143,17 +187,24 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.z;
   const int G = a.Hq / a.Hk;
+  // 1-D grid ordered heaviest query tiles first across all heads and batches, so
+  // that the causal tail is made of short CTAs (longest-first list scheduling)
+  const int n_q = (a.S + BQ - 1) / BQ;
+  const int units = pair_heads ? n_q : (n_q + 1) / 2;
+  const int slots = pair_heads ? a.Hq / 2 : a.Hq;
+  const int rank = blockIdx.x / (slots * a.B);
+  const int rest = blockIdx.x - rank * slots * a.B;
+  const int slot = rest % slots;
+  const int b = rest / slots;
+  const int unit = units - 1 - rank;
   QTile qtl[2];
   if (pair_heads) {
-    const int qt = gridDim.x - 1 - blockIdx.x;  // heavy causal tiles first
-    qtl[0] = make_qtile(a, 2 * blockIdx.y, qt);
-    qtl[1] = make_qtile(a, 2 * blockIdx.y + 1, qt);
+    qtl[0] = make_qtile(a, 2 * slot, unit);
+    qtl[1] = make_qtile(a, 2 * slot + 1, unit);
   } else {
-    const int i = gridDim.x - 1 - blockIdx.x;
-    qtl[0] = make_qtile(a, blockIdx.y, 2 * i);
-    qtl[1] = make_qtile(a, blockIdx.y, 2 * i + 1);
+    qtl[0] = make_qtile(a, slot, 2 * unit);
+    qtl[1] = make_qtile(a, slot, 2 * unit + 1);
   }
   const int hk = qtl[0].h / G;
   const bool live0 = qtl[0].hi >= qtl[0].lo, live1 = qtl[1].hi >= qtl[1].lo;
@@ -317,59 +368,27 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const int kv0 = t * BKV;
       const bool edge = (a.causal && kv0 + BKV - 1 > q0) | (kv0 + BKV > a.S) |
                         (a.window > 0 && q0 + BQ - 1 - kv0 >= a.window);
-      // pass 1 over the TMEM row: max of the (masked) raw scores
-      float mx = -INFINITY;
+      // the whole 128-column row of S in registers (one TMEM round trip)
+      uint32_t v[BKV];
 #pragma unroll
-      for (int c = 0; c < BKV / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tS + c * 32, v);
-        tmem_ld_wait();
+      for (int c = 0; c < BKV / 32; ++c)
+        tmem_ld_32x32b_x32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(v + c * 32));
+      tmem_ld_wait();
+      float alpha, rs;
+      if (edge) {
+        // valid key columns of this row form the range [c_lo, c_hi]
+        int c_hi = (a.causal ? min(qi, a.S - 1) : a.S - 1) - kv0;
+        const int c_lo = a.window > 0 ? qi - a.window + 1 - kv0 : 0;
+        if (qi >= a.S) c_hi = -1;
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          float x = __uint_as_float(v[e]);
-          if (edge) {
-            const int ki = kv0 + c * 32 + e;
-            const bool ok_k = (ki < a.S) & (qi < a.S) & (!a.causal | (ki <= qi)) &
-                              ((a.window <= 0) | (qi - ki < a.window));
-            x = ok_k ? x : -INFINITY;
-          }
-          mx = fmaxf(mx, x);
-        }
+        for (int e = 0; e < BKV; ++e)
+          v[e] = (e >= c_lo && e <= c_hi) ? v[e] : 0xff800000u;  // -inf
+        softmax_row<false>(v, scale2, m, l, alpha, rs);
+      } else {
+        softmax_row<true>(v, scale2, m, l, alpha, rs);
       }
-      const float mx2 = mx * scale2;
-      float m_new = m;
-      if (mx2 > m + kRescale) m_new = mx2;  // also taken on the first tile (m = -inf)
-      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      const float alpha = (m_new == m) ? 1.f : fast_exp2(m - m_use);
-      // pass 2: p = exp2(s * scale2 - m), packed two bf16 per 32-bit word
-      float rs = 0.f;
-      uint32_t pk[BKV / 2];
-#pragma unroll
-      for (int c = 0; c < BKV / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tS + c * 32, v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float p0 = fast_exp2(fmaf(__uint_as_float(v[e]), scale2, -m_use));
-          float p1 = fast_exp2(fmaf(__uint_as_float(v[e + 1]), scale2, -m_use));
-          if (edge) {
-            const int ka = kv0 + c * 32 + e, kb = ka + 1;
-            const bool oa = (ka < a.S) & (qi < a.S) & (!a.causal | (ka <= qi)) &
-                            ((a.window <= 0) | (qi - ka < a.window));
-            const bool ob = (kb < a.S) & (qi < a.S) & (!a.causal | (kb <= qi)) &
-                            ((a.window <= 0) | (qi - kb < a.window));
-            p0 = oa ? p0 : 0.f;
-            p1 = ob ? p1 : 0.f;
-          }
-          rs += p0 + p1;
-          pk[c * 16 + e / 2] = pack_bf16x2(p0, p1);
-        }
-      }
-      l = l * alpha + rs;
-      m = m_new;
-      tmem_st_32x32b_x32(tS, *reinterpret_cast<const uint32_t(*)[32]>(pk));
-      tmem_st_32x32b_x32(tS + 32, *reinterpret_cast<const uint32_t(*)[32]>(pk + 32));
+      tmem_st_32x32b_x32(tS, *reinterpret_cast<const uint32_t(*)[32]>(v));
+      tmem_st_32x32b_x32(tS + 32, *reinterpret_cast<const uint32_t(*)[32]>(v + 32));
       if (u > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
@@ -831,17 +850,14 @@ static void fwd_launch(const AttnArgs& a, cudaStream_t st) {
   CUtensorMap tq = map_bshd(a.q, a.B, a.S, a.Hq, D, a.q_row);
   CUtensorMap tk = map_bshd(a.k, a.B, a.S, a.Hk, D, a.k_row);
   CUtensorMap tv = map_bshd(a.v, a.B, a.S, a.Hk, D, a.v_row);
-  static bool set = false;
-  if (!set) {
-    PLG_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<D>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
-    set = true;
-  }
+  set_max_smem_once(reinterpret_cast<const void*>(attn_fwd_kernel<D>), C::kSmem);
   const int G = a.Hq / a.Hk;
   const int n_q = (a.S + BQ - 1) / BQ;
   const int pair_heads = (G % 2 == 0) ? 1 : 0;
-  dim3 grid(pair_heads ? n_q : (n_q + 1) / 2, pair_heads ? a.Hq / 2 : a.Hq, a.B);
-  attn_fwd_kernel<D><<<grid, kFwdThreads, C::kSmem, st>>>(tq, tk, tv, a, pair_heads);
+  const long long units = pair_heads ? n_q : (n_q + 1) / 2;
+  const long long ctas = units * (pair_heads ? a.Hq / 2 : a.Hq) * a.B;
+  if (ctas > 0x7fffffffLL) throw std::invalid_argument("attention: problem too large for one launch");
+  attn_fwd_kernel<D><<<static_cast<unsigned>(ctas), kFwdThreads, C::kSmem, st>>>(tq, tk, tv, a, pair_heads);
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -853,12 +869,7 @@ static void bwd_launch(const AttnBwdArgs& g, cudaStream_t st) {
   CUtensorMap tk = map_bshd(a.k, a.B, a.S, a.Hk, D, a.k_row);
   CUtensorMap tv = map_bshd(a.v, a.B, a.S, a.Hk, D, a.v_row);
   CUtensorMap td = map_bshd(g.dout, a.B, a.S, a.Hq, D, g.do_row);
-  static bool set = false;
-  if (!set) {
-    PLG_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<D>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
-    set = true;
-  }
+  set_max_smem_once(reinterpret_cast<const void*>(attn_bwd_kernel<D>), C::kSmem);
   const long long rows = static_cast<long long>(a.B) * a.S * a.Hq;
   attn_delta_kernel<<<(rows * 32 + 255) / 256, 256, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(a.o), a.o_row,

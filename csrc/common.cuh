@@ -70,6 +70,57 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Packed two-lane fp32 arithmetic (sm_100 f32x2 instructions): one issue slot
+// for two independent lanes of a softmax row.
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1,
+                                      float c0, float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+
+__device__ __forceinline__ void fadd2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+// max of three (sm_100 three-input max)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for two lanes on the FMA pipe instead of the SFU, used for a share of the
+// softmax exponentials so the SFU stops being the limiter. Range reduction:
+// x = j + f with j = rint(x) (adding 1.5 * 2^23 rounds to an integer held in the
+// low mantissa bits) and f in [-0.5, 0.5]; 2^f is a cubic fitted here to minimise
+// the relative error on that interval (iteratively reweighted least squares on
+// Chebyshev nodes, max relative error 7.5e-5, below bf16's 2^-9 rounding); the
+// exponent j is added to the result's exponent field. x is clamped to >= -126 so
+// that field never underflows: inputs below that return ~2^-126 instead of 0, so
+// callers use it only where no element is masked to -inf.
+__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& p0, float& p1) {
+  constexpr float kShift = 12582912.f;  // 1.5 * 2^23
+  constexpr float c0 = 0.99992806f, c1 = 0.69326097f, c2 = 0.24261114f, c3 = 0.05517165f;
+  x0 = fmaxf(x0, -126.f);
+  x1 = fmaxf(x1, -126.f);
+  float t0, t1, j0, j1, f0, f1, q0, q1;
+  fadd2(t0, t1, x0, x1, kShift, kShift);
+  fadd2(j0, j1, t0, t1, -kShift, -kShift);
+  ffma2(f0, f1, j0, j1, -1.f, -1.f, x0, x1);
+  ffma2(q0, q1, c3, c3, f0, f1, c2, c2);
+  ffma2(q0, q1, q0, q1, f0, f1, c1, c1);
+  ffma2(q0, q1, q0, q1, f0, f1, c0, c0);
+  p0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
+  p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -339,3 +390,23 @@ __device__ __forceinline__ void tmem_st_wait() {
                                " at " + __FILE__ + ":" + std::to_string(__LINE__));   \
     }                                                                                 \
   } while (0)
+
+#include <mutex>
+#include <set>
+#include <utility>
+
+namespace plg {
+// Raise a kernel's dynamic shared memory limit once per (kernel, device): the
+// attribute belongs to the device context, so a process driving several GPUs
+// must set it on each.
+inline void set_max_smem_once(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  PLG_CUDA_CHECK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> g(mu);
+  if (done.count({kernel, dev})) return;
+  PLG_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  done.insert({kernel, dev});
+}
+}  // namespace plg

@@ -452,12 +452,7 @@ static void launch(const GemmProblem& p, cudaStream_t stream) {
   const int work = tiles * splits;
   const int grid = work < sms ? work : sms;
   auto kern = gemm_kernel<BN, A_MN, B_MN>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    PLG_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        C_::kSmemBytes));
-    attr_set = true;
-  }
+  set_max_smem_once(reinterpret_cast<const void*>(kern), C_::kSmemBytes);
   kern<<<grid, kThreads, C_::kSmemBytes, stream>>>(ta, tb, a);
   PLG_CUDA_CHECK(cudaGetLastError());
 }
