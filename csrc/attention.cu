@@ -68,11 +68,13 @@ __device__ __forceinline__ bool key_ok(int qi, int ki, int S, int causal, int wi
 // --------------------------------------------------------------------- forward
 // Two 128-row query tiles per CTA, one softmax warpgroup each, so that one
 // group's softmax overlaps the tensor core working on the other group:
-//   warp 0       TMA: Q tiles once, then K_t / V_t (two stages each, released
+//   warps 0..3   softmax group 0 (query tile 0), warps 4..7 group 1
+//   warp 8       TMA: Q tiles once, then K_t / V_t (two stages each, released
 //                separately: K after the S MMAs, V after the PV MMAs)
-//   warp 1       TMEM owner + MMA issuer, per tile t in the order
+//   warp 9       TMEM owner + MMA issuer, per tile t in the order
 //                PV_0(t), S_0(t+1), PV_1(t), S_1(t+1)
-//   warps 2..5   softmax group 0 (query tile 0), warps 6..9 group 1
+//   warps 10,11  idle; with 8 and 9 they form the warpgroup whose registers
+//                are handed to the softmax groups (setmaxnreg is per warpgroup)
 // S_w lives in TMEM; the softmax group overwrites it in place with P (bf16,
 // two per 32-bit column) and the PV MMA reads P straight from TMEM (A operand
 // in tensor memory), so P never touches shared memory. O_w stays in TMEM; it
@@ -81,7 +83,16 @@ __device__ __forceinline__ bool key_ok(int qi, int ki, int S, int causal, int wi
 // branches.
 // The two query tiles are two heads of one GQA group (same keys, same range)
 // when the group size is even, else two consecutive row tiles of one head.
-constexpr int kFwdThreads = 320;
+constexpr int kFwdThreads = 384;
+constexpr int kFwdTmaWarp = 8, kFwdMmaWarp = 9;  // warps 10, 11 only lend registers
+// Register split (setmaxnreg): launched at 168 per thread (the most 384 threads
+// can hold), the control warpgroup drops to 80 and the softmax warpgroups rise
+// to 208: 8*32*208 + 4*32*80 = 63488 <= 384*168 = 64512 registers, and each
+// SM sub-partition (one warp of every warpgroup) needs 208+208+80 <= 512 per lane.
+// Neither role spills at these limits.
+constexpr int kFwdRegsSoftmax = 208, kFwdRegsCtl = 80, kFwdRegsLaunch = 168;
+static_assert(8 * 32 * kFwdRegsSoftmax + 4 * 32 * kFwdRegsCtl <= kFwdThreads * kFwdRegsLaunch,
+              "register split exceeds the launch allocation");
 constexpr float kRescale = 8.0f;
 
 template <int D>
@@ -227,18 +238,24 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 1) {
+  if (warp == kFwdMmaWarp) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+
   uint8_t* sQ = smem + C::kQ;
   uint8_t* sK = smem + C::kK;
   uint8_t* sV = smem + C::kV;
 
-  if (warp == 0) {
+  // registers move from the TMA/MMA warpgroup to the two softmax warpgroups;
+  // each setmaxnreg heads the branch of its warpgroup so the compiler applies
+  // the matching register limit to all code of that role
+  if (warp >= 8) {
+  setmaxnreg_dec<kFwdRegsCtl>();
+  if (warp == kFwdTmaWarp) {
     if (lane == 0 && n > 0) {
       bool ok = true;
       uint32_t kin = 0, vin = 0, kpar = 0, vpar = 0;  // stages in flight and their parity
@@ -280,7 +297,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == kFwdMmaWarp) {
     if (lane == 0 && n > 0) {
       constexpr uint32_t id_s = make_idesc_bf16_f32(128, 128, false, false);
       constexpr uint32_t id_o = make_idesc_bf16_f32(128, D, false, true);
@@ -341,9 +358,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tc_commit(mma_done);
       if (!mbar_wait_bounded(mma_done, 0, nullptr)) record_status(a.status, kTimeoutDrain);
     }
+  }
   } else {
+    setmaxnreg_inc<kFwdRegsSoftmax>();
     // ------------------------------------------------------ softmax groups
-    const int w = (warp - 2) >> 2;
+    const int w = warp >> 2;
     const QTile me = qtl[w];
     const int nw = me.hi - me.lo + 1;
     const int quad = warp & 3;
@@ -438,7 +457,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
   }
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kFwdMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -768,6 +787,421 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
+// ------------------------------------------------------- backward, head_dim 128
+// One CTA per (128-key tile, kv head, batch), heaviest causal key tiles first.
+// The loop runs over steps of 64 query rows (all q heads of the GQA group and
+// every query block that sees the keys). Per step j, with buffers b = j & 1:
+//   S^T_j  = K Q_j^T   -> TMEM S_b   (128 keys x 64 queries, fp32)
+//   dP^T_j = V dO_j^T  -> TMEM dP_b
+//   compute warps: P^T = exp2(S^T * scale*log2e - lse*log2e) -> bf16 into S_b,
+//                  dS^T = P^T (dP^T * scale - delta * scale) -> bf16 into smem
+//   dV += P^T dO_j  (A from TMEM)      dK += dS^T Q_j
+//   dQ^T_j = K^T dS^T_j -> TMEM dP_b (d x 64 queries), read out by the drain
+//   warps and added into the fp32 dQ workspace with vector-free coalesced
+//   reductions (a warp covers 32 consecutive d of one query row).
+// The MMA warp issues S/dP of step j+1 before dV/dK/dQ of step j, so the
+// compute warps work on step j+1 while the tensor core finishes step j.
+// TMEM: dV [0,128), dK [128,256), S_b at 256+128b, dP_b at 320+128b.
+// lse*log2e and delta*scale come pre-negated from a pre-pass, padded to a
+// multiple of 64 queries ([B*Hq][2][S64]) so each step fetches them with two
+// 256-byte bulk copies; padded queries carry -inf / 0 and contribute nothing.
+constexpr int kB3Threads = 384;
+constexpr int kB3TmaWarp = 8, kB3MmaWarp = 9;  // warps 0..3 compute, 4..7 dQ drain
+// setmaxnreg split of the 384 x 168 launch allocation: 128*(224 + 112 + 96) = 55296
+// <= 64512, and 224 + 112 + 96 <= 512 per lane of each SM sub-partition. No role
+// spills at these limits.
+constexpr int kB3RegsComp = 224, kB3RegsDrain = 112, kB3RegsCtl = 96, kB3RegsLaunch = 168;
+static_assert(128 * (kB3RegsComp + kB3RegsDrain + kB3RegsCtl) <= kB3Threads * kB3RegsLaunch,
+              "register split exceeds the launch allocation");
+constexpr int kBQ3 = 64;
+
+struct Bwd3 {
+  static constexpr int D = 128;
+  static constexpr int kKVTile = 128 * D * 2;  // 32 KB
+  static constexpr int kQTile = kBQ3 * D * 2;  // 16 KB, two [64 x 64] boxes
+  static constexpr int kQBox = kBQ3 * 128;     // bytes of one [64 rows x 64] box
+  static constexpr int kStages = 3;
+  static constexpr int kK = 0;
+  static constexpr int kV = kKVTile;
+  static constexpr int kQ = 2 * kKVTile;                      // [stage] Q, dO
+  static constexpr int kDS = kQ + kStages * 2 * kQTile;       // [2] dS^T [128 x 64] bf16
+  static constexpr int kStats = kDS + 2 * 128 * kBQ3 * 2;     // [stage] 2 x 64 floats
+  static constexpr int kBar = kStats + kStages * 512;
+  static constexpr int kSmem = kBar + 256 + 1024;             // + manual 1024 alignment
+  static constexpr int kTdV = 0, kTdK = 128;
+  static constexpr int kTS0 = 256, kTdP0 = 320;               // + 128 * b
+};
+
+// K-major SW128 descriptor for k-step kk of a 64-row tile stored as [64 x 64] boxes
+__device__ __forceinline__ uint64_t desc_kmajor64(uint32_t base, int kk) {
+  return make_smem_desc(base + (kk >> 2) * Bwd3::kQBox + (kk & 3) * 32, 16, 1024, kLayoutSW128);
+}
+// MN-major SW128 descriptor for k-step kk (16 rows) of a 64-row tile, the 64-wide
+// column boxes being the MN atoms
+__device__ __forceinline__ uint64_t desc_mnmajor64(uint32_t base, int kk) {
+  return make_smem_desc(base + kk * 2048, Bwd3::kQBox, 1024, kLayoutSW128);
+}
+
+__global__ void __launch_bounds__(kB3Threads, 1)
+    attn_bwd3_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                     AttnBwdArgs g) {
+  using C = Bwd3;
+  constexpr int D = C::D;
+  const AttnArgs& a = g.f;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBar);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qd_full = bars + 1;    // [kStages]
+  uint64_t* qd_empty = bars + 4;   // [kStages]
+  uint64_t* s_full = bars + 7;     // [2]
+  uint64_t* p_full = bars + 9;     // [2]
+  uint64_t* dq_full = bars + 11;   // [2]
+  uint64_t* dq_free = bars + 13;   // [2]
+  uint64_t* mma_done = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int per_tile = a.Hk * a.B;
+  const int jt = blockIdx.x / per_tile;
+  const int rest = blockIdx.x - jt * per_tile;
+  const int hk = rest % a.Hk, b = rest / a.Hk;
+  const int G = a.Hq / a.Hk;
+  const int kv0 = jt * BKV;
+  const int n_qb = (a.S + kBQ3 - 1) / kBQ3;
+  const int S64 = n_qb * kBQ3;
+  const int qb_lo = a.causal ? kv0 / kBQ3 : 0;
+  int qb_hi = n_qb - 1;
+  if (a.window > 0) qb_hi = min(qb_hi, (kv0 + BKV - 1 + a.window - 1) / kBQ3);
+  const int n = qb_hi >= qb_lo ? (qb_hi - qb_lo + 1) * G : 0;
+  // step j: query block qb_lo + j / G, head hk * G + j % G
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&qd_full[s], 1);
+      mbar_init(&qd_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&dq_full[i], 1);
+      mbar_init(&dq_free[i], 4);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == kB3MmaWarp) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  uint8_t* sK = smem + C::kK;
+  uint8_t* sV = smem + C::kV;
+  auto sQ = [&](int s) { return smem + C::kQ + s * 2 * C::kQTile; };
+  auto sDO = [&](int s) { return smem + C::kQ + s * 2 * C::kQTile + C::kQTile; };
+  auto sDS = [&](int bb) { return smem + C::kDS + bb * 128 * kBQ3 * 2; };
+  auto sStats = [&](int s) { return reinterpret_cast<float*>(smem + C::kStats + s * 512); };
+
+  if (warp >= 8) {
+    setmaxnreg_dec<kB3RegsCtl>();
+    if (warp == kB3TmaWarp && lane == 0 && n > 0) {
+      // ------------------------------------------------------------ producer
+      bool ok = true;
+      int last = -1;  // last step whose loads were issued
+      mbar_arrive_expect_tx(kv_full, 2 * C::kKVTile);
+#pragma unroll
+      for (int x = 0; x < D / 64; ++x) {
+        tma_load_4d(sK + x * kBox, &tmK, kv_full, x * 64, hk, kv0, b);
+        tma_load_4d(sV + x * kBox, &tmV, kv_full, x * 64, hk, kv0, b);
+      }
+      for (int j = 0; j < n; ++j) {
+        const int s = j % C::kStages, u = j / C::kStages;
+        if (u > 0 && !mbar_wait_bounded(&qd_empty[s], (u - 1) & 1, abort_flag)) {
+          record_status(a.status, 30);
+          ok = false;
+          break;
+        }
+        const int h = hk * G + j % G, q0 = (qb_lo + j / G) * kBQ3;
+        mbar_arrive_expect_tx(&qd_full[s], 2 * C::kQTile + 512);
+#pragma unroll
+        for (int x = 0; x < D / 64; ++x) {
+          tma_load_4d(sQ(s) + x * C::kQBox, &tmQ, &qd_full[s], x * 64, h, q0, b);
+          tma_load_4d(sDO(s) + x * C::kQBox, &tmDO, &qd_full[s], x * 64, h, q0, b);
+        }
+        const float* st = g.delta + (static_cast<long long>(b) * a.Hq + h) * 2 * S64 + q0;
+        bulk_load(sStats(s), st, 256, &qd_full[s]);
+        bulk_load(sStats(s) + 64, st + S64, 256, &qd_full[s]);
+        last = j;
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        // let every copy still in flight land before the CTA can exit
+        if (!mbar_wait_bounded(kv_full, 0, nullptr)) record_status(a.status, kTimeoutDrain);
+        for (int j = last - C::kStages + 1; j <= last; ++j)
+          if (j >= 0 && !mbar_wait_bounded(&qd_full[j % C::kStages], (j / C::kStages) & 1, nullptr))
+            record_status(a.status, kTimeoutDrain);
+      }
+    } else if (warp == kB3MmaWarp && lane == 0 && n > 0) {
+      // ------------------------------------------------------------ MMA issuer
+      constexpr uint32_t id_s = make_idesc_bf16_f32(128, kBQ3, false, false);  // S^T, dP^T
+      constexpr uint32_t id_kv = make_idesc_bf16_f32(128, D, false, true);     // dV, dK
+      constexpr uint32_t id_dq = make_idesc_bf16_f32(128, kBQ3, true, true);   // dQ^T
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV);
+      bool ok = mbar_wait_bounded(kv_full, 0, abort_flag);
+      if (!ok) record_status(a.status, 31);
+      auto issue_sdp = [&](int j) -> bool {
+        const int s = j % C::kStages, bj = j & 1;
+        if (!mbar_wait_bounded(&qd_full[s], (j / C::kStages) & 1, abort_flag)) {
+          record_status(a.status, 32);
+          return false;
+        }
+        tc_fence_after();
+        const uint32_t aQ = smem_u32(sQ(s)), aDO = smem_u32(sDO(s));
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          tc_mma_ss(tmem + C::kTS0 + 128 * bj, desc_kmajor(aK, kk), desc_kmajor64(aQ, kk), id_s,
+                    kk > 0 ? 1u : 0u);
+        // dP_b still holds dQ^T of step j-2 until the drain warps have read it
+        if (j >= 2 && !mbar_wait_bounded(&dq_free[bj], ((j - 2) >> 1) & 1, abort_flag)) {
+          record_status(a.status, 33);
+          return false;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          tc_mma_ss(tmem + C::kTdP0 + 128 * bj, desc_kmajor(aV, kk), desc_kmajor64(aDO, kk), id_s,
+                    kk > 0 ? 1u : 0u);
+        tc_commit(&s_full[bj]);
+        return true;
+      };
+      if (ok) ok = issue_sdp(0);
+      for (int j = 0; j < n && ok; ++j) {
+        if (j + 1 < n && !issue_sdp(j + 1)) {
+          ok = false;
+          break;
+        }
+        const int s = j % C::kStages, bj = j & 1;
+        if (!mbar_wait_bounded(&p_full[bj], (j >> 1) & 1, abort_flag)) {
+          record_status(a.status, 34);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t aQ = smem_u32(sQ(s)), aDO = smem_u32(sDO(s)), aDS = smem_u32(sDS(bj));
+#pragma unroll
+        for (int kk = 0; kk < kBQ3 / 16; ++kk)
+          tc_mma_ts(tmem + C::kTdV, tmem + C::kTS0 + 128 * bj + kk * 8, desc_mnmajor64(aDO, kk),
+                    id_kv, (j > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < kBQ3 / 16; ++kk)
+          tc_mma_ss(tmem + C::kTdK, desc_kmajor(aDS, kk), desc_mnmajor64(aQ, kk), id_kv,
+                    (j > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&qd_empty[s]);
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk)
+          tc_mma_ss(tmem + C::kTdP0 + 128 * bj, desc_mnmajor(aK, kk), desc_mnmajor(aDS, kk), id_dq,
+                    kk > 0 ? 1u : 0u);
+        tc_commit(&dq_full[bj]);
+      }
+      if (!ok) *abort_flag = 1;
+      tc_commit(mma_done);
+      if (!mbar_wait_bounded(mma_done, 0, nullptr)) record_status(a.status, kTimeoutDrain);
+    }
+  } else if (warp >= 4) {
+    setmaxnreg_dec<kB3RegsDrain>();
+    // -------------------------------------------------------------- dQ drain
+    const int quad = warp & 3;
+    const int dcol = quad * 32 + lane;  // TMEM lane = head-dim index of dQ^T
+    const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    for (int j = 0; j < n; ++j) {
+      const int bj = j & 1;
+      if (!warp_wait(&dq_full[bj], (j >> 1) & 1, abort_flag)) {
+        record_status(a.status, 35);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      uint32_t v[kBQ3];
+      tmem_ld_32x32b_x32(trow + C::kTdP0 + 128 * bj, *reinterpret_cast<uint32_t(*)[32]>(v));
+      tmem_ld_32x32b_x32(trow + C::kTdP0 + 128 * bj + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&dq_free[bj]);
+      const int h = hk * G + j % G, q0 = (qb_lo + j / G) * kBQ3;
+      const long long stride = static_cast<long long>(a.Hq) * D;
+      float* dst = g.dq_acc + ((static_cast<long long>(b) * a.S + q0) * a.Hq + h) * D + dcol;
+      const int nv = min(kBQ3, a.S - q0);
+#pragma unroll
+      for (int c = 0; c < kBQ3; ++c)
+        if (c < nv) atomicAdd(dst + c * stride, __uint_as_float(v[c]));
+    }
+  } else {
+    setmaxnreg_inc<kB3RegsComp>();
+    // ----------------------------------------------------------- P / dS warps
+    const int quad = warp;
+    const int r = quad * 32 + lane;  // TMEM lane = key row
+    const int ki = kv0 + r;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const float scale2 = a.scale * kLog2e, scale = a.scale;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      const int s = j % C::kStages, bj = j & 1;
+      if (!warp_wait(&s_full[bj], (j >> 1) & 1, abort_flag) ||
+          !warp_wait(&qd_full[s], (j / C::kStages) & 1, abort_flag)) {
+        record_status(a.status, 36);
+        *abort_flag = 1;
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int q0 = (qb_lo + j / G) * kBQ3;
+      uint32_t sv[kBQ3], dv[kBQ3];
+      tmem_ld_32x32b_x32(trow + C::kTS0 + 128 * bj, *reinterpret_cast<uint32_t(*)[32]>(sv));
+      tmem_ld_32x32b_x32(trow + C::kTS0 + 128 * bj + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+      tmem_ld_32x32b_x32(trow + C::kTdP0 + 128 * bj, *reinterpret_cast<uint32_t(*)[32]>(dv));
+      tmem_ld_32x32b_x32(trow + C::kTdP0 + 128 * bj + 32, *reinterpret_cast<uint32_t(*)[32]>(dv + 32));
+      const float4* st4 = reinterpret_cast<const float4*>(sStats(s));
+      const bool edge = (a.causal && kv0 + BKV - 1 > q0) ||
+                        (a.window > 0 && q0 + kBQ3 - 1 - kv0 >= a.window);
+      const int c_lo = a.causal ? ki - q0 : -(1 << 30);
+      const int c_hi = a.window > 0 ? ki + a.window - 1 - q0 : (1 << 30);
+      tmem_ld_wait();
+      uint32_t pk[kBQ3 / 2], dk[kBQ3 / 2];
+#pragma unroll
+      for (int c = 0; c < kBQ3; c += 4) {
+        const float4 nl = st4[c / 4];        // -lse * log2(e)
+        const float4 nd = st4[16 + c / 4];   // -delta * scale
+        float p0, p1, p2, p3, t0, t1, t2, t3;
+        ffma2(p0, p1, __uint_as_float(sv[c]), __uint_as_float(sv[c + 1]), scale2, scale2, nl.x, nl.y);
+        ffma2(p2, p3, __uint_as_float(sv[c + 2]), __uint_as_float(sv[c + 3]), scale2, scale2, nl.z, nl.w);
+        p0 = fast_exp2(p0);
+        p1 = fast_exp2(p1);
+        p2 = fast_exp2(p2);
+        p3 = fast_exp2(p3);
+        if (edge) {
+          p0 = (c >= c_lo && c <= c_hi) ? p0 : 0.f;
+          p1 = (c + 1 >= c_lo && c + 1 <= c_hi) ? p1 : 0.f;
+          p2 = (c + 2 >= c_lo && c + 2 <= c_hi) ? p2 : 0.f;
+          p3 = (c + 3 >= c_lo && c + 3 <= c_hi) ? p3 : 0.f;
+        }
+        ffma2(t0, t1, __uint_as_float(dv[c]), __uint_as_float(dv[c + 1]), scale, scale, nd.x, nd.y);
+        ffma2(t2, t3, __uint_as_float(dv[c + 2]), __uint_as_float(dv[c + 3]), scale, scale, nd.z, nd.w);
+        fmul2(t0, t1, t0, t1, p0, p1);
+        fmul2(t2, t3, t2, t3, p2, p3);
+        pk[c / 2] = pack_bf16x2(p0, p1);
+        pk[c / 2 + 1] = pack_bf16x2(p2, p3);
+        dk[c / 2] = pack_bf16x2(t0, t1);
+        dk[c / 2 + 1] = pack_bf16x2(t2, t3);
+      }
+      // P^T into the S columns (two bf16 per column), dS^T into smem (SW128 rows)
+      tmem_st_32x32b_x32(trow + C::kTS0 + 128 * bj, pk);
+      uint8_t* ds_row = sDS(bj) + r * 128;
+#pragma unroll
+      for (int c16 = 0; c16 < 8; ++c16)
+        *reinterpret_cast<uint4*>(ds_row + ((c16 ^ (r & 7)) << 4)) =
+            make_uint4(dk[c16 * 4], dk[c16 * 4 + 1], dk[c16 * 4 + 2], dk[c16 * 4 + 3]);
+      tmem_st_wait();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[bj]);
+    }
+    // dK, dV of this key tile
+    __nv_bfloat16* dkr = reinterpret_cast<__nv_bfloat16*>(g.dk) +
+                         (static_cast<long long>(b) * a.S + ki) * g.dk_row + hk * D;
+    __nv_bfloat16* dvr = reinterpret_cast<__nv_bfloat16*>(g.dv) +
+                         (static_cast<long long>(b) * a.S + ki) * g.dv_row + hk * D;
+    if (n == 0) {
+      if (ki < a.S)
+        for (int c = 0; c < D; c += 8) {
+          *reinterpret_cast<uint4*>(dkr + c) = make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(dvr + c) = make_uint4(0, 0, 0, 0);
+        }
+    } else if (ok) {
+      if (warp_wait(mma_done, 0, abort_flag)) {
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t u[32], w32[32];
+          tmem_ld_32x32b_x32(trow + C::kTdV + c * 32, u);
+          tmem_ld_32x32b_x32(trow + C::kTdK + c * 32, w32);
+          tmem_ld_wait();
+          if (ki < a.S) {
+#pragma unroll
+            for (int e = 0; e < 32; e += 8) {
+              uint4 vv, kk4;
+              vv.x = pack_bf16x2(__uint_as_float(u[e]), __uint_as_float(u[e + 1]));
+              vv.y = pack_bf16x2(__uint_as_float(u[e + 2]), __uint_as_float(u[e + 3]));
+              vv.z = pack_bf16x2(__uint_as_float(u[e + 4]), __uint_as_float(u[e + 5]));
+              vv.w = pack_bf16x2(__uint_as_float(u[e + 6]), __uint_as_float(u[e + 7]));
+              kk4.x = pack_bf16x2(__uint_as_float(w32[e]), __uint_as_float(w32[e + 1]));
+              kk4.y = pack_bf16x2(__uint_as_float(w32[e + 2]), __uint_as_float(w32[e + 3]));
+              kk4.z = pack_bf16x2(__uint_as_float(w32[e + 4]), __uint_as_float(w32[e + 5]));
+              kk4.w = pack_bf16x2(__uint_as_float(w32[e + 6]), __uint_as_float(w32[e + 7]));
+              *reinterpret_cast<uint4*>(dvr + c * 32 + e) = vv;
+              *reinterpret_cast<uint4*>(dkr + c * 32 + e) = kk4;
+            }
+          }
+        }
+      } else {
+        record_status(a.status, 37);
+        *abort_flag = 1;
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == kB3MmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// Backward pre-pass for the head_dim-128 kernel: per (b, h) row of the stats
+// workspace [B*Hq][2][S64], -lse*log2(e) and -scale * rowsum(dO * O); queries
+// beyond S get -inf and 0.
+__global__ void attn_bwd_stats_kernel(const __nv_bfloat16* __restrict__ o, long long o_row,
+                                      const __nv_bfloat16* __restrict__ dout, long long do_row,
+                                      const float* __restrict__ lse, float* __restrict__ stats,
+                                      int B, int S, int S64, int H, int D, float scale) {
+  const long long wid = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const long long total = static_cast<long long>(B) * S64 * H;
+  if (wid >= total) return;
+  const int h = static_cast<int>(wid % H);
+  const long long bs = wid / H;
+  const int bb = static_cast<int>(bs / S64), s = static_cast<int>(bs % S64);
+  float* row = stats + (static_cast<long long>(bb) * H + h) * 2 * S64;
+  if (s >= S) {
+    if (lane == 0) {
+      row[s] = -INFINITY;
+      row[S64 + s] = 0.f;
+    }
+    return;
+  }
+  const long long tok = static_cast<long long>(bb) * S + s;
+  const __nv_bfloat16* orow = o + tok * o_row + h * D;
+  const __nv_bfloat16* drow = dout + tok * do_row + h * D;
+  float acc = 0.f;
+  for (int c = lane * 2; c < D; c += 64) {
+    const float2 x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(orow + c));
+    const float2 y = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(drow + c));
+    acc += x.x * y.x + x.y * y.y;
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) {
+    row[s] = -lse[(static_cast<long long>(bb) * H + h) * S + s] * kLog2e;
+    row[S64 + s] = -acc * scale;
+  }
+}
+
 // delta[b, h, s] = sum_d dO * O
 __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, long long o_row,
                                   const __nv_bfloat16* __restrict__ dout, long long do_row,
@@ -805,23 +1239,9 @@ __global__ void attn_dq_cast_kernel(const float* __restrict__ acc, __nv_bfloat16
 }
 
 // ------------------------------------------------------------------- host side
-static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    cudaDriverEntryPointQueryResult q;
-    void* p = nullptr;
-    PLG_CUDA_CHECK(cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000,
-                                                    cudaEnableDefault, &q));
-    if (q != cudaDriverEntryPointSuccess || p == nullptr)
-      throw std::runtime_error("cuTensorMapEncodeTiled entry point not found");
-    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
-// [B, S, H, d] bf16 with token stride `row` (elements); box = 64 x 1 x 128 x 1
-static CUtensorMap map_bshd(const void* base, int B, int S, int H, int d, long long row) {
+// [B, S, H, d] bf16 with token stride `row` (elements); box = 64 x 1 x box_rows x 1
+static CUtensorMap map_bshd(const void* base, int B, int S, int H, int d, long long row,
+                            int box_rows = 128) {
   if (reinterpret_cast<uintptr_t>(base) & 15) throw std::invalid_argument("attention: base not 16B aligned");
   if ((row * 2) % 16) throw std::invalid_argument("attention: token stride must be a multiple of 8");
   CUtensorMap m;
@@ -829,12 +1249,10 @@ static CUtensorMap map_bshd(const void* base, int B, int S, int H, int d, long l
                         static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(B)};
   cuuint64_t strides[3] = {static_cast<cuuint64_t>(d) * 2, static_cast<cuuint64_t>(row) * 2,
                            static_cast<cuuint64_t>(row) * 2 * S};
-  cuuint32_t box[4] = {64, 1, 128, 1};
+  cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(box_rows), 1};
   cuuint32_t es[4] = {1, 1, 1, 1};
-  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims,
-                           strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = encode_tensor_map(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base),
+                                 dims, strides, box, es, CU_TENSOR_MAP_SWIZZLE_128B);
   if (r != CUDA_SUCCESS)
     throw std::runtime_error("attention: cuTensorMapEncodeTiled failed (" + std::to_string(r) +
                              ") dims {" + std::to_string(d) + "," + std::to_string(H) + "," +
@@ -851,6 +1269,17 @@ static void fwd_launch(const AttnArgs& a, cudaStream_t st) {
   CUtensorMap tk = map_bshd(a.k, a.B, a.S, a.Hk, D, a.k_row);
   CUtensorMap tv = map_bshd(a.v, a.B, a.S, a.Hk, D, a.v_row);
   set_max_smem_once(reinterpret_cast<const void*>(attn_fwd_kernel<D>), C::kSmem);
+  static const int regs = [] {
+    cudaFuncAttributes fa;
+    PLG_CUDA_CHECK(cudaFuncGetAttributes(&fa, attn_fwd_kernel<D>));
+    return fa.numRegs;
+  }();
+  // the setmaxnreg split assumes this launch allocation; with fewer registers
+  // the softmax warpgroups' increase could never be granted
+  if (regs != kFwdRegsLaunch)
+    throw std::runtime_error("attention forward: kernel built with " + std::to_string(regs) +
+                             " registers per thread, the register split needs " +
+                             std::to_string(kFwdRegsLaunch));
   const int G = a.Hq / a.Hk;
   const int n_q = (a.S + BQ - 1) / BQ;
   const int pair_heads = (G % 2 == 0) ? 1 : 0;
@@ -858,6 +1287,44 @@ static void fwd_launch(const AttnArgs& a, cudaStream_t st) {
   const long long ctas = units * (pair_heads ? a.Hq / 2 : a.Hq) * a.B;
   if (ctas > 0x7fffffffLL) throw std::invalid_argument("attention: problem too large for one launch");
   attn_fwd_kernel<D><<<static_cast<unsigned>(ctas), kFwdThreads, C::kSmem, st>>>(tq, tk, tv, a, pair_heads);
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+static void bwd3_launch(const AttnBwdArgs& g, cudaStream_t st) {
+  using C = Bwd3;
+  const AttnArgs& a = g.f;
+  CUtensorMap tq = map_bshd(a.q, a.B, a.S, a.Hq, C::D, a.q_row, kBQ3);
+  CUtensorMap tk = map_bshd(a.k, a.B, a.S, a.Hk, C::D, a.k_row);
+  CUtensorMap tv = map_bshd(a.v, a.B, a.S, a.Hk, C::D, a.v_row);
+  CUtensorMap td = map_bshd(g.dout, a.B, a.S, a.Hq, C::D, g.do_row, kBQ3);
+  set_max_smem_once(reinterpret_cast<const void*>(attn_bwd3_kernel), C::kSmem);
+  static const int regs = [] {
+    cudaFuncAttributes fa;
+    PLG_CUDA_CHECK(cudaFuncGetAttributes(&fa, attn_bwd3_kernel));
+    return fa.numRegs;
+  }();
+  if (regs != kB3RegsLaunch)
+    throw std::runtime_error("attention backward: kernel built with " + std::to_string(regs) +
+                             " registers per thread, the register split needs " +
+                             std::to_string(kB3RegsLaunch));
+  const int S64 = (a.S + kBQ3 - 1) / kBQ3 * kBQ3;
+  const long long srows = static_cast<long long>(a.B) * S64 * a.Hq;
+  attn_bwd_stats_kernel<<<(srows * 32 + 255) / 256, 256, 0, st>>>(
+      reinterpret_cast<const __nv_bfloat16*>(a.o), a.o_row,
+      reinterpret_cast<const __nv_bfloat16*>(g.dout), g.do_row, a.lse, g.delta, a.B, a.S, S64,
+      a.Hq, C::D, a.scale);
+  PLG_CUDA_CHECK(cudaGetLastError());
+  const long long rows = static_cast<long long>(a.B) * a.S * a.Hq;
+  PLG_CUDA_CHECK(cudaMemsetAsync(g.dq_acc, 0, sizeof(float) * rows * C::D, st));
+  const long long ctas = static_cast<long long>((a.S + BKV - 1) / BKV) * a.Hk * a.B;
+  if (ctas > 0x7fffffffLL) throw std::invalid_argument("attention: problem too large for one launch");
+  attn_bwd3_kernel<<<static_cast<unsigned>(ctas), kB3Threads, C::kSmem, st>>>(tq, tk, tv, td, g);
+  PLG_CUDA_CHECK(cudaGetLastError());
+  const long long nel = rows * C::D;
+  long long blocks = (nel + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  attn_dq_cast_kernel<<<blocks, 256, 0, st>>>(g.dq_acc, reinterpret_cast<__nv_bfloat16*>(g.dq),
+                                              g.dq_row, a.B, a.S, a.Hq, C::D);
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -898,7 +1365,7 @@ void attn_fwd(const AttnArgs& a, cudaStream_t st) {
 void attn_bwd(const AttnBwdArgs& g, cudaStream_t st) {
   const AttnArgs& a = g.f;
   if (a.Hq % a.Hk) throw std::invalid_argument("attention: Hq must be a multiple of Hk");
-  if (a.d == 128) return attn::bwd_launch<128>(g, st);
+  if (a.d == 128) return attn::bwd3_launch(g, st);
   if (a.d == 64) return attn::bwd_launch<64>(g, st);
   throw std::invalid_argument("attention: head_dim must be 64 or 128");
 }

@@ -286,7 +286,6 @@ plg::AttnArgs attn_args(const at::Tensor& q, const at::Tensor& k, const at::Tens
   a.causal = causal ? 1 : 0;
   a.window = static_cast<int>(window);
   a.status = status_ptr(status);
-  a.debug = 0;
   return a;
 }
 
@@ -315,7 +314,11 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at:
   b.dout = dout.data_ptr(); b.do_row = dout.stride(1);
   b.dq = dq.data_ptr(); b.dk = dk.data_ptr(); b.dv = dv.data_ptr();
   b.dq_row = dq.stride(1); b.dk_row = dk.stride(1); b.dv_row = dv.stride(1);
-  TORCH_CHECK(is_f32(dq_acc) && dq_acc.is_contiguous() && is_f32(delta), "attention workspaces");
+  TORCH_CHECK(is_f32(dq_acc) && dq_acc.is_contiguous() && is_f32(delta) && delta.is_contiguous(),
+              "attention workspaces");
+  TORCH_CHECK(dq_acc.numel() >= static_cast<int64_t>(b.f.B) * b.f.S * b.f.Hq * b.f.d &&
+                  delta.numel() >= plg::attn_bwd_stats_floats(b.f.B, b.f.Hq, b.f.S),
+              "attention backward workspaces too small");
   b.dq_acc = dq_acc.data_ptr<float>();
   b.delta = delta.data_ptr<float>();
   plg::attn_bwd(b, cur_stream());

@@ -232,6 +232,25 @@ __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// 1-D bulk copy global -> shared (no multicast): both addresses 16-byte aligned,
+// bytes a multiple of 16; completes tx on bar.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes),
+        "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void fmul2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
 // named barrier over a subset of warps (id 1..15; count = threads, multiple of 32)
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
@@ -371,6 +390,19 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
       : "memory");
 }
 
+// Per-warpgroup register reallocation. Every warp of a warpgroup must execute
+// the same one; increases block until other warpgroups have released enough of
+// the registers the CTA was launched with, so callers must check that the split
+// fits the launch allocation (see the attention forward launcher).
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -391,11 +423,45 @@ __device__ __forceinline__ void tmem_st_wait() {
     }                                                                                 \
   } while (0)
 
+#include <cudaTypedefs.h>
+
 #include <mutex>
 #include <set>
+#include <stdexcept>
+#include <string>
 #include <utility>
 
 namespace plg {
+// cuTensorMapEncodeTiled through the runtime's driver entry point. The driver
+// call needs a current context on the calling thread; a thread that has made no
+// runtime call yet (autograd's per-device worker, for one) can lack it, so the
+// device's primary context is made current first (cudaSetDevice does that).
+inline CUresult encode_tensor_map(CUtensorMap* m, CUtensorMapDataType dtype, cuuint32_t rank,
+                                  void* base, const cuuint64_t* dims, const cuuint64_t* strides,
+                                  const cuuint32_t* box, const cuuint32_t* elem_strides,
+                                  CUtensorMapSwizzle swizzle) {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    PLG_CUDA_CHECK(cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000,
+                                                    cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || p == nullptr)
+      throw std::runtime_error("cuTensorMapEncodeTiled entry point not found");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  thread_local int current_dev = -1;
+  int dev = 0;
+  PLG_CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev != current_dev) {
+    PLG_CUDA_CHECK(cudaSetDevice(dev));
+    current_dev = dev;
+  }
+  return fn(m, dtype, rank, base, dims, strides, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
 // Raise a kernel's dynamic shared memory limit once per (kernel, device): the
 // attribute belongs to the device context, so a process driving several GPUs
 // must set it on each.

@@ -360,21 +360,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 // --------------------------------------------------------------------------
 // host side
 // --------------------------------------------------------------------------
-static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    cudaDriverEntryPointQueryResult q;
-    void* p = nullptr;
-    PLG_CUDA_CHECK(cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000,
-                                                    cudaEnableDefault, &q));
-    if (q != cudaDriverEntryPointSuccess || p == nullptr)
-      throw std::runtime_error("cuTensorMapEncodeTiled entry point not found");
-    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
 // 2-D bf16 tensor map over a row-major [rows, cols] matrix with leading dim `ld`
 // (elements); box = box_cols x box_rows; 128-byte swizzle.
 static CUtensorMap make_map_2d(const void* base, long long rows, long long cols, long long ld,
@@ -384,10 +369,8 @@ static CUtensorMap make_map_2d(const void* base, long long rows, long long cols,
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
   cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base),
-                               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = encode_tensor_map(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base),
+                                 dims, strides, box, estr, CU_TENSOR_MAP_SWIZZLE_128B);
   if (r != CUDA_SUCCESS)
     throw std::runtime_error("cuTensorMapEncodeTiled failed with code " + std::to_string(r));
   return m;

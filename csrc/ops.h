@@ -114,7 +114,6 @@ struct AttnArgs {
   int causal;
   int window;                                    // > 0: keys k with q - k < window only
   int* status;
-  int debug;                                     // bisection switches (0 in production)
 };
 void attn_fwd(const AttnArgs& a, cudaStream_t stream);
 struct AttnBwdArgs {
@@ -123,8 +122,12 @@ struct AttnBwdArgs {
   void* dq; void* dk; void* dv;                  // bf16, same layouts as q, k, v
   long long dq_row, dk_row, dv_row;
   float* dq_acc;                                 // fp32 workspace [B, S, Hq, d]
-  float* delta;                                  // fp32 workspace [B, Hq, S]
+  float* delta;                                  // fp32 workspace, attn_bwd_stats_floats()
 };
+// floats the backward's stats workspace needs: [B * Hq][2][S rounded up to 64]
+inline long long attn_bwd_stats_floats(int B, int Hq, int S) {
+  return static_cast<long long>(B) * Hq * 2 * ((S + 63) / 64 * 64);
+}
 void attn_bwd(const AttnBwdArgs& a, cudaStream_t stream);
 
 }  // namespace plg

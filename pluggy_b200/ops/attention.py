@@ -59,7 +59,8 @@ def attn_bwd(q, k, v, o, lse, do, *, causal=True, window=0, scale=None, dq=None,
     dv = torch.empty(v.shape, dtype=v.dtype, device=v.device) if dv is None else dv
     do = do.contiguous()
     dq_acc = torch.empty((B, S, Hq, d), dtype=torch.float32, device=q.device)
-    delta = torch.empty((B, Hq, S), dtype=torch.float32, device=q.device)
+    # [B * Hq][2][S rounded up to 64]: -lse*log2(e) and -scale*rowsum(dO*O)
+    delta = torch.empty(B * Hq * 2 * ((S + 63) // 64 * 64), dtype=torch.float32, device=q.device)
     ext().attn_bwd(q, k, v, o, lse, do, dq, dk, dv, dq_acc, delta, float(scale), bool(causal),
                    int(window or 0), status_word(q.device))
     return dq, dk, dv
