@@ -297,67 +297,94 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
       }
     }
-  } else if (warp == kFwdMmaWarp) {
-    if (lane == 0 && n > 0) {
-      constexpr uint32_t id_s = make_idesc_bf16_f32(128, 128, false, false);
-      constexpr uint32_t id_o = make_idesc_bf16_f32(128, D, false, true);
-      const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV);
-      auto act = [&](int w, int t) { return t >= qtl[w].lo && t <= qtl[w].hi; };
-      auto issue_s = [&](int w, int i) {
-        const int st = i & 1;
+  } else if (warp == kFwdMmaWarp && n > 0) {
+    // the whole warp walks the loop (warp-uniform descriptors); one lane issues
+    const bool leader = elect_one_sync();
+    constexpr uint32_t id_s = make_idesc_bf16_f32(128, 128, false, false);
+    constexpr uint32_t id_o = make_idesc_bf16_f32(128, D, false, true);
+    const uint64_t dQ0 = make_smem_desc(smem_u32(sQ), 16, 1024, kLayoutSW128);
+    const uint64_t dK0 = make_smem_desc(smem_u32(sK), 16, 1024, kLayoutSW128);
+    const uint64_t dV0 = make_smem_desc(smem_u32(sV), kBox, 1024, kLayoutSW128);
+    const int lo0 = qtl[0].lo, hi0 = qtl[0].hi, lo1 = qtl[1].lo, hi1 = qtl[1].hi;
+    auto issue_s = [&](int w, int i) {
+      const int st = i & 1;
+      if (leader) {
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
-          tc_mma_ss(tmem + w * 128, desc_kmajor(aQ + w * C::kTile, kk),
-                    desc_kmajor(aK + st * C::kTile, kk), id_s, kk > 0 ? 1u : 0u);
+          tc_mma_ss(tmem + w * 128, desc_advance(dQ0, w * C::kTile + (kk >> 2) * kBox + (kk & 3) * 32),
+                    desc_advance(dK0, st * C::kTile + (kk >> 2) * kBox + (kk & 3) * 32), id_s,
+                    kk > 0 ? 1u : 0u);
         tc_commit(&s_full[w]);
-      };
-      bool ok = mbar_wait_bounded(q_full, 0, abort_flag) && mbar_wait_bounded(&k_full[0], 0, abort_flag);
-      if (ok) {
-        tc_fence_after();
-        for (int w = 0; w < 2; ++w)
-          if (act(w, t_lo)) issue_s(w, 0);
-        tc_commit(&k_empty[0]);
       }
-      for (int i = 0; i < n && ok; ++i) {
-        const int t = t_lo + i, st = i & 1;
-        if (!mbar_wait_bounded(&v_full[st], (i >> 1) & 1, abort_flag)) { record_status(a.status, 12); ok = false; break; }
-        bool k_next = false;
-        for (int w = 0; w < 2 && ok; ++w) {
-          if (act(w, t)) {
-            const int u = t - qtl[w].lo;
-            if (!mbar_wait_bounded(&p_full[w], u & 1, abort_flag)) { record_status(a.status, 13); ok = false; break; }
-            tc_fence_after();
+      __syncwarp();
+    };
+    bool ok = warp_wait(q_full, 0, abort_flag) && warp_wait(&k_full[0], 0, abort_flag);
+    if (ok) {
+      tc_fence_after();
+      if (t_lo >= lo0 && t_lo <= hi0) issue_s(0, 0);
+      if (t_lo >= lo1 && t_lo <= hi1) issue_s(1, 0);
+      if (leader) tc_commit(&k_empty[0]);
+      __syncwarp();
+    }
+    for (int i = 0; i < n && ok; ++i) {
+      const int t = t_lo + i, st = i & 1;
+      if (!warp_wait(&v_full[st], (i >> 1) & 1, abort_flag)) {
+        if (leader) record_status(a.status, 12);
+        ok = false;
+        break;
+      }
+      bool k_next = false;
 #pragma unroll
-            for (int kk = 0; kk < BKV / 16; ++kk)
-              tc_mma_ts(tmem + C::kTO + w * D, tmem + w * 128 + kk * 8,
-                        desc_mnmajor(aV + st * C::kTile, kk), id_o, (u > 0 || kk > 0) ? 1u : 0u);
+      for (int w = 0; w < 2; ++w) {
+        const int lo = w == 0 ? lo0 : lo1, hi = w == 0 ? hi0 : hi1;
+        if (ok && t >= lo && t <= hi) {
+          const int u = t - lo;
+          if (!warp_wait(&p_full[w], u & 1, abort_flag)) {
+            if (leader) record_status(a.status, 13);
+            ok = false;
+          } else {
+            tc_fence_after();
+            if (leader) {
+#pragma unroll
+              for (int kk = 0; kk < BKV / 16; ++kk)
+                tc_mma_ts(tmem + C::kTO + w * D, tmem + w * 128 + kk * 8,
+                          desc_advance(dV0, st * C::kTile + kk * 2048), id_o,
+                          (u > 0 || kk > 0) ? 1u : 0u);
+            }
+            __syncwarp();
           }
-          if (i + 1 < n && act(w, t + 1)) {
-            if (!k_next) {
-              if (!mbar_wait_bounded(&k_full[(i + 1) & 1], ((i + 1) >> 1) & 1, abort_flag)) {
-                record_status(a.status, 14);
-                ok = false;
-                break;
-              }
+        }
+        if (ok && i + 1 < n && t + 1 >= lo && t + 1 <= hi) {
+          if (!k_next) {
+            if (!warp_wait(&k_full[(i + 1) & 1], ((i + 1) >> 1) & 1, abort_flag)) {
+              if (leader) record_status(a.status, 14);
+              ok = false;
+            } else {
               tc_fence_after();
               k_next = true;
             }
-            issue_s(w, i + 1);
           }
+          if (ok) issue_s(w, i + 1);
         }
-        if (!ok) break;
+      }
+      if (!ok) break;
+      if (leader) {
         tc_commit(&v_empty[st]);
         if (i + 1 < n) tc_commit(&k_empty[(i + 1) & 1]);
       }
-      if (!ok) {
-        record_status(a.status, kTimeoutTmaFull);
-        *abort_flag = 1;
-      }
+      __syncwarp();
+    }
+    if (!ok) {
+      if (leader) record_status(a.status, kTimeoutTmaFull);
+      *abort_flag = 1;
+    }
+    if (leader) {
       tc_commit(&o_done[0]);
       tc_commit(&o_done[1]);
       tc_commit(mma_done);
-      if (!mbar_wait_bounded(mma_done, 0, nullptr)) record_status(a.status, kTimeoutDrain);
     }
+    __syncwarp();
+    if (!warp_wait(mma_done, 0, nullptr) && leader) record_status(a.status, kTimeoutDrain);
   }
   } else {
     setmaxnreg_inc<kFwdRegsSoftmax>();
@@ -825,9 +852,11 @@ struct Bwd3 {
   static constexpr int kV = kKVTile;
   static constexpr int kQ = 2 * kKVTile;                      // [stage] Q, dO
   static constexpr int kDS = kQ + kStages * 2 * kQTile;       // [2] dS^T [128 x 64] bf16
-  static constexpr int kStats = kDS + 2 * 128 * kBQ3 * 2;     // [stage] 2 x 64 floats
+  static constexpr int kDQ = kDS + 2 * 128 * kBQ3 * 2;        // [4 warps] dQ [64 q x 32 d] fp32
+  static constexpr int kStats = kDQ + 4 * kBQ3 * 32 * 4;      // [stage] 2 x 64 floats
   static constexpr int kBar = kStats + kStages * 512;
   static constexpr int kSmem = kBar + 256 + 1024;             // + manual 1024 alignment
+  static_assert(kSmem <= 232448, "backward shared memory exceeds the per-CTA limit");
   static constexpr int kTdV = 0, kTdK = 128;
   static constexpr int kTS0 = 256, kTdP0 = 320;               // + 128 * b
 };
@@ -842,10 +871,21 @@ __device__ __forceinline__ uint64_t desc_mnmajor64(uint32_t base, int kk) {
   return make_smem_desc(base + kk * 2048, Bwd3::kQBox, 1024, kLayoutSW128);
 }
 
+// Per-step timeline of CTA 0 (SM clock), recorded only when a trace buffer is
+// given: 0 producer issued Q/dO, 1 MMA issued S/dP(j), 2 MMA saw P(j) ready,
+// 3 MMA issued dQ(j), 4 compute saw S/dP(j), 5 compute released P(j), 6 drain saw
+// dQ(j), 7 drain released the TMEM columns, 8 drain issued the reductions,
+// 9 compute has S/dP in registers, 10 compute finished the math, 11 compute's
+// P / dS stores completed.
+__device__ __forceinline__ void trace_ev(long long* trace, int ev, int j) {
+  if (trace != nullptr && blockIdx.x == 0 && j < kAttnTraceSteps)
+    trace[ev * kAttnTraceSteps + j] = clock64();
+}
+
 __global__ void __launch_bounds__(kB3Threads, 1)
     attn_bwd3_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                     AttnBwdArgs g) {
+                     const __grid_constant__ CUtensorMap tmDQ, AttnBwdArgs g) {
   using C = Bwd3;
   constexpr int D = C::D;
   const AttnArgs& a = g.f;
@@ -938,6 +978,7 @@ __global__ void __launch_bounds__(kB3Threads, 1)
         const float* st = g.delta + (static_cast<long long>(b) * a.Hq + h) * 2 * S64 + q0;
         bulk_load(sStats(s), st, 256, &qd_full[s]);
         bulk_load(sStats(s) + 64, st + S64, 256, &qd_full[s]);
+        trace_ev(g.trace, 0, j);
         last = j;
       }
       if (!ok) {
@@ -948,37 +989,51 @@ __global__ void __launch_bounds__(kB3Threads, 1)
           if (j >= 0 && !mbar_wait_bounded(&qd_full[j % C::kStages], (j / C::kStages) & 1, nullptr))
             record_status(a.status, kTimeoutDrain);
       }
-    } else if (warp == kB3MmaWarp && lane == 0 && n > 0) {
+    } else if (warp == kB3MmaWarp && n > 0) {
       // ------------------------------------------------------------ MMA issuer
+      // The whole warp walks the loop (descriptors stay warp-uniform); the
+      // elected lane issues the MMAs and commits.
+      const bool leader = elect_one_sync();
       constexpr uint32_t id_s = make_idesc_bf16_f32(128, kBQ3, false, false);  // S^T, dP^T
       constexpr uint32_t id_kv = make_idesc_bf16_f32(128, D, false, true);     // dV, dK
       constexpr uint32_t id_dq = make_idesc_bf16_f32(128, kBQ3, true, true);   // dQ^T
-      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV);
-      bool ok = mbar_wait_bounded(kv_full, 0, abort_flag);
-      if (!ok) record_status(a.status, 31);
+      const uint64_t kK = make_smem_desc(smem_u32(sK), 16, 1024, kLayoutSW128);
+      const uint64_t kV = make_smem_desc(smem_u32(sV), 16, 1024, kLayoutSW128);
+      const uint64_t mK = make_smem_desc(smem_u32(sK), kBox, 1024, kLayoutSW128);
+      bool ok = warp_wait(kv_full, 0, abort_flag);
+      if (!ok && leader) record_status(a.status, 31);
       auto issue_sdp = [&](int j) -> bool {
         const int s = j % C::kStages, bj = j & 1;
-        if (!mbar_wait_bounded(&qd_full[s], (j / C::kStages) & 1, abort_flag)) {
-          record_status(a.status, 32);
+        if (!warp_wait(&qd_full[s], (j / C::kStages) & 1, abort_flag)) {
+          if (leader) record_status(a.status, 32);
           return false;
         }
         tc_fence_after();
-        const uint32_t aQ = smem_u32(sQ(s)), aDO = smem_u32(sDO(s));
+        const uint64_t kQ = make_smem_desc(smem_u32(sQ(s)), 16, 1024, kLayoutSW128);
+        const uint64_t kDO = make_smem_desc(smem_u32(sDO(s)), 16, 1024, kLayoutSW128);
+        if (leader) {
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          tc_mma_ss(tmem + C::kTS0 + 128 * bj, desc_kmajor(aK, kk), desc_kmajor64(aQ, kk), id_s,
-                    kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < D / 16; ++kk)
+            tc_mma_ss(tmem + C::kTS0 + 128 * bj, desc_advance(kK, (kk >> 2) * kBox + (kk & 3) * 32),
+                      desc_advance(kQ, (kk >> 2) * C::kQBox + (kk & 3) * 32), id_s, kk > 0 ? 1u : 0u);
+        }
+        __syncwarp();
         // dP_b still holds dQ^T of step j-2 until the drain warps have read it
-        if (j >= 2 && !mbar_wait_bounded(&dq_free[bj], ((j - 2) >> 1) & 1, abort_flag)) {
-          record_status(a.status, 33);
+        if (j >= 2 && !warp_wait(&dq_free[bj], ((j - 2) >> 1) & 1, abort_flag)) {
+          if (leader) record_status(a.status, 33);
           return false;
         }
         tc_fence_after();
+        if (leader) {
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          tc_mma_ss(tmem + C::kTdP0 + 128 * bj, desc_kmajor(aV, kk), desc_kmajor64(aDO, kk), id_s,
-                    kk > 0 ? 1u : 0u);
-        tc_commit(&s_full[bj]);
+          for (int kk = 0; kk < D / 16; ++kk)
+            tc_mma_ss(tmem + C::kTdP0 + 128 * bj, desc_advance(kV, (kk >> 2) * kBox + (kk & 3) * 32),
+                      desc_advance(kDO, (kk >> 2) * C::kQBox + (kk & 3) * 32), id_s,
+                      kk > 0 ? 1u : 0u);
+          tc_commit(&s_full[bj]);
+          trace_ev(g.trace, 1, j);
+        }
+        __syncwarp();
         return true;
       };
       if (ok) ok = issue_sdp(0);
@@ -988,38 +1043,48 @@ __global__ void __launch_bounds__(kB3Threads, 1)
           break;
         }
         const int s = j % C::kStages, bj = j & 1;
-        if (!mbar_wait_bounded(&p_full[bj], (j >> 1) & 1, abort_flag)) {
-          record_status(a.status, 34);
+        if (!warp_wait(&p_full[bj], (j >> 1) & 1, abort_flag)) {
+          if (leader) record_status(a.status, 34);
           ok = false;
           break;
         }
+        if (leader) trace_ev(g.trace, 2, j);
         tc_fence_after();
-        const uint32_t aQ = smem_u32(sQ(s)), aDO = smem_u32(sDO(s)), aDS = smem_u32(sDS(bj));
+        const uint64_t mQ = make_smem_desc(smem_u32(sQ(s)), C::kQBox, 1024, kLayoutSW128);
+        const uint64_t mDO = make_smem_desc(smem_u32(sDO(s)), C::kQBox, 1024, kLayoutSW128);
+        const uint64_t kDS = make_smem_desc(smem_u32(sDS(bj)), 16, 1024, kLayoutSW128);
+        const uint64_t mDS = make_smem_desc(smem_u32(sDS(bj)), kBox, 1024, kLayoutSW128);
+        const uint32_t acc0 = j > 0 ? 1u : 0u;
+        if (leader) {
 #pragma unroll
-        for (int kk = 0; kk < kBQ3 / 16; ++kk)
-          tc_mma_ts(tmem + C::kTdV, tmem + C::kTS0 + 128 * bj + kk * 8, desc_mnmajor64(aDO, kk),
-                    id_kv, (j > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kBQ3 / 16; ++kk)
+            tc_mma_ts(tmem + C::kTdV, tmem + C::kTS0 + 128 * bj + kk * 8, desc_advance(mDO, kk * 2048),
+                      id_kv, kk > 0 ? 1u : acc0);
 #pragma unroll
-        for (int kk = 0; kk < kBQ3 / 16; ++kk)
-          tc_mma_ss(tmem + C::kTdK, desc_kmajor(aDS, kk), desc_mnmajor64(aQ, kk), id_kv,
-                    (j > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(&qd_empty[s]);
+          for (int kk = 0; kk < kBQ3 / 16; ++kk)
+            tc_mma_ss(tmem + C::kTdK, desc_advance(kDS, kk * 32), desc_advance(mQ, kk * 2048), id_kv,
+                      kk > 0 ? 1u : acc0);
+          tc_commit(&qd_empty[s]);
 #pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk)
-          tc_mma_ss(tmem + C::kTdP0 + 128 * bj, desc_mnmajor(aK, kk), desc_mnmajor(aDS, kk), id_dq,
-                    kk > 0 ? 1u : 0u);
-        tc_commit(&dq_full[bj]);
+          for (int kk = 0; kk < BKV / 16; ++kk)
+            tc_mma_ss(tmem + C::kTdP0 + 128 * bj, desc_advance(mK, kk * 2048),
+                      desc_advance(mDS, kk * 2048), id_dq, kk > 0 ? 1u : 0u);
+          tc_commit(&dq_full[bj]);
+          trace_ev(g.trace, 3, j);
+        }
+        __syncwarp();
       }
       if (!ok) *abort_flag = 1;
-      tc_commit(mma_done);
-      if (!mbar_wait_bounded(mma_done, 0, nullptr)) record_status(a.status, kTimeoutDrain);
+      if (leader) tc_commit(mma_done);
+      __syncwarp();
+      if (!warp_wait(mma_done, 0, nullptr) && leader) record_status(a.status, kTimeoutDrain);
     }
   } else if (warp >= 4) {
     setmaxnreg_dec<kB3RegsDrain>();
     // -------------------------------------------------------------- dQ drain
-    const int quad = warp & 3;
-    const int dcol = quad * 32 + lane;  // TMEM lane = head-dim index of dQ^T
+    const int quad = warp & 3;          // TMEM lanes = head-dim rows 32*quad.. of dQ^T
     const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    float* stg = reinterpret_cast<float*>(smem + C::kDQ) + quad * kBQ3 * 32;
     for (int j = 0; j < n; ++j) {
       const int bj = j & 1;
       if (!warp_wait(&dq_full[bj], (j >> 1) & 1, abort_flag)) {
@@ -1027,6 +1092,7 @@ __global__ void __launch_bounds__(kB3Threads, 1)
         *abort_flag = 1;
         break;
       }
+      if (lane == 0 && quad == 0) trace_ev(g.trace, 6, j);
       tc_fence_after();
       uint32_t v[kBQ3];
       tmem_ld_32x32b_x32(trow + C::kTdP0 + 128 * bj, *reinterpret_cast<uint32_t(*)[32]>(v));
@@ -1035,14 +1101,24 @@ __global__ void __launch_bounds__(kB3Threads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&dq_free[bj]);
-      const int h = hk * G + j % G, q0 = (qb_lo + j / G) * kBQ3;
-      const long long stride = static_cast<long long>(a.Hq) * D;
-      float* dst = g.dq_acc + ((static_cast<long long>(b) * a.S + q0) * a.Hq + h) * D + dcol;
-      const int nv = min(kBQ3, a.S - q0);
+      if (lane == 0 && quad == 0) trace_ev(g.trace, 7, j);
+      // stage this warp's [64 q x 32 d] slice and reduce-add it into the fp32
+      // workspace with one bulk tensor operation (rows past S are clipped)
+      if (lane == 0) bulk_wait_group_read<0>();  // previous slice has left smem
+      __syncwarp();
 #pragma unroll
-      for (int c = 0; c < kBQ3; ++c)
-        if (c < nv) atomicAdd(dst + c * stride, __uint_as_float(v[c]));
+      for (int c = 0; c < kBQ3; ++c) stg[c * 32 + lane] = __uint_as_float(v[c]);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const int h = hk * G + j % G, q0 = (qb_lo + j / G) * kBQ3;
+        tma_reduce_add_4d(&tmDQ, stg, quad * 32, h, q0, b);
+        bulk_commit_group();
+      }
+      if (lane == 0 && quad == 0) trace_ev(g.trace, 8, j);
     }
+    if (lane == 0) bulk_wait_group<0>();  // reductions done before the CTA exits
+    __syncwarp();
   } else {
     setmaxnreg_inc<kB3RegsComp>();
     // ----------------------------------------------------------- P / dS warps
@@ -1061,6 +1137,7 @@ __global__ void __launch_bounds__(kB3Threads, 1)
         ok = false;
         break;
       }
+      if (lane == 0 && quad == 0) trace_ev(g.trace, 4, j);
       tc_fence_after();
       const int q0 = (qb_lo + j / G) * kBQ3;
       uint32_t sv[kBQ3], dv[kBQ3];
@@ -1074,6 +1151,7 @@ __global__ void __launch_bounds__(kB3Threads, 1)
       const int c_lo = a.causal ? ki - q0 : -(1 << 30);
       const int c_hi = a.window > 0 ? ki + a.window - 1 - q0 : (1 << 30);
       tmem_ld_wait();
+      if (lane == 0 && quad == 0) trace_ev(g.trace, 9, j);
       uint32_t pk[kBQ3 / 2], dk[kBQ3 / 2];
 #pragma unroll
       for (int c = 0; c < kBQ3; c += 4) {
@@ -1101,6 +1179,7 @@ __global__ void __launch_bounds__(kB3Threads, 1)
         dk[c / 2] = pack_bf16x2(t0, t1);
         dk[c / 2 + 1] = pack_bf16x2(t2, t3);
       }
+      if (lane == 0 && quad == 0) trace_ev(g.trace, 10, j);
       // P^T into the S columns (two bf16 per column), dS^T into smem (SW128 rows)
       tmem_st_32x32b_x32(trow + C::kTS0 + 128 * bj, pk);
       uint8_t* ds_row = sDS(bj) + r * 128;
@@ -1110,9 +1189,11 @@ __global__ void __launch_bounds__(kB3Threads, 1)
             make_uint4(dk[c16 * 4], dk[c16 * 4 + 1], dk[c16 * 4 + 2], dk[c16 * 4 + 3]);
       tmem_st_wait();
       fence_proxy_async_smem();
+      if (lane == 0 && quad == 0) trace_ev(g.trace, 11, j);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[bj]);
+      if (lane == 0 && quad == 0) trace_ev(g.trace, 5, j);
     }
     // dK, dV of this key tile
     __nv_bfloat16* dkr = reinterpret_cast<__nv_bfloat16*>(g.dk) +
@@ -1262,6 +1343,22 @@ static CUtensorMap map_bshd(const void* base, int B, int S, int H, int d, long l
   return m;
 }
 
+// fp32 dQ workspace [B, S, Hq, d] for bulk reduce-add; box = 32 d x 1 x 64 q x 1
+static CUtensorMap map_dq_acc(float* base, int B, int S, int H, int d) {
+  CUtensorMap m;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(H),
+                        static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(d) * 4, static_cast<cuuint64_t>(H) * d * 4,
+                           static_cast<cuuint64_t>(H) * d * 4 * S};
+  cuuint32_t box[4] = {32, 1, static_cast<cuuint32_t>(kBQ3), 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = encode_tensor_map(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, dims, strides, box, es,
+                                 CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (r != CUDA_SUCCESS)
+    throw std::runtime_error("attention: dQ workspace tensor map failed (" + std::to_string(r) + ")");
+  return m;
+}
+
 template <int D>
 static void fwd_launch(const AttnArgs& a, cudaStream_t st) {
   using C = Fwd<D>;
@@ -1297,6 +1394,7 @@ static void bwd3_launch(const AttnBwdArgs& g, cudaStream_t st) {
   CUtensorMap tk = map_bshd(a.k, a.B, a.S, a.Hk, C::D, a.k_row);
   CUtensorMap tv = map_bshd(a.v, a.B, a.S, a.Hk, C::D, a.v_row);
   CUtensorMap td = map_bshd(g.dout, a.B, a.S, a.Hq, C::D, g.do_row, kBQ3);
+  CUtensorMap tdq = map_dq_acc(g.dq_acc, a.B, a.S, a.Hq, C::D);
   set_max_smem_once(reinterpret_cast<const void*>(attn_bwd3_kernel), C::kSmem);
   static const int regs = [] {
     cudaFuncAttributes fa;
@@ -1318,7 +1416,7 @@ static void bwd3_launch(const AttnBwdArgs& g, cudaStream_t st) {
   PLG_CUDA_CHECK(cudaMemsetAsync(g.dq_acc, 0, sizeof(float) * rows * C::D, st));
   const long long ctas = static_cast<long long>((a.S + BKV - 1) / BKV) * a.Hk * a.B;
   if (ctas > 0x7fffffffLL) throw std::invalid_argument("attention: problem too large for one launch");
-  attn_bwd3_kernel<<<static_cast<unsigned>(ctas), kB3Threads, C::kSmem, st>>>(tq, tk, tv, td, g);
+  attn_bwd3_kernel<<<static_cast<unsigned>(ctas), kB3Threads, C::kSmem, st>>>(tq, tk, tv, td, tdq, g);
   PLG_CUDA_CHECK(cudaGetLastError());
   const long long nel = rows * C::D;
   long long blocks = (nel + 255) / 256;

@@ -301,7 +301,8 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at:
 void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o,
               at::Tensor& lse, const at::Tensor& dout, at::Tensor& dq, at::Tensor& dk,
               at::Tensor& dv, at::Tensor& dq_acc, at::Tensor& delta, double scale, bool causal,
-              int64_t window, const c10::optional<at::Tensor>& status) {
+              int64_t window, const c10::optional<at::Tensor>& status,
+              const c10::optional<at::Tensor>& trace) {
   check_cuda(q, "q");
   const c10::cuda::CUDAGuard guard(q.device());
   plg::AttnBwdArgs b{};
@@ -321,6 +322,13 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at:
               "attention backward workspaces too small");
   b.dq_acc = dq_acc.data_ptr<float>();
   b.delta = delta.data_ptr<float>();
+  b.trace = nullptr;
+  if (trace.has_value()) {
+    TORCH_CHECK(trace->is_cuda() && trace->scalar_type() == at::kLong && trace->is_contiguous() &&
+                    trace->numel() >= plg::kAttnTraceEvents * plg::kAttnTraceSteps,
+                "attention trace buffer: int64 cuda tensor of at least 12 x 256");
+    b.trace = reinterpret_cast<long long*>(trace->data_ptr<int64_t>());
+  }
   plg::attn_bwd(b, cur_stream());
 }
 
@@ -344,5 +352,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("multi_scale", &multi_scale);
   m.def("adamw_multi", &adamw_multi);
   m.def("attn_fwd", &attn_fwd);
-  m.def("attn_bwd", &attn_bwd);
+  m.def("attn_bwd", &attn_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"),
+        py::arg("lse"), py::arg("dout"), py::arg("dq"), py::arg("dk"), py::arg("dv"),
+        py::arg("dq_acc"), py::arg("delta"), py::arg("scale"), py::arg("causal"),
+        py::arg("window"), py::arg("status") = py::none(), py::arg("trace") = py::none());
 }

@@ -139,6 +139,20 @@ __device__ __forceinline__ bool elect_one_lane() {
   return (threadIdx.x & 31) == 0;
 }
 
+// elect.sync over the full warp: true on exactly one lane. A warp that runs its
+// MMA loop together (so descriptors and loop state stay warp-uniform) issues
+// each tcgen05 instruction from the elected lane only; callers elect once and
+// keep the result, since commits must come from the thread that issued.
+__device__ __forceinline__ bool elect_one_sync() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .b32 r;\n\t.reg .pred p;\n\t"
+      "elect.sync r|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // ----------------------------------------------------------------------------
 // mbarrier
 // ----------------------------------------------------------------------------
@@ -251,6 +265,32 @@ __device__ __forceinline__ void fmul2(float& d0, float& d1, float a0, float a1, 
       : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
 
+// 4-D tiled reduce-add (fp32) of a shared-memory box into global memory through
+// the tensor map, tracked by the issuing thread's bulk async-group. Coordinates
+// must be non-negative; out-of-range rows are clipped.
+__device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* map, const void* smem_src,
+                                                  int32_t x, int32_t y, int32_t z, int32_t w) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.tile.bulk_group"
+      " [%0, {%2, %3, %4, %5}], [%1];"
+      ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(smem_src)), "r"(x), "r"(y), "r"(z),
+        "r"(w)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// wait until at most N of this thread's bulk groups still read shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// wait until at most N of this thread's bulk groups are still in flight
+template <int N>
+__device__ __forceinline__ void bulk_wait_group() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // named barrier over a subset of warps (id 1..15; count = threads, multiple of 32)
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
@@ -279,6 +319,13 @@ __device__ __forceinline__ uint64_t make_smem_desc(uint32_t saddr, uint32_t lbo_
 }
 
 constexpr uint32_t kLayoutSW128 = 2;
+
+// Descriptor of the same layout starting `bytes` further on: the start address
+// field holds (address >> 4) in the low 14 bits and shared memory stays below
+// 256 KB, so the sum never carries out of the field.
+__device__ __forceinline__ uint64_t desc_advance(uint64_t d, uint32_t bytes) {
+  return d + (bytes >> 4);
+}
 
 // Instruction descriptor for kind::f16 with bf16 A/B and fp32 accumulation.
 //   [4,6) D format (1 = f32), [7,10) A format (1 = bf16), [10,13) B format (1 = bf16)

@@ -123,7 +123,10 @@ struct AttnBwdArgs {
   long long dq_row, dk_row, dv_row;
   float* dq_acc;                                 // fp32 workspace [B, S, Hq, d]
   float* delta;                                  // fp32 workspace, attn_bwd_stats_floats()
+  long long* trace;                              // optional [kAttnTraceEvents][kAttnTraceSteps]
+                                                 // SM clock stamps of CTA 0 (null: off)
 };
+constexpr int kAttnTraceEvents = 12, kAttnTraceSteps = 256;
 // floats the backward's stats workspace needs: [B * Hq][2][S rounded up to 64]
 inline long long attn_bwd_stats_floats(int B, int Hq, int S) {
   return static_cast<long long>(B) * Hq * 2 * ((S + 63) / 64 * 64);

@@ -51,7 +51,11 @@ def attn_fwd(q, k, v, *, causal=True, window=0, scale=None):
     return o, lse
 
 
-def attn_bwd(q, k, v, o, lse, do, *, causal=True, window=0, scale=None, dq=None, dk=None, dv=None):
+def attn_bwd(q, k, v, o, lse, do, *, causal=True, window=0, scale=None, dq=None, dk=None, dv=None,
+             trace=None):
+    """Backward of flash attention. ``trace`` (int64 [10, 256] on the device,
+    head_dim 128 only) receives SM-clock stamps of the first CTA's pipeline events
+    per step, for timeline analysis of the kernel."""
     B, S, Hq, d = q.shape
     scale = 1.0 / math.sqrt(d) if scale is None else scale
     dq = torch.empty_like(q, memory_format=torch.contiguous_format) if dq is None else dq
@@ -62,7 +66,7 @@ def attn_bwd(q, k, v, o, lse, do, *, causal=True, window=0, scale=None, dq=None,
     # [B * Hq][2][S rounded up to 64]: -lse*log2(e) and -scale*rowsum(dO*O)
     delta = torch.empty(B * Hq * 2 * ((S + 63) // 64 * 64), dtype=torch.float32, device=q.device)
     ext().attn_bwd(q, k, v, o, lse, do, dq, dk, dv, dq_acc, delta, float(scale), bool(causal),
-                   int(window or 0), status_word(q.device))
+                   int(window or 0), status_word(q.device), trace)
     return dq, dk, dv
 
 
