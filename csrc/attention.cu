@@ -1157,23 +1157,21 @@ __global__ void __launch_bounds__(kB3Threads, 1)
       for (int c = 0; c < kBQ3; c += 4) {
         const float4 nl = st4[c / 4];        // -lse * log2(e)
         const float4 nd = st4[16 + c / 4];   // -delta * scale
-        float p0, p1, p2, p3, t0, t1, t2, t3;
-        ffma2(p0, p1, __uint_as_float(sv[c]), __uint_as_float(sv[c + 1]), scale2, scale2, nl.x, nl.y);
-        ffma2(p2, p3, __uint_as_float(sv[c + 2]), __uint_as_float(sv[c + 3]), scale2, scale2, nl.z, nl.w);
-        p0 = fast_exp2(p0);
-        p1 = fast_exp2(p1);
-        p2 = fast_exp2(p2);
-        p3 = fast_exp2(p3);
+        // scalar FMAs: measured faster than the packed f32x2 forms in this loop
+        float p0 = fast_exp2(fmaf(__uint_as_float(sv[c]), scale2, nl.x));
+        float p1 = fast_exp2(fmaf(__uint_as_float(sv[c + 1]), scale2, nl.y));
+        float p2 = fast_exp2(fmaf(__uint_as_float(sv[c + 2]), scale2, nl.z));
+        float p3 = fast_exp2(fmaf(__uint_as_float(sv[c + 3]), scale2, nl.w));
         if (edge) {
           p0 = (c >= c_lo && c <= c_hi) ? p0 : 0.f;
           p1 = (c + 1 >= c_lo && c + 1 <= c_hi) ? p1 : 0.f;
           p2 = (c + 2 >= c_lo && c + 2 <= c_hi) ? p2 : 0.f;
           p3 = (c + 3 >= c_lo && c + 3 <= c_hi) ? p3 : 0.f;
         }
-        ffma2(t0, t1, __uint_as_float(dv[c]), __uint_as_float(dv[c + 1]), scale, scale, nd.x, nd.y);
-        ffma2(t2, t3, __uint_as_float(dv[c + 2]), __uint_as_float(dv[c + 3]), scale, scale, nd.z, nd.w);
-        fmul2(t0, t1, t0, t1, p0, p1);
-        fmul2(t2, t3, t2, t3, p2, p3);
+        const float t0 = fmaf(__uint_as_float(dv[c]), scale, nd.x) * p0;
+        const float t1 = fmaf(__uint_as_float(dv[c + 1]), scale, nd.y) * p1;
+        const float t2 = fmaf(__uint_as_float(dv[c + 2]), scale, nd.z) * p2;
+        const float t3 = fmaf(__uint_as_float(dv[c + 3]), scale, nd.w) * p3;
         pk[c / 2] = pack_bf16x2(p0, p1);
         pk[c / 2 + 1] = pack_bf16x2(p2, p3);
         dk[c / 2] = pack_bf16x2(t0, t1);

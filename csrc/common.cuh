@@ -189,20 +189,34 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that lets the hardware suspend the thread until the phase completes
+// or `ns` nanoseconds pass, so a waiting warp stops competing for issue slots
+// with the warps doing the work.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase with the given parity to complete. Returns false if the
-// deadline passed or another role of the CTA raised `abort_flag`.
+// deadline passed or another role of the CTA raised `abort_flag`. Each sleep
+// lasts at most 1 ms, which bounds how late an abort is noticed.
+constexpr uint32_t kWaitSuspendNs = 1000000;
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   volatile int* abort_flag,
                                                   uint64_t deadline_ns = kWaitDeadlineNs) {
   if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = globaltimer_ns();
-  uint32_t spins = 0;
+  const uint64_t t0 = globaltimer_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 63u) == 0) {
-      if (abort_flag != nullptr && *abort_flag) return false;
-      if (globaltimer_ns() - t0 > deadline_ns) return false;
-    }
+    if (mbar_try_wait_suspend(bar, parity, kWaitSuspendNs)) return true;
+    if (abort_flag != nullptr && *abort_flag) return false;
+    if (globaltimer_ns() - t0 > deadline_ns) return false;
   }
 }
 
