@@ -1245,11 +1245,14 @@ __global__ void __launch_bounds__(kB3Threads, 1)
 
 // Backward pre-pass for the head_dim-128 kernel: per (b, h) row of the stats
 // workspace [B*Hq][2][S64], -lse*log2(e) and -scale * rowsum(dO * O); queries
-// beyond S get -inf and 0.
+// beyond S get -inf and 0. Also zeroes the fp32 dQ workspace row of each (b, s, h).
+// One warp per (b, s, h), 4 channels (8 bytes) per lane.
 __global__ void attn_bwd_stats_kernel(const __nv_bfloat16* __restrict__ o, long long o_row,
                                       const __nv_bfloat16* __restrict__ dout, long long do_row,
                                       const float* __restrict__ lse, float* __restrict__ stats,
-                                      int B, int S, int S64, int H, int D, float scale) {
+                                      float* __restrict__ dq_acc, int B, int S, int S64, int H,
+                                      float scale) {
+  constexpr int D = 128;
   const long long wid = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const long long total = static_cast<long long>(B) * S64 * H;
@@ -1266,18 +1269,34 @@ __global__ void attn_bwd_stats_kernel(const __nv_bfloat16* __restrict__ o, long 
     return;
   }
   const long long tok = static_cast<long long>(bb) * S + s;
-  const __nv_bfloat16* orow = o + tok * o_row + h * D;
-  const __nv_bfloat16* drow = dout + tok * do_row + h * D;
-  float acc = 0.f;
-  for (int c = lane * 2; c < D; c += 64) {
-    const float2 x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(orow + c));
-    const float2 y = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(drow + c));
-    acc += x.x * y.x + x.y * y.y;
-  }
+  const uint2 ov = *reinterpret_cast<const uint2*>(o + tok * o_row + h * D + lane * 4);
+  const uint2 dv = *reinterpret_cast<const uint2*>(dout + tok * do_row + h * D + lane * 4);
+  const float2 o0 = unpack_bf16x2(ov.x), o1 = unpack_bf16x2(ov.y);
+  const float2 d0 = unpack_bf16x2(dv.x), d1 = unpack_bf16x2(dv.y);
+  float acc = o0.x * d0.x + o0.y * d0.y + o1.x * d1.x + o1.y * d1.y;
   acc = warp_sum(acc);
+  reinterpret_cast<float4*>(dq_acc + (tok * H + h) * D)[lane] = make_float4(0.f, 0.f, 0.f, 0.f);
   if (lane == 0) {
     row[s] = -lse[(static_cast<long long>(bb) * H + h) * S + s] * kLog2e;
     row[S64 + s] = -acc * scale;
+  }
+}
+
+// dQ workspace (fp32 [B*S, H*D]) -> bf16 rows with stride dq_row; 8 values per access
+__global__ void attn_dq_cast8_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dq,
+                                     long long dq_row, long long tokens, int HD) {
+  const int c8 = HD / 8;
+  for (long long t = blockIdx.x; t < tokens; t += gridDim.x) {
+    const float4* src = reinterpret_cast<const float4*>(acc + t * HD);
+    for (int c = threadIdx.x; c < c8; c += blockDim.x) {
+      const float4 x = src[2 * c], y = src[2 * c + 1];
+      uint4 v;
+      v.x = pack_bf16x2(x.x, x.y);
+      v.y = pack_bf16x2(x.z, x.w);
+      v.z = pack_bf16x2(y.x, y.y);
+      v.w = pack_bf16x2(y.z, y.w);
+      *reinterpret_cast<uint4*>(dq + t * dq_row + c * 8) = v;
+    }
   }
 }
 
@@ -1405,22 +1424,23 @@ static void bwd3_launch(const AttnBwdArgs& g, cudaStream_t st) {
                              std::to_string(kB3RegsLaunch));
   const int S64 = (a.S + kBQ3 - 1) / kBQ3 * kBQ3;
   const long long srows = static_cast<long long>(a.B) * S64 * a.Hq;
+  if ((a.o_row % 8) || (g.do_row % 8) || (g.dq_row % 8) ||
+      (reinterpret_cast<uintptr_t>(a.o) & 15) || (reinterpret_cast<uintptr_t>(g.dout) & 15) ||
+      (reinterpret_cast<uintptr_t>(g.dq) & 15))
+    throw std::invalid_argument("attention backward: o, dout and dq rows must be 16-byte aligned");
   attn_bwd_stats_kernel<<<(srows * 32 + 255) / 256, 256, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(a.o), a.o_row,
-      reinterpret_cast<const __nv_bfloat16*>(g.dout), g.do_row, a.lse, g.delta, a.B, a.S, S64,
-      a.Hq, C::D, a.scale);
+      reinterpret_cast<const __nv_bfloat16*>(g.dout), g.do_row, a.lse, g.delta, g.dq_acc, a.B, a.S,
+      S64, a.Hq, a.scale);
   PLG_CUDA_CHECK(cudaGetLastError());
-  const long long rows = static_cast<long long>(a.B) * a.S * a.Hq;
-  PLG_CUDA_CHECK(cudaMemsetAsync(g.dq_acc, 0, sizeof(float) * rows * C::D, st));
   const long long ctas = static_cast<long long>((a.S + BKV - 1) / BKV) * a.Hk * a.B;
   if (ctas > 0x7fffffffLL) throw std::invalid_argument("attention: problem too large for one launch");
   attn_bwd3_kernel<<<static_cast<unsigned>(ctas), kB3Threads, C::kSmem, st>>>(tq, tk, tv, td, tdq, g);
   PLG_CUDA_CHECK(cudaGetLastError());
-  const long long nel = rows * C::D;
-  long long blocks = (nel + 255) / 256;
-  if (blocks > 148 * 32) blocks = 148 * 32;
-  attn_dq_cast_kernel<<<blocks, 256, 0, st>>>(g.dq_acc, reinterpret_cast<__nv_bfloat16*>(g.dq),
-                                              g.dq_row, a.B, a.S, a.Hq, C::D);
+  const long long tokens = static_cast<long long>(a.B) * a.S;
+  const long long cblocks = tokens < 148 * 16 ? tokens : 148 * 16;
+  attn_dq_cast8_kernel<<<static_cast<unsigned>(cblocks), 256, 0, st>>>(
+      g.dq_acc, reinterpret_cast<__nv_bfloat16*>(g.dq), g.dq_row, tokens, a.Hq * C::D);
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -112,8 +112,15 @@ plg::QkRopeArgs qk_args(const at::Tensor& qkv, at::Tensor& q, at::Tensor& k, at:
                         const c10::optional<at::Tensor>& wq, const c10::optional<at::Tensor>& wk,
                         const at::Tensor& inv_freq, const c10::optional<at::Tensor>& positions,
                         int64_t S, int64_t Hq, int64_t Hk, int64_t d, int64_t rot_dim, double eps,
-                        int64_t k_offset) {
+                        int64_t k_offset, const c10::optional<at::Tensor>& rope_table) {
   plg::QkRopeArgs a{};
+  a.rope_table = nullptr;
+  if (rope_table.has_value()) {
+    TORCH_CHECK(is_f32(*rope_table) && rope_table->is_contiguous() && rope_table->is_cuda() &&
+                    rope_table->numel() >= S * rot_dim,
+                "qk_norm_rope: rope_table must be fp32 [S, 2, rot_dim/2] on the device");
+    a.rope_table = rope_table->data_ptr<float>();
+  }
   a.qkv = qkv.data_ptr();
   a.ld_qkv = qkv.stride(0);
   a.q = q.data_ptr();
@@ -140,11 +147,12 @@ void qk_norm_rope_fwd(const at::Tensor& qkv, at::Tensor& q, at::Tensor& k, at::T
                       const c10::optional<at::Tensor>& wq, const c10::optional<at::Tensor>& wk,
                       const at::Tensor& inv_freq, const c10::optional<at::Tensor>& positions,
                       int64_t S, int64_t Hq, int64_t Hk, int64_t d, int64_t rot_dim, double eps,
-                      int64_t k_offset) {
+                      int64_t k_offset, const c10::optional<at::Tensor>& rope_table) {
   check_cuda(qkv, "qkv");
   TORCH_CHECK(is_bf16(qkv) && qkv.dim() == 2 && qkv.stride(1) == 1, "qkv must be bf16 [T, W]");
   const c10::cuda::CUDAGuard guard(qkv.device());
-  auto a = qk_args(qkv, q, k, rstd, wq, wk, inv_freq, positions, S, Hq, Hk, d, rot_dim, eps, k_offset);
+  auto a = qk_args(qkv, q, k, rstd, wq, wk, inv_freq, positions, S, Hq, Hk, d, rot_dim, eps, k_offset,
+                   rope_table);
   plg::qk_norm_rope_fwd(a, cur_stream());
 }
 
@@ -154,12 +162,13 @@ void qk_norm_rope_bwd(const at::Tensor& qkv, at::Tensor& rstd, const c10::option
                       int64_t d, int64_t rot_dim, double eps, int64_t k_offset,
                       const at::Tensor& dq, const at::Tensor& dk, at::Tensor& dqkv,
                       const c10::optional<at::Tensor>& dwq_partial,
-                      const c10::optional<at::Tensor>& dwk_partial, int64_t blocks) {
+                      const c10::optional<at::Tensor>& dwk_partial, int64_t blocks,
+                      const c10::optional<at::Tensor>& rope_table) {
   check_cuda(qkv, "qkv");
   const c10::cuda::CUDAGuard guard(qkv.device());
   at::Tensor q_dummy = dq, k_dummy = dk;
   auto a = qk_args(qkv, q_dummy, k_dummy, rstd, wq, wk, inv_freq, positions, S, Hq, Hk, d, rot_dim,
-                   eps, k_offset);
+                   eps, k_offset, rope_table);
   plg::qk_norm_rope_bwd(a, dq.data_ptr(), dk.data_ptr(), dqkv.data_ptr(), dqkv.stride(0),
                         dwq_partial.has_value() ? dwq_partial->data_ptr<float>() : nullptr,
                         dwk_partial.has_value() ? dwk_partial->data_ptr<float>() : nullptr,
@@ -332,7 +341,17 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at:
   plg::attn_bwd(b, cur_stream());
 }
 
+void colsum(const at::Tensor& part, at::Tensor& out) {
+  check_cuda(part, "part");
+  TORCH_CHECK(is_f32(part) && part.dim() == 2 && part.is_contiguous(), "colsum: fp32 [R, D] input");
+  TORCH_CHECK(is_f32(out) && out.is_contiguous() && out.numel() == part.size(1), "colsum: out [D]");
+  const c10::cuda::CUDAGuard guard(part.device());
+  plg::colsum(part.data_ptr<float>(), static_cast<int>(part.size(0)), static_cast<int>(part.size(1)),
+              out.data_ptr<float>(), cur_stream());
+}
+
 }  // namespace
+
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "pluggy_b200 sm_100a kernels";
@@ -344,6 +363,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("glu_fwd", &glu_fwd);
   m.def("glu_bwd", &glu_bwd);
   m.def("cast_f32_bf16", &cast_f32_bf16);
+  m.def("colsum", &colsum);
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd", &embedding_bwd);
   m.def("softcap", &softcap);

@@ -10,6 +10,8 @@
 // vector loads where alignment allows, fp32 accumulation, bf16/fp32 stores.
 #include <stdexcept>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "ops.h"
 
@@ -104,7 +106,9 @@ void rmsnorm_fwd_t(const void* x, const float* w, void* y, float* rstd, long lon
 // dx = rstd * (w*dy - xh * mean(w*dy*xh)) (+ dres),  xh = x * rstd
 // dw_partial[block, :] = sum over the block's rows of dy * xh
 template <typename TDY, typename TX, int NV>
-__global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
+// 128 threads and at most 128 registers: the caller's DW_BLOCKS (4 per SM) must all
+// be resident at once, or the grid-strided rows run in several waves
+__global__ void __launch_bounds__(128, 4) rmsnorm_bwd_kernel(
     const TDY* __restrict__ dy, const TX* __restrict__ x, const float* __restrict__ w,
     const float* __restrict__ rstd, const float* __restrict__ dres, float* __restrict__ dx_f32,
     __nv_bfloat16* __restrict__ dx_bf16, float* __restrict__ dw_partial, long long rows, int D) {
@@ -115,34 +119,62 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
   if (dw_partial)
     for (int i = threadIdx.x; i < D; i += blockDim.x) s_dw[i] = 0.f;
   __syncthreads();
+  // small D: dw accumulates in registers (lane-owned channels) and is reduced
+  // across warps once; large D: straight into shared memory
+  constexpr bool kRegDw = NV <= 8;
+  float dw_acc[kRegDw ? NV : 1][4];
+#pragma unroll
+  for (int j = 0; j < (kRegDw ? NV : 1); ++j)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dw_acc[j][i] = 0.f;
   for (long long row = (long long)blockIdx.x * nwarps + warp; row < rows;
        row += (long long)gridDim.x * nwarps) {
     const float r = rstd[row];
-    float g[NV][4], xh[NV][4];
+    // the raw row stays in registers between the two passes (bf16 dy packed, w
+    // re-read from L1)
+    constexpr bool kDyBf16 = std::is_same_v<TDY, __nv_bfloat16>;
+    uint2 dpk[kDyBf16 ? NV : 1];
+    float dvf[kDyBf16 ? 1 : NV][4];
+    auto dy_at = [&](int j, float (&v)[4]) {
+      if constexpr (kDyBf16) {
+        const float2 a = unpack_bf16x2(dpk[j].x), b = unpack_bf16x2(dpk[j].y);
+        v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = dvf[j][i];
+      }
+    };
+    float xvs[NV][4];
     float dot = 0.f;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       const int c = j * 128 + lane * 4;
-      float dv[4], xv[4];
-      ld4(dy + row * D + c, dv);
-      ld4(x + row * D + c, xv);
+      if constexpr (kDyBf16) dpk[j] = *reinterpret_cast<const uint2*>(dy + row * D + c);
+      else ld4(dy + row * D + c, dvf[j]);
+      float dvs_j[4];
+      dy_at(j, dvs_j);
+      ld4(x + row * D + c, xvs[j]);
       float wv[4] = {1.f, 1.f, 1.f, 1.f};
       if (w) ld4(w + c, wv);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        xh[j][i] = xv[i] * r;
-        g[j][i] = dv[i] * wv[i];
-        dot += g[j][i] * xh[j][i];
-        if (dw_partial) atomicAdd(&s_dw[c + i], dv[i] * xh[j][i]);
+        const float xh = xvs[j][i] * r;
+        dot += dvs_j[i] * wv[i] * xh;
+        if constexpr (kRegDw) dw_acc[j][i] += dvs_j[i] * xh;
+        else if (dw_partial) atomicAdd(&s_dw[c + i], dvs_j[i] * xh);
       }
     }
     dot = warp_sum(dot) / D;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       const int c = j * 128 + lane * 4;
+      float wv[4] = {1.f, 1.f, 1.f, 1.f};
+      if (w) ld4(w + c, wv);
+      float dvs_j[4];
+      dy_at(j, dvs_j);
       float o[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) o[i] = r * (g[j][i] - xh[j][i] * dot);
+      for (int i = 0; i < 4; ++i) o[i] = r * (dvs_j[i] * wv[i] - xvs[j][i] * r * dot);
       if (dres) {
         float rv[4];
         ld4(dres + row * D + c, rv);
@@ -154,6 +186,12 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
     }
   }
   if (dw_partial) {
+    if constexpr (kRegDw) {
+#pragma unroll
+      for (int j = 0; j < NV; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) atomicAdd(&s_dw[j * 128 + lane * 4 + i], dw_acc[j][i]);
+    }
     __syncthreads();
     for (int i = threadIdx.x; i < D; i += blockDim.x)
       dw_partial[(long long)blockIdx.x * D + i] = s_dw[i];
@@ -164,7 +202,7 @@ template <typename TDY, typename TX>
 void rmsnorm_bwd_t(const void* dy, const void* x, const float* w, const float* rstd,
                    const float* dres, float* dx_f32, void* dx_bf16, float* dw_partial,
                    int dw_blocks, long long rows, int D, cudaStream_t st) {
-  const int threads = 256;
+  const int threads = 128;
   const int nv = D / 128;
   const size_t sm = dw_partial ? D * sizeof(float) : 0;
 #define PLG_RMSB_CASE(NV)                                                                      \
@@ -185,145 +223,235 @@ void rmsnorm_bwd_t(const void* dy, const void* x, const float* w, const float* r
 }
 
 // ------------------------------------------------------------ QK-norm + RoPE
-// One warp per (token, head). Lane l owns first-half channels i = l + 32*j
-// (j < d/64) and their RoPE partners i + d/2.
-template <int NJ>
-__global__ void __launch_bounds__(256) qk_rope_fwd_kernel(QkRopeArgs a) {
-  const int lane = threadIdx.x & 31;
-  const long long gw = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int H = a.Hq + a.Hk;
-  if (gw >= a.T * H) return;
-  const long long t = gw / H;
-  const int h = static_cast<int>(gw - t * H);
-  const bool is_q = h < a.Hq;
-  const int d = a.d, half = d / 2;
-  const int col = is_q ? h * d : a.k_offset * d + (h - a.Hq) * d;
-  const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.qkv) + t * a.ld_qkv + col;
-  float lo[NJ], hi[NJ];
-  float ss = 0.f;
+// One warp per token, looping over all its q and k heads. Lane l owns the NV =
+// d/32 consecutive channels [l*NV, l*NV + NV) (one vector load per head row).
+// RoPE is rotate-half over the first rot_dim channels: channel i < rot_dim/2 pairs
+// with i + rot_dim/2 (a lane shuffle away). The token's cos/sin values are
+// computed once per lane and reused by every head.
+template <int NV>
+struct BfVec;
+template <>
+struct BfVec<2> { using T = uint32_t; };
+template <>
+struct BfVec<4> { using T = uint2; };
+template <>
+struct BfVec<8> { using T = uint4; };
+
+template <int NV>
+__device__ __forceinline__ void load_bf(const __nv_bfloat16* p, float (&v)[NV]) {
+  if constexpr (NV == 16) {
+    load_bf<8>(p, *reinterpret_cast<float(*)[8]>(v));
+    load_bf<8>(p + 8, *reinterpret_cast<float(*)[8]>(v + 8));
+  } else {
+    const typename BfVec<NV>::T raw = *reinterpret_cast<const typename BfVec<NV>::T*>(p);
+    const uint32_t* u = reinterpret_cast<const uint32_t*>(&raw);
 #pragma unroll
-  for (int j = 0; j < NJ; ++j) {
-    lo[j] = __bfloat162float(src[lane + 32 * j]);
-    hi[j] = __bfloat162float(src[lane + 32 * j + half]);
-    ss += lo[j] * lo[j] + hi[j] * hi[j];
-  }
-  const bool do_norm = is_q ? a.norm_q : a.norm_k;
-  float r = 1.f;
-  if (do_norm) {
-    ss = warp_sum(ss);
-    r = rsqrtf(ss / d + a.eps);
-    const float* w = is_q ? a.wq : a.wk;
-#pragma unroll
-    for (int j = 0; j < NJ; ++j) {
-      lo[j] *= r * w[lane + 32 * j];
-      hi[j] *= r * w[lane + 32 * j + half];
+    for (int k = 0; k < NV / 2; ++k) {
+      const float2 f = unpack_bf16x2(u[k]);
+      v[2 * k] = f.x;
+      v[2 * k + 1] = f.y;
     }
-  }
-  if (lane == 0 && a.rstd) a.rstd[t * H + h] = r;
-  const int pos = a.positions ? a.positions[t] : static_cast<int>(t % a.S);
-  const int rhalf = a.rot_dim / 2;
-  __nv_bfloat16* dst = is_q ? reinterpret_cast<__nv_bfloat16*>(a.q) + (t * a.Hq + h) * d
-                            : reinterpret_cast<__nv_bfloat16*>(a.k) + (t * a.Hk + (h - a.Hq)) * d;
-#pragma unroll
-  for (int j = 0; j < NJ; ++j) {
-    const int i = lane + 32 * j;
-    float o_lo = lo[j], o_hi = hi[j];
-    if (i < rhalf) {
-      // rotate-half pairs (i, i + rot_dim/2) inside the rotated prefix; for
-      // full rotation rot_dim == d and the partner is i + d/2.
-      float s, c;
-      sincosf(static_cast<float>(pos) * a.inv_freq[i], &s, &c);
-      if (rhalf == half) {
-        o_lo = lo[j] * c - hi[j] * s;
-        o_hi = hi[j] * c + lo[j] * s;
-      }
-    }
-    dst[i] = __float2bfloat16(o_lo);
-    dst[i + half] = __float2bfloat16(o_hi);
   }
 }
 
-template <int NJ>
-__global__ void __launch_bounds__(256) qk_rope_bwd_kernel(QkRopeArgs a, const __nv_bfloat16* dq,
+template <int NV>
+__device__ __forceinline__ void store_bf(__nv_bfloat16* p, const float (&v)[NV]) {
+  if constexpr (NV == 16) {
+    store_bf<8>(p, *reinterpret_cast<const float(*)[8]>(v));
+    store_bf<8>(p + 8, *reinterpret_cast<const float(*)[8]>(v + 8));
+  } else {
+    typename BfVec<NV>::T raw;
+    uint32_t* u = reinterpret_cast<uint32_t*>(&raw);
+#pragma unroll
+    for (int k = 0; k < NV / 2; ++k) u[k] = pack_bf16x2(v[2 * k], v[2 * k + 1]);
+    *reinterpret_cast<typename BfVec<NV>::T*>(p) = raw;
+  }
+}
+
+// cos/sin of this lane's channels for position pos (c0 = first channel of the lane)
+template <int NV>
+__device__ __forceinline__ void rope_angles(const QkRopeArgs& a, int pos, int c0, float (&cs)[NV],
+                                            float (&sn)[NV]) {
+  const int rh = a.rot_dim / 2;
+  if (a.rope_table != nullptr) {
+    // a lane's NV channels lie in one half of the rotated prefix (rh % NV == 0)
+    const float* row = a.rope_table + static_cast<long long>(pos) * a.rot_dim;
+    const int f0 = c0 < rh ? c0 : c0 - rh;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const bool rot = c0 + k < a.rot_dim;
+      cs[k] = rot ? row[f0 + k] : 1.f;
+      sn[k] = rot ? row[rh + f0 + k] : 0.f;
+    }
+    return;
+  }
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int c = c0 + k;
+    if (c < a.rot_dim) {
+      sincosf(static_cast<float>(pos) * a.inv_freq[c < rh ? c : c - rh], &sn[k], &cs[k]);
+    } else {
+      cs[k] = 1.f;
+      sn[k] = 0.f;
+    }
+  }
+}
+
+// heads per work item: each warp loads the rows of hc_for(NV) heads of one token
+// up front (memory-level parallelism), then normalises and rotates them
+constexpr int hc_for(int nv) { return nv >= 16 ? 1 : (nv >= 8 ? 2 : 4); }
+
+template <int NV>
+__global__ void __launch_bounds__(256, 2) qk_rope_fwd_kernel(QkRopeArgs a) {
+  constexpr int kHC = hc_for(NV);
+  const int lane = threadIdx.x & 31;
+  const int d = NV * 32, c0 = lane * NV;
+  const int H = a.Hq + a.Hk;
+  const int nch = (H + kHC - 1) / kHC;
+  const int rh = a.rot_dim / 2;
+  // partner lane of the rotate-half pair (lanes beyond rot_dim keep their own values)
+  const int off = rh / NV;
+  const int partner = c0 < rh ? lane + off : (c0 < a.rot_dim ? lane - off : lane);
+  const float sgn = c0 < rh ? -1.f : 1.f;
+  float wq[NV], wk[NV];
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    wq[k] = a.norm_q ? a.wq[c0 + k] : 1.f;
+    wk[k] = a.norm_k ? a.wk[c0 + k] : 1.f;
+  }
+  const long long items = a.T * nch;
+  for (long long it = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items;
+       it += (long long)gridDim.x * (blockDim.x >> 5)) {
+    const long long t = it / nch;
+    const int h0 = static_cast<int>(it - t * nch) * kHC;
+    const int pos = a.positions ? a.positions[t] : static_cast<int>(t % a.S);
+    const __nv_bfloat16* row = reinterpret_cast<const __nv_bfloat16*>(a.qkv) + t * a.ld_qkv;
+    float v[kHC][NV];
+#pragma unroll
+    for (int hh = 0; hh < kHC; ++hh) {
+      const int h = h0 + hh;
+      if (h < H) {
+        const int col = h < a.Hq ? h * d : a.k_offset * d + (h - a.Hq) * d;
+        load_bf<NV>(row + col + c0, v[hh]);
+      }
+    }
+    float cs[NV], sn[NV];
+    rope_angles<NV>(a, pos, c0, cs, sn);
+#pragma unroll
+    for (int hh = 0; hh < kHC; ++hh) {
+      const int h = h0 + hh;
+      if (h >= H) break;
+      const bool is_q = h < a.Hq;
+      float r = 1.f;
+      if (is_q ? a.norm_q : a.norm_k) {
+        float ss = 0.f;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) ss += v[hh][k] * v[hh][k];
+        ss = warp_sum(ss);
+        r = rsqrtf(ss / d + a.eps);
+#pragma unroll
+        for (int k = 0; k < NV; ++k) v[hh][k] *= r * (is_q ? wq[k] : wk[k]);
+      }
+      if (lane == 0 && a.rstd) a.rstd[t * H + h] = r;
+      float o[NV];
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        const float p = __shfl_sync(0xffffffffu, v[hh][k], partner);
+        o[k] = v[hh][k] * cs[k] + sgn * p * sn[k];
+      }
+      __nv_bfloat16* dst = is_q ? reinterpret_cast<__nv_bfloat16*>(a.q) + (t * a.Hq + h) * d
+                                : reinterpret_cast<__nv_bfloat16*>(a.k) + (t * a.Hk + (h - a.Hq)) * d;
+      store_bf<NV>(dst + c0, o);
+    }
+  }
+}
+
+// 128 threads, at most 128 registers: all DW_BLOCKS (4 per SM) resident at once
+template <int NV>
+__global__ void __launch_bounds__(128, 4) qk_rope_bwd_kernel(QkRopeArgs a, const __nv_bfloat16* dq,
                                                           const __nv_bfloat16* dk,
                                                           __nv_bfloat16* dqkv, long long ld_dqkv,
                                                           float* dwq_part, float* dwk_part) {
+  constexpr int kHC = hc_for(NV);
   extern __shared__ float s_dw[];  // [2 * d]: q weights then k weights
   const int lane = threadIdx.x & 31;
-  const int nwarps = blockDim.x >> 5;
-  const int d = a.d, half = d / 2;
+  const int d = NV * 32, c0 = lane * NV;
   for (int i = threadIdx.x; i < 2 * d; i += blockDim.x) s_dw[i] = 0.f;
   __syncthreads();
   const int H = a.Hq + a.Hk;
-  const int rhalf = a.rot_dim / 2;
-  float accq_lo[NJ], accq_hi[NJ], acck_lo[NJ], acck_hi[NJ];
+  const int nch = (H + kHC - 1) / kHC;
+  const int rh = a.rot_dim / 2;
+  const int off = rh / NV;
+  const int partner = c0 < rh ? lane + off : (c0 < a.rot_dim ? lane - off : lane);
+  // transpose of the rotation: d_lo = g_lo c + g_hi s, d_hi = g_hi c - g_lo s
+  const float sgn = c0 < rh ? 1.f : -1.f;
+  float wq[NV], wk[NV], accq[NV], acck[NV];
 #pragma unroll
-  for (int j = 0; j < NJ; ++j) accq_lo[j] = accq_hi[j] = acck_lo[j] = acck_hi[j] = 0.f;
-  for (long long gw = (long long)blockIdx.x * nwarps + (threadIdx.x >> 5); gw < a.T * H;
-       gw += (long long)gridDim.x * nwarps) {
-    const long long t = gw / H;
-    const int h = static_cast<int>(gw - t * H);
-    const bool is_q = h < a.Hq;
-    const int col = is_q ? h * d : a.k_offset * d + (h - a.Hq) * d;
-    const __nv_bfloat16* g = is_q ? dq + (t * a.Hq + h) * d : dk + (t * a.Hk + (h - a.Hq)) * d;
-    const __nv_bfloat16* xs = reinterpret_cast<const __nv_bfloat16*>(a.qkv) + t * a.ld_qkv + col;
+  for (int k = 0; k < NV; ++k) {
+    wq[k] = a.norm_q ? a.wq[c0 + k] : 1.f;
+    wk[k] = a.norm_k ? a.wk[c0 + k] : 1.f;
+    accq[k] = acck[k] = 0.f;
+  }
+  const long long items = a.T * nch;
+  for (long long it = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items;
+       it += (long long)gridDim.x * (blockDim.x >> 5)) {
+    const long long t = it / nch;
+    const int h0 = static_cast<int>(it - t * nch) * kHC;
     const int pos = a.positions ? a.positions[t] : static_cast<int>(t % a.S);
-    float glo[NJ], ghi[NJ], xlo[NJ], xhi[NJ];
+    const __nv_bfloat16* xrow = reinterpret_cast<const __nv_bfloat16*>(a.qkv) + t * a.ld_qkv;
+    __nv_bfloat16* orow = dqkv + t * ld_dqkv;
+    float g[kHC][NV], x[kHC][NV], rs[kHC];
 #pragma unroll
-    for (int j = 0; j < NJ; ++j) {
-      const int i = lane + 32 * j;
-      float gl = __bfloat162float(g[i]), gh = __bfloat162float(g[i + half]);
-      if (i < rhalf && rhalf == half) {
-        float s, c;
-        sincosf(static_cast<float>(pos) * a.inv_freq[i], &s, &c);
-        // transpose of the rotation
-        glo[j] = gl * c + gh * s;
-        ghi[j] = gh * c - gl * s;
-      } else {
-        glo[j] = gl;
-        ghi[j] = gh;
+    for (int hh = 0; hh < kHC; ++hh) {
+      const int h = h0 + hh;
+      if (h < H) {
+        const bool is_q = h < a.Hq;
+        const int col = is_q ? h * d : a.k_offset * d + (h - a.Hq) * d;
+        load_bf<NV>((is_q ? dq + (t * a.Hq + h) * d : dk + (t * a.Hk + (h - a.Hq)) * d) + c0, g[hh]);
+        load_bf<NV>(xrow + col + c0, x[hh]);
+        rs[hh] = (is_q ? a.norm_q : a.norm_k) ? a.rstd[t * H + h] : 1.f;
       }
-      xlo[j] = __bfloat162float(xs[i]);
-      xhi[j] = __bfloat162float(xs[i + half]);
     }
-    const bool do_norm = is_q ? a.norm_q : a.norm_k;
-    __nv_bfloat16* out = dqkv + t * ld_dqkv + col;
-    if (do_norm) {
-      const float r = a.rstd[t * H + h];
-      const float* w = is_q ? a.wq : a.wk;
-      float dot = 0.f;
+    float cs[NV], sn[NV];
+    rope_angles<NV>(a, pos, c0, cs, sn);
 #pragma unroll
-      for (int j = 0; j < NJ; ++j) {
-        const int i = lane + 32 * j;
-        const float xl = xlo[j] * r, xh = xhi[j] * r;
-        const float wl = w[i], wh = w[i + half];
-        dot += glo[j] * wl * xl + ghi[j] * wh * xh;
-        if (is_q) { accq_lo[j] += glo[j] * xl; accq_hi[j] += ghi[j] * xh; }
-        else { acck_lo[j] += glo[j] * xl; acck_hi[j] += ghi[j] * xh; }
-      }
-      dot = warp_sum(dot) / d;
+    for (int hh = 0; hh < kHC; ++hh) {
+      const int h = h0 + hh;
+      if (h >= H) break;
+      const bool is_q = h < a.Hq;
+      const int col = is_q ? h * d : a.k_offset * d + (h - a.Hq) * d;
+      float gr[NV];
 #pragma unroll
-      for (int j = 0; j < NJ; ++j) {
-        const int i = lane + 32 * j;
-        out[i] = __float2bfloat16(r * (glo[j] * w[i] - xlo[j] * r * dot));
-        out[i + half] = __float2bfloat16(r * (ghi[j] * w[i + half] - xhi[j] * r * dot));
+      for (int k = 0; k < NV; ++k) {
+        const float p = __shfl_sync(0xffffffffu, g[hh][k], partner);
+        gr[k] = g[hh][k] * cs[k] + sgn * p * sn[k];
       }
-    } else {
+      float o[NV];
+      if (is_q ? a.norm_q : a.norm_k) {
+        const float r = rs[hh];
+        float dot = 0.f;
 #pragma unroll
-      for (int j = 0; j < NJ; ++j) {
-        const int i = lane + 32 * j;
-        out[i] = __float2bfloat16(glo[j]);
-        out[i + half] = __float2bfloat16(ghi[j]);
+        for (int k = 0; k < NV; ++k) {
+          const float xh = x[hh][k] * r, w = is_q ? wq[k] : wk[k];
+          dot += gr[k] * w * xh;
+          if (is_q) accq[k] += gr[k] * xh;
+          else acck[k] += gr[k] * xh;
+        }
+        dot = warp_sum(dot) / d;
+#pragma unroll
+        for (int k = 0; k < NV; ++k)
+          o[k] = r * (gr[k] * (is_q ? wq[k] : wk[k]) - x[hh][k] * r * dot);
+      } else {
+#pragma unroll
+        for (int k = 0; k < NV; ++k) o[k] = gr[k];
       }
+      store_bf<NV>(orow + col + c0, o);
     }
   }
 #pragma unroll
-  for (int j = 0; j < NJ; ++j) {
-    const int i = lane + 32 * j;
-    atomicAdd(&s_dw[i], accq_lo[j]);
-    atomicAdd(&s_dw[i + half], accq_hi[j]);
-    atomicAdd(&s_dw[d + i], acck_lo[j]);
-    atomicAdd(&s_dw[d + i + half], acck_hi[j]);
+  for (int k = 0; k < NV; ++k) {
+    atomicAdd(&s_dw[c0 + k], accq[k]);
+    atomicAdd(&s_dw[d + c0 + k], acck[k]);
   }
   __syncthreads();
   for (int i = threadIdx.x; i < d; i += blockDim.x) {
@@ -359,15 +487,26 @@ void rmsnorm_bwd(const void* dy, bool dy_fp32, const void* x, bool x_fp32, const
     rmsnorm_bwd_t<__nv_bfloat16, __nv_bfloat16>(dy, x, w, rstd, dres, dx_f32, dx_bf16, dw_partial, dw_blocks, rows, D, st);
 }
 
+static void check_rope_args(const QkRopeArgs& a) {
+  const int nv = a.d / 32;
+  if (a.rot_dim < 0 || a.rot_dim > a.d || (a.rot_dim % (2 * nv)) != 0)
+    throw std::invalid_argument("qk_norm_rope: rot_dim must be a multiple of 2*d/32 and <= d");
+  if ((a.ld_qkv % 8) != 0 || (reinterpret_cast<uintptr_t>(a.qkv) & 15))
+    throw std::invalid_argument("qk_norm_rope: qkv rows must be 16-byte aligned");
+}
+
 void qk_norm_rope_fwd(const QkRopeArgs& a, cudaStream_t st) {
   if (a.T <= 0) return;
-  const long long warps = a.T * (a.Hq + a.Hk);
-  dim3 grid((warps + 7) / 8);
+  check_rope_args(a);
+  const int hc = hc_for(a.d / 32);
+  const long long items = a.T * ((a.Hq + a.Hk + hc - 1) / hc);
+  long long blocks = (items + 7) / 8;
+  if (blocks > 148 * 16) blocks = 148 * 16;
   switch (a.d) {
-    case 64: qk_rope_fwd_kernel<1><<<grid, 256, 0, st>>>(a); break;
-    case 128: qk_rope_fwd_kernel<2><<<grid, 256, 0, st>>>(a); break;
-    case 256: qk_rope_fwd_kernel<4><<<grid, 256, 0, st>>>(a); break;
-    case 512: qk_rope_fwd_kernel<8><<<grid, 256, 0, st>>>(a); break;
+    case 64: qk_rope_fwd_kernel<2><<<blocks, 256, 0, st>>>(a); break;
+    case 128: qk_rope_fwd_kernel<4><<<blocks, 256, 0, st>>>(a); break;
+    case 256: qk_rope_fwd_kernel<8><<<blocks, 256, 0, st>>>(a); break;
+    case 512: qk_rope_fwd_kernel<16><<<blocks, 256, 0, st>>>(a); break;
     default: throw std::invalid_argument("qk_norm_rope: head_dim must be 64/128/256/512");
   }
   PLG_CUDA_CHECK(cudaGetLastError());
@@ -377,15 +516,16 @@ void qk_norm_rope_bwd(const QkRopeArgs& a, const void* dq, const void* dk, void*
                       long long ld_dqkv, float* dwq_partial, float* dwk_partial, int dw_blocks,
                       cudaStream_t st) {
   if (a.T <= 0) return;
+  check_rope_args(a);
   const size_t sm = 2 * a.d * sizeof(float);
   auto q = reinterpret_cast<const __nv_bfloat16*>(dq);
   auto k = reinterpret_cast<const __nv_bfloat16*>(dk);
   auto o = reinterpret_cast<__nv_bfloat16*>(dqkv);
   switch (a.d) {
-    case 64: qk_rope_bwd_kernel<1><<<dw_blocks, 256, sm, st>>>(a, q, k, o, ld_dqkv, dwq_partial, dwk_partial); break;
-    case 128: qk_rope_bwd_kernel<2><<<dw_blocks, 256, sm, st>>>(a, q, k, o, ld_dqkv, dwq_partial, dwk_partial); break;
-    case 256: qk_rope_bwd_kernel<4><<<dw_blocks, 256, sm, st>>>(a, q, k, o, ld_dqkv, dwq_partial, dwk_partial); break;
-    case 512: qk_rope_bwd_kernel<8><<<dw_blocks, 256, sm, st>>>(a, q, k, o, ld_dqkv, dwq_partial, dwk_partial); break;
+    case 64: qk_rope_bwd_kernel<2><<<dw_blocks, 128, sm, st>>>(a, q, k, o, ld_dqkv, dwq_partial, dwk_partial); break;
+    case 128: qk_rope_bwd_kernel<4><<<dw_blocks, 128, sm, st>>>(a, q, k, o, ld_dqkv, dwq_partial, dwk_partial); break;
+    case 256: qk_rope_bwd_kernel<8><<<dw_blocks, 128, sm, st>>>(a, q, k, o, ld_dqkv, dwq_partial, dwk_partial); break;
+    case 512: qk_rope_bwd_kernel<16><<<dw_blocks, 128, sm, st>>>(a, q, k, o, ld_dqkv, dwq_partial, dwk_partial); break;
     default: throw std::invalid_argument("qk_norm_rope_bwd: head_dim must be 64/128/256/512");
   }
   PLG_CUDA_CHECK(cudaGetLastError());

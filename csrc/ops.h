@@ -57,6 +57,7 @@ struct QkRopeArgs {
   int norm_q; int norm_k;  // 0 skips the norm (Llama)
   int k_offset; int v_offset;  // column offsets (in heads*d units) of k and v within a row
   int full_width_norm;     // OLMo: q/k normalised over all heads' channels jointly
+  const float* rope_table; // optional [S][2][rot_dim/2] cos then sin per position (else sincosf)
 };
 void qk_norm_rope_fwd(const QkRopeArgs& a, cudaStream_t stream);
 // backward: dq [T,Hq,d], dk [T,Hk,d] -> dqkv (q and k parts) ; dwq/dwk partials
@@ -72,6 +73,8 @@ void glu_fwd(const void* gu, long long ld_gu, void* out, long long rows, int F, 
 void glu_bwd(const void* gu, long long ld_gu, const void* dout, void* dgu, long long rows, int F,
              int kind, cudaStream_t stream);
 void cast_f32_bf16(const float* x, void* y, long long n, cudaStream_t stream);
+// out[D] = column sums of part[R, D] (fixed summation order)
+void colsum(const float* part, int R, int D, float* out, cudaStream_t stream);
 void cast_bf16_f32(const void* x, float* y, long long n, cudaStream_t stream);
 void embedding_fwd(const int64_t* ids, const float* w, float* out_f32, long long T, int D,
                    float scale, cudaStream_t stream);

@@ -30,60 +30,87 @@ __device__ __forceinline__ void gelu_tanh(float x, float& y, float& dy) {
   dy = 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * k0 * (1.f + 3.f * k1 * x * x);
 }
 
-__global__ void glu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, long long ld,
-                               __nv_bfloat16* __restrict__ out, long long rows, int F, int kind) {
-  const long long n2 = rows * (F / 2);
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n2;
-       i += (long long)gridDim.x * blockDim.x) {
-    const long long r = i / (F / 2);
-    const int c = static_cast<int>(i - r * (F / 2)) * 2;
-    const float2 g = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(gu + r * ld + c));
-    const float2 u = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(gu + r * ld + F + c));
-    float a0, a1;
-    if (kind == 0) {
-      a0 = silu(g.x) * u.x;
-      a1 = silu(g.y) * u.y;
-    } else {
-      float y0, y1, d0, d1;
-      gelu_tanh(g.x, y0, d0);
-      gelu_tanh(g.y, y1, d1);
-      a0 = y0 * u.x;
-      a1 = y1 * u.y;
-    }
-    *reinterpret_cast<uint32_t*>(out + r * F + c) = pack_bf16x2(a0, a1);
+// GLU kernels: one block per group of rows, 8 channels (16 bytes) per thread
+// access; needs F % 8 == 0 and 16-byte aligned rows (checked by the launchers).
+__device__ __forceinline__ void glu_act(float g, float u, int kind, float& a) {
+  if (kind == 0) {
+    a = __fdividef(g, 1.f + fast_exp2(-g * kLog2e)) * u;
+  } else {
+    float y, dy;
+    gelu_tanh(g, y, dy);
+    a = y * u;
   }
 }
 
-__global__ void glu_bwd_kernel(const __nv_bfloat16* __restrict__ gu, long long ld,
-                               const __nv_bfloat16* __restrict__ dout,
-                               __nv_bfloat16* __restrict__ dgu, long long rows, int F, int kind) {
-  const long long n2 = rows * (F / 2);
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n2;
-       i += (long long)gridDim.x * blockDim.x) {
-    const long long r = i / (F / 2);
-    const int c = static_cast<int>(i - r * (F / 2)) * 2;
-    const float2 g = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(gu + r * ld + c));
-    const float2 u = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(gu + r * ld + F + c));
-    const float2 d = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(dout + r * F + c));
-    float dg0, dg1, du0, du1;
-    if (kind == 0) {
-      const float s0 = 1.f / (1.f + fast_exp2(-g.x * kLog2e));
-      const float s1 = 1.f / (1.f + fast_exp2(-g.y * kLog2e));
-      du0 = d.x * g.x * s0;
-      du1 = d.y * g.y * s1;
-      dg0 = d.x * u.x * s0 * (1.f + g.x * (1.f - s0));
-      dg1 = d.y * u.y * s1 * (1.f + g.y * (1.f - s1));
-    } else {
-      float y0, y1, e0, e1;
-      gelu_tanh(g.x, y0, e0);
-      gelu_tanh(g.y, y1, e1);
-      du0 = d.x * y0;
-      du1 = d.y * y1;
-      dg0 = d.x * u.x * e0;
-      dg1 = d.y * u.y * e1;
+__global__ void __launch_bounds__(256) glu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, long long ld,
+                                                      __nv_bfloat16* __restrict__ out, long long rows,
+                                                      int F, int kind) {
+  const int c8 = F / 8;
+  for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
+    const __nv_bfloat16* grow = gu + r * ld;
+    for (int c = threadIdx.x; c < c8; c += blockDim.x) {
+      const uint4 gv = *reinterpret_cast<const uint4*>(grow + c * 8);
+      const uint4 uv = *reinterpret_cast<const uint4*>(grow + F + c * 8);
+      const uint32_t* gp = reinterpret_cast<const uint32_t*>(&gv);
+      const uint32_t* up = reinterpret_cast<const uint32_t*>(&uv);
+      uint4 ov;
+      uint32_t* op = reinterpret_cast<uint32_t*>(&ov);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 g = unpack_bf16x2(gp[k]), u = unpack_bf16x2(up[k]);
+        float a0, a1;
+        glu_act(g.x, u.x, kind, a0);
+        glu_act(g.y, u.y, kind, a1);
+        op[k] = pack_bf16x2(a0, a1);
+      }
+      *reinterpret_cast<uint4*>(out + r * F + c * 8) = ov;
     }
-    *reinterpret_cast<uint32_t*>(dgu + r * ld + c) = pack_bf16x2(dg0, dg1);
-    *reinterpret_cast<uint32_t*>(dgu + r * ld + F + c) = pack_bf16x2(du0, du1);
+  }
+}
+
+__device__ __forceinline__ void glu_grad(float g, float u, float d, int kind, float& dg, float& du) {
+  if (kind == 0) {
+    const float sg = __fdividef(1.f, 1.f + fast_exp2(-g * kLog2e));
+    du = d * g * sg;
+    dg = d * u * sg * (1.f + g * (1.f - sg));
+  } else {
+    float y, e;
+    gelu_tanh(g, y, e);
+    du = d * y;
+    dg = d * u * e;
+  }
+}
+
+__global__ void __launch_bounds__(256) glu_bwd_kernel(const __nv_bfloat16* __restrict__ gu, long long ld,
+                                                      const __nv_bfloat16* __restrict__ dout,
+                                                      __nv_bfloat16* __restrict__ dgu, long long rows,
+                                                      int F, int kind) {
+  const int c8 = F / 8;
+  for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
+    const __nv_bfloat16* grow = gu + r * ld;
+    __nv_bfloat16* drow = dgu + r * ld;
+    for (int c = threadIdx.x; c < c8; c += blockDim.x) {
+      const uint4 gv = *reinterpret_cast<const uint4*>(grow + c * 8);
+      const uint4 uv = *reinterpret_cast<const uint4*>(grow + F + c * 8);
+      const uint4 dv = *reinterpret_cast<const uint4*>(dout + r * F + c * 8);
+      const uint32_t* gp = reinterpret_cast<const uint32_t*>(&gv);
+      const uint32_t* up = reinterpret_cast<const uint32_t*>(&uv);
+      const uint32_t* dp = reinterpret_cast<const uint32_t*>(&dv);
+      uint4 og, ou;
+      uint32_t* ogp = reinterpret_cast<uint32_t*>(&og);
+      uint32_t* oup = reinterpret_cast<uint32_t*>(&ou);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 g = unpack_bf16x2(gp[k]), u = unpack_bf16x2(up[k]), d = unpack_bf16x2(dp[k]);
+        float dg0, du0, dg1, du1;
+        glu_grad(g.x, u.x, d.x, kind, dg0, du0);
+        glu_grad(g.y, u.y, d.y, kind, dg1, du1);
+        ogp[k] = pack_bf16x2(dg0, dg1);
+        oup[k] = pack_bf16x2(du0, du1);
+      }
+      *reinterpret_cast<uint4*>(drow + c * 8) = og;
+      *reinterpret_cast<uint4*>(drow + F + c * 8) = ou;
+    }
   }
 }
 
@@ -315,6 +342,27 @@ __global__ void multi_sumsq_kernel(const int64_t* __restrict__ table, int ntenso
 }
 
 // deterministic final reduction of the per-chunk partials (one block)
+// out[c] = sum_r part[r, c] for a [R, D] fp32 matrix of per-block partial sums,
+// in a fixed order (deterministic): a block owns 32 columns, its 8 warps sum
+// strided row groups, then the warps' sums are added in shared memory.
+__global__ void __launch_bounds__(256) colsum_kernel(const float* __restrict__ part, int R, int D,
+                                                     float* __restrict__ out) {
+  __shared__ float acc[8][33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + lane;
+  float s = 0.f;
+  if (c < D)
+    for (int r = warp; r < R; r += 8) s += part[static_cast<long long>(r) * D + c];
+  acc[warp][lane] = s;
+  __syncthreads();
+  if (warp == 0 && c < D) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += acc[w][lane];
+    out[c] = t;
+  }
+}
+
 __global__ void reduce_partials_kernel(const float* __restrict__ partial, long long n,
                                        float* __restrict__ out) {
   __shared__ double s_red[32];
@@ -420,11 +468,22 @@ int grid_for(long long work, int per_block) {
 
 }  // namespace
 
+static void check_glu(const void* gu, long long ld_gu, const void* out, int F) {
+  if (F % 8 || ld_gu % 8 || (reinterpret_cast<uintptr_t>(gu) & 15) ||
+      (reinterpret_cast<uintptr_t>(out) & 15))
+    throw std::invalid_argument("glu: F and the row stride must be multiples of 8, buffers 16B aligned");
+}
+
+static unsigned glu_blocks(long long rows) {
+  const long long cap = 148LL * 16;
+  return static_cast<unsigned>(rows < cap ? rows : cap);
+}
+
 void glu_fwd(const void* gu, long long ld_gu, void* out, long long rows, int F, int kind,
              cudaStream_t st) {
   if (rows <= 0) return;
-  if (F % 2) throw std::invalid_argument("glu: F must be even");
-  glu_fwd_kernel<<<grid_for(rows * F / 2, 256), 256, 0, st>>>(
+  check_glu(gu, ld_gu, out, F);
+  glu_fwd_kernel<<<glu_blocks(rows), 128, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(gu), ld_gu, reinterpret_cast<__nv_bfloat16*>(out),
       rows, F, kind);
   PLG_CUDA_CHECK(cudaGetLastError());
@@ -433,10 +492,18 @@ void glu_fwd(const void* gu, long long ld_gu, void* out, long long rows, int F, 
 void glu_bwd(const void* gu, long long ld_gu, const void* dout, void* dgu, long long rows, int F,
              int kind, cudaStream_t st) {
   if (rows <= 0) return;
-  glu_bwd_kernel<<<grid_for(rows * F / 2, 256), 256, 0, st>>>(
+  check_glu(gu, ld_gu, dgu, F);
+  check_glu(dout, F, dout, F);
+  glu_bwd_kernel<<<glu_blocks(rows), 128, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(gu), ld_gu,
       reinterpret_cast<const __nv_bfloat16*>(dout), reinterpret_cast<__nv_bfloat16*>(dgu), rows,
       F, kind);
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+void colsum(const float* part, int R, int D, float* out, cudaStream_t st) {
+  if (D <= 0) return;
+  colsum_kernel<<<(D + 31) / 32, 256, 0, st>>>(part, R, D, out);
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 

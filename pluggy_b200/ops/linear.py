@@ -20,10 +20,50 @@ class WeightCache:
     Keyed on the parameter object; a copy is recast whenever the parameter's
     version counter moved (optimizer step, load_state_dict, manual edits), so
     forward passes within one optimizer step share one cast.
+
+    ``bind_optimizer(opt)`` (an optimizer with bf16 shadows, e.g.
+    :class:`~pluggy_b200.optimizer.fused_adamw.FusedAdamW`) removes even that
+    cast: every cached copy is registered as the parameter's shadow, the optimizer
+    writes the bf16 value in the same kernel that updates the fp32 master, and
+    tells the cache the copy is current.
     """
 
     def __init__(self):
-        self._store: dict[int, tuple[int, int, torch.Tensor]] = {}
+        self._store: dict = {}
+        self._params: dict[int, torch.Tensor] = {}
+        self._cat_params: dict[str, list[torch.Tensor]] = {}
+        self._opt = None
+
+    def bind_optimizer(self, opt) -> None:
+        if self._opt is opt:
+            return
+        self._opt = opt
+        opt.add_shadow_listener(self._shadows_written)
+        for key, (_, _, lp) in list(self._store.items()):
+            self._register(key, lp)
+
+    def _register(self, key, lp: torch.Tensor) -> None:
+        if isinstance(key, str):
+            off = 0
+            for p in self._cat_params[key]:
+                n = p.shape[0]
+                self._opt.register_bf16_shadow(p, lp[off:off + n])
+                off += n
+        else:
+            p = self._params.get(key)
+            if p is not None:
+                self._opt.register_bf16_shadow(p, lp)
+
+    def _shadows_written(self, params: list[torch.Tensor]) -> None:
+        ids = {id(p) for p in params}
+        for p in params:
+            hit = self._store.get(id(p))
+            if hit is not None:
+                self._store[id(p)] = (p._version, p.data_ptr(), hit[2])
+        for key, ps in self._cat_params.items():
+            hit = self._store.get(key)
+            if hit is not None and any(id(p) in ids for p in ps):
+                self._store[key] = (tuple((p._version, p.data_ptr()) for p in ps), None, hit[2])
 
     def get(self, p: torch.Tensor) -> torch.Tensor:
         key = id(p)
@@ -33,12 +73,16 @@ class WeightCache:
             return hit[2]
         from pluggy_b200.ops._ext import ext
 
-        lp = torch.empty(p.shape, dtype=torch.bfloat16, device=p.device)
+        lp = hit[2] if hit is not None and hit[2].shape == p.shape else torch.empty(
+            p.shape, dtype=torch.bfloat16, device=p.device)
         if p.is_cuda:
             ext().cast_f32_bf16(p.detach().contiguous(), lp)
         else:
             lp.copy_(p.detach())
         self._store[key] = (ver, p.data_ptr(), lp)
+        self._params[key] = p
+        if self._opt is not None and hit is None:
+            self._register(key, lp)
         return lp
 
     def get_cat(self, params: list[torch.Tensor], key: str) -> torch.Tensor:
@@ -50,7 +94,8 @@ class WeightCache:
         from pluggy_b200.ops._ext import ext
 
         rows = sum(p.shape[0] for p in params)
-        lp = torch.empty((rows, *params[0].shape[1:]), dtype=torch.bfloat16, device=params[0].device)
+        lp = hit[2] if hit is not None else torch.empty(
+            (rows, *params[0].shape[1:]), dtype=torch.bfloat16, device=params[0].device)
         off = 0
         for p in params:
             n = p.shape[0]
@@ -60,10 +105,17 @@ class WeightCache:
                 lp[off:off + n].copy_(p.detach())
             off += n
         self._store[key] = (vers, None, lp)
+        self._cat_params[key] = list(params)
+        if self._opt is not None and hit is None:
+            self._register(key, lp)
         return lp
 
     def clear(self) -> None:
         self._store.clear()
+        self._cat_params.clear()
+        self._params.clear()
+        if self._opt is not None:
+            self._opt.clear_bf16_shadows()
 
 
 class _Linear(torch.autograd.Function):

@@ -18,6 +18,13 @@ from pluggy_b200.ops._ext import ext
 DW_BLOCKS = 592  # 4 CTAs per SM on 148 SMs: dw partial sums reduced by the caller
 
 
+def _colsum(part: torch.Tensor) -> torch.Tensor:
+    """Deterministic column sum of the per-block dw partials [DW_BLOCKS, D]."""
+    out = torch.empty(part.shape[1], dtype=torch.float32, device=part.device)
+    ext().colsum(part, out)
+    return out
+
+
 def rms_norm_reference(x, weight=None, eps=1e-6):
     xf = x.float()
     y = xf * torch.rsqrt(xf.pow(2).mean(dim=-1, keepdim=True) + eps)
@@ -43,7 +50,7 @@ def rmsnorm_bwd(dy, x, w, rstd, *, dres=None, want_f32=True, want_bf16=False, wa
     part = (torch.empty((DW_BLOCKS, D), dtype=torch.float32, device=x.device)
             if (want_dw and w is not None) else None)
     ext().rmsnorm_bwd(dy, x, w, rstd, dres, dxf, dxb, part)
-    dw = part.sum(0) if part is not None else None
+    dw = _colsum(part) if part is not None else None
     return dxf, dxb, dw
 
 
@@ -71,9 +78,30 @@ def rms_norm(x: torch.Tensor, weight: torch.Tensor | None = None, eps: float = 1
     return rms_norm_reference(x, weight, eps)
 
 
+_ROPE_TABLES: dict = {}
+
+
+def rope_table(inv_freq: torch.Tensor, S: int, rot_dim: int) -> torch.Tensor:
+    """fp32 [S, 2, rot_dim/2] table of cos and sin of ``pos * inv_freq`` (the same
+    fp32 products the reference's rotary embedding takes cos/sin of), built once per
+    (frequencies, length) on the device so the kernels skip per-token sincos."""
+    key = (inv_freq.data_ptr(), inv_freq._version, int(S), int(rot_dim), inv_freq.device)
+    t = _ROPE_TABLES.get(key)
+    if t is None:
+        pos = torch.arange(S, dtype=torch.float32, device=inv_freq.device)
+        ang = torch.outer(pos, inv_freq[: rot_dim // 2].float())
+        t = torch.stack((ang.cos(), ang.sin()), dim=1).contiguous()
+        if len(_ROPE_TABLES) > 16:
+            _ROPE_TABLES.clear()
+        _ROPE_TABLES[key] = t
+    return t
+
+
 def qk_norm_rope_fwd(qkv, *, S, Hq, Hk, d, wq, wk, inv_freq, positions=None, eps=1e-6,
                      rot_dim=None, k_offset=None):
     """Normalise+rotate q and k of a fused projection ``qkv [T, (Hq+2Hk)*d]``.
+
+    ``positions`` (int32 [T], optional) must stay below ``S`` (the cos/sin table length).
 
     Returns (q [T,Hq,d], k [T,Hk,d], rstd [T, Hq+Hk]); v stays in ``qkv``.
     """
@@ -81,9 +109,10 @@ def qk_norm_rope_fwd(qkv, *, S, Hq, Hk, d, wq, wk, inv_freq, positions=None, eps
     q = torch.empty((T, Hq, d), dtype=torch.bfloat16, device=qkv.device)
     k = torch.empty((T, Hk, d), dtype=torch.bfloat16, device=qkv.device)
     rstd = torch.empty((T, Hq + Hk), dtype=torch.float32, device=qkv.device)
+    rd = int(d if rot_dim is None else rot_dim)
+    table = rope_table(inv_freq, S, rd) if rd > 0 else None
     ext().qk_norm_rope_fwd(qkv, q, k, rstd, wq, wk, inv_freq, positions, int(S), int(Hq), int(Hk),
-                           int(d), int(d if rot_dim is None else rot_dim), float(eps),
-                           int(Hq if k_offset is None else k_offset))
+                           int(d), rd, float(eps), int(Hq if k_offset is None else k_offset), table)
     return q, k, rstd
 
 
@@ -92,8 +121,9 @@ def qk_norm_rope_bwd(qkv, rstd, dq, dk, dqkv, *, S, Hq, Hk, d, wq, wk, inv_freq,
     """Writes dq/dk (pre-norm) into the q and k columns of ``dqkv``; returns (dwq, dwk)."""
     pq = torch.empty((DW_BLOCKS, d), dtype=torch.float32, device=qkv.device) if wq is not None else None
     pk = torch.empty((DW_BLOCKS, d), dtype=torch.float32, device=qkv.device) if wk is not None else None
+    rd = int(d if rot_dim is None else rot_dim)
+    table = rope_table(inv_freq, S, rd) if rd > 0 else None
     ext().qk_norm_rope_bwd(qkv, rstd, wq, wk, inv_freq, positions, int(S), int(Hq), int(Hk), int(d),
-                           int(d if rot_dim is None else rot_dim), float(eps),
-                           int(Hq if k_offset is None else k_offset), dq, dk, dqkv, pq, pk,
-                           DW_BLOCKS)
-    return (pq.sum(0) if pq is not None else None), (pk.sum(0) if pk is not None else None)
+                           rd, float(eps), int(Hq if k_offset is None else k_offset), dq, dk, dqkv,
+                           pq, pk, DW_BLOCKS, table)
+    return (_colsum(pq) if pq is not None else None), (_colsum(pk) if pk is not None else None)

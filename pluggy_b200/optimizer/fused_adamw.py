@@ -49,6 +49,19 @@ class FusedAdamW(torch.optim.AdamW):
     def clear_bf16_shadows(self) -> None:
         self._shadows.clear()
 
+    def add_shadow_listener(self, fn) -> None:
+        """``fn(params)`` runs after each step with the params whose shadows were written."""
+        if not hasattr(self, "_shadow_listeners"):
+            self._shadow_listeners = []
+        if fn not in self._shadow_listeners:
+            self._shadow_listeners.append(fn)
+
+    def _notify_shadows(self, ps) -> None:
+        written = [p for p in ps if id(p) in self._shadows]
+        if written:
+            for fn in getattr(self, "_shadow_listeners", ()):
+                fn(written)
+
     # ------------------------------------------------------------------- step
     @torch.no_grad()
     def step(self, closure=None):
@@ -94,6 +107,7 @@ class FusedAdamW(torch.optim.AdamW):
                     # the kernel wrote through raw pointers: tell autograd (and the bf16
                     # weight caches keyed on the version counter) that params changed
                     torch.autograd.graph.increment_version(ps)
+                    self._notify_shadows(ps)
                 else:
                     for p in ps:
                         g = p.grad if scale is None else p.grad * scale
@@ -106,4 +120,5 @@ class FusedAdamW(torch.optim.AdamW):
                         sh = self._shadows.get(id(p))
                         if sh is not None:
                             sh.copy_(p.view_as(sh))
+                    self._notify_shadows(ps)
         return loss

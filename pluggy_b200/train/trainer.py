@@ -94,6 +94,12 @@ class Trainer:
                                          self.config["objective"]["config"])
         opt = self.config["optimizer"]
         self.optimizer = build_optimizer(self.model, opt["name"], opt["config"])
+        # the optimizer writes the bf16 copies the GEMMs read (no per-step recast);
+        # FSDP2 gathers full weights per step, so there is nothing to keep current
+        wc = getattr(self.model, "weight_cache", None)
+        if (wc is not None and self.parallelism == "ddp"
+                and hasattr(self.optimizer, "add_shadow_listener")):
+            wc.bind_optimizer(self.optimizer)
         self.scheduler = build_scheduler(self.optimizer, opt["scheduler"])
         self.num_train_steps = opt["scheduler"]["total_steps"]
         self.max_norm = opt.get("max_norm")

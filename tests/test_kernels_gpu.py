@@ -339,3 +339,39 @@ def test_fused_model_matches_eager(family):
     for n, p in mc.named_parameters():
         r = rel(grads[n].cpu(), p.grad)
         assert r < 6e-2, (n, r)
+
+
+def test_colsum_matches_torch():
+    from pluggy_b200.ops.norm import _colsum
+
+    part = torch.randn(592, 1000, device=DEV)
+    assert torch.allclose(_colsum(part), part.sum(0), rtol=1e-5, atol=1e-4)
+
+
+def test_weight_cache_optimizer_shadows():
+    """After optimizer steps, the bf16 copies the GEMMs read equal a fresh cast of
+    the fp32 masters although the cache never recast them."""
+    from pluggy_b200.ops.linear import WeightCache
+    from pluggy_b200.optimizer.fused_adamw import FusedAdamW
+
+    torch.manual_seed(0)
+    w1 = torch.nn.Parameter(torch.randn(256, 128, device=DEV))
+    w2 = torch.nn.Parameter(torch.randn(64, 128, device=DEV))
+    w3 = torch.nn.Parameter(torch.randn(64, 128, device=DEV))
+    opt = FusedAdamW([w1, w2, w3], lr=1e-2)
+    wc = WeightCache()
+    wc.bind_optimizer(opt)
+    for _ in range(3):
+        a = wc.get(w1)
+        cat = wc.get_cat([w2, w3], "w23")
+        ref_a, ref_cat = a.clone(), cat.clone()
+        loss = (a.float() * w1).sum() + (cat.float() * torch.cat([w2, w3])).sum()
+        loss.backward()
+        opt.step()
+        opt.zero_grad()
+        a2 = wc.get(w1)
+        cat2 = wc.get_cat([w2, w3], "w23")
+        assert a2.data_ptr() == a.data_ptr() and cat2.data_ptr() == cat.data_ptr()
+        assert torch.equal(a2, w1.detach().bfloat16())
+        assert torch.equal(cat2, torch.cat([w2, w3]).detach().bfloat16())
+        assert not torch.equal(a2, ref_a) and not torch.equal(cat2, ref_cat)
