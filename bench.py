@@ -234,6 +234,12 @@ def run_reference(args, rank, local_rank, world, device) -> dict:
     for name in list(sys.modules):
         if name == "pluggy" or name.startswith("pluggy."):
             del sys.modules[name]
+    # the reference's top-level package has no __init__.py, and a regular package of
+    # the same name (pytest's plugin manager) sits in site-packages and would win the
+    # import: bind the name to the reference tree explicitly
+    pkg = types.ModuleType("pluggy")
+    pkg.__path__ = [os.path.join(REF_DIR, "pluggy")]
+    sys.modules["pluggy"] = pkg
     # the reference's model registry imports two modules missing from its tree
     for mod, cls in (("pluggy.models.grokathon_model.grokathon_model", "GrokathonModel"),
                      ("pluggy.models.hybrid_test.hybrid_test", "HybridTest")):
