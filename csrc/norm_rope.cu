@@ -223,49 +223,54 @@ void rmsnorm_bwd_t(const void* dy, const void* x, const float* w, const float* r
 }
 
 // ------------------------------------------------------------ QK-norm + RoPE
-// One warp per token, looping over all its q and k heads. Lane l owns the NV =
-// d/32 consecutive channels [l*NV, l*NV + NV) (one vector load per head row).
-// RoPE is rotate-half over the first rot_dim channels: channel i < rot_dim/2 pairs
-// with i + rot_dim/2 (a lane shuffle away). The token's cos/sin values are
-// computed once per lane and reused by every head.
-template <int NV>
-struct BfVec;
-template <>
-struct BfVec<2> { using T = uint32_t; };
-template <>
-struct BfVec<4> { using T = uint2; };
-template <>
-struct BfVec<8> { using T = uint4; };
+// Lane layout: a head row of d channels is spread over LPH = d / NV lanes of NV
+// consecutive channels each (NV = 8: one 16-byte access per lane; NV = 16 for
+// d = 512), so one warp instruction covers HPW = 32 / LPH heads. A work item is
+// (token, kRounds * HPW consecutive heads); all of its rows are loaded before any
+// is used, which keeps enough bytes in flight for the memory system.
+// RoPE is rotate-half over the first rot_dim channels: channel i < rot_dim/2
+// pairs with i + rot_dim/2, a lane shuffle away inside the head's lane group.
+template <int D>
+struct RopeLayout {
+  static constexpr int NV = D >= 512 ? 16 : 8;
+  static constexpr int LPH = D / NV;
+  static constexpr int HPW = 32 / LPH;
+  static constexpr int kRounds = D >= 512 ? 1 : (D >= 256 ? 2 : 4);
+};
 
 template <int NV>
-__device__ __forceinline__ void load_bf(const __nv_bfloat16* p, float (&v)[NV]) {
-  if constexpr (NV == 16) {
-    load_bf<8>(p, *reinterpret_cast<float(*)[8]>(v));
-    load_bf<8>(p + 8, *reinterpret_cast<float(*)[8]>(v + 8));
-  } else {
-    const typename BfVec<NV>::T raw = *reinterpret_cast<const typename BfVec<NV>::T*>(p);
+__device__ __forceinline__ void load_row(const __nv_bfloat16* p, float (&v)[NV]) {
+#pragma unroll
+  for (int q = 0; q < NV / 8; ++q) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(p + q * 8);
     const uint32_t* u = reinterpret_cast<const uint32_t*>(&raw);
 #pragma unroll
-    for (int k = 0; k < NV / 2; ++k) {
+    for (int k = 0; k < 4; ++k) {
       const float2 f = unpack_bf16x2(u[k]);
-      v[2 * k] = f.x;
-      v[2 * k + 1] = f.y;
+      v[q * 8 + 2 * k] = f.x;
+      v[q * 8 + 2 * k + 1] = f.y;
     }
   }
 }
 
 template <int NV>
-__device__ __forceinline__ void store_bf(__nv_bfloat16* p, const float (&v)[NV]) {
-  if constexpr (NV == 16) {
-    store_bf<8>(p, *reinterpret_cast<const float(*)[8]>(v));
-    store_bf<8>(p + 8, *reinterpret_cast<const float(*)[8]>(v + 8));
-  } else {
-    typename BfVec<NV>::T raw;
+__device__ __forceinline__ void store_row(__nv_bfloat16* p, const float (&v)[NV]) {
+#pragma unroll
+  for (int q = 0; q < NV / 8; ++q) {
+    uint4 raw;
     uint32_t* u = reinterpret_cast<uint32_t*>(&raw);
 #pragma unroll
-    for (int k = 0; k < NV / 2; ++k) u[k] = pack_bf16x2(v[2 * k], v[2 * k + 1]);
-    *reinterpret_cast<typename BfVec<NV>::T*>(p) = raw;
+    for (int k = 0; k < 4; ++k) u[k] = pack_bf16x2(v[q * 8 + 2 * k], v[q * 8 + 2 * k + 1]);
+    *reinterpret_cast<uint4*>(p + q * 8) = raw;
   }
+}
+
+// sum over the LPH lanes of one head group (aligned power-of-two groups)
+template <int LPH>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+  for (int o = LPH / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
 }
 
 // cos/sin of this lane's channels for position pos (c0 = first channel of the lane)
@@ -273,10 +278,10 @@ template <int NV>
 __device__ __forceinline__ void rope_angles(const QkRopeArgs& a, int pos, int c0, float (&cs)[NV],
                                             float (&sn)[NV]) {
   const int rh = a.rot_dim / 2;
+  const int f0 = c0 < rh ? c0 : c0 - rh;
   if (a.rope_table != nullptr) {
     // a lane's NV channels lie in one half of the rotated prefix (rh % NV == 0)
     const float* row = a.rope_table + static_cast<long long>(pos) * a.rot_dim;
-    const int f0 = c0 < rh ? c0 : c0 - rh;
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       const bool rot = c0 + k < a.rot_dim;
@@ -287,9 +292,8 @@ __device__ __forceinline__ void rope_angles(const QkRopeArgs& a, int pos, int c0
   }
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
-    const int c = c0 + k;
-    if (c < a.rot_dim) {
-      sincosf(static_cast<float>(pos) * a.inv_freq[c < rh ? c : c - rh], &sn[k], &cs[k]);
+    if (c0 + k < a.rot_dim) {
+      sincosf(static_cast<float>(pos) * a.inv_freq[f0 + k], &sn[k], &cs[k]);
     } else {
       cs[k] = 1.f;
       sn[k] = 0.f;
@@ -297,21 +301,18 @@ __device__ __forceinline__ void rope_angles(const QkRopeArgs& a, int pos, int c0
   }
 }
 
-// heads per work item: each warp loads the rows of hc_for(NV) heads of one token
-// up front (memory-level parallelism), then normalises and rotates them
-constexpr int hc_for(int nv) { return nv >= 16 ? 1 : (nv >= 8 ? 2 : 4); }
-
-template <int NV>
+template <int D>
 __global__ void __launch_bounds__(256, 2) qk_rope_fwd_kernel(QkRopeArgs a) {
-  constexpr int kHC = hc_for(NV);
+  using L = RopeLayout<D>;
+  constexpr int NV = L::NV, HPI = L::HPW * L::kRounds;
   const int lane = threadIdx.x & 31;
-  const int d = NV * 32, c0 = lane * NV;
+  const int sub = lane / L::LPH, ll = lane % L::LPH, c0 = ll * NV;
   const int H = a.Hq + a.Hk;
-  const int nch = (H + kHC - 1) / kHC;
+  const int nch = (H + HPI - 1) / HPI;
   const int rh = a.rot_dim / 2;
-  // partner lane of the rotate-half pair (lanes beyond rot_dim keep their own values)
   const int off = rh / NV;
-  const int partner = c0 < rh ? lane + off : (c0 < a.rot_dim ? lane - off : lane);
+  const int pl = c0 < rh ? ll + off : (c0 < a.rot_dim ? ll - off : ll);
+  const int partner = sub * L::LPH + pl;
   const float sgn = c0 < rh ? -1.f : 1.f;
   float wq[NV], wk[NV];
 #pragma unroll
@@ -323,140 +324,149 @@ __global__ void __launch_bounds__(256, 2) qk_rope_fwd_kernel(QkRopeArgs a) {
   for (long long it = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items;
        it += (long long)gridDim.x * (blockDim.x >> 5)) {
     const long long t = it / nch;
-    const int h0 = static_cast<int>(it - t * nch) * kHC;
+    const int h0 = static_cast<int>(it - t * nch) * HPI;
     const int pos = a.positions ? a.positions[t] : static_cast<int>(t % a.S);
     const __nv_bfloat16* row = reinterpret_cast<const __nv_bfloat16*>(a.qkv) + t * a.ld_qkv;
-    float v[kHC][NV];
+    float v[L::kRounds][NV];
 #pragma unroll
-    for (int hh = 0; hh < kHC; ++hh) {
-      const int h = h0 + hh;
+    for (int rr = 0; rr < L::kRounds; ++rr) {
+      const int h = h0 + rr * L::HPW + sub;
       if (h < H) {
-        const int col = h < a.Hq ? h * d : a.k_offset * d + (h - a.Hq) * d;
-        load_bf<NV>(row + col + c0, v[hh]);
+        const int col = h < a.Hq ? h * D : a.k_offset * D + (h - a.Hq) * D;
+        load_row<NV>(row + col + c0, v[rr]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < NV; ++k) v[rr][k] = 0.f;
       }
     }
     float cs[NV], sn[NV];
     rope_angles<NV>(a, pos, c0, cs, sn);
 #pragma unroll
-    for (int hh = 0; hh < kHC; ++hh) {
-      const int h = h0 + hh;
-      if (h >= H) break;
+    for (int rr = 0; rr < L::kRounds; ++rr) {
+      const int h = h0 + rr * L::HPW + sub;
       const bool is_q = h < a.Hq;
-      float r = 1.f;
-      if (is_q ? a.norm_q : a.norm_k) {
-        float ss = 0.f;
+      const bool do_norm = is_q ? a.norm_q : a.norm_k;
+      float ss = 0.f;
 #pragma unroll
-        for (int k = 0; k < NV; ++k) ss += v[hh][k] * v[hh][k];
-        ss = warp_sum(ss);
-        r = rsqrtf(ss / d + a.eps);
+      for (int k = 0; k < NV; ++k) ss += v[rr][k] * v[rr][k];
+      ss = group_sum<L::LPH>(ss);
+      const float r = do_norm ? rsqrtf(ss / D + a.eps) : 1.f;
 #pragma unroll
-        for (int k = 0; k < NV; ++k) v[hh][k] *= r * (is_q ? wq[k] : wk[k]);
-      }
-      if (lane == 0 && a.rstd) a.rstd[t * H + h] = r;
+      for (int k = 0; k < NV; ++k) v[rr][k] *= do_norm ? r * (is_q ? wq[k] : wk[k]) : 1.f;
       float o[NV];
 #pragma unroll
       for (int k = 0; k < NV; ++k) {
-        const float p = __shfl_sync(0xffffffffu, v[hh][k], partner);
-        o[k] = v[hh][k] * cs[k] + sgn * p * sn[k];
+        const float p = __shfl_sync(0xffffffffu, v[rr][k], partner);
+        o[k] = v[rr][k] * cs[k] + sgn * p * sn[k];
       }
-      __nv_bfloat16* dst = is_q ? reinterpret_cast<__nv_bfloat16*>(a.q) + (t * a.Hq + h) * d
-                                : reinterpret_cast<__nv_bfloat16*>(a.k) + (t * a.Hk + (h - a.Hq)) * d;
-      store_bf<NV>(dst + c0, o);
+      if (h < H) {
+        if (ll == 0 && a.rstd) a.rstd[t * H + h] = r;
+        __nv_bfloat16* dst = is_q ? reinterpret_cast<__nv_bfloat16*>(a.q) + (t * a.Hq + h) * D
+                                  : reinterpret_cast<__nv_bfloat16*>(a.k) + (t * a.Hk + (h - a.Hq)) * D;
+        store_row<NV>(dst + c0, o);
+      }
     }
   }
 }
 
 // 128 threads, at most 128 registers: all DW_BLOCKS (4 per SM) resident at once
-template <int NV>
+template <int D>
 __global__ void __launch_bounds__(128, 4) qk_rope_bwd_kernel(QkRopeArgs a, const __nv_bfloat16* dq,
-                                                          const __nv_bfloat16* dk,
-                                                          __nv_bfloat16* dqkv, long long ld_dqkv,
-                                                          float* dwq_part, float* dwk_part) {
-  constexpr int kHC = hc_for(NV);
-  extern __shared__ float s_dw[];  // [2 * d]: q weights then k weights
+                                                             const __nv_bfloat16* dk,
+                                                             __nv_bfloat16* dqkv, long long ld_dqkv,
+                                                             float* dwq_part, float* dwk_part) {
+  using L = RopeLayout<D>;
+  constexpr int NV = L::NV, HPI = L::HPW * L::kRounds;
+  extern __shared__ float s_dw[];  // [2 * D]: q weights then k weights
   const int lane = threadIdx.x & 31;
-  const int d = NV * 32, c0 = lane * NV;
-  for (int i = threadIdx.x; i < 2 * d; i += blockDim.x) s_dw[i] = 0.f;
+  const int sub = lane / L::LPH, ll = lane % L::LPH, c0 = ll * NV;
+  for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) s_dw[i] = 0.f;
   __syncthreads();
   const int H = a.Hq + a.Hk;
-  const int nch = (H + kHC - 1) / kHC;
+  const int nch = (H + HPI - 1) / HPI;
   const int rh = a.rot_dim / 2;
   const int off = rh / NV;
-  const int partner = c0 < rh ? lane + off : (c0 < a.rot_dim ? lane - off : lane);
+  const int pl = c0 < rh ? ll + off : (c0 < a.rot_dim ? ll - off : ll);
+  const int partner = sub * L::LPH + pl;
   // transpose of the rotation: d_lo = g_lo c + g_hi s, d_hi = g_hi c - g_lo s
   const float sgn = c0 < rh ? 1.f : -1.f;
-  float wq[NV], wk[NV], accq[NV], acck[NV];
+  float accq[NV], acck[NV];
 #pragma unroll
-  for (int k = 0; k < NV; ++k) {
-    wq[k] = a.norm_q ? a.wq[c0 + k] : 1.f;
-    wk[k] = a.norm_k ? a.wk[c0 + k] : 1.f;
-    accq[k] = acck[k] = 0.f;
-  }
+  for (int k = 0; k < NV; ++k) accq[k] = acck[k] = 0.f;
   const long long items = a.T * nch;
   for (long long it = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items;
        it += (long long)gridDim.x * (blockDim.x >> 5)) {
     const long long t = it / nch;
-    const int h0 = static_cast<int>(it - t * nch) * kHC;
+    const int h0 = static_cast<int>(it - t * nch) * HPI;
     const int pos = a.positions ? a.positions[t] : static_cast<int>(t % a.S);
     const __nv_bfloat16* xrow = reinterpret_cast<const __nv_bfloat16*>(a.qkv) + t * a.ld_qkv;
     __nv_bfloat16* orow = dqkv + t * ld_dqkv;
-    float g[kHC][NV], x[kHC][NV], rs[kHC];
+    float g[L::kRounds][NV], x[L::kRounds][NV], rs[L::kRounds];
 #pragma unroll
-    for (int hh = 0; hh < kHC; ++hh) {
-      const int h = h0 + hh;
+    for (int rr = 0; rr < L::kRounds; ++rr) {
+      const int h = h0 + rr * L::HPW + sub;
       if (h < H) {
         const bool is_q = h < a.Hq;
-        const int col = is_q ? h * d : a.k_offset * d + (h - a.Hq) * d;
-        load_bf<NV>((is_q ? dq + (t * a.Hq + h) * d : dk + (t * a.Hk + (h - a.Hq)) * d) + c0, g[hh]);
-        load_bf<NV>(xrow + col + c0, x[hh]);
-        rs[hh] = (is_q ? a.norm_q : a.norm_k) ? a.rstd[t * H + h] : 1.f;
+        const int col = is_q ? h * D : a.k_offset * D + (h - a.Hq) * D;
+        load_row<NV>((is_q ? dq + (t * a.Hq + h) * D : dk + (t * a.Hk + (h - a.Hq)) * D) + c0, g[rr]);
+        load_row<NV>(xrow + col + c0, x[rr]);
+        rs[rr] = (is_q ? a.norm_q : a.norm_k) ? a.rstd[t * H + h] : 1.f;
+      } else {
+#pragma unroll
+        for (int k = 0; k < NV; ++k) g[rr][k] = x[rr][k] = 0.f;
+        rs[rr] = 1.f;
       }
     }
     float cs[NV], sn[NV];
     rope_angles<NV>(a, pos, c0, cs, sn);
 #pragma unroll
-    for (int hh = 0; hh < kHC; ++hh) {
-      const int h = h0 + hh;
-      if (h >= H) break;
+    for (int rr = 0; rr < L::kRounds; ++rr) {
+      const int h = h0 + rr * L::HPW + sub;
       const bool is_q = h < a.Hq;
-      const int col = is_q ? h * d : a.k_offset * d + (h - a.Hq) * d;
+      const bool do_norm = (is_q ? a.norm_q : a.norm_k) && h < H;
+      const float* wp = is_q ? a.wq : a.wk;
       float gr[NV];
 #pragma unroll
       for (int k = 0; k < NV; ++k) {
-        const float p = __shfl_sync(0xffffffffu, g[hh][k], partner);
-        gr[k] = g[hh][k] * cs[k] + sgn * p * sn[k];
+        const float p = __shfl_sync(0xffffffffu, g[rr][k], partner);
+        gr[k] = g[rr][k] * cs[k] + sgn * p * sn[k];
       }
-      float o[NV];
-      if (is_q ? a.norm_q : a.norm_k) {
-        const float r = rs[hh];
-        float dot = 0.f;
+      const float r = rs[rr];
+      float dot = 0.f;
+      float wv[NV];
 #pragma unroll
-        for (int k = 0; k < NV; ++k) {
-          const float xh = x[hh][k] * r, w = is_q ? wq[k] : wk[k];
-          dot += gr[k] * w * xh;
+      for (int k = 0; k < NV; ++k) {
+        wv[k] = do_norm ? wp[c0 + k] : 1.f;
+        dot += gr[k] * wv[k] * x[rr][k] * r;
+      }
+      dot = group_sum<L::LPH>(dot) / D;
+      float o[NV];
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        if (do_norm) {
+          const float xh = x[rr][k] * r;
           if (is_q) accq[k] += gr[k] * xh;
           else acck[k] += gr[k] * xh;
+          o[k] = r * (gr[k] * wv[k] - xh * dot);
+        } else {
+          o[k] = gr[k];
         }
-        dot = warp_sum(dot) / d;
-#pragma unroll
-        for (int k = 0; k < NV; ++k)
-          o[k] = r * (gr[k] * (is_q ? wq[k] : wk[k]) - x[hh][k] * r * dot);
-      } else {
-#pragma unroll
-        for (int k = 0; k < NV; ++k) o[k] = gr[k];
       }
-      store_bf<NV>(orow + col + c0, o);
+      if (h < H) {
+        const int col = is_q ? h * D : a.k_offset * D + (h - a.Hq) * D;
+        store_row<NV>(orow + col + c0, o);
+      }
     }
   }
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
     atomicAdd(&s_dw[c0 + k], accq[k]);
-    atomicAdd(&s_dw[d + c0 + k], acck[k]);
+    atomicAdd(&s_dw[D + c0 + k], acck[k]);
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < d; i += blockDim.x) {
-    if (dwq_part) dwq_part[(long long)blockIdx.x * d + i] = s_dw[i];
-    if (dwk_part) dwk_part[(long long)blockIdx.x * d + i] = s_dw[d + i];
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    if (dwq_part) dwq_part[(long long)blockIdx.x * D + i] = s_dw[i];
+    if (dwk_part) dwk_part[(long long)blockIdx.x * D + i] = s_dw[D + i];
   }
 }
 
@@ -488,25 +498,35 @@ void rmsnorm_bwd(const void* dy, bool dy_fp32, const void* x, bool x_fp32, const
 }
 
 static void check_rope_args(const QkRopeArgs& a) {
-  const int nv = a.d / 32;
+  const int nv = a.d >= 512 ? 16 : 8;
   if (a.rot_dim < 0 || a.rot_dim > a.d || (a.rot_dim % (2 * nv)) != 0)
-    throw std::invalid_argument("qk_norm_rope: rot_dim must be a multiple of 2*d/32 and <= d");
-  if ((a.ld_qkv % 8) != 0 || (reinterpret_cast<uintptr_t>(a.qkv) & 15))
-    throw std::invalid_argument("qk_norm_rope: qkv rows must be 16-byte aligned");
+    throw std::invalid_argument("qk_norm_rope: rot_dim must be a multiple of 2*(d>=512 ? 16 : 8)");
+  if ((a.ld_qkv % 8) != 0 || (reinterpret_cast<uintptr_t>(a.qkv) & 15) ||
+      (a.q && (reinterpret_cast<uintptr_t>(a.q) & 15)) || (a.k && (reinterpret_cast<uintptr_t>(a.k) & 15)))
+    throw std::invalid_argument("qk_norm_rope: rows must be 16-byte aligned");
+}
+
+template <int D>
+static long long rope_items(const QkRopeArgs& a) {
+  constexpr int hpi = RopeLayout<D>::HPW * RopeLayout<D>::kRounds;
+  return a.T * ((a.Hq + a.Hk + hpi - 1) / hpi);
+}
+
+template <int D>
+static void rope_fwd_t(const QkRopeArgs& a, cudaStream_t st) {
+  long long blocks = (rope_items<D>(a) + 7) / 8;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  qk_rope_fwd_kernel<D><<<static_cast<unsigned>(blocks), 256, 0, st>>>(a);
 }
 
 void qk_norm_rope_fwd(const QkRopeArgs& a, cudaStream_t st) {
   if (a.T <= 0) return;
   check_rope_args(a);
-  const int hc = hc_for(a.d / 32);
-  const long long items = a.T * ((a.Hq + a.Hk + hc - 1) / hc);
-  long long blocks = (items + 7) / 8;
-  if (blocks > 148 * 16) blocks = 148 * 16;
   switch (a.d) {
-    case 64: qk_rope_fwd_kernel<2><<<blocks, 256, 0, st>>>(a); break;
-    case 128: qk_rope_fwd_kernel<4><<<blocks, 256, 0, st>>>(a); break;
-    case 256: qk_rope_fwd_kernel<8><<<blocks, 256, 0, st>>>(a); break;
-    case 512: qk_rope_fwd_kernel<16><<<blocks, 256, 0, st>>>(a); break;
+    case 64: rope_fwd_t<64>(a, st); break;
+    case 128: rope_fwd_t<128>(a, st); break;
+    case 256: rope_fwd_t<256>(a, st); break;
+    case 512: rope_fwd_t<512>(a, st); break;
     default: throw std::invalid_argument("qk_norm_rope: head_dim must be 64/128/256/512");
   }
   PLG_CUDA_CHECK(cudaGetLastError());
@@ -517,15 +537,18 @@ void qk_norm_rope_bwd(const QkRopeArgs& a, const void* dq, const void* dk, void*
                       cudaStream_t st) {
   if (a.T <= 0) return;
   check_rope_args(a);
+  if ((ld_dqkv % 8) || (reinterpret_cast<uintptr_t>(dqkv) & 15) ||
+      (reinterpret_cast<uintptr_t>(dq) & 15) || (reinterpret_cast<uintptr_t>(dk) & 15))
+    throw std::invalid_argument("qk_norm_rope_bwd: rows must be 16-byte aligned");
   const size_t sm = 2 * a.d * sizeof(float);
   auto q = reinterpret_cast<const __nv_bfloat16*>(dq);
   auto k = reinterpret_cast<const __nv_bfloat16*>(dk);
   auto o = reinterpret_cast<__nv_bfloat16*>(dqkv);
   switch (a.d) {
-    case 64: qk_rope_bwd_kernel<2><<<dw_blocks, 128, sm, st>>>(a, q, k, o, ld_dqkv, dwq_partial, dwk_partial); break;
-    case 128: qk_rope_bwd_kernel<4><<<dw_blocks, 128, sm, st>>>(a, q, k, o, ld_dqkv, dwq_partial, dwk_partial); break;
-    case 256: qk_rope_bwd_kernel<8><<<dw_blocks, 128, sm, st>>>(a, q, k, o, ld_dqkv, dwq_partial, dwk_partial); break;
-    case 512: qk_rope_bwd_kernel<16><<<dw_blocks, 128, sm, st>>>(a, q, k, o, ld_dqkv, dwq_partial, dwk_partial); break;
+    case 64: qk_rope_bwd_kernel<64><<<dw_blocks, 128, sm, st>>>(a, q, k, o, ld_dqkv, dwq_partial, dwk_partial); break;
+    case 128: qk_rope_bwd_kernel<128><<<dw_blocks, 128, sm, st>>>(a, q, k, o, ld_dqkv, dwq_partial, dwk_partial); break;
+    case 256: qk_rope_bwd_kernel<256><<<dw_blocks, 128, sm, st>>>(a, q, k, o, ld_dqkv, dwq_partial, dwk_partial); break;
+    case 512: qk_rope_bwd_kernel<512><<<dw_blocks, 128, sm, st>>>(a, q, k, o, ld_dqkv, dwq_partial, dwk_partial); break;
     default: throw std::invalid_argument("qk_norm_rope_bwd: head_dim must be 64/128/256/512");
   }
   PLG_CUDA_CHECK(cudaGetLastError());

@@ -11,6 +11,8 @@ The model fast path calls the raw launchers (``rmsnorm_fwd``/``rmsnorm_bwd``,
 
 from __future__ import annotations
 
+import weakref
+
 import torch
 
 from pluggy_b200.ops._ext import ext
@@ -85,15 +87,18 @@ def rope_table(inv_freq: torch.Tensor, S: int, rot_dim: int) -> torch.Tensor:
     """fp32 [S, 2, rot_dim/2] table of cos and sin of ``pos * inv_freq`` (the same
     fp32 products the reference's rotary embedding takes cos/sin of), built once per
     (frequencies, length) on the device so the kernels skip per-token sincos."""
-    key = (inv_freq.data_ptr(), inv_freq._version, int(S), int(rot_dim), inv_freq.device)
-    t = _ROPE_TABLES.get(key)
-    if t is None:
-        pos = torch.arange(S, dtype=torch.float32, device=inv_freq.device)
-        ang = torch.outer(pos, inv_freq[: rot_dim // 2].float())
-        t = torch.stack((ang.cos(), ang.sin()), dim=1).contiguous()
-        if len(_ROPE_TABLES) > 16:
-            _ROPE_TABLES.clear()
-        _ROPE_TABLES[key] = t
+    # keyed on the frequency tensor object itself (a weak reference guards against a
+    # new tensor reusing a freed one's id or storage)
+    key = (id(inv_freq), inv_freq._version, int(S), int(rot_dim))
+    hit = _ROPE_TABLES.get(key)
+    if hit is not None and hit[0]() is inv_freq:
+        return hit[1]
+    pos = torch.arange(S, dtype=torch.float32, device=inv_freq.device)
+    ang = torch.outer(pos, inv_freq[: rot_dim // 2].float())
+    t = torch.stack((ang.cos(), ang.sin()), dim=1).contiguous()
+    if len(_ROPE_TABLES) > 16:
+        _ROPE_TABLES.clear()
+    _ROPE_TABLES[key] = (weakref.ref(inv_freq), t)
     return t
 
 

@@ -119,8 +119,9 @@ def test_rmsnorm_fwd_bwd(D, xdt):
     assert rel(w.grad, wr.grad) < 1e-3
 
 
-def _ref_qk_rope(qkv, S, Hq, Hk, d, wq, wk, inv, eps):
+def _ref_qk_rope(qkv, S, Hq, Hk, d, wq, wk, inv, eps, rot_dim=None):
     T = qkv.shape[0]
+    rd = d if rot_dim is None else rot_dim
     q = qkv[:, :Hq * d].view(T, Hq, d)
     k = qkv[:, Hq * d:(Hq + Hk) * d].view(T, Hk, d)
 
@@ -129,38 +130,44 @@ def _ref_qk_rope(qkv, S, Hq, Hk, d, wq, wk, inv, eps):
 
     q, k = nrm(q, wq), nrm(k, wk)
     pos = (torch.arange(T, device=qkv.device) % S).float()
-    f = pos[:, None] * inv[None]
+    f = pos[:, None] * inv[None, : rd // 2]
     cos = torch.cat([f, f], -1).cos()[:, None]
     sin = torch.cat([f, f], -1).sin()[:, None]
 
     def rot(x):
-        h = d // 2
-        return x * cos + torch.cat([-x[..., h:], x[..., :h]], -1) * sin
+        # rotate-half over the first rd channels (HF partial rotary), the rest pass through
+        xr, xp = x[..., :rd], x[..., rd:]
+        h = rd // 2
+        xr = xr * cos + torch.cat([-xr[..., h:], xr[..., :h]], -1) * sin
+        return torch.cat([xr, xp], -1)
 
     return rot(q), rot(k)
 
 
-@pytest.mark.parametrize("d", [64, 128])
-def test_qk_norm_rope_fwd_bwd(d):
+@pytest.mark.parametrize("d,rot_frac,Hq,Hk", [(64, 1, 4, 2), (128, 1, 4, 2), (128, 1, 16, 8),
+                                               (128, 0.5, 4, 2), (256, 1, 3, 1), (128, 0, 2, 1)])
+def test_qk_norm_rope_fwd_bwd(d, rot_frac, Hq, Hk):
     from pluggy_b200.ops.norm import qk_norm_rope_bwd, qk_norm_rope_fwd
 
-    B, S, Hq, Hk = 2, 192, 4, 2
+    B, S = 2, 192
     T = B * S
+    rd = int(d * rot_frac)
     W = (Hq + 2 * Hk) * d
     qkv = torch.randn(T, W, device=DEV).bfloat16()
     wq = 1 + 0.1 * torch.randn(d, device=DEV)
     wk = 1 + 0.1 * torch.randn(d, device=DEV)
     inv = 1.0 / (1e6 ** (torch.arange(0, d, 2, device=DEV).float() / d))
-    q, k, rstd = qk_norm_rope_fwd(qkv, S=S, Hq=Hq, Hk=Hk, d=d, wq=wq, wk=wk, inv_freq=inv, eps=1e-6)
+    q, k, rstd = qk_norm_rope_fwd(qkv, S=S, Hq=Hq, Hk=Hk, d=d, wq=wq, wk=wk, inv_freq=inv, eps=1e-6,
+                                  rot_dim=rd)
     x = qkv.float().requires_grad_(True)
     wqr, wkr = wq.clone().requires_grad_(True), wk.clone().requires_grad_(True)
-    qr, kr = _ref_qk_rope(x, S, Hq, Hk, d, wqr, wkr, inv, 1e-6)
+    qr, kr = _ref_qk_rope(x, S, Hq, Hk, d, wqr, wkr, inv, 1e-6, rot_dim=rd)
     assert rel(q, qr) < 1e-2 and rel(k, kr) < 1e-2
     gq, gk = torch.randn_like(qr), torch.randn_like(kr)
     ((qr * gq).sum() + (kr * gk).sum()).backward()
     dqkv = torch.zeros(T, W, device=DEV, dtype=torch.bfloat16)
     dwq, dwk = qk_norm_rope_bwd(qkv, rstd, gq.bfloat16(), gk.bfloat16(), dqkv, S=S, Hq=Hq, Hk=Hk,
-                                d=d, wq=wq, wk=wk, inv_freq=inv, eps=1e-6)
+                                d=d, wq=wq, wk=wk, inv_freq=inv, eps=1e-6, rot_dim=rd)
     assert rel(dqkv[:, :(Hq + Hk) * d], x.grad[:, :(Hq + Hk) * d]) < 2e-2
     assert rel(dwq, wqr.grad) < 2e-2 and rel(dwk, wkr.grad) < 2e-2
 
