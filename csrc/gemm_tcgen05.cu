@@ -63,6 +63,102 @@ struct Cfg {
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
+// Epilogue of one accumulator row (this thread's TMEM lane): BN fp32 columns at
+// t_row -> alpha * acc (+ beta * D) -> C (bf16 / fp32 / split-K fp32 atomics).
+template <int BN>
+__device__ __forceinline__ void store_acc_row(const Args& args, uint32_t t_row, long long row,
+                                              bool row_ok, int col_base, int kb0) {
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    uint32_t r[32];
+    __syncwarp();
+    tmem_ld_32x32b_x32(t_row + c * 32, r);
+    tmem_ld_wait();
+    const int col0 = col_base + c * 32;
+    if (!row_ok || col0 >= args.N) continue;
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * args.alpha;
+    const bool full = col0 + 32 <= args.N;
+    if (args.D != nullptr && args.beta != 0.f && kb0 == 0) {
+      if (args.d_fp32) {
+        const float* dp = reinterpret_cast<const float*>(args.D) + row * args.ldd + col0;
+        if (full) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            float4 d4 = *reinterpret_cast<const float4*>(dp + i);
+            v[i] += args.beta * d4.x; v[i + 1] += args.beta * d4.y;
+            v[i + 2] += args.beta * d4.z; v[i + 3] += args.beta * d4.w;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (col0 + i < args.N) v[i] += args.beta * dp[i];
+        }
+      } else {
+        const __nv_bfloat16* dp =
+            reinterpret_cast<const __nv_bfloat16*>(args.D) + row * args.ldd + col0;
+        if (full) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 u = *reinterpret_cast<const uint4*>(dp + i);
+            float2 f0 = unpack_bf16x2(u.x), f1 = unpack_bf16x2(u.y);
+            float2 f2 = unpack_bf16x2(u.z), f3 = unpack_bf16x2(u.w);
+            v[i] += args.beta * f0.x; v[i + 1] += args.beta * f0.y;
+            v[i + 2] += args.beta * f1.x; v[i + 3] += args.beta * f1.y;
+            v[i + 4] += args.beta * f2.x; v[i + 5] += args.beta * f2.y;
+            v[i + 6] += args.beta * f3.x; v[i + 7] += args.beta * f3.y;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (col0 + i < args.N) v[i] += args.beta * __bfloat162float(dp[i]);
+        }
+      }
+    }
+    if (args.c_fp32) {
+      float* cp = reinterpret_cast<float*>(args.C) + row * args.ldc + col0;
+      if (args.splits > 1) {
+        if (full) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            atomicAdd(reinterpret_cast<float4*>(cp + i),
+                      make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (col0 + i < args.N) atomicAdd(cp + i, v[i]);
+        }
+      } else if (full) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+          *reinterpret_cast<float4*>(cp + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (col0 + i < args.N) cp[i] = v[i];
+      }
+    } else {
+      __nv_bfloat16* cp = reinterpret_cast<__nv_bfloat16*>(args.C) + row * args.ldc + col0;
+      if (full) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 u;
+          u.x = pack_bf16x2(v[i], v[i + 1]);
+          u.y = pack_bf16x2(v[i + 2], v[i + 3]);
+          u.z = pack_bf16x2(v[i + 4], v[i + 5]);
+          u.w = pack_bf16x2(v[i + 6], v[i + 7]);
+          *reinterpret_cast<uint4*>(cp + i) = u;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (col0 + i < args.N) cp[i] = __float2bfloat16(v[i]);
+      }
+    }
+  }
+}
+
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -255,95 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const long long row = (long long)mt * BM + row_in_tile;
       const bool row_ok = row < args.M;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        __syncwarp();
-        tmem_ld_32x32b_x32(t_row + c * 32, r);
-        tmem_ld_wait();
-        const int col0 = nt * BN + c * 32;
-        if (!row_ok || col0 >= args.N) continue;
-        float v[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * args.alpha;
-        const bool full = col0 + 32 <= args.N;
-        if (args.D != nullptr && args.beta != 0.f && kb0 == 0) {
-          if (args.d_fp32) {
-            const float* dp = reinterpret_cast<const float*>(args.D) + row * args.ldd + col0;
-            if (full) {
-#pragma unroll
-              for (int i = 0; i < 32; i += 4) {
-                float4 d4 = *reinterpret_cast<const float4*>(dp + i);
-                v[i] += args.beta * d4.x; v[i + 1] += args.beta * d4.y;
-                v[i + 2] += args.beta * d4.z; v[i + 3] += args.beta * d4.w;
-              }
-            } else {
-#pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if (col0 + i < args.N) v[i] += args.beta * dp[i];
-            }
-          } else {
-            const __nv_bfloat16* dp =
-                reinterpret_cast<const __nv_bfloat16*>(args.D) + row * args.ldd + col0;
-            if (full) {
-#pragma unroll
-              for (int i = 0; i < 32; i += 8) {
-                uint4 u = *reinterpret_cast<const uint4*>(dp + i);
-                float2 f0 = unpack_bf16x2(u.x), f1 = unpack_bf16x2(u.y);
-                float2 f2 = unpack_bf16x2(u.z), f3 = unpack_bf16x2(u.w);
-                v[i] += args.beta * f0.x; v[i + 1] += args.beta * f0.y;
-                v[i + 2] += args.beta * f1.x; v[i + 3] += args.beta * f1.y;
-                v[i + 4] += args.beta * f2.x; v[i + 5] += args.beta * f2.y;
-                v[i + 6] += args.beta * f3.x; v[i + 7] += args.beta * f3.y;
-              }
-            } else {
-#pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if (col0 + i < args.N) v[i] += args.beta * __bfloat162float(dp[i]);
-            }
-          }
-        }
-        if (args.c_fp32) {
-          float* cp = reinterpret_cast<float*>(args.C) + row * args.ldc + col0;
-          if (args.splits > 1) {
-            if (full) {
-#pragma unroll
-              for (int i = 0; i < 32; i += 4)
-                atomicAdd(reinterpret_cast<float4*>(cp + i),
-                          make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
-            } else {
-#pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if (col0 + i < args.N) atomicAdd(cp + i, v[i]);
-            }
-          } else if (full) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 4)
-              *reinterpret_cast<float4*>(cp + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (col0 + i < args.N) cp[i] = v[i];
-          }
-        } else {
-          __nv_bfloat16* cp = reinterpret_cast<__nv_bfloat16*>(args.C) + row * args.ldc + col0;
-          if (full) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-              uint4 u;
-              u.x = pack_bf16x2(v[i], v[i + 1]);
-              u.y = pack_bf16x2(v[i + 2], v[i + 3]);
-              u.z = pack_bf16x2(v[i + 4], v[i + 5]);
-              u.w = pack_bf16x2(v[i + 6], v[i + 7]);
-              *reinterpret_cast<uint4*>(cp + i) = u;
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (col0 + i < args.N) cp[i] = __float2bfloat16(v[i]);
-          }
-        }
-      }
+      store_acc_row<BN>(args, t_row, row, row_ok, nt * BN, kb0);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce_bar[buf]);
@@ -354,6 +362,246 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C_::kTmemCols);
+  }
+}
+
+// --------------------------------------------------------------------------
+// Two-SM variant: a cluster of 2 CTAs computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2 (M = 256). CTA rank r loads rows [128r, 128r+128) of
+// the A tile and columns [128r, 128r+128) of the B tile (its own halves, no
+// multicast), so per SM a k-block costs 32 KB of smem fill instead of 48 KB for
+// the same 128 x 256 of output: the L2-to-SM traffic per flop drops by a third.
+// Rank 0 issues the MMAs; stage, accumulator and teardown barriers in both CTAs
+// are signalled by multicast commits; the epilogues of both CTAs report an
+// accumulator drained to rank 0 (8 arrivals). Work units are (256 x 256 tile,
+// k-split) pairs walked by the clusters.
+// --------------------------------------------------------------------------
+struct PairCfg {
+  static constexpr int BN = 256;                 // pair tile N (each CTA loads 128)
+  static constexpr int kStages = 6;
+  static constexpr int kABytes = BM * BK * 2;    // 16 KB: this CTA's 128 rows
+  static constexpr int kBBytes = 128 * BK * 2;   // 16 KB: this CTA's 128 of 256 columns
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BN;       // two 128 x 256 fp32 accumulators per CTA
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+};
+
+template <bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     Args args) {
+  using C_ = PairCfg;
+  constexpr int BN = C_::BN;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* tiles = smem;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C_::kStages * C_::kStageBytes);
+  uint64_t* full_bar = bar;                         // [kStages] (rank 0's are used)
+  uint64_t* empty_bar = bar + C_::kStages;          // [kStages]
+  uint64_t* accf_bar = bar + 2 * C_::kStages;       // [2]
+  uint64_t* acce_bar = bar + 2 * C_::kStages + 2;   // [2] (rank 0's are used)
+  uint64_t* done_bar = bar + 2 * C_::kStages + 4;
+  uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(bar + 2 * C_::kStages + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_smem + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C_::kStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf_bar[b], 1);
+      mbar_init(&acce_bar[b], 8);  // 4 epilogue warps in each CTA of the pair
+    }
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_base_smem, C_::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  // barriers of both CTAs initialised and TMEM allocated before any remote use
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_smem;
+
+  const int total_tiles = args.m_tiles * args.n_tiles;  // 256 x 256 tiles
+  const int total_work = total_tiles * args.splits;
+  const int kb_per_split = (args.k_blocks + args.splits - 1) / args.splits;
+  auto decode = [&](int w, int& mt, int& nt, int& kb0, int& kb1) {
+    const int tile = w / args.splits;
+    const int sp = w - tile * args.splits;
+    if (args.raster_m) {
+      mt = tile % args.m_tiles;
+      nt = tile / args.m_tiles;
+    } else {
+      nt = tile % args.n_tiles;
+      mt = tile / args.n_tiles;
+    }
+    kb0 = sp * kb_per_split;
+    kb1 = min(args.k_blocks, kb0 + kb_per_split);
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      uint32_t armed_mask = 0, parity_mask = 0;
+      for (int w = pair; w < total_work && ok; w += npairs) {
+        int mt, nt, kb0, kb1;
+        decode(w, mt, nt, kb0, kb1);
+        const int m0 = mt * 2 * BM + static_cast<int>(rank) * BM;
+        const int n0 = nt * BN + static_cast<int>(rank) * 128;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, abort_flag)) {
+            record_status(args.status, kTimeoutSmemEmpty);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          uint8_t* sA = tiles + stage * C_::kStageBytes;
+          uint8_t* sB = sA + C_::kABytes;
+          // rank 0's barrier counts the bytes of both CTAs
+          if (leader) {
+            mbar_arrive_expect_tx(&full_bar[stage], 2 * C_::kStageBytes);
+            armed_mask |= 1u << stage;
+            parity_mask = (parity_mask & ~(1u << stage)) | (phase << stage);
+          }
+          const int k0 = kb * BK;
+          if (A_MN) {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j)
+              tma_load_2d_pair(sA + j * (BK * 128), &tmA, &full_bar[stage], m0 + j * 64, k0);
+          } else {
+            tma_load_2d_pair(sA, &tmA, &full_bar[stage], k0, m0);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+              tma_load_2d_pair(sB + j * (BK * 128), &tmB, &full_bar[stage], n0 + j * 64, k0);
+          } else {
+            tma_load_2d_pair(sB, &tmB, &full_bar[stage], k0, n0);
+          }
+          if (++stage == C_::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // unwind: let the copies in flight land before the CTA can exit
+        if (leader) {
+          for (int s = 0; s < C_::kStages; ++s)
+            if (((armed_mask >> s) & 1u) &&
+                !mbar_wait_bounded(&full_bar[s], (parity_mask >> s) & 1u, nullptr))
+              record_status(args.status, kTimeoutDrain);
+        } else {
+          const uint64_t t0 = globaltimer_ns();
+          while (globaltimer_ns() - t0 < 2000000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------------- MMA
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = make_idesc_bf16_f32(2 * BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int w = pair; w < total_work && ok; w += npairs, ++local) {
+        int mt, nt, kb0, kb1;
+        decode(w, mt, nt, kb0, kb1);
+        const int buf = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait_bounded(&acce_bar[buf], acc_phase ^ 1u, abort_flag)) {
+          record_status(args.status, kTimeoutAccEmpty);
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait_bounded(&full_bar[stage], phase, abort_flag)) {
+            record_status(args.status, kTimeoutTmaFull);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sA = smem_u32(tiles + stage * C_::kStageBytes);
+          const uint32_t sB = sA + C_::kABytes;
+          const uint64_t da0 = A_MN ? make_smem_desc(sA, BK * 128, 1024, kLayoutSW128)
+                                    : make_smem_desc(sA, 16, 1024, kLayoutSW128);
+          const uint64_t db0 = B_MN ? make_smem_desc(sB, BK * 128, 1024, kLayoutSW128)
+                                    : make_smem_desc(sB, 16, 1024, kLayoutSW128);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            tc_mma_ss_pair(d_tmem, desc_advance(da0, A_MN ? kk * 2048 : kk * 32),
+                           desc_advance(db0, B_MN ? kk * 2048 : kk * 32), idesc,
+                           (kb > kb0 || kk > 0) ? 1u : 0u);
+          tc_commit_pair(&empty_bar[stage], 0x3);  // frees the stage in both CTAs
+          if (++stage == C_::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair(&accf_bar[buf], 0x3);
+      }
+      if (!ok) *abort_flag = 1;
+      tc_commit_pair(done_bar, 0x3);
+    }
+    // every MMA reading this CTA's smem or writing its TMEM has finished
+    if (lane == 0 && !mbar_wait_bounded(done_bar, 0, nullptr)) record_status(args.status, kTimeoutDrain);
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int row_in_tile = q * 32 + lane;
+    int local = 0;
+    for (int w = pair; w < total_work; w += npairs, ++local) {
+      int mt, nt, kb0, kb1;
+      decode(w, mt, nt, kb0, kb1);
+      const int buf = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait_bounded(&accf_bar[buf], acc_phase, abort_flag)) {
+        record_status(args.status, kTimeoutAccFull);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const long long row = (long long)mt * 2 * BM + rank * BM + row_in_tile;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+      store_acc_row<BN>(args, t_row, row, row < args.M, nt * BN, kb0);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(&acce_bar[buf], 0);
+    }
+  }
+
+  __syncthreads();
+  // the peer must not exit (or free TMEM) while rank 0 may still signal it
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C_::kTmemCols);
   }
 }
 
@@ -386,6 +634,28 @@ static int num_sms() {
   return n;
 }
 
+// Split-K factor for fp32 outputs: the smallest modelled time over s = 1..8 with
+// at least 8 k-blocks per split, where time ~ waves(tiles * s, slots) / s (the
+// last wave is paid in full) times the cost of the extra fp32 reductions of C,
+// relative to the math about 15/k_blocks per split (>= 2%): the reduction moves
+// 4*M*N bytes per split against 2*M*N*K flops.
+static int choose_splits(int tiles, int slots, int k_blocks) {
+  int best = 1;
+  double best_cost = 1e30;
+  const double ovh = k_blocks > 0 ? (15.0 / k_blocks > 0.02 ? 15.0 / k_blocks : 0.02) : 0.02;
+  for (int s = 1; s <= 8; ++s) {
+    if (s > 1 && k_blocks / s < 8) break;
+    const long long units = static_cast<long long>(tiles) * s;
+    const long long waves = (units + slots - 1) / slots;
+    const double cost = static_cast<double>(waves) / s * (1.0 + ovh * (s - 1));
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return best;
+}
+
 template <int BN, bool A_MN, bool B_MN>
 static void launch(const GemmProblem& p, cudaStream_t stream) {
   using C_ = Cfg<BN>;
@@ -406,14 +676,7 @@ static void launch(const GemmProblem& p, cudaStream_t stream) {
   const int sms = num_sms();
   const int tiles = a.m_tiles * a.n_tiles;
   int splits = p.splits;
-  if (splits <= 0) {
-    splits = 1;
-    if (p.c_fp32 && p.allow_split) {
-      // split K until there is about one wave of work, keeping >= 8 k-blocks per split
-      while (tiles * splits * 2 <= sms * 2 && a.k_blocks / (splits * 2) >= 8) splits *= 2;
-      if (tiles * splits < sms && a.k_blocks / (splits * 2) >= 8) splits *= 2;
-    }
-  }
+  if (splits <= 0) splits = (p.c_fp32 && p.allow_split) ? choose_splits(tiles, sms, a.k_blocks) : 1;
   if (splits > a.k_blocks) splits = a.k_blocks;
   if (splits < 1) splits = 1;
   // every split must own at least one k-block
@@ -440,6 +703,70 @@ static void launch(const GemmProblem& p, cudaStream_t stream) {
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 
+template <bool A_MN, bool B_MN>
+static void launch_pair(const GemmProblem& p, cudaStream_t stream) {
+  using C_ = PairCfg;
+  constexpr int BN = C_::BN;
+  // per CTA: A box of 128 rows (or two 64-wide M-major boxes), B box of 128 rows
+  CUtensorMap ta = A_MN ? make_map_2d(p.A, p.K, p.M, p.lda, 64, BK)
+                        : make_map_2d(p.A, p.M, p.K, p.lda, BK, BM);
+  CUtensorMap tb = B_MN ? make_map_2d(p.B, p.K, p.N, p.ldb, 64, BK)
+                        : make_map_2d(p.B, p.N, p.K, p.ldb, BK, 128);
+  Args a;
+  a.M = p.M; a.N = p.N; a.K = p.K;
+  a.C = p.C; a.ldc = p.ldc; a.D = p.D; a.ldd = p.ldd;
+  a.alpha = p.alpha; a.beta = p.beta;
+  a.c_fp32 = p.c_fp32; a.d_fp32 = p.d_fp32;
+  a.m_tiles = (p.M + 2 * BM - 1) / (2 * BM);
+  a.n_tiles = (p.N + BN - 1) / BN;
+  a.k_blocks = (p.K + BK - 1) / BK;
+  a.status = p.status;
+  auto kern = gemm_pair_kernel<A_MN, B_MN>;
+  set_max_smem_once(reinterpret_cast<const void*>(kern), C_::kSmemBytes);
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C_::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // persistent grid: as many SM pairs as can hold a cluster at once
+  static int max_pairs = 0;
+  if (max_pairs == 0) {
+    cfg.gridDim = dim3(2 * (num_sms() / 2), 1, 1);
+    int n = 0;
+    PLG_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+    max_pairs = n > 0 ? n : 1;
+  }
+  const int pairs = max_pairs;
+  const int tiles = a.m_tiles * a.n_tiles;
+  int splits = p.splits;
+  if (splits <= 0) splits = (p.c_fp32 && p.allow_split) ? choose_splits(tiles, pairs, a.k_blocks) : 1;
+  if (splits > a.k_blocks) splits = a.k_blocks;
+  if (splits < 1) splits = 1;
+  while (splits > 1 && (splits - 1) * ((a.k_blocks + splits - 1) / splits) >= a.k_blocks) --splits;
+  a.splits = splits;
+  if (splits > 1) {
+    const bool accumulate_into_c = (p.D == p.C && p.beta == 1.f);
+    if (accumulate_into_c) {
+      a.D = nullptr;
+    } else {
+      if (p.D == p.C) throw std::invalid_argument("gemm: split-K with D == C needs beta == 1");
+      PLG_CUDA_CHECK(cudaMemsetAsync(p.C, 0, sizeof(float) * (size_t)p.ldc * (size_t)(p.M - 1) +
+                                                 sizeof(float) * (size_t)p.N, stream));
+    }
+  }
+  a.raster_m = (static_cast<long long>(p.N) > static_cast<long long>(p.M)) ? 1 : 0;
+  const int work = tiles * splits;
+  const int nclusters = work < pairs ? work : pairs;
+  cfg.gridDim = dim3(2 * nclusters, 1, 1);
+  PLG_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, a));
+}
+
 }  // namespace gemm
 
 void gemm_bf16(const GemmProblem& p, cudaStream_t stream) {
@@ -452,8 +779,19 @@ void gemm_bf16(const GemmProblem& p, cudaStream_t stream) {
   if (reinterpret_cast<uintptr_t>(p.C) & 15) throw std::invalid_argument("gemm: C must be 16-byte aligned");
   if (p.splits > 1 && !p.c_fp32) throw std::invalid_argument("gemm: split-K needs an fp32 output");
   const bool wide = p.N >= 256 && p.bn != 128;
+  // large problems: 256 x 256 tiles on SM pairs (bn == 256 keeps the one-SM kernel)
+  const bool pair = wide && p.bn == 0 && p.M >= 256 && num_sms() >= 2;
 #define PLG_GEMM_CASE(BN_, AM, BMJ) \
   if (p.a_mn_major == AM && p.b_mn_major == BMJ) return launch<BN_, AM, BMJ>(p, stream);
+#define PLG_GEMM_PAIR(AM, BMJ) \
+  if (p.a_mn_major == AM && p.b_mn_major == BMJ) return launch_pair<AM, BMJ>(p, stream);
+  if (pair) {
+    PLG_GEMM_PAIR(false, false)
+    PLG_GEMM_PAIR(false, true)
+    PLG_GEMM_PAIR(true, true)
+    PLG_GEMM_PAIR(true, false)
+  }
+#undef PLG_GEMM_PAIR
   if (wide) {
     PLG_GEMM_CASE(256, false, false)
     PLG_GEMM_CASE(256, false, true)
