@@ -18,8 +18,6 @@ namespace {
 
 constexpr float kLog2e = 1.4426950408889634f;
 
-__device__ __forceinline__ float silu(float x) { return x / (1.f + fast_exp2(-x * kLog2e)); }
-
 // tanh-approximated GELU and its derivative (Hendrycks & Gimpel 2016, eq. for
 // the tanh form): g(x) = 0.5 x (1 + tanh(k0 (x + k1 x^3))), k0 = sqrt(2/pi), k1 = 0.044715
 __device__ __forceinline__ void gelu_tanh(float x, float& y, float& dy) {
@@ -341,7 +339,6 @@ __global__ void multi_sumsq_kernel(const int64_t* __restrict__ table, int ntenso
   }
 }
 
-// deterministic final reduction of the per-chunk partials (one block)
 // out[c] = sum_r part[r, c] for a [R, D] fp32 matrix of per-block partial sums,
 // in a fixed order (deterministic): a block owns 32 columns, its 8 warps sum
 // strided row groups, then the warps' sums are added in shared memory.
@@ -363,6 +360,7 @@ __global__ void __launch_bounds__(256) colsum_kernel(const float* __restrict__ p
   }
 }
 
+// deterministic final reduction of the per-chunk partials (one block)
 __global__ void reduce_partials_kernel(const float* __restrict__ partial, long long n,
                                        float* __restrict__ out) {
   __shared__ double s_red[32];
