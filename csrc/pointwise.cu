@@ -8,10 +8,13 @@
 //   ce_rows      the per-chunk math of pluggy/loss/fused_linear_ce.py:31-58
 //                (lse, target gather, softmax - onehot masked by ignore_index)
 //   adamw/sumsq  torch.optim.AdamW(fused=True) and pluggy/core/grad_helper.py:8-34
+#include <cstdio>
+#include <mutex>
 #include <stdexcept>
 
 #include "common.cuh"
 #include "ops.h"
+#include "plg_noalloc.h"
 
 namespace plg {
 namespace {
@@ -566,6 +569,66 @@ void multi_sumsq(const int64_t* table, int ntensors, long long total_chunks, flo
   reduce_partials_kernel<<<1, 1024, 0, st>>>(out + 1, total_chunks, out);
   PLG_CUDA_CHECK(cudaGetLastError());
 }
+
+}  // namespace plg
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of multi_sumsq (declared in plg_noalloc.h): the
+// per-chunk partials live in a file-scope device array instead of a buffer the
+// caller allocates, for callers that cannot allocate device memory.
+static __device__ __align__(256) float g_noalloc_sumsq_scratch[PLG_NOALLOC_MAX_CHUNKS];
+
+extern "C" __attribute__((visibility("default"))) int plg_multi_sumsq_noalloc(
+    const int64_t* table, int ntensors, long long total_chunks, float* total_out, void* stream) {
+  if (total_chunks < 0 || total_chunks > PLG_NOALLOC_MAX_CHUNKS) {
+    std::fprintf(stderr,
+                 "plg_multi_sumsq_noalloc: total_chunks %lld outside [0, %d] (the scratch holds "
+                 "one partial sum per 65536-element chunk)\n",
+                 total_chunks, PLG_NOALLOC_MAX_CHUNKS);
+    return 1;
+  }
+  // scratch address per device, looked up once (cudaGetSymbolAddress allocates nothing)
+  static std::mutex mu;
+  static float* scratch[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    std::fprintf(stderr, "plg_multi_sumsq_noalloc: cudaGetDevice failed (%s)\n",
+                 cudaGetErrorString(e));
+    return 2;
+  }
+  float* part = nullptr;
+  {
+    std::lock_guard<std::mutex> g(mu);
+    if (scratch[dev] == nullptr) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_noalloc_sumsq_scratch);
+      if (e != cudaSuccess) {
+        std::fprintf(stderr, "plg_multi_sumsq_noalloc: cudaGetSymbolAddress failed (%s)\n",
+                     cudaGetErrorString(e));
+        return 2;
+      }
+      scratch[dev] = static_cast<float*>(p);
+    }
+    part = scratch[dev];
+  }
+  if (total_chunks == 0) {
+    e = cudaMemsetAsync(total_out, 0, sizeof(float), static_cast<cudaStream_t>(stream));
+  } else {
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    plg::multi_sumsq_kernel<<<plg::grid_for(total_chunks, 1), 512, 0, st>>>(table, ntensors,
+                                                                          total_chunks, part);
+    plg::reduce_partials_kernel<<<1, 1024, 0, st>>>(part, total_chunks, total_out);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) {
+    std::fprintf(stderr, "plg_multi_sumsq_noalloc: launch failed (%s)\n", cudaGetErrorString(e));
+    return 2;
+  }
+  return 0;
+}
+
+namespace plg {
 
 void multi_scale(const int64_t* table, int ntensors, long long total_chunks, const float* coef,
                  cudaStream_t st) {
