@@ -35,21 +35,36 @@ def grad_norm_sq(grads: list[torch.Tensor]) -> torch.Tensor:
     return torch.linalg.vector_norm(torch.stack(norms).float(), 2.0) ** 2
 
 
-def clip_grad_norm(params, mesh, max_norm, shard_dims=(), *, fold_into_optimizer: bool = False):
-    grads = _grads(params)
+def _norm_sq(grads: list[torch.Tensor]) -> torch.Tensor:
     if grads[0].is_cuda:
-        sq = grad_norm_sq(grads)
+        return grad_norm_sq(grads)
+    norms = torch._foreach_norm(grads, 2.0)
+    return torch.linalg.vector_norm(torch.stack(norms), 2.0) ** 2
+
+
+def clip_grad_norm(params, mesh, max_norm, shard_dims=(), *, fold_into_optimizer: bool = False,
+                   partial_over=None):
+    """``partial_over=(dims, param_ids)``: those params are further sharded over
+    ``dims`` (tensor parallelism), so their squared norms are summed over ``dims``
+    too, while the params replicated over ``dims`` are counted once."""
+    params = list(params)
+    grads = _grads(params)
+    if partial_over is None:
+        sq = _norm_sq(grads)
         for dim in shard_dims:
             all_reduce(sq, mesh, dim, "sum")
-        total = sq.sqrt()
     else:
-        norms = torch._foreach_norm(grads, 2.0)
-        total = torch.linalg.vector_norm(torch.stack(norms), 2.0)
-        if shard_dims:
-            total = total ** 2
-            for dim in shard_dims:
-                all_reduce(total, mesh, dim, "sum")
-            total = total ** 0.5
+        dims, ids = partial_over
+        part = [p.grad for p in params if p.grad is not None and id(p) in ids]
+        rep = [p.grad for p in params if p.grad is not None and id(p) not in ids]
+        sq = _norm_sq(part) if part else torch.zeros((), device=grads[0].device)
+        for dim in dims:
+            all_reduce(sq, mesh, dim, "sum")
+        if rep:
+            sq = sq + _norm_sq(rep)
+        for dim in shard_dims:
+            all_reduce(sq, mesh, dim, "sum")
+    total = sq.sqrt()
     if max_norm is None:
         return (total, None) if fold_into_optimizer else total
     coef = torch.clamp(max_norm / (total + 1e-6), max=1.0)

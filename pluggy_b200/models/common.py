@@ -23,7 +23,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from pluggy_b200.ops.attention import attention_reference, sdpa_masked
+from pluggy_b200.ops.attention import attention_reference, flash_attention, sdpa_masked
 from pluggy_b200.ops.elementwise import apply_rotary, swiglu_mul
 
 FP32_EPS = torch.finfo(torch.float32).eps
@@ -99,8 +99,12 @@ class GQAttention(nn.Module):
 def attend(Q, K, V, attention_mask=None, window: int = 0, scale=None):
     """[B,H,S,d] attention: causal (+window) fast form, or padded boolean mask."""
     if attention_mask is None:
-        o = attention_reference(Q.transpose(1, 2), K.transpose(1, 2), V.transpose(1, 2),
-                                causal=True, window=window, scale=scale)
+        q, k, v = Q.transpose(1, 2), K.transpose(1, 2), V.transpose(1, 2)
+        if q.is_cuda and q.shape[-1] in (64, 128):
+            o = flash_attention(q.to(torch.bfloat16).contiguous(), k.to(torch.bfloat16).contiguous(),
+                                v.to(torch.bfloat16).contiguous(), True, window, scale).to(Q.dtype)
+        else:
+            o = attention_reference(q, k, v, causal=True, window=window, scale=scale)
         return o.transpose(1, 2)
     S = Q.shape[-2]
     i = torch.arange(S, device=Q.device)

@@ -97,6 +97,7 @@ class Qwen3(nn.Module):
     # ------------------------------------------------------------------ paths
     def _use_fused(self, x, attention_mask, return_hidden_states) -> bool:
         return (x.is_cuda and attention_mask is None and not return_hidden_states
+                and getattr(self, "tp", None) is None
                 and self.token_emb.weight.dtype == torch.float32
                 and self.head_dim in (64, 128) and self.emb_dim % 128 == 0)
 

@@ -35,7 +35,20 @@ class ARObjective:
 
     def compute_loss(self, model: nn.Module, batch: dict[str, torch.Tensor]) -> torch.Tensor:
         core = getattr(model, "module", model)
-        if self.fused_linear_ce:
+        tp = getattr(core, "tp", None)
+        if tp is not None and tp.mesh.size(tp.dim) > 1:
+            # vocabulary-parallel head: full-sequence hidden against the local vocab rows
+            from pluggy_b200.parallel.tensor_parallel import (tp_hidden_for_head,
+                                                              vocab_parallel_cross_entropy)
+
+            assert self.fused_linear_ce, "tensor parallelism needs fused_linear_ce=True"
+            hidden = tp_hidden_for_head(core, model(batch["input_ids"], return_final_hidden=True))
+            labels = shift_labels(batch["labels"], self.ignore_index)
+            loss = vocab_parallel_cross_entropy(hidden.reshape(-1, hidden.shape[-1]),
+                                                core.lm_head.weight, labels.reshape(-1), tp.vstart,
+                                                tp.mesh, tp.dim, self.ignore_index,
+                                                self.ce_chunk_size)
+        elif self.fused_linear_ce:
             hidden = model(batch["input_ids"], return_final_hidden=True)
             labels = shift_labels(batch["labels"], self.ignore_index)
             lowp_fn = getattr(core, "lm_head_lowp", None)

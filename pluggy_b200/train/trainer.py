@@ -149,11 +149,12 @@ class Trainer:
     def _parallelize(self, model: nn.Module) -> nn.Module:
         self.parallelism = self.config.get("parallelism", "ddp")
         sizes = self.config["mesh"]
+        self.tp = None
         if sizes.get("tp", 1) > 1:
             from pluggy_b200.parallel.tensor_parallel import parallelize_tp
 
-            parallelize_tp(model, self.mesh, "tp", sequence_parallel=self.config.get("tp", {}).get(
-                "sequence_parallel", True))
+            self.tp = parallelize_tp(model, self.mesh, "tp", sequence_parallel=self.config.get(
+                "tp", {}).get("sequence_parallel", True))
         if sizes.get("ep", 1) > 1:
             from pluggy_b200.parallel.expert_parallel import parallelize_ep
 
@@ -302,15 +303,19 @@ class Trainer:
 
     def optimizer_step(self) -> torch.Tensor:
         """sync -> clip -> step -> zero_grad -> scheduler; returns the grad norm."""
+        if self.tp is not None:
+            self.tp.sync_replicated_grads()
         self.dp.sync()
         fused = self.device.type == "cuda" and hasattr(self.optimizer, "set_grad_scale")
+        partial = (("tp",), self.tp.sharded_param_ids()) if self.tp is not None else None
         if fused:
             gnorm, coef = clip_grad_norm(self.model.parameters(), self.mesh, self.max_norm,
-                                         shard_dims=self.grad_shard_dims, fold_into_optimizer=True)
+                                         shard_dims=self.grad_shard_dims, fold_into_optimizer=True,
+                                         partial_over=partial)
             self.optimizer.set_grad_scale(coef)
         else:
             gnorm = clip_grad_norm(self.model.parameters(), self.mesh, self.max_norm,
-                                   shard_dims=self.grad_shard_dims)
+                                   shard_dims=self.grad_shard_dims, partial_over=partial)
         self.optimizer.step()
         self.optimizer.zero_grad()
         self.scheduler.step()
