@@ -44,26 +44,30 @@ def _norm_sq(grads: list[torch.Tensor]) -> torch.Tensor:
 
 def clip_grad_norm(params, mesh, max_norm, shard_dims=(), *, fold_into_optimizer: bool = False,
                    partial_over=None):
-    """``partial_over=(dims, param_ids)``: those params are further sharded over
-    ``dims`` (tensor parallelism), so their squared norms are summed over ``dims``
-    too, while the params replicated over ``dims`` are counted once."""
+    """``partial_over``: a list of ``(dims, param_ids)`` (or one such pair). Those
+    params are further sharded over ``dims`` (tensor or expert parallelism), so
+    their squared norms are summed over ``dims`` too; params in no group are
+    replicated and counted once. The groups must be disjoint."""
     params = list(params)
     grads = _grads(params)
     if partial_over is None:
         sq = _norm_sq(grads)
-        for dim in shard_dims:
-            all_reduce(sq, mesh, dim, "sum")
     else:
-        dims, ids = partial_over
-        part = [p.grad for p in params if p.grad is not None and id(p) in ids]
-        rep = [p.grad for p in params if p.grad is not None and id(p) not in ids]
-        sq = _norm_sq(part) if part else torch.zeros((), device=grads[0].device)
-        for dim in dims:
-            all_reduce(sq, mesh, dim, "sum")
+        groups = [partial_over] if isinstance(partial_over, tuple) else list(partial_over)
+        claimed: set[int] = set()
+        sq = torch.zeros((), device=grads[0].device)
+        for dims, ids in groups:
+            part = [p.grad for p in params if p.grad is not None and id(p) in ids]
+            claimed |= set(ids)
+            gsq = _norm_sq(part) if part else torch.zeros((), device=grads[0].device)
+            for dim in dims:
+                all_reduce(gsq, mesh, dim, "sum")
+            sq = sq + gsq
+        rep = [p.grad for p in params if p.grad is not None and id(p) not in claimed]
         if rep:
             sq = sq + _norm_sq(rep)
-        for dim in shard_dims:
-            all_reduce(sq, mesh, dim, "sum")
+    for dim in shard_dims:
+        all_reduce(sq, mesh, dim, "sum")
     total = sq.sqrt()
     if max_norm is None:
         return (total, None) if fold_into_optimizer else total

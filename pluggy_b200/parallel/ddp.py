@@ -63,9 +63,13 @@ class DDP:
         self._fused = None
         if self.group_size == 1:
             return
+        # expert shards (expert parallelism over this axis) differ per rank by design:
+        # they are neither broadcast nor averaged here
         for t in [*model.parameters(), *model.buffers()]:
-            broadcast(t.detach(), mesh, dim, src=0)
-        params = [p for p in model.parameters() if p.requires_grad]
+            if not getattr(t, "_plg_expert_sharded", False):
+                broadcast(t.detach(), mesh, dim, src=0)
+        params = [p for p in model.parameters()
+                  if p.requires_grad and not getattr(p, "_plg_expert_sharded", False)]
         params.reverse()
         self._buckets = self._build_buckets(params, int(bucket_mb * 1024 * 1024))
         self._bucket_of = {p: b for b in self._buckets for p in b.params}

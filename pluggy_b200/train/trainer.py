@@ -155,10 +155,16 @@ class Trainer:
 
             self.tp = parallelize_tp(model, self.mesh, "tp", sequence_parallel=self.config.get(
                 "tp", {}).get("sequence_parallel", True))
-        if sizes.get("ep", 1) > 1:
+        # expert parallelism: "ep": {"dim": axis} splits the experts over that mesh
+        # axis (normally the dp axis itself: EP = DP)
+        self.ep = None
+        ep_cfg = self.config.get("ep")
+        if ep_cfg:
             from pluggy_b200.parallel.expert_parallel import parallelize_ep
 
-            parallelize_ep(model, self.mesh, "ep")
+            self.ep_dim = ep_cfg.get("dim", "dp") if isinstance(ep_cfg, dict) else "dp"
+            if self.mesh.size(self.ep_dim) > 1:
+                self.ep = parallelize_ep(model, self.mesh, self.ep_dim)
         if self.parallelism == "ddp":
             from pluggy_b200.parallel.ddp import DDP
 
@@ -213,13 +219,51 @@ class Trainer:
 
     # -------------------------------------------------------------- checkpoint
     @debug_time
+    def _model_sharded(self) -> bool:
+        """Tensor or expert parallelism: ranks hold different parameter shards."""
+        return getattr(self, "tp", None) is not None or getattr(self, "ep", None) is not None
+
+    def _full_model_state(self) -> dict[str, torch.Tensor]:
+        """The unsharded model state (collective when TP/EP shard the params)."""
+        sd = {k: v for k, v in self.model.state_dict().items()}
+        for handle in (getattr(self, "tp", None), getattr(self, "ep", None)):
+            if handle is not None:
+                full = handle.full_state_dict()
+                sd.update({k: full[k] for k in sd if full[k].shape != sd[k].shape})
+        return sd
+
+    def _load_full_model_state(self, sd: dict[str, torch.Tensor]) -> None:
+        local = {}
+        for name, t in self.model.state_dict().items():
+            full = sd[name]
+            mod_name = name.rpartition(".")[0]
+            mod = self.model.get_submodule(mod_name) if mod_name else self.model
+            if full.shape != t.shape:
+                first = getattr(mod, "first", None)
+                if first is not None:  # expert shard
+                    full = full[first:first + t.shape[0]]
+                else:  # tensor-parallel shard along the dimension that shrank
+                    d = 0 if full.shape[0] != t.shape[0] else 1
+                    r = self.mesh.coordinate("tp")
+                    k = t.shape[d]
+                    full = full.narrow(d, r * k, k)
+            local[name] = full
+        self.model.load_state_dict(local)
+
     def checkpoint(self, step: int) -> None:
         if self.parallelism == "fsdp2" and self.dp_size > 1:
             self._checkpoint_sharded(step)
+        elif self._model_sharded():
+            sd = self._full_model_state()
+            if self.rank == 0:
+                torch.save(sd, self.checkpointer._path(step, "model.pt", create=True))
+            torch.save(self.optimizer.state_dict(),
+                       os.path.join(self.checkpointer._step_dir(step, True),
+                                    f"optimizer_rank{self.rank}.pt"))
         elif self.rank == 0:
             self.checkpointer.save_model(self.model, step)
         if self.rank == 0:
-            if not (self.parallelism == "fsdp2" and self.dp_size > 1):
+            if not (self.parallelism == "fsdp2" and self.dp_size > 1) and not self._model_sharded():
                 self.checkpointer.save_optimizer(self.optimizer, step)
             self.checkpointer.save_scheduler(self.scheduler, step)
             self.checkpointer.save_trainer({"step": step, "config": self.config,
@@ -273,6 +317,9 @@ class Trainer:
             shard = self.checkpointer._load(step, f"model_shard_rank{self.rank}.pt")
             self.model.load_state_dict(shard)
             self.optimizer.load_state_dict(self.checkpointer._load(step, f"optimizer_rank{self.rank}.pt"))
+        elif self._model_sharded():
+            self._load_full_model_state(self.checkpointer._load(step, "model.pt"))
+            self.optimizer.load_state_dict(self.checkpointer._load(step, f"optimizer_rank{self.rank}.pt"))
         else:
             self.checkpointer.load_model(self.model, step)
             self.checkpointer.load_optimizer(self.optimizer, step)
@@ -306,8 +353,17 @@ class Trainer:
         if self.tp is not None:
             self.tp.sync_replicated_grads()
         self.dp.sync()
+        partial = []
+        if self.ep is not None:
+            self.ep.finish_grads(average_over_dim=self.ep_dim == "dp")
+            partial.append(((self.ep_dim,), self.ep.expert_param_ids()))
+        if self.tp is not None:
+            ids = self.tp.sharded_param_ids()
+            if self.ep is not None:
+                ids = ids - self.ep.expert_param_ids()
+            partial.append((("tp",), ids))
+        partial = partial or None
         fused = self.device.type == "cuda" and hasattr(self.optimizer, "set_grad_scale")
-        partial = (("tp",), self.tp.sharded_param_ids()) if self.tp is not None else None
         if fused:
             gnorm, coef = clip_grad_norm(self.model.parameters(), self.mesh, self.max_norm,
                                          shard_dims=self.grad_shard_dims, fold_into_optimizer=True,
