@@ -91,7 +91,16 @@ class GQAttention(nn.Module):
         if self.qk_norm:
             Q, K = self.q_norm(Q), self.k_norm(K)
         Q, K = apply_rotary(Q, cos, sin), apply_rotary(K, cos, sin)
-        o = attend(Q, K, V, attention_mask, window)
+        cp = getattr(self, "cp", None)
+        if cp is not None and cp.mesh.size(cp.dim) > 1:
+            # context parallel: this rank's zigzag tokens, keys/values around the ring
+            from pluggy_b200.parallel.context_parallel import ring_attention
+
+            assert attention_mask is None and not window, "context parallelism is causal-only"
+            o = ring_attention(Q.transpose(1, 2), K.transpose(1, 2), V.transpose(1, 2), cp.mesh,
+                               cp.dim).transpose(1, 2)
+        else:
+            o = attend(Q, K, V, attention_mask, window)
         B, _, S, _ = o.shape
         return self.o_proj(o.transpose(1, 2).reshape(B, S, -1))
 

@@ -97,7 +97,7 @@ class Qwen3(nn.Module):
     # ------------------------------------------------------------------ paths
     def _use_fused(self, x, attention_mask, return_hidden_states) -> bool:
         return (x.is_cuda and attention_mask is None and not return_hidden_states
-                and getattr(self, "tp", None) is None
+                and getattr(self, "tp", None) is None and getattr(self, "cp", None) is None
                 and self.token_emb.weight.dtype == torch.float32
                 and self.head_dim in (64, 128) and self.emb_dim % 128 == 0)
 
@@ -119,13 +119,17 @@ class Qwen3(nn.Module):
         return out.view(B, S, -1)
 
     def forward(self, x, attention_mask=None, return_hidden_states: bool = False,
-                return_final_hidden: bool = False):
-        if self._use_fused(x, attention_mask, return_hidden_states):
+                return_final_hidden: bool = False, position_ids=None):
+        """``position_ids`` (optional [B, S]) overrides the packed arange positions
+        (context parallelism feeds each rank's zigzag positions)."""
+        if position_ids is None and self._use_fused(x, attention_mask, return_hidden_states):
             hidden = self.fused_hidden(x)
             if return_final_hidden:
                 return hidden
             return linear(hidden, self.lm_head.weight, self.weight_cache.get(self.lm_head.weight))
         pos, cacheable, am = position_ids_for(x, attention_mask)
+        if position_ids is not None:
+            pos, cacheable = position_ids, False
         h = self.token_emb(x)
         cos, sin = self.rope(pos, cacheable=cacheable)
         hs = [h] if return_hidden_states else []

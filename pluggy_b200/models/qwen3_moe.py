@@ -197,13 +197,15 @@ class Qwen3Moe(nn.Module):
         return loss
 
     def forward(self, x, attention_mask=None, return_hidden_states: bool = False,
-                return_final_hidden: bool = False):
+                return_final_hidden: bool = False, position_ids=None):
         for b in self.blocks:
             if isinstance(b.ffn, Qwen3MoeSparseMLP):
                 b.ffn.last_router_logits = None
         self._router_logits = []
         B, S = x.shape
         fused = (x.is_cuda and attention_mask is None and not return_hidden_states
+                 and position_ids is None and getattr(self, "tp", None) is None
+                 and getattr(self, "cp", None) is None
                  and self.head_dim in (64, 128) and self.emb_dim % 128 == 0)
         if fused:
             h = _engine.Embedding.apply(x, self.token_emb.weight, 1.0)
@@ -219,6 +221,8 @@ class Qwen3Moe(nn.Module):
                 return hidden
             return linear(hidden, self.lm_head.weight, self.weight_cache.get(self.lm_head.weight))
         pos, cacheable, am = position_ids_for(x, attention_mask)
+        if position_ids is not None:
+            pos, cacheable = position_ids, False
         h = self.token_emb(x)
         cos, sin = self.rope(pos, cacheable=cacheable)
         hs = [h] if return_hidden_states else []

@@ -36,7 +36,21 @@ class ARObjective:
     def compute_loss(self, model: nn.Module, batch: dict[str, torch.Tensor]) -> torch.Tensor:
         core = getattr(model, "module", model)
         tp = getattr(core, "tp", None)
-        if tp is not None and tp.mesh.size(tp.dim) > 1:
+        cp = getattr(core, "cp", None)
+        if cp is not None and cp.mesh.size(cp.dim) > 1:
+            # context parallel: labels shifted on the full sequence, then each rank
+            # keeps its zigzag tokens; the loss is this rank's share of the global mean
+            from pluggy_b200.core.collective import all_reduce
+
+            assert self.fused_linear_ce, "context parallelism needs fused_linear_ce=True"
+            labels = shift_labels(batch["labels"], self.ignore_index)
+            ids, labels, pos = cp.shard_batch(batch["input_ids"], labels)
+            hidden = model(ids, return_final_hidden=True, position_ids=pos)
+            n_local = (labels != self.ignore_index).sum().float()
+            n_all = all_reduce(n_local.clone(), cp.mesh, cp.dim, "sum")
+            loss = fused_linear_cross_entropy(hidden, core.lm_head.weight, labels, self.ignore_index,
+                                              self.ce_chunk_size) * (n_local / n_all.clamp(min=1))
+        elif tp is not None and tp.mesh.size(tp.dim) > 1:
             # vocabulary-parallel head: full-sequence hidden against the local vocab rows
             from pluggy_b200.parallel.tensor_parallel import (tp_hidden_for_head,
                                                               vocab_parallel_cross_entropy)

@@ -155,6 +155,11 @@ class Trainer:
 
             self.tp = parallelize_tp(model, self.mesh, "tp", sequence_parallel=self.config.get(
                 "tp", {}).get("sequence_parallel", True))
+        self.cp = None
+        if sizes.get("cp", 1) > 1:
+            from pluggy_b200.parallel.context_parallel import parallelize_cp
+
+            self.cp = parallelize_cp(model, self.mesh, "cp")
         # expert parallelism: "ep": {"dim": axis} splits the experts over that mesh
         # axis (normally the dp axis itself: EP = DP)
         self.ep = None
@@ -353,6 +358,8 @@ class Trainer:
         if self.tp is not None:
             self.tp.sync_replicated_grads()
         self.dp.sync()
+        if self.cp is not None:
+            self.cp.sync_grads()
         partial = []
         if self.ep is not None:
             self.ep.finish_grads(average_over_dim=self.ep_dim == "dp")
