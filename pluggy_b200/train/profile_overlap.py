@@ -1,0 +1,140 @@
+"""Communication/compute overlap profiler.
+
+Parity: reference ``pluggy/train/profile_overlap.py:63-206``: after warm-up steps,
+a ``torch.profiler`` chrome trace of a few training steps is captured; the GPU
+kernels are split into communication (NCCL kernels, and this framework's fused
+collective kernels) and compute; each set is merged into a union of intervals,
+and the report gives hidden communication (intersection with compute), exposed
+communication (communication minus hidden), per-kernel exposure and per-stream
+busy time.
+
+``python -m pluggy_b200.train.profile_overlap --config X [--warmup 3] [--steps 2]
+[--out trace.json]`` profiles a run (one process per GPU, like the trainer);
+``analyze(trace_path)`` works on any saved chrome trace.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+from collections import defaultdict
+
+# kernel-name fragments that mark communication: NCCL's kernels and the fused
+# collective kernels of this package (pluggy_b200.comm)
+COMM_MARKERS = ("nccl", "plg_comm", "fused_allreduce", "allreduce_kernel", "reduce_scatter_kernel",
+                "all_gather_kernel")
+
+
+def union(intervals: list[tuple[float, float]]) -> list[tuple[float, float]]:
+    out: list[list[float]] = []
+    for s, e in sorted(intervals):
+        if out and s <= out[-1][1]:
+            out[-1][1] = max(out[-1][1], e)
+        else:
+            out.append([s, e])
+    return [(s, e) for s, e in out]
+
+
+def total(intervals) -> float:
+    return sum(e - s for s, e in intervals)
+
+
+def intersect_len(a: list[tuple[float, float]], b: list[tuple[float, float]]) -> float:
+    """Length of the intersection of two unions of disjoint sorted intervals."""
+    i = j = 0
+    acc = 0.0
+    while i < len(a) and j < len(b):
+        s = max(a[i][0], b[j][0])
+        e = min(a[i][1], b[j][1])
+        if e > s:
+            acc += e - s
+        if a[i][1] < b[j][1]:
+            i += 1
+        else:
+            j += 1
+    return acc
+
+
+def is_comm(name: str) -> bool:
+    n = name.lower()
+    return any(m in n for m in COMM_MARKERS)
+
+
+def analyze(trace_path: str) -> dict:
+    with open(trace_path) as f:
+        tr = json.load(f)
+    events = tr["traceEvents"] if isinstance(tr, dict) else tr
+    kernels = [e for e in events if e.get("ph") == "X" and e.get("cat") in ("kernel", "gpu_memcpy")
+               and "dur" in e]
+    comm, comp = [], []
+    per_stream = defaultdict(float)
+    per_kernel = defaultdict(lambda: [0.0, 0])
+    for e in kernels:
+        iv = (float(e["ts"]), float(e["ts"]) + float(e["dur"]))
+        (comm if is_comm(e["name"]) else comp).append((iv, e["name"]))
+        per_stream[str(e.get("tid"))] += float(e["dur"])
+    cu = union([iv for iv, _ in comm])
+    pu = union([iv for iv, _ in comp])
+    hidden = intersect_len(cu, pu)
+    exposed = total(cu) - hidden
+    for iv, name in comm:
+        ex = (iv[1] - iv[0]) - intersect_len([iv], pu)
+        per_kernel[name[:80]][0] += ex
+        per_kernel[name[:80]][1] += 1
+    return {
+        "comm_us": total(cu), "compute_us": total(pu), "hidden_us": hidden, "exposed_us": exposed,
+        "hidden_frac": hidden / total(cu) if cu else 1.0,
+        "per_kernel_exposed_us": {k: v[0] for k, v in sorted(per_kernel.items(), key=lambda kv: -kv[1][0])},
+        "per_stream_busy_us": dict(per_stream),
+    }
+
+
+def capture(config, warmup: int, steps: int, out: str, rank: int, local_rank: int,
+            world: int) -> str:
+    """Profile ``steps`` training steps after ``warmup`` (``config``: dict or JSON path)."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    from pluggy_b200.train.trainer import Trainer
+
+    tr = Trainer(config, rank=rank, local_rank=local_rank, world_size=world, benchmark=True)
+    for _ in range(warmup):
+        tr.train_step()
+    acts = [ProfilerActivity.CPU] + ([ProfilerActivity.CUDA] if torch.cuda.is_available() else [])
+    with profile(activities=acts) as prof:
+        for _ in range(steps):
+            tr.train_step()
+        if torch.cuda.is_available():
+            torch.cuda.synchronize()
+    path = out if world == 1 else f"{os.path.splitext(out)[0]}_rank{rank}.json"
+    prof.export_chrome_trace(path)
+    return path
+
+
+def main(argv=None) -> None:
+    import torch.distributed as dist
+
+    from pluggy_b200.train.train import init_distributed
+
+    p = argparse.ArgumentParser()
+    p.add_argument("--config", required=True)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--steps", type=int, default=2)
+    p.add_argument("--out", default="overlap_trace.json")
+    a = p.parse_args(argv)
+    rank, local_rank, world = init_distributed()
+    try:
+        path = capture(a.config, a.warmup, a.steps, a.out, rank, local_rank, world)
+        rep = analyze(path)
+        if rank == 0:
+            print(json.dumps({k: v for k, v in rep.items() if k != "per_kernel_exposed_us"}, indent=1))
+            for k, v in list(rep["per_kernel_exposed_us"].items())[:10]:
+                print(f"  exposed {v:10.1f} us  {k}")
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
