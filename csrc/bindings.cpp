@@ -350,8 +350,58 @@ void colsum(const at::Tensor& part, at::Tensor& out) {
               out.data_ptr<float>(), cur_stream());
 }
 
-}  // namespace
+// ------------------------------------------------------------ symmetric memory
+std::tuple<int64_t, at::Tensor> symm_malloc_b(int64_t bytes) {
+  at::Tensor h = at::empty({64}, at::TensorOptions().dtype(at::kByte));
+  void* p = plg::symm_malloc(static_cast<size_t>(bytes), h.data_ptr());
+  return {reinterpret_cast<int64_t>(p), h};
+}
 
+int64_t symm_open_b(const at::Tensor& handle) {
+  TORCH_CHECK(handle.numel() == 64 && handle.dtype() == at::kByte && !handle.is_cuda(),
+              "symm_open: 64-byte CPU handle");
+  return reinterpret_cast<int64_t>(plg::symm_open(handle.contiguous().data_ptr()));
+}
+
+void symm_close_b(int64_t p) { plg::symm_close(reinterpret_cast<void*>(p)); }
+void symm_free_b(int64_t p) { plg::symm_free(reinterpret_cast<void*>(p)); }
+
+// a tensor over device memory this module owns (no deleter: the owner frees it)
+at::Tensor tensor_from_ptr(int64_t ptr, std::vector<int64_t> shape, at::ScalarType dtype,
+                           int64_t device) {
+  auto opts = at::TensorOptions().dtype(dtype).device(at::kCUDA, static_cast<int>(device));
+  return at::from_blob(reinterpret_cast<void*>(ptr), shape, [](void*) {}, opts);
+}
+
+void symm_allreduce_avg_b(std::vector<int64_t> data, std::vector<int64_t> flags,
+                          std::vector<int64_t> sumsq, int64_t offset, int64_t numel, int64_t rank,
+                          int64_t epoch, int64_t chunks, const c10::optional<at::Tensor>& norm_sq,
+                          bool accumulate, const c10::optional<at::Tensor>& status) {
+  const int n = static_cast<int>(data.size());
+  TORCH_CHECK(n >= 1 && n <= plg::kSymmMaxRanks && flags.size() == data.size() &&
+                  sumsq.size() == data.size(), "symm_allreduce_avg: one pointer per rank");
+  plg::SymmAllReduceArgs a{};
+  for (int i = 0; i < n; ++i) {
+    a.data[i] = reinterpret_cast<float*>(data[i]);
+    a.flags[i] = reinterpret_cast<uint32_t*>(flags[i]);
+    a.sumsq[i] = reinterpret_cast<float*>(sumsq[i]);
+  }
+  a.offset = offset;
+  a.numel = numel;
+  a.rank = static_cast<int>(rank);
+  a.nranks = n;
+  a.chunks = static_cast<int>(chunks);
+  a.epoch = static_cast<uint32_t>(epoch);
+  a.status = status.has_value() ? status->data_ptr<int>() : nullptr;
+  float* ns = nullptr;
+  if (norm_sq.has_value()) {
+    TORCH_CHECK(is_f32(*norm_sq) && norm_sq->is_cuda(), "norm_sq: fp32 device tensor");
+    ns = norm_sq->data_ptr<float>();
+  }
+  plg::symm_allreduce_avg(a, ns, accumulate, cur_stream());
+}
+
+}  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "pluggy_b200 sm_100a kernels";
@@ -364,6 +414,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("glu_bwd", &glu_bwd);
   m.def("cast_f32_bf16", &cast_f32_bf16);
   m.def("colsum", &colsum);
+  m.def("symm_malloc", &symm_malloc_b);
+  m.def("symm_open", &symm_open_b);
+  m.def("symm_close", &symm_close_b);
+  m.def("symm_free", &symm_free_b);
+  m.def("tensor_from_ptr", &tensor_from_ptr);
+  m.def("symm_allreduce_avg", &symm_allreduce_avg_b);
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd", &embedding_bwd);
   m.def("softcap", &softcap);

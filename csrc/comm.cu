@@ -1,0 +1,198 @@
+// Collectives as sm_100a kernels over NVLink peer memory.
+//
+// Symmetric memory: every rank allocates the same-size buffer with cudaMalloc and
+// exports a CUDA IPC handle; the Python side exchanges the handles over the
+// process group and opens the peers' buffers here, so a kernel can load and store
+// any rank's buffer directly (NVLink 5 / NVSwitch P2P).
+//
+// Fused data-parallel gradient reduction (replaces the reference's
+// all_reduce(op="avg") of each DDP bucket, pluggy/parallelism/data_parallel.py:120-130,
+// plus the grad-norm pass of pluggy/core/grad_helper.py:17-33): the bucket lives in
+// the symmetric buffer; the range is split into n segments (one per owning rank)
+// of C chunks (one per CTA). CTA c of rank r
+//   1. tells every peer its copy of the bucket is ready (flag store, release, system scope),
+//      then waits (bounded) until every peer's CTA c said the same;
+//   2. sums chunk c of segment r over all ranks' copies (P2P loads), scales by
+//      1/n, accumulates the sum of squares of the result;
+//   3. stores the averaged chunk into every rank's copy (P2P stores) and its
+//      sum of squares into every rank's slot table, then signals "done";
+//   4. waits (bounded) for every peer's "done" of chunk c, i.e. until chunk c of
+//      every segment has been written into this rank's copy.
+// A CTA only ever waits for the CTA of the same index on other GPUs, and signals
+// before it waits, so no scheduling order can deadlock. Flags hold a monotonically
+// increasing epoch (no reset between launches). A wait that runs out of time
+// records a status code and returns.
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <stdexcept>
+#include <string>
+
+#include "common.cuh"
+#include "ops.h"
+
+namespace plg {
+namespace comm {
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// wait until *p >= want (flags only grow); false after the deadline
+__device__ __forceinline__ bool wait_flag(const uint32_t* p, uint32_t want) {
+  if (static_cast<int32_t>(ld_acquire_sys(p) - want) >= 0) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (static_cast<int32_t>(ld_acquire_sys(p) - want) >= 0) return true;
+    if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > kWaitDeadlineNs) return false;
+  }
+}
+
+__global__ void __launch_bounds__(512) allreduce_avg_kernel(SymmAllReduceArgs a) {
+  const int c = blockIdx.x, n = a.nranks, me = a.rank;
+  const uint32_t e_ready = 2u * a.epoch + 1u, e_done = 2u * a.epoch + 2u;
+  __shared__ int s_ok;
+  // 1. ready handshake with CTA c of every peer
+  if (threadIdx.x < n) {
+    const int p = threadIdx.x;
+    st_release_sys(a.flags[p] + (0 * kSymmMaxRanks + me) * kSymmMaxChunks + c, e_ready);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    for (int p = 0; p < n && ok; ++p)
+      ok = wait_flag(a.flags[me] + (0 * kSymmMaxRanks + p) * kSymmMaxChunks + c, e_ready);
+    if (!ok) record_status(a.status, kTimeoutPeerFlag);
+    s_ok = ok;
+  }
+  __syncthreads();
+  float ss = 0.f;
+  if (s_ok) {
+    // 2./3. reduce chunk c of my segment over all copies; write it back everywhere
+    const long long seg = (a.numel + n - 1) / n;
+    const long long s0 = me * seg, s1 = min(a.numel, s0 + seg);
+    const long long per = ((s1 - s0 + a.chunks - 1) / a.chunks + 3) & ~3LL;  // multiple of 4
+    const long long c0 = s0 + c * per, c1 = min(s1, c0 + per);
+    const float inv = 1.f / n;
+    const long long v0 = (c0 + 3) & ~3LL;  // float4-aligned interior (buffers are 16B aligned)
+    const long long v1 = max(v0, c1 & ~3LL);
+    for (long long i = c0 + threadIdx.x; i < min(v0, c1); i += blockDim.x) {
+      float acc = 0.f;
+      for (int p = 0; p < n; ++p) acc += a.data[p][a.offset + i];
+      acc *= inv;
+      ss += acc * acc;
+      for (int p = 0; p < n; ++p) a.data[p][a.offset + i] = acc;
+    }
+    for (long long i = v0 + 4LL * threadIdx.x; i < v1; i += 4LL * blockDim.x) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+      for (int p = 0; p < n; ++p) {
+        const float4 x = *reinterpret_cast<const float4*>(a.data[p] + a.offset + i);
+        acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+      }
+      acc.x *= inv; acc.y *= inv; acc.z *= inv; acc.w *= inv;
+      ss += acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w;
+#pragma unroll 8
+      for (int p = 0; p < n; ++p) *reinterpret_cast<float4*>(a.data[p] + a.offset + i) = acc;
+    }
+    for (long long i = v1 + threadIdx.x; i < c1; i += blockDim.x) {
+      float acc = 0.f;
+      for (int p = 0; p < n; ++p) acc += a.data[p][a.offset + i];
+      acc *= inv;
+      ss += acc * acc;
+      for (int p = 0; p < n; ++p) a.data[p][a.offset + i] = acc;
+    }
+  }
+  // chunk sum of squares into every rank's slot table
+  ss = warp_sum(ss);
+  __shared__ float s_red[16];
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += s_red[w];
+    for (int p = 0; p < n; ++p) a.sumsq[p][me * kSymmMaxChunks + c] = t;
+  }
+  __syncthreads();
+  // 3. done: my chunk c of segment `me` is in every copy
+  if (threadIdx.x == 0) __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < n) {
+    const int p = threadIdx.x;
+    st_release_sys(a.flags[p] + (1 * kSymmMaxRanks + me) * kSymmMaxChunks + c, e_done);
+  }
+  // 4. chunk c of every segment has arrived here
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    for (int p = 0; p < n && ok; ++p)
+      ok = wait_flag(a.flags[me] + (1 * kSymmMaxRanks + p) * kSymmMaxChunks + c, e_done);
+    if (!ok) record_status(a.status, kTimeoutPeerFlag);
+  }
+}
+
+// total = sum of the [nranks][chunks] slot table (fixed order: deterministic)
+__global__ void sumsq_total_kernel(const float* __restrict__ slots, int nranks, int chunks,
+                                   float* __restrict__ out, int accumulate) {
+  __shared__ double s[32];
+  double acc = 0.0;
+  for (int i = threadIdx.x; i < nranks * chunks; i += blockDim.x)
+    acc += slots[(i / chunks) * kSymmMaxChunks + (i % chunks)];
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) s[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += s[w];
+    out[0] = (accumulate ? out[0] : 0.f) + static_cast<float>(t);
+  }
+}
+
+}  // namespace comm
+
+void* symm_malloc(size_t bytes, void* ipc_handle_out) {
+  void* p = nullptr;
+  PLG_CUDA_CHECK(cudaMalloc(&p, bytes));
+  PLG_CUDA_CHECK(cudaMemset(p, 0, bytes));
+  cudaIpcMemHandle_t h;
+  PLG_CUDA_CHECK(cudaIpcGetMemHandle(&h, p));
+  std::memcpy(ipc_handle_out, &h, sizeof(h));
+  return p;
+}
+
+void* symm_open(const void* ipc_handle) {
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  void* p = nullptr;
+  PLG_CUDA_CHECK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  return p;
+}
+
+void symm_close(void* peer_ptr) { PLG_CUDA_CHECK(cudaIpcCloseMemHandle(peer_ptr)); }
+
+void symm_free(void* p) { PLG_CUDA_CHECK(cudaFree(p)); }
+
+void symm_allreduce_avg(const SymmAllReduceArgs& a, float* norm_sq, bool accumulate_norm,
+                        cudaStream_t st) {
+  if (a.nranks < 1 || a.nranks > kSymmMaxRanks)
+    throw std::invalid_argument("symm_allreduce_avg: 1..8 ranks");
+  if (a.chunks < 1 || a.chunks > kSymmMaxChunks)
+    throw std::invalid_argument("symm_allreduce_avg: chunks must be in 1..kSymmMaxChunks");
+  if (a.offset % 4) throw std::invalid_argument("symm_allreduce_avg: offset must be a multiple of 4");
+  if (a.numel > 0) {
+    comm::allreduce_avg_kernel<<<a.chunks, 512, 0, st>>>(a);
+    PLG_CUDA_CHECK(cudaGetLastError());
+  }
+  if (norm_sq != nullptr) {
+    comm::sumsq_total_kernel<<<1, 256, 0, st>>>(a.sumsq[a.rank], a.nranks, a.chunks, norm_sq,
+                                                accumulate_norm ? 1 : 0);
+    PLG_CUDA_CHECK(cudaGetLastError());
+  }
+}
+
+}  // namespace plg

@@ -136,4 +136,28 @@ inline long long attn_bwd_stats_floats(int B, int Hq, int S) {
 }
 void attn_bwd(const AttnBwdArgs& a, cudaStream_t stream);
 
+// ---------------------------------------------------------------- collectives
+// Symmetric (peer-mapped) device memory through CUDA IPC, and the fused
+// data-parallel gradient reduction over it (comm.cu).
+constexpr int kSymmMaxRanks = 8;
+constexpr int kSymmMaxChunks = 128;
+void* symm_malloc(size_t bytes, void* ipc_handle_out);  // zeroed; handle is 64 bytes
+void* symm_open(const void* ipc_handle);
+void symm_close(void* peer_ptr);
+void symm_free(void* p);
+struct SymmAllReduceArgs {
+  float* data[kSymmMaxRanks];      // every rank's data buffer (this rank's own included)
+  uint32_t* flags[kSymmMaxRanks];  // every rank's flag table [2][kSymmMaxRanks][kSymmMaxChunks]
+  float* sumsq[kSymmMaxRanks];     // every rank's slot table [kSymmMaxRanks][kSymmMaxChunks]
+  long long offset;                // first element of the range (multiple of 4)
+  long long numel;
+  int rank, nranks, chunks;
+  uint32_t epoch;                  // grows by one per call on every rank
+  int* status;
+};
+// average data[offset, offset+numel) over the ranks in place on every rank; with
+// norm_sq, also (accumulate_norm ? += : =) the sum of squares of the averaged range
+void symm_allreduce_avg(const SymmAllReduceArgs& a, float* norm_sq, bool accumulate_norm,
+                        cudaStream_t stream);
+
 }  // namespace plg

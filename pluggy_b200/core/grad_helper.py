@@ -43,14 +43,20 @@ def _norm_sq(grads: list[torch.Tensor]) -> torch.Tensor:
 
 
 def clip_grad_norm(params, mesh, max_norm, shard_dims=(), *, fold_into_optimizer: bool = False,
-                   partial_over=None):
+                   partial_over=None, precomputed_sq: torch.Tensor | None = None):
     """``partial_over``: a list of ``(dims, param_ids)`` (or one such pair). Those
     params are further sharded over ``dims`` (tensor or expert parallelism), so
     their squared norms are summed over ``dims`` too; params in no group are
-    replicated and counted once. The groups must be disjoint."""
+    replicated and counted once. The groups must be disjoint.
+
+    ``precomputed_sq``: the global sum of squares, already computed (the fused
+    data-parallel reducer produces it while it averages the grads)."""
     params = list(params)
     grads = _grads(params)
-    if partial_over is None:
+    if precomputed_sq is not None:
+        sq = precomputed_sq.reshape(())
+        shard_dims = ()
+    elif partial_over is None:
         sq = _norm_sq(grads)
     else:
         groups = [partial_over] if isinstance(partial_over, tuple) else list(partial_over)

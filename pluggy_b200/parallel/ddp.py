@@ -120,6 +120,13 @@ class DDP:
         _, work = all_reduce(b.grad_tensor(), self.mesh, self.dim, "avg", async_op=True)
         self._works.append(work)
 
+    def reduced_norm_sq(self):
+        """Sum of squares of the averaged grads, when the reducer computed it on the
+        way (the fused reducer does); else None."""
+        if self._fused is None or self.group_size == 1:
+            return None
+        return self._fused.reduced_norm_sq()
+
     def sync(self) -> None:
         if self.group_size == 1:
             return

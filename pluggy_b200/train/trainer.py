@@ -371,10 +371,14 @@ class Trainer:
             partial.append((("tp",), ids))
         partial = partial or None
         fused = self.device.type == "cuda" and hasattr(self.optimizer, "set_grad_scale")
+        # the fused DDP reducer already summed the squares of the averaged grads
+        pre = None
+        if partial is None and not self.grad_shard_dims and hasattr(self.dp, "reduced_norm_sq"):
+            pre = self.dp.reduced_norm_sq()
         if fused:
             gnorm, coef = clip_grad_norm(self.model.parameters(), self.mesh, self.max_norm,
                                          shard_dims=self.grad_shard_dims, fold_into_optimizer=True,
-                                         partial_over=partial)
+                                         partial_over=partial, precomputed_sq=pre)
             self.optimizer.set_grad_scale(coef)
         else:
             gnorm = clip_grad_norm(self.model.parameters(), self.mesh, self.max_norm,

@@ -16,14 +16,19 @@ def free_port() -> int:
         return s.getsockname()[1]
 
 
-def _entry(rank, world, port, fn, args, q, timeout_s):
+def _entry(rank, world, port, fn, args, q, timeout_s, backend="gloo"):
+    import torch
     import torch.distributed as dist
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                       WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
     try:
-        dist.init_process_group("gloo", rank=rank, world_size=world,
-                                timeout=timedelta(seconds=timeout_s))
+        kw = {}
+        if backend == "nccl":
+            torch.cuda.set_device(rank)
+            kw["device_id"] = torch.device("cuda", rank)
+        dist.init_process_group(backend, rank=rank, world_size=world,
+                                timeout=timedelta(seconds=timeout_s), **kw)
         fn(rank, world, *args)
         q.put((rank, None))
     except BaseException:  # noqa: BLE001 - reported to the parent
@@ -36,11 +41,14 @@ def _entry(rank, world, port, fn, args, q, timeout_s):
             pass
 
 
-def run_ranks(fn, world: int, *args, timeout_s: float = 60.0, join_s: float = 180.0):
+def run_ranks(fn, world: int, *args, timeout_s: float = 60.0, join_s: float = 180.0,
+              backend: str = "gloo"):
+    """``backend="nccl"``: rank r drives GPU r (needs ``world`` GPUs)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=_entry, args=(r, world, port, fn, args, q, timeout_s)) for r in range(world)]
+    procs = [ctx.Process(target=_entry, args=(r, world, port, fn, args, q, timeout_s, backend))
+             for r in range(world)]
     for p in procs:
         p.start()
     results = {}
