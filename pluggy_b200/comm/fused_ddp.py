@@ -51,8 +51,8 @@ class BucketReducer:
                 b.views.append(flat[o:o + p.numel()].view_as(p))
                 o += p.numel()
             self.offset[b.index] = (off, numel)
-        sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
-        self.chunks = chunks or min(128, max(8, sms // 2))
+        # 128 CTAs per bucket: measured best from 8 MB up on B200 (the buckets are 25 MB)
+        self.chunks = chunks or 128
         self.epoch = 0
         self.norm_sq = torch.zeros(1, dtype=torch.float32, device=self.data.device)
         self._first = True
