@@ -3,12 +3,18 @@
 Parity: reference ``pluggy/models/builder.py:11-24`` (same registry names).
 The reference also imports two modules that are absent from its tree
 (``grokathon_model``, ``hybrid_test``); this registry only lists families that
-exist. ``register_model`` lets the model-writer agent add generated families.
+exist. Families written by the model-writer agent are listed in JSON registry
+files (``{"key": "package.module:ClassName"}``): ``models/generated/registry.json``
+and any files named in ``PLG_MODEL_REGISTRY_FILES`` (``os.pathsep``-separated).
+They are imported on first use, so a broken generated file can only fail the run
+that asks for it.
 """
 
 from __future__ import annotations
 
 import importlib
+import json
+import os
 
 import torch.nn as nn
 
@@ -33,6 +39,32 @@ def register_model(name: str, dotted: str) -> None:
     MODEL_REGISTRY[name] = getattr(importlib.import_module(mod), cls)
 
 
+GENERATED_REGISTRY = os.path.join(os.path.dirname(os.path.abspath(__file__)), "generated",
+                                  "registry.json")
+
+
+def generated_entries() -> dict[str, str]:
+    """Registry key -> ``module:Class`` of the generated families (later files win)."""
+    out: dict[str, str] = {}
+    extra = [p for p in os.environ.get("PLG_MODEL_REGISTRY_FILES", "").split(os.pathsep) if p]
+    for path in [GENERATED_REGISTRY, *extra]:
+        try:
+            with open(path) as f:
+                out.update(json.load(f))
+        except FileNotFoundError:
+            continue
+    return out
+
+
+def resolve(model_name: str) -> type[nn.Module]:
+    if model_name not in MODEL_REGISTRY:
+        dotted = generated_entries().get(model_name)
+        if dotted is None:
+            raise KeyError(f"model name {model_name!r} not in registry: "
+                           f"{sorted(MODEL_REGISTRY) + sorted(generated_entries())}")
+        register_model(model_name, dotted)
+    return MODEL_REGISTRY[model_name]
+
+
 def build_model(model_name: str, model_config: dict) -> nn.Module:
-    assert model_name in MODEL_REGISTRY, f"model name {model_name!r} not in registry"
-    return MODEL_REGISTRY[model_name](**model_config)
+    return resolve(model_name)(**model_config)

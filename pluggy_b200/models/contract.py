@@ -140,15 +140,28 @@ def check(model: nn.Module, *, batch: int = 2, seq: int = 16, seed: int = 0,
 
 
 def main(argv=None) -> int:
-    p = argparse.ArgumentParser(description="check a registered model against the contract")
-    p.add_argument("--model", required=True)
+    p = argparse.ArgumentParser(description="check a model against the contract")
+    p.add_argument("--model", help="registry key")
+    p.add_argument("--module", help="module of an unregistered model (with --class)")
+    p.add_argument("--class", dest="cls", help="class name inside --module")
     p.add_argument("--config", required=True, help="JSON model config (or @file.json)")
     a = p.parse_args(argv)
     cfg = a.config
     if cfg.startswith("@"):
         with open(cfg[1:]) as f:
             cfg = f.read()
-    fails = check(build(a.model, json.loads(cfg)))
+    cfg = json.loads(cfg)
+    if a.module:
+        import importlib
+
+        if not a.cls:
+            p.error("--module needs --class")
+        model = getattr(importlib.import_module(a.module), a.cls)(**cfg)
+    elif a.model:
+        model = build(a.model, cfg)
+    else:
+        p.error("give --model, or --module and --class")
+    fails = check(model)
     for f in fails:
         print(f"FAIL {f}")
     print("contract: OK" if not fails else f"contract: {len(fails)} failure(s)")

@@ -37,17 +37,20 @@ def validate_config(cfg: dict) -> None:
     errs = [f"missing top-level key {k!r}" for k in REQUIRED_TOP if k not in cfg]
     if errs:
         raise ConfigError("; ".join(errs))
-    from pluggy_b200.models.builder import MODEL_REGISTRY
+    from pluggy_b200.models.builder import resolve
     from pluggy_b200.objectives.builder import OBJECTIVE_REGISTRY
     from pluggy_b200.optimizer.builder import OPTIMIZER_REGISTRY, SCHEDULER_REGISTRY
 
+    for k in ("model", "mesh", "optimizer", "objective", "data"):
+        if not isinstance(cfg[k], dict):
+            raise ConfigError(f"config block {k!r} must be an object")
     m = cfg["model"]
-    if m.get("name") not in MODEL_REGISTRY:
-        errs.append(f"model.name {m.get('name')!r} not in {sorted(MODEL_REGISTRY)}")
-    else:
-        e = kwarg_error(MODEL_REGISTRY[m["name"]], m.get("config", {}), "model.config")
+    try:
+        e = kwarg_error(resolve(m.get("name")), m.get("config", {}), "model.config")
         if e:
             errs.append(e)
+    except (KeyError, ImportError, AttributeError) as exc:
+        errs.append(f"model.name: {exc}")
     mesh = cfg["mesh"]
     if not isinstance(mesh, dict) or "dp" not in mesh or any(int(v) < 1 for v in mesh.values()):
         errs.append("mesh must map axis names (including 'dp') to positive sizes")
@@ -57,6 +60,8 @@ def validate_config(cfg: dict) -> None:
     if o.get("name") not in OPTIMIZER_REGISTRY:
         errs.append(f"optimizer.name {o.get('name')!r} not in {sorted(OPTIMIZER_REGISTRY)}")
     sch = o.get("scheduler", {})
+    if not isinstance(sch.get("total_steps"), int) or sch["total_steps"] < 1:
+        errs.append("optimizer.scheduler.total_steps must be a positive integer")
     if sch.get("type") not in SCHEDULER_REGISTRY:
         errs.append(f"optimizer.scheduler.type {sch.get('type')!r} not in {sorted(SCHEDULER_REGISTRY)}")
     else:
@@ -75,6 +80,14 @@ def validate_config(cfg: dict) -> None:
     for k in ("global_batch_size", "micro_batch_size", "seq_len"):
         if not isinstance(d.get(k), int) or d[k] < 1:
             errs.append(f"data.{k} must be a positive integer")
+    if not errs or all(not e.startswith("data.") for e in errs):
+        dp = mesh.get("dp", 1) if isinstance(mesh, dict) else 1
+        if isinstance(d.get("global_batch_size"), int) and isinstance(d.get("micro_batch_size"), int) \
+                and d["global_batch_size"] % (d["micro_batch_size"] * dp):
+            errs.append(f"data.global_batch_size {d['global_batch_size']} must be divisible by "
+                        f"micro_batch_size {d['micro_batch_size']} x dp {dp}")
+    if not d.get("synthetic") and not any(k in d for k in ("sources", "name", "data_files")):
+        errs.append("data needs 'name' (hub dataset), 'data_files', 'sources' or 'synthetic'")
     if not d.get("synthetic"):
         for k in ("tokenizer", "eos_token", "pad_token", "num_workers", "seed"):
             if k not in d:
