@@ -131,7 +131,7 @@ def build_synthetic_loader(data_cfg: dict, vocab_size: int, dp_rank: int, pin: b
     src = SyntheticZipfRows(vocab_size=vocab_size, seq_len=data_cfg["seq_len"],
                             eos_id=syn.get("eos_id"), seed=data_cfg.get("seed", 0), dp_rank=dp_rank,
                             zipf_s=syn.get("s", 1.1), min_doc=syn.get("min_doc", 512),
-                            max_doc=syn.get("max_doc", 4096))
+                            max_doc=syn.get("max_doc", 4096), kind=syn.get("kind", "zipf"))
     return SyntheticBatches(src, data_cfg["micro_batch_size"], pin=pin)
 
 

@@ -12,6 +12,9 @@ source produces exactly that, deterministically and resumably:
   maps to id ``k - 1``, except that the EOS id is never sampled as content;
 * document boundaries: the gap between two EOS tokens is drawn from
   ``U[min_doc, max_doc]``; a document may continue across rows (packed stream).
+
+``kind="uniform"`` draws ids uniformly from ``[0, vocab_size)`` with no EOS (the
+CPU/gloo plumbing config).
 """
 
 from __future__ import annotations
@@ -38,7 +41,11 @@ class SyntheticZipfRows(IterableDataset):
     """Infinite stream of ``{"input_ids": [seq_len]}`` rows for one dp shard."""
 
     def __init__(self, vocab_size: int, seq_len: int, eos_id: int | None = None, seed: int = 0,
-                 dp_rank: int = 0, zipf_s: float = 1.1, min_doc: int = 512, max_doc: int = 4096):
+                 dp_rank: int = 0, zipf_s: float = 1.1, min_doc: int = 512, max_doc: int = 4096,
+                 kind: str = "zipf"):
+        if kind not in ("zipf", "uniform"):
+            raise ValueError(f"synthetic kind must be 'zipf' or 'uniform', got {kind!r}")
+        self.kind = kind
         self.vocab_size = vocab_size
         self.seq_len = seq_len
         self.eos_id = vocab_size - 1 if eos_id is None else eos_id
@@ -53,6 +60,8 @@ class SyntheticZipfRows(IterableDataset):
         return np.random.Generator(np.random.Philox(key=[self.seed, (self.dp_rank << 40) | row]))
 
     def row(self, i: int) -> np.ndarray:
+        if self.kind == "uniform":  # ids uniform over the vocab, no document structure
+            return self._rng(i).integers(0, self.vocab_size, self.seq_len, dtype=np.int64)
         if self._table is None:
             self._table = ZipfTable(self.vocab_size, self.zipf_s)
         rng = self._rng(i)
