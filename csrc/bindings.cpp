@@ -147,12 +147,14 @@ void qk_norm_rope_fwd(const at::Tensor& qkv, at::Tensor& q, at::Tensor& k, at::T
                       const c10::optional<at::Tensor>& wq, const c10::optional<at::Tensor>& wk,
                       const at::Tensor& inv_freq, const c10::optional<at::Tensor>& positions,
                       int64_t S, int64_t Hq, int64_t Hk, int64_t d, int64_t rot_dim, double eps,
-                      int64_t k_offset, const c10::optional<at::Tensor>& rope_table) {
+                      int64_t k_offset, const c10::optional<at::Tensor>& rope_table,
+                      const c10::optional<at::Tensor>& status) {
   check_cuda(qkv, "qkv");
   TORCH_CHECK(is_bf16(qkv) && qkv.dim() == 2 && qkv.stride(1) == 1, "qkv must be bf16 [T, W]");
   const c10::cuda::CUDAGuard guard(qkv.device());
   auto a = qk_args(qkv, q, k, rstd, wq, wk, inv_freq, positions, S, Hq, Hk, d, rot_dim, eps, k_offset,
                    rope_table);
+  a.status = status.has_value() ? status->data_ptr<int>() : nullptr;
   plg::qk_norm_rope_fwd(a, cur_stream());
 }
 
@@ -163,12 +165,14 @@ void qk_norm_rope_bwd(const at::Tensor& qkv, at::Tensor& rstd, const c10::option
                       const at::Tensor& dq, const at::Tensor& dk, at::Tensor& dqkv,
                       const c10::optional<at::Tensor>& dwq_partial,
                       const c10::optional<at::Tensor>& dwk_partial, int64_t blocks,
-                      const c10::optional<at::Tensor>& rope_table) {
+                      const c10::optional<at::Tensor>& rope_table,
+                      const c10::optional<at::Tensor>& status) {
   check_cuda(qkv, "qkv");
   const c10::cuda::CUDAGuard guard(qkv.device());
   at::Tensor q_dummy = dq, k_dummy = dk;
   auto a = qk_args(qkv, q_dummy, k_dummy, rstd, wq, wk, inv_freq, positions, S, Hq, Hk, d, rot_dim,
                    eps, k_offset, rope_table);
+  a.status = status.has_value() ? status->data_ptr<int>() : nullptr;
   plg::qk_norm_rope_bwd(a, dq.data_ptr(), dk.data_ptr(), dqkv.data_ptr(), dqkv.stride(0),
                         dwq_partial.has_value() ? dwq_partial->data_ptr<float>() : nullptr,
                         dwk_partial.has_value() ? dwk_partial->data_ptr<float>() : nullptr,
@@ -408,8 +412,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
-  m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd);
-  m.def("qk_norm_rope_bwd", &qk_norm_rope_bwd);
+  m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd, py::arg("qkv"), py::arg("q"), py::arg("k"),
+        py::arg("rstd"), py::arg("wq"), py::arg("wk"), py::arg("inv_freq"), py::arg("positions"),
+        py::arg("S"), py::arg("Hq"), py::arg("Hk"), py::arg("d"), py::arg("rot_dim"), py::arg("eps"),
+        py::arg("k_offset"), py::arg("rope_table"), py::arg("status") = py::none());
+  m.def("qk_norm_rope_bwd", &qk_norm_rope_bwd, py::arg("qkv"), py::arg("rstd"), py::arg("wq"),
+        py::arg("wk"), py::arg("inv_freq"), py::arg("positions"), py::arg("S"), py::arg("Hq"),
+        py::arg("Hk"), py::arg("d"), py::arg("rot_dim"), py::arg("eps"), py::arg("k_offset"),
+        py::arg("dq"), py::arg("dk"), py::arg("dqkv"), py::arg("dwq_partial"), py::arg("dwk_partial"),
+        py::arg("blocks"), py::arg("rope_table"), py::arg("status") = py::none());
   m.def("glu_fwd", &glu_fwd);
   m.def("glu_bwd", &glu_bwd);
   m.def("cast_f32_bf16", &cast_f32_bf16);

@@ -8,6 +8,7 @@
 //                 from pluggy/kernels/rope.py:18-24: x*cos + rotate_half(x)*sin)
 // These are memory-bound: one warp per row (or per token-head), 16-byte
 // vector loads where alignment allows, fp32 accumulation, bf16/fp32 stores.
+#include <algorithm>
 #include <stdexcept>
 
 #include <type_traits>
@@ -301,10 +302,85 @@ __device__ __forceinline__ void rope_angles(const QkRopeArgs& a, int pos, int c0
   }
 }
 
+// One work item's inputs, loaded one item ahead of use: the warp issues the next
+// item's loads before it computes the current one, so every warp keeps two items'
+// rows in flight and the memory latency hides behind the arithmetic.
+// The backward holds twice the rows per head (x and dq/dk) plus the norm-weight
+// accumulators, so its items cover half as many heads; d = 512 rows are too wide
+// to hold two items in registers and are loaded at the top of each iteration.
+template <int D, bool kBwd>
+struct RopeItem {
+  using L = RopeLayout<D>;
+  static constexpr int NQ = L::NV / 8;
+  static constexpr int R = kBwd && L::kRounds > 1 ? L::kRounds / 2 : L::kRounds;
+  static constexpr int HPI = L::HPW * R;
+  static constexpr bool kPrefetch = D < 512;
+  uint4 x[R][NQ];               // pre-norm q/k rows (raw bf16)
+  uint4 g[kBwd ? R : 1][NQ];    // backward: dq/dk rows
+  float rs[kBwd ? R : 1];       // backward: saved rstd
+  float cs[L::NV], sn[L::NV];
+};
+
+template <int NV>
+__device__ __forceinline__ void unpack_row(const uint4 (&raw)[NV / 8], float (&v)[NV]) {
+#pragma unroll
+  for (int q = 0; q < NV / 8; ++q) {
+    const uint32_t* u = reinterpret_cast<const uint32_t*>(&raw[q]);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = unpack_bf16x2(u[k]);
+      v[q * 8 + 2 * k] = f.x;
+      v[q * 8 + 2 * k + 1] = f.y;
+    }
+  }
+}
+
+template <int D, bool kBwd>
+__device__ __forceinline__ void rope_fetch(const QkRopeArgs& a, const __nv_bfloat16* dq,
+                                           const __nv_bfloat16* dk, long long it, int nch, int sub,
+                                           int c0, RopeItem<D, kBwd>& f) {
+  using L = RopeLayout<D>;
+  using I = RopeItem<D, kBwd>;
+  constexpr int NQ = L::NV / 8;
+  const int H = a.Hq + a.Hk;
+  const long long t = it / nch;
+  const int h0 = static_cast<int>(it - t * nch) * I::HPI;
+  const int pos = a.positions ? a.positions[t] : static_cast<int>(t % a.S);
+  const __nv_bfloat16* row = reinterpret_cast<const __nv_bfloat16*>(a.qkv) + t * a.ld_qkv;
+#pragma unroll
+  for (int rr = 0; rr < I::R; ++rr) {
+    const int h = h0 + rr * L::HPW + sub;
+    const bool is_q = h < a.Hq;
+    if (h < H) {
+      const int col = is_q ? h * D : a.k_offset * D + (h - a.Hq) * D;
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) f.x[rr][q] = *reinterpret_cast<const uint4*>(row + col + c0 + q * 8);
+      if constexpr (kBwd) {
+        const __nv_bfloat16* gp = is_q ? dq + (t * a.Hq + h) * D : dk + (t * a.Hk + (h - a.Hq)) * D;
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) f.g[rr][q] = *reinterpret_cast<const uint4*>(gp + c0 + q * 8);
+        f.rs[rr] = (is_q ? a.norm_q : a.norm_k) ? a.rstd[t * H + h] : 1.f;
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) f.x[rr][q] = make_uint4(0u, 0u, 0u, 0u);
+      if constexpr (kBwd) {
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) f.g[rr][q] = make_uint4(0u, 0u, 0u, 0u);
+        f.rs[rr] = 1.f;
+      }
+    }
+  }
+  rope_angles<L::NV>(a, pos, c0, f.cs, f.sn);
+}
+
+// 256 threads, 2 CTAs per SM, a persistent grid: each warp walks work items
+// (token, 8 heads for d=128) with the next item's loads in flight.
 template <int D>
 __global__ void __launch_bounds__(256, 2) qk_rope_fwd_kernel(QkRopeArgs a) {
   using L = RopeLayout<D>;
-  constexpr int NV = L::NV, HPI = L::HPW * L::kRounds;
+  using I = RopeItem<D, false>;
+  constexpr int NV = L::NV, HPI = I::HPI;
   const int lane = threadIdx.x & 31;
   const int sub = lane / L::LPH, ll = lane % L::LPH, c0 = ll * NV;
   const int H = a.Hq + a.Hk;
@@ -321,43 +397,35 @@ __global__ void __launch_bounds__(256, 2) qk_rope_fwd_kernel(QkRopeArgs a) {
     wk[k] = a.norm_k ? a.wk[c0 + k] : 1.f;
   }
   const long long items = a.T * nch;
-  for (long long it = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items;
-       it += (long long)gridDim.x * (blockDim.x >> 5)) {
+  const long long stride = (long long)gridDim.x * (blockDim.x >> 5);
+  long long it = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  I cur;
+  if (I::kPrefetch && it < items) rope_fetch<D, false>(a, nullptr, nullptr, it, nch, sub, c0, cur);
+  for (; it < items; it += stride) {
+    I nxt;
+    if (!I::kPrefetch) rope_fetch<D, false>(a, nullptr, nullptr, it, nch, sub, c0, cur);
+    else if (it + stride < items) rope_fetch<D, false>(a, nullptr, nullptr, it + stride, nch, sub, c0, nxt);
     const long long t = it / nch;
     const int h0 = static_cast<int>(it - t * nch) * HPI;
-    const int pos = a.positions ? a.positions[t] : static_cast<int>(t % a.S);
-    const __nv_bfloat16* row = reinterpret_cast<const __nv_bfloat16*>(a.qkv) + t * a.ld_qkv;
-    float v[L::kRounds][NV];
 #pragma unroll
-    for (int rr = 0; rr < L::kRounds; ++rr) {
-      const int h = h0 + rr * L::HPW + sub;
-      if (h < H) {
-        const int col = h < a.Hq ? h * D : a.k_offset * D + (h - a.Hq) * D;
-        load_row<NV>(row + col + c0, v[rr]);
-      } else {
-#pragma unroll
-        for (int k = 0; k < NV; ++k) v[rr][k] = 0.f;
-      }
-    }
-    float cs[NV], sn[NV];
-    rope_angles<NV>(a, pos, c0, cs, sn);
-#pragma unroll
-    for (int rr = 0; rr < L::kRounds; ++rr) {
+    for (int rr = 0; rr < I::R; ++rr) {
       const int h = h0 + rr * L::HPW + sub;
       const bool is_q = h < a.Hq;
       const bool do_norm = is_q ? a.norm_q : a.norm_k;
+      float v[NV];
+      unpack_row<NV>(cur.x[rr], v);
       float ss = 0.f;
 #pragma unroll
-      for (int k = 0; k < NV; ++k) ss += v[rr][k] * v[rr][k];
+      for (int k = 0; k < NV; ++k) ss += v[k] * v[k];
       ss = group_sum<L::LPH>(ss);
       const float r = do_norm ? rsqrtf(ss / D + a.eps) : 1.f;
 #pragma unroll
-      for (int k = 0; k < NV; ++k) v[rr][k] *= do_norm ? r * (is_q ? wq[k] : wk[k]) : 1.f;
+      for (int k = 0; k < NV; ++k) v[k] *= do_norm ? r * (is_q ? wq[k] : wk[k]) : 1.f;
       float o[NV];
 #pragma unroll
       for (int k = 0; k < NV; ++k) {
-        const float p = __shfl_sync(0xffffffffu, v[rr][k], partner);
-        o[k] = v[rr][k] * cs[k] + sgn * p * sn[k];
+        const float p = __shfl_sync(0xffffffffu, v[k], partner);
+        o[k] = v[k] * cur.cs[k] + sgn * p * cur.sn[k];
       }
       if (h < H) {
         if (ll == 0 && a.rstd) a.rstd[t * H + h] = r;
@@ -366,6 +434,7 @@ __global__ void __launch_bounds__(256, 2) qk_rope_fwd_kernel(QkRopeArgs a) {
         store_row<NV>(dst + c0, o);
       }
     }
+    if (I::kPrefetch) cur = nxt;
   }
 }
 
@@ -376,7 +445,8 @@ __global__ void __launch_bounds__(128, 4) qk_rope_bwd_kernel(QkRopeArgs a, const
                                                              __nv_bfloat16* dqkv, long long ld_dqkv,
                                                              float* dwq_part, float* dwk_part) {
   using L = RopeLayout<D>;
-  constexpr int NV = L::NV, HPI = L::HPW * L::kRounds;
+  using I = RopeItem<D, true>;
+  constexpr int NV = L::NV, HPI = I::HPI;
   extern __shared__ float s_dw[];  // [2 * D]: q weights then k weights
   const int lane = threadIdx.x & 31;
   const int sub = lane / L::LPH, ll = lane % L::LPH, c0 = ll * NV;
@@ -394,57 +464,46 @@ __global__ void __launch_bounds__(128, 4) qk_rope_bwd_kernel(QkRopeArgs a, const
 #pragma unroll
   for (int k = 0; k < NV; ++k) accq[k] = acck[k] = 0.f;
   const long long items = a.T * nch;
-  for (long long it = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items;
-       it += (long long)gridDim.x * (blockDim.x >> 5)) {
+  const long long stride = (long long)gridDim.x * (blockDim.x >> 5);
+  long long it = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  I cur;
+  if (I::kPrefetch && it < items) rope_fetch<D, true>(a, dq, dk, it, nch, sub, c0, cur);
+  for (; it < items; it += stride) {
+    I nxt;
+    if (!I::kPrefetch) rope_fetch<D, true>(a, dq, dk, it, nch, sub, c0, cur);
+    else if (it + stride < items) rope_fetch<D, true>(a, dq, dk, it + stride, nch, sub, c0, nxt);
     const long long t = it / nch;
     const int h0 = static_cast<int>(it - t * nch) * HPI;
-    const int pos = a.positions ? a.positions[t] : static_cast<int>(t % a.S);
-    const __nv_bfloat16* xrow = reinterpret_cast<const __nv_bfloat16*>(a.qkv) + t * a.ld_qkv;
     __nv_bfloat16* orow = dqkv + t * ld_dqkv;
-    float g[L::kRounds][NV], x[L::kRounds][NV], rs[L::kRounds];
 #pragma unroll
-    for (int rr = 0; rr < L::kRounds; ++rr) {
-      const int h = h0 + rr * L::HPW + sub;
-      if (h < H) {
-        const bool is_q = h < a.Hq;
-        const int col = is_q ? h * D : a.k_offset * D + (h - a.Hq) * D;
-        load_row<NV>((is_q ? dq + (t * a.Hq + h) * D : dk + (t * a.Hk + (h - a.Hq)) * D) + c0, g[rr]);
-        load_row<NV>(xrow + col + c0, x[rr]);
-        rs[rr] = (is_q ? a.norm_q : a.norm_k) ? a.rstd[t * H + h] : 1.f;
-      } else {
-#pragma unroll
-        for (int k = 0; k < NV; ++k) g[rr][k] = x[rr][k] = 0.f;
-        rs[rr] = 1.f;
-      }
-    }
-    float cs[NV], sn[NV];
-    rope_angles<NV>(a, pos, c0, cs, sn);
-#pragma unroll
-    for (int rr = 0; rr < L::kRounds; ++rr) {
+    for (int rr = 0; rr < I::R; ++rr) {
       const int h = h0 + rr * L::HPW + sub;
       const bool is_q = h < a.Hq;
       const bool do_norm = (is_q ? a.norm_q : a.norm_k) && h < H;
       const float* wp = is_q ? a.wq : a.wk;
+      float g[NV], x[NV];
+      unpack_row<NV>(cur.g[rr], g);
+      unpack_row<NV>(cur.x[rr], x);
       float gr[NV];
 #pragma unroll
       for (int k = 0; k < NV; ++k) {
-        const float p = __shfl_sync(0xffffffffu, g[rr][k], partner);
-        gr[k] = g[rr][k] * cs[k] + sgn * p * sn[k];
+        const float p = __shfl_sync(0xffffffffu, g[k], partner);
+        gr[k] = g[k] * cur.cs[k] + sgn * p * cur.sn[k];
       }
-      const float r = rs[rr];
+      const float r = cur.rs[rr];
       float dot = 0.f;
       float wv[NV];
 #pragma unroll
       for (int k = 0; k < NV; ++k) {
         wv[k] = do_norm ? wp[c0 + k] : 1.f;
-        dot += gr[k] * wv[k] * x[rr][k] * r;
+        dot += gr[k] * wv[k] * x[k] * r;
       }
       dot = group_sum<L::LPH>(dot) / D;
       float o[NV];
 #pragma unroll
       for (int k = 0; k < NV; ++k) {
         if (do_norm) {
-          const float xh = x[rr][k] * r;
+          const float xh = x[k] * r;
           if (is_q) accq[k] += gr[k] * xh;
           else acck[k] += gr[k] * xh;
           o[k] = r * (gr[k] * wv[k] - xh * dot);
@@ -457,6 +516,7 @@ __global__ void __launch_bounds__(128, 4) qk_rope_bwd_kernel(QkRopeArgs a, const
         store_row<NV>(orow + col + c0, o);
       }
     }
+    if (I::kPrefetch) cur = nxt;
   }
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
@@ -467,6 +527,308 @@ __global__ void __launch_bounds__(128, 4) qk_rope_bwd_kernel(QkRopeArgs a, const
   for (int i = threadIdx.x; i < D; i += blockDim.x) {
     if (dwq_part) dwq_part[(long long)blockIdx.x * D + i] = s_dw[i];
     if (dwk_part) dwk_part[(long long)blockIdx.x * D + i] = s_dw[D + i];
+  }
+}
+
+// ---------------------------------------------------- QK-norm + RoPE, TMA-fed
+// The same math as the kernels above with the loads moved onto the bulk-copy
+// engine: each CTA walks tiles of `tt` tokens; thread 0 issues cp.async.bulk
+// copies of a tile's q/k rows (and, in the backward, its dq/dk rows, saved rstd
+// and the cos/sin table row) into a ring of shared-memory stages, so up to
+// `nst - 1` tiles per CTA are in flight while the warps work on the current one.
+// Work per stage: one (token, head) row per LPH lanes, read from shared memory.
+struct RopeTma {
+  const __nv_bfloat16* dq; const __nv_bfloat16* dk; __nv_bfloat16* dqkv; long long ld_dqkv;
+  float* dwq_part; float* dwk_part;
+  int tt;          // tokens per stage
+  int nst;         // stages (2..4)
+  int tok_bytes;   // shared bytes per token slot (16-byte multiple)
+  int off_g;       // backward: dq|dk rows
+  int off_rs;      // backward: rstd row (when rs_bulk)
+  int off_tab;     // cos|sin row (when a.rope_table)
+  int rs_bulk;     // rstd rows are bulk-copied (H % 4 == 0)
+};
+constexpr int kRopeTmaThreads = 128;
+constexpr int kRopeTmaMaxStages = 4;
+
+// Channel layout of a lane. Unpaired: NV consecutive channels (the rotation
+// partner sits a shuffle away). Paired (rot_dim == d): NV/2 channels of the lower
+// half and the same NV/2 channels of the upper half, so the rotation is local to
+// the lane and every cos/sin value is used twice.
+template <int D, bool kPaired>
+struct RopeLanes {
+  static constexpr int NV = RopeLayout<D>::NV;
+  static constexpr int LPH = RopeLayout<D>::LPH;
+  __device__ static int chan(int ll, int k) {
+    if constexpr (kPaired) return k < NV / 2 ? ll * (NV / 2) + k : D / 2 + ll * (NV / 2) + (k - NV / 2);
+    else return ll * NV + k;
+  }
+  // load NV bf16 channels of a row at `base` (shared or global) into floats
+  __device__ static void load(const uint8_t* base, int ll, float (&v)[NV]) {
+    if constexpr (kPaired) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const uint8_t* p = base + (half * (D / 2) + ll * (NV / 2)) * 2;
+#pragma unroll
+        for (int q = 0; q < NV / 8; ++q) {
+          const uint2 raw = *reinterpret_cast<const uint2*>(p + q * 8);
+          const float2 f0 = unpack_bf16x2(raw.x), f1 = unpack_bf16x2(raw.y);
+          v[half * (NV / 2) + q * 4 + 0] = f0.x;
+          v[half * (NV / 2) + q * 4 + 1] = f0.y;
+          v[half * (NV / 2) + q * 4 + 2] = f1.x;
+          v[half * (NV / 2) + q * 4 + 3] = f1.y;
+        }
+      }
+    } else {
+      uint4 raw[NV / 8];
+#pragma unroll
+      for (int q = 0; q < NV / 8; ++q) raw[q] = *reinterpret_cast<const uint4*>(base + (ll * NV + q * 8) * 2);
+      unpack_row<NV>(raw, v);
+    }
+  }
+  __device__ static void store(__nv_bfloat16* row, int ll, const float (&v)[NV]) {
+    if constexpr (kPaired) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        __nv_bfloat16* p = row + half * (D / 2) + ll * (NV / 2);
+#pragma unroll
+        for (int q = 0; q < NV / 8; ++q) {
+          uint2 raw;
+          raw.x = pack_bf16x2(v[half * (NV / 2) + q * 4 + 0], v[half * (NV / 2) + q * 4 + 1]);
+          raw.y = pack_bf16x2(v[half * (NV / 2) + q * 4 + 2], v[half * (NV / 2) + q * 4 + 3]);
+          *reinterpret_cast<uint2*>(p + q * 4) = raw;
+        }
+      }
+    } else {
+      store_row<NV>(row + ll * NV, v);
+    }
+  }
+};
+
+template <int D, bool kBwd, bool kPaired>
+__global__ void __launch_bounds__(kRopeTmaThreads, 4) qk_rope_tma_kernel(QkRopeArgs a, RopeTma b) {
+  using L = RopeLayout<D>;
+  using C = RopeLanes<D, kPaired>;
+  constexpr int NV = L::NV, HPW = L::HPW, NH = NV / 2;
+  constexpr int kWarps = kRopeTmaThreads / 32;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int H = a.Hq + a.Hk;
+  uint8_t* slots = smem;
+  int* s_pos = reinterpret_cast<int*>(smem + b.nst * b.tt * b.tok_bytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(
+      (reinterpret_cast<uintptr_t>(s_pos + b.nst * b.tt) + 7) & ~uintptr_t(7));
+  float* s_dw = reinterpret_cast<float*>(full + kRopeTmaMaxStages);  // [2 * D] (backward)
+  __shared__ int s_abort;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int sub = lane / L::LPH, ll = lane % L::LPH;
+  // unpaired layout: rotation partner lane and sign
+  const int c0 = ll * NV;
+  const int rh = a.rot_dim / 2;
+  const int off = rh / NV;
+  const int pl = c0 < rh ? ll + off : (c0 < a.rot_dim ? ll - off : ll);
+  const int partner = sub * L::LPH + pl;
+  const float sgn_f = c0 < rh ? -1.f : 1.f;   // forward rotation
+  const float sgn_b = -sgn_f;                 // its transpose
+  const int f0 = c0 < rh ? c0 : c0 - rh;
+  const bool rot_lane = c0 < a.rot_dim;
+  if (tid == 0) {
+    for (int s2 = 0; s2 < b.nst; ++s2) mbar_init(&full[s2], 1);
+    fence_barrier_init();
+    s_abort = 0;
+  }
+  if (kBwd)
+    for (int i = tid; i < 2 * D; i += blockDim.x) s_dw[i] = 0.f;
+  float wq[NV], wk[NV];
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    wq[k] = a.norm_q ? a.wq[C::chan(ll, k)] : 1.f;
+    wk[k] = a.norm_k ? a.wk[C::chan(ll, k)] : 1.f;
+  }
+  float accq[kBwd ? NV : 1], acck[kBwd ? NV : 1];
+#pragma unroll
+  for (int k = 0; k < (kBwd ? NV : 1); ++k) accq[k] = acck[k] = 0.f;
+  __syncthreads();
+
+  const long long ntiles = (a.T + b.tt - 1) / b.tt;
+  const uint32_t qbytes = a.Hq * D * 2, kbytes = a.Hk * D * 2;
+  const __nv_bfloat16* qkv = reinterpret_cast<const __nv_bfloat16*>(a.qkv);
+  // thread 0: positions of the tile, then every copy of the tile on one barrier
+  auto issue = [&](long long tile, int st) {
+    const long long t0 = tile * b.tt;
+    const int n = static_cast<int>(a.T - t0 < b.tt ? a.T - t0 : b.tt);
+    uint32_t per = qbytes + kbytes;
+    if (kBwd) per += qbytes + kbytes + (b.rs_bulk ? H * 4 : 0);
+    if (a.rope_table) per += a.rot_dim * 4;
+    for (int j = 0; j < n; ++j) {
+      const long long t = t0 + j;
+      s_pos[st * b.tt + j] = a.positions ? a.positions[t] : static_cast<int>(t % a.S);
+    }
+    mbar_arrive_expect_tx(&full[st], per * n);
+    for (int j = 0; j < n; ++j) {
+      const long long t = t0 + j;
+      uint8_t* slot = slots + (st * b.tt + j) * b.tok_bytes;
+      bulk_load(slot, qkv + t * a.ld_qkv, qbytes, &full[st]);
+      bulk_load(slot + qbytes, qkv + t * a.ld_qkv + static_cast<long long>(a.k_offset) * D, kbytes,
+                &full[st]);
+      if (kBwd) {
+        bulk_load(slot + b.off_g, b.dq + t * a.Hq * D, qbytes, &full[st]);
+        bulk_load(slot + b.off_g + qbytes, b.dk + t * a.Hk * D, kbytes, &full[st]);
+        if (b.rs_bulk) bulk_load(slot + b.off_rs, a.rstd + t * H, H * 4, &full[st]);
+      }
+      if (a.rope_table)
+        bulk_load(slot + b.off_tab, a.rope_table + static_cast<long long>(s_pos[st * b.tt + j]) * a.rot_dim,
+                  a.rot_dim * 4, &full[st]);
+    }
+  };
+  const long long first = blockIdx.x, stride = gridDim.x;
+  if (tid == 0)
+    for (int s2 = 0; s2 < b.nst - 1; ++s2)
+      if (first + s2 * stride < ntiles) issue(first + s2 * stride, s2);
+
+  int it = 0;
+  for (long long tile = first; tile < ntiles; tile += stride, ++it) {
+    const int st = it % b.nst;
+    if (tid == 0) {
+      const long long nt = tile + (b.nst - 1) * stride;
+      if (nt < ntiles) issue(nt, (it + b.nst - 1) % b.nst);
+    }
+    if (!mbar_wait_bounded(&full[st], (it / b.nst) & 1, &s_abort)) {
+      s_abort = 1;
+      record_status(a.status, kTimeoutTmaFull);
+    }
+    __syncthreads();
+    if (s_abort) break;
+    const long long t0 = tile * b.tt;
+    const int n = static_cast<int>(a.T - t0 < b.tt ? a.T - t0 : b.tt);
+    for (int j = 0; j < n; ++j) {
+      const long long t = t0 + j;
+      const uint8_t* slot = slots + (st * b.tt + j) * b.tok_bytes;
+      // cos / sin of this lane's channels (per token)
+      float cs[kPaired ? NH : NV], sn[kPaired ? NH : NV];
+      if constexpr (kPaired) {
+        if (a.rope_table) {
+          const float* tab = reinterpret_cast<const float*>(slot + b.off_tab);
+#pragma unroll
+          for (int k = 0; k < NH; ++k) {
+            cs[k] = tab[ll * NH + k];
+            sn[k] = tab[rh + ll * NH + k];
+          }
+        } else {
+          const float pos = static_cast<float>(s_pos[st * b.tt + j]);
+#pragma unroll
+          for (int k = 0; k < NH; ++k) sincosf(pos * a.inv_freq[ll * NH + k], &sn[k], &cs[k]);
+        }
+      } else if (a.rope_table) {
+        const float* tab = reinterpret_cast<const float*>(slot + b.off_tab);
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+          cs[k] = rot_lane ? tab[f0 + k] : 1.f;
+          sn[k] = rot_lane ? tab[rh + f0 + k] : 0.f;
+        }
+      } else {
+        rope_angles<NV>(a, s_pos[st * b.tt + j], c0, cs, sn);
+      }
+      for (int hb = warp * HPW; hb < H; hb += kWarps * HPW) {
+        const int h = hb + sub;
+        const bool live = h < H;
+        const int hh = live ? h : 0;
+        const bool is_q = hh < a.Hq;
+        const bool do_norm = is_q ? a.norm_q : a.norm_k;
+        float x[NV];
+        C::load(slot + hh * D * 2, ll, x);
+        if constexpr (!kBwd) {
+          float ss = 0.f;
+#pragma unroll
+          for (int k = 0; k < NV; ++k) ss += x[k] * x[k];
+          ss = group_sum<L::LPH>(ss);
+          const float rr = do_norm ? rsqrtf(ss / D + a.eps) : 1.f;
+#pragma unroll
+          for (int k = 0; k < NV; ++k) x[k] *= rr * (is_q ? wq[k] : wk[k]);
+          float o[NV];
+          if constexpr (kPaired) {
+#pragma unroll
+            for (int k = 0; k < NH; ++k) {
+              o[k] = x[k] * cs[k] - x[NH + k] * sn[k];
+              o[NH + k] = x[NH + k] * cs[k] + x[k] * sn[k];
+            }
+          } else {
+#pragma unroll
+            for (int k = 0; k < NV; ++k) {
+              const float p = __shfl_sync(0xffffffffu, x[k], partner);
+              o[k] = x[k] * cs[k] + sgn_f * p * sn[k];
+            }
+          }
+          if (live) {
+            if (ll == 0 && a.rstd) a.rstd[t * H + h] = rr;
+            __nv_bfloat16* dst = is_q ? reinterpret_cast<__nv_bfloat16*>(a.q) + (t * a.Hq + h) * D
+                                      : reinterpret_cast<__nv_bfloat16*>(a.k) + (t * a.Hk + (h - a.Hq)) * D;
+            C::store(dst, ll, o);
+          }
+        } else {
+          float g[NV];
+          C::load(slot + b.off_g + hh * D * 2, ll, g);
+          float gr[NV];
+          if constexpr (kPaired) {
+#pragma unroll
+            for (int k = 0; k < NH; ++k) {
+              gr[k] = g[k] * cs[k] + g[NH + k] * sn[k];
+              gr[NH + k] = g[NH + k] * cs[k] - g[k] * sn[k];
+            }
+          } else {
+#pragma unroll
+            for (int k = 0; k < NV; ++k) {
+              const float p = __shfl_sync(0xffffffffu, g[k], partner);
+              gr[k] = g[k] * cs[k] + sgn_b * p * sn[k];
+            }
+          }
+          const bool norm_row = do_norm && live;
+          const float rr = !norm_row ? 1.f
+                           : (b.rs_bulk ? reinterpret_cast<const float*>(slot + b.off_rs)[h] : a.rstd[t * H + h]);
+          float dot = 0.f;
+#pragma unroll
+          for (int k = 0; k < NV; ++k) dot += gr[k] * (is_q ? wq[k] : wk[k]) * x[k];
+          dot = group_sum<L::LPH>(dot) * rr / D;
+          float o[NV];
+#pragma unroll
+          for (int k = 0; k < NV; ++k) {
+            if (norm_row) {
+              const float xh = x[k] * rr;
+              if (is_q) accq[k] += gr[k] * xh;
+              else acck[k] += gr[k] * xh;
+              o[k] = rr * (gr[k] * (is_q ? wq[k] : wk[k]) - xh * dot);
+            } else {
+              o[k] = gr[k];
+            }
+          }
+          if (live) {
+            const int col = is_q ? h * D : a.k_offset * D + (h - a.Hq) * D;
+            C::store(b.dqkv + t * b.ld_dqkv + col, ll, o);
+          }
+        }
+      }
+    }
+    __syncthreads();  // stage st is free for the refill issued next iteration
+  }
+  if (s_abort) {
+    // wait (bounded) for copies still in flight into the stages before exiting
+    for (int s2 = 0; s2 < b.nst; ++s2) {
+      volatile int none = 0;
+      mbar_wait_bounded(&full[s2], 0, &none, 1000000ull);
+      mbar_wait_bounded(&full[s2], 1, &none, 1000000ull);
+    }
+    return;
+  }
+  if constexpr (kBwd) {
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      atomicAdd(&s_dw[C::chan(ll, k)], accq[k]);
+      atomicAdd(&s_dw[D + C::chan(ll, k)], acck[k]);
+    }
+    __syncthreads();
+    for (int i = tid; i < D; i += blockDim.x) {
+      if (b.dwq_part) b.dwq_part[(long long)blockIdx.x * D + i] = s_dw[i];
+      if (b.dwk_part) b.dwk_part[(long long)blockIdx.x * D + i] = s_dw[D + i];
+    }
   }
 }
 
@@ -508,20 +870,98 @@ static void check_rope_args(const QkRopeArgs& a) {
 
 template <int D>
 static long long rope_items(const QkRopeArgs& a) {
-  constexpr int hpi = RopeLayout<D>::HPW * RopeLayout<D>::kRounds;
+  constexpr int hpi = RopeItem<D, false>::HPI;
   return a.T * ((a.Hq + a.Hk + hpi - 1) / hpi);
 }
 
 template <int D>
 static void rope_fwd_t(const QkRopeArgs& a, cudaStream_t st) {
   long long blocks = (rope_items<D>(a) + 7) / 8;
-  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (blocks > 148 * 2) blocks = 148 * 2;  // persistent: the resident CTAs (2 per SM)
   qk_rope_fwd_kernel<D><<<static_cast<unsigned>(blocks), 256, 0, st>>>(a);
+}
+
+// Shared-memory plan of the TMA-fed kernels: token slot layout, tokens per stage
+// and stage count, sized for 4 CTAs per SM (<= ~54 KB each) where possible.
+static RopeTma rope_tma_plan(const QkRopeArgs& a, bool bwd) {
+  RopeTma b{};
+  const int H = a.Hq + a.Hk;
+  auto up16 = [](int x) { return (x + 15) & ~15; };
+  int off = H * a.d * 2;  // x rows
+  if (bwd) {
+    b.off_g = off;
+    off += H * a.d * 2;
+    b.rs_bulk = (H % 4) == 0;
+    if (b.rs_bulk) {
+      b.off_rs = off;
+      off = up16(off + H * 4);
+    }
+  }
+  if (a.rope_table) {
+    b.off_tab = off;
+    off += a.rot_dim * 4;
+  }
+  b.tok_bytes = up16(off);
+  b.tt = std::max(1, (13 * 1024) / b.tok_bytes);
+  b.nst = std::min(kRopeTmaMaxStages, std::max(2, (54 * 1024) / (b.tt * b.tok_bytes)));
+  return b;
+}
+
+static size_t rope_tma_smem(const RopeTma& b, int d, bool bwd) {
+  size_t bytes = static_cast<size_t>(b.nst) * b.tt * b.tok_bytes + b.nst * b.tt * sizeof(int) + 8;
+  bytes += kRopeTmaMaxStages * sizeof(uint64_t) + (bwd ? 2 * d * sizeof(float) : 0);
+  return bytes;
+}
+
+// The TMA path needs 16-byte-aligned rows and offsets (checked by check_rope_args)
+// and a rotated prefix the lane layout supports; d = 512 keeps the register path.
+static bool rope_tma_ok(const QkRopeArgs& a) {
+  return a.d == 64 || a.d == 128 || a.d == 256;
+}
+
+template <int D, bool kBwd, bool kPaired>
+static void rope_tma_launch_t(const QkRopeArgs& a, RopeTma b, int grid, cudaStream_t st) {
+  const size_t sm = rope_tma_smem(b, D, kBwd);
+  // the plan's size varies with the head counts: raise the limit once to what the
+  // device allows beside the kernel's static shared memory
+  static int limit[64] = {0};
+  int dev = 0;
+  PLG_CUDA_CHECK(cudaGetDevice(&dev));
+  if (limit[dev & 63] == 0) {
+    int optin = 0;
+    PLG_CUDA_CHECK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    cudaFuncAttributes fa{};
+    PLG_CUDA_CHECK(cudaFuncGetAttributes(&fa, reinterpret_cast<const void*>(&qk_rope_tma_kernel<D, kBwd, kPaired>)));
+    limit[dev & 63] = optin - static_cast<int>(fa.sharedSizeBytes);
+  }
+  if (sm > static_cast<size_t>(limit[dev & 63]))
+    throw std::invalid_argument("qk_norm_rope: a token's rows exceed shared memory");
+  set_max_smem_once(reinterpret_cast<const void*>(&qk_rope_tma_kernel<D, kBwd, kPaired>), limit[dev & 63]);
+  qk_rope_tma_kernel<D, kBwd, kPaired><<<grid, kRopeTmaThreads, sm, st>>>(a, b);
+}
+
+// full rotary uses the paired lane layout (no rotation shuffles)
+template <int D, bool kBwd>
+static void rope_tma_launch(const QkRopeArgs& a, RopeTma b, int grid, cudaStream_t st) {
+  if (a.rot_dim == D) rope_tma_launch_t<D, kBwd, true>(a, b, grid, st);
+  else rope_tma_launch_t<D, kBwd, false>(a, b, grid, st);
 }
 
 void qk_norm_rope_fwd(const QkRopeArgs& a, cudaStream_t st) {
   if (a.T <= 0) return;
   check_rope_args(a);
+  if (rope_tma_ok(a)) {
+    const RopeTma b = rope_tma_plan(a, false);
+    const long long tiles = (a.T + b.tt - 1) / b.tt;
+    const int grid = static_cast<int>(std::min<long long>(tiles, 148LL * 4));
+    switch (a.d) {
+      case 64: rope_tma_launch<64, false>(a, b, grid, st); break;
+      case 128: rope_tma_launch<128, false>(a, b, grid, st); break;
+      default: rope_tma_launch<256, false>(a, b, grid, st); break;
+    }
+    PLG_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   switch (a.d) {
     case 64: rope_fwd_t<64>(a, st); break;
     case 128: rope_fwd_t<128>(a, st); break;
@@ -540,6 +980,23 @@ void qk_norm_rope_bwd(const QkRopeArgs& a, const void* dq, const void* dk, void*
   if ((ld_dqkv % 8) || (reinterpret_cast<uintptr_t>(dqkv) & 15) ||
       (reinterpret_cast<uintptr_t>(dq) & 15) || (reinterpret_cast<uintptr_t>(dk) & 15))
     throw std::invalid_argument("qk_norm_rope_bwd: rows must be 16-byte aligned");
+  if (rope_tma_ok(a)) {
+    RopeTma b = rope_tma_plan(a, true);
+    b.dq = reinterpret_cast<const __nv_bfloat16*>(dq);
+    b.dk = reinterpret_cast<const __nv_bfloat16*>(dk);
+    b.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv);
+    b.ld_dqkv = ld_dqkv;
+    b.dwq_part = dwq_partial;
+    b.dwk_part = dwk_partial;
+    // one partial dw row per CTA: the grid is exactly dw_blocks
+    switch (a.d) {
+      case 64: rope_tma_launch<64, true>(a, b, dw_blocks, st); break;
+      case 128: rope_tma_launch<128, true>(a, b, dw_blocks, st); break;
+      default: rope_tma_launch<256, true>(a, b, dw_blocks, st); break;
+    }
+    PLG_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   const size_t sm = 2 * a.d * sizeof(float);
   auto q = reinterpret_cast<const __nv_bfloat16*>(dq);
   auto k = reinterpret_cast<const __nv_bfloat16*>(dk);

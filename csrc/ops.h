@@ -58,6 +58,7 @@ struct QkRopeArgs {
   int k_offset; int v_offset;  // column offsets (in heads*d units) of k and v within a row
   int full_width_norm;     // OLMo: q/k normalised over all heads' channels jointly
   const float* rope_table; // optional [S][2][rot_dim/2] cos then sin per position (else sincosf)
+  int* status = nullptr;   // device status word (bounded waits of the TMA-fed kernels)
 };
 void qk_norm_rope_fwd(const QkRopeArgs& a, cudaStream_t stream);
 // backward: dq [T,Hq,d], dk [T,Hk,d] -> dqkv (q and k parts) ; dwq/dwk partials

@@ -15,7 +15,7 @@ import weakref
 
 import torch
 
-from pluggy_b200.ops._ext import ext
+from pluggy_b200.ops._ext import ext, status_word
 
 DW_BLOCKS = 592  # 4 CTAs per SM on 148 SMs: dw partial sums reduced by the caller
 
@@ -117,7 +117,8 @@ def qk_norm_rope_fwd(qkv, *, S, Hq, Hk, d, wq, wk, inv_freq, positions=None, eps
     rd = int(d if rot_dim is None else rot_dim)
     table = rope_table(inv_freq, S, rd) if rd > 0 else None
     ext().qk_norm_rope_fwd(qkv, q, k, rstd, wq, wk, inv_freq, positions, int(S), int(Hq), int(Hk),
-                           int(d), rd, float(eps), int(Hq if k_offset is None else k_offset), table)
+                           int(d), rd, float(eps), int(Hq if k_offset is None else k_offset), table,
+                           status_word(qkv.device))
     return q, k, rstd
 
 
@@ -130,5 +131,5 @@ def qk_norm_rope_bwd(qkv, rstd, dq, dk, dqkv, *, S, Hq, Hk, d, wq, wk, inv_freq,
     table = rope_table(inv_freq, S, rd) if rd > 0 else None
     ext().qk_norm_rope_bwd(qkv, rstd, wq, wk, inv_freq, positions, int(S), int(Hq), int(Hk), int(d),
                            rd, float(eps), int(Hq if k_offset is None else k_offset), dq, dk, dqkv,
-                           pq, pk, DW_BLOCKS, table)
+                           pq, pk, DW_BLOCKS, table, status_word(qkv.device))
     return (_colsum(pq) if pq is not None else None), (_colsum(pk) if pk is not None else None)

@@ -172,6 +172,43 @@ def test_qk_norm_rope_fwd_bwd(d, rot_frac, Hq, Hk):
     assert rel(dwq, wqr.grad) < 2e-2 and rel(dwk, wkr.grad) < 2e-2
 
 
+@pytest.mark.parametrize("norm", [True, False])
+def test_qk_rope_positions_odd_tokens(norm):
+    """Explicit positions, a token count that does not fill the last tile, and the
+    no-norm (Llama) path of the TMA-fed kernels."""
+    from pluggy_b200.ops.norm import qk_norm_rope_bwd, qk_norm_rope_fwd
+
+    d, Hq, Hk, S, T = 128, 16, 8, 300, 257
+    W = (Hq + 2 * Hk) * d
+    qkv = torch.randn(T, W, device=DEV).bfloat16()
+    wq = (1 + 0.1 * torch.randn(d, device=DEV)) if norm else None
+    wk = (1 + 0.1 * torch.randn(d, device=DEV)) if norm else None
+    inv = 1.0 / (1e6 ** (torch.arange(0, d, 2, device=DEV).float() / d))
+    pos = torch.randint(0, S, (T,), device=DEV, dtype=torch.int32)
+    q, k, rstd = qk_norm_rope_fwd(qkv, S=S, Hq=Hq, Hk=Hk, d=d, wq=wq, wk=wk, inv_freq=inv, eps=1e-6,
+                                  positions=pos)
+    x = qkv.float().requires_grad_(True)
+    H = Hq + Hk
+    xs = x[:, :H * d].view(T, H, d)
+    if norm:
+        w = torch.cat([wq.expand(Hq, d), wk.expand(Hk, d)], 0)
+        xn = xs * torch.rsqrt(xs.pow(2).mean(-1, keepdim=True) + 1e-6) * w
+    else:
+        xn = xs
+    ang = pos.float()[:, None] * inv[None, :]
+    cos = torch.cat([ang.cos(), ang.cos()], -1)[:, None, :]
+    sin = torch.cat([ang.sin(), ang.sin()], -1)[:, None, :]
+    h = d // 2
+    ref = xn * cos + torch.cat([-xn[..., h:], xn[..., :h]], -1) * sin
+    assert rel(q, ref[:, :Hq]) < 1e-2 and rel(k, ref[:, Hq:]) < 1e-2
+    g = torch.randn_like(ref)
+    (ref * g).sum().backward()
+    dqkv = torch.zeros(T, W, device=DEV, dtype=torch.bfloat16)
+    qk_norm_rope_bwd(qkv, rstd, g[:, :Hq].bfloat16().contiguous(), g[:, Hq:].bfloat16().contiguous(),
+                     dqkv, S=S, Hq=Hq, Hk=Hk, d=d, wq=wq, wk=wk, inv_freq=inv, eps=1e-6, positions=pos)
+    assert rel(dqkv[:, :H * d], x.grad[:, :H * d]) < 2e-2
+
+
 # ----------------------------------------------------------------- pointwise
 @pytest.mark.parametrize("kind", [0, 1])
 def test_glu_fwd_bwd(kind):
