@@ -22,6 +22,7 @@
 #include <cudaTypedefs.h>
 
 #include <mutex>
+#include <algorithm>
 #include <stdexcept>
 #include <string>
 
@@ -1257,9 +1258,10 @@ __global__ void attn_bwd_stats_kernel(const __nv_bfloat16* __restrict__ o, long 
   const int lane = threadIdx.x & 31;
   const long long total = static_cast<long long>(B) * S64 * H;
   if (wid >= total) return;
-  const int h = static_cast<int>(wid % H);
-  const long long bs = wid / H;
-  const int bb = static_cast<int>(bs / S64), s = static_cast<int>(bs % S64);
+  // position fastest: consecutive warps write consecutive stats and read consecutive lse
+  const int s = static_cast<int>(wid % S64);
+  const long long bh = wid / S64;
+  const int h = static_cast<int>(bh % H), bb = static_cast<int>(bh / H);
   float* row = stats + (static_cast<long long>(bb) * H + h) * 2 * S64;
   if (s >= S) {
     if (lane == 0) {
@@ -1285,17 +1287,36 @@ __global__ void attn_bwd_stats_kernel(const __nv_bfloat16* __restrict__ o, long 
 // dQ workspace (fp32 [B*S, H*D]) -> bf16 rows with stride dq_row; 8 values per access
 __global__ void attn_dq_cast8_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dq,
                                      long long dq_row, long long tokens, int HD) {
+  // flat index over 8-value groups; four groups per thread in flight per iteration
   const int c8 = HD / 8;
-  for (long long t = blockIdx.x; t < tokens; t += gridDim.x) {
-    const float4* src = reinterpret_cast<const float4*>(acc + t * HD);
-    for (int c = threadIdx.x; c < c8; c += blockDim.x) {
-      const float4 x = src[2 * c], y = src[2 * c + 1];
-      uint4 v;
-      v.x = pack_bf16x2(x.x, x.y);
-      v.y = pack_bf16x2(x.z, x.w);
-      v.z = pack_bf16x2(y.x, y.y);
-      v.w = pack_bf16x2(y.z, y.w);
-      *reinterpret_cast<uint4*>(dq + t * dq_row + c * 8) = v;
+  const long long n8 = tokens * c8;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  constexpr int U = 4;
+  for (long long i0 = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i0 < n8;
+       i0 += U * stride) {
+    float4 x[U], y[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const long long i = i0 + u * stride;
+      if (i < n8) {
+        const float4* src = reinterpret_cast<const float4*>(acc) + 2 * i;
+        x[u] = src[0];
+        y[u] = src[1];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const long long i = i0 + u * stride;
+      if (i < n8) {
+        const long long t = i / c8;
+        const int c = static_cast<int>(i - t * c8);
+        uint4 v;
+        v.x = pack_bf16x2(x[u].x, x[u].y);
+        v.y = pack_bf16x2(x[u].z, x[u].w);
+        v.z = pack_bf16x2(y[u].x, y[u].y);
+        v.w = pack_bf16x2(y[u].z, y[u].w);
+        *reinterpret_cast<uint4*>(dq + t * dq_row + c * 8) = v;
+      }
     }
   }
 }
@@ -1438,7 +1459,8 @@ static void bwd3_launch(const AttnBwdArgs& g, cudaStream_t st) {
   attn_bwd3_kernel<<<static_cast<unsigned>(ctas), kB3Threads, C::kSmem, st>>>(tq, tk, tv, td, tdq, g);
   PLG_CUDA_CHECK(cudaGetLastError());
   const long long tokens = static_cast<long long>(a.B) * a.S;
-  const long long cblocks = tokens < 148 * 16 ? tokens : 148 * 16;
+  const long long groups = tokens * (a.Hq * C::D / 8);
+  const long long cblocks = std::max(1LL, std::min<long long>((groups + 255) / 256, 148 * 8));
   attn_dq_cast8_kernel<<<static_cast<unsigned>(cblocks), 256, 0, st>>>(
       g.dq_acc, reinterpret_cast<__nv_bfloat16*>(g.dq), g.dq_row, tokens, a.Hq * C::D);
   PLG_CUDA_CHECK(cudaGetLastError());

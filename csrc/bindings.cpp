@@ -405,6 +405,83 @@ void symm_allreduce_avg_b(std::vector<int64_t> data, std::vector<int64_t> flags,
   plg::symm_allreduce_avg(a, ns, accumulate, cur_stream());
 }
 
+// GEMM whose epilogue stores each row into its owner's staging slot (tensor-parallel
+// reduce-scatter along the sequence); rs_dst: every rank's staging base address
+void gemm_rs(const at::Tensor& a, const at::Tensor& b, bool b_mn_major, std::vector<int64_t> rs_dst,
+             int64_t rank, int64_t S, const c10::optional<at::Tensor>& status) {
+  check_cuda(a, "a");
+  check_cuda(b, "b");
+  TORCH_CHECK(is_bf16(a) && is_bf16(b) && a.dim() == 2 && b.dim() == 2, "gemm_rs: bf16 2-D operands");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1, "gemm_rs needs unit inner stride");
+  const int n = static_cast<int>(rs_dst.size());
+  TORCH_CHECK(n >= 1 && n <= 8, "gemm_rs: 1..8 ranks");
+  const c10::cuda::CUDAGuard guard(a.device());
+  plg::GemmProblem p;
+  p.M = static_cast<int>(a.size(0));
+  p.K = static_cast<int>(a.size(1));
+  p.N = static_cast<int>(b_mn_major ? b.size(1) : b.size(0));
+  TORCH_CHECK((b_mn_major ? b.size(0) : b.size(1)) == p.K, "gemm_rs: K mismatch");
+  p.A = a.data_ptr();
+  p.lda = a.stride(0);
+  p.B = b.data_ptr();
+  p.ldb = b.stride(0);
+  p.b_mn_major = b_mn_major;
+  p.ldc = p.N;
+  p.splits = 1;
+  p.allow_split = false;
+  p.rs_n = n;
+  p.rs_rank = static_cast<int>(rank);
+  p.rs_S = S;
+  for (int j = 0; j < n; ++j) p.rs_dst[j] = reinterpret_cast<void*>(rs_dst[j]);
+  p.status = status.has_value() ? status->data_ptr<int>() : nullptr;
+  plg::gemm_bf16(p, cur_stream());
+}
+
+plg::TpArgs tp_args(std::vector<int64_t> flags, std::vector<int64_t> bufs, int64_t rank, int64_t epoch,
+                    int64_t B, int64_t S, int64_t W, const c10::optional<at::Tensor>& status) {
+  const int n = static_cast<int>(flags.size());
+  TORCH_CHECK(n >= 1 && n <= plg::kSymmMaxRanks && bufs.size() == flags.size(),
+              "tp collective: one flag table and one buffer per rank (1..8)");
+  plg::TpArgs a;
+  a.n = n;
+  a.rank = static_cast<int>(rank);
+  a.epoch = static_cast<uint32_t>(epoch);
+  a.status = status.has_value() ? status->data_ptr<int>() : nullptr;
+  for (int j = 0; j < n; ++j) {
+    a.flags[j] = reinterpret_cast<uint32_t*>(flags[j]);
+    a.bufs[j] = reinterpret_cast<void*>(bufs[j]);
+  }
+  a.B = B;
+  a.S = S;
+  a.W = W;
+  return a;
+}
+
+void tp_collective(const std::string& op, const at::Tensor& t, std::vector<int64_t> flags,
+                   std::vector<int64_t> bufs, int64_t rank, int64_t epoch, int64_t B, int64_t S,
+                   const c10::optional<at::Tensor>& status) {
+  check_cuda(t, "t");
+  TORCH_CHECK(is_bf16(t) && t.dim() == 2 && t.stride(1) == 1, "tp collective: bf16 [rows, W] rows");
+  const c10::cuda::CUDAGuard guard(t.device());
+  auto a = tp_args(flags, bufs, rank, epoch, B, S, t.size(1), status);
+  const long long full = B * S, part = B * (S / static_cast<long long>(flags.size()));
+  if (op == "rs_push") {
+    TORCH_CHECK(t.size(0) == full, "rs_push: partial must be [B*S, W]");
+    plg::tp_rs_push(a, t.data_ptr(), t.stride(0), cur_stream());
+  } else if (op == "rs_finish") {
+    TORCH_CHECK(t.size(0) == part, "rs_finish: out must be [B*S/n, W]");
+    plg::tp_rs_finish(a, t.data_ptr(), t.stride(0), cur_stream());
+  } else if (op == "ag_stage") {
+    TORCH_CHECK(t.size(0) == part, "ag_stage: shard must be [B*S/n, W]");
+    plg::tp_ag_stage(a, t.data_ptr(), t.stride(0), cur_stream());
+  } else if (op == "ag_pull") {
+    TORCH_CHECK(t.size(0) == full, "ag_pull: out must be [B*S, W]");
+    plg::tp_ag_pull(a, t.data_ptr(), t.stride(0), cur_stream());
+  } else {
+    TORCH_CHECK(false, "tp collective: unknown op ", op);
+  }
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -431,6 +508,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_free", &symm_free_b);
   m.def("tensor_from_ptr", &tensor_from_ptr);
   m.def("symm_allreduce_avg", &symm_allreduce_avg_b);
+  m.def("gemm_rs", &gemm_rs, py::arg("a"), py::arg("b"), py::arg("b_mn_major"), py::arg("rs_dst"),
+        py::arg("rank"), py::arg("S"), py::arg("status") = py::none());
+  m.def("tp_collective", &tp_collective, py::arg("op"), py::arg("t"), py::arg("flags"), py::arg("bufs"),
+        py::arg("rank"), py::arg("epoch"), py::arg("B"), py::arg("S"), py::arg("status") = py::none());
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd", &embedding_bwd);
   m.def("softcap", &softcap);

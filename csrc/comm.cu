@@ -153,6 +153,151 @@ __global__ void sumsq_total_kernel(const float* __restrict__ slots, int nranks, 
   }
 }
 
+// ------------------------------------------------------------ tensor parallel
+// Rows are [B, S] flattened; with n ranks each owns seg = S / n positions of every
+// sequence. Row (b, s) -> owner s / seg, local row b * seg + s % seg.
+struct TpMap {
+  long long S, seg, rows;  // rows = B * seg per rank
+  __device__ __forceinline__ void split(long long row, int& owner, long long& lrow) const {
+    const long long b = row / S, s = row - b * S;
+    owner = static_cast<int>(s / seg);
+    lrow = b * seg + (s - owner * seg);
+  }
+  __device__ __forceinline__ long long join(int owner, long long lrow) const {
+    const long long b = lrow / seg;
+    return b * S + owner * seg + (lrow - b * seg);
+  }
+};
+
+__device__ __forceinline__ const void* tp_buf(const TpArgs& a, int j) {
+  const void* p = a.bufs[0];
+#pragma unroll
+  for (int i = 1; i < kSymmMaxRanks; ++i)
+    if (j == i) p = a.bufs[i];
+  return p;
+}
+
+__device__ __forceinline__ uint32_t* tp_flag(const TpArgs& a, int j) {
+  uint32_t* p = a.flags[0];
+#pragma unroll
+  for (int i = 1; i < kSymmMaxRanks; ++i)
+    if (j == i) p = a.flags[i];
+  return p;
+}
+
+// every CTA: publish "this rank's part of call `epoch` is in place" to each peer
+// (idempotent), then wait for every peer's; false (status recorded) on timeout
+__device__ bool tp_handshake(const TpArgs& a, int kind) {
+  __shared__ int s_ok;
+  if (threadIdx.x < a.n) {
+    __threadfence_system();
+    st_release_sys(tp_flag(a, threadIdx.x) + kind * kSymmMaxRanks + a.rank, a.epoch);
+  }
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    uint32_t* mine = tp_flag(a, a.rank) + kind * kSymmMaxRanks;
+    for (int p = 0; p < a.n && ok; ++p) ok = wait_flag(mine + p, a.epoch);
+    if (!ok) record_status(a.status, kTimeoutPeerFlag);
+    s_ok = ok;
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
+__global__ void __launch_bounds__(256) tp_rs_push_kernel(TpArgs a, const __nv_bfloat16* __restrict__ part,
+                                                         long long ld) {
+  const TpMap m{a.S, a.S / a.n, a.B * (a.S / a.n)};
+  const long long g8 = a.W / 8, total = a.B * a.S * g8;
+  for (long long g = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; g < total;
+       g += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long row = g / g8;
+    const long long c = (g - row * g8) * 8;
+    int owner;
+    long long lrow;
+    m.split(row, owner, lrow);
+    const uint4 v = *reinterpret_cast<const uint4*>(part + row * ld + c);
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(tp_buf(a, owner)));
+    *reinterpret_cast<uint4*>(dst + (a.rank * m.rows + lrow) * a.W + c) = v;
+  }
+  __threadfence_system();
+}
+
+__global__ void __launch_bounds__(256) tp_rs_finish_kernel(TpArgs a, __nv_bfloat16* __restrict__ out,
+                                                           long long ld_out) {
+  if (!tp_handshake(a, 0)) return;
+  const long long rows = a.B * (a.S / a.n), g8 = a.W / 8, total = rows * g8;
+  const __nv_bfloat16* st = reinterpret_cast<const __nv_bfloat16*>(tp_buf(a, a.rank));
+  for (long long g = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; g < total;
+       g += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = g / g8;
+    const long long c = (g - r * g8) * 8;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int p = 0; p < a.n; ++p) {  // fixed order: deterministic
+      const uint4 v = *reinterpret_cast<const uint4*>(st + (p * rows + r) * a.W + c);
+      const uint32_t* u = reinterpret_cast<const uint32_t*>(&v);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = unpack_bf16x2(u[k]);
+        acc[2 * k] += f.x;
+        acc[2 * k + 1] += f.y;
+      }
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(out + r * ld_out + c) = o;
+  }
+}
+
+__global__ void __launch_bounds__(256) tp_ag_stage_kernel(TpArgs a, const __nv_bfloat16* __restrict__ shard,
+                                                          long long ld) {
+  const long long rows = a.B * (a.S / a.n), g8 = a.W / 8, total = rows * g8;
+  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(tp_buf(a, a.rank)));
+  for (long long g = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; g < total;
+       g += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = g / g8;
+    const long long c = (g - r * g8) * 8;
+    *reinterpret_cast<uint4*>(dst + r * a.W + c) = *reinterpret_cast<const uint4*>(shard + r * ld + c);
+  }
+  __threadfence_system();
+}
+
+__global__ void __launch_bounds__(256) tp_ag_pull_kernel(TpArgs a, __nv_bfloat16* __restrict__ out,
+                                                         long long ld_out) {
+  if (!tp_handshake(a, 1)) return;
+  const TpMap m{a.S, a.S / a.n, a.B * (a.S / a.n)};
+  const long long g8 = a.W / 8, per = m.rows * g8, total = a.n * per;
+  constexpr int U = 4;  // four 16-byte peer loads in flight per thread
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long g0 = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; g0 < total;
+       g0 += U * stride) {
+    uint4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const long long g = g0 + u * stride;
+      if (g < total) {
+        const int p = static_cast<int>(g / per);
+        const long long rem = g - p * per;
+        const long long lrow = rem / g8, c = (rem - lrow * g8) * 8;
+        v[u] = *reinterpret_cast<const uint4*>(
+            reinterpret_cast<const __nv_bfloat16*>(tp_buf(a, p)) + lrow * a.W + c);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const long long g = g0 + u * stride;
+      if (g < total) {
+        const int p = static_cast<int>(g / per);
+        const long long rem = g - p * per;
+        const long long lrow = rem / g8, c = (rem - lrow * g8) * 8;
+        *reinterpret_cast<uint4*>(out + m.join(p, lrow) * ld_out + c) = v[u];
+      }
+    }
+  }
+}
+
 }  // namespace comm
 
 void* symm_malloc(size_t bytes, void* ipc_handle_out) {
@@ -193,6 +338,52 @@ void symm_allreduce_avg(const SymmAllReduceArgs& a, float* norm_sq, bool accumul
                                                 accumulate_norm ? 1 : 0);
     PLG_CUDA_CHECK(cudaGetLastError());
   }
+}
+
+static void tp_check(const TpArgs& a, long long ld, const void* p, const char* what) {
+  if (a.n < 1 || a.n > kSymmMaxRanks || a.rank < 0 || a.rank >= a.n)
+    throw std::invalid_argument(std::string(what) + ": 1..8 ranks");
+  if (a.S % a.n || a.W % 8 || ld % 8 || (reinterpret_cast<uintptr_t>(p) & 15))
+    throw std::invalid_argument(std::string(what) +
+                                ": S divisible by ranks, width and row stride multiples of 8, 16-byte rows");
+  for (int j = 0; j < a.n; ++j)
+    if (a.flags[j] == nullptr || a.bufs[j] == nullptr || (reinterpret_cast<uintptr_t>(a.bufs[j]) & 15))
+      throw std::invalid_argument(std::string(what) + ": every rank's flags and 16-byte aligned buffer");
+}
+
+static unsigned tp_grid(long long groups, int cap) {
+  long long g = (groups + 255) / 256;
+  if (g < 1) g = 1;
+  if (g > cap) g = cap;
+  return static_cast<unsigned>(g);
+}
+
+void tp_rs_push(const TpArgs& a, const void* partial, long long ld, cudaStream_t st) {
+  tp_check(a, ld, partial, "tp_rs_push");
+  comm::tp_rs_push_kernel<<<tp_grid(a.B * a.S * (a.W / 8), 148 * 8), 256, 0, st>>>(
+      a, reinterpret_cast<const __nv_bfloat16*>(partial), ld);
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+void tp_rs_finish(const TpArgs& a, void* out, long long ld_out, cudaStream_t st) {
+  tp_check(a, ld_out, out, "tp_rs_finish");
+  comm::tp_rs_finish_kernel<<<tp_grid(a.B * (a.S / a.n) * (a.W / 8), 148 * 4), 256, 0, st>>>(
+      a, reinterpret_cast<__nv_bfloat16*>(out), ld_out);
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+void tp_ag_stage(const TpArgs& a, const void* shard, long long ld, cudaStream_t st) {
+  tp_check(a, ld, shard, "tp_ag_stage");
+  comm::tp_ag_stage_kernel<<<tp_grid(a.B * (a.S / a.n) * (a.W / 8), 148 * 4), 256, 0, st>>>(
+      a, reinterpret_cast<const __nv_bfloat16*>(shard), ld);
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+void tp_ag_pull(const TpArgs& a, void* out, long long ld_out, cudaStream_t st) {
+  tp_check(a, ld_out, out, "tp_ag_pull");
+  comm::tp_ag_pull_kernel<<<tp_grid(a.B * a.S * (a.W / 8) / 4, 148 * 4), 256, 0, st>>>(
+      a, reinterpret_cast<__nv_bfloat16*>(out), ld_out);
+  PLG_CUDA_CHECK(cudaGetLastError());
 }
 
 }  // namespace plg

@@ -51,7 +51,24 @@ struct Args {
   int m_tiles, n_tiles, k_blocks;
   int raster_m;      // 1: m-tiles vary fastest
   int* status;
+  // reduce-scatter epilogue (see GemmProblem)
+  int rs_n, rs_rank;
+  long long rs_S, rs_seg, rs_rows;
+  void* rs_dst[8];
 };
+
+// destination of row `row` under the reduce-scatter epilogue; static indices only
+// (a dynamically indexed kernel parameter would be copied to local memory)
+__device__ __forceinline__ __nv_bfloat16* rs_row_ptr(const Args& args, long long row) {
+  const long long b = row / args.rs_S, s = row - b * args.rs_S;
+  const int owner = static_cast<int>(s / args.rs_seg);
+  const long long lrow = b * args.rs_seg + (s - owner * args.rs_seg);
+  void* base = args.rs_dst[0];
+#pragma unroll
+  for (int j = 1; j < 8; ++j)
+    if (owner == j) base = args.rs_dst[j];
+  return reinterpret_cast<__nv_bfloat16*>(base) + (args.rs_rank * args.rs_rows + lrow) * args.ldc;
+}
 
 template <int BN>
 struct Cfg {
@@ -139,7 +156,8 @@ __device__ __forceinline__ void store_acc_row(const Args& args, uint32_t t_row, 
           if (col0 + i < args.N) cp[i] = v[i];
       }
     } else {
-      __nv_bfloat16* cp = reinterpret_cast<__nv_bfloat16*>(args.C) + row * args.ldc + col0;
+      __nv_bfloat16* cp = (args.rs_n ? rs_row_ptr(args, row)
+                                     : reinterpret_cast<__nv_bfloat16*>(args.C) + row * args.ldc) + col0;
       if (full) {
 #pragma unroll
         for (int i = 0; i < 32; i += 8) {
@@ -356,6 +374,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce_bar[buf]);
     }
+    // reduce-scatter epilogue: this thread's peer stores are visible system-wide
+    // before the kernel ends (the finishing kernel's flags then publish them)
+    if (args.rs_n) __threadfence_system();
   }
 
   __syncthreads();
@@ -594,6 +615,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(&acce_bar[buf], 0);
     }
+    if (args.rs_n) __threadfence_system();
   }
 
   __syncthreads();
@@ -656,6 +678,25 @@ static int choose_splits(int tiles, int slots, int k_blocks) {
   return best;
 }
 
+static void set_rs_fields(const GemmProblem& p, Args& a) {
+  a.rs_n = p.rs_n;
+  a.rs_rank = p.rs_rank;
+  a.rs_S = p.rs_S;
+  for (int j = 0; j < 8; ++j) a.rs_dst[j] = p.rs_dst[j];
+  if (!p.rs_n) return;
+  if (p.rs_n < 1 || p.rs_n > 8 || p.rs_rank < 0 || p.rs_rank >= p.rs_n)
+    throw std::invalid_argument("gemm reduce-scatter: 1..8 ranks");
+  if (p.c_fp32 || p.D != nullptr || p.splits > 1)
+    throw std::invalid_argument("gemm reduce-scatter: bf16 output without addend or split-K only");
+  if (p.rs_S <= 0 || p.M % p.rs_S || p.rs_S % p.rs_n || p.ldc != p.N)
+    throw std::invalid_argument("gemm reduce-scatter: M = B*S, S divisible by ranks, ldc == N");
+  for (int j = 0; j < p.rs_n; ++j)
+    if (p.rs_dst[j] == nullptr || (reinterpret_cast<uintptr_t>(p.rs_dst[j]) & 15))
+      throw std::invalid_argument("gemm reduce-scatter: staging buffers must be 16-byte aligned");
+  a.rs_seg = p.rs_S / p.rs_n;
+  a.rs_rows = p.M / p.rs_n;
+}
+
 template <int BN, bool A_MN, bool B_MN>
 static void launch(const GemmProblem& p, cudaStream_t stream) {
   using C_ = Cfg<BN>;
@@ -673,10 +714,12 @@ static void launch(const GemmProblem& p, cudaStream_t stream) {
   a.n_tiles = (p.N + BN - 1) / BN;
   a.k_blocks = (p.K + BK - 1) / BK;
   a.status = p.status;
+  set_rs_fields(p, a);
   const int sms = num_sms();
   const int tiles = a.m_tiles * a.n_tiles;
   int splits = p.splits;
   if (splits <= 0) splits = (p.c_fp32 && p.allow_split) ? choose_splits(tiles, sms, a.k_blocks) : 1;
+  if (p.rs_n) splits = 1;
   if (splits > a.k_blocks) splits = a.k_blocks;
   if (splits < 1) splits = 1;
   // every split must own at least one k-block
@@ -721,6 +764,7 @@ static void launch_pair(const GemmProblem& p, cudaStream_t stream) {
   a.n_tiles = (p.N + BN - 1) / BN;
   a.k_blocks = (p.K + BK - 1) / BK;
   a.status = p.status;
+  set_rs_fields(p, a);
   auto kern = gemm_pair_kernel<A_MN, B_MN>;
   set_max_smem_once(reinterpret_cast<const void*>(kern), C_::kSmemBytes);
   cudaLaunchConfig_t cfg = {};
@@ -746,6 +790,7 @@ static void launch_pair(const GemmProblem& p, cudaStream_t stream) {
   const int tiles = a.m_tiles * a.n_tiles;
   int splits = p.splits;
   if (splits <= 0) splits = (p.c_fp32 && p.allow_split) ? choose_splits(tiles, pairs, a.k_blocks) : 1;
+  if (p.rs_n) splits = 1;
   if (splits > a.k_blocks) splits = a.k_blocks;
   if (splits < 1) splits = 1;
   while (splits > 1 && (splits - 1) * ((a.k_blocks + splits - 1) / splits) >= a.k_blocks) --splits;

@@ -29,6 +29,13 @@ struct GemmProblem {
   bool allow_split = true;
   int bn = 0;               // 0 automatic, else 128 or 256
   int* status = nullptr;    // device status word (bounded waits)
+  // Reduce-scatter epilogue (tensor parallel, sequence-sharded output): rows are
+  // [B, S] flattened; row (b, s) belongs to rank s / (S / rs_n) and is stored as
+  // bf16 into that rank's staging buffer rs_dst[owner] at slot rs_rank:
+  // staging[rs_rank][b * S/rs_n + s % (S/rs_n)][N]. C is not written.
+  int rs_n = 0, rs_rank = 0;
+  long long rs_S = 0;
+  void* rs_dst[8] = {};
 };
 void gemm_bf16(const GemmProblem& p, cudaStream_t stream);
 
@@ -158,6 +165,27 @@ struct SymmAllReduceArgs {
 };
 // average data[offset, offset+numel) over the ranks in place on every rank; with
 // norm_sq, also (accumulate_norm ? += : =) the sum of squares of the averaged range
+// Tensor-parallel collectives over peer memory (sequence dimension of [B, S, W]
+// rows). Flags: each rank's flag words [kTpKinds][kSymmMaxRanks] in symmetric
+// memory; `epoch` grows by one per call of a kind; staging/send buffers are
+// double-buffered by the caller (epoch parity).
+constexpr int kTpKinds = 4;  // 0: reduce-scatter, 1: all-gather
+struct TpArgs {
+  int n = 1, rank = 0;
+  uint32_t epoch = 0;
+  int* status = nullptr;
+  uint32_t* flags[kSymmMaxRanks] = {};
+  void* bufs[kSymmMaxRanks] = {};  // every rank's staging (RS) or send (AG) buffer
+  long long B = 0, S = 0, W = 0;   // rows are [B, S] flattened, W bf16 columns
+};
+// RS: push this rank's partial [B*S, W] rows into every owner's staging slot
+void tp_rs_push(const TpArgs& a, const void* partial, long long ld, cudaStream_t stream);
+// RS: signal, wait for every peer, out[B*S/n, W] = sum over slots of own staging
+void tp_rs_finish(const TpArgs& a, void* out, long long ld_out, cudaStream_t stream);
+// AG: copy this rank's shard [B*S/n, W] into its send buffer (bufs[rank])
+void tp_ag_stage(const TpArgs& a, const void* shard, long long ld, cudaStream_t stream);
+// AG: signal, wait for every peer, gather every rank's send buffer into out [B*S, W]
+void tp_ag_pull(const TpArgs& a, void* out, long long ld_out, cudaStream_t stream);
 void symm_allreduce_avg(const SymmAllReduceArgs& a, float* norm_sq, bool accumulate_norm,
                         cudaStream_t stream);
 

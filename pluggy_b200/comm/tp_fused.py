@@ -1,0 +1,163 @@
+"""Tensor-parallel collectives over NVLink peer memory, and the fused
+GEMM -> reduce-scatter of the row-parallel linears.
+
+Sequence parallelism moves activations between "each rank holds ``S / n`` of every
+sequence" and "every rank holds all of it". Here both directions run on this
+package's kernels (``csrc/comm.cu``, ``csrc/gemm_tcgen05.cu``) instead of NCCL:
+
+* reduce-scatter: each rank stores its partial rows straight into the owning
+  rank's staging slot with peer stores, then a finishing kernel signals the
+  peers, waits (bounded) for theirs and sums the slots in a fixed order;
+* fused GEMM -> reduce-scatter (row-parallel ``o_proj`` / ``down_proj``): the
+  tcgen05 GEMM's epilogue writes each output row directly into its owner's
+  staging slot over NVLink, so the transfer overlaps the GEMM tile by tile and
+  the partial product never lands in local memory;
+* all-gather: each rank stages its shard in its symmetric send buffer, signals,
+  and pulls every peer's shard with peer loads.
+
+Staging and send buffers are double-buffered by call parity; a rank cannot start
+call ``e + 2`` of a kind before every peer has signalled call ``e + 1``, which each
+peer does only after it finished reading call ``e``'s buffer, so two halves
+suffice. Flags hold monotonically growing epochs (no reset between calls).
+The buffers grow on demand (a collective step: every rank makes the same calls).
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from pluggy_b200.comm.symm import SymmetricBuffer
+from pluggy_b200.ops._ext import ext, status_word
+
+_RS, _AG = 0, 1
+_FLAG_BYTES = 4 * 8 * 4  # kinds x ranks x uint32
+
+
+class TPComm:
+    def __init__(self, mesh, dim: str, capacity_bytes: int = 32 << 20):
+        self.mesh, self.dim = mesh, dim
+        self.n, self.rank = mesh.size(dim), mesh.coordinate(dim)
+        self.flags = SymmetricBuffer(_FLAG_BYTES, mesh, dim)
+        self.cap = {_RS: 0, _AG: 0}
+        self.buf = {_RS: None, _AG: None}
+        self.epoch = {_RS: 0, _AG: 0}
+        self._grow(_RS, capacity_bytes)
+        self._grow(_AG, capacity_bytes // self.n)
+
+    def _grow(self, kind: int, half_bytes: int) -> None:
+        half = (int(half_bytes) + 4095) // 4096 * 4096
+        if half <= self.cap[kind]:
+            return
+        old = self.buf[kind]
+        if old is not None:
+            # peers may still read or write the old buffer: quiesce the axis first
+            torch.cuda.synchronize()
+            dist.barrier(group=self.mesh.get_group(self.dim))
+            old.close()
+        self.buf[kind] = SymmetricBuffer(2 * half, self.mesh, self.dim)
+        self.cap[kind] = half
+
+    def _args(self, kind: int, need: int):
+        self._grow(kind, need)
+        self.epoch[kind] += 1
+        e = self.epoch[kind]
+        off = (e % 2) * self.cap[kind]
+        bufs = [p + off for p in self.buf[kind].peers]
+        return self.flags.peers, bufs, e
+
+    # ------------------------------------------------------------ collectives
+    def reduce_scatter_seq(self, partial: torch.Tensor) -> torch.Tensor:
+        """[B, S, W] partial sums (bf16) -> this rank's summed [B, S / n, W]."""
+        B, S, W = partial.shape
+        p2 = partial.reshape(B * S, W).to(torch.bfloat16).contiguous()
+        flags, bufs, e = self._args(_RS, p2.numel() * 2)
+        out = torch.empty((B * (S // self.n), W), dtype=torch.bfloat16, device=partial.device)
+        st = status_word(partial.device)
+        ext().tp_collective("rs_push", p2, flags, bufs, self.rank, e, B, S, st)
+        ext().tp_collective("rs_finish", out, flags, bufs, self.rank, e, B, S, st)
+        return out.view(B, S // self.n, W)
+
+    def all_gather_seq(self, shard: torch.Tensor) -> torch.Tensor:
+        """[B, S / n, W] (bf16) -> [B, S, W] on every rank."""
+        B, s, W = shard.shape
+        S = s * self.n
+        x2 = shard.reshape(B * s, W).to(torch.bfloat16).contiguous()
+        flags, bufs, e = self._args(_AG, x2.numel() * 2)
+        out = torch.empty((B * S, W), dtype=torch.bfloat16, device=shard.device)
+        st = status_word(shard.device)
+        ext().tp_collective("ag_stage", x2, flags, bufs, self.rank, e, B, S, st)
+        ext().tp_collective("ag_pull", out, flags, bufs, self.rank, e, B, S, st)
+        return out.view(B, S, W)
+
+    def gemm_reduce_scatter(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """``(x [B, S, K] @ w [N, K]^T)`` summed over the axis, sequence-sharded:
+        [B, S / n, N]. One tcgen05 GEMM whose epilogue stores into the owners'
+        staging slots, then the finishing kernel."""
+        B, S, K = x.shape
+        N = w.shape[0]
+        x2 = x.reshape(B * S, K).to(torch.bfloat16).contiguous()
+        flags, bufs, e = self._args(_RS, B * S * N * 2)
+        st = status_word(x.device)
+        ext().gemm_rs(x2, w, False, bufs, self.rank, S, st)
+        out = torch.empty((B * (S // self.n), N), dtype=torch.bfloat16, device=x.device)
+        ext().tp_collective("rs_finish", out, flags, bufs, self.rank, e, B, S, st)
+        return out.view(B, S // self.n, N)
+
+    def close(self) -> None:
+        for b in (self.buf[_RS], self.buf[_AG], self.flags):
+            if b is not None:
+                b.close()
+
+
+# ------------------------------------------------------------------ autograd
+class GatherSeq(torch.autograd.Function):
+    """[B, S/n, W] -> [B, S, W] (bf16) forward; reduce-scatter of the grad backward."""
+
+    @staticmethod
+    def forward(ctx, x, comm):
+        ctx.comm, ctx.dtype = comm, x.dtype
+        return comm.all_gather_seq(x)
+
+    @staticmethod
+    def backward(ctx, g):
+        return ctx.comm.reduce_scatter_seq(g.contiguous()).to(ctx.dtype), None
+
+
+class ScatterSeq(torch.autograd.Function):
+    """Partial [B, S, W] -> this rank's reduced [B, S/n, W]; all-gather backward."""
+
+    @staticmethod
+    def forward(ctx, x, comm):
+        ctx.comm, ctx.dtype = comm, x.dtype
+        return comm.reduce_scatter_seq(x)
+
+    @staticmethod
+    def backward(ctx, g):
+        return ctx.comm.all_gather_seq(g.contiguous()).to(ctx.dtype), None
+
+
+class RowParallelMMRS(torch.autograd.Function):
+    """Row-parallel linear with the sequence reduce-scatter fused into the GEMM.
+
+    forward: y[B, S/n, N] = RS(x[B, S, K/n] @ W_shard^T);
+    backward: g = AG(dy) [B, S, N]; dx = g @ W_shard; dW = g^T x."""
+
+    @staticmethod
+    def forward(ctx, x, weight, comm):
+        w = weight.to(torch.bfloat16).contiguous()
+        ctx.comm, ctx.x_dtype = comm, x.dtype
+        x16 = x.to(torch.bfloat16).contiguous()
+        ctx.save_for_backward(x16, w)
+        return comm.gemm_reduce_scatter(x16, w)
+
+    @staticmethod
+    def backward(ctx, dy):
+        from pluggy_b200.ops.gemm import linear_dgrad, linear_wgrad
+
+        x16, w = ctx.saved_tensors
+        B, S, K = x16.shape
+        g = ctx.comm.all_gather_seq(dy.contiguous()).reshape(B * S, -1)
+        dx = linear_dgrad(g, w).view(B, S, K).to(ctx.x_dtype)
+        dw = linear_wgrad(g, x16.reshape(B * S, K))
+        return dx, dw, None

@@ -49,7 +49,8 @@ class _FusedLinearCE(torch.autograd.Function):
             V = w.shape[0]
             loss_sum = torch.zeros(1, dtype=torch.float32, device=dev)
             grad_h = torch.empty((N, D), dtype=torch.bfloat16, device=dev)
-            grad_w = torch.zeros((V, D), dtype=torch.float32, device=dev) if need_w else None
+            # the first chunk's wgrad GEMM writes grad_w (beta = 0), later ones accumulate
+            grad_w = torch.empty((V, D), dtype=torch.float32, device=dev) if need_w else None
             logits = torch.empty((min(chunk_size, N), V), dtype=torch.bfloat16, device=dev)
             lab = labels.contiguous()
             for s in range(0, N, chunk_size):
@@ -60,8 +61,10 @@ class _FusedLinearCE(torch.autograd.Function):
                               loss_sum, None)
                 gemm(lg, w, b_mn_major=True, out=grad_h[s:e])
                 if need_w:
-                    gemm(lg, h[s:e], a_mn_major=True, b_mn_major=True, out=grad_w, addend=grad_w,
-                         beta=1.0)
+                    gemm(lg, h[s:e], a_mn_major=True, b_mn_major=True, out=grad_w,
+                         addend=grad_w if s > 0 else None, beta=1.0)
+            if N == 0 and grad_w is not None:
+                grad_w.zero_()
             loss_sum = loss_sum[0]
             grad_h = grad_h.to(hidden.dtype)
         else:

@@ -14,6 +14,12 @@ module implements (``notes/ROADMAP.md:327-378`` of the reference):
 * sequence parallelism on the norms and the residual stream: between sublayers
   every rank holds ``S / tp`` of the tokens.
 
+On CUDA with sequence parallelism the sequence collectives run on this package's
+peer-memory kernels (:mod:`pluggy_b200.comm.tp_fused`): the row-parallel linears
+are one tcgen05 GEMM whose epilogue reduce-scatters into the owners' staging
+buffers over NVLink, and the column-parallel inputs are gathered with peer loads.
+All projections use the sm_100a GEMMs (:func:`pluggy_b200.ops.linear.linear`).
+
 Weights are initialised full on every rank (same seed) and sliced here, so a TP
 run starts from the same model as a single-GPU run. Parameters that stay
 replicated across the axis (norm weights, per-head q/k norms) get their gradients
@@ -28,6 +34,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from pluggy_b200.core.collective import all_gather, all_reduce, reduce_scatter
+from pluggy_b200.ops.linear import linear
 
 
 # ------------------------------------------------------------------ collectives
@@ -85,15 +92,21 @@ class _SharedInput:
     forward gathers once and autograd sums the branches' grads before the single
     backward reduction."""
 
-    def __init__(self, mesh, dim: str, sequence_parallel: bool):
-        self.mesh, self.dim, self.sp = mesh, dim, sequence_parallel
+    def __init__(self, mesh, dim: str, sequence_parallel: bool, comm=None):
+        self.mesh, self.dim, self.sp, self.comm = mesh, dim, sequence_parallel, comm
         self._src = None
         self._out = None
 
     def __call__(self, x):
         if x is not self._src:
-            self._out = (_GatherSeq.apply(x, self.mesh, self.dim) if self.sp
-                         else _CopyTo.apply(x, self.mesh, self.dim))
+            if self.sp and self.comm is not None:
+                from pluggy_b200.comm.tp_fused import GatherSeq
+
+                self._out = GatherSeq.apply(x, self.comm)
+            elif self.sp:
+                self._out = _GatherSeq.apply(x, self.mesh, self.dim)
+            else:
+                self._out = _CopyTo.apply(x, self.mesh, self.dim)
             self._src = x
         return self._out
 
@@ -113,13 +126,13 @@ class ColumnParallelLinear(nn.Module):
         self._enter = shared if shared is not None else _SharedInput(mesh, dim, sequence_parallel)
 
     def forward(self, x):
-        return F.linear(self._enter(x), self.weight)
+        return linear(self._enter(x), self.weight)
 
 
 class RowParallelLinear(nn.Module):
     """Partial x[..., in/tp] W_shard^T summed over the axis (reduce-scatter with SP)."""
 
-    def __init__(self, full: nn.Linear, mesh, dim: str, sequence_parallel: bool):
+    def __init__(self, full: nn.Linear, mesh, dim: str, sequence_parallel: bool, comm=None):
         super().__init__()
         n, r = mesh.size(dim), mesh.coordinate(dim)
         inp = full.weight.shape[1]
@@ -127,9 +140,14 @@ class RowParallelLinear(nn.Module):
         k = inp // n
         self.weight = nn.Parameter(full.weight.detach()[:, r * k:(r + 1) * k].clone())
         self.mesh, self.dim, self.sp = mesh, dim, sequence_parallel
+        self.comm = comm
 
     def forward(self, x):
-        y = F.linear(x, self.weight)
+        if self.sp and self.comm is not None and x.dim() == 3:
+            from pluggy_b200.comm.tp_fused import RowParallelMMRS
+
+            return RowParallelMMRS.apply(x, self.weight, self.comm)
+        y = linear(x, self.weight)
         return _ScatterSeq.apply(y, self.mesh, self.dim) if self.sp else _ReduceFrom.apply(y, self.mesh, self.dim)
 
 
@@ -228,6 +246,12 @@ class TensorParallel:
         self.sharded: list[nn.Parameter] = []
         self.replicated: list[nn.Parameter] = []  # replicated params with partial grads
         self.vstart = 0
+        self.comm = None  # peer-memory collectives (CUDA + sequence parallel)
+
+    def close(self) -> None:
+        if self.comm is not None:
+            self.comm.close()
+            self.comm = None
 
     @torch.no_grad()
     def sync_replicated_grads(self) -> None:
@@ -290,12 +314,26 @@ def _attention_modules(block):
     raise ValueError(f"no attention module with q_proj in {type(block).__name__}")
 
 
-def parallelize_tp(model: nn.Module, mesh, dim: str = "tp", sequence_parallel: bool = True) -> TensorParallel:
+def parallelize_tp(model: nn.Module, mesh, dim: str = "tp", sequence_parallel: bool = True,
+                   fused: bool | None = None) -> TensorParallel:
     """Shard ``model`` (a decoder with ``token_emb``, ``blocks``, ``norm``, ``lm_head``)
     over mesh axis ``dim``; returns the :class:`TensorParallel` handle (also stored
-    as ``model.tp``). Heads, FFN width and vocabulary must divide by the axis size."""
+    as ``model.tp``). Heads, FFN width and vocabulary must divide by the axis size.
+    ``fused`` (default: on CUDA with sequence parallelism) selects the peer-memory
+    collectives and the fused GEMM -> reduce-scatter."""
     n = mesh.size(dim)
     tp = TensorParallel(model, mesh, dim, sequence_parallel)
+    on_cuda = next(model.parameters()).is_cuda
+    if fused is None:
+        fused = on_cuda and sequence_parallel and n > 1
+    comm = None
+    if fused and n > 1:
+        if not (on_cuda and sequence_parallel):
+            raise ValueError("fused tensor-parallel collectives need CUDA and sequence parallelism")
+        from pluggy_b200.comm.tp_fused import TPComm
+
+        comm = TPComm(mesh, dim)
+    tp.comm = comm
     if n == 1:
         model.tp = tp
         tp.replicated = []
@@ -306,18 +344,18 @@ def parallelize_tp(model: nn.Module, mesh, dim: str = "tp", sequence_parallel: b
         _, att = _attention_modules(blk)
         assert att.num_heads % n == 0 and att.num_kv_heads % n == 0, \
             f"tp={n} must divide the query ({att.num_heads}) and KV ({att.num_kv_heads}) heads"
-        qkv_in = _SharedInput(mesh, dim, sequence_parallel)
+        qkv_in = _SharedInput(mesh, dim, sequence_parallel, comm)
         att.q_proj = ColumnParallelLinear(att.q_proj, mesh, dim, sequence_parallel, qkv_in)
         att.k_proj = ColumnParallelLinear(att.k_proj, mesh, dim, sequence_parallel, qkv_in)
         att.v_proj = ColumnParallelLinear(att.v_proj, mesh, dim, sequence_parallel, qkv_in)
-        att.o_proj = RowParallelLinear(att.o_proj, mesh, dim, sequence_parallel)
+        att.o_proj = RowParallelLinear(att.o_proj, mesh, dim, sequence_parallel, comm)
         att.num_heads //= n
         att.num_kv_heads //= n
         ffn = blk.ffn
-        gu_in = _SharedInput(mesh, dim, sequence_parallel)
+        gu_in = _SharedInput(mesh, dim, sequence_parallel, comm)
         ffn.gate_proj = ColumnParallelLinear(ffn.gate_proj, mesh, dim, sequence_parallel, gu_in)
         ffn.up_proj = ColumnParallelLinear(ffn.up_proj, mesh, dim, sequence_parallel, gu_in)
-        ffn.down_proj = RowParallelLinear(ffn.down_proj, mesh, dim, sequence_parallel)
+        ffn.down_proj = RowParallelLinear(ffn.down_proj, mesh, dim, sequence_parallel, comm)
     emb = VocabParallelEmbedding(model.token_emb, mesh, dim, sequence_parallel)
     model.token_emb = emb
     if tied:

@@ -153,8 +153,10 @@ class Trainer:
         if sizes.get("tp", 1) > 1:
             from pluggy_b200.parallel.tensor_parallel import parallelize_tp
 
-            self.tp = parallelize_tp(model, self.mesh, "tp", sequence_parallel=self.config.get(
-                "tp", {}).get("sequence_parallel", True))
+            tp_cfg = self.config.get("tp", {})
+            self.tp = parallelize_tp(model, self.mesh, "tp",
+                                     sequence_parallel=tp_cfg.get("sequence_parallel", True),
+                                     fused=tp_cfg.get("fused"))
         self.cp = None
         if sizes.get("cp", 1) > 1:
             from pluggy_b200.parallel.context_parallel import parallelize_cp

@@ -100,3 +100,93 @@ def _ddp_case(rank, world):
 def test_fused_ddp_matches_nccl_ddp():
     _need(2)
     run_ranks(_ddp_case, 2, backend="nccl")
+
+
+def _tp_collectives_case(rank, world):
+    import torch.distributed as dist
+
+    from pluggy_b200.comm.tp_fused import TPComm
+    from pluggy_b200.core.mesh import Mesh
+    from pluggy_b200.ops import _ext
+
+    mesh = Mesh({"tp": world})
+    comm = TPComm(mesh, "tp", capacity_bytes=1 << 20)  # small: forces a regrow below
+    bad = []
+    g = torch.Generator(device="cuda").manual_seed(100 + rank)
+    for it, (B, S, W) in enumerate([(2, 256, 512), (1, 1024, 256), (2, 256, 512), (3, 64, 1024),
+                                    (2, 2048, 1024)]):
+        part = torch.randn(B, S, W, device="cuda", generator=g).bfloat16()
+        got = comm.reduce_scatter_seq(part)
+        full = part.float()
+        dist.all_reduce(full)
+        want = full.view(B, world, S // world, W)[:, rank]
+        err = (got.float() - want).abs().max().item()
+        if err > 0.05 * want.abs().max().item():
+            bad.append(("rs", it, err))
+        shard = torch.randn(B, S // world, W, device="cuda", generator=g).bfloat16()
+        gathered = comm.all_gather_seq(shard)
+        parts = [torch.empty_like(shard) for _ in range(world)]
+        dist.all_gather(parts, shard.contiguous())
+        ref = torch.cat(parts, dim=1)
+        if not torch.equal(gathered, ref):
+            bad.append(("ag", it))
+        # fused GEMM -> reduce-scatter against GEMM + NCCL reduce-scatter
+        K, N = 256, W
+        x = torch.randn(B, S, K, device="cuda", generator=g).bfloat16()
+        w = torch.randn(N, K, device="cuda", generator=g).bfloat16() * 0.05
+        y = comm.gemm_reduce_scatter(x, w)
+        yf = (x.float().reshape(-1, K) @ w.float().t()).view(B, S, N)
+        dist.all_reduce(yf)
+        want = yf.view(B, world, S // world, N)[:, rank]
+        rel = ((y.float() - want).norm() / want.norm()).item()
+        if rel > 1e-2:
+            bad.append(("gemm_rs", it, rel))
+    torch.cuda.synchronize()
+    _ext.check_status()
+    comm.close()
+    assert not bad, bad
+
+
+def test_tp_peer_collectives_match_nccl():
+    _need(2)
+    run_ranks(_tp_collectives_case, 2, backend="nccl")
+
+
+def _tp_model_case(rank, world):
+    from pluggy_b200.core.mesh import Mesh
+    from pluggy_b200.models.qwen3 import Qwen3
+    from pluggy_b200.objectives.autoregressive import ARObjective
+    from pluggy_b200.ops import _ext
+    from pluggy_b200.parallel.tensor_parallel import parallelize_tp
+
+    mesh = Mesh({"tp": world})
+    cfg = dict(num_layers=2, num_heads=8, num_kv_heads=4, emb_dim=512, head_dim=64, vocab_size=4096,
+               ffn_dim=1024, tie_embeddings=True)
+    losses, grads = {}, {}
+    ids = torch.randint(0, 4096, (2, 512), generator=torch.Generator().manual_seed(0)).cuda()
+    for fused in (False, True):
+        torch.manual_seed(0)
+        m = Qwen3(**cfg).cuda()
+        m.init_weights()
+        tp = parallelize_tp(m, mesh, "tp", sequence_parallel=True, fused=fused)
+        loss = ARObjective(ce_chunk_size=512).compute_loss(m, {"input_ids": ids, "labels": ids})
+        loss.backward()
+        tp.sync_replicated_grads()
+        losses[fused] = float(loss)
+        grads[fused] = {n: p.grad.float().clone() for n, p in m.named_parameters() if p.grad is not None}
+        tp.close()
+    torch.cuda.synchronize()
+    _ext.check_status()
+    assert abs(losses[True] - losses[False]) < 2e-2 * abs(losses[False]), losses
+    bad = []
+    for n, gref in grads[False].items():
+        gf = grads[True][n]
+        rel = ((gf - gref).norm() / (gref.norm() + 1e-12)).item()
+        if rel > 5e-2:
+            bad.append((n, rel))
+    assert not bad, bad
+
+
+def test_tp2_fused_model_matches_nccl_path():
+    _need(2)
+    run_ranks(_tp_model_case, 2, backend="nccl")
