@@ -471,12 +471,12 @@ void tp_collective(const std::string& op, const at::Tensor& t, std::vector<int64
   } else if (op == "rs_finish") {
     TORCH_CHECK(t.size(0) == part, "rs_finish: out must be [B*S/n, W]");
     plg::tp_rs_finish(a, t.data_ptr(), t.stride(0), cur_stream());
-  } else if (op == "ag_stage") {
-    TORCH_CHECK(t.size(0) == part, "ag_stage: shard must be [B*S/n, W]");
-    plg::tp_ag_stage(a, t.data_ptr(), t.stride(0), cur_stream());
-  } else if (op == "ag_pull") {
-    TORCH_CHECK(t.size(0) == full, "ag_pull: out must be [B*S, W]");
-    plg::tp_ag_pull(a, t.data_ptr(), t.stride(0), cur_stream());
+  } else if (op == "ag_push") {
+    TORCH_CHECK(t.size(0) == part, "ag_push: shard must be [B*S/n, W]");
+    plg::tp_ag_push(a, t.data_ptr(), t.stride(0), cur_stream());
+  } else if (op == "ag_finish") {
+    TORCH_CHECK(t.size(0) == full, "ag_finish: out must be [B*S, W]");
+    plg::tp_ag_finish(a, t.data_ptr(), t.stride(0), cur_stream());
   } else {
     TORCH_CHECK(false, "tp collective: unknown op ", op);
   }

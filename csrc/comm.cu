@@ -251,50 +251,38 @@ __global__ void __launch_bounds__(256) tp_rs_finish_kernel(TpArgs a, __nv_bfloat
   }
 }
 
-__global__ void __launch_bounds__(256) tp_ag_stage_kernel(TpArgs a, const __nv_bfloat16* __restrict__ shard,
-                                                          long long ld) {
+// AG: this rank's shard rows go into slot `rank` of EVERY rank's receive buffer
+// (peer stores are posted over NVLink: pushing beats pulling with loads)
+__global__ void __launch_bounds__(256) tp_ag_push_kernel(TpArgs a, const __nv_bfloat16* __restrict__ shard,
+                                                         long long ld) {
   const long long rows = a.B * (a.S / a.n), g8 = a.W / 8, total = rows * g8;
-  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(tp_buf(a, a.rank)));
   for (long long g = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; g < total;
        g += static_cast<long long>(gridDim.x) * blockDim.x) {
     const long long r = g / g8;
     const long long c = (g - r * g8) * 8;
-    *reinterpret_cast<uint4*>(dst + r * a.W + c) = *reinterpret_cast<const uint4*>(shard + r * ld + c);
+    const uint4 v = *reinterpret_cast<const uint4*>(shard + r * ld + c);
+    for (int p = 0; p < a.n; ++p) {
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(tp_buf(a, (a.rank + p) % a.n)));
+      *reinterpret_cast<uint4*>(dst + (a.rank * rows + r) * a.W + c) = v;
+    }
   }
   __threadfence_system();
 }
 
-__global__ void __launch_bounds__(256) tp_ag_pull_kernel(TpArgs a, __nv_bfloat16* __restrict__ out,
-                                                         long long ld_out) {
+// AG: signal, wait for every peer's push, then copy the n slots into [B, S] order
+__global__ void __launch_bounds__(256) tp_ag_finish_kernel(TpArgs a, __nv_bfloat16* __restrict__ out,
+                                                           long long ld_out) {
   if (!tp_handshake(a, 1)) return;
   const TpMap m{a.S, a.S / a.n, a.B * (a.S / a.n)};
   const long long g8 = a.W / 8, per = m.rows * g8, total = a.n * per;
-  constexpr int U = 4;  // four 16-byte peer loads in flight per thread
-  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-  for (long long g0 = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; g0 < total;
-       g0 += U * stride) {
-    uint4 v[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const long long g = g0 + u * stride;
-      if (g < total) {
-        const int p = static_cast<int>(g / per);
-        const long long rem = g - p * per;
-        const long long lrow = rem / g8, c = (rem - lrow * g8) * 8;
-        v[u] = *reinterpret_cast<const uint4*>(
-            reinterpret_cast<const __nv_bfloat16*>(tp_buf(a, p)) + lrow * a.W + c);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const long long g = g0 + u * stride;
-      if (g < total) {
-        const int p = static_cast<int>(g / per);
-        const long long rem = g - p * per;
-        const long long lrow = rem / g8, c = (rem - lrow * g8) * 8;
-        *reinterpret_cast<uint4*>(out + m.join(p, lrow) * ld_out + c) = v[u];
-      }
-    }
+  const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(tp_buf(a, a.rank));
+  for (long long g = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; g < total;
+       g += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int p = static_cast<int>(g / per);
+    const long long rem = g - p * per;
+    const long long lrow = rem / g8, c = (rem - lrow * g8) * 8;
+    *reinterpret_cast<uint4*>(out + m.join(p, lrow) * ld_out + c) =
+        *reinterpret_cast<const uint4*>(rb + (p * m.rows + lrow) * a.W + c);
   }
 }
 
@@ -372,16 +360,16 @@ void tp_rs_finish(const TpArgs& a, void* out, long long ld_out, cudaStream_t st)
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 
-void tp_ag_stage(const TpArgs& a, const void* shard, long long ld, cudaStream_t st) {
-  tp_check(a, ld, shard, "tp_ag_stage");
-  comm::tp_ag_stage_kernel<<<tp_grid(a.B * (a.S / a.n) * (a.W / 8), 148 * 4), 256, 0, st>>>(
+void tp_ag_push(const TpArgs& a, const void* shard, long long ld, cudaStream_t st) {
+  tp_check(a, ld, shard, "tp_ag_push");
+  comm::tp_ag_push_kernel<<<tp_grid(a.B * (a.S / a.n) * (a.W / 8), 148 * 4), 256, 0, st>>>(
       a, reinterpret_cast<const __nv_bfloat16*>(shard), ld);
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 
-void tp_ag_pull(const TpArgs& a, void* out, long long ld_out, cudaStream_t st) {
-  tp_check(a, ld_out, out, "tp_ag_pull");
-  comm::tp_ag_pull_kernel<<<tp_grid(a.B * a.S * (a.W / 8) / 4, 148 * 4), 256, 0, st>>>(
+void tp_ag_finish(const TpArgs& a, void* out, long long ld_out, cudaStream_t st) {
+  tp_check(a, ld_out, out, "tp_ag_finish");
+  comm::tp_ag_finish_kernel<<<tp_grid(a.B * a.S * (a.W / 8), 148 * 8), 256, 0, st>>>(
       a, reinterpret_cast<__nv_bfloat16*>(out), ld_out);
   PLG_CUDA_CHECK(cudaGetLastError());
 }

@@ -70,6 +70,9 @@ __device__ __forceinline__ __nv_bfloat16* rs_row_ptr(const Args& args, long long
   return reinterpret_cast<__nv_bfloat16*>(base) + (args.rs_rank * args.rs_rows + lrow) * args.ldc;
 }
 
+// per epilogue warp: a 32 x 64 bf16 chunk for the reduce-scatter epilogue
+constexpr int kEpiStageBytes = 4 * 32 * 128;
+
 template <int BN>
 struct Cfg {
   static constexpr int kStages = (BN == 256) ? 4 : 6;
@@ -77,14 +80,67 @@ struct Cfg {
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BN;  // 256 or 512: a power of two
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ +
+                                    kEpiStageBytes;
 };
 
 // Epilogue of one accumulator row (this thread's TMEM lane): BN fp32 columns at
 // t_row -> alpha * acc (+ beta * D) -> C (bf16 / fp32 / split-K fp32 atomics).
+// Reduce-scatter epilogue of one warp's 32 accumulator rows: the rows go to a
+// peer's staging buffer over NVLink, where 16-byte stores scattered over 32 rows
+// would waste most of each link transaction. So the warp writes each 32 x 64
+// chunk (bf16) into its shared-memory slot (16-byte groups XOR-swizzled against
+// bank conflicts) and stores it back out row-contiguously: 8 lanes cover one
+// row's 128 bytes, 4 rows per instruction. A warp's 32 rows lie in one sequence
+// segment (segment length % 32 == 0), so they are consecutive rows of one owner.
+template <int BN>
+__device__ __forceinline__ void store_acc_rows_rs(const Args& args, uint32_t t_row, long long row,
+                                                  int col_base, uint8_t* stage) {
+  const int lane = threadIdx.x & 31;
+  const long long row_base = row - lane;
+  if (row_base >= args.M) return;  // warp-uniform
+  __nv_bfloat16* wbase = rs_row_ptr(args, row_base);
+#pragma unroll 1
+  for (int cp = 0; cp < BN / 64; ++cp) {
+    uint32_t u[32];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t r[32];
+      __syncwarp();
+      tmem_ld_32x32b_x32(t_row + (cp * 2 + h) * 32, r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        u[h * 16 + i] = pack_bf16x2(__uint_as_float(r[2 * i]) * args.alpha,
+                                    __uint_as_float(r[2 * i + 1]) * args.alpha);
+    }
+    uint4* srow = reinterpret_cast<uint4*>(stage + lane * 128);
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      srow[k ^ (lane & 7)] = make_uint4(u[4 * k], u[4 * k + 1], u[4 * k + 2], u[4 * k + 3]);
+    __syncwarp();
+    const int col0 = col_base + cp * 64;
+    const int k = lane & 7;
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int rl = it * 4 + (lane >> 3);
+      const int col = col0 + k * 8;
+      if (row_base + rl < args.M && col < args.N) {
+        const uint4 v = reinterpret_cast<const uint4*>(stage + rl * 128)[k ^ (rl & 7)];
+        *reinterpret_cast<uint4*>(wbase + rl * args.ldc + col) = v;
+      }
+    }
+  }
+  __syncwarp();
+}
+
 template <int BN>
 __device__ __forceinline__ void store_acc_row(const Args& args, uint32_t t_row, long long row,
-                                              bool row_ok, int col_base, int kb0) {
+                                              bool row_ok, int col_base, int kb0, uint8_t* stage) {
+  if (args.rs_n) {
+    store_acc_rows_rs<BN>(args, t_row, row, col_base, stage);
+    return;
+  }
 #pragma unroll 1
   for (int c = 0; c < BN / 32; ++c) {
     uint32_t r[32];
@@ -195,6 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* done_bar = bar + 2 * C_::kStages + 4;  // [1]
   uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(bar + 2 * C_::kStages + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_smem + 1);
+  uint8_t* epi_stage = smem + C_::kStages * C_::kStageBytes + 256;  // [4 warps][32][128 B]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -369,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const long long row = (long long)mt * BM + row_in_tile;
       const bool row_ok = row < args.M;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
-      store_acc_row<BN>(args, t_row, row, row_ok, nt * BN, kb0);
+      store_acc_row<BN>(args, t_row, row, row_ok, nt * BN, kb0, epi_stage + q * 32 * 128);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce_bar[buf]);
@@ -404,7 +461,7 @@ struct PairCfg {
   static constexpr int kBBytes = 128 * BK * 2;   // 16 KB: this CTA's 128 of 256 columns
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BN;       // two 128 x 256 fp32 accumulators per CTA
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256 + kEpiStageBytes;
 };
 
 template <bool A_MN, bool B_MN>
@@ -425,6 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* done_bar = bar + 2 * C_::kStages + 4;
   uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(bar + 2 * C_::kStages + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_smem + 1);
+  uint8_t* epi_stage = smem + C_::kStages * C_::kStageBytes + 256;  // [4 warps][32][128 B]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -610,7 +668,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const long long row = (long long)mt * 2 * BM + rank * BM + row_in_tile;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
-      store_acc_row<BN>(args, t_row, row, row < args.M, nt * BN, kb0);
+      store_acc_row<BN>(args, t_row, row, row < args.M, nt * BN, kb0, epi_stage + q * 32 * 128);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(&acce_bar[buf], 0);
@@ -695,6 +753,8 @@ static void set_rs_fields(const GemmProblem& p, Args& a) {
       throw std::invalid_argument("gemm reduce-scatter: staging buffers must be 16-byte aligned");
   a.rs_seg = p.rs_S / p.rs_n;
   a.rs_rows = p.M / p.rs_n;
+  if (a.rs_seg % 32 || p.N % 8)
+    throw std::invalid_argument("gemm reduce-scatter: S / ranks a multiple of 32, N a multiple of 8");
 }
 
 template <int BN, bool A_MN, bool B_MN>

@@ -182,10 +182,10 @@ struct TpArgs {
 void tp_rs_push(const TpArgs& a, const void* partial, long long ld, cudaStream_t stream);
 // RS: signal, wait for every peer, out[B*S/n, W] = sum over slots of own staging
 void tp_rs_finish(const TpArgs& a, void* out, long long ld_out, cudaStream_t stream);
-// AG: copy this rank's shard [B*S/n, W] into its send buffer (bufs[rank])
-void tp_ag_stage(const TpArgs& a, const void* shard, long long ld, cudaStream_t stream);
-// AG: signal, wait for every peer, gather every rank's send buffer into out [B*S, W]
-void tp_ag_pull(const TpArgs& a, void* out, long long ld_out, cudaStream_t stream);
+// AG: push this rank's shard [B*S/n, W] into slot `rank` of every rank's receive buffer
+void tp_ag_push(const TpArgs& a, const void* shard, long long ld, cudaStream_t stream);
+// AG: signal, wait for every peer, copy the slots of the own receive buffer into out [B*S, W]
+void tp_ag_finish(const TpArgs& a, void* out, long long ld_out, cudaStream_t stream);
 void symm_allreduce_avg(const SymmAllReduceArgs& a, float* norm_sq, bool accumulate_norm,
                         cudaStream_t stream);
 

@@ -12,10 +12,11 @@ package's kernels (``csrc/comm.cu``, ``csrc/gemm_tcgen05.cu``) instead of NCCL:
   tcgen05 GEMM's epilogue writes each output row directly into its owner's
   staging slot over NVLink, so the transfer overlaps the GEMM tile by tile and
   the partial product never lands in local memory;
-* all-gather: each rank stages its shard in its symmetric send buffer, signals,
-  and pulls every peer's shard with peer loads.
+* all-gather: each rank pushes its shard into its slot of every rank's receive
+  buffer with peer stores (posted writes beat round-trip loads over NVLink),
+  signals, and copies the slots of its own receive buffer into sequence order.
 
-Staging and send buffers are double-buffered by call parity; a rank cannot start
+Staging and receive buffers are double-buffered by call parity; a rank cannot start
 call ``e + 2`` of a kind before every peer has signalled call ``e + 1``, which each
 peer does only after it finished reading call ``e``'s buffer, so two halves
 suffice. Flags hold monotonically growing epochs (no reset between calls).
@@ -43,7 +44,7 @@ class TPComm:
         self.buf = {_RS: None, _AG: None}
         self.epoch = {_RS: 0, _AG: 0}
         self._grow(_RS, capacity_bytes)
-        self._grow(_AG, capacity_bytes // self.n)
+        self._grow(_AG, capacity_bytes)
 
     def _grow(self, kind: int, half_bytes: int) -> None:
         half = (int(half_bytes) + 4095) // 4096 * 4096
@@ -83,11 +84,11 @@ class TPComm:
         B, s, W = shard.shape
         S = s * self.n
         x2 = shard.reshape(B * s, W).to(torch.bfloat16).contiguous()
-        flags, bufs, e = self._args(_AG, x2.numel() * 2)
+        flags, bufs, e = self._args(_AG, x2.numel() * 2 * self.n)
         out = torch.empty((B * S, W), dtype=torch.bfloat16, device=shard.device)
         st = status_word(shard.device)
-        ext().tp_collective("ag_stage", x2, flags, bufs, self.rank, e, B, S, st)
-        ext().tp_collective("ag_pull", out, flags, bufs, self.rank, e, B, S, st)
+        ext().tp_collective("ag_push", x2, flags, bufs, self.rank, e, B, S, st)
+        ext().tp_collective("ag_finish", out, flags, bufs, self.rank, e, B, S, st)
         return out.view(B, S, W)
 
     def gemm_reduce_scatter(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
