@@ -482,6 +482,35 @@ void tp_collective(const std::string& op, const at::Tensor& t, std::vector<int64
   }
 }
 
+void ep_exchange(const std::string& op, const at::Tensor& t, std::vector<int64_t> flags,
+                 std::vector<int64_t> bufs, int64_t rank, int64_t epoch, int64_t kind,
+                 std::vector<int64_t> src_start, std::vector<int64_t> count,
+                 std::vector<int64_t> dst_off, int64_t rows, const c10::optional<at::Tensor>& status) {
+  check_cuda(t, "t");
+  TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1 && t.element_size() == 2,
+              "ep exchange: 2-D rows of a 2-byte dtype");
+  const c10::cuda::CUDAGuard guard(t.device());
+  auto a = tp_args(flags, bufs, rank, epoch, 1, static_cast<int64_t>(flags.size()), t.size(1), status);
+  if (op == "push") {
+    const size_t n = flags.size();
+    TORCH_CHECK(src_start.size() == n && count.size() == n && dst_off.size() == n,
+                "ep push: one segment per rank");
+    plg::EpSegs sg;
+    for (size_t p = 0; p < n; ++p) {
+      sg.src_start[p] = src_start[p];
+      sg.count[p] = count[p];
+      sg.dst_off[p] = dst_off[p];
+      TORCH_CHECK(src_start[p] + count[p] <= t.size(0), "ep push: segment past the source rows");
+    }
+    plg::ep_push(a, sg, t.data_ptr(), t.stride(0), cur_stream());
+  } else if (op == "finish") {
+    TORCH_CHECK(rows <= t.size(0), "ep finish: out has fewer rows than requested");
+    plg::ep_finish(a, static_cast<int>(kind), t.data_ptr(), rows, t.stride(0), cur_stream());
+  } else {
+    TORCH_CHECK(false, "ep exchange: unknown op ", op);
+  }
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -510,6 +539,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_allreduce_avg", &symm_allreduce_avg_b);
   m.def("gemm_rs", &gemm_rs, py::arg("a"), py::arg("b"), py::arg("b_mn_major"), py::arg("rs_dst"),
         py::arg("rank"), py::arg("S"), py::arg("status") = py::none());
+  m.def("ep_exchange", &ep_exchange, py::arg("op"), py::arg("t"), py::arg("flags"), py::arg("bufs"),
+        py::arg("rank"), py::arg("epoch"), py::arg("kind"), py::arg("src_start"), py::arg("count"),
+        py::arg("dst_off"), py::arg("rows"), py::arg("status") = py::none());
   m.def("tp_collective", &tp_collective, py::arg("op"), py::arg("t"), py::arg("flags"), py::arg("bufs"),
         py::arg("rank"), py::arg("epoch"), py::arg("B"), py::arg("S"), py::arg("status") = py::none());
   m.def("embedding_fwd", &embedding_fwd);

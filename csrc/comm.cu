@@ -286,6 +286,51 @@ __global__ void __launch_bounds__(256) tp_ag_finish_kernel(TpArgs a, __nv_bfloat
   }
 }
 
+// ------------------------------------------------------------- expert parallel
+__global__ void __launch_bounds__(256) ep_push_kernel(TpArgs a, EpSegs sg, const __nv_bfloat16* __restrict__ src,
+                                                      long long ld) {
+  const long long g8 = a.W / 8;
+  long long total = 0;
+  for (int p = 0; p < a.n; ++p) total += sg.count[p] * g8;
+  for (long long g = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; g < total;
+       g += static_cast<long long>(gridDim.x) * blockDim.x) {
+    long long rem = g;
+    int p = 0;
+    long long base = 0, start = 0, off = 0;
+#pragma unroll
+    for (int i = 0; i < kSymmMaxRanks; ++i) {  // static indices: no local-memory copy
+      if (i < a.n && p == i) {
+        const long long seg = sg.count[i] * g8;
+        if (rem < seg) {
+          start = sg.src_start[i];
+          off = sg.dst_off[i];
+        } else {
+          rem -= seg;
+          ++p;
+        }
+      }
+    }
+    (void)base;
+    const long long k = rem / g8, c = (rem - k * g8) * 8;
+    const uint4 v = *reinterpret_cast<const uint4*>(src + (start + k) * ld + c);
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(tp_buf(a, p)));
+    *reinterpret_cast<uint4*>(dst + (off + k) * a.W + c) = v;
+  }
+  __threadfence_system();
+}
+
+__global__ void __launch_bounds__(256) ep_finish_kernel(TpArgs a, int kind, __nv_bfloat16* __restrict__ out,
+                                                        long long rows, long long ld_out) {
+  if (!tp_handshake(a, kind)) return;
+  const long long g8 = a.W / 8, total = rows * g8;
+  const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(tp_buf(a, a.rank));
+  for (long long g = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; g < total;
+       g += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = g / g8, c = (g - r * g8) * 8;
+    *reinterpret_cast<uint4*>(out + r * ld_out + c) = *reinterpret_cast<const uint4*>(rb + r * a.W + c);
+  }
+}
+
 }  // namespace comm
 
 void* symm_malloc(size_t bytes, void* ipc_handle_out) {
@@ -371,6 +416,36 @@ void tp_ag_finish(const TpArgs& a, void* out, long long ld_out, cudaStream_t st)
   tp_check(a, ld_out, out, "tp_ag_finish");
   comm::tp_ag_finish_kernel<<<tp_grid(a.B * a.S * (a.W / 8), 148 * 8), 256, 0, st>>>(
       a, reinterpret_cast<__nv_bfloat16*>(out), ld_out);
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+void ep_push(const TpArgs& a, const EpSegs& sg, const void* src, long long ld, cudaStream_t st) {
+  if (a.n < 1 || a.n > kSymmMaxRanks || a.rank < 0 || a.rank >= a.n || a.W % 8 || ld % 8 ||
+      (reinterpret_cast<uintptr_t>(src) & 15))
+    throw std::invalid_argument("ep_push: 1..8 ranks, row width and stride multiples of 8, 16-byte rows");
+  long long rows = 0;
+  for (int p = 0; p < a.n; ++p) {
+    if (sg.count[p] < 0 || sg.src_start[p] < 0 || sg.dst_off[p] < 0)
+      throw std::invalid_argument("ep_push: negative segment");
+    if (sg.count[p] > 0 && (a.bufs[p] == nullptr || (reinterpret_cast<uintptr_t>(a.bufs[p]) & 15)))
+      throw std::invalid_argument("ep_push: every destination needs a 16-byte aligned buffer");
+    rows += sg.count[p];
+  }
+  if (rows == 0) return;
+  comm::ep_push_kernel<<<tp_grid(rows * (a.W / 8), 148 * 4), 256, 0, st>>>(
+      a, sg, reinterpret_cast<const __nv_bfloat16*>(src), ld);
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+void ep_finish(const TpArgs& a, int kind, void* out, long long rows, long long ld_out, cudaStream_t st) {
+  if (kind < 0 || kind >= kTpKinds) throw std::invalid_argument("ep_finish: flag kind out of range");
+  if (rows > 0 && (ld_out % 8 || (reinterpret_cast<uintptr_t>(out) & 15)))
+    throw std::invalid_argument("ep_finish: 16-byte aligned output rows");
+  for (int p = 0; p < a.n; ++p)
+    if (a.flags[p] == nullptr) throw std::invalid_argument("ep_finish: every rank's flag table");
+  // always launched, also with no rows to copy: the handshake keeps the ranks in step
+  comm::ep_finish_kernel<<<tp_grid(rows * (a.W / 8), 148 * 4), 256, 0, st>>>(
+      a, kind, reinterpret_cast<__nv_bfloat16*>(out), rows, ld_out);
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 

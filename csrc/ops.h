@@ -186,6 +186,18 @@ void tp_rs_finish(const TpArgs& a, void* out, long long ld_out, cudaStream_t str
 void tp_ag_push(const TpArgs& a, const void* shard, long long ld, cudaStream_t stream);
 // AG: signal, wait for every peer, copy the slots of the own receive buffer into out [B*S, W]
 void tp_ag_finish(const TpArgs& a, void* out, long long ld_out, cudaStream_t stream);
+// Expert-parallel row exchange (MoE dispatch / combine) over peer memory: segment p
+// of the source rows, [src_start[p], src_start[p] + count[p]), goes to rank p's
+// buffer (bufs[p]) at row dst_off[p]. Rows are W bf16 (W % 8 == 0; any 2-byte data).
+struct EpSegs {
+  long long src_start[kSymmMaxRanks] = {};
+  long long count[kSymmMaxRanks] = {};
+  long long dst_off[kSymmMaxRanks] = {};
+};
+void ep_push(const TpArgs& a, const EpSegs& sg, const void* src, long long ld, cudaStream_t stream);
+// signal (flag kind `kind`), wait for every peer, copy own buffer rows [0, rows) to out
+void ep_finish(const TpArgs& a, int kind, void* out, long long rows, long long ld_out,
+               cudaStream_t stream);
 void symm_allreduce_avg(const SymmAllReduceArgs& a, float* norm_sq, bool accumulate_norm,
                         cudaStream_t stream);
 

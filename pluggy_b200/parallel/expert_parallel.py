@@ -18,7 +18,10 @@ Per sparse layer and microbatch (``EPExperts.forward``):
 5. combine: the outputs return with the reverse all-to-all, are scaled by the
    routing weights and scatter-added into the token rows.
 
-Both exchanges are autograd functions whose backward is the reverse exchange.
+Both exchanges are autograd functions whose backward is the reverse exchange. On
+CUDA the count exchange, dispatch and combine run on this package's peer-memory
+kernels (:mod:`pluggy_b200.comm.ep_fused`: each rank stores its rows straight into
+the owners' receive buffers over NVLink) instead of NCCL all-to-alls.
 When the expert axis is also the data-parallel axis (the usual EP = DP layout),
 each expert's gradient already holds the contributions of every rank's tokens;
 :meth:`ExpertParallel.finish_grads` divides it by the axis size so it matches the
@@ -63,6 +66,7 @@ class EPExperts(nn.Module):
         for p in (self.gate_up_proj, self.down_proj):
             p._plg_expert_sharded = True  # kept out of the data-parallel all-reduce
         self.mesh, self.dim = mesh, dim
+        self.comm = None  # peer-memory exchange (set by parallelize_ep on CUDA)
 
     def forward(self, h, top_indices, top_weights):
         T, H = h.shape
@@ -74,20 +78,31 @@ class EPExperts(nn.Module):
         dest = torch.div(exp, self.local_experts, rounding_mode="floor")
         order = torch.argsort(dest * self.num_experts + exp, stable=True)
         s_tok, s_exp, s_w, s_dest = tok[order], exp[order], w[order], dest[order]
-        send_counts = torch.bincount(s_dest, minlength=n)
-        recv_counts = all_to_all(send_counts.clone(), self.mesh, self.dim)
-        send, recv = send_counts.tolist(), recv_counts.tolist()
-        # local expert ids of the pairs this rank will receive (no gradient)
-        rel = (s_exp - s_dest * self.local_experts).to(torch.int64)
-        r_exp = all_to_all(rel, self.mesh, self.dim, input_splits=send, output_splits=recv)
-        x = _AllToAllV.apply(h[s_tok].contiguous(), send, recv, self.mesh, self.dim)
+        if self.comm is not None:
+            from pluggy_b200.comm.ep_fused import ToOwners, ToSources
+
+            C = self.comm.exchange_counts(torch.bincount(exp, minlength=self.num_experts))
+            pl = self.comm.plan(C)
+            lc = torch.as_tensor(pl["local_counts"].reshape(-1), dtype=torch.int64)
+            r_exp = torch.repeat_interleave(torch.arange(self.local_experts).repeat(n), lc).to(h.device)
+            x = ToOwners.apply(h[s_tok].contiguous(), self.comm, pl)
+            back_fn = lambda y: ToSources.apply(y, self.comm, pl)  # noqa: E731
+        else:
+            send_counts = torch.bincount(s_dest, minlength=n)
+            recv_counts = all_to_all(send_counts.clone(), self.mesh, self.dim)
+            send, recv = send_counts.tolist(), recv_counts.tolist()
+            # local expert ids of the pairs this rank will receive (no gradient)
+            rel = (s_exp - s_dest * self.local_experts).to(torch.int64)
+            r_exp = all_to_all(rel, self.mesh, self.dim, input_splits=send, output_splits=recv)
+            x = _AllToAllV.apply(h[s_tok].contiguous(), send, recv, self.mesh, self.dim)
+            back_fn = lambda y: _AllToAllV.apply(y, recv, send, self.mesh, self.dim)  # noqa: E731
         if x.shape[0] > 0:
             ones = torch.ones(x.shape[0], 1, device=h.device, dtype=h.dtype)
             y = moe_expert_ffn(x, r_exp.view(-1, 1), ones, self.gate_up_proj, self.down_proj)
         else:
             # no rows for this rank's experts: keep the expert params in the graph
             y = x + 0.0 * (self.gate_up_proj.sum() + self.down_proj.sum()).to(x.dtype)
-        back = _AllToAllV.apply(y.to(h.dtype), recv, send, self.mesh, self.dim)
+        back = back_fn(y.to(h.dtype))
         out = torch.zeros(T, H, device=h.device, dtype=back.dtype)
         out.index_add_(0, s_tok, back * s_w.unsqueeze(1).to(back.dtype))
         return out.to(h.dtype)
@@ -99,6 +114,12 @@ class ExpertParallel:
     def __init__(self, model, mesh, dim):
         self.model, self.mesh, self.dim = model, mesh, dim
         self.expert_params: list[nn.Parameter] = []
+        self.comm = None
+
+    def close(self) -> None:
+        if self.comm is not None:
+            self.comm.close()
+            self.comm = None
 
     def expert_param_ids(self) -> set[int]:
         return {id(p) for p in self.expert_params}
@@ -137,10 +158,13 @@ class ExpertParallel:
         self.model.load_state_dict(local)
 
 
-def parallelize_ep(model: nn.Module, mesh, dim: str = "dp") -> ExpertParallel:
+def parallelize_ep(model: nn.Module, mesh, dim: str = "dp", fused: bool | None = None) -> ExpertParallel:
     """Replace the packed experts of every sparse block by :class:`EPExperts` over
-    ``dim``; returns the handle (also stored as ``model.ep``)."""
+    ``dim``; returns the handle (also stored as ``model.ep``). ``fused`` (default: on
+    CUDA) exchanges tokens over peer memory instead of NCCL all-to-alls."""
     ep = ExpertParallel(model, mesh, dim)
+    if fused is None:
+        fused = next(model.parameters()).is_cuda and mesh.size(dim) > 1
     for blk in model.blocks:
         ffn = getattr(blk, "ffn", None)
         experts = getattr(ffn, "experts", None)
@@ -148,6 +172,12 @@ def parallelize_ep(model: nn.Module, mesh, dim: str = "dp") -> ExpertParallel:
             continue
         ffn.experts = EPExperts(experts, mesh, dim)
         ep.expert_params += [ffn.experts.gate_up_proj, ffn.experts.down_proj]
+        if fused and mesh.size(dim) > 1:
+            if ep.comm is None:
+                from pluggy_b200.comm.ep_fused import EPComm
+
+                ep.comm = EPComm(mesh, dim, ffn.experts.num_experts, ffn.experts.emb_dim)
+            ffn.experts.comm = ep.comm
     model.ep = ep
     if hasattr(model, "weight_cache"):
         model.weight_cache.clear()

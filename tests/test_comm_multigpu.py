@@ -190,3 +190,49 @@ def _tp_model_case(rank, world):
 def test_tp2_fused_model_matches_nccl_path():
     _need(2)
     run_ranks(_tp_model_case, 2, backend="nccl")
+
+
+def _ep_model_case(rank, world):
+    from pluggy_b200.core.mesh import Mesh
+    from pluggy_b200.models.qwen3_moe import Qwen3Moe
+    from pluggy_b200.objectives.autoregressive import ARObjective
+    from pluggy_b200.ops import _ext
+    from pluggy_b200.parallel.expert_parallel import parallelize_ep
+
+    mesh = Mesh({"dp": world})
+    cfg = dict(num_layers=2, num_heads=4, num_kv_heads=2, emb_dim=256, head_dim=64, vocab_size=2048,
+               moe_ffn_dim=128, num_experts=8, top_k=2, ffn_dim=512, decoder_sparse_step=1)
+    g = torch.Generator().manual_seed(10 + rank)  # every rank routes its own tokens
+    batches = [torch.randint(0, 2048, (2, 256), generator=g).cuda() for _ in range(3)]
+    res = {}
+    for fused in (False, True):
+        torch.manual_seed(0)
+        m = Qwen3Moe(**cfg).cuda()
+        m.init_weights()
+        for blk in m.blocks:
+            if blk.use_moe:
+                torch.nn.init.normal_(blk.ffn.router.weight, 0.0, 0.5)
+        ep = parallelize_ep(m, mesh, "dp", fused=fused)
+        assert (ep.comm is not None) == fused
+        losses = []
+        for ids in batches:
+            m.zero_grad(set_to_none=True)
+            loss = ARObjective(ce_chunk_size=256).compute_loss(m, {"input_ids": ids, "labels": ids})
+            loss.backward()
+            losses.append(float(loss))
+        res[fused] = (losses, {n: p.grad.float().clone() for n, p in m.named_parameters()
+                               if p.grad is not None})
+        ep.close()
+    torch.cuda.synchronize()
+    _ext.check_status()
+    l0, g0 = res[False]
+    l1, g1 = res[True]
+    assert all(abs(a - b) < 2e-2 * abs(a) for a, b in zip(l0, l1)), (l0, l1)
+    bad = [(n, ((g1[n] - g).norm() / (g.norm() + 1e-12)).item()) for n, g in g0.items()
+           if ((g1[n] - g).norm() / (g.norm() + 1e-12)).item() > 5e-2]
+    assert not bad, bad
+
+
+def test_ep2_peer_exchange_matches_nccl_path():
+    _need(2)
+    run_ranks(_ep_model_case, 2, backend="nccl")
