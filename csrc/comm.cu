@@ -207,14 +207,16 @@ __device__ bool tp_handshake(const TpArgs& a, int kind) {
 __global__ void __launch_bounds__(256) tp_rs_push_kernel(TpArgs a, const __nv_bfloat16* __restrict__ part,
                                                          long long ld) {
   const TpMap m{a.S, a.S / a.n, a.B * (a.S / a.n)};
-  const long long g8 = a.W / 8, total = a.B * a.S * g8;
+  const long long g8 = a.W / 8, per = m.rows * g8, total = a.n * per;
+  // owners in rotated order (rank r starts with owner r): the ranks' writes spread
+  // over all links instead of all converging on one owner at a time
   for (long long g = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; g < total;
        g += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long row = g / g8;
-    const long long c = (g - row * g8) * 8;
-    int owner;
-    long long lrow;
-    m.split(row, owner, lrow);
+    const int i = static_cast<int>(g / per);
+    const int owner = (a.rank + i) % a.n;
+    const long long rem = g - i * per;
+    const long long lrow = rem / g8, c = (rem - lrow * g8) * 8;
+    const long long row = m.join(owner, lrow);
     const uint4 v = *reinterpret_cast<const uint4*>(part + row * ld + c);
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(tp_buf(a, owner)));
     *reinterpret_cast<uint4*>(dst + (a.rank * m.rows + lrow) * a.W + c) = v;
@@ -294,23 +296,34 @@ __global__ void __launch_bounds__(256) ep_push_kernel(TpArgs a, EpSegs sg, const
   for (int p = 0; p < a.n; ++p) total += sg.count[p] * g8;
   for (long long g = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; g < total;
        g += static_cast<long long>(gridDim.x) * blockDim.x) {
+    // segments in rotated order (rank r starts with peer r), so the ranks' writes
+    // spread over all links instead of converging on one peer at a time
     long long rem = g;
-    int p = 0;
-    long long base = 0, start = 0, off = 0;
+    int p = -1;
+    long long start = 0, off = 0;
 #pragma unroll
-    for (int i = 0; i < kSymmMaxRanks; ++i) {  // static indices: no local-memory copy
-      if (i < a.n && p == i) {
-        const long long seg = sg.count[i] * g8;
+    for (int i = 0; i < kSymmMaxRanks; ++i) {
+      if (i < a.n && p < 0) {
+        int q = a.rank + i;
+        q = q >= a.n ? q - a.n : q;
+        long long cnt = 0, st0 = 0, of0 = 0;
+#pragma unroll
+        for (int j = 0; j < kSymmMaxRanks; ++j)  // static indices: no local-memory copy
+          if (j == q) {
+            cnt = sg.count[j];
+            st0 = sg.src_start[j];
+            of0 = sg.dst_off[j];
+          }
+        const long long seg = cnt * g8;
         if (rem < seg) {
-          start = sg.src_start[i];
-          off = sg.dst_off[i];
+          p = q;
+          start = st0;
+          off = of0;
         } else {
           rem -= seg;
-          ++p;
         }
       }
     }
-    (void)base;
     const long long k = rem / g8, c = (rem - k * g8) * 8;
     const uint4 v = *reinterpret_cast<const uint4*>(src + (start + k) * ld + c);
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(tp_buf(a, p)));

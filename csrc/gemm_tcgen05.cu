@@ -53,6 +53,7 @@ struct Args {
   int* status;
   // reduce-scatter epilogue (see GemmProblem)
   int rs_n, rs_rank;
+  int rs_mshift;     // m-tile rotation: each rank starts on a different owner's rows
   long long rs_S, rs_seg, rs_rows;
   void* rs_dst[8];
 };
@@ -295,6 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       nt = tile % args.n_tiles;
       mt = tile / args.n_tiles;
     }
+    if (args.rs_mshift) mt = (mt + args.rs_mshift) % args.m_tiles;
     kb0 = sp * kb_per_split;
     kb1 = min(args.k_blocks, kb0 + kb_per_split);
   };
@@ -529,6 +531,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       nt = tile % args.n_tiles;
       mt = tile / args.n_tiles;
     }
+    if (args.rs_mshift) mt = (mt + args.rs_mshift) % args.m_tiles;
     kb0 = sp * kb_per_split;
     kb1 = min(args.k_blocks, kb0 + kb_per_split);
   };
@@ -736,9 +739,10 @@ static int choose_splits(int tiles, int slots, int k_blocks) {
   return best;
 }
 
-static void set_rs_fields(const GemmProblem& p, Args& a) {
+static void set_rs_fields(const GemmProblem& p, Args& a, int tile_m) {
   a.rs_n = p.rs_n;
   a.rs_rank = p.rs_rank;
+  a.rs_mshift = 0;
   a.rs_S = p.rs_S;
   for (int j = 0; j < 8; ++j) a.rs_dst[j] = p.rs_dst[j];
   if (!p.rs_n) return;
@@ -755,6 +759,9 @@ static void set_rs_fields(const GemmProblem& p, Args& a) {
   a.rs_rows = p.M / p.rs_n;
   if (a.rs_seg % 32 || p.N % 8)
     throw std::invalid_argument("gemm reduce-scatter: S / ranks a multiple of 32, N a multiple of 8");
+  // all ranks writing the same owner's rows at once would funnel into one link:
+  // rank r starts at owner r's rows
+  if (a.m_tiles > 0) a.rs_mshift = static_cast<int>((p.rs_rank * a.rs_seg / tile_m) % a.m_tiles);
 }
 
 template <int BN, bool A_MN, bool B_MN>
@@ -774,7 +781,7 @@ static void launch(const GemmProblem& p, cudaStream_t stream) {
   a.n_tiles = (p.N + BN - 1) / BN;
   a.k_blocks = (p.K + BK - 1) / BK;
   a.status = p.status;
-  set_rs_fields(p, a);
+  set_rs_fields(p, a, BM);
   const int sms = num_sms();
   const int tiles = a.m_tiles * a.n_tiles;
   int splits = p.splits;
@@ -824,7 +831,7 @@ static void launch_pair(const GemmProblem& p, cudaStream_t stream) {
   a.n_tiles = (p.N + BN - 1) / BN;
   a.k_blocks = (p.K + BK - 1) / BK;
   a.status = p.status;
-  set_rs_fields(p, a);
+  set_rs_fields(p, a, 2 * BM);
   auto kern = gemm_pair_kernel<A_MN, B_MN>;
   set_max_smem_once(reinterpret_cast<const void*>(kern), C_::kSmemBytes);
   cudaLaunchConfig_t cfg = {};
