@@ -23,9 +23,9 @@ B200 differences (same observable contract):
   prefetched while the current one computes (forward: i+1, backward: i-1);
   the compute stream waits on an event only when it needs the weights;
 * grad reduce-scatters are also issued on the comm stream and coalesced per
-  unit once the unit's last grad arrives;
-* ``gather="fused"`` (CUDA, dp>1) replaces NCCL with the peer-memory gather
-  kernel in ``pluggy_b200.comm`` (each CTA pulls peer shards over NVLink).
+  unit once the unit's last grad arrives.
+
+The collectives themselves are NCCL's (all-gather / reduce-scatter of fp32 shards).
 """
 
 from __future__ import annotations
