@@ -181,11 +181,55 @@ def case_glu_bwd(a, small):
     return (lambda: glu_bwd(gu, dout, out=out)), {"bytes": T * F * 10, "shape": {"T": T, "F": F}}
 
 
+def case_ce_rows(a, small):
+    """The fused CE's per-row pass over one logits chunk (bf16, in place)."""
+    from pluggy_b200.ops._ext import ext
+
+    N, V = (1024 if small else 4096), a.vocab
+    logits = _bf16(N, V)
+    labels = torch.randint(0, V, (N,), device="cuda")
+    loss = torch.zeros(1, device="cuda")
+    fn = lambda: ext().ce_rows(logits, labels, -100, 1.0, 0.0, None, loss, None)  # noqa: E731
+    return fn, {"bytes": N * V * 4, "shape": {"rows": N, "V": V}}
+
+
+def case_adamw(a, small):
+    from pluggy_b200.ops.optim import adamw_step
+
+    n = (64 if small else 256) << 20
+    p, g, m, v = (torch.randn(n, device="cuda") for _ in range(4))
+    sh = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    fn = lambda: adamw_step([p], [g], [m], [v], [sh], lr=1e-4, beta1=0.9, beta2=0.95,  # noqa: E731
+                            eps=1e-8, weight_decay=0.1, bias_correction1=0.9,
+                            bias_correction2=0.95)
+    return fn, {"bytes": n * (4 * 4 + 3 * 4 + 2), "shape": {"params": n}}
+
+
+def case_sumsq(a, small):
+    from pluggy_b200.ops.optim import multi_tensor_sumsq
+
+    ts = [torch.randn(n, device="cuda") for n in ([8 << 20] * (4 if small else 32))]
+    return (lambda: multi_tensor_sumsq(ts)), {"bytes": sum(t.numel() for t in ts) * 4,
+                                              "shape": {"tensors": len(ts)}}
+
+
+def case_embedding(a, small):
+    from pluggy_b200.ops._ext import ext
+
+    T, D, V = _tokens(a, small), a.dim, a.vocab
+    w = torch.randn(V, D, device="cuda")
+    ids = torch.randint(0, V, (T,), device="cuda")
+    out = torch.empty(T, D, device="cuda")
+    fn = lambda: ext().embedding_fwd(ids, w, out, 1.0)  # noqa: E731
+    return fn, {"bytes": T * D * 8, "shape": {"T": T, "D": D, "V": V}}
+
+
 CASES = {
     "gemm": case_gemm, "attn_fwd": case_attn_fwd, "attn_bwd": case_attn_bwd,
     "qk_rope_fwd": case_qk_rope_fwd, "qk_rope_bwd": case_qk_rope_bwd,
     "rmsnorm_fwd": case_rmsnorm_fwd, "rmsnorm_bwd": case_rmsnorm_bwd,
     "glu_fwd": case_glu_fwd, "glu_bwd": case_glu_bwd,
+    "ce_rows": case_ce_rows, "adamw": case_adamw, "sumsq": case_sumsq, "embedding": case_embedding,
 }
 
 
@@ -220,6 +264,7 @@ def main(argv=None) -> None:
     p.add_argument("--head-dim", type=int, default=128)
     p.add_argument("--dim", type=int, default=1024)
     p.add_argument("--ffn", type=int, default=3072)
+    p.add_argument("--vocab", type=int, default=151936)
     p.add_argument("--m", type=int, default=32768)
     p.add_argument("--n", type=int, default=4096)
     p.add_argument("--k", type=int, default=1024)
