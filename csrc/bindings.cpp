@@ -511,6 +511,21 @@ void ep_exchange(const std::string& op, const at::Tensor& t, std::vector<int64_t
   }
 }
 
+void fsdp_push_b(const at::Tensor& shard, const at::Tensor& table, std::vector<int64_t> flags,
+                 std::vector<int64_t> bufs, int64_t rank, int64_t epoch,
+                 const c10::optional<at::Tensor>& status) {
+  check_cuda(shard, "shard");
+  check_cuda(table, "table");
+  TORCH_CHECK(shard.is_contiguous() && (shard.numel() * shard.element_size()) % 16 == 0,
+              "fsdp_push: contiguous shard of whole 16-byte groups");
+  TORCH_CHECK(table.scalar_type() == at::kLong && table.dim() == 2 && table.size(1) == 3 &&
+                  table.is_contiguous(), "fsdp_push: int64 table [k, 3]");
+  const c10::cuda::CUDAGuard guard(shard.device());
+  auto a = tp_args(flags, bufs, rank, epoch, 1, static_cast<int64_t>(flags.size()), 8, status);
+  plg::fsdp_push(a, table.data_ptr<int64_t>(), static_cast<int>(table.size(0)),
+                 shard.numel() * shard.element_size() / 16, shard.data_ptr(), cur_stream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -539,6 +554,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_allreduce_avg", &symm_allreduce_avg_b);
   m.def("gemm_rs", &gemm_rs, py::arg("a"), py::arg("b"), py::arg("b_mn_major"), py::arg("rs_dst"),
         py::arg("rank"), py::arg("S"), py::arg("status") = py::none());
+  m.def("fsdp_push", &fsdp_push_b, py::arg("shard"), py::arg("table"), py::arg("flags"),
+        py::arg("bufs"), py::arg("rank"), py::arg("epoch"), py::arg("status") = py::none());
   m.def("ep_exchange", &ep_exchange, py::arg("op"), py::arg("t"), py::arg("flags"), py::arg("bufs"),
         py::arg("rank"), py::arg("epoch"), py::arg("kind"), py::arg("src_start"), py::arg("count"),
         py::arg("dst_off"), py::arg("rows"), py::arg("status") = py::none());

@@ -344,6 +344,26 @@ __global__ void __launch_bounds__(256) ep_finish_kernel(TpArgs a, int kind, __nv
   }
 }
 
+// ------------------------------------------------------------------ FSDP gather
+__global__ void __launch_bounds__(256) fsdp_push_kernel(TpArgs a, const int64_t* __restrict__ table, int k,
+                                                        long long total16, const uint4* __restrict__ shard) {
+  for (long long g = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; g < total16;
+       g += static_cast<long long>(gridDim.x) * blockDim.x) {
+    // parameter of this 16-byte group (a unit has a handful of parameters)
+    int i = 0;
+    while (i + 1 < k && table[3 * (i + 1)] <= g) ++i;
+    const long long local = g - table[3 * i];
+    const long long dst = table[3 * i + 1] + a.rank * table[3 * i + 2] + local;
+    const uint4 v = shard[g];
+    for (int p = 0; p < a.n; ++p) {
+      int q = a.rank + p;
+      q = q >= a.n ? q - a.n : q;
+      reinterpret_cast<uint4*>(const_cast<void*>(tp_buf(a, q)))[dst] = v;
+    }
+  }
+  __threadfence_system();
+}
+
 }  // namespace comm
 
 void* symm_malloc(size_t bytes, void* ipc_handle_out) {
@@ -459,6 +479,20 @@ void ep_finish(const TpArgs& a, int kind, void* out, long long rows, long long l
   // always launched, also with no rows to copy: the handshake keeps the ranks in step
   comm::ep_finish_kernel<<<tp_grid(rows * (a.W / 8), 148 * 4), 256, 0, st>>>(
       a, kind, reinterpret_cast<__nv_bfloat16*>(out), rows, ld_out);
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+void fsdp_push(const TpArgs& a, const int64_t* table, int k, long long total16, const void* shard,
+               cudaStream_t st) {
+  if (a.n < 1 || a.n > kSymmMaxRanks || a.rank < 0 || a.rank >= a.n || k < 1 ||
+      (reinterpret_cast<uintptr_t>(shard) & 15))
+    throw std::invalid_argument("fsdp_push: 1..8 ranks, a parameter table, 16-byte aligned shard");
+  for (int p = 0; p < a.n; ++p)
+    if (a.bufs[p] == nullptr || (reinterpret_cast<uintptr_t>(a.bufs[p]) & 15))
+      throw std::invalid_argument("fsdp_push: every rank's 16-byte aligned buffer");
+  if (total16 <= 0) return;
+  comm::fsdp_push_kernel<<<tp_grid(total16, 148 * 4), 256, 0, st>>>(
+      a, table, k, total16, reinterpret_cast<const uint4*>(shard));
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -198,6 +198,12 @@ void ep_push(const TpArgs& a, const EpSegs& sg, const void* src, long long ld, c
 // signal (flag kind `kind`), wait for every peer, copy own buffer rows [0, rows) to out
 void ep_finish(const TpArgs& a, int kind, void* out, long long rows, long long ld_out,
                cudaStream_t stream);
+// FSDP unit all-gather over peer memory: table [k][3] int64 (units of 16 bytes):
+// shard offset in this rank's flat shard, offset of the parameter in the unit's full
+// layout, shard length. This rank's shard of parameter i goes to every rank's buffer
+// at full_off_i + rank * shard_len_i. Finish with ep_finish (rows of 8 2-byte units).
+void fsdp_push(const TpArgs& a, const int64_t* table, int k, long long total16, const void* shard,
+               cudaStream_t stream);
 void symm_allreduce_avg(const SymmAllReduceArgs& a, float* norm_sq, bool accumulate_norm,
                         cudaStream_t stream);
 

@@ -113,8 +113,13 @@ class Qwen3(nn.Module):
         B, S = x.shape
         h = _engine.Embedding.apply(x, self.token_emb.weight, 1.0)
         inv = self.rope.inv_freq
+        fs = getattr(self, "_plg_fsdp", None)
         for i, blk in enumerate(self.blocks):
+            if fs is not None:
+                fs.fused_block_enter(i)
             h = blk.fused_forward(h, self.weight_cache, self._attn_cfg(B, S, blk), inv, i)
+            if fs is not None:
+                fs.fused_block_exit(i, h)
         out = _engine.FinalNorm.apply(h, self.norm.weight, norm_eps(self.norm))
         return out.view(B, S, -1)
 

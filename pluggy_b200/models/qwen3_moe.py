@@ -209,11 +209,16 @@ class Qwen3Moe(nn.Module):
                  and self.head_dim in (64, 128) and self.emb_dim % 128 == 0)
         if fused:
             h = _engine.Embedding.apply(x, self.token_emb.weight, 1.0)
+            fs = getattr(self, "_plg_fsdp", None)
             for i, blk in enumerate(self.blocks):
                 cfg = _engine.AttnCfg(B=B, S=S, Hq=blk.gqa.num_heads, Hk=blk.gqa.num_kv_heads,
                                       d=blk.gqa.head_dim, eps=norm_eps(blk.norm1),
                                       qk_eps=norm_eps(blk.gqa.q_norm, torch.bfloat16))
+                if fs is not None:
+                    fs.fused_block_enter(i)
                 h = blk.fused_forward(h, self.weight_cache, cfg, self.rope.inv_freq, i)
+                if fs is not None:
+                    fs.fused_block_exit(i, h)
             self._router_logits = self._collect()
             self._update_expert_counts(self._router_logits)
             hidden = _engine.FinalNorm.apply(h, self.norm.weight, norm_eps(self.norm)).view(B, S, -1)

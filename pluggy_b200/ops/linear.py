@@ -33,6 +33,9 @@ class WeightCache:
         self._params: dict[int, torch.Tensor] = {}
         self._cat_params: dict[str, list[torch.Tensor]] = {}
         self._opt = None
+        # set by FSDP2: a gather rewrites the full parameter's storage without moving
+        # its version counter, so every get() recasts (into the same bf16 buffer)
+        self.always_recast = False
 
     def bind_optimizer(self, opt) -> None:
         if self._opt is opt:
@@ -69,7 +72,7 @@ class WeightCache:
         key = id(p)
         ver = p._version
         hit = self._store.get(key)
-        if hit is not None and hit[0] == ver and hit[1] == p.data_ptr():
+        if hit is not None and hit[0] == ver and hit[1] == p.data_ptr() and not self.always_recast:
             return hit[2]
         from pluggy_b200.ops._ext import ext
 
@@ -89,7 +92,7 @@ class WeightCache:
         """bf16 concatenation (dim 0) of several params, cached as one buffer."""
         vers = tuple((p._version, p.data_ptr()) for p in params)
         hit = self._store.get(key)
-        if hit is not None and hit[0] == vers:
+        if hit is not None and hit[0] == vers and not self.always_recast:
             return hit[2]
         from pluggy_b200.ops._ext import ext
 

@@ -23,9 +23,12 @@ B200 differences (same observable contract):
   prefetched while the current one computes (forward: i+1, backward: i-1);
   the compute stream waits on an event only when it needs the weights;
 * grad reduce-scatters are also issued on the comm stream and coalesced per
-  unit once the unit's last grad arrives.
-
-The collectives themselves are NCCL's (all-gather / reduce-scatter of fp32 shards).
+  unit once the unit's last grad arrives;
+* a unit's full parameters are views of one flat storage, so on CUDA the gather is
+  one peer-memory push (every rank stores its shards into every rank's staging
+  buffer over NVLink, :mod:`pluggy_b200.comm.fsdp_fused`) plus one finishing copy,
+  instead of an NCCL all-gather (``gather="nccl"`` keeps NCCL). Gradient
+  reduce-scatters stay on NCCL.
 """
 
 from __future__ import annotations
@@ -46,22 +49,15 @@ class _ParamState:
             f"param dim 0 ({param.shape[0]}) not divisible by the dp size {n} (even shards only)"
         )
         self.param = param
+        self.full_shape = tuple(param.shape)
+        self.full_numel = param.numel()
         rows = param.shape[0] // n
         self.shard_shape = (rows, *param.shape[1:])
         self.shard_numel = param.numel() // n
-        self.full = torch.empty_like(param.data)
-        self.full_nbytes = self.full.untyped_storage().nbytes()
-        self.full.untyped_storage().resize_(0)
+        self.full: torch.Tensor | None = None  # a view of the unit's flat full storage
         self._init_shard = param.data.narrow(0, coord * rows, rows).clone()
         self.sharded: torch.Tensor | None = None
         self.grad_shard: torch.Tensor | None = None
-
-    def alloc_full(self) -> None:
-        if self.full.untyped_storage().nbytes() != self.full_nbytes:
-            self.full.untyped_storage().resize_(self.full_nbytes)
-
-    def free_full(self) -> None:
-        self.full.untyped_storage().resize_(0)
 
 
 class _Unit:
@@ -83,13 +79,34 @@ class _Unit:
             s.sharded = v
             s.param.data = v
             off += s.shard_numel
+        # every full parameter of the unit is a view of one flat storage, allocated
+        # while the unit is gathered and resized to 0 bytes otherwise (a use after
+        # resharding fails loudly)
+        full_numel = sum(s.full_numel for s in states)
+        self.full_flat = torch.empty(full_numel, dtype=dt, device=dev)
+        self.full_nbytes = self.full_flat.untyped_storage().nbytes()
+        off = 0
+        for s in states:
+            s.full = self.full_flat[off: off + s.full_numel].view(s.full_shape)
+            off += s.full_numel
+        self.full_flat.untyped_storage().resize_(0)
         self.gathered = False
         self.gather_event = None
         self.ready_grads: list[_ParamState] = []
+        self.peer_table = None  # peer-gather parameter table (device), built on first use
+
+    def alloc_full(self) -> None:
+        st = self.full_flat.untyped_storage()
+        if st.nbytes() != self.full_nbytes:
+            st.resize_(self.full_nbytes)
+
+    def free_full(self) -> None:
+        self.full_flat.untyped_storage().resize_(0)
 
 
 class FSDP2:
-    def __init__(self, model: nn.Module, mesh: MeshLike, dim: str = "dp", *, prefetch: bool = True):
+    def __init__(self, model: nn.Module, mesh: MeshLike, dim: str = "dp", *, prefetch: bool = True,
+                 gather: str = "auto"):
         self.mesh = mesh
         self.dim = dim
         self.group_size = mesh.size(dim)
@@ -116,6 +133,24 @@ class FSDP2:
         self._comm_stream = torch.cuda.Stream(device=dev) if self._cuda else None
         self._block_units = self._units[:-1]
         self._pending_work: list = []
+        # parameter all-gathers over peer memory ("peer") or NCCL ("nccl"); "auto" picks
+        # peer on CUDA when every parameter splits into whole 16-byte pieces
+        self._peer = None
+        aligned = all(s.full_numel % (4 * n) == 0 for u in self._units for s in u.params)
+        if gather not in ("auto", "peer", "nccl"):
+            raise ValueError(f"gather must be 'auto', 'peer' or 'nccl', got {gather!r}")
+        if gather == "peer" and not (self._cuda and aligned and dev.type == "cuda"):
+            raise ValueError("peer gathers need CUDA and parameters of whole 16-byte shards")
+        if gather == "peer" or (gather == "auto" and self._cuda and aligned):
+            from pluggy_b200.comm.fsdp_fused import PeerGather
+
+            self._peer = PeerGather(mesh, dim, max(u.full_nbytes for u in self._units))
+        # the models' fused CUDA path runs blocks through ``fused_forward`` (not the
+        # module call, so the module hooks do not fire): it calls these instead
+        model._plg_fsdp = self
+        if hasattr(model, "weight_cache"):
+            model.weight_cache.always_recast = True
+            model.weight_cache.clear()
 
     # --------------------------------------------------------------- plumbing
     def _install(self, module: nn.Module, unit: _Unit) -> None:
@@ -142,21 +177,22 @@ class FSDP2:
         """Launch the coalesced all-gather of ``unit`` (on the comm stream on CUDA)."""
         if unit.gathered:
             return
-        for s in unit.params:
-            s.alloc_full()
+        unit.alloc_full()
         ctx = torch.cuda.stream(self._comm_stream) if self._cuda else contextlib.nullcontext()
         if self._cuda:
             self._comm_stream.wait_stream(torch.cuda.current_stream())
         with ctx:
-            group = self._group()
-            with self._coalesced(group, unit):
-                for s in unit.params:
-                    dist.all_gather_into_tensor(s.full, s.sharded, group=group)
+            if self._peer is not None:
+                self._peer.gather(unit)
+            else:
+                group = self._group()
+                with self._coalesced(group, unit):
+                    for s in unit.params:
+                        dist.all_gather_into_tensor(s.full, s.sharded, group=group)
             if self._cuda:
                 unit.gather_event = torch.cuda.Event()
                 unit.gather_event.record(self._comm_stream)
-                for s in unit.params:
-                    s.full.record_stream(torch.cuda.current_stream())
+                unit.full_flat.record_stream(torch.cuda.current_stream())
         unit.gathered = True
 
     def _use(self, unit: _Unit) -> None:
@@ -184,8 +220,7 @@ class FSDP2:
 
     @torch._dynamo.disable
     def _reshard(self, unit: _Unit) -> None:
-        for s in unit.params:
-            s.free_full()
+        unit.free_full()
         unit.gathered = False
 
     @torch._dynamo.disable
@@ -206,7 +241,7 @@ class FSDP2:
             self._reduce_unit(unit)
             for st in unit.params:
                 st.param.data = st.sharded
-                st.free_full()
+            unit.free_full()
             unit.gathered = False
 
     def _reduce_unit(self, unit: _Unit) -> None:
@@ -258,6 +293,27 @@ class FSDP2:
                     assert s.grad_shard is not None, f"unit {unit.name}: no reduced grad to publish"
                     s.param.grad = s.grad_shard
                     s.grad_shard = None
+
+    @torch._dynamo.disable
+    def fused_block_enter(self, i: int) -> None:
+        """Before block ``i`` of a fused forward: gather it (and prefetch the next)."""
+        self._pre_forward(self._block_units[i])
+
+    @torch._dynamo.disable
+    def fused_block_exit(self, i: int, out: torch.Tensor) -> None:
+        """After block ``i``: reshard it; when the gradient of its output arrives,
+        re-gather it for its backward (what the module's backward pre-hook does)."""
+        unit = self._block_units[i]
+        self._reshard(unit)
+        if out.requires_grad:
+            out.register_hook(lambda g, u=unit: self._pre_backward(u))
+
+    def close(self) -> None:
+        """Release the peer-gather buffers (collective over the axis)."""
+        if getattr(self, "_peer", None) is not None:
+            torch.cuda.synchronize()
+            self._peer.close()
+            self._peer = None
 
     # ------------------------------------------------------------- inspection
     @property

@@ -236,3 +236,57 @@ def _ep_model_case(rank, world):
 def test_ep2_peer_exchange_matches_nccl_path():
     _need(2)
     run_ranks(_ep_model_case, 2, backend="nccl")
+
+
+def _fsdp_peer_case(rank, world):
+    from pluggy_b200.core.mesh import Mesh
+    from pluggy_b200.models.qwen3 import Qwen3
+    from pluggy_b200.objectives.autoregressive import ARObjective
+    from pluggy_b200.ops import _ext
+    from pluggy_b200.parallel.fsdp2 import FSDP2
+
+    mesh = Mesh({"dp": world})
+    cfg = dict(num_layers=2, num_heads=4, num_kv_heads=2, emb_dim=256, head_dim=64, vocab_size=2048,
+               ffn_dim=512, tie_embeddings=True)
+    g = torch.Generator().manual_seed(20 + rank)
+    batches = [torch.randint(0, 2048, (2, 128), generator=g).cuda() for _ in range(3)]
+    # the unsharded model's first loss on this rank's batch is the FSDP2 target
+    torch.manual_seed(0)
+    plain = Qwen3(**cfg).cuda()
+    plain.init_weights()
+    with torch.no_grad():
+        want0 = float(ARObjective(ce_chunk_size=256).compute_loss(
+            plain, {"input_ids": batches[0], "labels": batches[0]}))
+    del plain
+    res = {}
+    for mode in ("nccl", "peer"):
+        torch.manual_seed(0)
+        m = Qwen3(**cfg).cuda()
+        m.init_weights()
+        fs = FSDP2(m, mesh, "dp", gather=mode)
+        assert (fs._peer is not None) == (mode == "peer")
+        losses = []
+        for ids in batches:
+            loss = ARObjective(ce_chunk_size=256).compute_loss(m, {"input_ids": ids, "labels": ids})
+            loss.backward()
+            fs.sync()
+            losses.append(float(loss))
+            grads = {n: p.grad.float().clone() for n, p in m.named_parameters() if p.grad is not None}
+            m.zero_grad(set_to_none=True)
+        res[mode] = (losses, grads)
+        fs.close()
+    torch.cuda.synchronize()
+    _ext.check_status()
+    assert abs(res["nccl"][0][0] - want0) < 1e-3 * abs(want0), (res["nccl"][0][0], want0)
+    # the gathers are exact copies; the remaining differences come from float atomics
+    # elsewhere in the step (loss sum, dQ accumulation)
+    for a, b in zip(res["nccl"][0], res["peer"][0]):
+        assert abs(a - b) < 1e-5 * abs(a), (res["nccl"][0], res["peer"][0])
+    for n, gref in res["nccl"][1].items():
+        g = res["peer"][1][n]
+        assert ((g - gref).norm() / (gref.norm() + 1e-12)).item() < 1e-3, n
+
+
+def test_fsdp2_peer_gather_matches_nccl():
+    _need(2)
+    run_ranks(_fsdp_peer_case, 2, backend="nccl")
