@@ -408,7 +408,7 @@ void symm_allreduce_avg_b(std::vector<int64_t> data, std::vector<int64_t> flags,
 // GEMM whose epilogue stores each row into its owner's staging slot (tensor-parallel
 // reduce-scatter along the sequence); rs_dst: every rank's staging base address
 void gemm_rs(const at::Tensor& a, const at::Tensor& b, bool b_mn_major, std::vector<int64_t> rs_dst,
-             int64_t rank, int64_t S, const c10::optional<at::Tensor>& status) {
+             int64_t rank, int64_t S, int64_t cap_bytes, const c10::optional<at::Tensor>& status) {
   check_cuda(a, "a");
   check_cuda(b, "b");
   TORCH_CHECK(is_bf16(a) && is_bf16(b) && a.dim() == 2 && b.dim() == 2, "gemm_rs: bf16 2-D operands");
@@ -433,12 +433,14 @@ void gemm_rs(const at::Tensor& a, const at::Tensor& b, bool b_mn_major, std::vec
   p.rs_rank = static_cast<int>(rank);
   p.rs_S = S;
   for (int j = 0; j < n; ++j) p.rs_dst[j] = reinterpret_cast<void*>(rs_dst[j]);
+  p.rs_cap = cap_bytes;
   p.status = status.has_value() ? status->data_ptr<int>() : nullptr;
   plg::gemm_bf16(p, cur_stream());
 }
 
 plg::TpArgs tp_args(std::vector<int64_t> flags, std::vector<int64_t> bufs, int64_t rank, int64_t epoch,
-                    int64_t B, int64_t S, int64_t W, const c10::optional<at::Tensor>& status) {
+                    int64_t B, int64_t S, int64_t W, int64_t cap_bytes,
+                    const c10::optional<at::Tensor>& status) {
   const int n = static_cast<int>(flags.size());
   TORCH_CHECK(n >= 1 && n <= plg::kSymmMaxRanks && bufs.size() == flags.size(),
               "tp collective: one flag table and one buffer per rank (1..8)");
@@ -454,16 +456,17 @@ plg::TpArgs tp_args(std::vector<int64_t> flags, std::vector<int64_t> bufs, int64
   a.B = B;
   a.S = S;
   a.W = W;
+  a.cap16 = cap_bytes / 16;
   return a;
 }
 
 void tp_collective(const std::string& op, const at::Tensor& t, std::vector<int64_t> flags,
                    std::vector<int64_t> bufs, int64_t rank, int64_t epoch, int64_t B, int64_t S,
-                   const c10::optional<at::Tensor>& status) {
+                   int64_t cap_bytes, const c10::optional<at::Tensor>& status) {
   check_cuda(t, "t");
   TORCH_CHECK(is_bf16(t) && t.dim() == 2 && t.stride(1) == 1, "tp collective: bf16 [rows, W] rows");
   const c10::cuda::CUDAGuard guard(t.device());
-  auto a = tp_args(flags, bufs, rank, epoch, B, S, t.size(1), status);
+  auto a = tp_args(flags, bufs, rank, epoch, B, S, t.size(1), cap_bytes, status);
   const long long full = B * S, part = B * (S / static_cast<long long>(flags.size()));
   if (op == "rs_push") {
     TORCH_CHECK(t.size(0) == full, "rs_push: partial must be [B*S, W]");
@@ -485,12 +488,14 @@ void tp_collective(const std::string& op, const at::Tensor& t, std::vector<int64
 void ep_exchange(const std::string& op, const at::Tensor& t, std::vector<int64_t> flags,
                  std::vector<int64_t> bufs, int64_t rank, int64_t epoch, int64_t kind,
                  std::vector<int64_t> src_start, std::vector<int64_t> count,
-                 std::vector<int64_t> dst_off, int64_t rows, const c10::optional<at::Tensor>& status) {
+                 std::vector<int64_t> dst_off, int64_t rows, int64_t cap_bytes,
+                 const c10::optional<at::Tensor>& status) {
   check_cuda(t, "t");
   TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1 && t.element_size() == 2,
               "ep exchange: 2-D rows of a 2-byte dtype");
   const c10::cuda::CUDAGuard guard(t.device());
-  auto a = tp_args(flags, bufs, rank, epoch, 1, static_cast<int64_t>(flags.size()), t.size(1), status);
+  auto a = tp_args(flags, bufs, rank, epoch, 1, static_cast<int64_t>(flags.size()), t.size(1), cap_bytes,
+                   status);
   if (op == "push") {
     const size_t n = flags.size();
     TORCH_CHECK(src_start.size() == n && count.size() == n && dst_off.size() == n,
@@ -512,7 +517,7 @@ void ep_exchange(const std::string& op, const at::Tensor& t, std::vector<int64_t
 }
 
 void fsdp_push_b(const at::Tensor& shard, const at::Tensor& table, std::vector<int64_t> flags,
-                 std::vector<int64_t> bufs, int64_t rank, int64_t epoch,
+                 std::vector<int64_t> bufs, int64_t rank, int64_t epoch, int64_t cap_bytes,
                  const c10::optional<at::Tensor>& status) {
   check_cuda(shard, "shard");
   check_cuda(table, "table");
@@ -521,7 +526,7 @@ void fsdp_push_b(const at::Tensor& shard, const at::Tensor& table, std::vector<i
   TORCH_CHECK(table.scalar_type() == at::kLong && table.dim() == 2 && table.size(1) == 3 &&
                   table.is_contiguous(), "fsdp_push: int64 table [k, 3]");
   const c10::cuda::CUDAGuard guard(shard.device());
-  auto a = tp_args(flags, bufs, rank, epoch, 1, static_cast<int64_t>(flags.size()), 8, status);
+  auto a = tp_args(flags, bufs, rank, epoch, 1, static_cast<int64_t>(flags.size()), 8, cap_bytes, status);
   plg::fsdp_push(a, table.data_ptr<int64_t>(), static_cast<int>(table.size(0)),
                  shard.numel() * shard.element_size() / 16, shard.data_ptr(), cur_stream());
 }
@@ -553,14 +558,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tensor_from_ptr", &tensor_from_ptr);
   m.def("symm_allreduce_avg", &symm_allreduce_avg_b);
   m.def("gemm_rs", &gemm_rs, py::arg("a"), py::arg("b"), py::arg("b_mn_major"), py::arg("rs_dst"),
-        py::arg("rank"), py::arg("S"), py::arg("status") = py::none());
+        py::arg("rank"), py::arg("S"), py::arg("cap_bytes"), py::arg("status") = py::none());
   m.def("fsdp_push", &fsdp_push_b, py::arg("shard"), py::arg("table"), py::arg("flags"),
-        py::arg("bufs"), py::arg("rank"), py::arg("epoch"), py::arg("status") = py::none());
+        py::arg("bufs"), py::arg("rank"), py::arg("epoch"), py::arg("cap_bytes"),
+        py::arg("status") = py::none());
   m.def("ep_exchange", &ep_exchange, py::arg("op"), py::arg("t"), py::arg("flags"), py::arg("bufs"),
         py::arg("rank"), py::arg("epoch"), py::arg("kind"), py::arg("src_start"), py::arg("count"),
-        py::arg("dst_off"), py::arg("rows"), py::arg("status") = py::none());
+        py::arg("dst_off"), py::arg("rows"), py::arg("cap_bytes"), py::arg("status") = py::none());
   m.def("tp_collective", &tp_collective, py::arg("op"), py::arg("t"), py::arg("flags"), py::arg("bufs"),
-        py::arg("rank"), py::arg("epoch"), py::arg("B"), py::arg("S"), py::arg("status") = py::none());
+        py::arg("rank"), py::arg("epoch"), py::arg("B"), py::arg("S"), py::arg("cap_bytes"),
+        py::arg("status") = py::none());
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd", &embedding_bwd);
   m.def("softcap", &softcap);

@@ -177,6 +177,16 @@ __device__ __forceinline__ const void* tp_buf(const TpArgs& a, int j) {
   return p;
 }
 
+// 16-byte store into a peer's buffer at index `i16` (16-byte units), skipped (and
+// reported) when it would leave the buffer
+__device__ __forceinline__ void peer_store16(const TpArgs& a, int p, long long i16, uint4 v) {
+  if (i16 < 0 || i16 >= a.cap16) {
+    record_status(a.status, kOutOfBounds);
+    return;
+  }
+  reinterpret_cast<uint4*>(const_cast<void*>(tp_buf(a, p)))[i16] = v;
+}
+
 __device__ __forceinline__ uint32_t* tp_flag(const TpArgs& a, int j) {
   uint32_t* p = a.flags[0];
 #pragma unroll
@@ -218,8 +228,7 @@ __global__ void __launch_bounds__(256) tp_rs_push_kernel(TpArgs a, const __nv_bf
     const long long lrow = rem / g8, c = (rem - lrow * g8) * 8;
     const long long row = m.join(owner, lrow);
     const uint4 v = *reinterpret_cast<const uint4*>(part + row * ld + c);
-    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(tp_buf(a, owner)));
-    *reinterpret_cast<uint4*>(dst + (a.rank * m.rows + lrow) * a.W + c) = v;
+    peer_store16(a, owner, ((a.rank * m.rows + lrow) * a.W + c) / 8, v);
   }
   __threadfence_system();
 }
@@ -263,10 +272,8 @@ __global__ void __launch_bounds__(256) tp_ag_push_kernel(TpArgs a, const __nv_bf
     const long long r = g / g8;
     const long long c = (g - r * g8) * 8;
     const uint4 v = *reinterpret_cast<const uint4*>(shard + r * ld + c);
-    for (int p = 0; p < a.n; ++p) {
-      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(tp_buf(a, (a.rank + p) % a.n)));
-      *reinterpret_cast<uint4*>(dst + (a.rank * rows + r) * a.W + c) = v;
-    }
+    for (int p = 0; p < a.n; ++p)
+      peer_store16(a, (a.rank + p) % a.n, ((a.rank * rows + r) * a.W + c) / 8, v);
   }
   __threadfence_system();
 }
@@ -326,8 +333,7 @@ __global__ void __launch_bounds__(256) ep_push_kernel(TpArgs a, EpSegs sg, const
     }
     const long long k = rem / g8, c = (rem - k * g8) * 8;
     const uint4 v = *reinterpret_cast<const uint4*>(src + (start + k) * ld + c);
-    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(tp_buf(a, p)));
-    *reinterpret_cast<uint4*>(dst + (off + k) * a.W + c) = v;
+    peer_store16(a, p, ((off + k) * a.W + c) / 8, v);
   }
   __threadfence_system();
 }
@@ -358,7 +364,7 @@ __global__ void __launch_bounds__(256) fsdp_push_kernel(TpArgs a, const int64_t*
     for (int p = 0; p < a.n; ++p) {
       int q = a.rank + p;
       q = q >= a.n ? q - a.n : q;
-      reinterpret_cast<uint4*>(const_cast<void*>(tp_buf(a, q)))[dst] = v;
+      peer_store16(a, q, dst, v);
     }
   }
   __threadfence_system();
@@ -433,6 +439,8 @@ void tp_rs_push(const TpArgs& a, const void* partial, long long ld, cudaStream_t
 
 void tp_rs_finish(const TpArgs& a, void* out, long long ld_out, cudaStream_t st) {
   tp_check(a, ld_out, out, "tp_rs_finish");
+  if (a.B * a.S * a.W / 8 > a.cap16)
+    throw std::invalid_argument("tp_rs_finish: the staging buffer is smaller than the partial");
   comm::tp_rs_finish_kernel<<<tp_grid(a.B * (a.S / a.n) * (a.W / 8), 148 * 4), 256, 0, st>>>(
       a, reinterpret_cast<__nv_bfloat16*>(out), ld_out);
   PLG_CUDA_CHECK(cudaGetLastError());
@@ -447,6 +455,8 @@ void tp_ag_push(const TpArgs& a, const void* shard, long long ld, cudaStream_t s
 
 void tp_ag_finish(const TpArgs& a, void* out, long long ld_out, cudaStream_t st) {
   tp_check(a, ld_out, out, "tp_ag_finish");
+  if (a.B * a.S * a.W / 8 > a.cap16)
+    throw std::invalid_argument("tp_ag_finish: the receive buffer is smaller than the gathered rows");
   comm::tp_ag_finish_kernel<<<tp_grid(a.B * a.S * (a.W / 8), 148 * 8), 256, 0, st>>>(
       a, reinterpret_cast<__nv_bfloat16*>(out), ld_out);
   PLG_CUDA_CHECK(cudaGetLastError());
@@ -474,6 +484,8 @@ void ep_finish(const TpArgs& a, int kind, void* out, long long rows, long long l
   if (kind < 0 || kind >= kTpKinds) throw std::invalid_argument("ep_finish: flag kind out of range");
   if (rows > 0 && (ld_out % 8 || (reinterpret_cast<uintptr_t>(out) & 15)))
     throw std::invalid_argument("ep_finish: 16-byte aligned output rows");
+  if (rows * a.W / 8 > a.cap16)
+    throw std::invalid_argument("ep_finish: the receive buffer is smaller than the requested rows");
   for (int p = 0; p < a.n; ++p)
     if (a.flags[p] == nullptr) throw std::invalid_argument("ep_finish: every rank's flag table");
   // always launched, also with no rows to copy: the handshake keeps the ranks in step

@@ -31,6 +31,7 @@ enum StatusCode : int {
   kTimeoutPeerFlag = 5,     // a fused collective waited too long for a peer
   kTimeoutDrain = 6,        // unwinding waited too long for in-flight copies
   kBadArgument = 7,
+  kOutOfBounds = 8,         // a peer store would have left the destination buffer (skipped)
 };
 
 // default deadline for a single wait: 2 s of wall time on %globaltimer

@@ -55,6 +55,7 @@ struct Args {
   int rs_n, rs_rank;
   int rs_mshift;     // m-tile rotation: each rank starts on a different owner's rows
   long long rs_S, rs_seg, rs_rows;
+  long long rs_cap_rows;  // rows of N that fit in every staging buffer
   void* rs_dst[8];
 };
 
@@ -101,6 +102,15 @@ __device__ __forceinline__ void store_acc_rows_rs(const Args& args, uint32_t t_r
   const long long row_base = row - lane;
   if (row_base >= args.M) return;  // warp-uniform
   __nv_bfloat16* wbase = rs_row_ptr(args, row_base);
+  {
+    // the warp's 32 rows must lie inside the owner's staging buffer
+    const long long b = row_base / args.rs_S, s = row_base - b * args.rs_S;
+    const long long lrow = b * args.rs_seg + s % args.rs_seg;
+    if (args.rs_rank * args.rs_rows + lrow + 32 > args.rs_cap_rows) {
+      if ((threadIdx.x & 31) == 0) record_status(args.status, kOutOfBounds);
+      return;
+    }
+  }
 #pragma unroll 1
   for (int cp = 0; cp < BN / 64; ++cp) {
     uint32_t u[32];
@@ -757,6 +767,9 @@ static void set_rs_fields(const GemmProblem& p, Args& a, int tile_m) {
       throw std::invalid_argument("gemm reduce-scatter: staging buffers must be 16-byte aligned");
   a.rs_seg = p.rs_S / p.rs_n;
   a.rs_rows = p.M / p.rs_n;
+  a.rs_cap_rows = p.rs_cap / (2LL * p.N);
+  if (a.rs_cap_rows < static_cast<long long>(p.M))
+    throw std::invalid_argument("gemm reduce-scatter: the staging buffers are smaller than the output");
   if (a.rs_seg % 32 || p.N % 8)
     throw std::invalid_argument("gemm reduce-scatter: S / ranks a multiple of 32, N a multiple of 8");
   // all ranks writing the same owner's rows at once would funnel into one link:

@@ -36,6 +36,7 @@ struct GemmProblem {
   int rs_n = 0, rs_rank = 0;
   long long rs_S = 0;
   void* rs_dst[8] = {};
+  long long rs_cap = 0;     // bytes of every staging buffer (stores beyond are skipped)
 };
 void gemm_bf16(const GemmProblem& p, cudaStream_t stream);
 
@@ -177,6 +178,7 @@ struct TpArgs {
   uint32_t* flags[kSymmMaxRanks] = {};
   void* bufs[kSymmMaxRanks] = {};  // every rank's staging (RS) or send (AG) buffer
   long long B = 0, S = 0, W = 0;   // rows are [B, S] flattened, W bf16 columns
+  long long cap16 = 0;             // bytes / 16 of every bufs[p] (stores beyond are skipped)
 };
 // RS: push this rank's partial [B*S, W] rows into every owner's staging slot
 void tp_rs_push(const TpArgs& a, const void* partial, long long ld, cudaStream_t stream);

@@ -76,10 +76,10 @@ class EPComm:
         n = self.n
         st = status_word(cnt.device)
         ext().ep_exchange("push", row, self.flags.peers, bufs, self.rank, e, _COUNTS,
-                          [0] * n, [1] * n, [self.rank] * n, 0, st)
+                          [0] * n, [1] * n, [self.rank] * n, 0, half, st)
         out = torch.empty(n, self.cw, dtype=torch.int16, device=cnt.device)
         ext().ep_exchange("finish", out, self.flags.peers, bufs, self.rank, e, _COUNTS,
-                          [0] * n, [0] * n, [0] * n, n, st)
+                          [0] * n, [0] * n, [0] * n, n, half, st)
         return out.view(torch.int32)[:, :self.E].cpu().numpy().astype(np.int64)
 
     def plan(self, C: np.ndarray) -> dict:
@@ -111,10 +111,10 @@ class EPComm:
         if x2.shape[0] == 0:
             x2 = torch.zeros(1, self.H, dtype=torch.bfloat16, device=x.device)
         ext().ep_exchange("push", x2, self.flags.peers, bufs, self.rank, e, kind, src_start, count,
-                          dst_off, 0, st)
+                          dst_off, 0, half, st)
         o = out if out_rows > 0 else torch.empty(1, self.H, dtype=torch.bfloat16, device=x.device)
         ext().ep_exchange("finish", o, self.flags.peers, bufs, self.rank, e, kind, [0] * self.n,
-                          [0] * self.n, [0] * self.n, out_rows, st)
+                          [0] * self.n, [0] * self.n, out_rows, half, st)
         return out
 
     def to_owners(self, x_sorted: torch.Tensor, pl: dict) -> torch.Tensor:

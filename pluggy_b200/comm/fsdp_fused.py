@@ -47,11 +47,12 @@ class PeerGather:
         e = self.epoch
         bufs = [p + (e % 2) * self.half for p in self.buf.peers]
         st = status_word(unit.flat_shard.device)
-        ext().fsdp_push(unit.flat_shard, self._table(unit), self.flags.peers, bufs, self.rank, e, st)
+        ext().fsdp_push(unit.flat_shard, self._table(unit), self.flags.peers, bufs, self.rank, e,
+                        self.half, st)
         out = unit.full_flat.view(torch.int16).view(-1, 8)  # rows of 16 bytes
         n = self.n
         ext().ep_exchange("finish", out, self.flags.peers, bufs, self.rank, e, _KIND, [0] * n, [0] * n,
-                          [0] * n, out.shape[0], st)
+                          [0] * n, out.shape[0], self.half, st)
 
     def close(self) -> None:
         self.buf.close()

@@ -65,18 +65,18 @@ class TPComm:
         e = self.epoch[kind]
         off = (e % 2) * self.cap[kind]
         bufs = [p + off for p in self.buf[kind].peers]
-        return self.flags.peers, bufs, e
+        return self.flags.peers, bufs, e, self.cap[kind]
 
     # ------------------------------------------------------------ collectives
     def reduce_scatter_seq(self, partial: torch.Tensor) -> torch.Tensor:
         """[B, S, W] partial sums (bf16) -> this rank's summed [B, S / n, W]."""
         B, S, W = partial.shape
         p2 = partial.reshape(B * S, W).to(torch.bfloat16).contiguous()
-        flags, bufs, e = self._args(_RS, p2.numel() * 2)
+        flags, bufs, e, cap = self._args(_RS, p2.numel() * 2)
         out = torch.empty((B * (S // self.n), W), dtype=torch.bfloat16, device=partial.device)
         st = status_word(partial.device)
-        ext().tp_collective("rs_push", p2, flags, bufs, self.rank, e, B, S, st)
-        ext().tp_collective("rs_finish", out, flags, bufs, self.rank, e, B, S, st)
+        ext().tp_collective("rs_push", p2, flags, bufs, self.rank, e, B, S, cap, st)
+        ext().tp_collective("rs_finish", out, flags, bufs, self.rank, e, B, S, cap, st)
         return out.view(B, S // self.n, W)
 
     def all_gather_seq(self, shard: torch.Tensor) -> torch.Tensor:
@@ -84,11 +84,11 @@ class TPComm:
         B, s, W = shard.shape
         S = s * self.n
         x2 = shard.reshape(B * s, W).to(torch.bfloat16).contiguous()
-        flags, bufs, e = self._args(_AG, x2.numel() * 2 * self.n)
+        flags, bufs, e, cap = self._args(_AG, x2.numel() * 2 * self.n)
         out = torch.empty((B * S, W), dtype=torch.bfloat16, device=shard.device)
         st = status_word(shard.device)
-        ext().tp_collective("ag_push", x2, flags, bufs, self.rank, e, B, S, st)
-        ext().tp_collective("ag_finish", out, flags, bufs, self.rank, e, B, S, st)
+        ext().tp_collective("ag_push", x2, flags, bufs, self.rank, e, B, S, cap, st)
+        ext().tp_collective("ag_finish", out, flags, bufs, self.rank, e, B, S, cap, st)
         return out.view(B, S, W)
 
     def gemm_reduce_scatter(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
@@ -98,11 +98,11 @@ class TPComm:
         B, S, K = x.shape
         N = w.shape[0]
         x2 = x.reshape(B * S, K).to(torch.bfloat16).contiguous()
-        flags, bufs, e = self._args(_RS, B * S * N * 2)
+        flags, bufs, e, cap = self._args(_RS, B * S * N * 2)
         st = status_word(x.device)
-        ext().gemm_rs(x2, w, False, bufs, self.rank, S, st)
+        ext().gemm_rs(x2, w, False, bufs, self.rank, S, cap, st)
         out = torch.empty((B * (S // self.n), N), dtype=torch.bfloat16, device=x.device)
-        ext().tp_collective("rs_finish", out, flags, bufs, self.rank, e, B, S, st)
+        ext().tp_collective("rs_finish", out, flags, bufs, self.rank, e, B, S, cap, st)
         return out.view(B, S // self.n, N)
 
     def close(self) -> None:

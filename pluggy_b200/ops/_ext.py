@@ -28,6 +28,7 @@ _STATUS_NAMES = {
     5: "fused collective timed out waiting for a peer",
     6: "kernel unwinding timed out waiting for its in-flight copies",
     7: "bad kernel argument",
+    8: "a peer-memory store was outside its destination buffer and was skipped",
 }
 
 

@@ -215,14 +215,25 @@ class Trainer:
                                     config=self.config)
 
     def _log_metrics(self, metrics, step, tokens_per_step, t) -> None:
-        if self.wandb_run is None:
+        jsonl = self.config.get("logging", {}).get("jsonl")
+        if self.wandb_run is None and not jsonl:
             return
         log = {"train/loss": float(metrics["loss"]), "train/grad_norm": float(metrics["grad_norm"]),
                "train/lr": self.scheduler.get_last_lr()[0], "train/tokens": step * tokens_per_step,
                "perf/tps": tokens_per_step / t, "perf/step_time": t}
         if self.device.type == "cuda":
             log["perf/peak_mem_gib"] = torch.cuda.max_memory_allocated() / 2**30
-        self.wandb_run.log(log, step=step)
+        counts = getattr(self.model, "last_tokens_per_expert", None)
+        if isinstance(counts, torch.Tensor) and counts.numel():
+            # tokens routed to each expert (summed over the sparse layers) this step
+            c = counts.detach().float().reshape(-1, counts.shape[-1]).sum(0)
+            log["moe/expert_load_max_over_mean"] = float(c.max() / c.mean().clamp_min(1e-9))
+        if self.wandb_run is not None:
+            self.wandb_run.log(log, step=step)
+        if jsonl:
+            # one JSON object per optimizer step (rank 0), appended: survives restarts
+            with open(jsonl, "a") as f:
+                f.write(json.dumps({"step": step, **log}) + "\n")
 
     # -------------------------------------------------------------- checkpoint
     @debug_time

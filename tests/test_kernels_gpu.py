@@ -419,3 +419,26 @@ def test_weight_cache_optimizer_shadows():
         assert torch.equal(a2, w1.detach().bfloat16())
         assert torch.equal(cat2, torch.cat([w2, w3]).detach().bfloat16())
         assert not torch.equal(a2, ref_a) and not torch.equal(cat2, ref_cat)
+
+
+def test_peer_store_bounds_are_enforced():
+    """A push whose destination offset lies past the buffer is skipped and reported
+    (status 8) instead of writing outside the buffer; in-range rows still land."""
+    from pluggy_b200.ops import _ext
+
+    st = _ext.status_word()
+    st.zero_()
+    buf = torch.zeros(64 + 16, 8, dtype=torch.int16, device=DEV)  # 64 rows + a guard band
+    flags = torch.zeros(32, dtype=torch.int32, device=DEV)
+    src = torch.arange(4 * 8, dtype=torch.int16, device=DEV).view(4, 8)
+    cap = 64 * 16  # bytes the kernel may write: the guard band must stay zero
+    _ext.ext().ep_exchange("push", src, [flags.data_ptr()], [buf.data_ptr()], 0, 1, 1, [0], [4], [62],
+                           0, cap, st)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 8
+    assert torch.equal(buf[62:64], src[:2]) and int(buf[64:].abs().sum()) == 0
+    st.zero_()
+    _ext.ext().ep_exchange("push", src, [flags.data_ptr()], [buf.data_ptr()], 0, 2, 1, [0], [4], [10],
+                           0, cap, st)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0 and torch.equal(buf[10:14], src)

@@ -71,3 +71,22 @@ def test_cpu_plumbing_config_and_resume(tmp_path):
     assert r["resumed"] == L[5:], (r["resumed"], L[5:])  # exact replay after resume
     assert r["refused"]
     assert os.path.exists(tmp_path / "ck" / "cpu_plumbing" / "5" / ".complete")
+
+
+def _jsonl_run(rank, world, root, path):
+    cfg = json.loads(json.dumps(CFG))
+    cfg["mesh"] = {"dp": world}
+    cfg["data"]["global_batch_size"] = 4 * world
+    cfg["optimizer"]["scheduler"]["total_steps"] = 3
+    cfg["logging"] = {"jsonl": path}
+    cfg["checkpointing"] = {"save_steps": 10**9, "resume": None}
+    tr = _trainer(cfg, rank, world, root)
+    tr.train()
+
+
+def test_jsonl_metrics_log(tmp_path):
+    path = str(tmp_path / "metrics.jsonl")
+    run_ranks(_jsonl_run, 1, str(tmp_path / "ck"), path, timeout_s=120, join_s=600)
+    rows = [json.loads(x) for x in open(path)]
+    assert [r["step"] for r in rows] == [1, 2, 3]
+    assert {"train/loss", "train/grad_norm", "train/lr", "perf/tps"} <= set(rows[0])
