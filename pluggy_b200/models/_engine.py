@@ -59,6 +59,23 @@ def _to_bf16(x: torch.Tensor) -> torch.Tensor:
     return y
 
 
+def _grad_bf16(dy: torch.Tensor) -> torch.Tensor:
+    """bf16 copy of the residual-stream gradient. The norm backward of the sublayer
+    above writes it next to the fp32 gradient and hangs it on that tensor; autograd
+    hands the same tensor object down when nothing was summed into it, otherwise
+    (or for the first sublayer) it is cast here."""
+    lp = getattr(dy, "_plg_bf16", None)
+    if lp is not None and lp.shape == dy.shape:
+        return lp
+    return _to_bf16(dy)
+
+
+def _norm_bwd_with_bf16(dh, x, n_w, r, dy):
+    dx, dxb, dnw = _norm.rmsnorm_bwd(dh, x, n_w, r, dres=dy, want_f32=True, want_bf16=True)
+    dx._plg_bf16 = dxb
+    return dx, dnw
+
+
 class AttnSublayer(torch.autograd.Function):
     """x [T,H] fp32 -> x + Attn(RMSNorm(x)) [T,H] fp32."""
 
@@ -91,7 +108,7 @@ class AttnSublayer(torch.autograd.Function):
         Hq, Hk, d, B, S = cfg.Hq, cfg.Hk, cfg.d, cfg.B, cfg.S
         T = x.shape[0]
         dy = dy.contiguous()
-        dy_b = _to_bf16(dy)
+        dy_b = _grad_bf16(dy)
         o2 = o.view(T, Hq * d)
         do = linear_dgrad(dy_b, w_o)
         dWo = linear_wgrad(dy_b, o2)
@@ -108,7 +125,7 @@ class AttnSublayer(torch.autograd.Function):
                                           inv_freq=inv_freq, eps=cfg.qk_eps)
         dh = linear_dgrad(dqkv, w_qkv)
         dWqkv = linear_wgrad(dqkv, h)
-        dx, _, dnw = _norm.rmsnorm_bwd(dh, x, n_w, r, dres=dy, want_f32=True)
+        dx, dnw = _norm_bwd_with_bf16(dh, x, n_w, r, dy)
         nq, nk = Hq * d, Hk * d
         return (dx, dnw, dWqkv[:nq], dWqkv[nq:nq + nk], dWqkv[nq + nk:], dWo, dqn, dkn,
                 None, None, None)
@@ -134,13 +151,13 @@ class MlpSublayer(torch.autograd.Function):
         x, n_w, r, h, gu, a = ctx.saved_tensors
         w_gu, w_d = ctx.lowp
         dy = dy.contiguous()
-        dy_b = _to_bf16(dy)
+        dy_b = _grad_bf16(dy)
         da = linear_dgrad(dy_b, w_d)
         dWd = linear_wgrad(dy_b, a)
         dgu = glu_bwd(gu, da, ctx.kind)
         dh = linear_dgrad(dgu, w_gu)
         dWgu = linear_wgrad(dgu, h)
-        dx, _, dnw = _norm.rmsnorm_bwd(dh, x, n_w, r, dres=dy, want_f32=True)
+        dx, dnw = _norm_bwd_with_bf16(dh, x, n_w, r, dy)
         Fh = gu.shape[1] // 2
         return dx, dnw, dWgu[:Fh], dWgu[Fh:], dWd, None, None, None
 
