@@ -531,6 +531,25 @@ void fsdp_push_b(const at::Tensor& shard, const at::Tensor& table, std::vector<i
                  shard.numel() * shard.element_size() / 16, shard.data_ptr(), cur_stream());
 }
 
+void tp_norm_ag(const at::Tensor& x, const c10::optional<at::Tensor>& w, at::Tensor& rstd,
+                at::Tensor& out, std::vector<int64_t> flags, std::vector<int64_t> bufs, int64_t rank,
+                int64_t epoch, int64_t B, int64_t S, double eps, int64_t cap_bytes,
+                const c10::optional<at::Tensor>& status) {
+  check_cuda(x, "x");
+  TORCH_CHECK((is_f32(x) || is_bf16(x)) && x.dim() == 2 && x.stride(1) == 1, "tp_norm_ag: x [rows, W]");
+  TORCH_CHECK(is_f32(rstd) && rstd.is_contiguous() && rstd.numel() == x.size(0), "tp_norm_ag: rstd [rows]");
+  TORCH_CHECK(is_bf16(out) && out.dim() == 2 && out.size(1) == x.size(1) && out.stride(1) == 1,
+              "tp_norm_ag: out bf16 [B*S, W]");
+  if (w.has_value()) TORCH_CHECK(is_f32(*w) && w->numel() == x.size(1), "tp_norm_ag: fp32 weight [W]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto a = tp_args(flags, bufs, rank, epoch, B, S, x.size(1), cap_bytes, status);
+  TORCH_CHECK(x.size(0) == B * (S / static_cast<int64_t>(flags.size())), "tp_norm_ag: x must be [B*S/n, W]");
+  TORCH_CHECK(out.size(0) == B * S, "tp_norm_ag: out must be [B*S, W]");
+  plg::tp_norm_ag_push(a, x.data_ptr(), is_f32(x), x.stride(0), w.has_value() ? w->data_ptr<float>() : nullptr,
+                       static_cast<float>(eps), rstd.data_ptr<float>(), cur_stream());
+  plg::tp_ag_finish(a, out.data_ptr(), out.stride(0), cur_stream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -565,6 +584,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_exchange", &ep_exchange, py::arg("op"), py::arg("t"), py::arg("flags"), py::arg("bufs"),
         py::arg("rank"), py::arg("epoch"), py::arg("kind"), py::arg("src_start"), py::arg("count"),
         py::arg("dst_off"), py::arg("rows"), py::arg("cap_bytes"), py::arg("status") = py::none());
+  m.def("tp_norm_ag", &tp_norm_ag, py::arg("x"), py::arg("w"), py::arg("rstd"), py::arg("out"),
+        py::arg("flags"), py::arg("bufs"), py::arg("rank"), py::arg("epoch"), py::arg("B"), py::arg("S"),
+        py::arg("eps"), py::arg("cap_bytes"), py::arg("status") = py::none());
   m.def("tp_collective", &tp_collective, py::arg("op"), py::arg("t"), py::arg("flags"), py::arg("bufs"),
         py::arg("rank"), py::arg("epoch"), py::arg("B"), py::arg("S"), py::arg("cap_bytes"),
         py::arg("status") = py::none());

@@ -24,7 +24,9 @@
 // records a status code and returns.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstring>
+#include <type_traits>
 #include <stdexcept>
 #include <string>
 
@@ -295,6 +297,64 @@ __global__ void __launch_bounds__(256) tp_ag_finish_kernel(TpArgs a, __nv_bfloat
   }
 }
 
+// ------------------------------------------------ RMSNorm fused with the AG push
+// One CTA per row at a time, W / 8 threads, 8 channels (one 16-byte bf16 chunk) per
+// thread: the norm's output never lands in local memory, each thread stores its
+// chunk into every rank's receive slot (a warp writes 512 contiguous bytes).
+template <typename TX>
+__global__ void __launch_bounds__(1024) tp_norm_ag_push_kernel(TpArgs a, const TX* __restrict__ x,
+                                                               long long ld, const float* __restrict__ w,
+                                                               float eps, float* __restrict__ rstd_out) {
+  __shared__ float s_red[32];
+  const long long rows = a.B * (a.S / a.n);
+  const int c0 = threadIdx.x * 8;
+  float wv[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) wv[k] = w ? w[c0 + k] : 1.f;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
+    float v[8];
+    if constexpr (std::is_same<TX, float>::value) {
+      const float4 u0 = *reinterpret_cast<const float4*>(x + r * ld + c0);
+      const float4 u1 = *reinterpret_cast<const float4*>(x + r * ld + c0 + 4);
+      v[0] = u0.x; v[1] = u0.y; v[2] = u0.z; v[3] = u0.w;
+      v[4] = u1.x; v[5] = u1.y; v[6] = u1.z; v[7] = u1.w;
+    } else {
+      const uint4 u = *reinterpret_cast<const uint4*>(x + r * ld + c0);
+      const uint32_t* uu = reinterpret_cast<const uint32_t*>(&u);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = unpack_bf16x2(uu[k]);
+        v[2 * k] = f.x;
+        v[2 * k + 1] = f.y;
+      }
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) ss += v[k] * v[k];
+    ss = warp_sum(ss);
+    if (lane == 0) s_red[warp] = ss;
+    __syncthreads();
+    if (warp == 0) {
+      float t = lane < nw ? s_red[lane] : 0.f;
+      t = warp_sum(t);
+      if (lane == 0) s_red[0] = t;
+    }
+    __syncthreads();
+    const float rs = rsqrtf(s_red[0] / a.W + eps);
+    __syncthreads();  // s_red is reused by the next row
+    if (threadIdx.x == 0 && rstd_out) rstd_out[r] = rs;
+    uint4 o;
+    o.x = pack_bf16x2(v[0] * rs * wv[0], v[1] * rs * wv[1]);
+    o.y = pack_bf16x2(v[2] * rs * wv[2], v[3] * rs * wv[3]);
+    o.z = pack_bf16x2(v[4] * rs * wv[4], v[5] * rs * wv[5]);
+    o.w = pack_bf16x2(v[6] * rs * wv[6], v[7] * rs * wv[7]);
+    const long long dst16 = ((a.rank * rows + r) * a.W + c0) / 8;
+    for (int p = 0; p < a.n; ++p) peer_store16(a, (a.rank + p) % a.n, dst16, o);
+  }
+  __threadfence_system();
+}
+
 // ------------------------------------------------------------- expert parallel
 __global__ void __launch_bounds__(256) ep_push_kernel(TpArgs a, EpSegs sg, const __nv_bfloat16* __restrict__ src,
                                                       long long ld) {
@@ -505,6 +565,24 @@ void fsdp_push(const TpArgs& a, const int64_t* table, int k, long long total16, 
   if (total16 <= 0) return;
   comm::fsdp_push_kernel<<<tp_grid(total16, 148 * 4), 256, 0, st>>>(
       a, table, k, total16, reinterpret_cast<const uint4*>(shard));
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+void tp_norm_ag_push(const TpArgs& a, const void* x, bool x_fp32, long long ld, const float* w,
+                     float eps, float* rstd, cudaStream_t st) {
+  tp_check(a, ld, x, "tp_norm_ag_push");
+  if (a.W % 256 || a.W > 8192)
+    throw std::invalid_argument("tp_norm_ag_push: width must be a multiple of 256, at most 8192");
+  const long long rows = a.B * (a.S / a.n);
+  if (rows <= 0) return;
+  const unsigned grid = static_cast<unsigned>(std::min<long long>(rows, 148LL * 8));
+  const unsigned threads = static_cast<unsigned>(a.W / 8);
+  if (x_fp32)
+    comm::tp_norm_ag_push_kernel<float><<<grid, threads, 0, st>>>(a, reinterpret_cast<const float*>(x), ld,
+                                                                  w, eps, rstd);
+  else
+    comm::tp_norm_ag_push_kernel<__nv_bfloat16><<<grid, threads, 0, st>>>(
+        a, reinterpret_cast<const __nv_bfloat16*>(x), ld, w, eps, rstd);
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 

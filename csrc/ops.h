@@ -188,6 +188,11 @@ void tp_rs_finish(const TpArgs& a, void* out, long long ld_out, cudaStream_t str
 void tp_ag_push(const TpArgs& a, const void* shard, long long ld, cudaStream_t stream);
 // AG: signal, wait for every peer, copy the slots of the own receive buffer into out [B*S, W]
 void tp_ag_finish(const TpArgs& a, void* out, long long ld_out, cudaStream_t stream);
+// RMSNorm fused with the AG push: y = x * rsqrt(mean(x^2) + eps) * w of this rank's
+// shard rows [B*S/n, W] (x fp32 or bf16), stored as bf16 straight into slot `rank` of
+// every rank's receive buffer; rstd [B*S/n] kept locally. Finish with tp_ag_finish.
+void tp_norm_ag_push(const TpArgs& a, const void* x, bool x_fp32, long long ld, const float* w,
+                     float eps, float* rstd, cudaStream_t stream);
 // Expert-parallel row exchange (MoE dispatch / combine) over peer memory: segment p
 // of the source rows, [src_start[p], src_start[p] + count[p]), goes to rank p's
 // buffer (bufs[p]) at row dst_off[p]. Rows are W bf16 (W % 8 == 0; any 2-byte data).

@@ -91,6 +91,23 @@ class TPComm:
         ext().tp_collective("ag_finish", out, flags, bufs, self.rank, e, B, S, cap, st)
         return out.view(B, S, W)
 
+    def norm_all_gather_seq(self, x: torch.Tensor, w: torch.Tensor | None, eps: float):
+        """RMSNorm of this rank's rows fused with the sequence all-gather:
+        x [B, S / n, W] (fp32 or bf16) -> (y [B, S, W] bf16 on every rank, rstd [B * S / n])."""
+        B, s, W = x.shape
+        S = s * self.n
+        x2 = x.reshape(B * s, W)
+        if x2.dtype not in (torch.float32, torch.bfloat16):
+            x2 = x2.float()
+        x2 = x2.contiguous()
+        flags, bufs, e, cap = self._args(_AG, B * S * W * 2)
+        out = torch.empty((B * S, W), dtype=torch.bfloat16, device=x.device)
+        rstd = torch.empty(B * s, dtype=torch.float32, device=x.device)
+        wf = None if w is None else w.detach().float().contiguous()
+        ext().tp_norm_ag(x2, wf, rstd, out, flags, bufs, self.rank, e, B, S, float(eps), cap,
+                         status_word(x.device))
+        return out.view(B, S, W), rstd
+
     def gemm_reduce_scatter(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         """``(x [B, S, K] @ w [N, K]^T)`` summed over the axis, sequence-sharded:
         [B, S / n, N]. One tcgen05 GEMM whose epilogue stores into the owners'
@@ -136,6 +153,49 @@ class ScatterSeq(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g):
         return ctx.comm.all_gather_seq(g.contiguous()).to(ctx.dtype), None
+
+
+class NormGatherSeq(torch.autograd.Function):
+    """Pre-norm of a sequence-parallel block fused with the gather of its output:
+    x [B, S/n, W] -> RMSNorm(x) * w as bf16 [B, S, W] on every rank.
+    backward: reduce-scatter of the gradient, then the norm backward on this rank's rows."""
+
+    @staticmethod
+    def forward(ctx, x, weight, comm, eps):
+        y, rstd = comm.norm_all_gather_seq(x, weight, eps)
+        ctx.comm = comm
+        ctx.save_for_backward(x, weight, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, g):
+        from pluggy_b200.ops.norm import rmsnorm_bwd
+
+        x, weight, rstd = ctx.saved_tensors
+        B, s, W = x.shape
+        dy = ctx.comm.reduce_scatter_seq(g.contiguous()).reshape(B * s, W)
+        xf = x.reshape(B * s, W)
+        if xf.dtype not in (torch.float32, torch.bfloat16):
+            xf = xf.float()
+        dxf, _, dw = rmsnorm_bwd(dy, xf.contiguous(), None if weight is None else weight.detach().float(),
+                                 rstd, want_f32=True, want_dw=weight is not None)
+        dx = dxf.view(B, s, W).to(x.dtype)
+        return dx, (None if weight is None else dw.to(weight.dtype)), None, None
+
+
+class TPNormGather(torch.nn.Module):
+    """Drop-in for a block's pre-norm under sequence parallelism: returns the
+    gathered, normalised activation, so the column-parallel linears that follow
+    must not gather again. Keeps the norm's ``weight`` (same parameter, same
+    state-dict key)."""
+
+    def __init__(self, norm: torch.nn.Module, comm, eps: float):
+        super().__init__()
+        self.weight = norm.weight
+        self.comm, self.eps = comm, eps
+
+    def forward(self, x):
+        return NormGatherSeq.apply(x, self.weight, self.comm, self.eps)
 
 
 class RowParallelMMRS(torch.autograd.Function):

@@ -92,12 +92,15 @@ class _SharedInput:
     forward gathers once and autograd sums the branches' grads before the single
     backward reduction."""
 
-    def __init__(self, mesh, dim: str, sequence_parallel: bool, comm=None):
+    def __init__(self, mesh, dim: str, sequence_parallel: bool, comm=None, pre_gathered: bool = False):
         self.mesh, self.dim, self.sp, self.comm = mesh, dim, sequence_parallel, comm
+        self.pre_gathered = pre_gathered  # the preceding norm already gathered its output
         self._src = None
         self._out = None
 
     def __call__(self, x):
+        if self.pre_gathered:
+            return x
         if x is not self._src:
             if self.sp and self.comm is not None:
                 from pluggy_b200.comm.tp_fused import GatherSeq
@@ -306,6 +309,14 @@ class TensorParallel:
         self.model.load_state_dict(local)
 
 
+def _prenorm_forward():
+    """The pre-norm block forward (``x + attn(norm1(x))``, ``x + ffn(norm2(x))``) whose
+    norms may be fused with the sequence gather."""
+    from pluggy_b200.models.qwen3 import Qwen3TransformerBlock
+
+    return Qwen3TransformerBlock.forward
+
+
 def _attention_modules(block):
     for name in ("gqa", "attn", "attention"):
         mod = getattr(block, name, None)
@@ -344,7 +355,17 @@ def parallelize_tp(model: nn.Module, mesh, dim: str = "tp", sequence_parallel: b
         _, att = _attention_modules(blk)
         assert att.num_heads % n == 0 and att.num_kv_heads % n == 0, \
             f"tp={n} must divide the query ({att.num_heads}) and KV ({att.num_kv_heads}) heads"
-        qkv_in = _SharedInput(mesh, dim, sequence_parallel, comm)
+        # pre-norms fused with the sequence gather (peer-memory path, RMSNorm pre-norms)
+        fuse_norm = (comm is not None and isinstance(getattr(blk, "norm1", None), nn.RMSNorm)
+                     and isinstance(getattr(blk, "norm2", None), nn.RMSNorm)
+                     and type(blk).forward is _prenorm_forward())
+        if fuse_norm:
+            from pluggy_b200.comm.tp_fused import TPNormGather
+            from pluggy_b200.models.common import norm_eps
+
+            blk.norm1 = TPNormGather(blk.norm1, comm, norm_eps(blk.norm1))
+            blk.norm2 = TPNormGather(blk.norm2, comm, norm_eps(blk.norm2))
+        qkv_in = _SharedInput(mesh, dim, sequence_parallel, comm, pre_gathered=fuse_norm)
         att.q_proj = ColumnParallelLinear(att.q_proj, mesh, dim, sequence_parallel, qkv_in)
         att.k_proj = ColumnParallelLinear(att.k_proj, mesh, dim, sequence_parallel, qkv_in)
         att.v_proj = ColumnParallelLinear(att.v_proj, mesh, dim, sequence_parallel, qkv_in)
@@ -352,7 +373,7 @@ def parallelize_tp(model: nn.Module, mesh, dim: str = "tp", sequence_parallel: b
         att.num_heads //= n
         att.num_kv_heads //= n
         ffn = blk.ffn
-        gu_in = _SharedInput(mesh, dim, sequence_parallel, comm)
+        gu_in = _SharedInput(mesh, dim, sequence_parallel, comm, pre_gathered=fuse_norm)
         ffn.gate_proj = ColumnParallelLinear(ffn.gate_proj, mesh, dim, sequence_parallel, gu_in)
         ffn.up_proj = ColumnParallelLinear(ffn.up_proj, mesh, dim, sequence_parallel, gu_in)
         ffn.down_proj = RowParallelLinear(ffn.down_proj, mesh, dim, sequence_parallel, comm)
