@@ -21,6 +21,7 @@
 // delta = rowsum(dO * O) comes from a small pre-pass; a post-pass casts dQ.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <algorithm>
 #include <stdexcept>
@@ -136,9 +137,10 @@ __device__ __forceinline__ QTile make_qtile(const AttnArgs& a, int h, int qt) {
 // (word j is written after scores 2j and 2j+1 were consumed); m/l are
 // the running max (base 2, scaled) and sum. alpha is the factor the O row must
 // be multiplied by (1 when the max did not move by more than 2^kRescale).
-// kPoly moves one pair in four of the exponentials onto the FMA pipe
-// (exp2_poly2); it is used only on tiles without masked entries.
-template <bool kPoly>
+// kPolyMask selects which pairs of every eight pairs of exponentials run on the
+// FMA pipe (exp2_poly2) instead of the SFU; it is used only on tiles without
+// masked entries (0 on edge tiles).
+template <int kPolyMask>
 __device__ __forceinline__ void softmax_row(uint32_t (&v)[BKV], float scale2,
                                             float& m, float& l, float& alpha, float& rs) {
   float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
@@ -160,7 +162,7 @@ __device__ __forceinline__ void softmax_row(uint32_t (&v)[BKV], float scale2,
   for (int e = 0; e < BKV; e += 2) {
     float x0, x1, p0, p1;
     ffma2(x0, x1, __uint_as_float(v[e]), __uint_as_float(v[e + 1]), scale2, scale2, nm, nm);
-    if (kPoly && ((e >> 1) & 3) == 3) {
+    if (kPolyMask != 0 && ((kPolyMask >> ((e >> 1) & 7)) & 1)) {
       exp2_poly2(x0, x1, p0, p1);
     } else {
       p0 = fast_exp2(x0);
@@ -175,7 +177,7 @@ __device__ __forceinline__ void softmax_row(uint32_t (&v)[BKV], float scale2,
   m = m_new;
 }
 
-template <int D>
+template <int D, int kPolyMask>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, AttnArgs a, int pair_heads) {
@@ -430,9 +432,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
         for (int e = 0; e < BKV; ++e)
           v[e] = (e >= c_lo && e <= c_hi) ? v[e] : 0xff800000u;  // -inf
-        softmax_row<false>(v, scale2, m, l, alpha, rs);
+        softmax_row<0>(v, scale2, m, l, alpha, rs);
       } else {
-        softmax_row<true>(v, scale2, m, l, alpha, rs);
+        softmax_row<kPolyMask>(v, scale2, m, l, alpha, rs);
       }
       tmem_st_32x32b_x32(tS, *reinterpret_cast<const uint32_t(*)[32]>(v));
       tmem_st_32x32b_x32(tS + 32, *reinterpret_cast<const uint32_t(*)[32]>(v + 32));
@@ -1397,16 +1399,34 @@ static CUtensorMap map_dq_acc(float* base, int B, int S, int H, int d) {
   return m;
 }
 
+template <int D, int kPolyMask>
+static void fwd_launch_t(const AttnArgs& a, cudaStream_t st);
+
 template <int D>
 static void fwd_launch(const AttnArgs& a, cudaStream_t st) {
+  // share of the exponentials computed on the FMA pipe, in pairs per eight pairs
+  // (PLG_ATTN_POLY = 2, 3 or 4). Measured at B=8, S=4096, 16q/8kv x 128: 2 -> 0.552 ms,
+  // 3 -> 0.547 ms, 4 -> 0.575 ms (the FMA pipe becomes the limiter); 3 by default.
+  static const int poly = [] {
+    const char* e = std::getenv("PLG_ATTN_POLY");
+    const int v = e ? std::atoi(e) : 3;
+    return (v == 2 || v == 4) ? v : 3;
+  }();
+  if (poly == 3) return fwd_launch_t<D, 0xA4>(a, st);  // pairs 2, 5, 7
+  if (poly == 4) return fwd_launch_t<D, 0xAA>(a, st);  // odd pairs
+  return fwd_launch_t<D, 0x88>(a, st);                 // pairs 3, 7
+}
+
+template <int D, int kPolyMask>
+static void fwd_launch_t(const AttnArgs& a, cudaStream_t st) {
   using C = Fwd<D>;
   CUtensorMap tq = map_bshd(a.q, a.B, a.S, a.Hq, D, a.q_row);
   CUtensorMap tk = map_bshd(a.k, a.B, a.S, a.Hk, D, a.k_row);
   CUtensorMap tv = map_bshd(a.v, a.B, a.S, a.Hk, D, a.v_row);
-  set_max_smem_once(reinterpret_cast<const void*>(attn_fwd_kernel<D>), C::kSmem);
+  set_max_smem_once(reinterpret_cast<const void*>(attn_fwd_kernel<D, kPolyMask>), C::kSmem);
   static const int regs = [] {
     cudaFuncAttributes fa;
-    PLG_CUDA_CHECK(cudaFuncGetAttributes(&fa, attn_fwd_kernel<D>));
+    PLG_CUDA_CHECK(cudaFuncGetAttributes(&fa, attn_fwd_kernel<D, kPolyMask>));
     return fa.numRegs;
   }();
   // the setmaxnreg split assumes this launch allocation; with fewer registers
@@ -1421,7 +1441,8 @@ static void fwd_launch(const AttnArgs& a, cudaStream_t st) {
   const long long units = pair_heads ? n_q : (n_q + 1) / 2;
   const long long ctas = units * (pair_heads ? a.Hq / 2 : a.Hq) * a.B;
   if (ctas > 0x7fffffffLL) throw std::invalid_argument("attention: problem too large for one launch");
-  attn_fwd_kernel<D><<<static_cast<unsigned>(ctas), kFwdThreads, C::kSmem, st>>>(tq, tk, tv, a, pair_heads);
+  attn_fwd_kernel<D, kPolyMask><<<static_cast<unsigned>(ctas), kFwdThreads, C::kSmem, st>>>(tq, tk, tv, a,
+                                                                                       pair_heads);
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 
