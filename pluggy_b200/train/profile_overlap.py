@@ -22,8 +22,8 @@ from collections import defaultdict
 
 # kernel-name fragments that mark communication: NCCL's kernels and the fused
 # collective kernels of this package (pluggy_b200.comm)
-COMM_MARKERS = ("nccl", "plg_comm", "fused_allreduce", "allreduce_kernel", "reduce_scatter_kernel",
-                "all_gather_kernel")
+COMM_MARKERS = ("nccl", "plg::comm::", "comm::allreduce_avg", "sumsq_total", "tp_rs_", "tp_ag_",
+                "tp_norm_ag", "ep_push", "ep_finish", "fsdp_push")
 
 
 def union(intervals: list[tuple[float, float]]) -> list[tuple[float, float]]:
