@@ -224,6 +224,20 @@ def run_ours(args, rank, local_rank, world, device) -> dict:
 REF_DIR = os.path.join(ROOT, "baseline", "_ref")
 
 
+def _undecorated(fn):
+    """The function a timing decorator wraps. The reference's ``record_time``
+    (pluggy/utils.py:11-26) synchronises the device on both sides of every call and
+    does not set ``__wrapped__``, so the wrapped function is taken from the
+    wrapper's closure: both arms then time the same thing, the bare step."""
+    if hasattr(fn, "__wrapped__"):
+        return fn.__wrapped__
+    for cell in fn.__closure__ or ():
+        inner = cell.cell_contents
+        if callable(inner) and getattr(inner, "__name__", "") == "train_step":
+            return inner
+    return None
+
+
 def run_reference(args, rank, local_rank, world, device) -> dict:
     """The unmodified reference package (baseline/_ref) through its own Trainer.train_step."""
     import types
@@ -289,7 +303,7 @@ def run_reference(args, rank, local_rank, world, device) -> dict:
     batch = next(tr.prefetcher)
     real = tr.prefetcher
     tr.prefetcher = ResidentBatches(batch)
-    raw_step = T.train_step.__wrapped__ if hasattr(T.train_step, "__wrapped__") else None
+    raw_step = _undecorated(T.train_step)
 
     def step():
         if raw_step is not None:

@@ -550,6 +550,11 @@ void tp_norm_ag(const at::Tensor& x, const c10::optional<at::Tensor>& w, at::Ten
   plg::tp_ag_finish(a, out.data_ptr(), out.stride(0), cur_stream());
 }
 
+void set_peer_wait_deadline(int64_t ns) {
+  TORCH_CHECK(ns > 0, "set_peer_wait_deadline: the deadline must be positive");
+  plg::set_peer_wait_deadline_ns(static_cast<unsigned long long>(ns), cur_stream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -590,6 +595,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_collective", &tp_collective, py::arg("op"), py::arg("t"), py::arg("flags"), py::arg("bufs"),
         py::arg("rank"), py::arg("epoch"), py::arg("B"), py::arg("S"), py::arg("cap_bytes"),
         py::arg("status") = py::none());
+  m.def("set_peer_wait_deadline", &set_peer_wait_deadline, py::arg("ns"));
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd", &embedding_bwd);
   m.def("softcap", &softcap);

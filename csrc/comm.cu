@@ -45,14 +45,21 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
+// Deadline of every wait on a peer's flag, per device (default 2 s). The host
+// changes it with set_peer_wait_deadline_ns(): a test shortens it to make a wait
+// whose flag is never posted run out quickly; a job with very uneven ranks can
+// lengthen it.
+__device__ uint64_t g_peer_wait_deadline_ns = kWaitDeadlineNs;
+
 // wait until *p >= want (flags only grow); false after the deadline
 __device__ __forceinline__ bool wait_flag(const uint32_t* p, uint32_t want) {
   if (static_cast<int32_t>(ld_acquire_sys(p) - want) >= 0) return true;
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t deadline = *reinterpret_cast<volatile uint64_t*>(&g_peer_wait_deadline_ns);
   uint32_t spins = 0;
   while (true) {
     if (static_cast<int32_t>(ld_acquire_sys(p) - want) >= 0) return true;
-    if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > kWaitDeadlineNs) return false;
+    if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > deadline) return false;
   }
 }
 
@@ -584,6 +591,15 @@ void tp_norm_ag_push(const TpArgs& a, const void* x, bool x_fp32, long long ld, 
     comm::tp_norm_ag_push_kernel<__nv_bfloat16><<<grid, threads, 0, st>>>(
         a, reinterpret_cast<const __nv_bfloat16*>(x), ld, w, eps, rstd);
   PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+void set_peer_wait_deadline_ns(unsigned long long ns, cudaStream_t st) {
+  if (ns == 0) throw std::invalid_argument("set_peer_wait_deadline_ns: the deadline must be positive");
+  const uint64_t v = ns;
+  // ordered on the stream: kernels launched before the call keep the old deadline
+  PLG_CUDA_CHECK(cudaMemcpyToSymbolAsync(comm::g_peer_wait_deadline_ns, &v, sizeof(v), 0,
+                                         cudaMemcpyHostToDevice, st));
+  PLG_CUDA_CHECK(cudaStreamSynchronize(st));
 }
 
 }  // namespace plg

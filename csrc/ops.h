@@ -203,6 +203,9 @@ struct EpSegs {
 };
 void ep_push(const TpArgs& a, const EpSegs& sg, const void* src, long long ld, cudaStream_t stream);
 // signal (flag kind `kind`), wait for every peer, copy own buffer rows [0, rows) to out
+// Deadline (ns) of every peer-flag wait in the collective kernels on the
+// current device (default 2 s); ordered on `st` and synchronised.
+void set_peer_wait_deadline_ns(unsigned long long ns, cudaStream_t st);
 void ep_finish(const TpArgs& a, int kind, void* out, long long rows, long long ld_out,
                cudaStream_t stream);
 // FSDP unit all-gather over peer memory: table [k][3] int64 (units of 16 bytes):

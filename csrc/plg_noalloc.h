@@ -38,9 +38,12 @@ extern "C" {
 // cudaGetSymbolAddress (no allocation); make that first call before any
 // work on the device that must not see a runtime setup call.
 //
-// Returns 0 on success, 1 if total_chunks exceeds PLG_NOALLOC_MAX_CHUNKS (or
-// is negative) with nothing enqueued, 2 on a CUDA runtime error. A nonzero
-// return also prints one line naming the problem to stderr.
+// Returns 0 on success; 1 if total_chunks exceeds PLG_NOALLOC_MAX_CHUNKS, is
+// negative, or is positive with ntensors < 1 (nothing enqueued); 2 on a CUDA
+// runtime error. A CUDA error that is already pending on the calling thread when
+// the call starts is reported as 2 and left pending (cudaPeekAtLastError), with
+// nothing enqueued. A nonzero return also prints one line naming the problem to
+// stderr.
 int plg_multi_sumsq_noalloc(const int64_t* table, int ntensors, long long total_chunks,
                             float* total_out, void* stream);
 

@@ -589,6 +589,19 @@ extern "C" __attribute__((visibility("default"))) int plg_multi_sumsq_noalloc(
                  total_chunks, PLG_NOALLOC_MAX_CHUNKS);
     return 1;
   }
+  if (total_chunks > 0 && (ntensors < 1 || table == nullptr)) {
+    std::fprintf(stderr, "plg_multi_sumsq_noalloc: %lld chunks but an empty tensor table\n",
+                 total_chunks);
+    return 1;
+  }
+  // an error already pending on this thread belongs to the caller: report it
+  // without consuming it, and enqueue nothing
+  cudaError_t pending = cudaPeekAtLastError();
+  if (pending != cudaSuccess) {
+    std::fprintf(stderr, "plg_multi_sumsq_noalloc: a CUDA error was already pending (%s)\n",
+                 cudaGetErrorString(pending));
+    return 2;
+  }
   // scratch address per device, looked up once (cudaGetSymbolAddress allocates nothing)
   static std::mutex mu;
   static float* scratch[64] = {};
@@ -620,8 +633,12 @@ extern "C" __attribute__((visibility("default"))) int plg_multi_sumsq_noalloc(
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     plg::multi_sumsq_kernel<<<plg::grid_for(total_chunks, 1), 512, 0, st>>>(table, ntensors,
                                                                           total_chunks, part);
-    plg::reduce_partials_kernel<<<1, 1024, 0, st>>>(part, total_chunks, total_out);
+    // nothing was pending before the launch, so an error now is this launch's
     e = cudaGetLastError();
+    if (e == cudaSuccess) {
+      plg::reduce_partials_kernel<<<1, 1024, 0, st>>>(part, total_chunks, total_out);
+      e = cudaGetLastError();
+    }
   }
   if (e != cudaSuccess) {
     std::fprintf(stderr, "plg_multi_sumsq_noalloc: launch failed (%s)\n", cudaGetErrorString(e));

@@ -112,6 +112,11 @@ def attend(Q, K, V, attention_mask=None, window: int = 0, scale=None):
         if q.is_cuda and q.shape[-1] in (64, 128):
             o = flash_attention(q.to(torch.bfloat16).contiguous(), k.to(torch.bfloat16).contiguous(),
                                 v.to(torch.bfloat16).contiguous(), True, window, scale).to(Q.dtype)
+        elif q.is_cuda:
+            # head_dim outside the sm_100a kernels' {64, 128} (Gemma-4's 256/512 global
+            # heads): PyTorch SDPA in bf16, as the reference does for every head
+            # (pluggy/models/gemma4/gemma4.py:187-217); never the fp32 S x S math
+            return sdpa_causal_bf16(Q, K, V, window, scale).to(Q.dtype)
         else:
             o = attention_reference(q, k, v, causal=True, window=window, scale=scale)
         return o.transpose(1, 2)
@@ -122,6 +127,19 @@ def attend(Q, K, V, attention_mask=None, window: int = 0, scale=None):
         m = m & ((i[:, None] - i[None, :]) < window)
     m = m[None, None] & attention_mask[:, None, None, :].bool()
     return sdpa_masked(Q, K, V, m, scale=scale)
+
+
+def sdpa_causal_bf16(Q, K, V, window: int = 0, scale=None):
+    """[B,H,S,d] causal (+ sliding window) attention through PyTorch SDPA in bf16."""
+    Hq, Hk = Q.shape[1], K.shape[1]
+    q, k, v = (t.to(torch.bfloat16) for t in (Q, K, V))
+    if not window:
+        return F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=scale,
+                                              enable_gqa=Hq != Hk)
+    S = Q.shape[-2]
+    i = torch.arange(S, device=Q.device)
+    m = (i[None, :] <= i[:, None]) & ((i[:, None] - i[None, :]) < window)
+    return F.scaled_dot_product_attention(q, k, v, attn_mask=m, scale=scale, enable_gqa=Hq != Hk)
 
 
 class SwiGLU(nn.Module):

@@ -7,7 +7,9 @@ is built in-tree by ``python setup.py build_ext --inplace`` (or
 ``__graft_entry__.build()``).
 
 A per-device int32 status word is shared by every kernel that has bounded
-waits; ``check_status()`` raises if any of them timed out.
+waits; ``check_status()`` raises if any of them timed out. The deadline of the
+collective kernels' waits on a peer's flag is 2 s by default and is set per
+device with ``set_peer_wait_deadline()``.
 """
 
 from __future__ import annotations
@@ -76,3 +78,17 @@ def check_status(device: torch.device | None = None, reset: bool = True) -> None
             t.zero_()
         raise RuntimeError(f"sm_100a kernel reported status {code}: "
                            f"{_STATUS_NAMES.get(code, 'unknown')}")
+
+
+DEFAULT_PEER_WAIT_S = 2.0
+
+
+def set_peer_wait_deadline(seconds: float, device: torch.device | None = None) -> None:
+    """Deadline of every wait on a peer's flag in the collective kernels of ``device``
+    (kernels launched after the call on the current stream use it)."""
+    ns = int(seconds * 1e9)
+    if ns <= 0:
+        raise ValueError("the deadline must be positive")
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        ext().set_peer_wait_deadline(ns)

@@ -122,6 +122,8 @@ class Trainer:
         self.save_steps = ck.get("save_steps", 10**9)
         self.resume_scheduler = ck.get("resume_scheduler", True)
         self.resume_wandb_id = None
+        # how often (optimizer steps) the kernels' status word is read; 0 = never
+        self.status_check_steps = int(self.config.get("status_check_steps", 1))
         self.start_step = self._resume()
         self._setup_wandb()
         self.prefetcher = CUDAPrefetcher(self.dataloader, self.device)
@@ -236,7 +238,6 @@ class Trainer:
                 f.write(json.dumps({"step": step, **log}) + "\n")
 
     # -------------------------------------------------------------- checkpoint
-    @debug_time
     def _model_sharded(self) -> bool:
         """Tensor or expert parallelism: ranks hold different parameter shards."""
         return getattr(self, "tp", None) is not None or getattr(self, "ep", None) is not None
@@ -268,7 +269,20 @@ class Trainer:
             local[name] = full
         self.model.load_state_dict(local)
 
+    def check_device_status(self) -> None:
+        """Raise if a bounded wait in one of this rank's kernels gave up since the
+        last check (a peer that never answered, a stalled pipeline stage). Such a
+        kernel returns early and leaves its outputs incomplete, so training must
+        not go on from them, nor checkpoint them. One int32 read per call."""
+        if self.device.type != "cuda":
+            return
+        from pluggy_b200.ops import _ext
+
+        if _ext.available():
+            _ext.check_status(self.device)
+
     def checkpoint(self, step: int) -> None:
+        self.check_device_status()
         if self.parallelism == "fsdp2" and self.dp_size > 1:
             self._checkpoint_sharded(step)
         elif self._model_sharded():
@@ -424,6 +438,8 @@ class Trainer:
         tokens_per_step = self.config["data"]["seq_len"] * self.global_batch_size
         for step in range(n_steps):
             metrics, t = self.train_step()
+            if self.status_check_steps and (step + 1) % self.status_check_steps == 0:
+                self.check_device_status()
             if self.rank == 0:
                 print(self._line(step, metrics, tokens_per_step, t))
         self._print_peak()
@@ -437,6 +453,8 @@ class Trainer:
         try:
             for step in range(self.start_step, self.num_train_steps):
                 metrics, t = self.train_step()
+                if self.status_check_steps and (step + 1) % self.status_check_steps == 0:
+                    self.check_device_status()
                 if ((step + 1) % self.save_steps == 0 and step != 0) or (step + 1) == self.num_train_steps:
                     self.checkpoint(step + 1)
                 if self.rank == 0:

@@ -442,3 +442,40 @@ def test_peer_store_bounds_are_enforced():
                            0, cap, st)
     torch.cuda.synchronize()
     assert int(st.item()) == 0 and torch.equal(buf[10:14], src)
+
+
+def test_peer_wait_times_out_with_status():
+    """A collective kernel whose peer never posts its flag gives up after the
+    deadline, records status 5 (timed out waiting for a peer) and returns: the
+    context stays usable and check_status raises and resets the word. One GPU
+    plays rank 0 of two; "rank 1" is a zeroed flag table nobody writes."""
+    import time
+
+    from pluggy_b200.ops import _ext
+
+    st = _ext.status_word()
+    st.zero_()
+    flags = [torch.zeros(4096, dtype=torch.int32, device=DEV) for _ in range(2)]
+    bufs = [torch.zeros(64, 8, dtype=torch.int16, device=DEV) for _ in range(2)]
+    out = torch.zeros(4, 8, dtype=torch.int16, device=DEV)
+    _ext.set_peer_wait_deadline(1e-3)
+    try:
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        _ext.ext().ep_exchange("finish", out, [f.data_ptr() for f in flags],
+                               [b.data_ptr() for b in bufs], 0, 1, 0, [0, 0], [0, 0], [0, 0], 4,
+                               64 * 16, st)
+        torch.cuda.synchronize()
+        waited = time.perf_counter() - t0
+    finally:
+        _ext.set_peer_wait_deadline(_ext.DEFAULT_PEER_WAIT_S)
+    assert int(st.item()) == 5
+    assert waited < 1.0  # the 1 ms deadline, not the 2 s default
+    with pytest.raises(RuntimeError, match="status 5"):
+        _ext.check_status()
+    assert int(st.item()) == 0
+    # the device still runs work after the timed-out kernel
+    x = torch.ones(1024, device=DEV)
+    assert float((x * 2).sum()) == 2048.0
+    # rank 0's own flag was posted (signal before wait); the missing peer's was not
+    assert int(flags[0][0]) == 1 and int(flags[0][1]) == 0

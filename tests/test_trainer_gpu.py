@@ -1,0 +1,57 @@
+"""The trainer reads the kernels' status word: a bounded wait that gave up
+during a step stops training (and a checkpoint) with an error on that rank."""
+
+import json
+
+import pytest
+
+from tests._dist import run_ranks
+
+pytestmark = pytest.mark.gpu
+
+CFG = {
+    "run_name": "status_check", "seed": 0, "parallelism": "ddp", "mesh": {"dp": 1},
+    "model": {"name": "qwen3_dense", "config": {
+        "num_layers": 2, "emb_dim": 256, "num_heads": 4, "num_kv_heads": 2, "head_dim": 128,
+        "ffn_dim": 512, "vocab_size": 1024}},
+    "optimizer": {"name": "adamw", "config": {"lr": 1e-3, "weight_decay": 0.1, "betas": [0.9, 0.95]},
+                  "max_norm": 1.0, "scheduler": {"type": "cosine", "total_steps": 10, "warmup_ratio": 0.1}},
+    "objective": {"name": "AR", "config": {"ignore_index": -100, "fused_linear_ce": True,
+                                           "ce_chunk_size": 256}},
+    "data": {"synthetic": {"kind": "uniform"}, "seq_len": 256, "micro_batch_size": 2,
+             "global_batch_size": 2, "seed": 0},
+}
+
+
+def _run(rank, world, root, out):
+    from pluggy_b200.ops import _ext
+    from pluggy_b200.train.trainer import Trainer
+
+    tr = Trainer(json.loads(json.dumps(CFG)), rank=rank, local_rank=rank, world_size=world,
+                 checkpoint_root=root)
+    tr.train_n_step_test(1)  # healthy step: no error
+    res = {}
+    # a kernel that timed out waiting for a peer leaves status 5 behind
+    _ext.status_word(tr.device).fill_(5)
+    try:
+        tr.train_n_step_test(1)
+        res["step"] = "no error"
+    except RuntimeError as e:
+        res["step"] = str(e)
+    _ext.status_word(tr.device).fill_(5)
+    try:
+        tr.checkpoint(2)
+        res["checkpoint"] = "no error"
+    except RuntimeError as e:
+        res["checkpoint"] = str(e)
+    tr.train_n_step_test(1)  # the word was reset by the check: training can go on
+    with open(out, "w") as f:
+        json.dump(res, f)
+
+
+def test_trainer_raises_on_kernel_status(tmp_path):
+    out = str(tmp_path / "res.json")
+    run_ranks(_run, 1, str(tmp_path / "ck"), out, timeout_s=120, join_s=600, backend="nccl")
+    r = json.load(open(out))
+    assert "status 5" in r["step"], r
+    assert "status 5" in r["checkpoint"], r
