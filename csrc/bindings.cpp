@@ -405,6 +405,82 @@ void symm_allreduce_avg_b(std::vector<int64_t> data, std::vector<int64_t> flags,
   plg::symm_allreduce_avg(a, ns, accumulate, cur_stream());
 }
 
+plg::Zero1Args zero1_args(const std::vector<int64_t>& grads, const std::vector<int64_t>& params,
+                          const std::vector<int64_t>& flags, const std::vector<int64_t>& slots,
+                          int64_t offset, int64_t numel, int64_t rank, int64_t epoch, int64_t chunks,
+                          const c10::optional<at::Tensor>& status) {
+  const int n = static_cast<int>(grads.size());
+  TORCH_CHECK(n >= 1 && n <= plg::kSymmMaxRanks && params.size() == grads.size() &&
+                  flags.size() == grads.size() && slots.size() == grads.size(),
+              "zero1: one pointer per rank");
+  plg::Zero1Args a{};
+  for (int i = 0; i < n; ++i) {
+    a.grads[i] = reinterpret_cast<float*>(grads[i]);
+    a.params[i] = reinterpret_cast<float*>(params[i]);
+    a.flags[i] = reinterpret_cast<uint32_t*>(flags[i]);
+    a.sumsq[i] = reinterpret_cast<float*>(slots[i]);
+  }
+  a.offset = offset;
+  a.numel = numel;
+  a.rank = static_cast<int>(rank);
+  a.nranks = n;
+  a.chunks = static_cast<int>(chunks);
+  a.epoch = static_cast<uint32_t>(epoch);
+  a.status = status.has_value() ? status->data_ptr<int>() : nullptr;
+  return a;
+}
+
+void zero1_rs_b(std::vector<int64_t> grads, std::vector<int64_t> params, std::vector<int64_t> flags,
+                std::vector<int64_t> slots, int64_t offset, int64_t numel, int64_t rank, int64_t epoch,
+                int64_t chunks, const c10::optional<at::Tensor>& norm_sq, bool accumulate,
+                const c10::optional<at::Tensor>& status) {
+  auto a = zero1_args(grads, params, flags, slots, offset, numel, rank, epoch, chunks, status);
+  float* ns = nullptr;
+  if (norm_sq.has_value()) {
+    TORCH_CHECK(is_f32(*norm_sq) && norm_sq->is_cuda(), "norm_sq: fp32 device tensor");
+    ns = norm_sq->data_ptr<float>();
+  }
+  plg::zero1_reduce_scatter(a, ns, accumulate, cur_stream());
+}
+
+void zero1_adamw_ag_b(std::vector<int64_t> grads, std::vector<int64_t> params, std::vector<int64_t> flags,
+                      std::vector<int64_t> slots, int64_t offset, int64_t numel, int64_t rank,
+                      int64_t epoch, int64_t chunks, std::vector<double> lr, std::vector<double> wd,
+                      double beta1, double beta2, double eps, double bc1, double bc2,
+                      const c10::optional<at::Tensor>& grad_scale, const at::Tensor& rows,
+                      at::Tensor& exp_avg, at::Tensor& exp_avg_sq,
+                      const c10::optional<at::Tensor>& status) {
+  auto a = zero1_args(grads, params, flags, slots, offset, numel, rank, epoch, chunks, status);
+  TORCH_CHECK(lr.size() == wd.size() && lr.size() >= 1 && lr.size() <= 4, "zero1 adamw: 1..4 param groups");
+  TORCH_CHECK(rows.is_cuda() && rows.scalar_type() == at::kLong && rows.dim() == 2 && rows.size(1) == 3 &&
+                  rows.is_contiguous() && rows.size(0) >= 1, "zero1 adamw: int64 rows [k, 3] on the device");
+  TORCH_CHECK(is_f32(exp_avg) && is_f32(exp_avg_sq) && exp_avg.is_contiguous() && exp_avg_sq.is_contiguous() &&
+                  exp_avg.numel() == exp_avg_sq.numel(), "zero1 adamw: fp32 slice state");
+  const int64_t n = static_cast<int64_t>(grads.size());
+  const int64_t seg = ((numel + n - 1) / n + 3) / 4 * 4;
+  const int64_t s0 = std::min<int64_t>(numel, rank * seg), s1 = std::min<int64_t>(numel, s0 + seg);
+  TORCH_CHECK(exp_avg.numel() >= s1 - s0, "zero1 adamw: the slice state is shorter than the owned slice");
+  plg::Zero1Adam h;
+  for (size_t g = 0; g < lr.size(); ++g) {
+    h.lr[g] = static_cast<float>(lr[g]);
+    h.wd[g] = static_cast<float>(wd[g]);
+  }
+  h.beta1 = static_cast<float>(beta1);
+  h.beta2 = static_cast<float>(beta2);
+  h.eps = static_cast<float>(eps);
+  h.bc1 = static_cast<float>(bc1);
+  h.bc2 = static_cast<float>(bc2);
+  if (grad_scale.has_value()) {
+    TORCH_CHECK(is_f32(*grad_scale) && grad_scale->is_cuda(), "grad_scale: fp32 device scalar");
+    h.grad_scale = grad_scale->data_ptr<float>();
+  }
+  h.rows = rows.data_ptr<int64_t>();
+  h.nrows = static_cast<int>(rows.size(0));
+  h.exp_avg = exp_avg.data_ptr<float>();
+  h.exp_avg_sq = exp_avg_sq.data_ptr<float>();
+  plg::zero1_adamw_allgather(a, h, cur_stream());
+}
+
 // GEMM whose epilogue stores each row into its owner's staging slot (tensor-parallel
 // reduce-scatter along the sequence); rs_dst: every rank's staging base address
 void gemm_rs(const at::Tensor& a, const at::Tensor& b, bool b_mn_major, std::vector<int64_t> rs_dst,
@@ -596,6 +672,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("rank"), py::arg("epoch"), py::arg("B"), py::arg("S"), py::arg("cap_bytes"),
         py::arg("status") = py::none());
   m.def("set_peer_wait_deadline", &set_peer_wait_deadline, py::arg("ns"));
+  m.def("zero1_rs", &zero1_rs_b, py::arg("grads"), py::arg("params"), py::arg("flags"),
+        py::arg("slots"), py::arg("offset"), py::arg("numel"), py::arg("rank"), py::arg("epoch"),
+        py::arg("chunks"), py::arg("norm_sq"), py::arg("accumulate"), py::arg("status") = py::none());
+  m.def("zero1_adamw_ag", &zero1_adamw_ag_b, py::arg("grads"), py::arg("params"), py::arg("flags"),
+        py::arg("slots"), py::arg("offset"), py::arg("numel"), py::arg("rank"), py::arg("epoch"),
+        py::arg("chunks"), py::arg("lr"), py::arg("wd"), py::arg("beta1"), py::arg("beta2"),
+        py::arg("eps"), py::arg("bc1"), py::arg("bc2"), py::arg("grad_scale"), py::arg("rows"),
+        py::arg("exp_avg"), py::arg("exp_avg_sq"), py::arg("status") = py::none());
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd", &embedding_bwd);
   m.def("softcap", &softcap);

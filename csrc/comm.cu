@@ -145,6 +145,150 @@ __global__ void __launch_bounds__(512) allreduce_avg_kernel(SymmAllReduceArgs a)
   }
 }
 
+// ------------------------------------------------------------------- ZeRO-1
+// Data parallelism with the optimizer state sharded (ZeRO stage 1) and the two
+// halves of the gradient all-reduce split around the optimizer:
+//   zero1_rs_kernel (per bucket, during backward): CTA c of rank r averages chunk
+//     c of r's slice over every rank's grad arena (peer loads) into r's own arena,
+//     sums the squares of the result (the clip's norm) into every rank's slot table;
+//   zero1_adamw_ag_kernel (per bucket, after the global norm is known): AdamW on
+//     r's slice with r's optimizer state, the new fp32 params stored into every
+//     rank's param arena (peer stores).
+// Both follow the allreduce_avg_kernel protocol: CTA c signals before it waits and
+// only ever waits for CTA c of the peers; flags carry per-kind epochs.
+__device__ __forceinline__ void zero1_slice(long long numel, int n, int r, long long& s0,
+                                            long long& s1) {
+  const long long seg = ((numel + n - 1) / n + 3) & ~3LL;
+  s0 = min(numel, static_cast<long long>(r) * seg);
+  s1 = min(numel, s0 + seg);
+}
+
+__device__ __forceinline__ uint32_t* zero1_flag(const Zero1Args& a, int table, int kind, int src, int c) {
+  return a.flags[table] + (kind * kSymmMaxRanks + src) * kSymmMaxChunks + c;
+}
+
+// signal kind `kind` of chunk c to every rank, then wait for every rank's; false on timeout
+__device__ bool zero1_handshake(const Zero1Args& a, int kind) {
+  __shared__ int s_ok;
+  const int c = blockIdx.x;
+  if (threadIdx.x < a.nranks) st_release_sys(zero1_flag(a, threadIdx.x, kind, a.rank, c), a.epoch);
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    for (int p = 0; p < a.nranks && ok; ++p) ok = wait_flag(zero1_flag(a, a.rank, kind, p, c), a.epoch);
+    if (!ok) record_status(a.status, kTimeoutPeerFlag);
+    s_ok = ok;
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
+__device__ __forceinline__ void zero1_chunk(const Zero1Args& a, long long& c0, long long& c1,
+                                            long long& s0) {
+  long long s1;
+  zero1_slice(a.numel, a.nranks, a.rank, s0, s1);
+  const long long per = ((s1 - s0 + a.chunks - 1) / a.chunks + 3) & ~3LL;
+  c0 = min(s1, s0 + blockIdx.x * per);
+  c1 = min(s1, c0 + per);
+}
+
+__global__ void __launch_bounds__(512) zero1_rs_kernel(Zero1Args a) {
+  const int n = a.nranks, me = a.rank, c = blockIdx.x;
+  const bool ok = zero1_handshake(a, 0);
+  float ss = 0.f;
+  if (ok) {
+    long long c0, c1, s0;
+    zero1_chunk(a, c0, c1, s0);
+    const float inv = 1.f / n;
+    const long long v1 = c0 + ((c1 - c0) & ~3LL);  // c0 is a multiple of 4: float4 body
+    float* mine = a.grads[me] + a.offset;
+    for (long long i = c0 + 4LL * threadIdx.x; i < v1; i += 4LL * blockDim.x) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+      for (int p = 0; p < n; ++p) {  // fixed rank order: deterministic sums
+        const float4 x = *reinterpret_cast<const float4*>(a.grads[p] + a.offset + i);
+        acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+      }
+      acc.x *= inv; acc.y *= inv; acc.z *= inv; acc.w *= inv;
+      ss += acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w;
+      *reinterpret_cast<float4*>(mine + i) = acc;
+    }
+    for (long long i = v1 + threadIdx.x; i < c1; i += blockDim.x) {
+      float acc = 0.f;
+      for (int p = 0; p < n; ++p) acc += a.grads[p][a.offset + i];
+      acc *= inv;
+      ss += acc * acc;
+      mine[i] = acc;
+    }
+  }
+  ss = warp_sum(ss);
+  __shared__ float s_red[16];
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += s_red[w];
+    for (int p = 0; p < n; ++p) a.sumsq[p][me * kSymmMaxChunks + c] = t;
+    __threadfence_system();
+  }
+  __syncthreads();
+  // done: this CTA has read chunk c of its slice from every copy (peers may reuse
+  // their grad arenas) and published its sum of squares
+  zero1_handshake(a, 1);
+}
+
+__device__ __forceinline__ int zero1_group(const int64_t* rows, int nrows, long long i, int& r) {
+  while (r + 1 < nrows && rows[3 * r + 1] <= i) ++r;
+  return static_cast<int>(rows[3 * r + 2]);
+}
+
+__global__ void __launch_bounds__(512) zero1_adamw_ag_kernel(Zero1Args a, Zero1Adam h) {
+  const int n = a.nranks, me = a.rank;
+  long long c0, c1, s0;
+  zero1_chunk(a, c0, c1, s0);
+  const float scale = h.grad_scale ? *h.grad_scale : 1.f;
+  const float b1 = h.beta1, b2 = h.beta2, eps = h.eps;
+  const float rbc2 = rsqrtf(h.bc2);
+  const float* g = a.grads[me] + a.offset;
+  const float* pin = a.params[me] + a.offset;
+  int r = 0;
+  const long long v1 = c0 + ((c1 - c0) & ~3LL);
+  for (long long i = c0 + 4LL * threadIdx.x; i < v1; i += 4LL * blockDim.x) {
+    float4 pp = *reinterpret_cast<const float4*>(pin + i);
+    const float4 gg = *reinterpret_cast<const float4*>(g + i);
+    float* const mp = h.exp_avg + (i - s0);  // slice state is indexed from the slice start
+    float* const vp = h.exp_avg_sq + (i - s0);
+    float4 mm = *reinterpret_cast<const float4*>(mp);
+    float4 vv = *reinterpret_cast<const float4*>(vp);
+    float* P = &pp.x; const float* G = &gg.x; float* M = &mm.x; float* W = &vv.x;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {  // a param boundary may fall inside the vector
+      const int grp = zero1_group(h.rows, h.nrows, i + j, r);
+      const float lr = h.lr[grp];
+      adamw_update(P[j], M[j], W[j], G[j] * scale, 1.f - lr * h.wd[grp], b1, b2, lr / h.bc1, rbc2, eps);
+    }
+    *reinterpret_cast<float4*>(mp) = mm;
+    *reinterpret_cast<float4*>(vp) = vv;
+    for (int k = 0; k < n; ++k) {  // rotated: rank r starts with itself
+      int q = me + k;
+      q = q >= n ? q - n : q;
+      *reinterpret_cast<float4*>(a.params[q] + a.offset + i) = pp;
+    }
+  }
+  for (long long i = v1 + threadIdx.x; i < c1; i += blockDim.x) {
+    float pj = pin[i], mj = h.exp_avg[i - s0], vj = h.exp_avg_sq[i - s0];
+    const int grp = zero1_group(h.rows, h.nrows, i, r);
+    const float lr = h.lr[grp];
+    adamw_update(pj, mj, vj, g[i] * scale, 1.f - lr * h.wd[grp], b1, b2, lr / h.bc1, rbc2, eps);
+    h.exp_avg[i - s0] = mj;
+    h.exp_avg_sq[i - s0] = vj;
+    for (int q = 0; q < n; ++q) a.params[q][a.offset + i] = pj;
+  }
+  __threadfence_system();
+  __syncthreads();
+  // done: chunk c of this rank's slice is in every arena; wait for the peers' chunk c
+  zero1_handshake(a, 2);
+}
+
 // total = sum of the [nranks][chunks] slot table (fixed order: deterministic)
 __global__ void sumsq_total_kernel(const float* __restrict__ slots, int nranks, int chunks,
                                    float* __restrict__ out, int accumulate) {
@@ -477,6 +621,39 @@ void symm_allreduce_avg(const SymmAllReduceArgs& a, float* norm_sq, bool accumul
                                                 accumulate_norm ? 1 : 0);
     PLG_CUDA_CHECK(cudaGetLastError());
   }
+}
+
+static void zero1_check(const Zero1Args& a, const char* what) {
+  if (a.nranks < 1 || a.nranks > kSymmMaxRanks || a.rank < 0 || a.rank >= a.nranks)
+    throw std::invalid_argument(std::string(what) + ": 1..8 ranks");
+  if (a.chunks < 1 || a.chunks > kSymmMaxChunks)
+    throw std::invalid_argument(std::string(what) + ": chunks must be in 1..kSymmMaxChunks");
+  if (a.offset % 4 || a.numel < 0) throw std::invalid_argument(std::string(what) + ": offset must be a multiple of 4");
+  for (int p = 0; p < a.nranks; ++p)
+    if (a.grads[p] == nullptr || a.params[p] == nullptr || a.flags[p] == nullptr || a.sumsq[p] == nullptr ||
+        (reinterpret_cast<uintptr_t>(a.grads[p]) & 15) || (reinterpret_cast<uintptr_t>(a.params[p]) & 15))
+      throw std::invalid_argument(std::string(what) + ": every rank's 16-byte aligned arenas and tables");
+}
+
+void zero1_reduce_scatter(const Zero1Args& a, float* norm_sq, bool accumulate, cudaStream_t st) {
+  zero1_check(a, "zero1_reduce_scatter");
+  // launched also for an empty bucket: the handshakes keep the ranks' epochs in step
+  comm::zero1_rs_kernel<<<a.chunks, 512, 0, st>>>(a);
+  PLG_CUDA_CHECK(cudaGetLastError());
+  if (norm_sq != nullptr) {
+    comm::sumsq_total_kernel<<<1, 256, 0, st>>>(a.sumsq[a.rank], a.nranks, a.chunks, norm_sq,
+                                                accumulate ? 1 : 0);
+    PLG_CUDA_CHECK(cudaGetLastError());
+  }
+}
+
+void zero1_adamw_allgather(const Zero1Args& a, const Zero1Adam& h, cudaStream_t st) {
+  zero1_check(a, "zero1_adamw_allgather");
+  if (h.nrows < 1 || h.rows == nullptr || h.exp_avg == nullptr || h.exp_avg_sq == nullptr ||
+      (reinterpret_cast<uintptr_t>(h.exp_avg) & 15) || (reinterpret_cast<uintptr_t>(h.exp_avg_sq) & 15))
+    throw std::invalid_argument("zero1_adamw_allgather: a row table and 16-byte aligned slice state");
+  comm::zero1_adamw_ag_kernel<<<a.chunks, 512, 0, st>>>(a, h);
+  PLG_CUDA_CHECK(cudaGetLastError());
 }
 
 static void tp_check(const TpArgs& a, long long ld, const void* p, const char* what) {

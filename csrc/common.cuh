@@ -122,6 +122,16 @@ __device__ __forceinline__ void exp2_poly2(float x0, float x1, float& p0, float&
   p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
 }
 
+// One AdamW element update (decoupled weight decay): decay = 1 - lr * wd,
+// step = lr / bc1, rbc2 = 1 / sqrt(bc2); g already multiplied by the clip scale.
+__device__ __forceinline__ void adamw_update(float& p, float& m, float& v, float g, float decay,
+                                             float b1, float b2, float step, float rbc2, float eps) {
+  p *= decay;
+  m += (1.f - b1) * (g - m);
+  v = b2 * v + (1.f - b2) * g * g;
+  p -= step * m / (sqrtf(v) * rbc2 + eps);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

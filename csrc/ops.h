@@ -166,6 +166,39 @@ struct SymmAllReduceArgs {
 };
 // average data[offset, offset+numel) over the ranks in place on every rank; with
 // norm_sq, also (accumulate_norm ? += : =) the sum of squares of the averaged range
+// ZeRO-1 inside data parallelism. A bucket [offset, offset + numel) of the grad
+// and fp32 param arenas (same layout on every rank) is owned in slices: with
+// seg = ceil(numel / n) rounded up to a multiple of 4, rank r owns
+// [min(numel, r * seg), min(numel, (r + 1) * seg)).
+constexpr int kZero1Kinds = 3;  // flag kinds: 0 RS ready, 1 RS done, 2 AG done
+struct Zero1Args {
+  float* grads[kSymmMaxRanks];     // every rank's grad arena
+  float* params[kSymmMaxRanks];    // every rank's fp32 param arena
+  uint32_t* flags[kSymmMaxRanks];  // every rank's flag table [kZero1Kinds][kSymmMaxRanks][kSymmMaxChunks]
+  float* sumsq[kSymmMaxRanks];     // every rank's slot table [kSymmMaxRanks][kSymmMaxChunks]
+  long long offset, numel;         // bucket range in elements (offset a multiple of 4)
+  int rank, nranks, chunks;
+  uint32_t epoch;                  // grows by one per call of the same kernel on every rank
+  int* status;
+};
+// Reduce-scatter: the own slice of the own grad arena becomes the average over the
+// ranks (peer loads); the sum of squares of the averaged slice goes into every
+// rank's slot table, and (accumulate ? += : =) into norm_sq.
+void zero1_reduce_scatter(const Zero1Args& a, float* norm_sq, bool accumulate, cudaStream_t st);
+struct Zero1Adam {
+  float lr[4] = {}, wd[4] = {};    // per param group
+  float beta1 = 0.9f, beta2 = 0.999f, eps = 1e-8f, bc1 = 1.f, bc2 = 1.f;
+  const float* grad_scale = nullptr;  // device scalar (clip coefficient) or null
+  const int64_t* rows = nullptr;   // device [nrows][3]: start, end (bucket elements), group
+  int nrows = 0;                   //   sorted and covering [0, numel)
+  float* exp_avg = nullptr;        // own-slice optimizer state (slice length)
+  float* exp_avg_sq = nullptr;
+};
+// AdamW on the own slice (grads already averaged), the updated fp32 params stored
+// into every rank's param arena (peer stores); returns once every peer's slice of
+// the bucket has landed in this rank's arena.
+void zero1_adamw_allgather(const Zero1Args& a, const Zero1Adam& h, cudaStream_t st);
+
 // Tensor-parallel collectives over peer memory (sequence dimension of [B, S, W]
 // rows). Flags: each rank's flag words [kTpKinds][kSymmMaxRanks] in symmetric
 // memory; `epoch` grows by one per call of a kind; staging/send buffers are
@@ -202,10 +235,10 @@ struct EpSegs {
   long long dst_off[kSymmMaxRanks] = {};
 };
 void ep_push(const TpArgs& a, const EpSegs& sg, const void* src, long long ld, cudaStream_t stream);
-// signal (flag kind `kind`), wait for every peer, copy own buffer rows [0, rows) to out
 // Deadline (ns) of every peer-flag wait in the collective kernels on the
 // current device (default 2 s); ordered on `st` and synchronised.
 void set_peer_wait_deadline_ns(unsigned long long ns, cudaStream_t st);
+// signal (flag kind `kind`), wait for every peer, copy own buffer rows [0, rows) to out
 void ep_finish(const TpArgs& a, int kind, void* out, long long rows, long long ld_out,
                cudaStream_t stream);
 // FSDP unit all-gather over peer memory: table [k][3] int64 (units of 16 bytes):

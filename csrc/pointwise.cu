@@ -432,11 +432,7 @@ __global__ void __launch_bounds__(512) adamw_kernel(const int64_t* __restrict__ 
         float* P = &pp.x; float* G = &gg.x; float* M = &mm.x; float* W = &vv.x;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const float gj = G[j] * scale;
-          P[j] *= decay;
-          M[j] += (1.f - b1) * (gj - M[j]);
-          W[j] = b2 * W[j] + (1.f - b2) * gj * gj;
-          P[j] -= step * M[j] / (sqrtf(W[j]) * rbc2 + eps);
+          adamw_update(P[j], M[j], W[j], G[j] * scale, decay, b1, b2, step, rbc2, eps);
         }
         *reinterpret_cast<float4*>(p + e) = pp;
         *reinterpret_cast<float4*>(m + e) = mm;
@@ -451,11 +447,8 @@ __global__ void __launch_bounds__(512) adamw_kernel(const int64_t* __restrict__ 
       i0 = off + n4 * 4;
     }
     for (long long e = i0 + threadIdx.x; e < end; e += blockDim.x) {
-      const float gj = g[e] * scale;
-      float pj = p[e] * decay;
-      float mj = m[e] + (1.f - b1) * (gj - m[e]);
-      float vj = b2 * v[e] + (1.f - b2) * gj * gj;
-      pj -= step * mj / (sqrtf(vj) * rbc2 + eps);
+      float pj = p[e], mj = m[e], vj = v[e];
+      adamw_update(pj, mj, vj, g[e] * scale, decay, b1, b2, step, rbc2, eps);
       p[e] = pj; m[e] = mj; v[e] = vj;
       if (sh) sh[e] = __float2bfloat16(pj);
     }

@@ -66,6 +66,9 @@ class Qwen3TransformerBlock(nn.Module):
 
 
 class Qwen3(nn.Module):
+    # the forward calls ``_plg_param_gate.enter`` (ZeRO-1 DDP: wait for each block's
+    # parameter all-gather just before the block)
+    param_gate_aware = True
     rope_base = 1_000_000
     tie_default = True
     block_cls = Qwen3TransformerBlock
@@ -111,15 +114,22 @@ class Qwen3(nn.Module):
     def fused_hidden(self, x: torch.Tensor) -> torch.Tensor:
         """Packed causal forward on the sm_100a kernels; returns bf16 [B, S, D]."""
         B, S = x.shape
+        gate = getattr(self, "_plg_param_gate", None)
+        if gate is not None:
+            gate.enter("emb")
         h = _engine.Embedding.apply(x, self.token_emb.weight, 1.0)
         inv = self.rope.inv_freq
         fs = getattr(self, "_plg_fsdp", None)
         for i, blk in enumerate(self.blocks):
+            if gate is not None:
+                gate.enter(i)
             if fs is not None:
                 fs.fused_block_enter(i)
             h = blk.fused_forward(h, self.weight_cache, self._attn_cfg(B, S, blk), inv, i)
             if fs is not None:
                 fs.fused_block_exit(i, h)
+        if gate is not None:
+            gate.enter("all")
         out = _engine.FinalNorm.apply(h, self.norm.weight, norm_eps(self.norm))
         return out.view(B, S, -1)
 
@@ -132,6 +142,9 @@ class Qwen3(nn.Module):
             if return_final_hidden:
                 return hidden
             return linear(hidden, self.lm_head.weight, self.weight_cache.get(self.lm_head.weight))
+        gate = getattr(self, "_plg_param_gate", None)
+        if gate is not None:
+            gate.enter("all")
         pos, cacheable, am = position_ids_for(x, attention_mask)
         if position_ids is not None:
             pos, cacheable = position_ids, False

@@ -20,6 +20,13 @@ one sm_100a kernel reads every peer's copy over NVLink, sums, scales by 1/N and
 writes the result back into the grad views, accumulating the sum of squares of
 the reduced grads for the clip on the way. Both paths leave exactly the same
 ``.grad`` contract for clip and optimizer.
+
+``reducer="zero1"`` (:mod:`pluggy_b200.comm.zero1`) splits each bucket's
+all-reduce around the optimizer: a reduce-scatter during backward, AdamW on the
+rank's slice only (``zero1_optimizer`` wraps the built AdamW), then an
+all-gather of the updated parameters that the next forward waits for block by
+block. After ``sync()`` only the rank's own slice of each bucket holds averaged
+grads; the optimizer reads nothing else.
 """
 
 from __future__ import annotations
@@ -61,6 +68,7 @@ class DDP:
         self._works: list = []
         self.reducer_name = reducer
         self._fused = None
+        self.zero1 = None
         if self.group_size == 1:
             return
         # expert shards (expert parallelism over this axis) differ per rank by design:
@@ -77,8 +85,15 @@ class DDP:
             from pluggy_b200.comm.fused_ddp import BucketReducer
 
             self._fused = BucketReducer(mesh, dim, self._buckets)
+        elif reducer == "zero1":
+            from pluggy_b200.comm.zero1 import ParamGate, Zero1Reducer
+
+            self._fused = self.zero1 = Zero1Reducer(mesh, dim, self._buckets)
+            self._gate = ParamGate(model, self._bucket_of)
+            self._gate_used = bool(getattr(type(model), "param_gate_aware", False))
+            model._plg_param_gate = self._gate
         elif reducer != "nccl":
-            raise ValueError(f"unknown DDP reducer {reducer!r}: expected 'nccl' or 'fused'")
+            raise ValueError(f"unknown DDP reducer {reducer!r}: expected 'nccl', 'fused' or 'zero1'")
         for p in params:
             p.register_post_accumulate_grad_hook(self._on_grad_ready)
 
@@ -119,6 +134,15 @@ class DDP:
             return
         _, work = all_reduce(b.grad_tensor(), self.mesh, self.dim, "avg", async_op=True)
         self._works.append(work)
+
+    def zero1_optimizer(self, base):
+        """The optimizer for ``reducer="zero1"``: AdamW over this rank's slices, built
+        from ``base``'s param groups and hyper-parameters. Other reducers: ``base``."""
+        if self.zero1 is None:
+            return base
+        from pluggy_b200.comm.zero1 import Zero1AdamW
+
+        return Zero1AdamW(base, self.zero1, self._gate, self._gate_used)
 
     def reduced_norm_sq(self):
         """Sum of squares of the averaged grads, when the reducer computed it on the

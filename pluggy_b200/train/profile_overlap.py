@@ -23,7 +23,7 @@ from collections import defaultdict
 # kernel-name fragments that mark communication: NCCL's kernels and the fused
 # collective kernels of this package (pluggy_b200.comm)
 COMM_MARKERS = ("nccl", "plg::comm::", "comm::allreduce_avg", "sumsq_total", "tp_rs_", "tp_ag_",
-                "tp_norm_ag", "ep_push", "ep_finish", "fsdp_push")
+                "tp_norm_ag", "ep_push", "ep_finish", "fsdp_push", "zero1_rs", "zero1_adamw_ag")
 
 
 def union(intervals: list[tuple[float, float]]) -> list[tuple[float, float]]:
@@ -90,6 +90,40 @@ def analyze(trace_path: str) -> dict:
     }
 
 
+def short_name(name: str) -> str:
+    """Kernel function name without namespaces, template arguments or parameters."""
+    n = name.replace("(anonymous namespace)::", "").split("(")[0]
+    depth, out = 0, []
+    for ch in n:  # drop <...> (nested)
+        if ch == "<":
+            depth += 1
+        elif ch == ">":
+            depth = max(0, depth - 1)
+        elif depth == 0:
+            out.append(ch)
+    n = "".join(out).strip()
+    n = n.split(" ")[-1]
+    return n.split("::")[-1] or name[:60]
+
+
+def kernel_table(trace_path: str, steps: int = 1) -> list[dict]:
+    """Per-kernel device time per step from a chrome trace: name, ms/step,
+    launches/step and share of the summed kernel time, largest first."""
+    with open(trace_path) as f:
+        tr = json.load(f)
+    events = tr["traceEvents"] if isinstance(tr, dict) else tr
+    acc = defaultdict(lambda: [0.0, 0])
+    for e in events:
+        if e.get("ph") == "X" and e.get("cat") in ("kernel", "gpu_memcpy", "gpu_memset") and "dur" in e:
+            k = short_name(e["name"])
+            acc[k][0] += float(e["dur"])
+            acc[k][1] += 1
+    tot = sum(v[0] for v in acc.values()) or 1.0
+    rows = [{"kernel": k, "ms_per_step": v[0] / 1e3 / steps, "launches_per_step": v[1] / steps,
+             "share": v[0] / tot} for k, v in acc.items()]
+    return sorted(rows, key=lambda r: -r["ms_per_step"])
+
+
 def capture(config, warmup: int, steps: int, out: str, rank: int, local_rank: int,
             world: int) -> str:
     """Profile ``steps`` training steps after ``warmup`` (``config``: dict or JSON path)."""
@@ -122,6 +156,8 @@ def main(argv=None) -> None:
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--steps", type=int, default=2)
     p.add_argument("--out", default="overlap_trace.json")
+    p.add_argument("--kernels", type=int, default=0,
+                   help="also print the N largest kernels (device ms per step)")
     a = p.parse_args(argv)
     rank, local_rank, world = init_distributed()
     try:
@@ -131,6 +167,14 @@ def main(argv=None) -> None:
             print(json.dumps({k: v for k, v in rep.items() if k != "per_kernel_exposed_us"}, indent=1))
             for k, v in list(rep["per_kernel_exposed_us"].items())[:10]:
                 print(f"  exposed {v:10.1f} us  {k}")
+            if a.kernels:
+                rows = kernel_table(path, a.steps)
+                print(f"{'kernel':48s} {'ms/step':>9s} {'launches':>9s} {'share':>7s}")
+                for r in rows[:a.kernels]:
+                    print(f"{r['kernel'][:48]:48s} {r['ms_per_step']:9.3f} "
+                          f"{r['launches_per_step']:9.0f} {100 * r['share']:6.1f}%")
+                print(f"{'total':48s} {sum(r['ms_per_step'] for r in rows):9.3f} "
+                      f"{sum(r['launches_per_step'] for r in rows):9.0f}")
     finally:
         if dist.is_initialized():
             dist.destroy_process_group()

@@ -94,6 +94,9 @@ class Trainer:
                                          self.config["objective"]["config"])
         opt = self.config["optimizer"]
         self.optimizer = build_optimizer(self.model, opt["name"], opt["config"])
+        if self.parallelism == "ddp":
+            # ZeRO-1 data parallelism updates this rank's slices only
+            self.optimizer = self.dp.zero1_optimizer(self.optimizer)
         # the optimizer writes the bf16 copies the GEMMs read (no per-step recast);
         # FSDP2 gathers full weights per step, so there is nothing to keep current
         wc = getattr(self.model, "weight_cache", None)
@@ -281,9 +284,21 @@ class Trainer:
         if _ext.available():
             _ext.check_status(self.device)
 
+    def _optimizer_sharded(self) -> bool:
+        """ZeRO-1 data parallelism: each rank holds the AdamW state of its slices only."""
+        return getattr(getattr(self, "dp", None), "zero1", None) is not None
+
     def checkpoint(self, step: int) -> None:
         self.check_device_status()
-        if self.parallelism == "fsdp2" and self.dp_size > 1:
+        if hasattr(self.optimizer, "wait_params"):
+            self.optimizer.wait_params()
+        if self._optimizer_sharded():
+            if self.rank == 0:
+                self.checkpointer.save_model(self.model, step)
+            torch.save(self.optimizer.state_dict(),
+                       os.path.join(self.checkpointer._step_dir(step, True),
+                                    f"optimizer_rank{self.rank}.pt"))
+        elif self.parallelism == "fsdp2" and self.dp_size > 1:
             self._checkpoint_sharded(step)
         elif self._model_sharded():
             sd = self._full_model_state()
@@ -295,7 +310,8 @@ class Trainer:
         elif self.rank == 0:
             self.checkpointer.save_model(self.model, step)
         if self.rank == 0:
-            if not (self.parallelism == "fsdp2" and self.dp_size > 1) and not self._model_sharded():
+            if not (self.parallelism == "fsdp2" and self.dp_size > 1) and not self._model_sharded() \
+                    and not self._optimizer_sharded():
                 self.checkpointer.save_optimizer(self.optimizer, step)
             self.checkpointer.save_scheduler(self.scheduler, step)
             self.checkpointer.save_trainer({"step": step, "config": self.config,
@@ -351,6 +367,9 @@ class Trainer:
             self.optimizer.load_state_dict(self.checkpointer._load(step, f"optimizer_rank{self.rank}.pt"))
         elif self._model_sharded():
             self._load_full_model_state(self.checkpointer._load(step, "model.pt"))
+            self.optimizer.load_state_dict(self.checkpointer._load(step, f"optimizer_rank{self.rank}.pt"))
+        elif self._optimizer_sharded():
+            self.checkpointer.load_model(self.model, step)
             self.optimizer.load_state_dict(self.checkpointer._load(step, f"optimizer_rank{self.rank}.pt"))
         else:
             self.checkpointer.load_model(self.model, step)

@@ -102,6 +102,71 @@ def test_fused_ddp_matches_nccl_ddp():
     run_ranks(_ddp_case, 2, backend="nccl")
 
 
+def _zero1_case(rank, world):
+    import copy
+
+    import torch.distributed as dist
+
+    from pluggy_b200.core.grad_helper import clip_grad_norm
+    from pluggy_b200.core.mesh import Mesh
+    from pluggy_b200.models.qwen3 import Qwen3
+    from pluggy_b200.objectives.autoregressive import ARObjective
+    from pluggy_b200.ops import _ext
+    from pluggy_b200.optimizer.builder import build_optimizer
+    from pluggy_b200.parallel.ddp import DDP
+
+    mesh = Mesh({"dp": world})
+    torch.manual_seed(0)
+    base = Qwen3(num_layers=2, num_heads=4, num_kv_heads=2, emb_dim=256, head_dim=128,
+                 vocab_size=1024, ffn_dim=512).cuda()
+    base.init_weights()
+    init = {n: p.detach().clone() for n, p in base.named_parameters()}
+    cfg = {"lr": 1e-3, "weight_decay": 0.1, "betas": [0.9, 0.95]}
+    models, ddps, opts = {}, {}, {}
+    for r in ("nccl", "zero1"):
+        models[r] = copy.deepcopy(base)
+        ddps[r] = DDP(models[r], mesh, "dp", bucket_mb=1, reducer=r)
+        opts[r] = ddps[r].zero1_optimizer(build_optimizer(models[r], "adamw", dict(cfg)))
+    g = torch.Generator(device="cuda").manual_seed(100 + rank)
+    bad = []
+    for step in range(3):
+        ids = torch.randint(0, 1024, (2, 256), device="cuda", generator=g)
+        b = {"input_ids": ids, "labels": ids}
+        norms = {}
+        for r, m in models.items():
+            ARObjective(ce_chunk_size=256).compute_loss(m, b).backward()
+            ddps[r].sync()
+            gn, coef = clip_grad_norm(m.parameters(), mesh, 1.0, fold_into_optimizer=True,
+                                      precomputed_sq=ddps[r].reduced_norm_sq())
+            norms[r] = float(gn)
+            opts[r].set_grad_scale(coef)
+            opts[r].step()
+            opts[r].zero_grad()
+        opts["zero1"].wait_params()
+        torch.cuda.synchronize()
+        if abs(norms["nccl"] - norms["zero1"]) > 1e-4 * norms["nccl"]:
+            bad.append(("norm", step, norms))
+        for (n, p), (_, q) in zip(models["nccl"].named_parameters(), models["zero1"].named_parameters()):
+            upd = (p.detach() - init[n]).norm().item()
+            diff = (p.detach() - q.detach()).norm().item()
+            if diff > 1e-2 * max(upd, 1e-12):
+                bad.append((step, n, diff, upd))
+    # the replicas are bitwise identical on every rank
+    flat = torch.cat([p.detach().reshape(-1) for p in models["zero1"].parameters()])
+    allf = [torch.empty_like(flat) for _ in range(world)]
+    dist.all_gather(allf, flat)
+    if not all(torch.equal(allf[0], x) for x in allf[1:]):
+        bad.append("replicas differ")
+    _ext.check_status()
+    ddps["zero1"].zero1.close()
+    assert not bad, bad
+
+
+def test_zero1_ddp_matches_nccl_ddp():
+    _need(2)
+    run_ranks(_zero1_case, 2, backend="nccl")
+
+
 def _tp_collectives_case(rank, world):
     import torch.distributed as dist
 
