@@ -38,15 +38,49 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 METRIC = "train tokens/sec, 8×B200 device-timed max-over-ranks, 1/2/4/8 GPU vs ref NCCL"
 MODEL_CFG = {"num_layers": 28, "num_heads": 16, "num_kv_heads": 8, "emb_dim": 1024,
              "head_dim": 128, "vocab_size": 151936, "ffn_dim": 3072}
-MICRO, SEQ = 8, 4096
 BASELINE_VALUE = None  # BASELINE.json "published" is empty: no number to divide by
 
+# The BASELINE.json configs. "ddp06b" (config 2) is the headline the driver runs;
+# the others are the FSDP2, expert-parallel and tensor-parallel configs (3, 4, 5),
+# selected with --config. "ref" is the reference's own data-parallel strategy for
+# the same model: the reference has no tensor or expert parallelism, so configs 4
+# and 5 are compared against its FSDP2 / DDP of the same model.
+BENCH_CONFIGS = {
+    "ddp06b": {"model": "qwen3_dense", "cfg": MODEL_CFG, "micro": 8, "seq": 4096, "parallel": "ddp",
+               "ref": "ddp", "label": "qwen3-0.6B-shaped (28L, d1024, 16q/8kv x128, ffn 3072, V151936, tied)"},
+    "fsdp4b": {"model": "qwen3_dense", "micro": 4, "seq": 4096, "parallel": "fsdp2", "ref": "fsdp2",
+               "cfg": {"num_layers": 36, "num_heads": 32, "num_kv_heads": 8, "emb_dim": 2560,
+                       "head_dim": 128, "vocab_size": 151936, "ffn_dim": 9728},
+               "label": "qwen3-4B-shaped (36L, d2560, 32q/8kv x128, ffn 9728, V151936, tied)"},
+    "moe_ep": {"model": "qwen3_moe", "micro": 2, "seq": 4096, "parallel": "ep", "ref": "fsdp2",
+               "cfg": {"num_layers": 24, "num_heads": 32, "num_kv_heads": 4, "emb_dim": 2048,
+                       "head_dim": 128, "vocab_size": 151936, "moe_ffn_dim": 768, "num_experts": 128,
+                       "top_k": 8, "router_aux_loss_coef": 0.001},
+               "label": "qwen3-MoE-shaped (24L, d2048, 32q/4kv x128, 128 experts top-8, ffn 768, V151936)"},
+    "llama_tp": {"model": "llama3_2", "micro": 2, "seq": 8192, "parallel": "tp", "ref": "ddp",
+                 "cfg": {"num_layers": 16, "num_heads": 32, "num_kv_heads": 8, "emb_dim": 2048,
+                         "head_dim": 64, "ffn_dim": 8192, "vocab_size": 128256, "rope_base": 500000.0,
+                         "tie_embeddings": True},
+                 "label": "llama-3.2-1B-shaped (16L, d2048, 32q/8kv x64, ffn 8192, V128256, tied)"},
+}
 
-def train_config(n_gpus: int, reducer: str = "nccl") -> dict:
-    return {
-        "model": {"name": "qwen3_dense", "config": dict(MODEL_CFG)},
-        "mesh": {"dp": n_gpus},
-        "parallelism": "ddp",
+
+def layout(name: str, n_gpus: int) -> dict:
+    """Mesh, parallelism string and tokens per step of config ``name`` on n GPUs."""
+    bc = BENCH_CONFIGS[name]
+    tp = min(4, n_gpus) if bc["parallel"] == "tp" else 1
+    dp = n_gpus // tp
+    par = {"ddp": f"dp{dp}", "fsdp2": f"fsdp{dp}", "ep": f"ep{dp}", "tp": f"tp{tp}xdp{dp}"}[bc["parallel"]]
+    return {"tp": tp, "dp": dp, "parallelism": par, "tokens": bc["micro"] * bc["seq"] * dp}
+
+
+def train_config(n_gpus: int, reducer: str = "nccl", name: str = "ddp06b") -> dict:
+    bc = BENCH_CONFIGS[name]
+    lay = layout(name, n_gpus)
+    cfg = {
+        "model": {"name": bc["model"], "config": dict(bc["cfg"])},
+        "mesh": {"dp": lay["dp"]},
+        "parallelism": "fsdp2" if bc["parallel"] == "fsdp2" else "ddp",
         "ddp": {"bucket_mb": 25, "reducer": reducer},
         "optimizer": {"name": "adamw",
                       "config": {"lr": 3e-4, "weight_decay": 0.1, "betas": [0.9, 0.95], "fused": True},
@@ -56,12 +90,18 @@ def train_config(n_gpus: int, reducer: str = "nccl") -> dict:
         "objective": {"name": "AR", "config": {"ignore_index": -100, "fused_linear_ce": True,
                                                "ce_chunk_size": 4096}},
         "data": {"synthetic": {"kind": "zipf", "s": 1.1, "min_doc": 512, "max_doc": 4096},
-                 "global_batch_size": MICRO * n_gpus, "micro_batch_size": MICRO, "seq_len": SEQ,
-                 "seed": 42},
+                 "global_batch_size": bc["micro"] * lay["dp"], "micro_batch_size": bc["micro"],
+                 "seq_len": bc["seq"], "seed": 42},
         "checkpointing": {"save_steps": 10**9, "resume": None},
         "seed": 0,
         "run_name": "bench",
     }
+    if bc["parallel"] == "ep":
+        cfg["ep"] = {"dim": "dp"}
+    if bc["parallel"] == "tp" and lay["tp"] > 1:
+        cfg["mesh"]["tp"] = lay["tp"]
+        cfg["tp"] = {"sequence_parallel": True}
+    return cfg
 
 
 # ------------------------------------------------------------------------ clocks
@@ -180,7 +220,8 @@ def run_ours(args, rank, local_rank, world, device) -> dict:
     from pluggy_b200.utils.launch_count import count_launches
 
     reducer = os.environ.get("PLG_DDP_REDUCER", "nccl")
-    trainer = Trainer(train_config(world, reducer), rank=rank, local_rank=local_rank,
+    bc = BENCH_CONFIGS[args.config]
+    trainer = Trainer(train_config(world, reducer, args.config), rank=rank, local_rank=local_rank,
                       world_size=world, benchmark=True)
     # kernel-only arm: the batch is already on the device
     batch = next(trainer.prefetcher)
@@ -200,7 +241,7 @@ def run_ours(args, rank, local_rank, world, device) -> dict:
 
     # end-to-end arm through the public Trainer.train_step (H2D of every batch + loss read)
     trainer.prefetcher = real_prefetcher
-    h2d = MICRO * SEQ * 8  # int64 ids; labels are the same host tensor (copied once)
+    h2d = bc["micro"] * bc["seq"] * 8  # int64 ids; labels are the same host tensor (copied once)
     d2h = 4
 
     def e2e_step():
@@ -209,7 +250,7 @@ def run_ours(args, rank, local_rank, world, device) -> dict:
 
     e2e_ms = timed_loop(e2e_step, max(1, args.steps // 2), 1, device)
     _ext.check_status(device)
-    tokens = MICRO * SEQ * world
+    tokens = layout(args.config, world)["tokens"]
     return {
         "value": tokens / (ms / 1e3), "ms_per_step": ms, "clocks": clk.summary(),
         "gpu_launches": launches,
@@ -272,9 +313,25 @@ def run_reference(args, rank, local_rank, world, device) -> dict:
 
     from pluggy_b200.dataloader.synthetic import SyntheticBatches, SyntheticZipfRows
 
-    cfg = train_config(world)
-    cfg["model"]["config"].pop("ffn_dim")
-    cfg["model"]["config"]["ffn_dim"] = MODEL_CFG["ffn_dim"]
+    import inspect
+
+    from pluggy.models.builder import MODEL_REGISTRY
+    from pluggy.parallelism.fsdp2 import FSDP2
+
+    bc = BENCH_CONFIGS[args.config]
+    micro, seq = bc["micro"], bc["seq"]
+    # the reference runs its own data-parallel strategy over all N GPUs (it has no
+    # tensor or expert parallelism): DDP or FSDP2 with the same micro-batch per rank
+    cfg = train_config(world, "nccl", "ddp06b")
+    cfg["mesh"] = {"dp": world}
+    cfg["parallelism"] = bc["ref"]
+    cfg["data"]["global_batch_size"] = micro * world
+    # constructor arguments the reference model does not take (its Qwen3 is always
+    # tied and its Llama3 always untied) are dropped
+    cls = MODEL_REGISTRY[bc["model"]]
+    accepted = set(inspect.signature(cls.__init__).parameters)
+    mcfg = {k: v for k, v in bc["cfg"].items() if k in accepted}
+    cfg["model"] = {"name": bc["model"], "config": mcfg}
     T = ref_trainer_mod.Trainer
     tr = object.__new__(T)  # the reference __init__ needs a network tokenizer and dataset
     tr.config, tr.rank, tr.world_size, tr.benchmark = cfg, rank, world, True
@@ -282,7 +339,7 @@ def run_reference(args, rank, local_rank, world, device) -> dict:
     tr.mesh = Mesh(cfg["mesh"])
     tr.dp_size = tr.mesh.size("dp")
     torch.manual_seed(0)
-    tr.model = build_model("qwen3_dense", cfg["model"]["config"])
+    tr.model = build_model(bc["model"], mcfg)
     tr.model.to(device)
     tr.model.init_weights()
     tr._parallelize(tr.model)
@@ -293,13 +350,13 @@ def run_reference(args, rank, local_rank, world, device) -> dict:
     tr.scheduler = build_scheduler(tr.optimizer, cfg["optimizer"]["scheduler"])
     tr.max_norm = 1.0
     tr.global_batch_size = cfg["data"]["global_batch_size"]
-    tr.micro_batch_size = MICRO
+    tr.micro_batch_size = micro
     tr.microbatches_per_step = 1
     tr.wandb_run = None
-    src = SyntheticZipfRows(vocab_size=MODEL_CFG["vocab_size"], seq_len=SEQ, seed=42,
+    src = SyntheticZipfRows(vocab_size=bc["cfg"]["vocab_size"], seq_len=seq, seed=42,
                             dp_rank=tr.mesh.coordinate("dp"))
-    tr.prefetcher = CUDAPrefetcher(SyntheticBatches(src, MICRO, pin=True), device)
-    assert isinstance(tr.dp, DDP)
+    tr.prefetcher = CUDAPrefetcher(SyntheticBatches(src, micro, pin=True), device)
+    assert isinstance(tr.dp, FSDP2 if bc["ref"] == "fsdp2" else DDP)
     batch = next(tr.prefetcher)
     real = tr.prefetcher
     tr.prefetcher = ResidentBatches(batch)
@@ -320,10 +377,11 @@ def run_reference(args, rank, local_rank, world, device) -> dict:
         metrics["loss"].item()
 
     e2e_ms = timed_loop(e2e_step, max(1, args.steps // 2), 1, device)
-    tokens = MICRO * SEQ * world
+    tokens = micro * seq * world
     return {"value": tokens / (ms / 1e3), "ms_per_step": ms, "clocks": clk.summary(),
+            "ref_parallelism": f"{bc['ref']}{world}", "tokens_per_step": tokens,
             "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
-                    "h2d_bytes_per_step": MICRO * SEQ * 8 * 2, "d2h_bytes_per_step": 4,
+                    "h2d_bytes_per_step": micro * seq * 8 * 2, "d2h_bytes_per_step": 4,
                     "api": "pluggy.train.trainer.Trainer.train_step"},
             "peak_mem_gib": torch.cuda.max_memory_allocated() / 2**30}
 
@@ -335,6 +393,9 @@ def main():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--config", choices=sorted(BENCH_CONFIGS), default="ddp06b",
+                   help="BASELINE.json config: ddp06b (2, the headline), fsdp4b (3), moe_ep (4), "
+                        "llama_tp (5)")
     args = p.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -355,27 +416,44 @@ def main():
     os.environ.setdefault("WORLD_SIZE", "1")
     dist.init_process_group("nccl", timeout=timedelta(minutes=5), device_id=device)
     try:
-        if args.impl == "reference":
-            res = run_reference(args, rank, local_rank, world, device)
-        else:
-            res = run_ours(args, rank, local_rank, world, device)
+        try:
+            if args.impl == "reference":
+                res = run_reference(args, rank, local_rank, world, device)
+            else:
+                res = run_ours(args, rank, local_rank, world, device)
+        except torch.cuda.OutOfMemoryError as e:
+            # a config that does not fit this many GPUs (e.g. the 14.5B-parameter MoE on one)
+            if rank == 0:
+                print(json.dumps({"metric": METRIC, "impl": args.impl, "n_gpus": world,
+                                  "bench_config": args.config,
+                                  "unavailable": f"out of device memory at {world} GPU(s): "
+                                                 f"{str(e).splitlines()[0][:160]}"}))
+            sys.stdout.flush()
+            os._exit(0)
         clocks = gather_clocks(res.get("clocks", {}), device) if "clocks" in res else None
         if rank == 0:
             if "unavailable" in res:
                 print(json.dumps({"metric": METRIC, "impl": args.impl, "unavailable": res["unavailable"]}))
                 return
+            bc = BENCH_CONFIGS[args.config]
+            lay = layout(args.config, world)
+            par = res.get("ref_parallelism", lay["parallelism"]) if args.impl == "reference" \
+                else lay["parallelism"]
+            tokens = res.get("tokens_per_step", lay["tokens"])
             line = {
                 "metric": METRIC, "value": res["value"], "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
                 "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": (res["value"] / BASELINE_VALUE) if BASELINE_VALUE else None,
                 "dtype": "bf16", "data": "synthetic (Zipf(1.1) ids, EOS every U[512,4096]; random init)",
-                "config": {"model": "qwen3-0.6B-shaped (28L, d1024, 16q/8kv x128, ffn 3072, V151936, tied)",
-                           "global_batch": MICRO * world, "seq_len": SEQ, "parallelism": f"dp{world}",
-                           "micro_batch_per_gpu": MICRO, "l2": "inputs larger than L2 (GBs of activations)"},
+                "config": {"model": bc["label"], "global_batch": tokens // bc["seq"], "seq_len": bc["seq"],
+                           "parallelism": par, "micro_batch_per_gpu": bc["micro"],
+                           "l2": "inputs larger than L2 (GBs of activations)"},
                 "clocks": clocks, "e2e": res.get("e2e"),
                 "peak_mem_gib": res.get("peak_mem_gib"),
             }
+            if args.config != "ddp06b":
+                line["bench_config"] = args.config
             if args.impl == "reference":
                 line["impl"] = "reference"
             else:

@@ -11,6 +11,8 @@ like the NCCL path.
 
 from __future__ import annotations
 
+import os
+
 import torch
 
 from pluggy_b200.comm.symm import SymmetricBuffer
@@ -51,12 +53,15 @@ class BucketReducer:
                 b.views.append(flat[o:o + p.numel()].view_as(p))
                 o += p.numel()
             self.offset[b.index] = (off, numel)
-        # 128 CTAs per bucket: measured best from 8 MB up on B200 (the buckets are 25 MB)
-        self.chunks = chunks or 128
+        # 128 CTAs per bucket: measured best from 8 MB up on B200 (the buckets are 25 MB);
+        # PLG_COMM_CTAS overrides it for measurements
+        self.chunks = chunks or int(os.environ.get("PLG_COMM_CTAS", "128"))
         self.epoch = 0
         self.norm_sq = torch.zeros(1, dtype=torch.float32, device=self.data.device)
         self._first = True
-        self.stream = torch.cuda.Stream()
+        # high priority: at each kernel boundary the block scheduler places the
+        # reduction's CTAs before pending compute CTAs
+        self.stream = torch.cuda.Stream(priority=-1)
 
     def launch(self, b):
         off, numel = self.offset[b.index]

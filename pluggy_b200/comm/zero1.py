@@ -34,6 +34,7 @@ host-side logic.
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 import torch.distributed as dist
@@ -103,12 +104,15 @@ class Zero1Reducer:
                     o += p.numel()
                 self.offset[b.index] = (off, numel)
                 self.slice[b.index] = owned_slice(numel, self.n, self.rank)
-        self.chunks = chunks or 128
+        # CTAs per bucket kernel (PLG_COMM_CTAS overrides the default for measurements)
+        self.chunks = chunks or int(os.environ.get("PLG_COMM_CTAS", "128"))
         self.rs_epoch = 0
         self.ag_epoch = 0
         self.norm_sq = torch.zeros(1, dtype=torch.float32, device=self.device)
         self._first = True
-        self.stream = torch.cuda.Stream(self.device) if self.cuda else None
+        # high priority: at each kernel boundary the block scheduler places the
+        # collective's CTAs before pending compute CTAs
+        self.stream = torch.cuda.Stream(self.device, priority=-1) if self.cuda else None
 
     @staticmethod
     def _numel(b) -> int:
