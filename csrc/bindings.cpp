@@ -72,6 +72,72 @@ void gemm(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool b_mn_m
   plg::gemm_bf16(p, cur_stream());
 }
 
+// Grouped GEMM (MoE experts). mode 1: a [rows, K] (K-major), b = every group's
+// matrix stacked [G * b_rows, ...] (K-major [G*N, K] or MN-major [G*K, N]),
+// table = int32 [rows / 128] group of each 128-row tile (-1: skipped);
+// c [rows, N]. mode 2: a [rows, M] and b [rows, N] both MN-major over the same
+// rows, table = int32 [G + 1] row offsets (multiples of 64); c [G * M, N].
+void gemm_grouped(const at::Tensor& a, const at::Tensor& b, bool b_mn_major, at::Tensor& c,
+                  int64_t mode, const at::Tensor& table, int64_t groups, int64_t b_rows,
+                  double alpha, double beta, const c10::optional<at::Tensor>& status) {
+  check_cuda(a, "a");
+  check_cuda(b, "b");
+  check_cuda(c, "c");
+  check_cuda(table, "table");
+  TORCH_CHECK(is_bf16(a) && is_bf16(b), "gemm_grouped operands must be bf16");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && c.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1 &&
+                  c.stride(1) == 1, "gemm_grouped takes 2-D tensors with unit inner stride");
+  TORCH_CHECK(is_bf16(c) || is_f32(c), "gemm_grouped output must be bf16 or fp32");
+  TORCH_CHECK(table.scalar_type() == at::kInt && table.is_contiguous(), "gemm_grouped: int32 table");
+  TORCH_CHECK(groups >= 1, "gemm_grouped: at least one group");
+  const c10::cuda::CUDAGuard guard(a.device());
+  plg::GemmProblem p;
+  p.grp_mode = static_cast<int>(mode);
+  p.grp_count = static_cast<int>(groups);
+  p.A = a.data_ptr();
+  p.lda = a.stride(0);
+  p.B = b.data_ptr();
+  p.ldb = b.stride(0);
+  p.b_mn_major = b_mn_major;
+  p.C = c.data_ptr();
+  p.ldc = c.stride(0);
+  p.c_fp32 = is_f32(c);
+  if (mode == 1) {
+    p.M = static_cast<int>(a.size(0));
+    p.K = static_cast<int>(a.size(1));
+    p.N = static_cast<int>(b_mn_major ? b.size(1) : b_rows);
+    TORCH_CHECK(b.size(0) == groups * b_rows, "gemm_grouped mode 1: b must stack groups * b_rows rows");
+    TORCH_CHECK(b_mn_major ? b_rows == p.K : b.size(1) == p.K, "gemm_grouped mode 1: K mismatch");
+    TORCH_CHECK(table.numel() >= (p.M + 127) / 128, "gemm_grouped mode 1: one table entry per 128 rows");
+    TORCH_CHECK(c.size(0) == p.M && c.size(1) == p.N, "gemm_grouped mode 1: c must be [rows, N]");
+    p.grp_tile = table.data_ptr<int>();
+    p.grp_b_rows = b_rows;
+  } else if (mode == 2) {
+    TORCH_CHECK(b_mn_major, "gemm_grouped mode 2: b is MN-major");
+    p.a_mn_major = true;
+    p.K = static_cast<int>(a.size(0));
+    p.M = static_cast<int>(a.size(1));
+    p.N = static_cast<int>(b.size(1));
+    TORCH_CHECK(b.size(0) == p.K, "gemm_grouped mode 2: a and b must span the same rows");
+    TORCH_CHECK(table.numel() == groups + 1, "gemm_grouped mode 2: groups + 1 offsets");
+    TORCH_CHECK(c.size(0) == groups * p.M && c.size(1) == p.N, "gemm_grouped mode 2: c must be [G*M, N]");
+    p.grp_koff = table.data_ptr<int>();
+  } else {
+    TORCH_CHECK(false, "gemm_grouped: mode 1 or 2");
+  }
+  if (beta != 0.0) {
+    p.D = c.data_ptr();
+    p.ldd = c.stride(0);
+    p.d_fp32 = is_f32(c);
+  }
+  p.alpha = static_cast<float>(alpha);
+  p.beta = static_cast<float>(beta);
+  p.splits = 1;
+  p.allow_split = false;
+  p.status = status_ptr(status);
+  plg::gemm_bf16(p, cur_stream());
+}
+
 void rmsnorm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& w, at::Tensor& y,
                  const c10::optional<at::Tensor>& rstd, double eps) {
   check_cuda(x, "x");
@@ -636,6 +702,9 @@ void set_peer_wait_deadline(int64_t ns) {
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "pluggy_b200 sm_100a kernels";
   m.def("gemm", &gemm);
+  m.def("gemm_grouped", &gemm_grouped, py::arg("a"), py::arg("b"), py::arg("b_mn_major"), py::arg("c"),
+        py::arg("mode"), py::arg("table"), py::arg("groups"), py::arg("b_rows"), py::arg("alpha"),
+        py::arg("beta"), py::arg("status") = py::none());
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd, py::arg("qkv"), py::arg("q"), py::arg("k"),

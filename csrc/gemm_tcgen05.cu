@@ -57,6 +57,14 @@ struct Args {
   long long rs_S, rs_seg, rs_rows;
   long long rs_cap_rows;  // rows of N that fit in every staging buffer
   void* rs_dst[8];
+  // grouped GEMM (MoE experts; see GemmProblem): 0 none, 1 a group per m tile,
+  // 2 a k range per group
+  int grp_mode;
+  const int* grp_tile;   // mode 1: [m_tiles] group of each m tile (-1: no work)
+  long long grp_b_rows;  // mode 1: rows of B per group (B is [groups * rows, cols])
+  const int* grp_koff;   // mode 2: [groups + 1] row offsets of the k ranges (multiples of BK)
+  long long grp_c_rows;  // mode 2: rows of C per group (C is [groups * M, N])
+  int grp_count;         // mode 2: number of groups
 };
 
 // destination of row `row` under the reduce-scatter epilogue; static indices only
@@ -147,7 +155,8 @@ __device__ __forceinline__ void store_acc_rows_rs(const Args& args, uint32_t t_r
 
 template <int BN>
 __device__ __forceinline__ void store_acc_row(const Args& args, uint32_t t_row, long long row,
-                                              bool row_ok, int col_base, int kb0, uint8_t* stage) {
+                                              bool row_ok, int col_base, int kb0, uint8_t* stage,
+                                              bool zero = false) {
   if (args.rs_n) {
     store_acc_rows_rs<BN>(args, t_row, row, col_base, stage);
     return;
@@ -162,7 +171,7 @@ __device__ __forceinline__ void store_acc_row(const Args& args, uint32_t t_row, 
     if (!row_ok || col0 >= args.N) continue;
     float v[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * args.alpha;
+    for (int i = 0; i < 32; ++i) v[i] = zero ? 0.f : __uint_as_float(r[i]) * args.alpha;
     const bool full = col0 + 32 <= args.N;
     if (args.D != nullptr && args.beta != 0.f && kb0 == 0) {
       if (args.d_fp32) {
@@ -293,12 +302,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_base_smem;
 
   const int total_tiles = args.m_tiles * args.n_tiles;
-  const int total_work = total_tiles * args.splits;
+  const int total_work = total_tiles * (args.grp_mode == 2 ? args.grp_count : args.splits);
   const int kb_per_split = (args.k_blocks + args.splits - 1) / args.splits;
 
-  auto decode = [&](int w, int& mt, int& nt, int& kb0, int& kb1) {
-    int tile = w / args.splits;
-    int sp = w - tile * args.splits;
+  // work unit -> tile (mt, nt), k-block range and group g; false: no work (mode 1
+  // m tile beyond the last group). Every role decodes the same units.
+  auto decode = [&](int w, int& mt, int& nt, int& kb0, int& kb1, int& g) -> bool {
+    g = 0;
+    int tile, sp = 0;
+    if (args.grp_mode == 2) {
+      g = w / total_tiles;
+      tile = w - g * total_tiles;
+    } else {
+      tile = w / args.splits;
+      sp = w - tile * args.splits;
+    }
     if (args.raster_m) {
       mt = tile % args.m_tiles;
       nt = tile / args.m_tiles;
@@ -307,8 +325,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       mt = tile / args.n_tiles;
     }
     if (args.rs_mshift) mt = (mt + args.rs_mshift) % args.m_tiles;
+    if (args.grp_mode == 2) {
+      kb0 = args.grp_koff[g] / BK;
+      kb1 = args.grp_koff[g + 1] / BK;
+      return true;
+    }
     kb0 = sp * kb_per_split;
     kb1 = min(args.k_blocks, kb0 + kb_per_split);
+    if (args.grp_mode == 1) {
+      g = args.grp_tile[mt];
+      return g >= 0;
+    }
+    return true;
   };
 
   if (warp == 0) {
@@ -319,8 +347,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       uint32_t issued_mask = 0, parity_mask = 0;  // per stage: issued, and the phase parity
       for (int w = blockIdx.x; w < total_work && ok; w += gridDim.x) {
-        int mt, nt, kb0, kb1;
-        decode(w, mt, nt, kb0, kb1);
+        int mt, nt, kb0, kb1, g;
+        if (!decode(w, mt, nt, kb0, kb1, g)) continue;
+        // mode 1: B rows of group g start at g * grp_b_rows
+        const int b_row0 = args.grp_mode == 1 ? static_cast<int>(g * args.grp_b_rows) : 0;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, abort_flag)) {
             record_status(args.status, kTimeoutSmemEmpty);
@@ -343,9 +373,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (B_MN) {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
-              tma_load_2d(sB + j * (BK * 128), &tmB, &full_bar[stage], nt * BN + j * 64, k0);
+              tma_load_2d(sB + j * (BK * 128), &tmB, &full_bar[stage], nt * BN + j * 64, b_row0 + k0);
           } else {
-            tma_load_2d(sB, &tmB, &full_bar[stage], k0, nt * BN);
+            tma_load_2d(sB, &tmB, &full_bar[stage], k0, b_row0 + nt * BN);
           }
           issued_mask |= 1u << stage;
           parity_mask = (parity_mask & ~(1u << stage)) | (phase << stage);
@@ -372,11 +402,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc = make_idesc_bf16_f32(BM, BN, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
-      int local = 0;
+      int local = -1;
       bool ok = true;
-      for (int w = blockIdx.x; w < total_work && ok; w += gridDim.x, ++local) {
-        int mt, nt, kb0, kb1;
-        decode(w, mt, nt, kb0, kb1);
+      for (int w = blockIdx.x; w < total_work && ok; w += gridDim.x) {
+        int mt, nt, kb0, kb1, g;
+        if (!decode(w, mt, nt, kb0, kb1, g)) continue;
+        ++local;
         const int buf = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait_bounded(&acce_bar[buf], acc_phase ^ 1u, abort_flag)) {
@@ -423,10 +454,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_in_tile = q * 32 + lane;
-    int local = 0;
-    for (int w = blockIdx.x; w < total_work; w += gridDim.x, ++local) {
-      int mt, nt, kb0, kb1;
-      decode(w, mt, nt, kb0, kb1);
+    int local = -1;
+    for (int w = blockIdx.x; w < total_work; w += gridDim.x) {
+      int mt, nt, kb0, kb1, g;
+      if (!decode(w, mt, nt, kb0, kb1, g)) continue;
+      ++local;
       const int buf = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait_bounded(&accf_bar[buf], acc_phase, abort_flag)) {
@@ -437,8 +469,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const long long row = (long long)mt * BM + row_in_tile;
       const bool row_ok = row < args.M;
+      // mode 2: group g's rows of C; an empty k range stores zeros
+      const long long crow = args.grp_mode == 2 ? g * args.grp_c_rows + row : row;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
-      store_acc_row<BN>(args, t_row, row, row_ok, nt * BN, kb0, epi_stage + q * 32 * 128);
+      // the addend D is applied by the first k split (mode 2 has one split per group)
+      store_acc_row<BN>(args, t_row, crow, row_ok, nt * BN, args.grp_mode == 2 ? 0 : kb0,
+                        epi_stage + q * 32 * 128, kb1 <= kb0);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce_bar[buf]);
@@ -783,9 +819,11 @@ static void launch(const GemmProblem& p, cudaStream_t stream) {
   // A map
   CUtensorMap ta = A_MN ? make_map_2d(p.A, p.K, p.M, p.lda, 64, BK)
                         : make_map_2d(p.A, p.M, p.K, p.lda, BK, BM);
-  CUtensorMap tb = B_MN ? make_map_2d(p.B, p.K, p.N, p.ldb, 64, BK)
-                        : make_map_2d(p.B, p.N, p.K, p.ldb, BK, BN);
-  Args a;
+  // grouped mode 1: B stacks every group's matrix
+  const long long b_rows = (p.grp_mode == 1) ? p.grp_count * p.grp_b_rows : (B_MN ? p.K : p.N);
+  CUtensorMap tb = B_MN ? make_map_2d(p.B, b_rows, p.N, p.ldb, 64, BK)
+                        : make_map_2d(p.B, b_rows, p.K, p.ldb, BK, BN);
+  Args a{};
   a.M = p.M; a.N = p.N; a.K = p.K;
   a.C = p.C; a.ldc = p.ldc; a.D = p.D; a.ldd = p.ldd;
   a.alpha = p.alpha; a.beta = p.beta;
@@ -795,11 +833,17 @@ static void launch(const GemmProblem& p, cudaStream_t stream) {
   a.k_blocks = (p.K + BK - 1) / BK;
   a.status = p.status;
   set_rs_fields(p, a, BM);
+  a.grp_mode = p.grp_mode;
+  a.grp_tile = p.grp_tile;
+  a.grp_b_rows = p.grp_b_rows;
+  a.grp_koff = p.grp_koff;
+  a.grp_c_rows = p.M;
+  a.grp_count = p.grp_count;
   const int sms = num_sms();
   const int tiles = a.m_tiles * a.n_tiles;
   int splits = p.splits;
   if (splits <= 0) splits = (p.c_fp32 && p.allow_split) ? choose_splits(tiles, sms, a.k_blocks) : 1;
-  if (p.rs_n) splits = 1;
+  if (p.rs_n || p.grp_mode) splits = 1;
   if (splits > a.k_blocks) splits = a.k_blocks;
   if (splits < 1) splits = 1;
   // every split must own at least one k-block
@@ -818,7 +862,10 @@ static void launch(const GemmProblem& p, cudaStream_t stream) {
   }
   // raster: walk along the operand that is re-read from L2 less
   a.raster_m = (static_cast<long long>(p.N) > static_cast<long long>(p.M)) ? 1 : 0;
-  const int work = tiles * splits;
+  // grouped mode 1: consecutive units walk one m tile's n tiles (one expert's rows
+  // stay in L2 while its weights stream)
+  if (p.grp_mode == 1) a.raster_m = 0;
+  const int work = tiles * (p.grp_mode == 2 ? p.grp_count : splits);
   const int grid = work < sms ? work : sms;
   auto kern = gemm_kernel<BN, A_MN, B_MN>;
   set_max_smem_once(reinterpret_cast<const void*>(kern), C_::kSmemBytes);
@@ -835,7 +882,7 @@ static void launch_pair(const GemmProblem& p, cudaStream_t stream) {
                         : make_map_2d(p.A, p.M, p.K, p.lda, BK, BM);
   CUtensorMap tb = B_MN ? make_map_2d(p.B, p.K, p.N, p.ldb, 64, BK)
                         : make_map_2d(p.B, p.N, p.K, p.ldb, BK, 128);
-  Args a;
+  Args a{};
   a.M = p.M; a.N = p.N; a.K = p.K;
   a.C = p.C; a.ldc = p.ldc; a.D = p.D; a.ldd = p.ldd;
   a.alpha = p.alpha; a.beta = p.beta;
@@ -903,9 +950,22 @@ void gemm_bf16(const GemmProblem& p, cudaStream_t stream) {
   if (p.ldc % (p.c_fp32 ? 4 : 8)) throw std::invalid_argument("gemm: ldc must keep rows 16-byte aligned");
   if (reinterpret_cast<uintptr_t>(p.C) & 15) throw std::invalid_argument("gemm: C must be 16-byte aligned");
   if (p.splits > 1 && !p.c_fp32) throw std::invalid_argument("gemm: split-K needs an fp32 output");
+  if (p.grp_mode) {
+    if (p.grp_mode < 0 || p.grp_mode > 2 || p.grp_count < 1 || p.rs_n)
+      throw std::invalid_argument("gemm grouped: mode 1 or 2, at least one group, no reduce-scatter");
+    if (p.grp_mode == 1 && (p.grp_tile == nullptr || p.grp_b_rows <= 0 ||
+                            (p.b_mn_major ? (p.K != p.grp_b_rows || p.K % BK)
+                                          : p.N > p.grp_b_rows)))
+      throw std::invalid_argument("gemm grouped mode 1: a tile table and B blocks of N rows "
+                                  "(K-major) or K rows, a multiple of 64 (MN-major)");
+    if (p.grp_mode == 2 && (p.grp_koff == nullptr || !p.a_mn_major || !p.b_mn_major))
+      throw std::invalid_argument("gemm grouped mode 2: k offsets, A and B both MN-major");
+    if (p.grp_mode == 2 && p.D != nullptr && p.D != p.C)
+      throw std::invalid_argument("gemm grouped mode 2: the addend can only be C itself");
+  }
   const bool wide = p.N >= 256 && p.bn != 128;
   // large problems: 256 x 256 tiles on SM pairs (bn == 256 keeps the one-SM kernel)
-  const bool pair = wide && p.bn == 0 && p.M >= 256 && num_sms() >= 2;
+  const bool pair = wide && p.bn == 0 && p.M >= 256 && num_sms() >= 2 && !p.grp_mode;
 #define PLG_GEMM_CASE(BN_, AM, BMJ) \
   if (p.a_mn_major == AM && p.b_mn_major == BMJ) return launch<BN_, AM, BMJ>(p, stream);
 #define PLG_GEMM_PAIR(AM, BMJ) \

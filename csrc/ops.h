@@ -37,6 +37,19 @@ struct GemmProblem {
   long long rs_S = 0;
   void* rs_dst[8] = {};
   long long rs_cap = 0;     // bytes of every staging buffer (stores beyond are skipped)
+  // Grouped GEMM over grp_count groups (MoE experts), one-SM 128-row tiles, no split-K:
+  //  grp_mode 1: the group of each 128-row m tile is grp_tile[m_tile] (device int32,
+  //    -1 = no work: the tile is skipped); B stacks the groups' matrices as
+  //    [grp_count * grp_b_rows, cols] and a tile reads its group's block (K-major B:
+  //    grp_b_rows >= N; MN-major B: grp_b_rows == K, a multiple of 64).
+  //  grp_mode 2: M and N are per group; A and B are MN-major over the same rows, and
+  //    group g sums over rows [grp_koff[g], grp_koff[g + 1]) (device int32 [grp_count + 1],
+  //    multiples of 64), writing rows [g * M, (g + 1) * M) of C; an empty range writes 0.
+  int grp_mode = 0;
+  const int* grp_tile = nullptr;
+  long long grp_b_rows = 0;
+  const int* grp_koff = nullptr;
+  int grp_count = 0;
 };
 void gemm_bf16(const GemmProblem& p, cudaStream_t stream);
 

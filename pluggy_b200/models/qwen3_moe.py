@@ -13,8 +13,8 @@ Parity: reference ``pluggy/models/qwen3_moe/qwen3_moe.py:140-444``:
 * ``last_tokens_per_expert`` per-expert token counts for logging.
 
 CUDA path: the attention sublayer is the fused ``_engine.AttnSublayer``; the
-sparse MLP composes this package's kernels (RMSNorm, router GEMM, expert
-grouped GEMMs + GLU). Under expert parallelism the ``experts`` module is
+sparse MLP composes this package's kernels (RMSNorm, router GEMM, one grouped
+tcgen05 GEMM launch per expert projection over all experts + the GLU kernel). Under expert parallelism the ``experts`` module is
 replaced by ``pluggy_b200.parallel.expert_parallel.EPExperts``.
 """
 
@@ -56,7 +56,12 @@ class Qwen3MoeExperts(nn.Module):
         self.down_proj = nn.Parameter(torch.empty(num_experts, emb_dim, moe_ffn_dim))
 
     def forward(self, h, top_indices, top_weights):
-        return moe_expert_ffn(h, top_indices, top_weights, self.gate_up_proj, self.down_proj)
+        gu_lp = dn_lp = None
+        cache = getattr(self, "weight_cache", None)
+        if cache is not None and h.is_cuda:
+            gu_lp, dn_lp = cache.get(self.gate_up_proj), cache.get(self.down_proj)
+        return moe_expert_ffn(h, top_indices, top_weights, self.gate_up_proj, self.down_proj,
+                              gu_lowp=gu_lp, dn_lowp=dn_lp)
 
 
 class Qwen3MoeSparseMLP(nn.Module):
@@ -146,6 +151,11 @@ class Qwen3Moe(nn.Module):
         self._router_logits: list[torch.Tensor] = []
         self.last_tokens_per_expert: torch.Tensor | None = None
         self.weight_cache = WeightCache()
+        # the expert banks' bf16 copies come from the same cache (kept current by the
+        # optimizer instead of a cast of the whole bank on every forward)
+        for b in self.blocks:
+            if b.use_moe:
+                b.ffn.experts.weight_cache = self.weight_cache
 
     def init_weights(self, std: float = 0.02) -> None:
         for m in self.modules():

@@ -5,9 +5,11 @@ Parity: reference ``pluggy/kernels/moe.py:38-168`` (``moe_expert_ffn``: sort the
 ``gate_up_proj (E, 2I, H)`` / ``down_proj (E, H, I)``, scale by the routing
 weight, scatter-add back). The loop and grouped forms give identical results.
 
-CUDA path: pairs are sorted once; every expert's two GEMMs run on this
-package's tcgen05 GEMM through :func:`pluggy_b200.ops.grouped.grouped_linear`
-(one launch per GEMM over all experts) and the GLU is the sm_100a kernel.
+CUDA path: pairs are sorted once by expert; each of the FFN's projections is
+ONE launch of this package's grouped tcgen05 GEMM over all experts
+(:func:`pluggy_b200.ops.grouped.grouped_swiglu_ffn`: a device-computed padded
+per-expert row layout, no host synchronisation) and the GLU is the sm_100a
+kernel; the combine is a scatter-add of the route-weighted rows.
 """
 
 from __future__ import annotations
@@ -36,7 +38,8 @@ def _expert_ffn_loop(hidden, top_indices, top_weights, gate_up_proj, down_proj):
     return out
 
 
-def _expert_ffn_sorted(hidden, top_indices, top_weights, gate_up_proj, down_proj):
+def _expert_ffn_sorted(hidden, top_indices, top_weights, gate_up_proj, down_proj, gu_lowp=None,
+                       dn_lowp=None):
     from pluggy_b200.ops.grouped import grouped_swiglu_ffn
 
     T, H = hidden.shape
@@ -46,10 +49,10 @@ def _expert_ffn_sorted(hidden, top_indices, top_weights, gate_up_proj, down_proj
     exp = top_indices.reshape(-1)
     w = top_weights.reshape(-1)
     order = torch.argsort(exp, stable=True)
-    s_tok, s_w = tok[order], w[order]
+    s_tok, s_w, s_exp = tok[order], w[order], exp[order]
     counts = torch.bincount(exp, minlength=E)
     x = hidden[s_tok]
-    y = grouped_swiglu_ffn(x, counts, gate_up_proj, down_proj)
+    y = grouped_swiglu_ffn(x, s_exp, counts, gate_up_proj, down_proj, gu_lowp, dn_lowp)
     y = y * s_w.unsqueeze(1).to(y.dtype)
     out = torch.zeros(T, H, device=hidden.device, dtype=y.dtype)
     out.index_add_(0, s_tok, y)
@@ -57,7 +60,7 @@ def _expert_ffn_sorted(hidden, top_indices, top_weights, gate_up_proj, down_proj
 
 
 def moe_expert_ffn(hidden, top_indices, top_weights, gate_up_proj, down_proj, *,
-                   use_grouped_mm: bool | None = None):
+                   use_grouped_mm: bool | None = None, gu_lowp=None, dn_lowp=None):
     """Dropless top-k expert FFN; ``use_grouped_mm`` None = auto (CUDA -> sorted grouped path)."""
     assert hidden.dim() == 2 and top_indices.shape == top_weights.shape
     assert top_indices.shape[0] == hidden.shape[0]
@@ -65,5 +68,6 @@ def moe_expert_ffn(hidden, top_indices, top_weights, gate_up_proj, down_proj, *,
     if use_grouped_mm is None:
         use_grouped_mm = hidden.is_cuda
     if use_grouped_mm:
-        return _expert_ffn_sorted(hidden, top_indices, top_weights, gate_up_proj, down_proj)
+        return _expert_ffn_sorted(hidden, top_indices, top_weights, gate_up_proj, down_proj,
+                                  gu_lowp, dn_lowp)
     return _expert_ffn_loop(hidden, top_indices, top_weights, gate_up_proj, down_proj)

@@ -98,7 +98,12 @@ class EPExperts(nn.Module):
             back_fn = lambda y: _AllToAllV.apply(y, recv, send, self.mesh, self.dim)  # noqa: E731
         if x.shape[0] > 0:
             ones = torch.ones(x.shape[0], 1, device=h.device, dtype=h.dtype)
-            y = moe_expert_ffn(x, r_exp.view(-1, 1), ones, self.gate_up_proj, self.down_proj)
+            gu_lp = dn_lp = None
+            cache = getattr(self, "weight_cache", None)
+            if cache is not None and h.is_cuda:
+                gu_lp, dn_lp = cache.get(self.gate_up_proj), cache.get(self.down_proj)
+            y = moe_expert_ffn(x, r_exp.view(-1, 1), ones, self.gate_up_proj, self.down_proj,
+                               gu_lowp=gu_lp, dn_lowp=dn_lp)
         else:
             # no rows for this rank's experts: keep the expert params in the graph
             y = x + 0.0 * (self.gate_up_proj.sum() + self.down_proj.sum()).to(x.dtype)
@@ -171,6 +176,7 @@ def parallelize_ep(model: nn.Module, mesh, dim: str = "dp", fused: bool | None =
         if experts is None or not hasattr(experts, "gate_up_proj"):
             continue
         ffn.experts = EPExperts(experts, mesh, dim)
+        ffn.experts.weight_cache = getattr(model, "weight_cache", None)
         ep.expert_params += [ffn.experts.gate_up_proj, ffn.experts.down_proj]
         if fused and mesh.size(dim) > 1:
             if ep.comm is None:

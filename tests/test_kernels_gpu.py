@@ -385,6 +385,86 @@ def test_fused_model_matches_eager(family):
         assert r < 6e-2, (n, r)
 
 
+# --------------------------------------------------------------- grouped GEMM (MoE)
+def test_grouped_gemm_modes_match_fp32():
+    """Mode 1 (a group per 128-row tile, skipped tiles) and mode 2 (a k range per
+    group, empty groups write zeros) against per-group fp32 matmuls."""
+    from pluggy_b200.ops._ext import ext
+    from pluggy_b200.ops.grouped import expert_layout
+
+    torch.manual_seed(0)
+    E, K, N = 6, 192, 320
+    counts = torch.tensor([130, 0, 5, 256, 1, 77], device=DEV)
+    P = int(counts.sum())
+    poff, shift, tg, R = expert_layout(counts, P)
+    ex = torch.repeat_interleave(torch.arange(E, device=DEV), counts)
+    dst = torch.arange(P, device=DEV) + shift[ex]
+    x = torch.randn(P, K, device=DEV).bfloat16()
+    x_pad = torch.zeros(R, K, dtype=torch.bfloat16, device=DEV)
+    x_pad[dst] = x
+    w = (torch.randn(E, N, K, device=DEV) * 0.05).bfloat16()
+    # mode 1, K-major B (forward)
+    y = torch.empty(R, N, dtype=torch.bfloat16, device=DEV)
+    ext().gemm_grouped(x_pad, w.view(E * N, K), False, y, 1, tg, E, N, 1.0, 0.0)
+    ref = torch.einsum("pk,pnk->pn", x.float(), w.float()[ex])
+    assert rel(y[dst].float(), ref) < 1e-2
+    # mode 1, MN-major B (input gradient): dx = dy W_e
+    dy = torch.randn(P, N, device=DEV).bfloat16()
+    dy_pad = torch.zeros(R, N, dtype=torch.bfloat16, device=DEV)
+    dy_pad[dst] = dy
+    wt = (torch.randn(E, N, K, device=DEV) * 0.05).bfloat16()  # [E, rows=N(k dim), K(out)]
+    dx = torch.empty(R, K, dtype=torch.bfloat16, device=DEV)
+    ext().gemm_grouped(dy_pad, wt.view(E * N, K), True, dx, 1, tg, E, N, 1.0, 0.0)
+    ref = torch.einsum("pn,pnk->pk", dy.float(), wt.float()[ex])
+    assert rel(dx[dst].float(), ref) < 1e-2
+    # mode 2 (weight gradient): dW_e = dy_e^T x_e, fp32, empty expert -> 0
+    dw = torch.full((E * N, K), float("nan"), device=DEV)
+    ext().gemm_grouped(dy_pad, x_pad, True, dw, 2, poff, E, 0, 1.0, 0.0)
+    dw = dw.view(E, N, K)
+    off = 0
+    for e, n in enumerate(counts.tolist()):
+        want = dy[off:off + n].float().t() @ x[off:off + n].float()
+        if n == 0:
+            assert torch.count_nonzero(dw[e]) == 0
+        else:
+            assert rel(dw[e], want) < 1e-2, e
+        off += n
+    # mode 2 accumulating into C (beta = 1)
+    base = torch.randn(E * N, K, device=DEV)
+    acc = base.clone()
+    ext().gemm_grouped(dy_pad, x_pad, True, acc, 2, poff, E, 0, 1.0, 1.0)
+    assert rel(acc.view(E, N, K) - base.view(E, N, K), dw) < 1e-4
+
+
+def test_grouped_swiglu_ffn_matches_loop():
+    """The one-launch-per-projection grouped FFN against the per-expert loop (fp32
+    CPU math), forward and every gradient; includes an expert with no rows."""
+    from pluggy_b200.ops.moe import moe_expert_ffn
+
+    torch.manual_seed(1)
+    T, H, I, E, k = 200, 256, 128, 8, 2
+    h = torch.randn(T, H, device=DEV)
+    logits = torch.randn(T, E, device=DEV)
+    logits[:, 3] = -1e9  # expert 3 gets nothing
+    w, idx = torch.topk(torch.softmax(logits, -1), k, dim=-1)
+    gu = (torch.randn(E, 2 * I, H, device=DEV) * 0.05).requires_grad_()
+    dn = (torch.randn(E, H, I, device=DEV) * 0.05).requires_grad_()
+    hx = h.clone().requires_grad_()
+    y = moe_expert_ffn(hx, idx, w, gu, dn)
+    gy = torch.randn_like(y)
+    (y * gy).sum().backward()
+    gc = gu.detach().cpu().requires_grad_()
+    dc = dn.detach().cpu().requires_grad_()
+    hc = h.cpu().requires_grad_()
+    yc = moe_expert_ffn(hc, idx.cpu(), w.cpu(), gc, dc, use_grouped_mm=False)
+    (yc * gy.cpu()).sum().backward()
+    assert rel(y.cpu(), yc) < 2e-2
+    assert rel(hx.grad.cpu(), hc.grad) < 3e-2
+    assert rel(gu.grad.cpu(), gc.grad) < 3e-2
+    assert rel(dn.grad.cpu(), dc.grad) < 3e-2
+    assert torch.count_nonzero(gu.grad[3]) == 0 and torch.count_nonzero(dn.grad[3]) == 0
+
+
 def test_colsum_matches_torch():
     from pluggy_b200.ops.norm import _colsum
 
