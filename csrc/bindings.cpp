@@ -305,17 +305,40 @@ void softcap(const at::Tensor& x, at::Tensor& y, double cap) {
 }
 
 void ce_rows(at::Tensor& logits, const at::Tensor& labels, int64_t ignore_index, double grad_scale,
-             double softcap, const c10::optional<at::Tensor>& lse, at::Tensor& loss_sum,
-             const c10::optional<at::Tensor>& n_valid) {
+             double softcap, const c10::optional<at::Tensor>& lse,
+             const c10::optional<at::Tensor>& loss_sum, const c10::optional<at::Tensor>& n_valid,
+             const c10::optional<at::Tensor>& row_loss) {
   check_cuda(logits, "logits");
   TORCH_CHECK(is_bf16(logits) && logits.dim() == 2 && logits.stride(1) == 1, "ce logits layout");
   TORCH_CHECK(labels.scalar_type() == at::kLong && labels.is_contiguous(), "ce labels");
+  if (row_loss.has_value())
+    TORCH_CHECK(is_f32(*row_loss) && row_loss->is_contiguous() && row_loss->numel() == logits.size(0),
+                "ce row_loss: fp32 [rows]");
+  TORCH_CHECK(loss_sum.has_value() || row_loss.has_value(), "ce_rows: loss_sum or row_loss");
   const c10::cuda::CUDAGuard guard(logits.device());
   plg::ce_rows(logits.data_ptr(), logits.stride(0), labels.data_ptr<int64_t>(), logits.size(0),
                static_cast<int>(logits.size(1)), static_cast<int>(ignore_index),
                static_cast<float>(grad_scale), static_cast<float>(softcap),
-               lse.has_value() ? lse->data_ptr<float>() : nullptr, loss_sum.data_ptr<float>(),
-               n_valid.has_value() ? n_valid->data_ptr<int>() : nullptr, cur_stream());
+               lse.has_value() ? lse->data_ptr<float>() : nullptr,
+               loss_sum.has_value() ? loss_sum->data_ptr<float>() : nullptr,
+               n_valid.has_value() ? n_valid->data_ptr<int>() : nullptr, cur_stream(),
+               row_loss.has_value() ? row_loss->data_ptr<float>() : nullptr);
+}
+
+void embedding_bwd_sorted(const at::Tensor& ids_sorted, const at::Tensor& pos_sorted,
+                          const at::Tensor& dout, at::Tensor& dw, double scale) {
+  check_cuda(dout, "dout");
+  TORCH_CHECK(ids_sorted.scalar_type() == at::kLong && pos_sorted.scalar_type() == at::kLong &&
+                  ids_sorted.is_contiguous() && pos_sorted.is_contiguous() &&
+                  ids_sorted.numel() == pos_sorted.numel() && ids_sorted.numel() == dout.size(0),
+              "embedding_bwd_sorted: int64 sorted ids and positions, one per dout row");
+  TORCH_CHECK(is_f32(dout) && is_f32(dw) && dout.is_contiguous() && dw.is_contiguous() &&
+                  dout.dim() == 2 && dw.dim() == 2 && dout.size(1) == dw.size(1),
+              "embedding_bwd_sorted: fp32 dout [T, D] and dw [V, D]");
+  const c10::cuda::CUDAGuard guard(dout.device());
+  plg::embedding_bwd_sorted(ids_sorted.data_ptr<int64_t>(), pos_sorted.data_ptr<int64_t>(),
+                            dout.data_ptr<float>(), dw.data_ptr<float>(), dout.size(0),
+                            static_cast<int>(dout.size(1)), static_cast<float>(scale), cur_stream());
 }
 
 void multi_sumsq(const at::Tensor& table, int64_t ntensors, int64_t total_chunks, at::Tensor& out) {
@@ -752,7 +775,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd", &embedding_bwd);
   m.def("softcap", &softcap);
-  m.def("ce_rows", &ce_rows);
+  m.def("ce_rows", &ce_rows, py::arg("logits"), py::arg("labels"), py::arg("ignore_index"),
+        py::arg("grad_scale"), py::arg("softcap"), py::arg("lse"), py::arg("loss_sum"),
+        py::arg("n_valid"), py::arg("row_loss") = py::none());
+  m.def("embedding_bwd_sorted", &embedding_bwd_sorted);
   m.def("multi_sumsq", &multi_sumsq);
   m.def("multi_scale", &multi_scale);
   m.def("adamw_multi", &adamw_multi);

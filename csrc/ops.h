@@ -103,17 +103,22 @@ void embedding_fwd(const int64_t* ids, const float* w, float* out_f32, long long
 // dw[ids[t]] += scale * dout[t]  (fp32 atomics)
 void embedding_bwd(const int64_t* ids, const float* dout, float* dw, long long T, int D,
                    float scale, cudaStream_t stream);
+// deterministic form: ids sorted ascending (stable) with their token positions;
+// dw[id] += scale * sum of dout rows of that id, summed in token order, no atomics
+void embedding_bwd_sorted(const int64_t* ids_sorted, const int64_t* pos_sorted, const float* dout,
+                          float* dw, long long T, int D, float scale, cudaStream_t stream);
 // y = cap * tanh(x / cap)
 void softcap_fwd(const void* x, void* y, long long n, float cap, bool bf16, cudaStream_t stream);
 
 // ---------------------------------------------------------------- cross entropy
 // Per row of bf16 logits [rows, V]: lse, loss = lse - logit[label] (0 for
 // ignored rows), and in place: logits <- (softmax - onehot) * grad_scale.
-// loss_sum accumulates sum of row losses (fp32 atomic). softcap > 0 applies
+// row_loss (when given) receives every row's loss, for a deterministic sum by the
+// caller; otherwise loss_sum accumulates them (fp32 atomic). softcap > 0 applies
 // cap*tanh(x/cap) first (its derivative folded into the gradient).
 void ce_rows(void* logits, long long ld, const int64_t* labels, long long rows, int V,
              int ignore_index, float grad_scale, float softcap, float* lse_out, float* loss_sum,
-             int* n_valid, cudaStream_t stream);
+             int* n_valid, cudaStream_t stream, float* row_loss = nullptr);
 
 // ---------------------------------------------------------------- optimizer
 struct TensorRef { void* p; long long n; };

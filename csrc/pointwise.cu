@@ -165,6 +165,42 @@ __global__ void embedding_bwd_kernel(const int64_t* __restrict__ ids,
   }
 }
 
+// Deterministic embedding backward over ids sorted ascending (stable): the CTA of
+// the first sorted position of each id sums that id's dout rows in sorted order
+// (= token order) and adds the sum into dw[id]. Every id has exactly one owner
+// CTA, so there are no atomics and the result does not depend on scheduling.
+__global__ void __launch_bounds__(256) embedding_bwd_sorted_kernel(
+    const int64_t* __restrict__ ids_sorted, const int64_t* __restrict__ pos_sorted,
+    const float* __restrict__ dout, float* __restrict__ dw, long long T, int D, float scale) {
+  const long long i = blockIdx.x;
+  if (i >= T) return;
+  const int64_t id = ids_sorted[i];
+  if (i > 0 && ids_sorted[i - 1] == id) return;  // not the first position of the run
+  // run end: scan forward blockDim positions at a time
+  __shared__ long long s_end;
+  if (threadIdx.x == 0) s_end = T;
+  __syncthreads();
+  for (long long base = i + 1; base < T; base += blockDim.x) {
+    const long long j = base + threadIdx.x;
+    const bool stop = j < T && ids_sorted[j] != id;
+    if (stop) atomicMin(reinterpret_cast<unsigned long long*>(&s_end), static_cast<unsigned long long>(j));
+    if (__syncthreads_or(stop || base + blockDim.x >= T)) break;
+  }
+  const long long end = s_end;
+  float* dst = dw + id * (long long)D;
+  for (int c = threadIdx.x * 4; c < D; c += blockDim.x * 4) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+    for (long long j = i; j < end; ++j) {
+      const float4 v = *reinterpret_cast<const float4*>(dout + pos_sorted[j] * D + c);
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    float4 d = *reinterpret_cast<float4*>(dst + c);
+    d.x += acc.x * scale; d.y += acc.y * scale; d.z += acc.z * scale; d.w += acc.w * scale;
+    *reinterpret_cast<float4*>(dst + c) = d;
+  }
+}
+
 template <typename T>
 __global__ void softcap_kernel(const T* __restrict__ x, T* __restrict__ y, long long n, float cap) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
@@ -184,7 +220,7 @@ constexpr int kCeThreads = 1024;
 __global__ void __launch_bounds__(kCeThreads, 2) ce_rows_kernel(
     __nv_bfloat16* __restrict__ logits, long long ld, const int64_t* __restrict__ labels, int V,
     int ignore_index, float grad_scale, float softcap, float* __restrict__ lse_out,
-    float* __restrict__ loss_sum, int* __restrict__ n_valid) {
+    float* __restrict__ loss_sum, int* __restrict__ n_valid, float* __restrict__ row_loss) {
   const long long row = blockIdx.x;
   __nv_bfloat16* x = logits + row * ld;
   const int64_t lab = labels[row];
@@ -251,12 +287,16 @@ __global__ void __launch_bounds__(kCeThreads, 2) ce_rows_kernel(
   const float lse = s_m[0] + logf(s_s[0]);
   if (threadIdx.x == 0) {
     if (lse_out) lse_out[row] = lse;
+    float loss = 0.f;
     if (valid) {
       float tgt = __bfloat162float(x[lab]);
       if (cap) tgt = softcap * tanhf(tgt / softcap);
-      atomicAdd(loss_sum, lse - tgt);
+      loss = lse - tgt;
       if (n_valid) atomicAdd(n_valid, 1);
     }
+    // per-row losses (summed later in a fixed order) or an fp32 atomic sum
+    if (row_loss) row_loss[row] = loss;
+    else if (valid && loss_sum) atomicAdd(loss_sum, loss);
   }
   __syncthreads();  // the target logit is read before pass 2 overwrites it
   // pass 2: gradient in place
@@ -532,6 +572,15 @@ void embedding_bwd(const int64_t* ids, const float* dout, float* dw, long long T
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 
+void embedding_bwd_sorted(const int64_t* ids_sorted, const int64_t* pos_sorted, const float* dout,
+                          float* dw, long long T, int D, float scale, cudaStream_t st) {
+  if (T <= 0) return;
+  if (D % 4 || (reinterpret_cast<uintptr_t>(dout) & 15) || (reinterpret_cast<uintptr_t>(dw) & 15))
+    throw std::invalid_argument("embedding_bwd_sorted: D a multiple of 4, 16-byte aligned rows");
+  embedding_bwd_sorted_kernel<<<T, 256, 0, st>>>(ids_sorted, pos_sorted, dout, dw, T, D, scale);
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
 void softcap_fwd(const void* x, void* y, long long n, float cap, bool bf16, cudaStream_t st) {
   if (n <= 0) return;
   if (bf16)
@@ -545,13 +594,13 @@ void softcap_fwd(const void* x, void* y, long long n, float cap, bool bf16, cuda
 
 void ce_rows(void* logits, long long ld, const int64_t* labels, long long rows, int V,
              int ignore_index, float grad_scale, float softcap, float* lse_out, float* loss_sum,
-             int* n_valid, cudaStream_t st) {
+             int* n_valid, cudaStream_t st, float* row_loss) {
   if (rows <= 0) return;
   if ((ld % 8) || (reinterpret_cast<uintptr_t>(logits) & 15))
     throw std::invalid_argument("ce_rows: logits rows must be 16-byte aligned");
   ce_rows_kernel<<<rows, kCeThreads, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(logits), ld, labels,
                                               V, ignore_index, grad_scale, softcap, lse_out,
-                                              loss_sum, n_valid);
+                                              loss_sum, n_valid, row_loss);
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -163,7 +163,8 @@ class MlpSublayer(torch.autograd.Function):
 
 
 class Embedding(torch.autograd.Function):
-    """ids [T] -> w[ids] * scale as fp32 [T, D]; backward scatter-adds (fp32 atomics)."""
+    """ids [T] -> w[ids] * scale as fp32 [T, D]; backward sums each id's rows in token
+    order (ids sorted once; deterministic, no atomics)."""
 
     @staticmethod
     def forward(ctx, ids, w, scale: float):
@@ -179,7 +180,8 @@ class Embedding(torch.autograd.Function):
     def backward(ctx, dy):
         (ids,) = ctx.saved_tensors
         dw = torch.zeros(ctx.shape, dtype=torch.float32, device=dy.device)
-        ext().embedding_bwd(ids, dy.contiguous().float(), dw, float(ctx.scale))
+        ids_sorted, pos = torch.sort(ids, stable=True)
+        ext().embedding_bwd_sorted(ids_sorted, pos, dy.contiguous().float(), dw, float(ctx.scale))
         return None, dw, None
 
 

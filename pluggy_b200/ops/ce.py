@@ -47,7 +47,8 @@ class _FusedLinearCE(torch.autograd.Function):
             h = hidden.to(torch.bfloat16).contiguous()
             w = w_lowp if w_lowp is not None else weight.to(torch.bfloat16)
             V = w.shape[0]
-            loss_sum = torch.zeros(1, dtype=torch.float32, device=dev)
+            # per-row losses, summed once in a fixed order (deterministic)
+            row_loss = torch.empty(N, dtype=torch.float32, device=dev)
             grad_h = torch.empty((N, D), dtype=torch.bfloat16, device=dev)
             # the first chunk's wgrad GEMM writes grad_w (beta = 0), later ones accumulate
             grad_w = torch.empty((V, D), dtype=torch.float32, device=dev) if need_w else None
@@ -58,14 +59,14 @@ class _FusedLinearCE(torch.autograd.Function):
                 lg = logits[: e - s]
                 gemm(h[s:e], w, out=lg)
                 ext().ce_rows(lg, lab[s:e], int(ignore_index), 1.0, float(softcap or 0.0), None,
-                              loss_sum, None)
+                              None, None, row_loss[s:e])
                 gemm(lg, w, b_mn_major=True, out=grad_h[s:e])
                 if need_w:
                     gemm(lg, h[s:e], a_mn_major=True, b_mn_major=True, out=grad_w,
                          addend=grad_w if s > 0 else None, beta=1.0)
             if N == 0 and grad_w is not None:
                 grad_w.zero_()
-            loss_sum = loss_sum[0]
+            loss_sum = row_loss.sum()
             grad_h = grad_h.to(hidden.dtype)
         else:
             assert not softcap, "softcap on the fused-CE path is a CUDA-only option"

@@ -239,6 +239,66 @@ def test_embedding_fwd_bwd():
     assert rel(w.grad, ref) < 1e-6
 
 
+def test_embedding_bwd_deterministic_with_a_hot_id():
+    """Zipf-like ids (one id on a third of the positions, runs longer than a CTA):
+    the sorted backward matches index_add in fp64 and is bitwise identical on a rerun."""
+    from pluggy_b200.models._engine import Embedding
+
+    torch.manual_seed(3)
+    V, D, T = 5000, 1024, 4096
+    ids = torch.randint(0, V, (T,), device=DEV)
+    ids[::3] = 7
+    w = torch.randn(V, D, device=DEV, requires_grad=True)
+    g = torch.randn(T, D, device=DEV)
+    grads = []
+    for _ in range(2):
+        w.grad = None
+        Embedding.apply(ids, w, 1.0).backward(g)
+        grads.append(w.grad.clone())
+    assert torch.equal(grads[0], grads[1])
+    ref = torch.zeros(V, D, dtype=torch.float64, device=DEV).index_add_(0, ids, g.double())
+    assert rel(grads[0], ref) < 1e-6
+
+
+def test_kernels_rerun_bitwise():
+    """Kernels whose summation order is fixed (no atomics on floats) give bitwise
+    identical results on a second run: a race would show up as a difference."""
+    from pluggy_b200.ops import optim
+    from pluggy_b200.ops.attention import attn_fwd
+    from pluggy_b200.ops.ce import fused_linear_cross_entropy
+    from pluggy_b200.ops.gemm import linear_dgrad, linear_fwd
+    from pluggy_b200.ops.norm import rmsnorm_bwd, rmsnorm_fwd
+
+    torch.manual_seed(4)
+    x = torch.randn(3000, 1024, device=DEV).bfloat16()
+    w = (torch.randn(1536, 1024, device=DEV) * 0.05).bfloat16()
+    dy = torch.randn(3000, 1536, device=DEV).bfloat16()
+    q = torch.randn(2, 512, 4, 128, device=DEV).bfloat16()
+    k = torch.randn(2, 512, 2, 128, device=DEV).bfloat16()
+    v = torch.randn(2, 512, 2, 128, device=DEV).bfloat16()
+    xf = torch.randn(3000, 1024, device=DEV)
+    nw = torch.rand(1024, device=DEV) + 0.5
+    dn = torch.randn(3000, 1024, device=DEV)
+    h = (torch.randn(700, 256, device=DEV) * 0.5).bfloat16()
+    wv = (torch.randn(3000, 256, device=DEV) * 0.05)
+    lab = torch.randint(0, 3000, (700,), device=DEV)
+    ts = [torch.randn(n, device=DEV) for n in (100, 70000, 65536 * 3)]
+
+    def run():
+        out = [linear_fwd(x, w), linear_dgrad(dy, w), attn_fwd(q, k, v)[0]]
+        yb, r = rmsnorm_fwd(xf, nw, 1e-6)
+        out += [yb, r]
+        out += list(rmsnorm_bwd(dn, xf, nw, r))
+        out.append(fused_linear_cross_entropy(h, wv, lab, -100, 256))
+        out.append(optim.multi_tensor_sumsq(ts))
+        return out
+
+    a, b = run(), run()
+    for i, (u, t) in enumerate(zip(a, b)):
+        if isinstance(u, torch.Tensor):
+            assert torch.equal(u, t), i
+
+
 # ------------------------------------------------------------- fused lin-CE
 @pytest.mark.parametrize("N,chunk", [(1000, 256), (2048, 2048), (333, 4096)])
 def test_fused_linear_ce(N, chunk):
