@@ -307,14 +307,23 @@ void softcap(const at::Tensor& x, at::Tensor& y, double cap) {
 void ce_rows(at::Tensor& logits, const at::Tensor& labels, int64_t ignore_index, double grad_scale,
              double softcap, const c10::optional<at::Tensor>& lse,
              const c10::optional<at::Tensor>& loss_sum, const c10::optional<at::Tensor>& n_valid,
-             const c10::optional<at::Tensor>& row_loss) {
+             const c10::optional<at::Tensor>& row_loss, const c10::optional<at::Tensor>& stats,
+             const c10::optional<at::Tensor>& lse_in, int64_t label_offset) {
   check_cuda(logits, "logits");
   TORCH_CHECK(is_bf16(logits) && logits.dim() == 2 && logits.stride(1) == 1, "ce logits layout");
   TORCH_CHECK(labels.scalar_type() == at::kLong && labels.is_contiguous(), "ce labels");
   if (row_loss.has_value())
     TORCH_CHECK(is_f32(*row_loss) && row_loss->is_contiguous() && row_loss->numel() == logits.size(0),
                 "ce row_loss: fp32 [rows]");
-  TORCH_CHECK(loss_sum.has_value() || row_loss.has_value(), "ce_rows: loss_sum or row_loss");
+  if (stats.has_value())
+    TORCH_CHECK(is_f32(*stats) && stats->is_contiguous() && stats->numel() == 3 * logits.size(0),
+                "ce stats: fp32 [rows, 3]");
+  if (lse_in.has_value())
+    TORCH_CHECK(is_f32(*lse_in) && lse_in->is_contiguous() && lse_in->numel() == logits.size(0),
+                "ce lse_in: fp32 [rows]");
+  TORCH_CHECK(!(stats.has_value() && lse_in.has_value()), "ce_rows: stats or lse_in, not both");
+  TORCH_CHECK(loss_sum.has_value() || row_loss.has_value() || stats.has_value() || lse_in.has_value(),
+              "ce_rows: loss_sum, row_loss, stats or lse_in");
   const c10::cuda::CUDAGuard guard(logits.device());
   plg::ce_rows(logits.data_ptr(), logits.stride(0), labels.data_ptr<int64_t>(), logits.size(0),
                static_cast<int>(logits.size(1)), static_cast<int>(ignore_index),
@@ -322,7 +331,9 @@ void ce_rows(at::Tensor& logits, const at::Tensor& labels, int64_t ignore_index,
                lse.has_value() ? lse->data_ptr<float>() : nullptr,
                loss_sum.has_value() ? loss_sum->data_ptr<float>() : nullptr,
                n_valid.has_value() ? n_valid->data_ptr<int>() : nullptr, cur_stream(),
-               row_loss.has_value() ? row_loss->data_ptr<float>() : nullptr);
+               row_loss.has_value() ? row_loss->data_ptr<float>() : nullptr,
+               stats.has_value() ? stats->data_ptr<float>() : nullptr,
+               lse_in.has_value() ? lse_in->data_ptr<float>() : nullptr, label_offset);
 }
 
 void embedding_bwd_sorted(const at::Tensor& ids_sorted, const at::Tensor& pos_sorted,
@@ -777,7 +788,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("softcap", &softcap);
   m.def("ce_rows", &ce_rows, py::arg("logits"), py::arg("labels"), py::arg("ignore_index"),
         py::arg("grad_scale"), py::arg("softcap"), py::arg("lse"), py::arg("loss_sum"),
-        py::arg("n_valid"), py::arg("row_loss") = py::none());
+        py::arg("n_valid"), py::arg("row_loss") = py::none(), py::arg("stats") = py::none(),
+        py::arg("lse_in") = py::none(), py::arg("label_offset") = 0);
   m.def("embedding_bwd_sorted", &embedding_bwd_sorted);
   m.def("multi_sumsq", &multi_sumsq);
   m.def("multi_scale", &multi_scale);

@@ -118,7 +118,12 @@ void softcap_fwd(const void* x, void* y, long long n, float cap, bool bf16, cuda
 // cap*tanh(x/cap) first (its derivative folded into the gradient).
 void ce_rows(void* logits, long long ld, const int64_t* labels, long long rows, int V,
              int ignore_index, float grad_scale, float softcap, float* lse_out, float* loss_sum,
-             int* n_valid, cudaStream_t stream, float* row_loss = nullptr);
+             int* n_valid, cudaStream_t stream, float* row_loss = nullptr,
+             float* stats_out = nullptr, const float* lse_in = nullptr, long long label_offset = 0);
+// Vocabulary-parallel rows (columns [label_offset, label_offset + V) of the full
+// vocabulary): with stats_out [rows][3], only (max, sum of exp, owned target
+// logit or 0) are written and the logits are left alone; with lse_in [rows] (the
+// full-vocabulary lse), only the in-place gradient pass runs.
 
 // ---------------------------------------------------------------- optimizer
 struct TensorRef { void* p; long long n; };

@@ -220,15 +220,25 @@ constexpr int kCeThreads = 1024;
 __global__ void __launch_bounds__(kCeThreads, 2) ce_rows_kernel(
     __nv_bfloat16* __restrict__ logits, long long ld, const int64_t* __restrict__ labels, int V,
     int ignore_index, float grad_scale, float softcap, float* __restrict__ lse_out,
-    float* __restrict__ loss_sum, int* __restrict__ n_valid, float* __restrict__ row_loss) {
+    float* __restrict__ loss_sum, int* __restrict__ n_valid, float* __restrict__ row_loss,
+    float* __restrict__ stats_out, const float* __restrict__ lse_in, long long label_offset) {
   const long long row = blockIdx.x;
   __nv_bfloat16* x = logits + row * ld;
-  const int64_t lab = labels[row];
-  const bool valid = lab != ignore_index;
+  const int64_t lab_g = labels[row];
+  const bool valid = lab_g != ignore_index;
+  // vocabulary-parallel rows hold the columns [label_offset, label_offset + V) of the
+  // full vocabulary: the target is on this row only when its label falls inside
+  const long long lab = valid ? lab_g - label_offset : -1;
+  const bool owned = valid && lab >= 0 && lab < V;
   const bool cap = softcap > 0.f;
   __shared__ float s_m[kCeThreads / 32], s_s[kCeThreads / 32];
   float m = -INFINITY, s = 0.f;
   const int nvec = V / 8;
+  float lse;
+  if (lse_in != nullptr) {
+    // gradient pass of a vocabulary-parallel row: the lse over the full vocabulary is given
+    lse = lse_in[row];
+  } else {
   for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
     uint4 u = reinterpret_cast<const uint4*>(x)[i];
     float f[8];
@@ -284,7 +294,22 @@ __global__ void __launch_bounds__(kCeThreads, 2) ce_rows_kernel(
     if (lane == 0) { s_m[0] = m; s_s[0] = s; }
   }
   __syncthreads();
-  const float lse = s_m[0] + logf(s_s[0]);
+  lse = s_m[0] + logf(s_s[0]);
+  if (stats_out != nullptr) {
+    // statistics pass of a vocabulary-parallel row: (max, sum of exp relative to the
+    // max, target logit or 0) of this shard; the caller combines the shards
+    if (threadIdx.x == 0) {
+      float tgt = 0.f;
+      if (owned) {
+        tgt = __bfloat162float(x[lab]);
+        if (cap) tgt = softcap * tanhf(tgt / softcap);
+      }
+      stats_out[3 * row] = s_m[0];
+      stats_out[3 * row + 1] = s_s[0];
+      stats_out[3 * row + 2] = tgt;
+    }
+    return;
+  }
   if (threadIdx.x == 0) {
     if (lse_out) lse_out[row] = lse;
     float loss = 0.f;
@@ -299,6 +324,7 @@ __global__ void __launch_bounds__(kCeThreads, 2) ce_rows_kernel(
     else if (valid && loss_sum) atomicAdd(loss_sum, loss);
   }
   __syncthreads();  // the target logit is read before pass 2 overwrites it
+  }
   // pass 2: gradient in place
   const float gs = valid ? grad_scale : 0.f;
   for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
@@ -594,13 +620,15 @@ void softcap_fwd(const void* x, void* y, long long n, float cap, bool bf16, cuda
 
 void ce_rows(void* logits, long long ld, const int64_t* labels, long long rows, int V,
              int ignore_index, float grad_scale, float softcap, float* lse_out, float* loss_sum,
-             int* n_valid, cudaStream_t st, float* row_loss) {
+             int* n_valid, cudaStream_t st, float* row_loss, float* stats_out,
+             const float* lse_in, long long label_offset) {
   if (rows <= 0) return;
   if ((ld % 8) || (reinterpret_cast<uintptr_t>(logits) & 15))
     throw std::invalid_argument("ce_rows: logits rows must be 16-byte aligned");
   ce_rows_kernel<<<rows, kCeThreads, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(logits), ld, labels,
                                               V, ignore_index, grad_scale, softcap, lse_out,
-                                              loss_sum, n_valid, row_loss);
+                                              loss_sum, n_valid, row_loss, stats_out, lse_in,
+                                              label_offset);
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -58,10 +58,12 @@ class ARObjective:
             assert self.fused_linear_ce, "tensor parallelism needs fused_linear_ce=True"
             hidden = tp_hidden_for_head(core, model(batch["input_ids"], return_final_hidden=True))
             labels = shift_labels(batch["labels"], self.ignore_index)
+            lowp_fn = getattr(core, "lm_head_lowp", None)
+            lowp = lowp_fn() if (callable(lowp_fn) and hidden.is_cuda) else None
             loss = vocab_parallel_cross_entropy(hidden.reshape(-1, hidden.shape[-1]),
                                                 core.lm_head.weight, labels.reshape(-1), tp.vstart,
                                                 tp.mesh, tp.dim, self.ignore_index,
-                                                self.ce_chunk_size)
+                                                self.ce_chunk_size, w_lowp=lowp)
         elif self.fused_linear_ce:
             hidden = model(batch["input_ids"], return_final_hidden=True)
             labels = shift_labels(batch["labels"], self.ignore_index)

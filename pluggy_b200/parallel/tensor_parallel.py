@@ -190,7 +190,10 @@ class _VocabParallelCE(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, hidden, w_local, labels, vstart, mesh, dim, ignore_index, chunk):
+    def forward(ctx, hidden, w_local, labels, vstart, mesh, dim, ignore_index, chunk, w_lowp=None):
+        if hidden.is_cuda:
+            return _VocabParallelCE._forward_cuda(ctx, hidden, w_local, labels, vstart, mesh, dim,
+                                                  ignore_index, chunk, w_lowp)
         T = hidden.shape[0]
         Vl = w_local.shape[0]
         gh = torch.empty(hidden.shape, dtype=torch.float32, device=hidden.device)
@@ -226,17 +229,68 @@ class _VocabParallelCE(torch.autograd.Function):
         return loss_sum / n_valid
 
     @staticmethod
+    def _forward_cuda(ctx, hidden, w_local, labels, vstart, mesh, dim, ignore_index, chunk, w_lowp):
+        """The same algorithm on the sm_100a kernels: per chunk, the local bf16 logits
+        (tcgen05 GEMM), this shard's (max, sum of exp, owned target logit) per row
+        (``ce_rows`` statistics pass), ONE all-gather of those three numbers per row,
+        the full-vocabulary lse combined locally, the gradient written in place over
+        the logits (``ce_rows`` gradient pass), then grad_hidden and grad_W GEMMs."""
+        from pluggy_b200.ops._ext import ext
+        from pluggy_b200.ops.gemm import gemm
+
+        T, D = hidden.shape
+        Vl = w_local.shape[0]
+        dev = hidden.device
+        n = mesh.size(dim)
+        h = hidden.to(torch.bfloat16).contiguous()
+        w = w_lowp if w_lowp is not None else w_local.detach().to(torch.bfloat16)
+        lab = labels.contiguous()
+        valid_all = lab != ignore_index
+        gh = torch.empty((T, D), dtype=torch.float32, device=dev)
+        gw = torch.empty(w_local.shape, dtype=torch.float32, device=dev)
+        row_loss = torch.empty(T, dtype=torch.float32, device=dev)
+        logits = torch.empty((min(chunk, T), Vl), dtype=torch.bfloat16, device=dev)
+        for s in range(0, T, chunk):
+            e = min(s + chunk, T)
+            c = e - s
+            lg = logits[:c]
+            gemm(h[s:e], w, out=lg)
+            st = torch.empty((c, 3), dtype=torch.float32, device=dev)
+            ext().ce_rows(lg, lab[s:e], int(ignore_index), 1.0, 0.0, None, None, None, None, st,
+                          None, int(vstart))
+            allst = all_gather(st, mesh, dim, gather_dim=0).view(n, c, 3)
+            m_all, s_all, t_all = allst[..., 0], allst[..., 1], allst[..., 2]
+            M = m_all.max(dim=0).values
+            lse = M + (s_all * torch.exp(m_all - M)).sum(0).log()
+            tgt = t_all.sum(0)
+            valid = valid_all[s:e]
+            row_loss[s:e] = torch.where(valid, lse - tgt, torch.zeros_like(lse))
+            ext().ce_rows(lg, lab[s:e], int(ignore_index), 1.0, 0.0, None, None, None, None, None,
+                          lse.contiguous(), int(vstart))
+            # this rank's share of grad_hidden; the caller's entry collective sums it
+            gemm(lg, w, b_mn_major=True, out=gh[s:e], out_dtype=torch.float32)
+            gemm(lg, h[s:e], a_mn_major=True, b_mn_major=True, out=gw,
+                 addend=gw if s > 0 else None, beta=1.0)
+        if T == 0:
+            gw.zero_()
+        n_valid = valid_all.sum().clamp(min=1).float()
+        ctx.save_for_backward(gh, gw, n_valid)
+        ctx.h_dtype, ctx.w_dtype = hidden.dtype, w_local.dtype
+        return row_loss.sum() / n_valid
+
+    @staticmethod
     def backward(ctx, grad_out):
         gh, gw, n_valid = ctx.saved_tensors
         s = grad_out / n_valid
-        return (gh * s).to(ctx.h_dtype), (gw * s).to(ctx.w_dtype), None, None, None, None, None, None
+        return (gh * s).to(ctx.h_dtype), (gw * s).to(ctx.w_dtype), None, None, None, None, None, None, None
 
 
 def vocab_parallel_cross_entropy(hidden, w_local, labels, vstart, mesh, dim, ignore_index=-100,
-                                 chunk=4096):
-    """Mean CE over valid rows of ``hidden [T, D] @ W^T`` with W's rows sharded over ``dim``."""
+                                 chunk=4096, w_lowp=None):
+    """Mean CE over valid rows of ``hidden [T, D] @ W^T`` with W's rows sharded over ``dim``.
+    ``w_lowp``: a bf16 copy of ``w_local`` (CUDA; else it is cast here)."""
     return _VocabParallelCE.apply(hidden, w_local, labels, int(vstart), mesh, dim, int(ignore_index),
-                                  int(chunk))
+                                  int(chunk), w_lowp)
 
 
 # ------------------------------------------------------------------ the plan

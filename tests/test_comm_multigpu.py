@@ -217,6 +217,46 @@ def test_tp_peer_collectives_match_nccl():
     run_ranks(_tp_collectives_case, 2, backend="nccl")
 
 
+def _vocab_ce_case(rank, world):
+    import torch.distributed as dist
+
+    from pluggy_b200.core.mesh import Mesh
+    from pluggy_b200.ops.ce import fused_linear_cross_entropy
+    from pluggy_b200.parallel.tensor_parallel import vocab_parallel_cross_entropy
+
+    mesh = Mesh({"tp": world})
+    torch.manual_seed(0)  # same full problem on every rank
+    N, D, V = 1500, 256, 6000
+    h = (torch.randn(N, D, device="cuda") * 0.5).bfloat16()
+    w = torch.randn(V, D, device="cuda") * 0.05
+    lab = torch.randint(0, V, (N,), device="cuda")
+    lab[::5] = -100
+    Vl = V // world
+    hl = h.clone().requires_grad_(True)
+    wl = w[rank * Vl:(rank + 1) * Vl].clone().requires_grad_(True)
+    loss = vocab_parallel_cross_entropy(hl, wl, lab, rank * Vl, mesh, "tp", -100, 512)
+    loss.backward()
+    gh = hl.grad.float().clone()
+    dist.all_reduce(gh)  # the TP entry collective sums the ranks' grad_hidden shares
+    hr = h.clone().requires_grad_(True)
+    wr = w.clone().requires_grad_(True)
+    ref = fused_linear_cross_entropy(hr, wr, lab, -100, 512)
+    ref.backward()
+    bad = []
+    if abs(loss.item() - ref.item()) > 1e-3 * ref.item():
+        bad.append(("loss", loss.item(), ref.item()))
+    rh = ((gh - hr.grad.float()).norm() / hr.grad.float().norm()).item()
+    rw = ((wl.grad - wr.grad[rank * Vl:(rank + 1) * Vl]).norm() / wr.grad.norm()).item()
+    if rh > 2e-2 or rw > 2e-2:
+        bad.append(("grads", rh, rw))
+    assert not bad, bad
+
+
+def test_vocab_parallel_ce_matches_single_gpu():
+    _need(2)
+    run_ranks(_vocab_ce_case, 2, backend="nccl")
+
+
 def _tp_model_case(rank, world):
     from pluggy_b200.core.mesh import Mesh
     from pluggy_b200.models.qwen3 import Qwen3
