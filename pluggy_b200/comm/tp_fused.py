@@ -108,16 +108,17 @@ class TPComm:
                          status_word(x.device))
         return out.view(B, S, W), rstd
 
-    def gemm_reduce_scatter(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-        """``(x [B, S, K] @ w [N, K]^T)`` summed over the axis, sequence-sharded:
-        [B, S / n, N]. One tcgen05 GEMM whose epilogue stores into the owners'
-        staging slots, then the finishing kernel."""
+    def gemm_reduce_scatter(self, x: torch.Tensor, w: torch.Tensor, w_mn_major: bool = False) -> torch.Tensor:
+        """``(x [B, S, K] @ w [N, K]^T)`` (or ``x @ w`` with ``w`` [K, N] when
+        ``w_mn_major``) summed over the axis, sequence-sharded: [B, S / n, N]. One
+        tcgen05 GEMM whose epilogue stores into the owners' staging slots, then the
+        finishing kernel."""
         B, S, K = x.shape
-        N = w.shape[0]
+        N = w.shape[1] if w_mn_major else w.shape[0]
         x2 = x.reshape(B * S, K).to(torch.bfloat16).contiguous()
         flags, bufs, e, cap = self._args(_RS, B * S * N * 2)
         st = status_word(x.device)
-        ext().gemm_rs(x2, w, False, bufs, self.rank, S, cap, st)
+        ext().gemm_rs(x2, w, w_mn_major, bufs, self.rank, S, cap, st)
         out = torch.empty((B * (S // self.n), N), dtype=torch.bfloat16, device=x.device)
         ext().tp_collective("rs_finish", out, flags, bufs, self.rank, e, B, S, cap, st)
         return out.view(B, S // self.n, N)

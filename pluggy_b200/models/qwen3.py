@@ -65,6 +65,27 @@ class Qwen3TransformerBlock(nn.Module):
                                          f.down_proj.weight, (w_gu, w_d), norm_eps(self.norm2), SILU)
 
 
+    def fused_forward_tp(self, x, cache: WeightCache, cfg: _engine.AttnCfg, inv_freq, idx: int, comm):
+        """Tensor/sequence-parallel form of :meth:`fused_forward`: ``x`` is this rank's
+        sequence shard [B*S/tp, D] fp32; the weights are this rank's head/column shards."""
+        from pluggy_b200.parallel.tp_engine import TPAttnSublayer, TPMlpSublayer
+
+        g = self.attention
+        w_qkv = cache.get_cat([g.q_proj.weight, g.k_proj.weight, g.v_proj.weight], f"b{idx}.qkv")
+        w_o = cache.get(g.o_proj.weight)
+        qn = g.q_norm.weight if g.qk_norm else None
+        kn = g.k_norm.weight if g.qk_norm else None
+        x = TPAttnSublayer.apply(x, self.norm1.weight, g.q_proj.weight, g.k_proj.weight,
+                                 g.v_proj.weight, g.o_proj.weight, qn, kn, (w_qkv, w_o), cfg, inv_freq,
+                                 comm)
+        f = self.ffn
+        w_gu = cache.get_cat([f.gate_proj.weight, f.up_proj.weight], f"b{idx}.gu")
+        w_d = cache.get(f.down_proj.weight)
+        return TPMlpSublayer.apply(x, self.norm2.weight, f.gate_proj.weight, f.up_proj.weight,
+                                   f.down_proj.weight, (w_gu, w_d), norm_eps(self.norm2), SILU,
+                                   cfg.B, cfg.S, comm)
+
+
 class Qwen3(nn.Module):
     # the forward calls ``_plg_param_gate.enter`` (ZeRO-1 DDP: wait for each block's
     # parameter all-gather just before the block)
@@ -104,6 +125,34 @@ class Qwen3(nn.Module):
                 and self.token_emb.weight.dtype == torch.float32
                 and self.head_dim in (64, 128) and self.emb_dim % 128 == 0)
 
+    def _use_fused_tp(self, x, attention_mask, return_hidden_states) -> bool:
+        """Tensor parallelism with sequence parallelism on the peer-memory collectives,
+        with the pre-norms fused into the gathers: the blocks run as TP sublayers."""
+        tp = getattr(self, "tp", None)
+        if not (x.is_cuda and attention_mask is None and not return_hidden_states and tp is not None
+                and tp.comm is not None and tp.sp and getattr(self, "cp", None) is None
+                and self.head_dim in (64, 128) and self.emb_dim % 128 == 0
+                and x.shape[1] % tp.comm.n == 0):
+            return False
+        from pluggy_b200.comm.tp_fused import TPNormGather
+
+        return all(isinstance(b.norm1, TPNormGather) and isinstance(b.norm2, TPNormGather)
+                   and hasattr(b, "fused_forward_tp") for b in self.blocks)
+
+    def fused_hidden_tp(self, x: torch.Tensor) -> torch.Tensor:
+        """Packed causal forward under TP + SP on the sm_100a kernels; returns this
+        rank's sequence shard of the final hidden, bf16 [B, S/tp, D]."""
+        B, S = x.shape
+        comm = self.tp.comm
+        h = self.token_emb(x)  # vocabulary-parallel lookup, reduce-scattered along the sequence
+        D = h.shape[-1]
+        h = h.reshape(-1, D).float().contiguous()
+        inv = self.rope.inv_freq
+        for i, blk in enumerate(self.blocks):
+            h = blk.fused_forward_tp(h, self.weight_cache, self._attn_cfg(B, S, blk), inv, i, comm)
+        out = _engine.FinalNorm.apply(h, self.norm.weight, norm_eps(self.norm))
+        return out.view(B, S // comm.n, D)
+
     def _attn_cfg(self, B, S, block) -> _engine.AttnCfg:
         g = block.attention
         return _engine.AttnCfg(B=B, S=S, Hq=g.num_heads, Hk=g.num_kv_heads, d=g.head_dim,
@@ -137,6 +186,9 @@ class Qwen3(nn.Module):
                 return_final_hidden: bool = False, position_ids=None):
         """``position_ids`` (optional [B, S]) overrides the packed arange positions
         (context parallelism feeds each rank's zigzag positions)."""
+        if (position_ids is None and return_final_hidden
+                and self._use_fused_tp(x, attention_mask, return_hidden_states)):
+            return self.fused_hidden_tp(x)
         if position_ids is None and self._use_fused(x, attention_mask, return_hidden_states):
             hidden = self.fused_hidden(x)
             if return_final_hidden:

@@ -273,6 +273,11 @@ def _tp_model_case(rank, world):
         torch.manual_seed(0)
         m = Qwen3(**cfg).cuda()
         m.init_weights()
+        # the TP engine runs the per-head q/k norms in bf16 (eps = bf16 eps, as the
+        # reference under autocast): give the eager NCCL path the same eps
+        for mod in m.modules():
+            if isinstance(mod, torch.nn.RMSNorm) and mod.normalized_shape[0] == cfg["head_dim"]:
+                mod.eps = torch.finfo(torch.bfloat16).eps
         tp = parallelize_tp(m, mesh, "tp", sequence_parallel=True, fused=fused)
         loss = ARObjective(ce_chunk_size=512).compute_loss(m, {"input_ids": ids, "labels": ids})
         loss.backward()
