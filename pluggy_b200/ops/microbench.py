@@ -224,12 +224,95 @@ def case_embedding(a, small):
     return fn, {"bytes": T * D * 8, "shape": {"T": T, "D": D, "V": V}}
 
 
+def case_embedding_bwd(a, small):
+    """Deterministic (sorted) embedding backward with Zipf(1.1)-distributed ids."""
+    from pluggy_b200.ops._ext import ext
+
+    T, D, V = _tokens(a, small), a.dim, a.vocab
+    r = torch.arange(1, V + 1, device="cuda", dtype=torch.float64)
+    p = r.pow(-1.1)
+    ids = torch.multinomial((p / p.sum()).float(), T, replacement=True)
+    dout = torch.randn(T, D, device="cuda")
+    dw = torch.zeros(V, D, device="cuda")
+
+    def fn():
+        s, pos = torch.sort(ids, stable=True)
+        ext().embedding_bwd_sorted(s, pos, dout, dw, 1.0)
+    # algorithmic bytes: dout read once, the touched rows of dw read and written
+    touched = int(torch.unique(ids).numel())
+    return fn, {"bytes": T * D * 4 + touched * D * 8, "shape": {"T": T, "D": D, "unique_ids": touched}}
+
+
+def case_grouped_gemm(a, small):
+    """One MoE expert projection over all experts (grouped tcgen05 GEMM, mode 1):
+    T tokens x top-k rows routed uniformly over E experts, [E, N, K] weights."""
+    from pluggy_b200.ops._ext import ext
+    from pluggy_b200.ops.grouped import expert_layout
+
+    E, topk, K, N = a.experts, a.topk, a.dim, a.n
+    P = (2048 if small else 8192) * topk
+    ex = torch.randint(0, E, (P,), device="cuda").sort().values
+    counts = torch.bincount(ex, minlength=E)
+    poff, shift, tg, R = expert_layout(counts, P)
+    x = torch.zeros(R, K, device="cuda", dtype=torch.bfloat16)
+    x[torch.arange(P, device="cuda") + shift[ex]] = _bf16(P, K)
+    w = _bf16(E * N, K)
+    out = torch.empty(R, N, device="cuda", dtype=torch.bfloat16)
+    if a.layout == "tn":  # weight gradient (mode 2): dW_e = dy_e^T x_e
+        dy = _bf16(R, N)
+        dw = torch.empty(E * N, K, device="cuda", dtype=torch.float32)
+        fn = lambda: ext().gemm_grouped(dy, x, True, dw, 2, poff, E, 0, 1.0, 0.0)  # noqa: E731
+    else:
+        fn = lambda: ext().gemm_grouped(x, w, False, out, 1, tg, E, N, 1.0, 0.0)  # noqa: E731
+    return fn, {"flops": 2 * P * N * K, "shape": {"rows": P, "padded_rows": int(poff[-1]),
+                                                   "E": E, "N": N, "K": K, "layout": a.layout}}
+
+
+def case_zero1(a, small):
+    """ZeRO-1 reduce-scatter and AdamW+all-gather kernels on one rank (no peers: the
+    local memory side of the kernels; NVLink rates come from the multi-GPU runs)."""
+    from pluggy_b200.comm.symm import SymmetricBuffer
+    from pluggy_b200.core.mesh import Mesh
+    from pluggy_b200.ops._ext import ext, status_word
+
+    import torch.distributed as dist
+
+    if not dist.is_initialized():
+        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:29533", rank=0, world_size=1)
+    mesh = Mesh({"dp": 1})
+    n = (64 if small else 256) << 20
+    g = SymmetricBuffer(n * 4, mesh, "dp")
+    pa = SymmetricBuffer(n * 4, mesh, "dp")
+    fl = SymmetricBuffer(3 * 8 * 128 * 4, mesh, "dp")
+    sl = SymmetricBuffer(8 * 128 * 4, mesh, "dp")
+    g.tensor(0, [n]).normal_()
+    pa.tensor(0, [n]).normal_()
+    m, v = torch.zeros(n, device="cuda"), torch.zeros(n, device="cuda")
+    rows = torch.tensor([[0, n, 0]], dtype=torch.int64, device="cuda")
+    norm = torch.zeros(1, device="cuda")
+    ep = [0, 0]
+    st = status_word()
+
+    def rs():
+        ep[0] += 1
+        ext().zero1_rs(g.peers, pa.peers, fl.peers, sl.peers, 0, n, 0, ep[0], 128, norm, False, st)
+
+    def ag():
+        ep[1] += 1
+        ext().zero1_adamw_ag(g.peers, pa.peers, fl.peers, sl.peers, 0, n, 0, ep[1], 128, [1e-4], [0.1],
+                             0.9, 0.95, 1e-8, 0.9, 0.95, None, rows, m, v, st)
+    fn = ag if a.layout == "tn" else rs
+    nbytes = n * (4 + 4) if fn is rs else n * (4 * 4 + 3 * 4)
+    return fn, {"bytes": nbytes, "shape": {"elements": n, "kernel": "adamw_ag" if fn is ag else "rs"}}
+
+
 CASES = {
     "gemm": case_gemm, "attn_fwd": case_attn_fwd, "attn_bwd": case_attn_bwd,
     "qk_rope_fwd": case_qk_rope_fwd, "qk_rope_bwd": case_qk_rope_bwd,
     "rmsnorm_fwd": case_rmsnorm_fwd, "rmsnorm_bwd": case_rmsnorm_bwd,
     "glu_fwd": case_glu_fwd, "glu_bwd": case_glu_bwd,
     "ce_rows": case_ce_rows, "adamw": case_adamw, "sumsq": case_sumsq, "embedding": case_embedding,
+    "embedding_bwd": case_embedding_bwd, "grouped_gemm": case_grouped_gemm, "zero1": case_zero1,
 }
 
 
@@ -269,6 +352,8 @@ def main(argv=None) -> None:
     p.add_argument("--n", type=int, default=4096)
     p.add_argument("--k", type=int, default=1024)
     p.add_argument("--layout", default="nt", choices=["nt", "nn", "tn"])
+    p.add_argument("--experts", type=int, default=128)
+    p.add_argument("--topk", type=int, default=8)
     a = p.parse_args(argv)
     if not torch.cuda.is_available():
         raise SystemExit("microbench needs a CUDA device")

@@ -11,7 +11,12 @@ plan implemented here (``notes/ROADMAP.md:380-407`` of the reference):
 * backward: a second ring in the same direction carries each key/value block
   together with its dK/dV accumulator; every rank adds its contribution using
   the final output and log-sum-exp, and the accumulator arrives back at the
-  block's owner after ``n`` hops.
+  block's owner after ``n`` hops;
+* overlap: every hop is issued asynchronously before the step's blocks compute
+  (forward: the next K/V; backward: the next K/V, and the accumulated dK/dV that
+  the neighbour sent at the end of its step is waited for only after this
+  step's contribution has been computed into a fresh buffer), so the transfers
+  run under the attention kernels instead of between them.
 
 A (query chunk, key chunk) pair is skipped when the key chunk lies after the
 query chunk, computed with a causal mask when it is the same chunk, and computed
@@ -132,6 +137,10 @@ class _RingAttention(torch.autograd.Function):
         for step in range(n):
             src = (r - step) % n
             k_ids = (src, 2 * n - 1 - src)
+            # the next hop's K/V are in flight while this step's blocks compute
+            work = None
+            if step + 1 < n:
+                kv_next, work = ring_send_recv(kv, mesh, dim, async_op=True)
             kb, vb = kv[0], kv[1]
             for a in range(2):
                 for b in range(2):
@@ -144,8 +153,9 @@ class _RingAttention(torch.autograd.Function):
                         o[a], lse[a] = ob, lb
                     else:
                         o[a], lse[a] = _merge(o[a], lse[a], ob, lb)
-            if step + 1 < n:
-                kv = ring_send_recv(kv, mesh, dim)
+            if work is not None:
+                work.wait()
+                kv = kv_next
         out = torch.cat(o, dim=1)
         lse_all = torch.cat(lse, dim=2)
         ctx.save_for_backward(q, k, v, out, lse_all)
@@ -161,10 +171,16 @@ class _RingAttention(torch.autograd.Function):
         q_ids = (r, 2 * n - 1 - r)
         dq = torch.zeros(q.shape, dtype=torch.float32, device=q.device)
         kv = torch.stack([k, v])
-        dkv = torch.zeros(kv.shape, dtype=torch.float32, device=q.device)
+        dkv_in, dkv_work = None, None
         for step in range(n):
             src = (r - step) % n
             k_ids = (src, 2 * n - 1 - src)
+            # prefetch the next hop's K/V while this step computes
+            kv_work = None
+            if step + 1 < n:
+                kv_next, kv_work = ring_send_recv(kv, mesh, dim, async_op=True)
+            # this step's contribution to the travelling block's dK/dV, in a fresh buffer
+            part = torch.zeros(kv.shape, dtype=torch.float32, device=q.device)
             for a in range(2):
                 qs = slice(a * c, (a + 1) * c)
                 for b in range(2):
@@ -175,11 +191,21 @@ class _RingAttention(torch.autograd.Function):
                     g_q, g_k, g_v = _block_bwd(q[:, qs], kv[0][:, ks], kv[1][:, ks], out[:, qs],
                                                lse[:, :, qs], do[:, qs], rel == 1, scale)
                     dq[:, qs] += g_q
-                    dkv[0][:, ks] += g_k
-                    dkv[1][:, ks] += g_v
-            # the block and its accumulator move on together; after n hops both are home
-            kv = ring_send_recv(kv, mesh, dim)
-            dkv = ring_send_recv(dkv, mesh, dim)
+                    part[0][:, ks] += g_k
+                    part[1][:, ks] += g_v
+            # the block's accumulated dK/dV from the ranks that saw it before (sent at the
+            # end of their previous step, so the transfer overlapped this step's compute)
+            if dkv_work is not None:
+                dkv_work.wait()
+                part += dkv_in
+            # accumulator and block move on together; after n hops both are home
+            dkv_in, dkv_work = ring_send_recv(part, mesh, dim, async_op=True)
+            if kv_work is not None:
+                kv_work.wait()
+                kv = kv_next
+        if dkv_work is not None:
+            dkv_work.wait()
+        dkv = dkv_in
         return dq.to(q.dtype), dkv[0].to(k.dtype), dkv[1].to(v.dtype), None, None, None
 
 
