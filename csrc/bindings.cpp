@@ -707,6 +707,20 @@ void fsdp_push_b(const at::Tensor& shard, const at::Tensor& table, std::vector<i
                  shard.numel() * shard.element_size() / 16, shard.data_ptr(), cur_stream());
 }
 
+void fsdp_push_lowp_b(const at::Tensor& shard, const at::Tensor& table, int64_t total16,
+                      std::vector<int64_t> flags, std::vector<int64_t> bufs, int64_t rank, int64_t epoch,
+                      int64_t cap_bytes, const c10::optional<at::Tensor>& status) {
+  check_cuda(shard, "shard");
+  check_cuda(table, "table");
+  TORCH_CHECK(is_f32(shard) && shard.is_contiguous(), "fsdp_push_lowp: contiguous fp32 shard");
+  TORCH_CHECK(table.scalar_type() == at::kLong && table.dim() == 2 && table.size(1) == 5 &&
+                  table.is_contiguous(), "fsdp_push_lowp: int64 table [k, 5]");
+  const c10::cuda::CUDAGuard guard(shard.device());
+  auto a = tp_args(flags, bufs, rank, epoch, 1, static_cast<int64_t>(flags.size()), 8, cap_bytes, status);
+  plg::fsdp_push_lowp(a, table.data_ptr<int64_t>(), static_cast<int>(table.size(0)), total16,
+                      shard.data_ptr<float>(), cur_stream());
+}
+
 void tp_norm_ag(const at::Tensor& x, const c10::optional<at::Tensor>& w, at::Tensor& rstd,
                 at::Tensor& out, std::vector<int64_t> flags, std::vector<int64_t> bufs, int64_t rank,
                 int64_t epoch, int64_t B, int64_t S, double eps, int64_t cap_bytes,
@@ -764,6 +778,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("rank"), py::arg("S"), py::arg("cap_bytes"), py::arg("status") = py::none());
   m.def("fsdp_push", &fsdp_push_b, py::arg("shard"), py::arg("table"), py::arg("flags"),
         py::arg("bufs"), py::arg("rank"), py::arg("epoch"), py::arg("cap_bytes"),
+        py::arg("status") = py::none());
+  m.def("fsdp_push_lowp", &fsdp_push_lowp_b, py::arg("shard"), py::arg("table"), py::arg("total16"),
+        py::arg("flags"), py::arg("bufs"), py::arg("rank"), py::arg("epoch"), py::arg("cap_bytes"),
         py::arg("status") = py::none());
   m.def("ep_exchange", &ep_exchange, py::arg("op"), py::arg("t"), py::arg("flags"), py::arg("bufs"),
         py::arg("rank"), py::arg("epoch"), py::arg("kind"), py::arg("src_start"), py::arg("count"),

@@ -562,6 +562,41 @@ __global__ void __launch_bounds__(256) ep_finish_kernel(TpArgs a, int kind, __nv
 }
 
 // ------------------------------------------------------------------ FSDP gather
+// Low-precision unit gather: every rank pushes its fp32 parameter shards into every
+// rank's slot of the unit, matrices cast to bf16 on the way (half the NVLink bytes),
+// vectors kept fp32. table [k][5] int64: first 16-byte destination group of the row
+// (running sum), source offset in the fp32 shard (elements), destination offset of
+// the parameter in the slot (16-byte units), this rank's shard length (16-byte
+// destination units), kind (0: bf16, 1: fp32). The rank's shard of parameter i lands
+// at dst_off16_i + rank * len16_i.
+__global__ void __launch_bounds__(256) fsdp_push_lowp_kernel(TpArgs a, const int64_t* __restrict__ table,
+                                                             int k, long long total16,
+                                                             const float* __restrict__ shard) {
+  for (long long g = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; g < total16;
+       g += static_cast<long long>(gridDim.x) * blockDim.x) {
+    int i = 0;
+    while (i + 1 < k && table[5 * (i + 1)] <= g) ++i;
+    const int64_t* r = table + 5 * i;
+    const long long local = g - r[0];
+    uint4 v;
+    if (r[4] == 0) {
+      const float4* src = reinterpret_cast<const float4*>(shard + r[1] + local * 8);
+      const float4 x0 = src[0], x1 = src[1];
+      v = make_uint4(pack_bf16x2(x0.x, x0.y), pack_bf16x2(x0.z, x0.w), pack_bf16x2(x1.x, x1.y),
+                     pack_bf16x2(x1.z, x1.w));
+    } else {
+      v = *reinterpret_cast<const uint4*>(shard + r[1] + local * 4);
+    }
+    const long long dst = r[2] + a.rank * r[3] + local;
+    for (int p = 0; p < a.n; ++p) {
+      int q = a.rank + p;
+      q = q >= a.n ? q - a.n : q;
+      peer_store16(a, q, dst, v);
+    }
+  }
+  __threadfence_system();
+}
+
 __global__ void __launch_bounds__(256) fsdp_push_kernel(TpArgs a, const int64_t* __restrict__ table, int k,
                                                         long long total16, const uint4* __restrict__ shard) {
   for (long long g = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; g < total16;
@@ -735,6 +770,19 @@ void ep_finish(const TpArgs& a, int kind, void* out, long long rows, long long l
   // always launched, also with no rows to copy: the handshake keeps the ranks in step
   comm::ep_finish_kernel<<<tp_grid(rows * (a.W / 8), 148 * 4), 256, 0, st>>>(
       a, kind, reinterpret_cast<__nv_bfloat16*>(out), rows, ld_out);
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+void fsdp_push_lowp(const TpArgs& a, const int64_t* table, int k, long long total16, const float* shard,
+                    cudaStream_t st) {
+  if (a.n < 1 || a.n > kSymmMaxRanks || a.rank < 0 || a.rank >= a.n || k < 1 ||
+      (reinterpret_cast<uintptr_t>(shard) & 15))
+    throw std::invalid_argument("fsdp_push_lowp: 1..8 ranks, a parameter table, 16-byte aligned shard");
+  for (int p = 0; p < a.n; ++p)
+    if (a.bufs[p] == nullptr || (reinterpret_cast<uintptr_t>(a.bufs[p]) & 15))
+      throw std::invalid_argument("fsdp_push_lowp: every rank's 16-byte aligned slot");
+  if (total16 <= 0) return;
+  comm::fsdp_push_lowp_kernel<<<tp_grid(total16, 148 * 4), 256, 0, st>>>(a, table, k, total16, shard);
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 

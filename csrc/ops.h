@@ -268,6 +268,10 @@ void ep_finish(const TpArgs& a, int kind, void* out, long long rows, long long l
 // shard offset in this rank's flat shard, offset of the parameter in the unit's full
 // layout, shard length. This rank's shard of parameter i goes to every rank's buffer
 // at full_off_i + rank * shard_len_i. Finish with ep_finish (rows of 8 2-byte units).
+// Low-precision form: fp32 shard in, matrices stored as bf16 (vectors as fp32) straight
+// into every rank's slot; table [k][5] (see comm.cu). Finish with ep_finish (0 rows).
+void fsdp_push_lowp(const TpArgs& a, const int64_t* table, int k, long long total16, const float* shard,
+                    cudaStream_t stream);
 void fsdp_push(const TpArgs& a, const int64_t* table, int k, long long total16, const void* shard,
                cudaStream_t stream);
 void symm_allreduce_avg(const SymmAllReduceArgs& a, float* norm_sq, bool accumulate_norm,

@@ -1,5 +1,17 @@
 """FSDP parameter all-gather over NVLink peer memory.
 
+Two forms:
+
+* :class:`PeerGather` (fp32): the unit's full fp32 parameters, for models that
+  read their parameters directly;
+* :class:`SlotGather` (low precision): for the fused-engine models, whose GEMMs
+  read bf16 weights. Each rank casts its fp32 shards to bf16 while pushing them
+  (half the NVLink bytes) straight into the consumer's buffer, a slot of
+  symmetric memory that the GEMMs read in place (no finishing copy, no separate
+  cast, no full-size fp32 copy of the unit); 1-D parameters (norm weights) travel
+  as fp32. Two slots, alternating by block index, hold the unit being computed
+  and the one being prefetched.
+
 A unit's full parameters are one flat buffer (parameter i at ``full_off_i``, its
 dim-0 shard of rank r at ``full_off_i + r * shard_len_i``). :meth:`PeerGather.gather`
 launches one push kernel (``csrc/comm.cu``: every rank stores each of its parameter
@@ -53,6 +65,83 @@ class PeerGather:
         n = self.n
         ext().ep_exchange("finish", out, self.flags.peers, bufs, self.rank, e, _KIND, [0] * n, [0] * n,
                           [0] * n, out.shape[0], self.half, st)
+
+    def close(self) -> None:
+        self.buf.close()
+        self.flags.close()
+
+
+def _align16(nbytes: int) -> int:
+    return (nbytes + 15) // 16 * 16
+
+
+class SlotLayout:
+    """Where each parameter of a unit lives in its slot: matrices first (bf16, in
+    block order, so q|k|v and gate|up stay contiguous), then vectors (fp32)."""
+
+    def __init__(self, states, n: int):
+        self.entries = []  # (state, kind, byte offset)
+        off = 0
+        mats = [s for s in states if len(s.full_shape) >= 2]
+        vecs = [s for s in states if len(s.full_shape) < 2]
+        for s in mats:
+            self.entries.append((s, 0, off))
+            off = _align16(off + 2 * s.full_numel)
+        for s in vecs:
+            self.entries.append((s, 1, off))
+            off = _align16(off + 4 * s.full_numel)
+        self.nbytes = off
+        # every rank's shard must be whole 16-byte groups at 16-byte offsets
+        self.ok = all((s.shard_numel * (2 if k == 0 else 4)) % 16 == 0 for s, k, _ in self.entries)
+
+    def table(self, shard_order, device) -> tuple[torch.Tensor, int]:
+        """The push kernel's rows; ``shard_order``: the states in the order of the
+        unit's flat fp32 shard (the source offsets)."""
+        rows, g, src = [], 0, 0
+        src_off = {}
+        for s in shard_order:
+            src_off[id(s)] = src
+            src += s.shard_numel
+        for s, kind, off in self.entries:
+            esize = 2 if kind == 0 else 4
+            len16 = s.shard_numel * esize // 16
+            rows.append([g, src_off[id(s)], off // 16, len16, kind])
+            g += len16
+        return torch.tensor(rows, dtype=torch.int64, device=device), g
+
+
+class SlotGather:
+    def __init__(self, mesh, dim: str, slot_bytes: int, nslots: int = 2):
+        self.mesh, self.dim = mesh, dim
+        self.n, self.rank = mesh.size(dim), mesh.coordinate(dim)
+        self.slot = (int(slot_bytes) + 4095) // 4096 * 4096
+        self.nslots = nslots
+        self.flags = SymmetricBuffer(_FLAG_BYTES, mesh, dim)
+        self.buf = SymmetricBuffer(nslots * self.slot, mesh, dim)
+        self.epoch = 0
+
+    def views(self, layout: SlotLayout, slot: int) -> dict:
+        """id(param) -> the parameter's full tensor inside slot ``slot`` (bf16 or fp32)."""
+        out = {}
+        base = slot * self.slot
+        for s, kind, off in layout.entries:
+            dt = torch.bfloat16 if kind == 0 else torch.float32
+            out[id(s.param)] = self.buf.tensor(base + off, list(s.full_shape), dt)
+        return out
+
+    def gather(self, unit, slot: int) -> None:
+        """Fill slot ``slot`` of every rank from every rank's ``unit.flat_shard``."""
+        self.epoch += 1
+        e = self.epoch
+        bufs = [p + slot * self.slot for p in self.buf.peers]
+        st = status_word(unit.flat_shard.device)
+        ext().fsdp_push_lowp(unit.flat_shard, unit.slot_table, unit.slot_groups, self.flags.peers, bufs,
+                             self.rank, e, self.slot, st)
+        n = self.n
+        empty = torch.empty((0, 8), dtype=torch.int16, device=unit.flat_shard.device)
+        # handshake only: the pushes already landed in place
+        ext().ep_exchange("finish", empty, self.flags.peers, bufs, self.rank, e, _KIND, [0] * n,
+                          [0] * n, [0] * n, 0, self.slot, st)
 
     def close(self) -> None:
         self.buf.close()

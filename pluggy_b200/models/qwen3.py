@@ -90,6 +90,9 @@ class Qwen3(nn.Module):
     # the forward calls ``_plg_param_gate.enter`` (ZeRO-1 DDP: wait for each block's
     # parameter all-gather just before the block)
     param_gate_aware = True
+    # the CUDA path reads every matrix weight as bf16 through ``weight_cache`` (FSDP2
+    # can then gather them in low precision straight into the GEMMs' buffers)
+    fused_engine = True
     rope_base = 1_000_000
     tie_default = True
     block_cls = Qwen3TransformerBlock
@@ -197,6 +200,10 @@ class Qwen3(nn.Module):
         gate = getattr(self, "_plg_param_gate", None)
         if gate is not None:
             gate.enter("all")
+        fs = getattr(self, "_plg_fsdp", None)
+        if fs is not None and getattr(fs, "_slots", None) is not None and x.is_cuda:
+            raise RuntimeError("FSDP2 low-precision gathers serve the fused packed path only; build "
+                               "FSDP2(..., lowp_gather=False) for masked or hidden-state forwards")
         pos, cacheable, am = position_ids_for(x, attention_mask)
         if position_ids is not None:
             pos, cacheable = position_ids, False

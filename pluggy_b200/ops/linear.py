@@ -36,6 +36,9 @@ class WeightCache:
         # set by FSDP2: a gather rewrites the full parameter's storage without moving
         # its version counter, so every get() recasts (into the same bf16 buffer)
         self.always_recast = False
+        # set by FSDP2's low-precision gathers: ``provider(params)`` returns the bf16
+        # weights already gathered in place (or None), read instead of a cached copy
+        self.provider = None
 
     def bind_optimizer(self, opt) -> None:
         if self._opt is opt:
@@ -69,6 +72,10 @@ class WeightCache:
                 self._store[key] = (tuple((p._version, p.data_ptr()) for p in ps), None, hit[2])
 
     def get(self, p: torch.Tensor) -> torch.Tensor:
+        if self.provider is not None:
+            v = self.provider([p])
+            if v is not None:
+                return v
         key = id(p)
         ver = p._version
         hit = self._store.get(key)
@@ -90,6 +97,10 @@ class WeightCache:
 
     def get_cat(self, params: list[torch.Tensor], key: str) -> torch.Tensor:
         """bf16 concatenation (dim 0) of several params, cached as one buffer."""
+        if self.provider is not None:
+            v = self.provider(list(params))
+            if v is not None:
+                return v
         vers = tuple((p._version, p.data_ptr()) for p in params)
         hit = self._store.get(key)
         if hit is not None and hit[0] == vers and not self.always_recast:

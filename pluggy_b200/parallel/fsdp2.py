@@ -28,7 +28,15 @@ B200 differences (same observable contract):
   one peer-memory push (every rank stores its shards into every rank's staging
   buffer over NVLink, :mod:`pluggy_b200.comm.fsdp_fused`) plus one finishing copy,
   instead of an NCCL all-gather (``gather="nccl"`` keeps NCCL). Gradient
-  reduce-scatters stay on NCCL.
+  reduce-scatters stay on NCCL;
+* for the fused-engine models (their GEMMs read bf16 weights through the weight
+  cache) the block units are gathered in low precision: each rank casts its shards
+  to bf16 while pushing them into a slot of symmetric memory that the GEMMs then
+  read in place (half the bytes, no finishing copy, no cast pass, and no
+  full-size copy of the unit kept anywhere: during a block only the slot and the
+  gradients hold full-size data). Norm weights travel as fp32. While a block unit is
+  in use its matrix parameters are zero-byte placeholders of the full shape, so
+  autograd accumulates full-shape gradients for the reduce-scatter.
 """
 
 from __future__ import annotations
@@ -106,7 +114,7 @@ class _Unit:
 
 class FSDP2:
     def __init__(self, model: nn.Module, mesh: MeshLike, dim: str = "dp", *, prefetch: bool = True,
-                 gather: str = "auto"):
+                 gather: str = "auto", lowp_gather: bool = True):
         self.mesh = mesh
         self.dim = dim
         self.group_size = mesh.size(dim)
@@ -145,6 +153,28 @@ class FSDP2:
             from pluggy_b200.comm.fsdp_fused import PeerGather
 
             self._peer = PeerGather(mesh, dim, max(u.full_nbytes for u in self._units))
+        # low-precision slot gathers for the block units of fused-engine models
+        self._slots = None
+        self._slot_views: dict[int, torch.Tensor] = {}
+        for u in self._units:
+            u.slot = None
+        if (self._peer is not None and lowp_gather and getattr(type(model), "fused_engine", False)
+                and hasattr(model, "weight_cache")):
+            from pluggy_b200.comm.fsdp_fused import SlotGather, SlotLayout
+
+            layouts = [SlotLayout(u.params, n) for u in self._block_units]
+            if layouts and all(lay.ok for lay in layouts):
+                self._slots = SlotGather(mesh, dim, max(lay.nbytes for lay in layouts))
+                for i, (u, lay) in enumerate(zip(self._block_units, layouts, strict=True)):
+                    u.slot = i % 2
+                    u.slot_table, u.slot_groups = lay.table(u.params, dev)
+                    views = self._slots.views(lay, u.slot)
+                    u.slot_views = views
+                    self._slot_views.update(views)
+                    # zero-byte stand-ins of the full shape (the GEMMs read the slot)
+                    u.placeholders = {id(st.param): torch.empty(1, dtype=st.param.dtype, device=dev)
+                                      .expand(st.full_shape) for st in u.params if len(st.full_shape) >= 2}
+                model.weight_cache.provider = self._lowp_view
         # the models' fused CUDA path runs blocks through ``fused_forward`` (not the
         # module call, so the module hooks do not fire): it calls these instead
         model._plg_fsdp = self
@@ -173,9 +203,34 @@ class FSDP2:
             return dist._coalescing_manager(group=group, device=unit.flat_shard.device)
         return contextlib.nullcontext()
 
+    def _lowp_view(self, params) -> torch.Tensor | None:
+        """The weight cache's source of bf16 weights: the slot views of block-unit
+        matrices (one view over consecutive parameters for a concatenation), else None."""
+        views = [self._slot_views.get(id(p)) for p in params]
+        if not views or any(v is None or v.dtype != torch.bfloat16 for v in views):
+            return None
+        if len(views) == 1:
+            return views[0]
+        for a, b in zip(views, views[1:]):
+            if b.data_ptr() != a.data_ptr() + a.numel() * 2 or b.shape[1:] != a.shape[1:]:
+                return None
+        from pluggy_b200.ops._ext import ext
+
+        rows = sum(v.shape[0] for v in views)
+        return ext().tensor_from_ptr(views[0].data_ptr(), [rows, *views[0].shape[1:]], torch.bfloat16,
+                                     views[0].device.index)
+
     def _issue_gather(self, unit: _Unit) -> None:
         """Launch the coalesced all-gather of ``unit`` (on the comm stream on CUDA)."""
         if unit.gathered:
+            return
+        if unit.slot is not None:
+            self._comm_stream.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(self._comm_stream):
+                self._slots.gather(unit, unit.slot)
+                unit.gather_event = torch.cuda.Event()
+                unit.gather_event.record(self._comm_stream)
+            unit.gathered = True
             return
         unit.alloc_full()
         ctx = torch.cuda.stream(self._comm_stream) if self._cuda else contextlib.nullcontext()
@@ -199,6 +254,11 @@ class FSDP2:
         if unit.gather_event is not None:
             torch.cuda.current_stream().wait_event(unit.gather_event)
             unit.gather_event = None
+        if unit.slot is not None:
+            for s in unit.params:
+                ph = unit.placeholders.get(id(s.param))
+                s.param.data = ph if ph is not None else unit.slot_views[id(s.param)]
+            return
         for s in unit.params:
             s.param.data = s.full
 
@@ -314,6 +374,10 @@ class FSDP2:
             torch.cuda.synchronize()
             self._peer.close()
             self._peer = None
+        if getattr(self, "_slots", None) is not None:
+            torch.cuda.synchronize()
+            self._slots.close()
+            self._slots = None
 
     # ------------------------------------------------------------- inspection
     @property
