@@ -105,7 +105,10 @@ void rmsnorm_fwd_t(const void* x, const float* w, void* y, float* rstd, long lon
 
 // ------------------------------------------------------------------ RMSNorm bwd
 // dx = rstd * (w*dy - xh * mean(w*dy*xh)) (+ dres),  xh = x * rstd
-// dw_partial[block, :] = sum over the block's rows of dy * xh
+// dw_partial[block, :] = sum over the block's rows of dy * xh, in a fixed order:
+// each warp owns a slice of shared memory ([warps][D], lane-owned columns, rows
+// in the warp's order) and the slices are summed warp by warp at the end, so the
+// partials are bitwise reproducible (no atomics)
 template <typename TDY, typename TX, int NV>
 // 128 threads and at most 128 registers: the caller's DW_BLOCKS (4 per SM) must all
 // be resident at once, or the grid-strided rows run in several waves
@@ -113,12 +116,13 @@ __global__ void __launch_bounds__(128, 4) rmsnorm_bwd_kernel(
     const TDY* __restrict__ dy, const TX* __restrict__ x, const float* __restrict__ w,
     const float* __restrict__ rstd, const float* __restrict__ dres, float* __restrict__ dx_f32,
     __nv_bfloat16* __restrict__ dx_bf16, float* __restrict__ dw_partial, long long rows, int D) {
-  extern __shared__ float s_dw[];  // [D]
+  extern __shared__ float s_dw_all[];  // [warps][D]
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int nwarps = blockDim.x >> 5;
+  float* s_dw = s_dw_all + warp * D;  // this warp's slice
   if (dw_partial)
-    for (int i = threadIdx.x; i < D; i += blockDim.x) s_dw[i] = 0.f;
+    for (int i = threadIdx.x; i < nwarps * D; i += blockDim.x) s_dw_all[i] = 0.f;
   __syncthreads();
   // small D: dw accumulates in registers (lane-owned channels) and is reduced
   // across warps once; large D: straight into shared memory
@@ -162,7 +166,7 @@ __global__ void __launch_bounds__(128, 4) rmsnorm_bwd_kernel(
         const float xh = xvs[j][i] * r;
         dot += dvs_j[i] * wv[i] * xh;
         if constexpr (kRegDw) dw_acc[j][i] += dvs_j[i] * xh;
-        else if (dw_partial) atomicAdd(&s_dw[c + i], dvs_j[i] * xh);
+        else if (dw_partial) s_dw[c + i] += dvs_j[i] * xh;  // lane-owned column of this warp
       }
     }
     dot = warp_sum(dot) / D;
@@ -191,11 +195,14 @@ __global__ void __launch_bounds__(128, 4) rmsnorm_bwd_kernel(
 #pragma unroll
       for (int j = 0; j < NV; ++j)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) atomicAdd(&s_dw[j * 128 + lane * 4 + i], dw_acc[j][i]);
+        for (int i = 0; i < 4; ++i) s_dw[j * 128 + lane * 4 + i] = dw_acc[j][i];
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < D; i += blockDim.x)
-      dw_partial[(long long)blockIdx.x * D + i] = s_dw[i];
+    for (int i = threadIdx.x; i < D; i += blockDim.x) {
+      float t = 0.f;
+      for (int w2 = 0; w2 < nwarps; ++w2) t += s_dw_all[w2 * D + i];
+      dw_partial[(long long)blockIdx.x * D + i] = t;
+    }
   }
 }
 
@@ -205,9 +212,13 @@ void rmsnorm_bwd_t(const void* dy, const void* x, const float* w, const float* r
                    int dw_blocks, long long rows, int D, cudaStream_t st) {
   const int threads = 128;
   const int nv = D / 128;
-  const size_t sm = dw_partial ? D * sizeof(float) : 0;
+  const size_t sm = dw_partial ? (threads / 32) * D * sizeof(float) : 0;
 #define PLG_RMSB_CASE(NV)                                                                      \
   case NV:                                                                                     \
+    if (sm > 48 * 1024)                                                                        \
+      PLG_CUDA_CHECK(cudaFuncSetAttribute(rmsnorm_bwd_kernel<TDY, TX, NV>,                     \
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,         \
+                                          static_cast<int>(sm)));                              \
     rmsnorm_bwd_kernel<TDY, TX, NV><<<dw_blocks, threads, sm, st>>>(                           \
         reinterpret_cast<const TDY*>(dy), reinterpret_cast<const TX*>(x), w, rstd, dres,       \
         dx_f32, reinterpret_cast<__nv_bfloat16*>(dx_bf16), dw_partial, rows, D);               \

@@ -13,6 +13,7 @@ CPU tensors use the same math through SDPA (the test oracle).
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 import torch.nn.functional as F
@@ -51,6 +52,25 @@ def attn_fwd(q, k, v, *, causal=True, window=0, scale=None):
     return o, lse
 
 
+def _attn_bwd_d64_padded(q, k, v, o, lse, do, causal, window, scale, dq, dk, dv):
+    """head_dim 64 through the head_dim-128 backward kernel: q, k, v, o and dO are
+    zero-padded to 128 channels (the padded channels add 0 to every score and to
+    rowsum(dO * O), so lse and the softmax are unchanged) and the gradients' first 64
+    channels are the result. The 128-wide kernel (double-buffered S/dP in TMEM,
+    dedicated dQ drain warps) pays for the doubled work with its higher tensor-core
+    utilisation (``PLG_ATTN_D64_PAD=0`` selects the 64-wide kernel)."""
+    pad = [F.pad(t, (0, 64)) for t in (q, k, v, o, do)]
+    dq_p, dk_p, dv_p = attn_bwd(*pad[:4], lse, pad[4], causal=causal, window=window, scale=scale)
+    outs = []
+    for g, out in ((dq_p, dq), (dk_p, dk), (dv_p, dv)):
+        if out is None:
+            outs.append(g[..., :64].contiguous())
+        else:
+            out.copy_(g[..., :64])
+            outs.append(out)
+    return tuple(outs)
+
+
 def attn_bwd(q, k, v, o, lse, do, *, causal=True, window=0, scale=None, dq=None, dk=None, dv=None,
              trace=None):
     """Backward of flash attention. ``trace`` (int64 [10, 256] on the device,
@@ -58,6 +78,8 @@ def attn_bwd(q, k, v, o, lse, do, *, causal=True, window=0, scale=None, dq=None,
     per step, for timeline analysis of the kernel."""
     B, S, Hq, d = q.shape
     scale = 1.0 / math.sqrt(d) if scale is None else scale
+    if d == 64 and trace is None and os.environ.get("PLG_ATTN_D64_PAD", "1") != "0":
+        return _attn_bwd_d64_padded(q, k, v, o, lse, do, causal, window, scale, dq, dk, dv)
     dq = torch.empty_like(q, memory_format=torch.contiguous_format) if dq is None else dq
     dk = torch.empty(k.shape, dtype=k.dtype, device=k.device) if dk is None else dk
     dv = torch.empty(v.shape, dtype=v.dtype, device=v.device) if dv is None else dv
