@@ -347,9 +347,12 @@ void embedding_bwd_sorted(const at::Tensor& ids_sorted, const at::Tensor& pos_so
                   dout.dim() == 2 && dw.dim() == 2 && dout.size(1) == dw.size(1),
               "embedding_bwd_sorted: fp32 dout [T, D] and dw [V, D]");
   const c10::cuda::CUDAGuard guard(dout.device());
+  // partial sums of long runs (rows touched only for ids with more than 64 tokens)
+  at::Tensor scratch = at::empty_like(dout);
   plg::embedding_bwd_sorted(ids_sorted.data_ptr<int64_t>(), pos_sorted.data_ptr<int64_t>(),
-                            dout.data_ptr<float>(), dw.data_ptr<float>(), dout.size(0),
-                            static_cast<int>(dout.size(1)), static_cast<float>(scale), cur_stream());
+                            dout.data_ptr<float>(), dw.data_ptr<float>(), scratch.data_ptr<float>(),
+                            dout.size(0), static_cast<int>(dout.size(1)), static_cast<float>(scale),
+                            cur_stream());
 }
 
 void multi_sumsq(const at::Tensor& table, int64_t ntensors, int64_t total_chunks, at::Tensor& out) {

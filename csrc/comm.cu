@@ -191,7 +191,7 @@ __device__ __forceinline__ void zero1_chunk(const Zero1Args& a, long long& c0, l
   c1 = min(s1, c0 + per);
 }
 
-__global__ void __launch_bounds__(512) zero1_rs_kernel(Zero1Args a) {
+__global__ void __launch_bounds__(1024) zero1_rs_kernel(Zero1Args a) {
   const int n = a.nranks, me = a.rank, c = blockIdx.x;
   const bool ok = zero1_handshake(a, 0);
   float ss = 0.f;
@@ -221,7 +221,7 @@ __global__ void __launch_bounds__(512) zero1_rs_kernel(Zero1Args a) {
     }
   }
   ss = warp_sum(ss);
-  __shared__ float s_red[16];
+  __shared__ float s_red[32];
   if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = ss;
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -241,7 +241,7 @@ __device__ __forceinline__ int zero1_group(const int64_t* rows, int nrows, long 
   return static_cast<int>(rows[3 * r + 2]);
 }
 
-__global__ void __launch_bounds__(512) zero1_adamw_ag_kernel(Zero1Args a, Zero1Adam h) {
+__global__ void __launch_bounds__(1024) zero1_adamw_ag_kernel(Zero1Args a, Zero1Adam h) {
   const int n = a.nranks, me = a.rank;
   long long c0, c1, s0;
   zero1_chunk(a, c0, c1, s0);
@@ -673,7 +673,7 @@ static void zero1_check(const Zero1Args& a, const char* what) {
 void zero1_reduce_scatter(const Zero1Args& a, float* norm_sq, bool accumulate, cudaStream_t st) {
   zero1_check(a, "zero1_reduce_scatter");
   // launched also for an empty bucket: the handshakes keep the ranks' epochs in step
-  comm::zero1_rs_kernel<<<a.chunks, 512, 0, st>>>(a);
+  comm::zero1_rs_kernel<<<a.chunks, 1024, 0, st>>>(a);
   PLG_CUDA_CHECK(cudaGetLastError());
   if (norm_sq != nullptr) {
     comm::sumsq_total_kernel<<<1, 256, 0, st>>>(a.sumsq[a.rank], a.nranks, a.chunks, norm_sq,
@@ -687,7 +687,7 @@ void zero1_adamw_allgather(const Zero1Args& a, const Zero1Adam& h, cudaStream_t 
   if (h.nrows < 1 || h.rows == nullptr || h.exp_avg == nullptr || h.exp_avg_sq == nullptr ||
       (reinterpret_cast<uintptr_t>(h.exp_avg) & 15) || (reinterpret_cast<uintptr_t>(h.exp_avg_sq) & 15))
     throw std::invalid_argument("zero1_adamw_allgather: a row table and 16-byte aligned slice state");
-  comm::zero1_adamw_ag_kernel<<<a.chunks, 512, 0, st>>>(a, h);
+  comm::zero1_adamw_ag_kernel<<<a.chunks, 1024, 0, st>>>(a, h);
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -104,9 +104,11 @@ void embedding_fwd(const int64_t* ids, const float* w, float* out_f32, long long
 void embedding_bwd(const int64_t* ids, const float* dout, float* dw, long long T, int D,
                    float scale, cudaStream_t stream);
 // deterministic form: ids sorted ascending (stable) with their token positions;
-// dw[id] += scale * sum of dout rows of that id, summed in token order, no atomics
+// dw[id] += scale * sum of dout rows of that id, summed in token order, no atomics;
+// scratch: fp32 [T, D] (rows written only for ids with more than 64 tokens)
 void embedding_bwd_sorted(const int64_t* ids_sorted, const int64_t* pos_sorted, const float* dout,
-                          float* dw, long long T, int D, float scale, cudaStream_t stream);
+                          float* dw, float* scratch, long long T, int D, float scale,
+                          cudaStream_t stream);
 // y = cap * tanh(x / cap)
 void softcap_fwd(const void* x, void* y, long long n, float cap, bool bf16, cudaStream_t stream);
 

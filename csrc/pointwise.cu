@@ -165,34 +165,82 @@ __global__ void embedding_bwd_kernel(const int64_t* __restrict__ ids,
   }
 }
 
-// Deterministic embedding backward over ids sorted ascending (stable): the CTA of
-// the first sorted position of each id sums that id's dout rows in sorted order
-// (= token order) and adds the sum into dw[id]. Every id has exactly one owner
-// CTA, so there are no atomics and the result does not depend on scheduling.
-__global__ void __launch_bounds__(256) embedding_bwd_sorted_kernel(
+// Deterministic embedding backward over ids sorted ascending (stable). The sorted
+// positions are cut into pieces: a piece starts at the first position of an id's run
+// and at every multiple of kEmbPiece, so a frequent id (Zipf: one id can own 10% of
+// the tokens) is spread over many CTAs. Pass 1: the CTA of each piece sums the
+// piece's dout rows in sorted (= token) order; a run that is one piece adds its sum
+// into dw[id] directly, a longer run's pieces are written to a scratch row at the
+// piece's first position. Pass 2: the CTA at the start of each multi-piece run adds
+// its pieces in order into dw[id]. Every id has exactly one writer and every sum has
+// a fixed order: no atomics, bitwise reproducible.
+constexpr int kEmbPiece = 64;
+
+__device__ __forceinline__ long long emb_run_end(const int64_t* ids, long long i, long long T,
+                                                 long long limit) {
+  // first position > i with a different id, scanning at most up to `limit`
+  __shared__ long long s_end;
+  if (threadIdx.x == 0) s_end = limit;
+  __syncthreads();
+  const int64_t id = ids[i];
+  for (long long base = i + 1; base < limit; base += blockDim.x) {
+    const long long j = base + threadIdx.x;
+    const bool stop = j < limit && ids[j] != id;
+    if (stop) atomicMin(reinterpret_cast<unsigned long long*>(&s_end), static_cast<unsigned long long>(j));
+    if (__syncthreads_or(stop || base + blockDim.x >= limit)) break;
+  }
+  const long long e = s_end;
+  __syncthreads();
+  return e;
+}
+
+__global__ void __launch_bounds__(256) embedding_bwd_pieces_kernel(
     const int64_t* __restrict__ ids_sorted, const int64_t* __restrict__ pos_sorted,
-    const float* __restrict__ dout, float* __restrict__ dw, long long T, int D, float scale) {
+    const float* __restrict__ dout, float* __restrict__ dw, float* __restrict__ scratch, long long T,
+    int D, float scale) {
   const long long i = blockIdx.x;
   if (i >= T) return;
   const int64_t id = ids_sorted[i];
-  if (i > 0 && ids_sorted[i - 1] == id) return;  // not the first position of the run
-  // run end: scan forward blockDim positions at a time
-  __shared__ long long s_end;
-  if (threadIdx.x == 0) s_end = T;
-  __syncthreads();
-  for (long long base = i + 1; base < T; base += blockDim.x) {
-    const long long j = base + threadIdx.x;
-    const bool stop = j < T && ids_sorted[j] != id;
-    if (stop) atomicMin(reinterpret_cast<unsigned long long*>(&s_end), static_cast<unsigned long long>(j));
-    if (__syncthreads_or(stop || base + blockDim.x >= T)) break;
-  }
-  const long long end = s_end;
-  float* dst = dw + id * (long long)D;
+  const bool run_start = i == 0 || ids_sorted[i - 1] != id;
+  if (!run_start && i % kEmbPiece != 0) return;  // not the first position of a piece
+  const long long window_end = min(T, (i / kEmbPiece + 1) * kEmbPiece);
+  const long long end = emb_run_end(ids_sorted, i, T, window_end);
+  // a single-piece run starts here and ends before the window does (or at T)
+  const bool whole = run_start && (end < window_end || end == T ||
+                                   ids_sorted[window_end] != id);
+  float* dst = whole ? dw + id * (long long)D : scratch + i * (long long)D;
   for (int c = threadIdx.x * 4; c < D; c += blockDim.x * 4) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4
     for (long long j = i; j < end; ++j) {
       const float4 v = *reinterpret_cast<const float4*>(dout + pos_sorted[j] * D + c);
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    if (whole) {
+      float4 d = *reinterpret_cast<float4*>(dst + c);
+      d.x += acc.x * scale; d.y += acc.y * scale; d.z += acc.z * scale; d.w += acc.w * scale;
+      *reinterpret_cast<float4*>(dst + c) = d;
+    } else {
+      *reinterpret_cast<float4*>(dst + c) = acc;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) embedding_bwd_combine_kernel(
+    const int64_t* __restrict__ ids_sorted, const float* __restrict__ scratch, float* __restrict__ dw,
+    long long T, int D, float scale) {
+  const long long i = blockIdx.x;
+  if (i >= T) return;
+  const int64_t id = ids_sorted[i];
+  if (i > 0 && ids_sorted[i - 1] == id) return;  // not a run start
+  const long long window_end = min(T, (i / kEmbPiece + 1) * kEmbPiece);
+  if (window_end >= T || ids_sorted[window_end] != id) return;  // single-piece run: done in pass 1
+  const long long end = emb_run_end(ids_sorted, window_end - 1, T, T);
+  float* dst = dw + id * (long long)D;
+  for (int c = threadIdx.x * 4; c < D; c += blockDim.x * 4) {
+    float4 acc = *reinterpret_cast<const float4*>(scratch + i * (long long)D + c);  // first piece
+    for (long long p = window_end; p < end; p += kEmbPiece) {
+      const float4 v = *reinterpret_cast<const float4*>(scratch + p * (long long)D + c);
       acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
     }
     float4 d = *reinterpret_cast<float4*>(dst + c);
@@ -599,11 +647,13 @@ void embedding_bwd(const int64_t* ids, const float* dout, float* dw, long long T
 }
 
 void embedding_bwd_sorted(const int64_t* ids_sorted, const int64_t* pos_sorted, const float* dout,
-                          float* dw, long long T, int D, float scale, cudaStream_t st) {
+                          float* dw, float* scratch, long long T, int D, float scale, cudaStream_t st) {
   if (T <= 0) return;
-  if (D % 4 || (reinterpret_cast<uintptr_t>(dout) & 15) || (reinterpret_cast<uintptr_t>(dw) & 15))
+  if (D % 4 || (reinterpret_cast<uintptr_t>(dout) & 15) || (reinterpret_cast<uintptr_t>(dw) & 15) ||
+      (reinterpret_cast<uintptr_t>(scratch) & 15))
     throw std::invalid_argument("embedding_bwd_sorted: D a multiple of 4, 16-byte aligned rows");
-  embedding_bwd_sorted_kernel<<<T, 256, 0, st>>>(ids_sorted, pos_sorted, dout, dw, T, D, scale);
+  embedding_bwd_pieces_kernel<<<T, 256, 0, st>>>(ids_sorted, pos_sorted, dout, dw, scratch, T, D, scale);
+  embedding_bwd_combine_kernel<<<T, 256, 0, st>>>(ids_sorted, scratch, dw, T, D, scale);
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 
