@@ -336,6 +336,16 @@ void ce_rows(at::Tensor& logits, const at::Tensor& labels, int64_t ignore_index,
                lse_in.has_value() ? lse_in->data_ptr<float>() : nullptr, label_offset);
 }
 
+void exp2_poly_eval_b(const at::Tensor& x, at::Tensor& poly, at::Tensor& ref) {
+  check_cuda(x, "x");
+  TORCH_CHECK(is_f32(x) && is_f32(poly) && is_f32(ref) && x.is_contiguous() && poly.is_contiguous() &&
+                  ref.is_contiguous() && poly.numel() == x.numel() && ref.numel() == x.numel(),
+              "exp2_poly_eval: fp32 contiguous tensors of one size");
+  const c10::cuda::CUDAGuard guard(x.device());
+  plg::exp2_poly_eval(x.data_ptr<float>(), poly.data_ptr<float>(), ref.data_ptr<float>(), x.numel(),
+                      cur_stream());
+}
+
 void embedding_bwd_sorted(const at::Tensor& ids_sorted, const at::Tensor& pos_sorted,
                           const at::Tensor& dout, at::Tensor& dw, double scale) {
   check_cuda(dout, "dout");
@@ -811,6 +821,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("n_valid"), py::arg("row_loss") = py::none(), py::arg("stats") = py::none(),
         py::arg("lse_in") = py::none(), py::arg("label_offset") = 0);
   m.def("embedding_bwd_sorted", &embedding_bwd_sorted);
+  m.def("exp2_poly_eval", &exp2_poly_eval_b);
   m.def("multi_sumsq", &multi_sumsq);
   m.def("multi_scale", &multi_scale);
   m.def("adamw_multi", &adamw_multi);

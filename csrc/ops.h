@@ -109,6 +109,8 @@ void embedding_bwd(const int64_t* ids, const float* dout, float* dw, long long T
 void embedding_bwd_sorted(const int64_t* ids_sorted, const int64_t* pos_sorted, const float* dout,
                           float* dw, float* scratch, long long T, int D, float scale,
                           cudaStream_t stream);
+// poly[i] = 2^x[i] by the attention kernels' FMA-pipe cubic, ref[i] = exp2f(x[i])
+void exp2_poly_eval(const float* x, float* poly, float* ref, long long n, cudaStream_t stream);
 // y = cap * tanh(x / cap)
 void softcap_fwd(const void* x, void* y, long long n, float cap, bool bf16, cudaStream_t stream);
 

@@ -569,6 +569,23 @@ __global__ void __launch_bounds__(512) adamw_kernel(const int64_t* __restrict__ 
   }
 }
 
+// 2^x by the FMA-pipe cubic the attention kernels use for part of their softmax
+// (exp2_poly2) and by CUDA's exp2f, side by side, for the error-bound test.
+__global__ void exp2_poly_eval_kernel(const float* __restrict__ x, float* __restrict__ poly,
+                                      float* __restrict__ ref, long long n) {
+  const long long i = 2 * (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x);
+  if (i >= n) return;
+  const float x0 = x[i], x1 = i + 1 < n ? x[i + 1] : 0.f;
+  float p0, p1;
+  exp2_poly2(x0, x1, p0, p1);
+  poly[i] = p0;
+  ref[i] = exp2f(x0);
+  if (i + 1 < n) {
+    poly[i + 1] = p1;
+    ref[i + 1] = exp2f(x1);
+  }
+}
+
 int grid_for(long long work, int per_block) {
   long long b = (work + per_block - 1) / per_block;
   if (b > 148 * 16) b = 148 * 16;
@@ -654,6 +671,13 @@ void embedding_bwd_sorted(const int64_t* ids_sorted, const int64_t* pos_sorted, 
     throw std::invalid_argument("embedding_bwd_sorted: D a multiple of 4, 16-byte aligned rows");
   embedding_bwd_pieces_kernel<<<T, 256, 0, st>>>(ids_sorted, pos_sorted, dout, dw, scratch, T, D, scale);
   embedding_bwd_combine_kernel<<<T, 256, 0, st>>>(ids_sorted, scratch, dw, T, D, scale);
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+void exp2_poly_eval(const float* x, float* poly, float* ref, long long n, cudaStream_t st) {
+  if (n <= 0) return;
+  const long long pairs = (n + 1) / 2;
+  exp2_poly_eval_kernel<<<static_cast<unsigned>((pairs + 255) / 256), 256, 0, st>>>(x, poly, ref, n);
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -393,6 +393,63 @@ def test_attention_fwd_bwd(B, S, Hq, Hk, d, causal, window):
     assert rel(v.grad, vr.grad) < 3e-2, rel(v.grad, vr.grad)
 
 
+def test_exp2_poly_error_bound():
+    """The FMA-pipe 2^x (a cubic on [-1/2, 1/2] after range reduction) that the attention
+    forward uses for part of its softmax stays within 1e-4 relative error of CUDA's exp2f
+    over the softmax argument range [-126, 0]."""
+    from pluggy_b200.ops._ext import ext
+
+    x = torch.cat([torch.linspace(-126.0, 0.0, 1 << 20, device=DEV),
+                   torch.rand(1 << 20, device=DEV) * -20.0,
+                   torch.arange(-126, 1, device=DEV, dtype=torch.float32)])
+    poly, ref = torch.empty_like(x), torch.empty_like(x)
+    ext().exp2_poly_eval(x, poly, ref)
+    rel = ((poly - ref).abs() / ref).max().item()
+    assert rel < 1e-4, rel
+    # integers (f = 0 after range reduction): off by the cubic's constant term only
+    assert ((poly[-127:] - ref[-127:]).abs() / ref[-127:]).max().item() < 1e-4
+
+
+@pytest.mark.parametrize("causal", [True])
+def test_attention_benchmark_shape_against_fp32(causal):
+    """The benchmark's attention shape (S = 4096, 16 q / 8 kv heads, d = 128), B = 2:
+    forward output and all three gradients against fp32 math computed head by head."""
+    from pluggy_b200.ops.attention import flash_attention
+
+    torch.manual_seed(5)
+    B, S, Hq, Hk, d = 2, 4096, 16, 8, 128
+    q = torch.randn(B, S, Hq, d, device=DEV).bfloat16().requires_grad_()
+    k = torch.randn(B, S, Hk, d, device=DEV).bfloat16().requires_grad_()
+    v = torch.randn(B, S, Hk, d, device=DEV).bfloat16().requires_grad_()
+    o = flash_attention(q, k, v, causal=causal)
+    do = torch.randn_like(o)
+    o.backward(do)
+    scale = 1.0 / math.sqrt(d)
+    mask = torch.ones(S, S, device=DEV, dtype=torch.bool).tril()
+    errs = {"o": [0.0, 0.0], "dq": [0.0, 0.0], "dk": [0.0, 0.0], "dv": [0.0, 0.0]}
+    dk_ref = torch.zeros(B, S, Hk, d, device=DEV)
+    dv_ref = torch.zeros(B, S, Hk, d, device=DEV)
+    for b in range(B):
+        for h in range(Hq):
+            hk = h // (Hq // Hk)
+            qf = q[b, :, h].detach().float().requires_grad_()
+            kf = k[b, :, hk].detach().float().requires_grad_()
+            vf = v[b, :, hk].detach().float().requires_grad_()
+            s_ = (qf @ kf.t()) * scale
+            p_ = torch.softmax(s_.masked_fill(~mask, float("-inf")), -1)
+            of = p_ @ vf
+            of.backward(do[b, :, h].float())
+            for name, got, want in (("o", o[b, :, h].float(), of.detach()), ("dq", q.grad[b, :, h].float(), qf.grad)):
+                errs[name][0] += (got - want).pow(2).sum().item()
+                errs[name][1] += want.pow(2).sum().item()
+            dk_ref[b, :, hk] += kf.grad
+            dv_ref[b, :, hk] += vf.grad
+    for name, got, want in (("dk", k.grad.float(), dk_ref), ("dv", v.grad.float(), dv_ref)):
+        errs[name] = [(got - want).pow(2).sum().item(), want.pow(2).sum().item()]
+    for name, (num, den) in errs.items():
+        assert math.sqrt(num / den) < 2e-2, (name, math.sqrt(num / den))
+
+
 def test_attention_lse():
     from pluggy_b200.ops.attention import attn_fwd
 
