@@ -385,7 +385,7 @@ def run_reference(args, rank, local_rank, world, device) -> dict:
     e2e_ms = timed_loop(e2e_step, max(1, args.steps // 2), 1, device)
     tokens = micro * seq * world
     return {"value": tokens / (ms / 1e3), "ms_per_step": ms, "clocks": clk.summary(),
-            "ref_parallelism": f"{bc['ref']}{world}", "tokens_per_step": tokens,
+            "ref_parallelism": f"{bc['ref']}-dp{world}", "tokens_per_step": tokens,
             "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": micro * seq * 8 * 2, "d2h_bytes_per_step": 4,
                     "api": "pluggy.train.trainer.Trainer.train_step"},
