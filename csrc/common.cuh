@@ -102,7 +102,8 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 // x = j + f with j = rint(x) (adding 1.5 * 2^23 rounds to an integer held in the
 // low mantissa bits) and f in [-0.5, 0.5]; 2^f is a cubic fitted here to minimise
 // the relative error on that interval (iteratively reweighted least squares on
-// Chebyshev nodes, max relative error 7.5e-5, below bf16's 2^-9 rounding); the
+// Chebyshev nodes; max relative error against exp2f 1.44e-4 over [-126, 0], measured
+// by the GPU test, an order of magnitude below bf16's 2^-9 rounding); the
 // exponent j is added to the result's exponent field. x is clamped to >= -126 so
 // that field never underflows: inputs below that return ~2^-126 instead of 0, so
 // callers use it only where no element is masked to -inf.
