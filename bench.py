@@ -96,6 +96,9 @@ def train_config(n_gpus: int, reducer: str = "nccl", name: str = "ddp06b") -> di
         "seed": 0,
         "run_name": "bench",
     }
+    if bc["parallel"] == "fsdp2":
+        # FSDP2 gradient reduce-scatter: NCCL (default) or the peer-memory kernel
+        cfg["fsdp2"] = {"reduce": os.environ.get("PLG_FSDP_REDUCE", "nccl")}
     if bc["parallel"] == "ep":
         cfg["ep"] = {"dim": "dp"}
     if bc["parallel"] == "tp" and lay["tp"] > 1:

@@ -734,6 +734,36 @@ void fsdp_push_lowp_b(const at::Tensor& shard, const at::Tensor& table, int64_t 
                       shard.data_ptr<float>(), cur_stream());
 }
 
+void fsdp_rs_b(std::vector<int64_t> stage, std::vector<int64_t> flags, const at::Tensor& table,
+               at::Tensor& out, bool accumulate, double scale, int64_t rank, int64_t epoch, int64_t chunks,
+               const c10::optional<at::Tensor>& status) {
+  check_cuda(out, "out");
+  check_cuda(table, "table");
+  TORCH_CHECK(is_f32(out) && out.is_contiguous(), "fsdp_rs: contiguous fp32 shard accumulator");
+  TORCH_CHECK(table.scalar_type() == at::kLong && table.dim() == 2 && table.size(1) == 3 &&
+                  table.is_contiguous(), "fsdp_rs: int64 table [k, 3]");
+  const int n = static_cast<int>(stage.size());
+  TORCH_CHECK(n >= 1 && n <= plg::kSymmMaxRanks && flags.size() == stage.size(), "fsdp_rs: one slot per rank");
+  const c10::cuda::CUDAGuard guard(out.device());
+  plg::FsdpRsArgs a;
+  for (int i = 0; i < n; ++i) {
+    a.stage[i] = reinterpret_cast<float*>(stage[i]);
+    a.flags[i] = reinterpret_cast<uint32_t*>(flags[i]);
+  }
+  a.table = table.data_ptr<int64_t>();
+  a.k = static_cast<int>(table.size(0));
+  a.shard_numel = out.numel();
+  a.out = out.data_ptr<float>();
+  a.accumulate = accumulate ? 1 : 0;
+  a.scale = static_cast<float>(scale);
+  a.rank = static_cast<int>(rank);
+  a.nranks = n;
+  a.chunks = static_cast<int>(chunks);
+  a.epoch = static_cast<uint32_t>(epoch);
+  a.status = status.has_value() ? status->data_ptr<int>() : nullptr;
+  plg::fsdp_reduce_scatter(a, cur_stream());
+}
+
 void tp_norm_ag(const at::Tensor& x, const c10::optional<at::Tensor>& w, at::Tensor& rstd,
                 at::Tensor& out, std::vector<int64_t> flags, std::vector<int64_t> bufs, int64_t rank,
                 int64_t epoch, int64_t B, int64_t S, double eps, int64_t cap_bytes,
@@ -791,6 +821,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("rank"), py::arg("S"), py::arg("cap_bytes"), py::arg("status") = py::none());
   m.def("fsdp_push", &fsdp_push_b, py::arg("shard"), py::arg("table"), py::arg("flags"),
         py::arg("bufs"), py::arg("rank"), py::arg("epoch"), py::arg("cap_bytes"),
+        py::arg("status") = py::none());
+  m.def("fsdp_rs", &fsdp_rs_b, py::arg("stage"), py::arg("flags"), py::arg("table"), py::arg("out"),
+        py::arg("accumulate"), py::arg("scale"), py::arg("rank"), py::arg("epoch"), py::arg("chunks"),
         py::arg("status") = py::none());
   m.def("fsdp_push_lowp", &fsdp_push_lowp_b, py::arg("shard"), py::arg("table"), py::arg("total16"),
         py::arg("flags"), py::arg("bufs"), py::arg("rank"), py::arg("epoch"), py::arg("cap_bytes"),

@@ -562,6 +562,51 @@ __global__ void __launch_bounds__(256) ep_finish_kernel(TpArgs a, int kind, __nv
 }
 
 // ------------------------------------------------------------------ FSDP gather
+// FSDP gradient reduce-scatter (see ops.h): CTA c reduces chunk c of the rank's flat
+// shard after a ready handshake with CTA c of every peer, then signals done (peers
+// may refill their staging slot) and waits for the peers' done.
+__device__ bool fsdp_rs_handshake(const FsdpRsArgs& a, int kind) {
+  __shared__ int s_ok;
+  const int c = blockIdx.x;
+  if (threadIdx.x < a.nranks)
+    st_release_sys(a.flags[threadIdx.x] + (kind * kSymmMaxRanks + a.rank) * kSymmMaxChunks + c, a.epoch);
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    for (int p = 0; p < a.nranks && ok; ++p)
+      ok = wait_flag(a.flags[a.rank] + (kind * kSymmMaxRanks + p) * kSymmMaxChunks + c, a.epoch);
+    if (!ok) record_status(a.status, kTimeoutPeerFlag);
+    s_ok = ok;
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
+__global__ void __launch_bounds__(1024) fsdp_rs_kernel(FsdpRsArgs a) {
+  if (fsdp_rs_handshake(a, 0)) {
+    const long long per = ((a.shard_numel + a.chunks - 1) / a.chunks + 3) & ~3LL;
+    const long long c0 = min(a.shard_numel, blockIdx.x * per), c1 = min(a.shard_numel, c0 + per);
+    int r = 0;
+    for (long long s4 = c0 + 4LL * threadIdx.x; s4 < c1; s4 += 4LL * blockDim.x) {
+      while (r + 1 < a.k && a.table[3 * (r + 1)] <= s4) ++r;
+      const int64_t* row = a.table + 3 * r;
+      const long long full = row[1] + a.rank * row[2] + (s4 - row[0]);  // 4-aligned: one row
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+      for (int p = 0; p < a.nranks; ++p) {  // fixed rank order: deterministic
+        const float4 v = *reinterpret_cast<const float4*>(a.stage[p] + full);
+        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+      }
+      float4* o = reinterpret_cast<float4*>(a.out + s4);
+      float4 prev = a.accumulate ? *o : make_float4(0.f, 0.f, 0.f, 0.f);
+      prev.x += acc.x * a.scale; prev.y += acc.y * a.scale;
+      prev.z += acc.z * a.scale; prev.w += acc.w * a.scale;
+      *o = prev;
+    }
+  }
+  __syncthreads();
+  fsdp_rs_handshake(a, 1);
+}
+
 // Low-precision unit gather: every rank pushes its fp32 parameter shards into every
 // rank's slot of the unit, matrices cast to bf16 on the way (half the NVLink bytes),
 // vectors kept fp32. table [k][5] int64: first 16-byte destination group of the row
@@ -770,6 +815,20 @@ void ep_finish(const TpArgs& a, int kind, void* out, long long rows, long long l
   // always launched, also with no rows to copy: the handshake keeps the ranks in step
   comm::ep_finish_kernel<<<tp_grid(rows * (a.W / 8), 148 * 4), 256, 0, st>>>(
       a, kind, reinterpret_cast<__nv_bfloat16*>(out), rows, ld_out);
+  PLG_CUDA_CHECK(cudaGetLastError());
+}
+
+void fsdp_reduce_scatter(const FsdpRsArgs& a, cudaStream_t st) {
+  if (a.nranks < 1 || a.nranks > kSymmMaxRanks || a.rank < 0 || a.rank >= a.nranks)
+    throw std::invalid_argument("fsdp_reduce_scatter: 1..8 ranks");
+  if (a.chunks < 1 || a.chunks > kSymmMaxChunks || a.k < 1 || a.table == nullptr || a.out == nullptr ||
+      a.shard_numel % 4 || (reinterpret_cast<uintptr_t>(a.out) & 15))
+    throw std::invalid_argument("fsdp_reduce_scatter: chunks in 1..128, a table, a 16-byte aligned "
+                                "shard of whole float4 groups");
+  for (int p = 0; p < a.nranks; ++p)
+    if (a.stage[p] == nullptr || a.flags[p] == nullptr || (reinterpret_cast<uintptr_t>(a.stage[p]) & 15))
+      throw std::invalid_argument("fsdp_reduce_scatter: every rank's 16-byte aligned staging and flags");
+  comm::fsdp_rs_kernel<<<a.chunks, 1024, 0, st>>>(a);
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 

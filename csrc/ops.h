@@ -272,6 +272,26 @@ void ep_finish(const TpArgs& a, int kind, void* out, long long rows, long long l
 // shard offset in this rank's flat shard, offset of the parameter in the unit's full
 // layout, shard length. This rank's shard of parameter i goes to every rank's buffer
 // at full_off_i + rank * shard_len_i. Finish with ep_finish (rows of 8 2-byte units).
+// FSDP gradient reduce-scatter over peer memory: every rank holds its full unit
+// gradient (fp32, the unit's full layout) in a staging slot; rank r sums its shard
+// of every parameter over the ranks' slots (fixed rank order), scales by `scale` and
+// writes (accumulate ? += : =) into its flat fp32 grad-shard accumulator.
+// table [k][3] int64 (elements): offset in the flat shard, offset of the parameter in
+// the full layout, shard length. Offsets and lengths must be multiples of 4.
+struct FsdpRsArgs {
+  float* stage[kSymmMaxRanks] = {};
+  uint32_t* flags[kSymmMaxRanks] = {};  // [2 kinds][kSymmMaxRanks][kSymmMaxChunks]
+  const int64_t* table = nullptr;
+  int k = 0;
+  long long shard_numel = 0;
+  float* out = nullptr;
+  int accumulate = 0;
+  float scale = 1.f;
+  int rank = 0, nranks = 1, chunks = 1;
+  uint32_t epoch = 0;
+  int* status = nullptr;
+};
+void fsdp_reduce_scatter(const FsdpRsArgs& a, cudaStream_t stream);
 // Low-precision form: fp32 shard in, matrices stored as bf16 (vectors as fp32) straight
 // into every rank's slot; table [k][5] (see comm.cu). Finish with ep_finish (0 rows).
 void fsdp_push_lowp(const TpArgs& a, const int64_t* table, int k, long long total16, const float* shard,

@@ -146,3 +146,51 @@ class SlotGather:
     def close(self) -> None:
         self.buf.close()
         self.flags.close()
+
+
+_RS_FLAG_BYTES = 2 * 8 * 128 * 4
+
+
+class PeerReduceScatter:
+    """FSDP gradient reduce-scatter over peer memory (``csrc/comm.cu`` ``fsdp_rs_kernel``).
+
+    Each rank copies a unit's full fp32 gradients into a staging slot of symmetric
+    memory (two slots alternating by call); one kernel then sums this rank's shard of
+    every parameter over all ranks' slots with peer loads, in rank order, scales by
+    1/N and writes or accumulates it straight into the rank's flat fp32 grad-shard
+    buffer: no NCCL output tensors, no separate accumulate pass."""
+
+    def __init__(self, mesh, dim: str, max_unit_bytes: int, chunks: int = 128):
+        self.mesh, self.dim = mesh, dim
+        self.n, self.rank = mesh.size(dim), mesh.coordinate(dim)
+        self.slot = (int(max_unit_bytes) + 4095) // 4096 * 4096
+        self.flags = SymmetricBuffer(_RS_FLAG_BYTES, mesh, dim)
+        self.buf = SymmetricBuffer(2 * self.slot, mesh, dim)
+        self.chunks = chunks
+        self.epoch = 0
+
+    @staticmethod
+    def plan(states, device):
+        """(table, full offsets) for the states that take gradients, in unit order."""
+        rows, so, fo, offs = [], 0, 0, []
+        for s in states:
+            rows.append([so, fo, s.shard_numel])
+            offs.append(fo)
+            so += s.shard_numel
+            fo += s.full_numel
+        return torch.tensor(rows, dtype=torch.int64, device=device), offs
+
+    def reduce(self, unit, grads, accumulate: bool) -> None:
+        self.epoch += 1
+        e = self.epoch
+        base = (e % 2) * self.slot
+        views = [self.buf.tensor(base + 4 * off, [s.full_numel])
+                 for s, off in zip(unit.rs_states, unit.rs_offsets, strict=True)]
+        torch._foreach_copy_(views, [g.reshape(-1) for g in grads])
+        ext().fsdp_rs([p + base for p in self.buf.peers], self.flags.peers, unit.rs_table, unit.grad_flat,
+                      bool(accumulate), 1.0 / self.n, self.rank, e, self.chunks,
+                      status_word(unit.grad_flat.device))
+
+    def close(self) -> None:
+        self.buf.close()
+        self.flags.close()

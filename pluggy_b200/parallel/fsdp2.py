@@ -29,6 +29,10 @@ B200 differences (same observable contract):
   buffer over NVLink, :mod:`pluggy_b200.comm.fsdp_fused`) plus one finishing copy,
   instead of an NCCL all-gather (``gather="nccl"`` keeps NCCL). Gradient
   reduce-scatters stay on NCCL;
+* ``reduce="peer"``: the gradient reduce-scatter is one peer-memory kernel per unit
+  (``fsdp_rs_kernel``: each rank stages its full unit gradient in symmetric memory, sums
+  its shards over the ranks' copies and writes or accumulates them straight into a flat
+  fp32 grad-shard buffer) instead of NCCL;
 * for the fused-engine models (their GEMMs read bf16 weights through the weight
   cache) the block units are gathered in low precision: each rank casts its shards
   to bf16 while pushing them into a slot of symmetric memory that the GEMMs then
@@ -114,7 +118,7 @@ class _Unit:
 
 class FSDP2:
     def __init__(self, model: nn.Module, mesh: MeshLike, dim: str = "dp", *, prefetch: bool = True,
-                 gather: str = "auto", lowp_gather: bool = True):
+                 gather: str = "auto", lowp_gather: bool = True, reduce: str = "nccl"):
         self.mesh = mesh
         self.dim = dim
         self.group_size = mesh.size(dim)
@@ -153,6 +157,28 @@ class FSDP2:
             from pluggy_b200.comm.fsdp_fused import PeerGather
 
             self._peer = PeerGather(mesh, dim, max(u.full_nbytes for u in self._units))
+        # gradient reduce-scatter: NCCL, or the peer-memory kernel that accumulates into
+        # a flat fp32 grad-shard buffer per unit
+        self._peer_rs = None
+        if reduce not in ("nccl", "peer"):
+            raise ValueError(f"reduce must be 'nccl' or 'peer', got {reduce!r}")
+        if reduce == "peer":
+            if not (self._cuda and aligned):
+                raise ValueError("peer reduce-scatters need CUDA and parameters of whole 16-byte shards")
+            from pluggy_b200.comm.fsdp_fused import PeerReduceScatter
+
+            for u in self._units:
+                u.rs_states = [st for st in u.params if st.param.requires_grad]
+                u.rs_table, u.rs_offsets = PeerReduceScatter.plan(u.rs_states, dev)
+                u.grad_flat = torch.zeros(sum(st.shard_numel for st in u.rs_states),
+                                          dtype=torch.float32, device=dev)
+                off = 0
+                for st in u.rs_states:
+                    st.rs_view = u.grad_flat[off:off + st.shard_numel].view(st.shard_shape)
+                    off += st.shard_numel
+                u.grad_acc = False
+            self._peer_rs = PeerReduceScatter(
+                mesh, dim, max(4 * sum(st.full_numel for st in u.rs_states) for u in self._units))
         # low-precision slot gathers for the block units of fused-engine models
         self._slots = None
         self._slot_views: dict[int, torch.Tensor] = {}
@@ -306,6 +332,21 @@ class FSDP2:
 
     def _reduce_unit(self, unit: _Unit) -> None:
         """Average each full grad of ``unit`` into its fp32 shard accumulator."""
+        if self._peer_rs is not None:
+            ready = {id(s) for s in unit.ready_grads}
+            assert all(id(s) in ready for s in unit.rs_states), f"unit {unit.name}: missing grads"
+            grads = [s.param.grad for s in unit.rs_states]
+            self._comm_stream.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(self._comm_stream):
+                self._peer_rs.reduce(unit, grads, accumulate=unit.grad_acc)
+                for g in grads:
+                    g.record_stream(self._comm_stream)
+            unit.grad_acc = True
+            for s in unit.rs_states:
+                s.grad_shard = s.rs_view
+                s.param.grad = None
+            unit.ready_grads = []
+            return
         group = self._group()
         n = self.group_size
         nccl = dist.get_backend(group) == "nccl"
@@ -353,6 +394,8 @@ class FSDP2:
                     assert s.grad_shard is not None, f"unit {unit.name}: no reduced grad to publish"
                     s.param.grad = s.grad_shard
                     s.grad_shard = None
+            # peer reduce-scatter: the next step's first microbatch overwrites the shards
+            unit.grad_acc = False
 
     @torch._dynamo.disable
     def fused_block_enter(self, i: int) -> None:
@@ -378,6 +421,10 @@ class FSDP2:
             torch.cuda.synchronize()
             self._slots.close()
             self._slots = None
+        if getattr(self, "_peer_rs", None) is not None:
+            torch.cuda.synchronize()
+            self._peer_rs.close()
+            self._peer_rs = None
 
     # ------------------------------------------------------------- inspection
     @property

@@ -186,7 +186,10 @@ class Trainer:
         elif self.parallelism == "fsdp2":
             from pluggy_b200.parallel.fsdp2 import FSDP2
 
-            self.dp = FSDP2(model, self.mesh, dim="dp")
+            fs_cfg = self.config.get("fsdp2", {})
+            self.dp = FSDP2(model, self.mesh, dim="dp", gather=fs_cfg.get("gather", "auto"),
+                            lowp_gather=fs_cfg.get("lowp_gather", True),
+                            reduce=fs_cfg.get("reduce", "nccl"))
         else:
             raise ValueError(f"unknown parallelism {self.parallelism!r}: expected 'ddp' or 'fsdp2'")
         self.grad_shard_dims = ("dp",) if (self.parallelism == "fsdp2" and self.dp_size > 1) else ()

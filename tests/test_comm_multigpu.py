@@ -369,15 +369,18 @@ def _fsdp_peer_case(rank, world):
             plain, {"input_ids": batches[0], "labels": batches[0]}))
     del plain
     res = {}
-    for mode in ("nccl", "peer", "peer_fp32"):
+    for mode in ("nccl", "peer", "peer_fp32", "peer_rs"):
         torch.manual_seed(0)
         m = Qwen3(**cfg).cuda()
         m.init_weights()
         fs = FSDP2(m, mesh, "dp", gather="nccl" if mode == "nccl" else "peer",
-                   lowp_gather=mode == "peer")
+                   lowp_gather=mode in ("peer", "peer_rs"),
+                   reduce="peer" if mode == "peer_rs" else "nccl")
         assert (fs._peer is not None) == (mode != "nccl")
         # "peer": block units gathered as bf16 straight into the GEMMs' slots
-        assert (fs._slots is not None) == (mode == "peer")
+        assert (fs._slots is not None) == (mode in ("peer", "peer_rs"))
+        # "peer_rs": gradients reduce-scattered by the peer-memory kernel
+        assert (fs._peer_rs is not None) == (mode == "peer_rs")
         losses = []
         for ids in batches:
             loss = ARObjective(ce_chunk_size=256).compute_loss(m, {"input_ids": ids, "labels": ids})
@@ -393,7 +396,7 @@ def _fsdp_peer_case(rank, world):
     assert abs(res["nccl"][0][0] - want0) < 1e-3 * abs(want0), (res["nccl"][0][0], want0)
     # the gathers are exact copies; the remaining differences come from float atomics
     # elsewhere in the step (loss sum, dQ accumulation)
-    for mode in ("peer", "peer_fp32"):
+    for mode in ("peer", "peer_fp32", "peer_rs"):
         for a, b in zip(res["nccl"][0], res[mode][0]):
             assert abs(a - b) < 1e-5 * abs(a), (mode, res["nccl"][0], res[mode][0])
         for n, gref in res["nccl"][1].items():
