@@ -74,7 +74,7 @@ def layout(name: str, n_gpus: int) -> dict:
     return {"tp": tp, "dp": dp, "parallelism": par, "tokens": bc["micro"] * bc["seq"] * dp}
 
 
-def train_config(n_gpus: int, reducer: str = "nccl", name: str = "ddp06b") -> dict:
+def train_config(n_gpus: int, reducer: str = "auto", name: str = "ddp06b") -> dict:
     bc = BENCH_CONFIGS[name]
     lay = layout(name, n_gpus)
     cfg = {
@@ -222,7 +222,8 @@ def run_ours(args, rank, local_rank, world, device) -> dict:
     from pluggy_b200.train.trainer import Trainer
     from pluggy_b200.utils.launch_count import count_launches
 
-    reducer = os.environ.get("PLG_DDP_REDUCER", "nccl")
+    # "auto": ZeRO-1 for plain data parallelism on 2+ GPUs, NCCL otherwise (the trainer's rule)
+    reducer = os.environ.get("PLG_DDP_REDUCER", "auto")
     bc = BENCH_CONFIGS[args.config]
     trainer = Trainer(train_config(world, reducer, args.config), rank=rank, local_rank=local_rank,
                       world_size=world, benchmark=True)

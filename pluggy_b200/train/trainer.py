@@ -181,8 +181,20 @@ class Trainer:
             from pluggy_b200.parallel.ddp import DDP
 
             ddp_cfg = self.config.get("ddp", {})
+            reducer = ddp_cfg.get("reducer", "auto")
+            # ZeRO-1 leaves only each rank's slice of the gradients averaged and sums the
+            # clip's squares during the reduce-scatter: it composes with plain data
+            # parallelism only (tensor/context parallelism reduce more axes afterwards,
+            # expert parameters are not bucketed)
+            plain = self.tp is None and self.cp is None and self.ep is None
+            if reducer == "auto":
+                reducer = "zero1" if (self.device.type == "cuda" and plain and self.dp_size > 1) \
+                    else "nccl"
+            elif reducer == "zero1" and not plain:
+                raise ValueError("ddp.reducer 'zero1' composes with plain data parallelism only "
+                                 "(no tp, cp or ep axes); use 'fused' or 'nccl'")
             self.dp = DDP(model, self.mesh, dim="dp", bucket_mb=ddp_cfg.get("bucket_mb", 25),
-                          reducer=ddp_cfg.get("reducer", "nccl"))
+                          reducer=reducer)
         elif self.parallelism == "fsdp2":
             from pluggy_b200.parallel.fsdp2 import FSDP2
 
