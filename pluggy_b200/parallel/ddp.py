@@ -144,6 +144,9 @@ class DDP:
             return base
         from pluggy_b200.comm.zero1 import Zero1AdamW
 
+        if not isinstance(base, torch.optim.AdamW):
+            raise ValueError(f"ZeRO-1 runs AdamW on the owned slices; got {type(base).__name__}")
+
         return Zero1AdamW(base, self.zero1, self._gate, self._gate_used)
 
     def reduced_norm_sq(self):

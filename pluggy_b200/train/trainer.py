@@ -187,12 +187,13 @@ class Trainer:
             # parallelism only (tensor/context parallelism reduce more axes afterwards,
             # expert parameters are not bucketed)
             plain = self.tp is None and self.cp is None and self.ep is None
+            adamw = self.config["optimizer"].get("name") == "adamw"
             if reducer == "auto":
-                reducer = "zero1" if (self.device.type == "cuda" and plain and self.dp_size > 1) \
-                    else "nccl"
-            elif reducer == "zero1" and not plain:
-                raise ValueError("ddp.reducer 'zero1' composes with plain data parallelism only "
-                                 "(no tp, cp or ep axes); use 'fused' or 'nccl'")
+                reducer = "zero1" if (self.device.type == "cuda" and plain and adamw
+                                      and self.dp_size > 1) else "nccl"
+            elif reducer == "zero1" and not (plain and adamw):
+                raise ValueError("ddp.reducer 'zero1' composes with plain data parallelism and AdamW "
+                                 "only (no tp, cp or ep axes); use 'fused' or 'nccl'")
             self.dp = DDP(model, self.mesh, dim="dp", bucket_mb=ddp_cfg.get("bucket_mb", 25),
                           reducer=reducer)
         elif self.parallelism == "fsdp2":
