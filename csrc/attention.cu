@@ -817,7 +817,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
-// ------------------------------------------------------- backward, head_dim 128
+// ------------------------------------------------ backward, head_dim 64 and 128
 // One CTA per (128-key tile, kv head, batch), heaviest causal key tiles first.
 // The loop runs over steps of 64 query rows (all q heads of the GQA group and
 // every query block that sees the keys). Per step j, with buffers b = j & 1:
@@ -835,6 +835,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // lse*log2e and delta*scale come pre-negated from a pre-pass, padded to a
 // multiple of 64 queries ([B*Hq][2][S64]) so each step fetches them with two
 // 256-byte bulk copies; padded queries carry -inf / 0 and contribute nothing.
+// head_dim 64 runs the same pipeline with half-width K/V/Q/dO tiles, dV/dK MMAs of
+// N = 64 and a dQ^T MMA that keeps M = 128: its A operand (K^T, MN-major) spans two
+// 64-row atoms and the second one is V's tile, which sits right after K's, so TMEM
+// lanes 64..127 of dQ^T hold V^T dS^T and the drain warps of those lanes skip them.
 constexpr int kB3Threads = 384;
 constexpr int kB3TmaWarp = 8, kB3MmaWarp = 9;  // warps 0..3 compute, 4..7 dQ drain
 // setmaxnreg split of the 384 x 168 launch allocation: 128*(224 + 112 + 96) = 55296
@@ -845,8 +849,10 @@ static_assert(128 * (kB3RegsComp + kB3RegsDrain + kB3RegsCtl) <= kB3Threads * kB
               "register split exceeds the launch allocation");
 constexpr int kBQ3 = 64;
 
+template <int kD>
 struct Bwd3 {
-  static constexpr int D = 128;
+  static_assert(kD == 64 || kD == 128, "backward head_dim");
+  static constexpr int D = kD;
   static constexpr int kKVTile = 128 * D * 2;  // 32 KB
   static constexpr int kQTile = kBQ3 * D * 2;  // 16 KB, two [64 x 64] boxes
   static constexpr int kQBox = kBQ3 * 128;     // bytes of one [64 rows x 64] box
@@ -864,16 +870,6 @@ struct Bwd3 {
   static constexpr int kTS0 = 256, kTdP0 = 320;               // + 128 * b
 };
 
-// K-major SW128 descriptor for k-step kk of a 64-row tile stored as [64 x 64] boxes
-__device__ __forceinline__ uint64_t desc_kmajor64(uint32_t base, int kk) {
-  return make_smem_desc(base + (kk >> 2) * Bwd3::kQBox + (kk & 3) * 32, 16, 1024, kLayoutSW128);
-}
-// MN-major SW128 descriptor for k-step kk (16 rows) of a 64-row tile, the 64-wide
-// column boxes being the MN atoms
-__device__ __forceinline__ uint64_t desc_mnmajor64(uint32_t base, int kk) {
-  return make_smem_desc(base + kk * 2048, Bwd3::kQBox, 1024, kLayoutSW128);
-}
-
 // Per-step timeline of CTA 0 (SM clock), recorded only when a trace buffer is
 // given: 0 producer issued Q/dO, 1 MMA issued S/dP(j), 2 MMA saw P(j) ready,
 // 3 MMA issued dQ(j), 4 compute saw S/dP(j), 5 compute released P(j), 6 drain saw
@@ -885,12 +881,14 @@ __device__ __forceinline__ void trace_ev(long long* trace, int ev, int j) {
     trace[ev * kAttnTraceSteps + j] = clock64();
 }
 
+template <int kD>
 __global__ void __launch_bounds__(kB3Threads, 1)
     attn_bwd3_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                      const __grid_constant__ CUtensorMap tmDQ, AttnBwdArgs g) {
-  using C = Bwd3;
+  using C = Bwd3<kD>;
   constexpr int D = C::D;
+  static_assert(kD != 64 || C::kV == C::kK + kBox, "dQ^T's second A atom must be V's tile");
   const AttnArgs& a = g.f;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -1097,14 +1095,18 @@ __global__ void __launch_bounds__(kB3Threads, 1)
       }
       if (lane == 0 && quad == 0) trace_ev(g.trace, 6, j);
       tc_fence_after();
+      const bool live = quad * 32 < D;  // TMEM lanes that are rows of dQ^T
       uint32_t v[kBQ3];
-      tmem_ld_32x32b_x32(trow + C::kTdP0 + 128 * bj, *reinterpret_cast<uint32_t(*)[32]>(v));
-      tmem_ld_32x32b_x32(trow + C::kTdP0 + 128 * bj + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
-      tmem_ld_wait();
+      if (live) {
+        tmem_ld_32x32b_x32(trow + C::kTdP0 + 128 * bj, *reinterpret_cast<uint32_t(*)[32]>(v));
+        tmem_ld_32x32b_x32(trow + C::kTdP0 + 128 * bj + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+        tmem_ld_wait();
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&dq_free[bj]);
       if (lane == 0 && quad == 0) trace_ev(g.trace, 7, j);
+      if (!live) continue;
       // stage this warp's [64 q x 32 d] slice and reduce-add it into the fp32
       // workspace with one bulk tensor operation (rows past S are clipped)
       if (lane == 0) bulk_wait_group_read<0>();  // previous slice has left smem
@@ -1249,13 +1251,14 @@ __global__ void __launch_bounds__(kB3Threads, 1)
 // Backward pre-pass for the head_dim-128 kernel: per (b, h) row of the stats
 // workspace [B*Hq][2][S64], -lse*log2(e) and -scale * rowsum(dO * O); queries
 // beyond S get -inf and 0. Also zeroes the fp32 dQ workspace row of each (b, s, h).
-// One warp per (b, s, h), 4 channels (8 bytes) per lane.
+// One warp per (b, s, h), D / 32 channels per lane.
+template <int D>
 __global__ void attn_bwd_stats_kernel(const __nv_bfloat16* __restrict__ o, long long o_row,
                                       const __nv_bfloat16* __restrict__ dout, long long do_row,
                                       const float* __restrict__ lse, float* __restrict__ stats,
                                       float* __restrict__ dq_acc, int B, int S, int S64, int H,
                                       float scale) {
-  constexpr int D = 128;
+  static_assert(D == 64 || D == 128, "stats head_dim");
   const long long wid = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const long long total = static_cast<long long>(B) * S64 * H;
@@ -1273,13 +1276,22 @@ __global__ void attn_bwd_stats_kernel(const __nv_bfloat16* __restrict__ o, long 
     return;
   }
   const long long tok = static_cast<long long>(bb) * S + s;
-  const uint2 ov = *reinterpret_cast<const uint2*>(o + tok * o_row + h * D + lane * 4);
-  const uint2 dv = *reinterpret_cast<const uint2*>(dout + tok * do_row + h * D + lane * 4);
-  const float2 o0 = unpack_bf16x2(ov.x), o1 = unpack_bf16x2(ov.y);
-  const float2 d0 = unpack_bf16x2(dv.x), d1 = unpack_bf16x2(dv.y);
-  float acc = o0.x * d0.x + o0.y * d0.y + o1.x * d1.x + o1.y * d1.y;
+  float acc;
+  if constexpr (D == 128) {
+    const uint2 ov = *reinterpret_cast<const uint2*>(o + tok * o_row + h * D + lane * 4);
+    const uint2 dv = *reinterpret_cast<const uint2*>(dout + tok * do_row + h * D + lane * 4);
+    const float2 o0 = unpack_bf16x2(ov.x), o1 = unpack_bf16x2(ov.y);
+    const float2 d0 = unpack_bf16x2(dv.x), d1 = unpack_bf16x2(dv.y);
+    acc = o0.x * d0.x + o0.y * d0.y + o1.x * d1.x + o1.y * d1.y;
+    reinterpret_cast<float4*>(dq_acc + (tok * H + h) * D)[lane] = make_float4(0.f, 0.f, 0.f, 0.f);
+  } else {
+    const float2 o0 = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(o + tok * o_row + h * D + lane * 2));
+    const float2 d0 =
+        unpack_bf16x2(*reinterpret_cast<const uint32_t*>(dout + tok * do_row + h * D + lane * 2));
+    acc = o0.x * d0.x + o0.y * d0.y;
+    reinterpret_cast<float2*>(dq_acc + (tok * H + h) * D)[lane] = make_float2(0.f, 0.f);
+  }
   acc = warp_sum(acc);
-  reinterpret_cast<float4*>(dq_acc + (tok * H + h) * D)[lane] = make_float4(0.f, 0.f, 0.f, 0.f);
   if (lane == 0) {
     row[s] = -lse[(static_cast<long long>(bb) * H + h) * S + s] * kLog2e;
     row[S64 + s] = -acc * scale;
@@ -1446,18 +1458,19 @@ static void fwd_launch_t(const AttnArgs& a, cudaStream_t st) {
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 
+template <int D>
 static void bwd3_launch(const AttnBwdArgs& g, cudaStream_t st) {
-  using C = Bwd3;
+  using C = Bwd3<D>;
   const AttnArgs& a = g.f;
   CUtensorMap tq = map_bshd(a.q, a.B, a.S, a.Hq, C::D, a.q_row, kBQ3);
   CUtensorMap tk = map_bshd(a.k, a.B, a.S, a.Hk, C::D, a.k_row);
   CUtensorMap tv = map_bshd(a.v, a.B, a.S, a.Hk, C::D, a.v_row);
   CUtensorMap td = map_bshd(g.dout, a.B, a.S, a.Hq, C::D, g.do_row, kBQ3);
   CUtensorMap tdq = map_dq_acc(g.dq_acc, a.B, a.S, a.Hq, C::D);
-  set_max_smem_once(reinterpret_cast<const void*>(attn_bwd3_kernel), C::kSmem);
+  set_max_smem_once(reinterpret_cast<const void*>(attn_bwd3_kernel<D>), C::kSmem);
   static const int regs = [] {
     cudaFuncAttributes fa;
-    PLG_CUDA_CHECK(cudaFuncGetAttributes(&fa, attn_bwd3_kernel));
+    PLG_CUDA_CHECK(cudaFuncGetAttributes(&fa, attn_bwd3_kernel<D>));
     return fa.numRegs;
   }();
   if (regs != kB3RegsLaunch)
@@ -1470,14 +1483,14 @@ static void bwd3_launch(const AttnBwdArgs& g, cudaStream_t st) {
       (reinterpret_cast<uintptr_t>(a.o) & 15) || (reinterpret_cast<uintptr_t>(g.dout) & 15) ||
       (reinterpret_cast<uintptr_t>(g.dq) & 15))
     throw std::invalid_argument("attention backward: o, dout and dq rows must be 16-byte aligned");
-  attn_bwd_stats_kernel<<<(srows * 32 + 255) / 256, 256, 0, st>>>(
+  attn_bwd_stats_kernel<D><<<(srows * 32 + 255) / 256, 256, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(a.o), a.o_row,
       reinterpret_cast<const __nv_bfloat16*>(g.dout), g.do_row, a.lse, g.delta, g.dq_acc, a.B, a.S,
       S64, a.Hq, a.scale);
   PLG_CUDA_CHECK(cudaGetLastError());
   const long long ctas = static_cast<long long>((a.S + BKV - 1) / BKV) * a.Hk * a.B;
   if (ctas > 0x7fffffffLL) throw std::invalid_argument("attention: problem too large for one launch");
-  attn_bwd3_kernel<<<static_cast<unsigned>(ctas), kB3Threads, C::kSmem, st>>>(tq, tk, tv, td, tdq, g);
+  attn_bwd3_kernel<D><<<static_cast<unsigned>(ctas), kB3Threads, C::kSmem, st>>>(tq, tk, tv, td, tdq, g);
   PLG_CUDA_CHECK(cudaGetLastError());
   const long long tokens = static_cast<long long>(a.B) * a.S;
   const long long groups = tokens * (a.Hq * C::D / 8);
@@ -1524,8 +1537,15 @@ void attn_fwd(const AttnArgs& a, cudaStream_t st) {
 void attn_bwd(const AttnBwdArgs& g, cudaStream_t st) {
   const AttnArgs& a = g.f;
   if (a.Hq % a.Hk) throw std::invalid_argument("attention: Hq must be a multiple of Hk");
-  if (a.d == 128) return attn::bwd3_launch(g, st);
-  if (a.d == 64) return attn::bwd_launch<64>(g, st);
+  if (a.d == 128) return attn::bwd3_launch<128>(g, st);
+  if (a.d == 64) {
+    // PLG_ATTN_BWD64=group selects the single-group head_dim-64 kernel
+    static const bool group = [] {
+      const char* e = std::getenv("PLG_ATTN_BWD64");
+      return e != nullptr && std::string(e) == "group";
+    }();
+    return group ? attn::bwd_launch<64>(g, st) : attn::bwd3_launch<64>(g, st);
+  }
   throw std::invalid_argument("attention: head_dim must be 64 or 128");
 }
 

@@ -53,12 +53,11 @@ def attn_fwd(q, k, v, *, causal=True, window=0, scale=None):
 
 
 def _attn_bwd_d64_padded(q, k, v, o, lse, do, causal, window, scale, dq, dk, dv):
-    """head_dim 64 through the head_dim-128 backward kernel: q, k, v, o and dO are
-    zero-padded to 128 channels (the padded channels add 0 to every score and to
-    rowsum(dO * O), so lse and the softmax are unchanged) and the gradients' first 64
-    channels are the result. The 128-wide kernel (double-buffered S/dP in TMEM,
-    dedicated dQ drain warps) pays for the doubled work with its higher tensor-core
-    utilisation (``PLG_ATTN_D64_PAD=0`` selects the 64-wide kernel)."""
+    """head_dim 64 through the head_dim-128 backward kernel (``PLG_ATTN_D64_PAD=1``): q,
+    k, v, o and dO are zero-padded to 128 channels (the padded channels add 0 to every
+    score and to rowsum(dO * O), so lse and the softmax are unchanged) and the
+    gradients' first 64 channels are the result. Kept as a cross-check of the native
+    head_dim-64 instance of the pipelined kernel, which is the default."""
     pad = [F.pad(t, (0, 64)) for t in (q, k, v, o, do)]
     dq_p, dk_p, dv_p = attn_bwd(*pad[:4], lse, pad[4], causal=causal, window=window, scale=scale)
     outs = []
@@ -73,12 +72,14 @@ def _attn_bwd_d64_padded(q, k, v, o, lse, do, causal, window, scale, dq, dk, dv)
 
 def attn_bwd(q, k, v, o, lse, do, *, causal=True, window=0, scale=None, dq=None, dk=None, dv=None,
              trace=None):
-    """Backward of flash attention. ``trace`` (int64 [10, 256] on the device,
-    head_dim 128 only) receives SM-clock stamps of the first CTA's pipeline events
-    per step, for timeline analysis of the kernel."""
+    """Backward of flash attention: one pipelined kernel for head_dim 64 and 128 (the
+    earlier single-group head_dim-64 kernel stays selectable with
+    ``PLG_ATTN_BWD64=group``). ``trace`` (int64 [12, 256] on the device) receives
+    SM-clock stamps of the first CTA's pipeline events per step, for timeline analysis
+    of the kernel."""
     B, S, Hq, d = q.shape
     scale = 1.0 / math.sqrt(d) if scale is None else scale
-    if d == 64 and trace is None and os.environ.get("PLG_ATTN_D64_PAD", "1") != "0":
+    if d == 64 and trace is None and os.environ.get("PLG_ATTN_D64_PAD", "0") == "1":
         return _attn_bwd_d64_padded(q, k, v, o, lse, do, causal, window, scale, dq, dk, dv)
     dq = torch.empty_like(q, memory_format=torch.contiguous_format) if dq is None else dq
     dk = torch.empty(k.shape, dtype=k.dtype, device=k.device) if dk is None else dk

@@ -370,6 +370,9 @@ ATTN_CASES = [
     (1, 512, 2, 1, 128, True, 160),
     (1, 256, 2, 2, 64, False, 0),
     (2, 1024, 16, 8, 128, True, 0),
+    (2, 200, 4, 1, 64, True, 0),
+    (1, 512, 4, 2, 64, True, 160),
+    (1, 2048, 8, 2, 64, True, 0),
 ]
 
 
