@@ -82,7 +82,12 @@ def analyze(trace_path: str) -> dict:
         ex = (iv[1] - iv[0]) - intersect_len([iv], pu)
         per_kernel[name[:80]][0] += ex
         per_kernel[name[:80]][1] += 1
+    allu = union([iv for iv, _ in comm + comp])
+    span = (allu[-1][1] - allu[0][0]) if allu else 0.0
     return {
+        # span: first kernel start to last kernel end; busy: time any kernel runs. The
+        # difference is device idle time (host-bound launches, synchronisations).
+        "span_us": span, "busy_us": total(allu), "idle_us": span - total(allu),
         "comm_us": total(cu), "compute_us": total(pu), "hidden_us": hidden, "exposed_us": exposed,
         "hidden_frac": hidden / total(cu) if cu else 1.0,
         "per_kernel_exposed_us": {k: v[0] for k, v in sorted(per_kernel.items(), key=lambda kv: -kv[1][0])},
