@@ -70,12 +70,14 @@ class Qwen3MoeSparseMLP(nn.Module):
         self.router = Qwen3MoeTopKRouter(emb_dim, num_experts, top_k, norm_topk_prob)
         self.experts = Qwen3MoeExperts(emb_dim, moe_ffn_dim, num_experts)
         self.last_router_logits: torch.Tensor | None = None
+        self.last_top_idx: torch.Tensor | None = None
 
     def forward(self, x):
         shp = x.shape
         flat = x.reshape(-1, shp[-1])
         logits, w, idx = self.router(flat)
         self.last_router_logits = logits
+        self.last_top_idx = idx.detach()
         return self.experts(flat, idx, w).reshape(shp)
 
 
@@ -112,8 +114,10 @@ def load_balancing_loss(router_logits, num_experts: int, top_k: int):
     logits = torch.cat([g.float() for g in router_logits], dim=0)
     probs = F.softmax(logits, dim=-1)
     _, top = torch.topk(probs, top_k, dim=-1)
-    tokens_per_expert = F.one_hot(top, num_experts).float().mean(dim=0)
-    return (tokens_per_expert * probs.mean(dim=0).unsqueeze(0)).sum() * num_experts
+    # the reference's one_hot(top, E).mean(0) summed over the k slots: the fraction of
+    # (token, slot) pairs routed to each expert, counted without the [T, k, E] one-hot
+    frac = torch.bincount(top.reshape(-1), minlength=num_experts).float() / top.shape[0]
+    return (frac * probs.mean(dim=0)).sum() * num_experts
 
 
 def router_z_loss(router_logits):
@@ -184,14 +188,18 @@ class Qwen3Moe(nn.Module):
                 if isinstance(b.ffn, Qwen3MoeSparseMLP) and b.ffn.last_router_logits is not None]
 
     def _update_expert_counts(self, logits) -> None:
+        """Tokens routed to each expert this forward, summed over the sparse layers
+        (from the routers' own top-k choices)."""
         if not logits:
             self.last_tokens_per_expert = None
             return
         counts = torch.zeros(self.num_experts, device=logits[0].device)
         with torch.no_grad():
-            for g in logits:
-                _, idx = torch.topk(F.softmax(g.float(), dim=-1), self.top_k, dim=-1)
-                counts += F.one_hot(idx, self.num_experts).float().sum(dim=(0, 1))
+            for b in self.blocks:
+                idx = getattr(b.ffn, "last_top_idx", None) if isinstance(b.ffn, Qwen3MoeSparseMLP) \
+                    else None
+                if idx is not None:
+                    counts += torch.bincount(idx.reshape(-1), minlength=self.num_experts).float()
         self.last_tokens_per_expert = counts
 
     def aux_loss(self):
@@ -211,6 +219,7 @@ class Qwen3Moe(nn.Module):
         for b in self.blocks:
             if isinstance(b.ffn, Qwen3MoeSparseMLP):
                 b.ffn.last_router_logits = None
+                b.ffn.last_top_idx = None
         self._router_logits = []
         B, S = x.shape
         fused = (x.is_cuda and attention_mask is None and not return_hidden_states

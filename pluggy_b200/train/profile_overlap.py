@@ -148,6 +148,11 @@ def capture(config, warmup: int, steps: int, out: str, rank: int, local_rank: in
             torch.cuda.synchronize()
     path = out if world == 1 else f"{os.path.splitext(out)[0]}_rank{rank}.json"
     prof.export_chrome_trace(path)
+    if torch.cuda.is_available():
+        ms = torch.cuda.memory_stats()
+        # allocator retries (cudaFree + retry under memory pressure) synchronise the device
+        print(json.dumps({"rank": rank, "max_mem_gib": torch.cuda.max_memory_allocated() / 2**30,
+                          "alloc_retries": ms.get("num_alloc_retries", 0)}))
     return path
 
 
