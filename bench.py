@@ -55,8 +55,9 @@ BENCH_CONFIGS = {
     "moe_ep": {"model": "qwen3_moe", "micro": 2, "seq": 4096, "parallel": "ep", "ref": "fsdp2",
                "cfg": {"num_layers": 24, "num_heads": 32, "num_kv_heads": 4, "emb_dim": 2048,
                        "head_dim": 128, "vocab_size": 151936, "moe_ffn_dim": 768, "num_experts": 128,
-                       "top_k": 8, "router_aux_loss_coef": 0.001},
-               "label": "qwen3-MoE-shaped (24L, d2048, 32q/4kv x128, 128 experts top-8, ffn 768, V151936)"},
+                       "top_k": 8, "router_aux_loss_coef": 0.001, "router_init_std": 0.02},
+               "label": "qwen3-MoE-shaped (24L, d2048, 32q/4kv x128, 128 experts top-8, ffn 768, V151936, "
+                        "router N(0, 0.02) init)"},
     "llama_tp": {"model": "llama3_2", "micro": 2, "seq": 8192, "parallel": "tp", "ref": "ddp",
                  "cfg": {"num_layers": 16, "num_heads": 32, "num_kv_heads": 8, "emb_dim": 2048,
                          "head_dim": 64, "ffn_dim": 8192, "vocab_size": 128256, "rope_base": 500000.0,
@@ -346,6 +347,14 @@ def run_reference(args, rank, local_rank, world, device) -> dict:
     tr.model = build_model(bc["model"], mcfg)
     tr.model.to(device)
     tr.model.init_weights()
+    std = bc["cfg"].get("router_init_std", 0.0)
+    if std > 0:
+        # the same router weight draw as this framework's arm (the reference's init
+        # leaves the routers at zeros); its model code is untouched
+        with torch.no_grad():
+            for m in tr.model.modules():
+                if type(m).__name__ == "Qwen3MoeTopKRouter":
+                    m.weight.normal_(0.0, std)
     tr._parallelize(tr.model)
     tr._compile(tr.model)
     torch.manual_seed(1 + tr.mesh.coordinate("dp"))

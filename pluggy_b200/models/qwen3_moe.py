@@ -133,9 +133,14 @@ class Qwen3Moe(nn.Module):
                  top_k: int = 8, ffn_dim: int | None = None, norm_topk_prob: bool = True,
                  decoder_sparse_step: int = 1, mlp_only_layers: list[int] | None = None,
                  router_aux_loss_coef: float = 0.001, router_z_loss_coef: float = 0.001,
-                 rope_base: float = 1_000_000.0, tie_embeddings: bool = False):
+                 rope_base: float = 1_000_000.0, tie_embeddings: bool = False,
+                 router_init_std: float = 0.0):
         super().__init__()
         mlp_only = set(mlp_only_layers or [])
+        # 0 keeps the routers at zeros through init_weights (the reference's init: every
+        # token's top-k then ties on the same experts until training spreads them);
+        # > 0 draws them N(0, router_init_std), a router that already spreads tokens
+        self.router_init_std = router_init_std
         self.num_experts, self.top_k = num_experts, top_k
         self.router_aux_loss_coef, self.router_z_loss_coef = router_aux_loss_coef, router_z_loss_coef
         self.head_dim, self.emb_dim = head_dim, emb_dim
@@ -175,6 +180,8 @@ class Qwen3Moe(nn.Module):
             if isinstance(b.ffn, Qwen3MoeSparseMLP):
                 nn.init.normal_(b.ffn.experts.gate_up_proj, 0.0, std)
                 nn.init.normal_(b.ffn.experts.down_proj, 0.0, std)
+                if self.router_init_std > 0:
+                    nn.init.normal_(b.ffn.router.weight, 0.0, self.router_init_std)
         s = (2 * len(self.blocks)) ** -0.5
         for b in self.blocks:
             b.gqa.o_proj.weight.data.mul_(s)

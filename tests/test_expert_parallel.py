@@ -109,3 +109,24 @@ def _ep_trainer(rank, world):
 
 def test_ep2_trainer_steps():
     run_ranks(_ep_trainer, 2)
+
+
+def test_router_init_and_routing_spread():
+    """The reference's router init (zeros) sends every token to the same top-k experts
+    (all probabilities tie); ``router_init_std`` draws the routers N(0, std) instead and
+    the tokens spread over the experts."""
+    from pluggy_b200.models.qwen3_moe import Qwen3Moe
+
+    kw = dict(num_layers=1, num_heads=2, num_kv_heads=1, emb_dim=64, head_dim=32, vocab_size=97,
+              moe_ffn_dim=32, num_experts=16, top_k=2)
+    torch.manual_seed(0)
+    x = torch.randint(0, 97, (2, 24))
+    for std, spread in ((0.0, False), (0.02, True)):
+        m = Qwen3Moe(**kw, router_init_std=std)
+        m.init_weights()
+        w = m.blocks[0].ffn.router.weight
+        assert bool((w != 0).any()) == spread
+        m(x)
+        used = int((m.last_tokens_per_expert > 0).sum())
+        assert (used > kw["top_k"]) == spread, used
+        assert float(m.last_tokens_per_expert.sum()) == 2 * 24 * kw["top_k"]
