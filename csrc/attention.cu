@@ -839,14 +839,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // N = 64 and a dQ^T MMA that keeps M = 128: its A operand (K^T, MN-major) spans two
 // 64-row atoms and the second one is V's tile, which sits right after K's, so TMEM
 // lanes 64..127 of dQ^T hold V^T dS^T and the drain warps of those lanes skip them.
-constexpr int kB3Threads = 384;
-constexpr int kB3TmaWarp = 8, kB3MmaWarp = 9;  // warps 0..3 compute, 4..7 dQ drain
-// setmaxnreg split of the 384 x 168 launch allocation: 128*(224 + 112 + 96) = 55296
-// <= 64512, and 224 + 112 + 96 <= 512 per lane of each SM sub-partition. No role
-// spills at these limits.
-constexpr int kB3RegsComp = 224, kB3RegsDrain = 112, kB3RegsCtl = 96, kB3RegsLaunch = 168;
-static_assert(128 * (kB3RegsComp + kB3RegsDrain + kB3RegsCtl) <= kB3Threads * kB3RegsLaunch,
+// The P / dS work (exp2 and the dS products of 128 keys x 64 queries per step) is
+// split over two warpgroups, one per 32-query half of the step: with one warpgroup
+// the math of a step took longer than the step's five MMAs (SM-clock timeline of the
+// pipeline), so the tensor core waited on it.
+constexpr int kB3Threads = 512;
+// warps 0..7 P / dS (warp w: key rows 32 * (w & 3).., queries 32 * (w >> 2)..),
+// 8..11 dQ drain, 12 TMA producer, 13 MMA issuer
+constexpr int kB3TmaWarp = 12, kB3MmaWarp = 13;
+// setmaxnreg split of the 512 x 128 launch allocation: 256 * 152 + 128 * (112 + 96)
+// = 65536, and 152 + 152 + 112 + 96 = 512 per lane of each SM sub-partition.
+constexpr int kB3RegsComp = 152, kB3RegsDrain = 112, kB3RegsCtl = 96, kB3RegsLaunch = 128;
+static_assert(256 * kB3RegsComp + 128 * (kB3RegsDrain + kB3RegsCtl) <= kB3Threads * kB3RegsLaunch,
               "register split exceeds the launch allocation");
+static_assert(2 * kB3RegsComp + kB3RegsDrain + kB3RegsCtl <= 512,
+              "register split exceeds a sub-partition's registers per lane");
 constexpr int kBQ3 = 64;
 
 template <int kD>
@@ -928,7 +935,7 @@ __global__ void __launch_bounds__(kB3Threads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4);
+      mbar_init(&p_full[i], 8);
       mbar_init(&dq_full[i], 1);
       mbar_init(&dq_free[i], 4);
     }
@@ -950,7 +957,7 @@ __global__ void __launch_bounds__(kB3Threads, 1)
   auto sDS = [&](int bb) { return smem + C::kDS + bb * 128 * kBQ3 * 2; };
   auto sStats = [&](int s) { return reinterpret_cast<float*>(smem + C::kStats + s * 512); };
 
-  if (warp >= 8) {
+  if (warp >= 12) {
     setmaxnreg_dec<kB3RegsCtl>();
     if (warp == kB3TmaWarp && lane == 0 && n > 0) {
       // ------------------------------------------------------------ producer
@@ -1080,7 +1087,7 @@ __global__ void __launch_bounds__(kB3Threads, 1)
       __syncwarp();
       if (!warp_wait(mma_done, 0, nullptr) && leader) record_status(a.status, kTimeoutDrain);
     }
-  } else if (warp >= 4) {
+  } else if (warp >= 8) {
     setmaxnreg_dec<kB3RegsDrain>();
     // -------------------------------------------------------------- dQ drain
     const int quad = warp & 3;          // TMEM lanes = head-dim rows 32*quad.. of dQ^T
@@ -1127,7 +1134,8 @@ __global__ void __launch_bounds__(kB3Threads, 1)
   } else {
     setmaxnreg_inc<kB3RegsComp>();
     // ----------------------------------------------------------- P / dS warps
-    const int quad = warp;
+    constexpr int kHalf = kBQ3 / 2;  // queries per warp per step
+    const int quad = warp & 3, half = warp >> 2;
     const int r = quad * 32 + lane;  // TMEM lane = key row
     const int ki = kv0 + r;
     const uint32_t trow = tmem + (static_cast<uint32_t>(quad * 32) << 16);
@@ -1142,27 +1150,25 @@ __global__ void __launch_bounds__(kB3Threads, 1)
         ok = false;
         break;
       }
-      if (lane == 0 && quad == 0) trace_ev(g.trace, 4, j);
+      if (lane == 0 && warp == 0) trace_ev(g.trace, 4, j);
       tc_fence_after();
-      const int q0 = (qb_lo + j / G) * kBQ3;
-      uint32_t sv[kBQ3], dv[kBQ3];
-      tmem_ld_32x32b_x32(trow + C::kTS0 + 128 * bj, *reinterpret_cast<uint32_t(*)[32]>(sv));
-      tmem_ld_32x32b_x32(trow + C::kTS0 + 128 * bj + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
-      tmem_ld_32x32b_x32(trow + C::kTdP0 + 128 * bj, *reinterpret_cast<uint32_t(*)[32]>(dv));
-      tmem_ld_32x32b_x32(trow + C::kTdP0 + 128 * bj + 32, *reinterpret_cast<uint32_t(*)[32]>(dv + 32));
-      const float4* st4 = reinterpret_cast<const float4*>(sStats(s));
+      const int q0 = (qb_lo + j / G) * kBQ3 + half * kHalf;  // first query of this warp
+      uint32_t sv[kHalf], dv[kHalf];
+      tmem_ld_32x32b_x32(trow + C::kTS0 + 128 * bj + half * kHalf, sv);
+      tmem_ld_32x32b_x32(trow + C::kTdP0 + 128 * bj + half * kHalf, dv);
+      // [0, 64): -lse * log2(e), [64, 128): -delta * scale of the step's 64 queries
+      const float4* st4 = reinterpret_cast<const float4*>(sStats(s)) + half * (kHalf / 4);
       const bool edge = (a.causal && kv0 + BKV - 1 > q0) ||
-                        (a.window > 0 && q0 + kBQ3 - 1 - kv0 >= a.window);
+                        (a.window > 0 && q0 + kHalf - 1 - kv0 >= a.window);
       const int c_lo = a.causal ? ki - q0 : -(1 << 30);
       const int c_hi = a.window > 0 ? ki + a.window - 1 - q0 : (1 << 30);
       tmem_ld_wait();
-      if (lane == 0 && quad == 0) trace_ev(g.trace, 9, j);
-      uint32_t pk[kBQ3 / 2], dk[kBQ3 / 2];
+      if (lane == 0 && warp == 0) trace_ev(g.trace, 9, j);
+      uint32_t pk[kHalf / 2], dk[kHalf / 2];
 #pragma unroll
-      for (int c = 0; c < kBQ3; c += 4) {
-        const float4 nl = st4[c / 4];        // -lse * log2(e)
-        const float4 nd = st4[16 + c / 4];   // -delta * scale
-        // scalar FMAs: measured faster than the packed f32x2 forms in this loop
+      for (int c = 0; c < kHalf; c += 4) {
+        const float4 nl = st4[c / 4];                // -lse * log2(e)
+        const float4 nd = st4[kBQ3 / 4 + c / 4];     // -delta * scale
         float p0 = fast_exp2(fmaf(__uint_as_float(sv[c]), scale2, nl.x));
         float p1 = fast_exp2(fmaf(__uint_as_float(sv[c + 1]), scale2, nl.y));
         float p2 = fast_exp2(fmaf(__uint_as_float(sv[c + 2]), scale2, nl.z));
@@ -1182,30 +1188,34 @@ __global__ void __launch_bounds__(kB3Threads, 1)
         dk[c / 2] = pack_bf16x2(t0, t1);
         dk[c / 2 + 1] = pack_bf16x2(t2, t3);
       }
-      if (lane == 0 && quad == 0) trace_ev(g.trace, 10, j);
-      // P^T into the S columns (two bf16 per column), dS^T into smem (SW128 rows)
-      tmem_st_32x32b_x32(trow + C::kTS0 + 128 * bj, pk);
+      if (lane == 0 && warp == 0) trace_ev(g.trace, 10, j);
+      // P^T into this half's S columns (two bf16 per column), dS^T into this half's
+      // 64 bytes of the key row in smem (SW128 rows of 128 bytes)
+      tmem_st_32x32b_x16(trow + C::kTS0 + 128 * bj + half * (kHalf / 2), pk);
       uint8_t* ds_row = sDS(bj) + r * 128;
 #pragma unroll
-      for (int c16 = 0; c16 < 8; ++c16)
+      for (int i = 0; i < 4; ++i) {
+        const int c16 = half * 4 + i;
         *reinterpret_cast<uint4*>(ds_row + ((c16 ^ (r & 7)) << 4)) =
-            make_uint4(dk[c16 * 4], dk[c16 * 4 + 1], dk[c16 * 4 + 2], dk[c16 * 4 + 3]);
+            make_uint4(dk[i * 4], dk[i * 4 + 1], dk[i * 4 + 2], dk[i * 4 + 3]);
+      }
       tmem_st_wait();
       fence_proxy_async_smem();
-      if (lane == 0 && quad == 0) trace_ev(g.trace, 11, j);
+      if (lane == 0 && warp == 0) trace_ev(g.trace, 11, j);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[bj]);
-      if (lane == 0 && quad == 0) trace_ev(g.trace, 5, j);
+      if (lane == 0 && warp == 0) trace_ev(g.trace, 5, j);
     }
-    // dK, dV of this key tile
+    // dK, dV of this key tile: each half writes half of the head_dim columns
+    constexpr int kCols = D / 2;
     __nv_bfloat16* dkr = reinterpret_cast<__nv_bfloat16*>(g.dk) +
-                         (static_cast<long long>(b) * a.S + ki) * g.dk_row + hk * D;
+                         (static_cast<long long>(b) * a.S + ki) * g.dk_row + hk * D + half * kCols;
     __nv_bfloat16* dvr = reinterpret_cast<__nv_bfloat16*>(g.dv) +
-                         (static_cast<long long>(b) * a.S + ki) * g.dv_row + hk * D;
+                         (static_cast<long long>(b) * a.S + ki) * g.dv_row + hk * D + half * kCols;
     if (n == 0) {
       if (ki < a.S)
-        for (int c = 0; c < D; c += 8) {
+        for (int c = 0; c < kCols; c += 8) {
           *reinterpret_cast<uint4*>(dkr + c) = make_uint4(0, 0, 0, 0);
           *reinterpret_cast<uint4*>(dvr + c) = make_uint4(0, 0, 0, 0);
         }
@@ -1213,10 +1223,10 @@ __global__ void __launch_bounds__(kB3Threads, 1)
       if (warp_wait(mma_done, 0, abort_flag)) {
         tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < kCols / 32; ++c) {
           uint32_t u[32], w32[32];
-          tmem_ld_32x32b_x32(trow + C::kTdV + c * 32, u);
-          tmem_ld_32x32b_x32(trow + C::kTdK + c * 32, w32);
+          tmem_ld_32x32b_x32(trow + C::kTdV + half * kCols + c * 32, u);
+          tmem_ld_32x32b_x32(trow + C::kTdK + half * kCols + c * 32, w32);
           tmem_ld_wait();
           if (ki < a.S) {
 #pragma unroll
