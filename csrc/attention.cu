@@ -888,18 +888,13 @@ __device__ __forceinline__ void trace_ev(long long* trace, int ev, int j) {
     trace[ev * kAttnTraceSteps + j] = clock64();
 }
 
-// kPolyMask: which pairs of every eight pairs of exponentials run on the FMA pipe
-// (exp2_poly2) instead of the SFU. The SFU is the limiter of the P / dS math (its
-// issue rate ran at the sustained peak in the profile of the all-SFU kernel); masked
-// entries are zeroed after the exponential, so the polynomial's -126 clamp is harmless.
-template <int kD, int kPolyMask>
+template <int kD>
 __global__ void __launch_bounds__(kB3Threads, 1)
     attn_bwd3_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                      const __grid_constant__ CUtensorMap tmDQ, AttnBwdArgs g) {
   using C = Bwd3<kD>;
   constexpr int D = C::D;
-  static_assert((kPolyMask & ~0xff) == 0, "poly mask covers eight pairs");
   static_assert(kD != 64 || C::kV == C::kK + kBox, "dQ^T's second A atom must be V's tile");
   const AttnArgs& a = g.f;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -1174,23 +1169,10 @@ __global__ void __launch_bounds__(kB3Threads, 1)
       for (int c = 0; c < kHalf; c += 4) {
         const float4 nl = st4[c / 4];                // -lse * log2(e)
         const float4 nd = st4[kBQ3 / 4 + c / 4];     // -delta * scale
-        const float x0 = fmaf(__uint_as_float(sv[c]), scale2, nl.x);
-        const float x1 = fmaf(__uint_as_float(sv[c + 1]), scale2, nl.y);
-        const float x2 = fmaf(__uint_as_float(sv[c + 2]), scale2, nl.z);
-        const float x3 = fmaf(__uint_as_float(sv[c + 3]), scale2, nl.w);
-        float p0, p1, p2, p3;
-        if ((kPolyMask >> ((c >> 1) & 7)) & 1) {
-          exp2_poly2(x0, x1, p0, p1);
-        } else {
-          p0 = fast_exp2(x0);
-          p1 = fast_exp2(x1);
-        }
-        if ((kPolyMask >> (((c >> 1) + 1) & 7)) & 1) {
-          exp2_poly2(x2, x3, p2, p3);
-        } else {
-          p2 = fast_exp2(x2);
-          p3 = fast_exp2(x3);
-        }
+        float p0 = fast_exp2(fmaf(__uint_as_float(sv[c]), scale2, nl.x));
+        float p1 = fast_exp2(fmaf(__uint_as_float(sv[c + 1]), scale2, nl.y));
+        float p2 = fast_exp2(fmaf(__uint_as_float(sv[c + 2]), scale2, nl.z));
+        float p3 = fast_exp2(fmaf(__uint_as_float(sv[c + 3]), scale2, nl.w));
         if (edge) {
           p0 = (c >= c_lo && c <= c_hi) ? p0 : 0.f;
           p1 = (c + 1 >= c_lo && c + 1 <= c_hi) ? p1 : 0.f;
@@ -1486,26 +1468,8 @@ static void fwd_launch_t(const AttnArgs& a, cudaStream_t st) {
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 
-template <int D, int kPolyMask>
-static void bwd3_launch_t(const AttnBwdArgs& g, cudaStream_t st);
-
 template <int D>
 static void bwd3_launch(const AttnBwdArgs& g, cudaStream_t st) {
-  // share of the backward's exponentials computed on the FMA pipe, in pairs per eight
-  // pairs (PLG_ATTN_BWD_POLY = 0, 2, 3 or 4)
-  static const int poly = [] {
-    const char* e = std::getenv("PLG_ATTN_BWD_POLY");
-    const int v = e ? std::atoi(e) : 3;
-    return (v == 0 || v == 2 || v == 4) ? v : 3;
-  }();
-  if (poly == 3) return bwd3_launch_t<D, 0xA4>(g, st);  // pairs 2, 5, 7
-  if (poly == 4) return bwd3_launch_t<D, 0xAA>(g, st);  // odd pairs
-  if (poly == 2) return bwd3_launch_t<D, 0x88>(g, st);  // pairs 3, 7
-  return bwd3_launch_t<D, 0>(g, st);
-}
-
-template <int D, int kPolyMask>
-static void bwd3_launch_t(const AttnBwdArgs& g, cudaStream_t st) {
   using C = Bwd3<D>;
   const AttnArgs& a = g.f;
   CUtensorMap tq = map_bshd(a.q, a.B, a.S, a.Hq, C::D, a.q_row, kBQ3);
@@ -1513,10 +1477,10 @@ static void bwd3_launch_t(const AttnBwdArgs& g, cudaStream_t st) {
   CUtensorMap tv = map_bshd(a.v, a.B, a.S, a.Hk, C::D, a.v_row);
   CUtensorMap td = map_bshd(g.dout, a.B, a.S, a.Hq, C::D, g.do_row, kBQ3);
   CUtensorMap tdq = map_dq_acc(g.dq_acc, a.B, a.S, a.Hq, C::D);
-  set_max_smem_once(reinterpret_cast<const void*>(attn_bwd3_kernel<D, kPolyMask>), C::kSmem);
+  set_max_smem_once(reinterpret_cast<const void*>(attn_bwd3_kernel<D>), C::kSmem);
   static const int regs = [] {
     cudaFuncAttributes fa;
-    PLG_CUDA_CHECK(cudaFuncGetAttributes(&fa, attn_bwd3_kernel<D, kPolyMask>));
+    PLG_CUDA_CHECK(cudaFuncGetAttributes(&fa, attn_bwd3_kernel<D>));
     return fa.numRegs;
   }();
   if (regs != kB3RegsLaunch)
@@ -1536,8 +1500,7 @@ static void bwd3_launch_t(const AttnBwdArgs& g, cudaStream_t st) {
   PLG_CUDA_CHECK(cudaGetLastError());
   const long long ctas = static_cast<long long>((a.S + BKV - 1) / BKV) * a.Hk * a.B;
   if (ctas > 0x7fffffffLL) throw std::invalid_argument("attention: problem too large for one launch");
-  attn_bwd3_kernel<D, kPolyMask><<<static_cast<unsigned>(ctas), kB3Threads, C::kSmem, st>>>(tq, tk, tv, td,
-                                                                                          tdq, g);
+  attn_bwd3_kernel<D><<<static_cast<unsigned>(ctas), kB3Threads, C::kSmem, st>>>(tq, tk, tv, td, tdq, g);
   PLG_CUDA_CHECK(cudaGetLastError());
   const long long tokens = static_cast<long long>(a.B) * a.S;
   const long long groups = tokens * (a.Hq * C::D / 8);
