@@ -824,11 +824,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 //   S^T_j  = K Q_j^T   -> TMEM S_b   (128 keys x 64 queries, fp32)
 //   dP^T_j = V dO_j^T  -> TMEM dP_b
 //   compute warps: P^T = exp2(S^T * scale*log2e - lse*log2e) -> bf16 into S_b,
-//                  dS^T = P^T (dP^T * scale - delta * scale) -> bf16 into smem
-//   dV += P^T dO_j  (A from TMEM)      dK += dS^T Q_j
+//                  dS^T = P^T (dP^T * scale - delta * scale) -> bf16 into S_b
+//                  and into smem
+//   dV += P^T dO_j, dK += dS^T Q_j  (A operands from TMEM)
 //   dQ^T_j = K^T dS^T_j -> TMEM dP_b (d x 64 queries), read out by the drain
-//   warps and added into the fp32 dQ workspace with vector-free coalesced
-//   reductions (a warp covers 32 consecutive d of one query row).
+//   warps and added into the fp32 dQ workspace (red.global, a warp covering 32
+//   consecutive d of one query row, or a staged bulk tensor reduce-add).
+// Shared-memory bandwidth is the limiter at these N = 64 MMA shapes (operand
+// reads of the SS MMAs plus the TMA writes and dS stores are ~2 KB per 16 queries
+// and keys), so the A operands that can come from TMEM do.
 // The MMA warp issues S/dP of step j+1 before dV/dK/dQ of step j, so the
 // compute warps work on step j+1 while the tensor core finishes step j.
 // TMEM: dV [0,128), dK [128,256), S_b at 256+128b, dP_b at 320+128b.
@@ -888,7 +892,17 @@ __device__ __forceinline__ void trace_ev(long long* trace, int ev, int j) {
     trace[ev * kAttnTraceSteps + j] = clock64();
 }
 
-template <int kD>
+// fp32 add into global memory without a return value (a reduction at L2)
+__device__ __forceinline__ void red_add_f32(float* p, float v) {
+  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+
+// kDqRed: the drain warps add their dQ^T rows into the fp32 workspace with
+// red.global (32 consecutive d of one query per instruction) instead of staging them
+// in shared memory for one bulk tensor reduce-add; the kernel's shared-memory traffic
+// (MMA operand reads, TMA writes, dS stores) is its limiter, and staging adds a write
+// and a read of 32 KB per step.
+template <int kD, bool kDqRed>
 __global__ void __launch_bounds__(kB3Threads, 1)
     attn_bwd3_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -1060,18 +1074,19 @@ __global__ void __launch_bounds__(kB3Threads, 1)
         tc_fence_after();
         const uint64_t mQ = make_smem_desc(smem_u32(sQ(s)), C::kQBox, 1024, kLayoutSW128);
         const uint64_t mDO = make_smem_desc(smem_u32(sDO(s)), C::kQBox, 1024, kLayoutSW128);
-        const uint64_t kDS = make_smem_desc(smem_u32(sDS(bj)), 16, 1024, kLayoutSW128);
         const uint64_t mDS = make_smem_desc(smem_u32(sDS(bj)), kBox, 1024, kLayoutSW128);
         const uint32_t acc0 = j > 0 ? 1u : 0u;
         if (leader) {
+          // A operands from TMEM: P^T and dS^T of query half h (16 queries per k-step,
+          // 8 packed columns) sit at S_b columns 32h.. and 32h + 16..
 #pragma unroll
           for (int kk = 0; kk < kBQ3 / 16; ++kk)
-            tc_mma_ts(tmem + C::kTdV, tmem + C::kTS0 + 128 * bj + kk * 8, desc_advance(mDO, kk * 2048),
-                      id_kv, kk > 0 ? 1u : acc0);
+            tc_mma_ts(tmem + C::kTdV, tmem + C::kTS0 + 128 * bj + (kk >> 1) * 32 + (kk & 1) * 8,
+                      desc_advance(mDO, kk * 2048), id_kv, kk > 0 ? 1u : acc0);
 #pragma unroll
           for (int kk = 0; kk < kBQ3 / 16; ++kk)
-            tc_mma_ss(tmem + C::kTdK, desc_advance(kDS, kk * 32), desc_advance(mQ, kk * 2048), id_kv,
-                      kk > 0 ? 1u : acc0);
+            tc_mma_ts(tmem + C::kTdK, tmem + C::kTS0 + 128 * bj + (kk >> 1) * 32 + 16 + (kk & 1) * 8,
+                      desc_advance(mQ, kk * 2048), id_kv, kk > 0 ? 1u : acc0);
           tc_commit(&qd_empty[s]);
 #pragma unroll
           for (int kk = 0; kk < BKV / 16; ++kk)
@@ -1114,6 +1129,18 @@ __global__ void __launch_bounds__(kB3Threads, 1)
       if (lane == 0) mbar_arrive(&dq_free[bj]);
       if (lane == 0 && quad == 0) trace_ev(g.trace, 7, j);
       if (!live) continue;
+      if constexpr (kDqRed) {
+        const int h = hk * G + j % G, q0 = (qb_lo + j / G) * kBQ3;
+        const long long qstride = static_cast<long long>(a.Hq) * D;
+        float* dst = g.dq_acc + (static_cast<long long>(b) * a.S + q0) * qstride +
+                     static_cast<long long>(h) * D + quad * 32 + lane;
+        const int nq = min(kBQ3, a.S - q0);
+#pragma unroll
+        for (int c = 0; c < kBQ3; ++c)
+          if (c < nq) red_add_f32(dst + c * qstride, __uint_as_float(v[c]));
+        if (lane == 0 && quad == 0) trace_ev(g.trace, 8, j);
+        continue;
+      }
       // stage this warp's [64 q x 32 d] slice and reduce-add it into the fp32
       // workspace with one bulk tensor operation (rows past S are clipped)
       if (lane == 0) bulk_wait_group_read<0>();  // previous slice has left smem
@@ -1189,9 +1216,11 @@ __global__ void __launch_bounds__(kB3Threads, 1)
         dk[c / 2 + 1] = pack_bf16x2(t2, t3);
       }
       if (lane == 0 && warp == 0) trace_ev(g.trace, 10, j);
-      // P^T into this half's S columns (two bf16 per column), dS^T into this half's
-      // 64 bytes of the key row in smem (SW128 rows of 128 bytes)
-      tmem_st_32x32b_x16(trow + C::kTS0 + 128 * bj + half * (kHalf / 2), pk);
+      // P^T and dS^T (two bf16 per column) into the 32 S columns this warp has read
+      // itself (the other half's columns may still be unread), dS^T also into this
+      // half's 64 bytes of the key row in smem (SW128 rows of 128 bytes) for dQ
+      tmem_st_32x32b_x16(trow + C::kTS0 + 128 * bj + half * kHalf, pk);
+      tmem_st_32x32b_x16(trow + C::kTS0 + 128 * bj + half * kHalf + kHalf / 2, dk);
       uint8_t* ds_row = sDS(bj) + r * 128;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -1468,8 +1497,22 @@ static void fwd_launch_t(const AttnArgs& a, cudaStream_t st) {
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 
+template <int D, bool kDqRed>
+static void bwd3_launch_t(const AttnBwdArgs& g, cudaStream_t st);
+
 template <int D>
 static void bwd3_launch(const AttnBwdArgs& g, cudaStream_t st) {
+  // dQ accumulation: PLG_ATTN_DQ=red (red.global from registers) or tma (staged in
+  // shared memory, one bulk tensor reduce-add per warp and step)
+  static const bool red = [] {
+    const char* e = std::getenv("PLG_ATTN_DQ");
+    return !(e != nullptr && std::string(e) == "tma");
+  }();
+  return red ? bwd3_launch_t<D, true>(g, st) : bwd3_launch_t<D, false>(g, st);
+}
+
+template <int D, bool kDqRed>
+static void bwd3_launch_t(const AttnBwdArgs& g, cudaStream_t st) {
   using C = Bwd3<D>;
   const AttnArgs& a = g.f;
   CUtensorMap tq = map_bshd(a.q, a.B, a.S, a.Hq, C::D, a.q_row, kBQ3);
@@ -1477,10 +1520,10 @@ static void bwd3_launch(const AttnBwdArgs& g, cudaStream_t st) {
   CUtensorMap tv = map_bshd(a.v, a.B, a.S, a.Hk, C::D, a.v_row);
   CUtensorMap td = map_bshd(g.dout, a.B, a.S, a.Hq, C::D, g.do_row, kBQ3);
   CUtensorMap tdq = map_dq_acc(g.dq_acc, a.B, a.S, a.Hq, C::D);
-  set_max_smem_once(reinterpret_cast<const void*>(attn_bwd3_kernel<D>), C::kSmem);
+  set_max_smem_once(reinterpret_cast<const void*>(attn_bwd3_kernel<D, kDqRed>), C::kSmem);
   static const int regs = [] {
     cudaFuncAttributes fa;
-    PLG_CUDA_CHECK(cudaFuncGetAttributes(&fa, attn_bwd3_kernel<D>));
+    PLG_CUDA_CHECK(cudaFuncGetAttributes(&fa, attn_bwd3_kernel<D, kDqRed>));
     return fa.numRegs;
   }();
   if (regs != kB3RegsLaunch)
@@ -1500,7 +1543,8 @@ static void bwd3_launch(const AttnBwdArgs& g, cudaStream_t st) {
   PLG_CUDA_CHECK(cudaGetLastError());
   const long long ctas = static_cast<long long>((a.S + BKV - 1) / BKV) * a.Hk * a.B;
   if (ctas > 0x7fffffffLL) throw std::invalid_argument("attention: problem too large for one launch");
-  attn_bwd3_kernel<D><<<static_cast<unsigned>(ctas), kB3Threads, C::kSmem, st>>>(tq, tk, tv, td, tdq, g);
+  attn_bwd3_kernel<D, kDqRed><<<static_cast<unsigned>(ctas), kB3Threads, C::kSmem, st>>>(tq, tk, tv, td,
+                                                                                       tdq, g);
   PLG_CUDA_CHECK(cudaGetLastError());
   const long long tokens = static_cast<long long>(a.B) * a.S;
   const long long groups = tokens * (a.Hq * C::D / 8);
