@@ -828,11 +828,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 //                  and into smem
 //   dV += P^T dO_j, dK += dS^T Q_j  (A operands from TMEM)
 //   dQ^T_j = K^T dS^T_j -> TMEM dP_b (d x 64 queries), read out by the drain
-//   warps and added into the fp32 dQ workspace (red.global, a warp covering 32
-//   consecutive d of one query row, or a staged bulk tensor reduce-add).
-// Shared-memory bandwidth is the limiter at these N = 64 MMA shapes (operand
-// reads of the SS MMAs plus the TMA writes and dS stores are ~2 KB per 16 queries
-// and keys), so the A operands that can come from TMEM do.
+//   warps, staged in smem and added into the fp32 dQ workspace with one bulk
+//   tensor reduce-add per warp (red.global from registers measured 1.3x slower).
+// The A operands that can come from TMEM do (P^T, dS^T), which spares shared
+// memory the operand reads of dV and dK.
 // The MMA warp issues S/dP of step j+1 before dV/dK/dQ of step j, so the
 // compute warps work on step j+1 while the tensor core finishes step j.
 // TMEM: dV [0,128), dK [128,256), S_b at 256+128b, dP_b at 320+128b.
@@ -892,17 +891,7 @@ __device__ __forceinline__ void trace_ev(long long* trace, int ev, int j) {
     trace[ev * kAttnTraceSteps + j] = clock64();
 }
 
-// fp32 add into global memory without a return value (a reduction at L2)
-__device__ __forceinline__ void red_add_f32(float* p, float v) {
-  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
-}
-
-// kDqRed: the drain warps add their dQ^T rows into the fp32 workspace with
-// red.global (32 consecutive d of one query per instruction) instead of staging them
-// in shared memory for one bulk tensor reduce-add; the kernel's shared-memory traffic
-// (MMA operand reads, TMA writes, dS stores) is its limiter, and staging adds a write
-// and a read of 32 KB per step.
-template <int kD, bool kDqRed>
+template <int kD>
 __global__ void __launch_bounds__(kB3Threads, 1)
     attn_bwd3_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -1129,18 +1118,6 @@ __global__ void __launch_bounds__(kB3Threads, 1)
       if (lane == 0) mbar_arrive(&dq_free[bj]);
       if (lane == 0 && quad == 0) trace_ev(g.trace, 7, j);
       if (!live) continue;
-      if constexpr (kDqRed) {
-        const int h = hk * G + j % G, q0 = (qb_lo + j / G) * kBQ3;
-        const long long qstride = static_cast<long long>(a.Hq) * D;
-        float* dst = g.dq_acc + (static_cast<long long>(b) * a.S + q0) * qstride +
-                     static_cast<long long>(h) * D + quad * 32 + lane;
-        const int nq = min(kBQ3, a.S - q0);
-#pragma unroll
-        for (int c = 0; c < kBQ3; ++c)
-          if (c < nq) red_add_f32(dst + c * qstride, __uint_as_float(v[c]));
-        if (lane == 0 && quad == 0) trace_ev(g.trace, 8, j);
-        continue;
-      }
       // stage this warp's [64 q x 32 d] slice and reduce-add it into the fp32
       // workspace with one bulk tensor operation (rows past S are clipped)
       if (lane == 0) bulk_wait_group_read<0>();  // previous slice has left smem
@@ -1497,22 +1474,8 @@ static void fwd_launch_t(const AttnArgs& a, cudaStream_t st) {
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 
-template <int D, bool kDqRed>
-static void bwd3_launch_t(const AttnBwdArgs& g, cudaStream_t st);
-
 template <int D>
 static void bwd3_launch(const AttnBwdArgs& g, cudaStream_t st) {
-  // dQ accumulation: PLG_ATTN_DQ=red (red.global from registers) or tma (staged in
-  // shared memory, one bulk tensor reduce-add per warp and step)
-  static const bool red = [] {
-    const char* e = std::getenv("PLG_ATTN_DQ");
-    return !(e != nullptr && std::string(e) == "tma");
-  }();
-  return red ? bwd3_launch_t<D, true>(g, st) : bwd3_launch_t<D, false>(g, st);
-}
-
-template <int D, bool kDqRed>
-static void bwd3_launch_t(const AttnBwdArgs& g, cudaStream_t st) {
   using C = Bwd3<D>;
   const AttnArgs& a = g.f;
   CUtensorMap tq = map_bshd(a.q, a.B, a.S, a.Hq, C::D, a.q_row, kBQ3);
@@ -1520,10 +1483,10 @@ static void bwd3_launch_t(const AttnBwdArgs& g, cudaStream_t st) {
   CUtensorMap tv = map_bshd(a.v, a.B, a.S, a.Hk, C::D, a.v_row);
   CUtensorMap td = map_bshd(g.dout, a.B, a.S, a.Hq, C::D, g.do_row, kBQ3);
   CUtensorMap tdq = map_dq_acc(g.dq_acc, a.B, a.S, a.Hq, C::D);
-  set_max_smem_once(reinterpret_cast<const void*>(attn_bwd3_kernel<D, kDqRed>), C::kSmem);
+  set_max_smem_once(reinterpret_cast<const void*>(attn_bwd3_kernel<D>), C::kSmem);
   static const int regs = [] {
     cudaFuncAttributes fa;
-    PLG_CUDA_CHECK(cudaFuncGetAttributes(&fa, attn_bwd3_kernel<D, kDqRed>));
+    PLG_CUDA_CHECK(cudaFuncGetAttributes(&fa, attn_bwd3_kernel<D>));
     return fa.numRegs;
   }();
   if (regs != kB3RegsLaunch)
@@ -1543,7 +1506,7 @@ static void bwd3_launch_t(const AttnBwdArgs& g, cudaStream_t st) {
   PLG_CUDA_CHECK(cudaGetLastError());
   const long long ctas = static_cast<long long>((a.S + BKV - 1) / BKV) * a.Hk * a.B;
   if (ctas > 0x7fffffffLL) throw std::invalid_argument("attention: problem too large for one launch");
-  attn_bwd3_kernel<D, kDqRed><<<static_cast<unsigned>(ctas), kB3Threads, C::kSmem, st>>>(tq, tk, tv, td,
+  attn_bwd3_kernel<D><<<static_cast<unsigned>(ctas), kB3Threads, C::kSmem, st>>>(tq, tk, tv, td,
                                                                                        tdq, g);
   PLG_CUDA_CHECK(cudaGetLastError());
   const long long tokens = static_cast<long long>(a.B) * a.S;
