@@ -1264,53 +1264,56 @@ __global__ void __launch_bounds__(kB3Threads, 1)
   }
 }
 
-// Backward pre-pass for the head_dim-128 kernel: per (b, h) row of the stats
-// workspace [B*Hq][2][S64], -lse*log2(e) and -scale * rowsum(dO * O); queries
-// beyond S get -inf and 0. Also zeroes the fp32 dQ workspace row of each (b, s, h).
-// One warp per (b, s, h), D / 32 channels per lane.
+// Backward pre-pass of the pipelined kernel: per (b, h) row of the stats workspace
+// [B*Hq][2][S64], -lse*log2(e) and -scale * rowsum(dO * O); queries beyond S get -inf
+// and 0. Half a warp per (b, s, h) (D / 16 channels per lane, 16 or 8 bytes), two rows
+// per warp; position fastest, so consecutive rows read consecutive lse and write
+// consecutive stats.
 template <int D>
 __global__ void attn_bwd_stats_kernel(const __nv_bfloat16* __restrict__ o, long long o_row,
                                       const __nv_bfloat16* __restrict__ dout, long long do_row,
                                       const float* __restrict__ lse, float* __restrict__ stats,
-                                      float* __restrict__ dq_acc, int B, int S, int S64, int H,
-                                      float scale) {
+                                      int B, int S, int S64, int H, float scale) {
   static_assert(D == 64 || D == 128, "stats head_dim");
-  const long long wid = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
+  const long long row_id = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;
+  const int l16 = threadIdx.x & 15;
   const long long total = static_cast<long long>(B) * S64 * H;
-  if (wid >= total) return;
-  // position fastest: consecutive warps write consecutive stats and read consecutive lse
-  const int s = static_cast<int>(wid % S64);
-  const long long bh = wid / S64;
+  const bool valid = row_id < total;
+  const long long rid = valid ? row_id : 0;  // every lane takes part in the shuffles
+  const int s = static_cast<int>(rid % S64);
+  const long long bh = rid / S64;
   const int h = static_cast<int>(bh % H), bb = static_cast<int>(bh / H);
-  float* row = stats + (static_cast<long long>(bb) * H + h) * 2 * S64;
-  if (s >= S) {
-    if (lane == 0) {
+  float acc = 0.f;
+  const long long tok = static_cast<long long>(bb) * S + s;
+  if (valid && s < S) {
+    if constexpr (D == 128) {
+      const uint4 ov = *reinterpret_cast<const uint4*>(o + tok * o_row + h * D + l16 * 8);
+      const uint4 dv = *reinterpret_cast<const uint4*>(dout + tok * do_row + h * D + l16 * 8);
+      const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w}, dw[4] = {dv.x, dv.y, dv.z, dv.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 x = unpack_bf16x2(ow[e]), y = unpack_bf16x2(dw[e]);
+        acc = fmaf(x.x, y.x, fmaf(x.y, y.y, acc));
+      }
+    } else {
+      const uint2 ov = *reinterpret_cast<const uint2*>(o + tok * o_row + h * D + l16 * 4);
+      const uint2 dv = *reinterpret_cast<const uint2*>(dout + tok * do_row + h * D + l16 * 4);
+      const float2 x0 = unpack_bf16x2(ov.x), x1 = unpack_bf16x2(ov.y);
+      const float2 y0 = unpack_bf16x2(dv.x), y1 = unpack_bf16x2(dv.y);
+      acc = x0.x * y0.x + x0.y * y0.y + x1.x * y1.x + x1.y * y1.y;
+    }
+  }
+#pragma unroll
+  for (int off = 8; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (valid && l16 == 0) {
+    float* row = stats + (static_cast<long long>(bb) * H + h) * 2 * S64;
+    if (s >= S) {
       row[s] = -INFINITY;
       row[S64 + s] = 0.f;
+    } else {
+      row[s] = -lse[(static_cast<long long>(bb) * H + h) * S + s] * kLog2e;
+      row[S64 + s] = -acc * scale;
     }
-    return;
-  }
-  const long long tok = static_cast<long long>(bb) * S + s;
-  float acc;
-  if constexpr (D == 128) {
-    const uint2 ov = *reinterpret_cast<const uint2*>(o + tok * o_row + h * D + lane * 4);
-    const uint2 dv = *reinterpret_cast<const uint2*>(dout + tok * do_row + h * D + lane * 4);
-    const float2 o0 = unpack_bf16x2(ov.x), o1 = unpack_bf16x2(ov.y);
-    const float2 d0 = unpack_bf16x2(dv.x), d1 = unpack_bf16x2(dv.y);
-    acc = o0.x * d0.x + o0.y * d0.y + o1.x * d1.x + o1.y * d1.y;
-    reinterpret_cast<float4*>(dq_acc + (tok * H + h) * D)[lane] = make_float4(0.f, 0.f, 0.f, 0.f);
-  } else {
-    const float2 o0 = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(o + tok * o_row + h * D + lane * 2));
-    const float2 d0 =
-        unpack_bf16x2(*reinterpret_cast<const uint32_t*>(dout + tok * do_row + h * D + lane * 2));
-    acc = o0.x * d0.x + o0.y * d0.y;
-    reinterpret_cast<float2*>(dq_acc + (tok * H + h) * D)[lane] = make_float2(0.f, 0.f);
-  }
-  acc = warp_sum(acc);
-  if (lane == 0) {
-    row[s] = -lse[(static_cast<long long>(bb) * H + h) * S + s] * kLog2e;
-    row[S64 + s] = -acc * scale;
   }
 }
 
@@ -1499,10 +1502,12 @@ static void bwd3_launch(const AttnBwdArgs& g, cudaStream_t st) {
       (reinterpret_cast<uintptr_t>(a.o) & 15) || (reinterpret_cast<uintptr_t>(g.dout) & 15) ||
       (reinterpret_cast<uintptr_t>(g.dq) & 15))
     throw std::invalid_argument("attention backward: o, dout and dq rows must be 16-byte aligned");
-  attn_bwd_stats_kernel<D><<<(srows * 32 + 255) / 256, 256, 0, st>>>(
+  PLG_CUDA_CHECK(cudaMemsetAsync(g.dq_acc, 0,
+                                  sizeof(float) * static_cast<size_t>(a.B) * a.S * a.Hq * D, st));
+  attn_bwd_stats_kernel<D><<<(srows * 16 + 255) / 256, 256, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(a.o), a.o_row,
-      reinterpret_cast<const __nv_bfloat16*>(g.dout), g.do_row, a.lse, g.delta, g.dq_acc, a.B, a.S,
-      S64, a.Hq, a.scale);
+      reinterpret_cast<const __nv_bfloat16*>(g.dout), g.do_row, a.lse, g.delta, a.B, a.S, S64, a.Hq,
+      a.scale);
   PLG_CUDA_CHECK(cudaGetLastError());
   const long long ctas = static_cast<long long>((a.S + BKV - 1) / BKV) * a.Hk * a.B;
   if (ctas > 0x7fffffffLL) throw std::invalid_argument("attention: problem too large for one launch");
