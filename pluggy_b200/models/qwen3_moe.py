@@ -29,7 +29,7 @@ from pluggy_b200.models.common import (GQAttention, RotaryEmbedding, SwiGLU, def
                                        norm_eps, position_ids_for)
 from pluggy_b200.models.qwen3 import Qwen3TransformerBlock
 from pluggy_b200.ops.linear import WeightCache, linear
-from pluggy_b200.ops.moe import moe_expert_ffn
+from pluggy_b200.ops.moe import expert_histogram, moe_expert_ffn
 
 
 class Qwen3MoeTopKRouter(nn.Module):
@@ -116,7 +116,7 @@ def load_balancing_loss(router_logits, num_experts: int, top_k: int):
     _, top = torch.topk(probs, top_k, dim=-1)
     # the reference's one_hot(top, E).mean(0) summed over the k slots: the fraction of
     # (token, slot) pairs routed to each expert, counted without the [T, k, E] one-hot
-    frac = torch.bincount(top.reshape(-1), minlength=num_experts).float() / top.shape[0]
+    frac = expert_histogram(top, num_experts).float() / top.shape[0]
     return (frac * probs.mean(dim=0)).sum() * num_experts
 
 
@@ -206,7 +206,7 @@ class Qwen3Moe(nn.Module):
                 idx = getattr(b.ffn, "last_top_idx", None) if isinstance(b.ffn, Qwen3MoeSparseMLP) \
                     else None
                 if idx is not None:
-                    counts += torch.bincount(idx.reshape(-1), minlength=self.num_experts).float()
+                    counts += expert_histogram(idx, self.num_experts).float()
         self.last_tokens_per_expert = counts
 
     def aux_loss(self):

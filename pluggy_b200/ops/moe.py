@@ -20,6 +20,15 @@ import torch.nn.functional as F
 from pluggy_b200.ops.elementwise import swiglu_mul
 
 
+def expert_histogram(idx: torch.Tensor, n: int) -> torch.Tensor:
+    """int64 [n]: how many entries of ``idx`` (values in [0, n)) equal each value.
+    A scatter-add, so it stays on the device: ``torch.bincount`` on CUDA reads the
+    input's minimum and maximum back to the host to size its output."""
+    flat = idx.reshape(-1).to(torch.int64)
+    out = torch.zeros(n, dtype=torch.int64, device=idx.device)
+    return out.scatter_add_(0, flat, torch.ones_like(flat))
+
+
 def _expert_ffn_loop(hidden, top_indices, top_weights, gate_up_proj, down_proj):
     T, H = hidden.shape
     E = gate_up_proj.shape[0]
@@ -50,7 +59,7 @@ def _expert_ffn_sorted(hidden, top_indices, top_weights, gate_up_proj, down_proj
     w = top_weights.reshape(-1)
     order = torch.argsort(exp, stable=True)
     s_tok, s_w, s_exp = tok[order], w[order], exp[order]
-    counts = torch.bincount(exp, minlength=E)
+    counts = expert_histogram(exp, E)
     x = hidden[s_tok]
     y = grouped_swiglu_ffn(x, s_exp, counts, gate_up_proj, down_proj, gu_lowp, dn_lowp)
     y = y * s_w.unsqueeze(1).to(y.dtype)

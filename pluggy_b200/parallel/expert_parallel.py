@@ -34,7 +34,7 @@ import torch
 import torch.nn as nn
 
 from pluggy_b200.core.collective import all_gather, all_to_all
-from pluggy_b200.ops.moe import moe_expert_ffn
+from pluggy_b200.ops.moe import expert_histogram, moe_expert_ffn
 
 
 class _AllToAllV(torch.autograd.Function):
@@ -81,14 +81,14 @@ class EPExperts(nn.Module):
         if self.comm is not None:
             from pluggy_b200.comm.ep_fused import ToOwners, ToSources
 
-            C = self.comm.exchange_counts(torch.bincount(exp, minlength=self.num_experts))
+            C = self.comm.exchange_counts(expert_histogram(exp, self.num_experts))
             pl = self.comm.plan(C)
             lc = torch.as_tensor(pl["local_counts"].reshape(-1), dtype=torch.int64)
             r_exp = torch.repeat_interleave(torch.arange(self.local_experts).repeat(n), lc).to(h.device)
             x = ToOwners.apply(h[s_tok].contiguous(), self.comm, pl)
             back_fn = lambda y: ToSources.apply(y, self.comm, pl)  # noqa: E731
         else:
-            send_counts = torch.bincount(s_dest, minlength=n)
+            send_counts = expert_histogram(s_dest, n)
             recv_counts = all_to_all(send_counts.clone(), self.mesh, self.dim)
             send, recv = send_counts.tolist(), recv_counts.tolist()
             # local expert ids of the pairs this rank will receive (no gradient)
