@@ -301,17 +301,9 @@ __global__ void __launch_bounds__(kCeThreads, 2) ce_rows_kernel(
       if (cap) f[j] = softcap * tanhf(f[j] / softcap);
       lm = fmaxf(lm, f[j]);
     }
-    // half of the exponentials on the FMA pipe (the SFU is this loop's limiter next to
-    // the row's HBM traffic); arguments are <= 0, and the polynomial's -126 clamp only
-    // adds ~1e-38 terms to the sum
-    float e[8];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) e[j] = fast_exp2((f[j] - lm) * kLog2e);
-    exp2_poly2((f[4] - lm) * kLog2e, (f[5] - lm) * kLog2e, e[4], e[5]);
-    exp2_poly2((f[6] - lm) * kLog2e, (f[7] - lm) * kLog2e, e[6], e[7]);
     float acc = s * fast_exp2((m - lm) * kLog2e);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc += e[j];
+    for (int j = 0; j < 8; ++j) acc += fast_exp2((f[j] - lm) * kLog2e);
     m = lm;
     s = acc;
   }
@@ -396,13 +388,7 @@ __global__ void __launch_bounds__(kCeThreads, 2) ce_rows_kernel(
         a = softcap * ta; b = softcap * tb;
         ca = 1.f - ta * ta; cb = 1.f - tb * tb;
       }
-      float pa, pb;
-      if (j >= 2) {
-        exp2_poly2((a - lse) * kLog2e, (b - lse) * kLog2e, pa, pb);
-      } else {
-        pa = fast_exp2((a - lse) * kLog2e);
-        pb = fast_exp2((b - lse) * kLog2e);
-      }
+      float pa = fast_exp2((a - lse) * kLog2e), pb = fast_exp2((b - lse) * kLog2e);
       const int c = i * 8 + j * 2;
       if (c == lab) pa -= 1.f;
       if (c + 1 == lab) pb -= 1.f;
