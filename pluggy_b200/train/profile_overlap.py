@@ -95,6 +95,36 @@ def analyze(trace_path: str) -> dict:
     }
 
 
+SYNC_MARKERS = ("cudaStreamSynchronize", "cudaDeviceSynchronize", "cudaEventSynchronize",
+                "aten::_local_scalar_dense", "aten::item")
+
+
+def idle_gaps(trace_path: str, top: int = 8) -> dict:
+    """Where the device idles: the ``top`` longest gaps between consecutive kernels
+    (with the kernels on both sides) and the host calls that wait for the device."""
+    with open(trace_path) as f:
+        tr = json.load(f)
+    events = tr["traceEvents"] if isinstance(tr, dict) else tr
+    ks = sorted((float(e["ts"]), float(e["ts"]) + float(e["dur"]), e["name"]) for e in events
+                if e.get("ph") == "X" and e.get("cat") in ("kernel", "gpu_memcpy", "gpu_memset")
+                and "dur" in e)
+    gaps = []
+    end, last = None, None
+    for t0, t1, name in ks:
+        if end is not None and t0 > end:
+            gaps.append((t0 - end, short_name(last), short_name(name)))
+        if end is None or t1 > end:
+            end, last = t1, name
+    gaps.sort(reverse=True)
+    syncs = defaultdict(lambda: [0, 0.0])
+    for e in events:
+        if e.get("ph") == "X" and any(m == e.get("name") for m in SYNC_MARKERS):
+            syncs[e["name"]][0] += 1
+            syncs[e["name"]][1] += float(e.get("dur", 0.0))
+    return {"gaps_us": [(round(g, 1), a, b) for g, a, b in gaps[:top]],
+            "host_waits": {k: {"calls": v[0], "us": round(v[1], 1)} for k, v in syncs.items()}}
+
+
 def short_name(name: str) -> str:
     """Kernel function name without namespaces, template arguments or parameters."""
     n = name.replace("(anonymous namespace)::", "").split("(")[0]
@@ -130,20 +160,23 @@ def kernel_table(trace_path: str, steps: int = 1) -> list[dict]:
 
 
 def capture(config, warmup: int, steps: int, out: str, rank: int, local_rank: int,
-            world: int) -> str:
-    """Profile ``steps`` training steps after ``warmup`` (``config``: dict or JSON path)."""
+            world: int, raw: bool = False) -> str:
+    """Profile ``steps`` training steps after ``warmup`` (``config``: dict or JSON path).
+    ``raw`` runs the step without the per-step timing synchronisations, as the
+    throughput benchmark does."""
     import torch
     from torch.profiler import ProfilerActivity, profile
 
     from pluggy_b200.train.trainer import Trainer
 
     tr = Trainer(config, rank=rank, local_rank=local_rank, world_size=world, benchmark=True)
+    step = tr._train_step if raw else tr.train_step
     for _ in range(warmup):
-        tr.train_step()
+        step()
     acts = [ProfilerActivity.CPU] + ([ProfilerActivity.CUDA] if torch.cuda.is_available() else [])
     with profile(activities=acts) as prof:
         for _ in range(steps):
-            tr.train_step()
+            step()
         if torch.cuda.is_available():
             torch.cuda.synchronize()
     path = out if world == 1 else f"{os.path.splitext(out)[0]}_rank{rank}.json"
@@ -166,17 +199,20 @@ def main(argv=None) -> None:
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--steps", type=int, default=2)
     p.add_argument("--out", default="overlap_trace.json")
+    p.add_argument("--raw", action="store_true",
+                   help="profile the step without its timing synchronisations (as bench.py runs it)")
     p.add_argument("--kernels", type=int, default=0,
                    help="also print the N largest kernels (device ms per step)")
     a = p.parse_args(argv)
     rank, local_rank, world = init_distributed()
     try:
-        path = capture(a.config, a.warmup, a.steps, a.out, rank, local_rank, world)
+        path = capture(a.config, a.warmup, a.steps, a.out, rank, local_rank, world, raw=a.raw)
         rep = analyze(path)
         if rank == 0:
             print(json.dumps({k: v for k, v in rep.items() if k != "per_kernel_exposed_us"}, indent=1))
             for k, v in list(rep["per_kernel_exposed_us"].items())[:10]:
                 print(f"  exposed {v:10.1f} us  {k}")
+            print(json.dumps(idle_gaps(path), indent=1))
             if a.kernels:
                 rows = kernel_table(path, a.steps)
                 print(f"{'kernel':48s} {'ms/step':>9s} {'launches':>9s} {'share':>7s}")
