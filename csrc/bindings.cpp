@@ -380,13 +380,19 @@ void multi_scale(const at::Tensor& table, int64_t ntensors, int64_t total_chunks
 
 void adamw_multi(const at::Tensor& table, int64_t ntensors, int64_t total_chunks, double lr,
                  double beta1, double beta2, double eps, double wd, double bc1, double bc2,
-                 const c10::optional<at::Tensor>& grad_scale) {
+                 const c10::optional<at::Tensor>& grad_scale,
+                 const c10::optional<at::Tensor>& hyper) {
   const c10::cuda::CUDAGuard guard(table.device());
+  if (hyper.has_value())
+    TORCH_CHECK(hyper->is_cuda() && hyper->scalar_type() == at::kFloat && hyper->numel() >= 3 &&
+                    hyper->is_contiguous(),
+                "adamw_multi: hyper must be a contiguous fp32 device tensor of (lr, bc1, bc2)");
   plg::adamw_multi(table.data_ptr<int64_t>(), static_cast<int>(ntensors), total_chunks,
                    static_cast<float>(lr), static_cast<float>(beta1), static_cast<float>(beta2),
                    static_cast<float>(eps), static_cast<float>(wd), static_cast<float>(bc1),
                    static_cast<float>(bc2),
-                   grad_scale.has_value() ? grad_scale->data_ptr<float>() : nullptr, cur_stream());
+                   grad_scale.has_value() ? grad_scale->data_ptr<float>() : nullptr,
+                   hyper.has_value() ? hyper->data_ptr<float>() : nullptr, cur_stream());
 }
 
 plg::AttnArgs attn_args(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
@@ -857,7 +863,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("exp2_poly_eval", &exp2_poly_eval_b);
   m.def("multi_sumsq", &multi_sumsq);
   m.def("multi_scale", &multi_scale);
-  m.def("adamw_multi", &adamw_multi);
+  m.def("adamw_multi", &adamw_multi, py::arg("table"), py::arg("ntensors"), py::arg("total_chunks"),
+        py::arg("lr"), py::arg("beta1"), py::arg("beta2"), py::arg("eps"), py::arg("wd"),
+        py::arg("bc1"), py::arg("bc2"), py::arg("grad_scale") = py::none(),
+        py::arg("hyper") = py::none());
   m.def("attn_fwd", &attn_fwd);
   m.def("attn_bwd", &attn_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"),
         py::arg("lse"), py::arg("dout"), py::arg("dq"), py::arg("dk"), py::arg("dv"),

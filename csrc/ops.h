@@ -139,7 +139,7 @@ void multi_scale(const int64_t* table, int ntensors, long long total_chunks, con
 // table rows: [param f32*, grad f32*, m f32*, v f32*, shadow bf16* (or 0), numel, chunk_start]
 void adamw_multi(const int64_t* table, int ntensors, long long total_chunks, float lr, float beta1,
                  float beta2, float eps, float weight_decay, float bc1, float bc2,
-                 const float* grad_scale, cudaStream_t stream);
+                 const float* grad_scale, const float* hyper, cudaStream_t stream);
 constexpr int kOptChunk = 65536;
 
 // ---------------------------------------------------------------- attention

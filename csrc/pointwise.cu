@@ -514,8 +514,16 @@ __global__ void __launch_bounds__(512) adamw_kernel(const int64_t* __restrict__ 
                                                     int ntensors, long long total_chunks,
                                                     float lr, float b1, float b2, float eps,
                                                     float wd, float bc1, float bc2,
-                                                    const float* __restrict__ gscale) {
+                                                    const float* __restrict__ gscale,
+                                                    const float* __restrict__ hyper) {
   const float scale = gscale ? *gscale : 1.f;
+  // device-resident (lr, bc1, bc2) when given: a step replayed from a CUDA graph reads
+  // the values the host wrote for this step instead of the ones baked into the launch
+  if (hyper != nullptr) {
+    lr = hyper[0];
+    bc1 = hyper[1];
+    bc2 = hyper[2];
+  }
   const float step = lr / bc1;
   const float rbc2 = rsqrtf(bc2);
   const float decay = 1.f - lr * wd;
@@ -803,11 +811,11 @@ void multi_scale(const int64_t* table, int ntensors, long long total_chunks, con
 
 void adamw_multi(const int64_t* table, int ntensors, long long total_chunks, float lr, float beta1,
                  float beta2, float eps, float weight_decay, float bc1, float bc2,
-                 const float* grad_scale, cudaStream_t st) {
+                 const float* grad_scale, const float* hyper, cudaStream_t st) {
   if (total_chunks <= 0) return;
   adamw_kernel<<<grid_for(total_chunks, 1), 512, 0, st>>>(table, ntensors, total_chunks, lr, beta1,
                                                          beta2, eps, weight_decay, bc1, bc2,
-                                                         grad_scale);
+                                                         grad_scale, hyper);
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 

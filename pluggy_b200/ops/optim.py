@@ -3,10 +3,15 @@
 Each op is ONE launch over every tensor of the list: a small int64 table of
 (pointers, numel, first chunk) is built on the host, copied with a pinned
 non-blocking H2D copy, and the kernel grid-strides over 64K-element chunks,
-locating each chunk's tensor by binary search in the table.
+locating each chunk's tensor by binary search in the table. Tables are kept by
+content (the same pointers give the same table), so a steady-state step uploads
+nothing, and a step captured into a CUDA graph keeps the table it was captured
+with alive.
 """
 
 from __future__ import annotations
+
+from collections import OrderedDict
 
 import torch
 
@@ -15,13 +20,28 @@ from pluggy_b200.ops._ext import ext
 CHUNK = 65536
 
 
+_TABLES: OrderedDict = OrderedDict()
+_TABLES_MAX = 64
+
+
 def _table(rows: list[list[int]], numels: list[int], device) -> tuple[torch.Tensor, int]:
     data, start = [], 0
     for r, n in zip(rows, numels, strict=True):
         data.append(r + [n, start])
         start += (n + CHUNK - 1) // CHUNK
-    t = torch.tensor(data, dtype=torch.int64).pin_memory()
-    return t.to(device, non_blocking=True), start
+    key = (str(device), tuple(tuple(r) for r in data))
+    hit = _TABLES.get(key)
+    if hit is not None:
+        _TABLES.move_to_end(key)
+        return hit[1], start
+    host = torch.tensor(data, dtype=torch.int64).pin_memory()
+    dev = host.to(device, non_blocking=True)
+    # the pinned source stays referenced: a copy captured into a CUDA graph reads it
+    # again on every replay
+    _TABLES[key] = (host, dev)
+    if len(_TABLES) > _TABLES_MAX and not torch.cuda.is_current_stream_capturing():
+        _TABLES.popitem(last=False)
+    return dev, start
 
 
 def _ptr(t: torch.Tensor | None) -> int:
@@ -48,7 +68,10 @@ def multi_tensor_scale_(tensors: list[torch.Tensor], coef: torch.Tensor) -> None
 
 
 def adamw_step(params, grads, exp_avgs, exp_avg_sqs, shadows, *, lr, beta1, beta2, eps,
-               weight_decay, bias_correction1, bias_correction2, grad_scale=None) -> None:
+               weight_decay, bias_correction1, bias_correction2, grad_scale=None,
+               hyper=None) -> None:
+    """``hyper``: optional fp32 device tensor (lr, bias_correction1, bias_correction2)
+    read by the kernel in place of the scalar arguments."""
     rows, numels = [], []
     for p, g, m, v, s in zip(params, grads, exp_avgs, exp_avg_sqs, shadows, strict=True):
         if p.numel() == 0:
@@ -62,4 +85,5 @@ def adamw_step(params, grads, exp_avgs, exp_avg_sqs, shadows, *, lr, beta1, beta
     table, chunks = _table(rows, numels, params[0].device)
     gs = None if grad_scale is None else grad_scale.reshape(1).float()
     ext().adamw_multi(table, len(rows), chunks, float(lr), float(beta1), float(beta2), float(eps),
-                      float(weight_decay), float(bias_correction1), float(bias_correction2), gs)
+                      float(weight_decay), float(bias_correction1), float(bias_correction2), gs,
+                      hyper)

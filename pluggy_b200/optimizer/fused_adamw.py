@@ -13,6 +13,9 @@ frameworks unchanged. Only ``step()`` differs:
   bf16 copy of each updated param into a registered shadow tensor (the bf16
   weights the GEMMs read), replacing a separate cast pass.
 * CPU params: the exact AdamW math in eager torch (oracle / gloo tests).
+* CUDA-graph steps (``use_device_hyper``): the kernel reads (lr, bc1, bc2) from a
+  per-group device tensor that :meth:`advance` fills on the host before each replay,
+  and :meth:`step` (run once, under capture) leaves the step counts to ``advance``.
 
 Math (decoupled weight decay, PyTorch's formulation):
 ``p -= lr*wd*p; m = b1*m + (1-b1)*g; v = b2*v + (1-b2)*g^2;
@@ -35,6 +38,35 @@ class FusedAdamW(torch.optim.AdamW):
         self.use_kernel = True if fused is None else bool(fused)
         self._grad_scale: torch.Tensor | None = None
         self._shadows: dict[int, torch.Tensor] = {}
+        self._hyper: list[torch.Tensor] | None = None
+
+    # ------------------------------------------------------- CUDA-graph steps
+    def use_device_hyper(self, device) -> None:
+        """Switch to device-resident (lr, bc1, bc2) per param group (see :meth:`advance`).
+        Every param must already have its state (run one eager step first)."""
+        assert all(len(self.state[p]) > 0 for g in self.param_groups for p in g["params"]), (
+            "use_device_hyper: run an eager step first so every param has its AdamW state")
+        self._hyper = [torch.zeros(3, dtype=torch.float32, device=device)
+                       for _ in self.param_groups]
+
+    @torch.no_grad()
+    def advance(self) -> None:
+        """The host half of one step in device-hyper mode: count the step and upload
+        this step's (lr, bc1, bc2) of each group (a fresh pinned buffer per upload, so an
+        upload still queued behind earlier work is never overwritten)."""
+        assert self._hyper is not None, "advance() needs use_device_hyper()"
+        for group, hyper in zip(self.param_groups, self._hyper, strict=True):
+            ps = group["params"]
+            if not ps:
+                continue
+            for p in ps:
+                self.state[p]["step"] += 1
+            step = float(self.state[ps[0]]["step"])
+            b1, b2 = group["betas"]
+            lr = group["lr"]
+            lr = float(lr) if not torch.is_tensor(lr) else float(lr.item())
+            host = torch.tensor([lr, 1 - b1 ** step, 1 - b2 ** step], dtype=torch.float32)
+            hyper.copy_(host.pin_memory(), non_blocking=True)
 
     # ------------------------------------------------------------------ hooks
     def set_grad_scale(self, coef: torch.Tensor | None) -> None:
@@ -71,6 +103,8 @@ class FusedAdamW(torch.optim.AdamW):
                 loss = closure()
         scale = self._grad_scale
         self._grad_scale = None
+        if self._hyper is not None:
+            return self._step_device_hyper(scale, loss)
         for group in self.param_groups:
             params = [p for p in group["params"] if p.grad is not None]
             if not params:
@@ -121,4 +155,22 @@ class FusedAdamW(torch.optim.AdamW):
                         if sh is not None:
                             sh.copy_(p.view_as(sh))
                     self._notify_shadows(ps)
+        return loss
+
+    def _step_device_hyper(self, scale, loss):
+        from pluggy_b200.ops import optim as _optim
+
+        for group, hyper in zip(self.param_groups, self._hyper, strict=True):
+            ps = [p for p in group["params"] if p.grad is not None]
+            if not ps:
+                continue
+            assert ps[0].is_cuda and self.use_kernel, "device-hyper steps run the CUDA kernel"
+            b1, b2 = group["betas"]
+            _optim.adamw_step(
+                ps, [p.grad for p in ps], [self.state[p]["exp_avg"] for p in ps],
+                [self.state[p]["exp_avg_sq"] for p in ps], [self._shadows.get(id(p)) for p in ps],
+                lr=0.0, beta1=b1, beta2=b2, eps=group["eps"], weight_decay=group["weight_decay"],
+                bias_correction1=1.0, bias_correction2=1.0, grad_scale=scale, hyper=hyper)
+            torch.autograd.graph.increment_version(ps)
+            self._notify_shadows(ps)
         return loss

@@ -127,6 +127,11 @@ class Trainer:
         self.resume_wandb_id = None
         # how often (optimizer steps) the kernels' status word is read; 0 = never
         self.status_check_steps = int(self.config.get("status_check_steps", 1))
+        # "cuda_graph": true replays the whole step (forward, loss, backward, clip, AdamW)
+        # from one CUDA graph after an eager first step (single GPU, plain data parallelism)
+        self.cuda_graph = bool(self.config.get("cuda_graph", False))
+        self._graph = None
+        self._graph_eager_steps = 1
         self.start_step = self._resume()
         self._setup_wandb()
         self.prefetcher = CUDAPrefetcher(self.dataloader, self.device)
@@ -409,13 +414,13 @@ class Trainer:
     def get_batch_prefetcher(self):
         return next(self.prefetcher)
 
-    def micro_train_step(self) -> torch.Tensor:
-        batch = self.get_batch_prefetcher()
+    def micro_train_step(self, batch=None) -> torch.Tensor:
+        batch = self.get_batch_prefetcher() if batch is None else batch
         loss = self.objective.compute_loss(self.model, batch) / self.microbatches_per_step
         loss.backward()
         return loss.detach()
 
-    def optimizer_step(self) -> torch.Tensor:
+    def optimizer_step(self, scheduler_step: bool = True) -> torch.Tensor:
         """sync -> clip -> step -> zero_grad -> scheduler; returns the grad norm."""
         if self.tp is not None:
             self.tp.sync_replicated_grads()
@@ -447,10 +452,61 @@ class Trainer:
                                    shard_dims=self.grad_shard_dims, partial_over=partial)
         self.optimizer.step()
         self.optimizer.zero_grad()
-        self.scheduler.step()
+        if scheduler_step:
+            self.scheduler.step()
         return gnorm
 
+    # ------------------------------------------------------------ CUDA graph
+    def _graph_ok(self) -> str | None:
+        if self.device.type != "cuda":
+            return "needs a CUDA device"
+        if self.world_size != 1 or any(x is not None for x in (self.tp, self.cp, self.ep)):
+            return "runs on one GPU without tp, cp or ep"
+        if self.microbatches_per_step != 1:
+            return "needs one microbatch per step"
+        if not (hasattr(self.optimizer, "use_device_hyper") and self.optimizer.use_kernel):
+            return "needs the fused AdamW optimizer"
+        return None
+
+    def _graph_step(self) -> dict[str, torch.Tensor]:
+        """One step replayed from a CUDA graph. The first call runs eagerly (lazy state,
+        kernel attributes, tensor maps); the second captures the step on the batch
+        buffers it then refills before every replay. The host keeps what the graph
+        cannot: the step count, the learning rate and the bias corrections (uploaded
+        to the optimizer's device hyperparameters) and the scheduler."""
+        batch = self.get_batch_prefetcher()
+        if self._graph is None and self._graph_eager_steps > 0:
+            self._graph_eager_steps -= 1
+            loss = self.micro_train_step(batch)
+            return {"loss": loss, "grad_norm": self.optimizer_step()}
+        if self._graph is None:
+            why = self._graph_ok()
+            if why is not None:
+                raise ValueError(f"cuda_graph {why}")
+            self._static_batch = {k: v.clone() for k, v in batch.items()}
+            self.optimizer.use_device_hyper(self.device)
+            torch.cuda.synchronize(self.device)
+            torch.cuda.empty_cache()  # the graph's pool takes the eager step's cached blocks
+            from pluggy_b200.utils.launch_count import count_launches
+
+            g = torch.cuda.CUDAGraph()
+            with count_launches() as cnt, torch.cuda.graph(g):
+                loss = self.micro_train_step(self._static_batch)
+                gnorm = self.optimizer_step(scheduler_step=False)
+            self._graph, self._static_out = g, (loss, gnorm)
+            self.graph_kernels = cnt.count  # this package's kernels in one replay
+        else:
+            for k, v in batch.items():
+                self._static_batch[k].copy_(v, non_blocking=True)
+        self.optimizer.advance()
+        self._graph.replay()
+        self.scheduler.step()
+        loss, gnorm = self._static_out
+        return {"loss": loss.clone(), "grad_norm": gnorm.clone()}
+
     def _train_step(self) -> dict[str, torch.Tensor]:
+        if self.cuda_graph:
+            return self._graph_step()
         loss = torch.zeros((), device=self.device)
         self.dp.requires_sync = False
         for _ in range(self.microbatches_per_step - 1):
