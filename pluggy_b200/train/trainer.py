@@ -31,6 +31,7 @@ from __future__ import annotations
 
 import json
 import os
+import warnings
 from datetime import datetime
 
 import torch
@@ -490,9 +491,17 @@ class Trainer:
             from pluggy_b200.utils.launch_count import count_launches
 
             g = torch.cuda.CUDAGraph()
-            with count_launches() as cnt, torch.cuda.graph(g):
-                loss = self.micro_train_step(self._static_batch)
-                gnorm = self.optimizer_step(scheduler_step=False)
+            try:
+                with count_launches() as cnt, torch.cuda.graph(g):
+                    loss = self.micro_train_step(self._static_batch)
+                    gnorm = self.optimizer_step(scheduler_step=False)
+            except RuntimeError as e:
+                # nothing of the captured step ran: continue with eager steps
+                warnings.warn(f"cuda_graph: capture failed, running eager steps ({e})")
+                self.cuda_graph, self.optimizer._hyper = False, None
+                self.optimizer.zero_grad()
+                loss = self.micro_train_step(batch)
+                return {"loss": loss, "grad_norm": self.optimizer_step()}
             self._graph, self._static_out = g, (loss, gnorm)
             self.graph_kernels = cnt.count  # this package's kernels in one replay
         else:
