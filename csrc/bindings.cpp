@@ -209,6 +209,27 @@ plg::QkRopeArgs qk_args(const at::Tensor& qkv, at::Tensor& q, at::Tensor& k, at:
   return a;
 }
 
+void rope_apply(const at::Tensor& x, const at::Tensor& cos, const at::Tensor& sin, at::Tensor& y,
+                bool backward) {
+  // x [B, H, S, d] bf16 (last dim contiguous), cos/sin [Bc, 1, S, d] fp32, y contiguous
+  TORCH_CHECK(x.is_cuda() && x.dim() == 4 && x.scalar_type() == at::kBFloat16 && x.stride(3) == 1,
+              "rope_apply: x must be a [B, H, S, d] bf16 CUDA tensor with a contiguous last dim");
+  TORCH_CHECK(cos.scalar_type() == at::kFloat && sin.scalar_type() == at::kFloat && cos.dim() == 4 &&
+                  cos.sizes() == sin.sizes() && cos.strides() == sin.strides() && cos.stride(3) == 1,
+              "rope_apply: cos/sin must be fp32 [Bc, 1, S, d] tables with equal strides");
+  const int B = x.size(0), H = x.size(1), S = x.size(2), d = x.size(3);
+  TORCH_CHECK(cos.size(1) == 1 && cos.size(2) == S && cos.size(3) == d &&
+                  (cos.size(0) == 1 || cos.size(0) == B),
+              "rope_apply: cos/sin shape does not match x");
+  TORCH_CHECK(y.is_contiguous() && y.sizes() == x.sizes() && y.scalar_type() == at::kBFloat16,
+              "rope_apply: y must be a contiguous bf16 tensor of x's shape");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const long long cs_b = cos.size(0) == 1 ? 0 : cos.stride(0);
+  plg::rope_apply(x.data_ptr(), x.stride(0), x.stride(1), x.stride(2), cos.data_ptr<float>(),
+                  sin.data_ptr<float>(), cs_b, cos.stride(2), y.data_ptr(), B, H, S, d, backward,
+                  cur_stream());
+}
+
 void qk_norm_rope_fwd(const at::Tensor& qkv, at::Tensor& q, at::Tensor& k, at::Tensor& rstd,
                       const c10::optional<at::Tensor>& wq, const c10::optional<at::Tensor>& wk,
                       const at::Tensor& inv_freq, const c10::optional<at::Tensor>& positions,
@@ -804,6 +825,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("beta"), py::arg("status") = py::none());
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("rope_apply", &rope_apply);
   m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd, py::arg("qkv"), py::arg("q"), py::arg("k"),
         py::arg("rstd"), py::arg("wq"), py::arg("wk"), py::arg("inv_freq"), py::arg("positions"),
         py::arg("S"), py::arg("Hq"), py::arg("Hk"), py::arg("d"), py::arg("rot_dim"), py::arg("eps"),

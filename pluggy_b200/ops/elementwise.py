@@ -89,8 +89,49 @@ def rotate_half(x: torch.Tensor) -> torch.Tensor:
     return torch.cat((-x[..., h:], x[..., :h]), dim=-1)
 
 
+class _Rope(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, cos, sin):
+        from pluggy_b200.ops._ext import ext
+
+        y = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+        ext().rope_apply(x, cos, sin, y, False)
+        ctx.save_for_backward(cos, sin)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        from pluggy_b200.ops._ext import ext
+
+        cos, sin = ctx.saved_tensors
+        dx = torch.empty(dy.shape, dtype=torch.bfloat16, device=dy.device)
+        ext().rope_apply(dy.contiguous() if dy.stride(-1) != 1 else dy, cos, sin, dx, True)
+        return dx, None, None
+
+
+def _rope_kernel_ok(x, cos, sin) -> bool:
+    if not (x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 4 and x.stride(-1) == 1):
+        return False
+    B, _, S, d = x.shape
+    if d % 4 or any(st % 2 for st in x.stride()[:3]) or x.data_ptr() % 4:
+        return False
+    if cos.dim() != 4 or cos.dtype != torch.float32 or sin.shape != cos.shape:
+        return False
+    if cos.shape[1] != 1 or cos.shape[2] != S or cos.shape[3] != d or cos.shape[0] not in (1, B):
+        return False
+    return (cos.stride() == sin.stride() and cos.stride(-1) == 1 and cos.stride(2) % 2 == 0
+            and (cos.shape[0] == 1 or cos.stride(0) % 2 == 0)
+            and cos.data_ptr() % 8 == 0 and sin.data_ptr() % 8 == 0)
+
+
 def apply_rotary(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-    """``x*cos + rotate_half(x)*sin`` with cos/sin broadcast against x (reference layout)."""
+    """``x*cos + rotate_half(x)*sin`` with cos/sin broadcast against x (reference layout
+    ``[B, H, S, d]``, ``pluggy/kernels/rope.py:12-24``). bf16 CUDA tensors with fp32
+    ``[B|1, 1, S, d]`` tables run the sm_100a kernel (fp32 math, any B/H/S strides, so
+    transposed views of a projection need no copy); everything else is eager torch with
+    the reference's casts."""
+    if _rope_kernel_ok(x, cos, sin):
+        return _Rope.apply(x, cos.detach(), sin.detach())
     cos = cos.to(x.dtype)
     sin = sin.to(x.dtype)
     return x * cos + rotate_half(x) * sin

@@ -680,3 +680,32 @@ def test_peer_wait_times_out_with_status():
     assert float((x * 2).sum()) == 2048.0
     # rank 0's own flag was posted (signal before wait); the missing peer's was not
     assert int(flags[0][0]) == 1 and int(flags[0][1]) == 0
+
+
+@pytest.mark.parametrize("B,H,S,d,bcast,transposed", [
+    (2, 4, 96, 128, True, True), (1, 3, 50, 64, False, False), (2, 2, 33, 256, False, True)])
+def test_rope_kernel_fwd_bwd(B, H, S, d, bcast, transposed):
+    """The RoPE kernel against fp32 eager math, on transposed [B, S, H, d] views and on
+    contiguous [B, H, S, d], with a batch-broadcast or per-batch cos/sin table."""
+    from pluggy_b200.ops.elementwise import _rope_kernel_ok, apply_rotary, rotate_half
+
+    torch.manual_seed(d + S)
+    pos = torch.arange(S, device=DEV).float()[None].expand(1 if bcast else B, S)
+    inv = 1.0 / (10000.0 ** (torch.arange(0, d, 2, device=DEV).float() / d))
+    f = pos[:, :, None] * inv
+    emb = torch.cat([f, f], -1)
+    cos, sin = emb.cos()[:, None], emb.sin()[:, None]
+    if transposed:
+        x = torch.randn(B, S, H, d, device=DEV).bfloat16().transpose(1, 2)
+    else:
+        x = torch.randn(B, H, S, d, device=DEV).bfloat16()
+    x.requires_grad_(True)
+    assert _rope_kernel_ok(x, cos, sin)
+    y = apply_rotary(x, cos, sin)
+    xf = x.detach().float().requires_grad_(True)
+    yf = xf * cos + rotate_half(xf) * sin
+    assert rel(y, yf) < 1e-2, rel(y, yf)
+    g = torch.randn_like(yf)
+    y.backward(g.bfloat16())
+    yf.backward(g)
+    assert rel(x.grad, xf.grad) < 1e-2, rel(x.grad, xf.grad)
