@@ -11,6 +11,11 @@ CFGS = {
                      vocab_size=128, ffn_dim=128),
     "qwen3_moe": dict(num_layers=2, num_heads=4, num_kv_heads=2, emb_dim=64, head_dim=16,
                       vocab_size=128, moe_ffn_dim=32, num_experts=4, top_k=2, ffn_dim=128),
+    "olmo3": dict(num_layers=4, num_heads=4, num_kv_heads=2, emb_dim=64, head_dim=16,
+                  vocab_size=128, ffn_dim=128, sliding_window=8),
+    "gemma4": dict(num_layers=3, num_heads=4, num_kv_heads=2, emb_dim=64, head_dim=16,
+                   global_head_dim=32, vocab_size=128, ffn_dim=128, sliding_window=8,
+                   layer_pattern=3, num_kv_shared_layers=1, hidden_size_per_layer_input=8),
 }
 
 

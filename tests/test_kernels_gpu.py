@@ -709,3 +709,36 @@ def test_rope_kernel_fwd_bwd(B, H, S, d, bcast, transposed):
     y.backward(g.bfloat16())
     yf.backward(g)
     assert rel(x.grad, xf.grad) < 1e-2, rel(x.grad, xf.grad)
+
+
+@pytest.mark.parametrize("name,cfg", [
+    ("olmo3", dict(num_layers=4, num_heads=4, num_kv_heads=2, emb_dim=256, head_dim=64,
+                   vocab_size=2048, ffn_dim=512, sliding_window=64)),
+    ("gemma4", dict(num_layers=3, num_heads=4, num_kv_heads=2, emb_dim=256, head_dim=64,
+                    global_head_dim=128, vocab_size=2048, ffn_dim=512, sliding_window=64,
+                    layer_pattern=3)),
+])
+def test_composed_model_families_match_fp32(name, cfg):
+    """OLMo-3 and Gemma-4 on CUDA (this package's GEMMs, norms, RoPE, GLU, attention and
+    fused CE) against the same weights in fp32 on the CPU."""
+    from pluggy_b200.models.builder import build_model
+    from pluggy_b200.objectives.autoregressive import ARObjective
+
+    torch.manual_seed(0)
+    m = build_model(name, cfg).to(DEV)
+    m.init_weights()
+    ids = torch.randint(0, 2048, (2, 256), device=DEV)
+    batch = {"input_ids": ids, "labels": ids}
+    obj = ARObjective(ce_chunk_size=128)
+    loss = obj.compute_loss(m, batch)
+    loss.backward()
+    grads = {n: p.grad.detach().clone() for n, p in m.named_parameters() if p.grad is not None}
+    mc = build_model(name, cfg)
+    mc.load_state_dict({k: v.cpu() for k, v in m.state_dict().items()})
+    lc = obj.compute_loss(mc, {k: v.cpu() for k, v in batch.items()})
+    lc.backward()
+    assert abs(loss.item() - lc.item()) < 2e-2 * lc.item(), (loss.item(), lc.item())
+    for n, p in mc.named_parameters():
+        if p.grad is not None and p.grad.abs().max() > 0:
+            r = rel(grads[n].cpu(), p.grad)
+            assert r < 8e-2, (n, r)
