@@ -194,6 +194,16 @@ def norm_eps(module: nn.RMSNorm, dtype: torch.dtype = torch.float32) -> float:
     return torch.finfo(dtype).eps if module.eps is None else float(module.eps)
 
 
+def apply_norm(module: nn.RMSNorm, x: torch.Tensor) -> torch.Tensor:
+    """``module(x)``; CUDA inputs whose width the RMSNorm kernel takes run it (fp32
+    statistics, the module's weight and resolved eps, output in x's dtype)."""
+    from pluggy_b200.ops.norm import rms_norm
+
+    if x.is_cuda and x.shape[-1] % 128 == 0 and x.dtype in (torch.float32, torch.bfloat16):
+        return rms_norm(x, module.weight, norm_eps(module, x.dtype))
+    return module(x)
+
+
 def scaled_init_std(d: int) -> float:
     return 1.0 / math.sqrt(d)
 

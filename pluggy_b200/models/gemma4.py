@@ -28,7 +28,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from pluggy_b200.models.common import attend, position_ids_for
+from pluggy_b200.models.common import apply_norm, attend, position_ids_for
 from pluggy_b200.ops.attention import flash_attention
 from pluggy_b200.ops.elementwise import apply_rotary, geglu_mul, logit_softcap
 from pluggy_b200.ops.linear import WeightCache, linear
@@ -124,7 +124,8 @@ class Gemma4Attention(nn.Module):
         return x.reshape(B, S, n, self.head_dim).transpose(1, 2)
 
     def forward(self, x, cos, sin, attention_mask, shared_kv, cache=None):
-        Q = apply_rotary(self.q_norm(self._split(_lin(self.q_proj, x, cache), self.num_heads)), cos, sin)
+        Q = apply_rotary(apply_norm(self.q_norm, self._split(_lin(self.q_proj, x, cache), self.num_heads)),
+                         cos, sin)
         if self.is_kv_shared_layer:
             K, V = shared_kv[self.layer_type]
             K, V = K.to(Q.device, Q.dtype), V.to(Q.device, Q.dtype)
@@ -132,7 +133,7 @@ class Gemma4Attention(nn.Module):
             K = self._split(_lin(self.k_proj, x, cache), self.num_kv_heads)
             V = K if (self.use_k_eq_v or self.v_proj is None) else \
                 self._split(_lin(self.v_proj, x, cache), self.num_kv_heads)
-            K = apply_rotary(self.k_norm(K), cos, sin)
+            K = apply_rotary(apply_norm(self.k_norm, K), cos, sin)
             V = rms_norm_no_scale(V, self.rms_norm_eps)
             if self.store_full_length_kv:
                 shared_kv[self.layer_type] = (K, V)
@@ -167,12 +168,12 @@ class Gemma4TransformerBlock(nn.Module):
             self.ple_norm = nn.RMSNorm(emb_dim, eps=rms_norm_eps)
 
     def forward(self, x, cos, sin, attention_mask, shared_kv, ple_input=None, cache=None):
-        x = x + self.post_attn_norm(self.attn(self.input_norm(x), cos, sin, attention_mask, shared_kv,
-                                              cache))
-        x = x + self.post_ffn_norm(self.ffn(self.pre_ffn_norm(x), cache))
+        a = self.attn(apply_norm(self.input_norm, x), cos, sin, attention_mask, shared_kv, cache)
+        x = x + apply_norm(self.post_attn_norm, a)
+        x = x + apply_norm(self.post_ffn_norm, self.ffn(apply_norm(self.pre_ffn_norm, x), cache))
         if self.ple_dim > 0 and ple_input is not None:
             gated = F.gelu(_lin(self.ple_gate, x, cache), approximate="tanh") * ple_input
-            x = x + self.ple_norm(_lin(self.ple_proj, gated, cache))
+            x = x + apply_norm(self.ple_norm, _lin(self.ple_proj, gated, cache))
         return x
 
 
@@ -277,6 +278,6 @@ class Gemma4(nn.Module):
             if return_hidden_states:
                 hs.append(h)
         if return_final_hidden:
-            return self.norm(h)
-        logits = logit_softcap(self.lm_head(self.norm(h)), self.final_logit_softcapping)
+            return apply_norm(self.norm, h)
+        logits = logit_softcap(self.lm_head(apply_norm(self.norm, h)), self.final_logit_softcapping)
         return (logits, hs) if return_hidden_states else logits

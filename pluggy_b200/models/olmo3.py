@@ -21,7 +21,7 @@ from __future__ import annotations
 import torch
 import torch.nn as nn
 
-from pluggy_b200.models.common import RotaryEmbedding, SwiGLU, attend, position_ids_for
+from pluggy_b200.models.common import RotaryEmbedding, SwiGLU, apply_norm, attend, position_ids_for
 from pluggy_b200.ops.attention import flash_attention
 from pluggy_b200.ops.elementwise import apply_rotary
 from pluggy_b200.ops.linear import WeightCache, linear
@@ -136,6 +136,6 @@ class Olmo3(nn.Module):
             if return_hidden_states:
                 hs.append(h)
         if return_final_hidden:
-            return self.norm(h)
-        logits = self.lm_head(self.norm(h))
+            return apply_norm(self.norm, h)
+        logits = self.lm_head(apply_norm(self.norm, h))
         return (logits, hs) if return_hidden_states else logits
