@@ -83,14 +83,17 @@ def _graph_vs_eager(rank, world, root, out):
 
 
 def test_cuda_graph_step_matches_eager(tmp_path):
-    """The whole step replayed from a CUDA graph (after one eager step) gives the same
-    losses and parameters as eager steps: the kernels are deterministic and the graph
-    reads the learning rate and bias corrections the host uploads each step."""
+    """The whole step replayed from a CUDA graph (after one eager step) gives the losses
+    and parameters of eager steps: the graph reads the learning rate and bias corrections
+    the host uploads each step. Not bitwise: the attention dQ accumulation adds fp32
+    partials in arrival order."""
     out = str(tmp_path / "res.json")
     run_ranks(_graph_vs_eager, 1, str(tmp_path / "ck"), out, timeout_s=120, join_s=600,
               backend="nccl")
     r = json.load(open(out))
     assert r["True"]["captured"] and not r["False"]["captured"]
     assert r["True"]["steps"] == r["False"]["steps"] == [5.0, 5.0, 5.0]
-    assert r["True"]["losses"] == r["False"]["losses"], r
-    assert r["True"]["params"] == r["False"]["params"]
+    for a, b in zip(r["True"]["losses"], r["False"]["losses"], strict=True):
+        assert abs(a - b) <= 1e-4 * abs(b), r
+    for a, b in zip(r["True"]["params"], r["False"]["params"], strict=True):
+        assert abs(a - b) <= 1e-3 * max(1.0, abs(b)), (a, b)
