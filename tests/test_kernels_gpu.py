@@ -720,13 +720,23 @@ def test_rope_kernel_fwd_bwd(B, H, S, d, bcast, transposed):
 ])
 def test_composed_model_families_match_fp32(name, cfg):
     """OLMo-3 and Gemma-4 on CUDA (this package's GEMMs, norms, RoPE, GLU, attention and
-    fused CE) against the same weights in fp32 on the CPU."""
+    fused CE) against the same weights in fp32 on the CPU. Gemma's attention has scale
+    1 on per-head-normalised q and k: at the init norm weights (1) the logits have a std
+    of ~sqrt(head_dim) and the softmax is so peaked that rounding the weights to bf16
+    alone moves the fp32 gradients by ~40 %; the q/k-norm weights are set to 0.3 here
+    (1.6 % on the same check), so the comparison measures the kernels, not that."""
     from pluggy_b200.models.builder import build_model
     from pluggy_b200.objectives.autoregressive import ARObjective
 
     torch.manual_seed(0)
     m = build_model(name, cfg).to(DEV)
     m.init_weights()
+    if name == "gemma4":
+        with torch.no_grad():
+            for b in m.blocks:
+                for nm in (b.attn.q_norm, b.attn.k_norm):
+                    if nm is not None:
+                        nm.weight.fill_(0.3)
     ids = torch.randint(0, 2048, (2, 256), device=DEV)
     batch = {"input_ids": ids, "labels": ids}
     obj = ARObjective(ce_chunk_size=128)
