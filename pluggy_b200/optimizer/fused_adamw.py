@@ -66,7 +66,10 @@ class FusedAdamW(torch.optim.AdamW):
             lr = group["lr"]
             lr = float(lr) if not torch.is_tensor(lr) else float(lr.item())
             host = torch.tensor([lr, 1 - b1 ** step, 1 - b2 ** step], dtype=torch.float32)
-            hyper.copy_(host.pin_memory(), non_blocking=True)
+            if hyper.is_cuda:
+                hyper.copy_(host.pin_memory(), non_blocking=True)
+            else:
+                hyper.copy_(host)
 
     # ------------------------------------------------------------------ hooks
     def set_grad_scale(self, coef: torch.Tensor | None) -> None:

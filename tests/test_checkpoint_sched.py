@@ -147,3 +147,27 @@ def test_scheduler_resume(kind):
     assert rest == pytest.approx(lrs[20:])
     cls = WarmupStableDecaySchedulder if kind == "wsd" else CosineAnnealingScheduler
     assert isinstance(s, cls)
+
+
+def test_fused_adamw_device_hyper_bookkeeping():
+    """CUDA-graph steps keep the host bookkeeping out of the graph: ``advance`` counts
+    the step and writes this step's (lr, 1 - b1^t, 1 - b2^t) per group, and the state
+    dict keeps the same step counts as eager steps."""
+    from pluggy_b200.optimizer.fused_adamw import FusedAdamW
+
+    ps = [nn.Parameter(torch.randn(4, 3)), nn.Parameter(torch.randn(3))]
+    opt = FusedAdamW([{"params": ps[:1], "weight_decay": 0.1}, {"params": ps[1:], "weight_decay": 0.0}],
+                     lr=1e-3, betas=(0.9, 0.95))
+    for p in ps:
+        p.grad = torch.randn_like(p)
+    opt.step()  # eager first step creates the state
+    opt.use_device_hyper("cpu")
+    for g in opt.param_groups:
+        g["lr"] = 5e-4
+    opt.advance()
+    opt.advance()
+    assert [float(opt.state[p]["step"]) for p in ps] == [3.0, 3.0]
+    for hyper in opt._hyper:
+        assert torch.allclose(hyper, torch.tensor([5e-4, 1 - 0.9 ** 3, 1 - 0.95 ** 3]))
+    sd = opt.state_dict()
+    assert all(float(s["step"]) == 3.0 for s in sd["state"].values())
