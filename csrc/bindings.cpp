@@ -357,6 +357,29 @@ void ce_rows(at::Tensor& logits, const at::Tensor& labels, int64_t ignore_index,
                lse_in.has_value() ? lse_in->data_ptr<float>() : nullptr, label_offset);
 }
 
+void router_topk_b(const at::Tensor& logits, int64_t k, bool renorm, const c10::optional<at::Tensor>& probs,
+                   at::Tensor& w, at::Tensor& idx, const c10::optional<at::Tensor>& counts) {
+  check_cuda(logits, "logits");
+  TORCH_CHECK(logits.dim() == 2 && logits.is_contiguous() && (is_bf16(logits) || is_f32(logits)),
+              "router_topk: logits must be a contiguous [T, E] bf16 or fp32 tensor");
+  const long long T = logits.size(0);
+  const int E = static_cast<int>(logits.size(1));
+  TORCH_CHECK(is_f32(w) && w.is_contiguous() && w.numel() == T * k, "router_topk: w is fp32 [T, k]");
+  TORCH_CHECK(idx.scalar_type() == at::kLong && idx.is_contiguous() && idx.numel() == T * k,
+              "router_topk: idx is int64 [T, k]");
+  if (probs.has_value())
+    TORCH_CHECK(is_f32(*probs) && probs->is_contiguous() && probs->numel() == T * E,
+                "router_topk: probs is fp32 [T, E]");
+  if (counts.has_value())
+    TORCH_CHECK(counts->scalar_type() == at::kInt && counts->is_contiguous() && counts->numel() == E,
+                "router_topk: counts is int32 [E]");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  plg::router_topk(logits.data_ptr(), is_bf16(logits), T, E, static_cast<int>(k), renorm,
+                   probs.has_value() ? probs->data_ptr<float>() : nullptr, w.data_ptr<float>(),
+                   idx.data_ptr<int64_t>(), counts.has_value() ? counts->data_ptr<int>() : nullptr,
+                   cur_stream());
+}
+
 void exp2_poly_eval_b(const at::Tensor& x, at::Tensor& poly, at::Tensor& ref) {
   check_cuda(x, "x");
   TORCH_CHECK(is_f32(x) && is_f32(poly) && is_f32(ref) && x.is_contiguous() && poly.is_contiguous() &&
@@ -883,6 +906,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("lse_in") = py::none(), py::arg("label_offset") = 0);
   m.def("embedding_bwd_sorted", &embedding_bwd_sorted);
   m.def("exp2_poly_eval", &exp2_poly_eval_b);
+  m.def("router_topk", &router_topk_b, py::arg("logits"), py::arg("k"), py::arg("renorm"),
+        py::arg("probs"), py::arg("w"), py::arg("idx"), py::arg("counts") = py::none());
   m.def("multi_sumsq", &multi_sumsq);
   m.def("multi_scale", &multi_scale);
   m.def("adamw_multi", &adamw_multi, py::arg("table"), py::arg("ntensors"), py::arg("total_chunks"),

@@ -116,6 +116,11 @@ void embedding_bwd_sorted(const int64_t* ids_sorted, const int64_t* pos_sorted, 
                           cudaStream_t stream);
 // poly[i] = 2^x[i] by the attention kernels' FMA-pipe cubic, ref[i] = exp2f(x[i])
 void exp2_poly_eval(const float* x, float* poly, float* ref, long long n, cudaStream_t stream);
+// MoE router over logits [T, E]: probs [T, E] fp32 (optional), top-k weights [T, k] fp32
+// (renormalised over the k when asked), expert ids [T, k] int64, histogram counts [E] int32
+// (optional, accumulated)
+void router_topk(const void* logits, bool bf16, long long T, int E, int k, bool renorm, float* probs,
+                 float* w, int64_t* idx, int* counts, cudaStream_t stream);
 // y = cap * tanh(x / cap)
 void softcap_fwd(const void* x, void* y, long long n, float cap, bool bf16, cudaStream_t stream);
 

@@ -682,6 +682,99 @@ void embedding_bwd_sorted(const int64_t* ids_sorted, const int64_t* pos_sorted, 
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 
+// ------------------------------------------------------------------ MoE router
+// One warp per token: fp32 softmax over the E router logits, the top k (largest
+// probability first, the lower expert index on ties, as a sort would give), the
+// weights renormalised over the k when asked, and the per-expert histogram of the
+// choices (int32 atomics: exact). kE = E / 32 logits per lane.
+template <int kE, typename T>
+__global__ void __launch_bounds__(256) router_topk_kernel(const T* __restrict__ logits, long long T_,
+                                                          int k, int renorm, float* __restrict__ probs,
+                                                          float* __restrict__ w_out,
+                                                          int64_t* __restrict__ idx_out,
+                                                          int* __restrict__ counts) {
+  constexpr int E = kE * 32;
+  const long long tok = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (tok >= T_) return;
+  float v[kE];
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < kE; ++j) {
+    v[j] = static_cast<float>(logits[tok * E + j * 32 + lane]);
+    m = fmaxf(m, v[j]);
+  }
+  m = warp_max(m);
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < kE; ++j) {
+    v[j] = expf(v[j] - m);
+    s += v[j];
+  }
+  s = warp_sum(s);
+  const float inv = 1.f / s;
+#pragma unroll
+  for (int j = 0; j < kE; ++j) {
+    v[j] *= inv;
+    if (probs != nullptr) probs[tok * E + j * 32 + lane] = v[j];
+  }
+  unsigned taken = 0;
+  float wsum = 0.f, wmine = 0.f;
+  int mine = -1;  // lane r < k keeps the r-th choice
+  for (int r = 0; r < k; ++r) {
+    float bv = -1.f;
+    int bi = E;
+#pragma unroll
+    for (int j = 0; j < kE; ++j)
+      if (!((taken >> j) & 1u) && v[j] > bv) {
+        bv = v[j];
+        bi = j * 32 + lane;
+      }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    wsum += bv;
+    if (lane == r) {
+      mine = bi;
+      wmine = bv;
+    }
+  }
+  if (lane < k) {
+    idx_out[tok * k + lane] = mine;
+    w_out[tok * k + lane] = renorm ? wmine / wsum : wmine;
+    if (counts != nullptr) atomicAdd(counts + mine, 1);
+  }
+}
+
+void router_topk(const void* logits, bool bf16, long long T, int E, int k, bool renorm, float* probs,
+                 float* w, int64_t* idx, int* counts, cudaStream_t st) {
+  if (E % 32 || E > 512 || k < 1 || k > 32 || k > E)
+    throw std::invalid_argument("router_topk: E a multiple of 32 up to 512, 1 <= k <= min(32, E)");
+  if (T <= 0) return;
+  const unsigned blocks = static_cast<unsigned>((T * 32 + 255) / 256);
+#define PLG_ROUTER(KE)                                                                              \
+  if (E == KE * 32) {                                                                               \
+    if (bf16)                                                                                       \
+      router_topk_kernel<KE, __nv_bfloat16><<<blocks, 256, 0, st>>>(                                \
+          static_cast<const __nv_bfloat16*>(logits), T, k, renorm, probs, w, idx, counts);          \
+    else                                                                                            \
+      router_topk_kernel<KE, float><<<blocks, 256, 0, st>>>(static_cast<const float*>(logits), T,   \
+                                                            k, renorm, probs, w, idx, counts);      \
+    PLG_CUDA_CHECK(cudaGetLastError());                                                             \
+    return;                                                                                         \
+  }
+  PLG_ROUTER(1) PLG_ROUTER(2) PLG_ROUTER(4) PLG_ROUTER(8) PLG_ROUTER(16)
+#undef PLG_ROUTER
+  throw std::invalid_argument("router_topk: E must be 32, 64, 128, 256 or 512");
+}
+
 void exp2_poly_eval(const float* x, float* poly, float* ref, long long n, cudaStream_t st) {
   if (n <= 0) return;
   const long long pairs = (n + 1) / 2;

@@ -32,6 +32,40 @@ from pluggy_b200.ops.linear import WeightCache, linear
 from pluggy_b200.ops.moe import expert_histogram, moe_expert_ffn
 
 
+class _RouterTopK(torch.autograd.Function):
+    """Softmax (fp32) + top-k + optional renormalisation in one sm_100a kernel launch;
+    the backward is the chain rule through the renormalisation and the softmax."""
+
+    @staticmethod
+    def forward(ctx, logits, k: int, renorm: bool):
+        from pluggy_b200.ops._ext import ext
+
+        lg = logits.contiguous()
+        T, E = lg.shape
+        probs = torch.empty((T, E), dtype=torch.float32, device=lg.device)
+        w = torch.empty((T, k), dtype=torch.float32, device=lg.device)
+        idx = torch.empty((T, k), dtype=torch.int64, device=lg.device)
+        ext().router_topk(lg, k, renorm, probs, w, idx)
+        ctx.save_for_backward(probs, w, idx)
+        ctx.renorm, ctx.dtype = renorm, logits.dtype
+        ctx.mark_non_differentiable(idx)
+        return w, idx
+
+    @staticmethod
+    def backward(ctx, dw, _didx):
+        probs, w, idx = ctx.saved_tensors
+        dw = dw.float()
+        if ctx.renorm:
+            # w = p_sel / S, S = sum of the selected p: dL/dp_sel = (dw - <dw, w>) / S
+            s = probs.gather(1, idx).sum(-1, keepdim=True)
+            dsel = (dw - (dw * w).sum(-1, keepdim=True)) / s
+        else:
+            dsel = dw
+        dp = torch.zeros_like(probs).scatter_add_(1, idx, dsel)
+        dlogits = probs * (dp - (dp * probs).sum(-1, keepdim=True))
+        return dlogits.to(ctx.dtype), None, None
+
+
 class Qwen3MoeTopKRouter(nn.Module):
     def __init__(self, emb_dim: int, num_experts: int, top_k: int, norm_topk_prob: bool = True):
         super().__init__()
@@ -41,6 +75,10 @@ class Qwen3MoeTopKRouter(nn.Module):
 
     def forward(self, h):
         logits = linear(h, self.weight) if h.is_cuda else F.linear(h, self.weight)
+        E = logits.shape[-1]
+        if logits.is_cuda and E % 32 == 0 and E <= 512 and self.top_k <= min(32, E):
+            w, idx = _RouterTopK.apply(logits, self.top_k, self.norm_topk_prob)
+            return logits, w.to(h.dtype), idx
         probs = F.softmax(logits, dim=-1, dtype=torch.float32)
         w, idx = torch.topk(probs, self.top_k, dim=-1)
         if self.norm_topk_prob:

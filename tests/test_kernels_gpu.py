@@ -752,3 +752,34 @@ def test_composed_model_families_match_fp32(name, cfg):
         if p.grad is not None and p.grad.abs().max() > 0:
             r = rel(grads[n].cpu(), p.grad)
             assert r < 8e-2, (n, r)
+
+
+@pytest.mark.parametrize("E,k,renorm,dtype", [(128, 8, True, torch.bfloat16), (64, 4, False, torch.float32),
+                                               (512, 2, True, torch.float32)])
+def test_router_topk_kernel(E, k, renorm, dtype):
+    """The fused router (softmax, top-k, renormalisation, histogram) against the eager
+    softmax/topk path, forward and backward."""
+    from pluggy_b200.models.qwen3_moe import _RouterTopK
+    from pluggy_b200.ops._ext import ext
+
+    torch.manual_seed(E + k)
+    T = 1000
+    logits = torch.randn(T, E, device=DEV).to(dtype).requires_grad_(True)
+    w, idx = _RouterTopK.apply(logits, k, renorm)
+    lf = logits.detach().float().requires_grad_(True)
+    p = torch.softmax(lf, -1)
+    pw, pidx = torch.topk(p, k, dim=-1)
+    if renorm:
+        pw = pw / pw.sum(-1, keepdim=True)
+    assert torch.equal(idx.sort(-1).values, pidx.sort(-1).values)
+    assert rel(w.gather(1, idx.argsort(-1)), pw.gather(1, pidx.argsort(-1))) < 1e-5
+    # the same upstream gradient per (token, expert) for both selections
+    G = torch.randn(T, E, device=DEV)
+    (w * G.gather(1, idx)).sum().backward()
+    (pw * G.gather(1, pidx)).sum().backward()
+    assert rel(logits.grad.float(), lf.grad) < 2e-2
+    counts = torch.zeros(E, dtype=torch.int32, device=DEV)
+    ww = torch.empty(T, k, device=DEV)
+    ii = torch.empty(T, k, dtype=torch.int64, device=DEV)
+    ext().router_topk(logits.detach().contiguous(), k, renorm, None, ww, ii, counts)
+    assert torch.equal(counts.long(), torch.bincount(ii.view(-1), minlength=E))
