@@ -834,7 +834,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // memory the operand reads of dV and dK.
 // The MMA warp issues S/dP of step j+1 before dV/dK/dQ of step j, so the
 // compute warps work on step j+1 while the tensor core finishes step j.
-// TMEM: dV [0,128), dK [128,256), S_b at 256+128b, dP_b at 320+128b.
+// TMEM: dV [0,128), dK [128,256), S_b at 256+128b, dP_b at 320+128b. After the
+// P / dS warps of query half h (queries 32h..32h+31) have read S_b, they overwrite
+// S_b columns 32h..32h+15 with P^T and 32h+16..32h+31 with dS^T (bf16 pairs).
 // lse*log2e and delta*scale come pre-negated from a pre-pass, padded to a
 // multiple of 64 queries ([B*Hq][2][S64]) so each step fetches them with two
 // 256-byte bulk copies; padded queries carry -inf / 0 and contribute nothing.
