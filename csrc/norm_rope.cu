@@ -13,6 +13,8 @@
 
 #include <type_traits>
 
+#include <cstdlib>
+
 #include "common.cuh"
 #include "ops.h"
 
@@ -913,8 +915,20 @@ static RopeTma rope_tma_plan(const QkRopeArgs& a, bool bwd) {
     off += a.rot_dim * 4;
   }
   b.tok_bytes = up16(off);
-  b.tt = std::max(1, (13 * 1024) / b.tok_bytes);
-  b.nst = std::min(kRopeTmaMaxStages, std::max(2, (54 * 1024) / (b.tt * b.tok_bytes)));
+  // shared-memory budgets (KB) of one tile and of all stages of a CTA; four CTAs per SM
+  // (PLG_ROPE_TILE_KB / PLG_ROPE_STAGES_KB override them for tuning)
+  static const int tile_kb = [] {
+    const char* e = std::getenv("PLG_ROPE_TILE_KB");
+    const int v = e ? std::atoi(e) : 13;
+    return v >= 4 && v <= 48 ? v : 13;
+  }();
+  static const int stages_kb = [] {
+    const char* e = std::getenv("PLG_ROPE_STAGES_KB");
+    const int v = e ? std::atoi(e) : 54;
+    return v >= 16 && v <= 54 ? v : 54;
+  }();
+  b.tt = std::max(1, (tile_kb * 1024) / b.tok_bytes);
+  b.nst = std::min(kRopeTmaMaxStages, std::max(2, (stages_kb * 1024) / (b.tt * b.tok_bytes)));
   return b;
 }
 
