@@ -27,6 +27,8 @@
 #include <stdexcept>
 #include <string>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "ops.h"
 
@@ -1268,53 +1270,65 @@ __global__ void __launch_bounds__(kB3Threads, 1)
 
 // Backward pre-pass of the pipelined kernel: per (b, h) row of the stats workspace
 // [B*Hq][2][S64], -lse*log2(e) and -scale * rowsum(dO * O); queries beyond S get -inf
-// and 0. Half a warp per (b, s, h) (D / 16 channels per lane, 16 or 8 bytes), two rows
-// per warp; position fastest, so consecutive rows read consecutive lse and write
-// consecutive stats.
+// and 0. Half a warp per four consecutive positions of one (b, h) (S64 is a multiple of
+// 64): D / 16 channels per lane and row, the eight row loads of a lane issued before
+// any math, lanes 0..3 writing the four results.
 template <int D>
 __global__ void attn_bwd_stats_kernel(const __nv_bfloat16* __restrict__ o, long long o_row,
                                       const __nv_bfloat16* __restrict__ dout, long long do_row,
                                       const float* __restrict__ lse, float* __restrict__ stats,
                                       int B, int S, int S64, int H, float scale) {
   static_assert(D == 64 || D == 128, "stats head_dim");
-  const long long row_id = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;
+  constexpr int R = 4;
+  using V = std::conditional_t<D == 128, uint4, uint2>;  // D / 16 bf16 per lane
+  constexpr int NW = sizeof(V) / 4;
+  const long long r0 = ((static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4) * R;
   const int l16 = threadIdx.x & 15;
   const long long total = static_cast<long long>(B) * S64 * H;
-  const bool valid = row_id < total;
-  const long long rid = valid ? row_id : 0;  // every lane takes part in the shuffles
-  const int s = static_cast<int>(rid % S64);
+  const bool valid = r0 < total;
+  const long long rid = valid ? r0 : 0;  // every lane takes part in the shuffles
+  const int s0 = static_cast<int>(rid % S64);
   const long long bh = rid / S64;
   const int h = static_cast<int>(bh % H), bb = static_cast<int>(bh / H);
-  float acc = 0.f;
-  const long long tok = static_cast<long long>(bb) * S + s;
-  if (valid && s < S) {
-    if constexpr (D == 128) {
-      const uint4 ov = *reinterpret_cast<const uint4*>(o + tok * o_row + h * D + l16 * 8);
-      const uint4 dv = *reinterpret_cast<const uint4*>(dout + tok * do_row + h * D + l16 * 8);
-      const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w}, dw[4] = {dv.x, dv.y, dv.z, dv.w};
+  V ov[R], dv[R];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 x = unpack_bf16x2(ow[e]), y = unpack_bf16x2(dw[e]);
-        acc = fmaf(x.x, y.x, fmaf(x.y, y.y, acc));
-      }
-    } else {
-      const uint2 ov = *reinterpret_cast<const uint2*>(o + tok * o_row + h * D + l16 * 4);
-      const uint2 dv = *reinterpret_cast<const uint2*>(dout + tok * do_row + h * D + l16 * 4);
-      const float2 x0 = unpack_bf16x2(ov.x), x1 = unpack_bf16x2(ov.y);
-      const float2 y0 = unpack_bf16x2(dv.x), y1 = unpack_bf16x2(dv.y);
-      acc = x0.x * y0.x + x0.y * y0.y + x1.x * y1.x + x1.y * y1.y;
+  for (int r = 0; r < R; ++r) {
+    const int s = s0 + r;
+    if (valid && s < S) {
+      const long long tok = static_cast<long long>(bb) * S + s;
+      ov[r] = *reinterpret_cast<const V*>(o + tok * o_row + h * D + l16 * (D / 16));
+      dv[r] = *reinterpret_cast<const V*>(dout + tok * do_row + h * D + l16 * (D / 16));
     }
   }
+  float acc[R];
 #pragma unroll
-  for (int off = 8; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (valid && l16 == 0) {
+  for (int r = 0; r < R; ++r) {
+    acc[r] = 0.f;
+    if (valid && s0 + r < S) {
+      const uint32_t* ow = reinterpret_cast<const uint32_t*>(&ov[r]);
+      const uint32_t* dw = reinterpret_cast<const uint32_t*>(&dv[r]);
+#pragma unroll
+      for (int e = 0; e < NW; ++e) {
+        const float2 x = unpack_bf16x2(ow[e]), y = unpack_bf16x2(dw[e]);
+        acc[r] = fmaf(x.x, y.x, fmaf(x.y, y.y, acc[r]));
+      }
+    }
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], off);
+  }
+  if (valid && l16 < R) {
+    float a = acc[0];
+#pragma unroll
+    for (int r = 1; r < R; ++r)
+      if (l16 == r) a = acc[r];
+    const int s = s0 + l16;
     float* row = stats + (static_cast<long long>(bb) * H + h) * 2 * S64;
     if (s >= S) {
       row[s] = -INFINITY;
       row[S64 + s] = 0.f;
     } else {
       row[s] = -lse[(static_cast<long long>(bb) * H + h) * S + s] * kLog2e;
-      row[S64 + s] = -acc * scale;
+      row[S64 + s] = -a * scale;
     }
   }
 }
@@ -1506,7 +1520,7 @@ static void bwd3_launch(const AttnBwdArgs& g, cudaStream_t st) {
     throw std::invalid_argument("attention backward: o, dout and dq rows must be 16-byte aligned");
   PLG_CUDA_CHECK(cudaMemsetAsync(g.dq_acc, 0,
                                   sizeof(float) * static_cast<size_t>(a.B) * a.S * a.Hq * D, st));
-  attn_bwd_stats_kernel<D><<<(srows * 16 + 255) / 256, 256, 0, st>>>(
+  attn_bwd_stats_kernel<D><<<(srows * 4 + 255) / 256, 256, 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(a.o), a.o_row,
       reinterpret_cast<const __nv_bfloat16*>(g.dout), g.do_row, a.lse, g.delta, a.B, a.S, S64, a.Hq,
       a.scale);

@@ -12,6 +12,8 @@
 #include <mutex>
 #include <stdexcept>
 
+#include <cstdlib>
+
 #include "common.cuh"
 #include "ops.h"
 #include "plg_noalloc.h"
@@ -265,7 +267,10 @@ __global__ void softcap_kernel(const T* __restrict__ x, T* __restrict__ y, long 
 // in flight at once, so pass 2 re-reads the row from L2 instead of DRAM.
 constexpr int kCeThreads = 1024;
 
-__global__ void __launch_bounds__(kCeThreads, 2) ce_rows_kernel(
+// kCeBatch: row loads in flight per thread before their math; kCeMinBlocks: resident
+// blocks per SM the register budget is sized for (2 -> 32 registers, 1 -> 64)
+template <int kCeBatch, int kCeMinBlocks>
+__global__ void __launch_bounds__(kCeThreads, kCeMinBlocks) ce_rows_kernel(
     __nv_bfloat16* __restrict__ logits, long long ld, const int64_t* __restrict__ labels, int V,
     int ignore_index, float grad_scale, float softcap, float* __restrict__ lse_out,
     float* __restrict__ loss_sum, int* __restrict__ n_valid, float* __restrict__ row_loss,
@@ -287,8 +292,19 @@ __global__ void __launch_bounds__(kCeThreads, 2) ce_rows_kernel(
     // gradient pass of a vocabulary-parallel row: the lse over the full vocabulary is given
     lse = lse_in[row];
   } else {
-  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
-    uint4 u = reinterpret_cast<const uint4*>(x)[i];
+  // kCeBatch row loads in flight per thread before their math (the same elements in
+  // the same order as a one-load loop, so the result is unchanged)
+  for (int i0 = threadIdx.x; i0 < nvec; i0 += kCeBatch * blockDim.x) {
+  uint4 ub[kCeBatch];
+#pragma unroll
+  for (int q = 0; q < kCeBatch; ++q) {
+    const int i = i0 + q * blockDim.x;
+    if (i < nvec) ub[q] = reinterpret_cast<const uint4*>(x)[i];
+  }
+#pragma unroll
+  for (int q = 0; q < kCeBatch; ++q) {
+    if (i0 + q * static_cast<int>(blockDim.x) >= nvec) break;
+    const uint4 u = ub[q];
     float f[8];
     float2 t;
     t = unpack_bf16x2(u.x); f[0] = t.x; f[1] = t.y;
@@ -306,6 +322,7 @@ __global__ void __launch_bounds__(kCeThreads, 2) ce_rows_kernel(
     for (int j = 0; j < 8; ++j) acc += fast_exp2((f[j] - lm) * kLog2e);
     m = lm;
     s = acc;
+  }
   }
   for (int i = nvec * 8 + threadIdx.x; i < V; i += blockDim.x) {
     float f = __bfloat162float(x[i]);
@@ -375,8 +392,18 @@ __global__ void __launch_bounds__(kCeThreads, 2) ce_rows_kernel(
   }
   // pass 2: gradient in place
   const float gs = valid ? grad_scale : 0.f;
-  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
-    uint4 u = reinterpret_cast<uint4*>(x)[i];
+  for (int i0 = threadIdx.x; i0 < nvec; i0 += kCeBatch * blockDim.x) {
+  uint4 ub[kCeBatch];
+#pragma unroll
+  for (int q = 0; q < kCeBatch; ++q) {
+    const int i = i0 + q * blockDim.x;
+    if (i < nvec) ub[q] = reinterpret_cast<const uint4*>(x)[i];
+  }
+#pragma unroll
+  for (int q = 0; q < kCeBatch; ++q) {
+    const int i = i0 + q * blockDim.x;
+    if (i >= nvec) break;
+    uint4 u = ub[q];
     uint32_t* w = reinterpret_cast<uint32_t*>(&u);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -395,6 +422,7 @@ __global__ void __launch_bounds__(kCeThreads, 2) ce_rows_kernel(
       w[j] = pack_bf16x2(pa * gs * ca, pb * gs * cb);
     }
     reinterpret_cast<uint4*>(x)[i] = u;
+  }
   }
   for (int i = nvec * 8 + threadIdx.x; i < V; i += blockDim.x) {
     float a = __bfloat162float(x[i]);
@@ -800,10 +828,18 @@ void ce_rows(void* logits, long long ld, const int64_t* labels, long long rows, 
   if (rows <= 0) return;
   if ((ld % 8) || (reinterpret_cast<uintptr_t>(logits) & 15))
     throw std::invalid_argument("ce_rows: logits rows must be 16-byte aligned");
-  ce_rows_kernel<<<rows, kCeThreads, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(logits), ld, labels,
-                                              V, ignore_index, grad_scale, softcap, lse_out,
-                                              loss_sum, n_valid, row_loss, stats_out, lse_in,
-                                              label_offset);
+  // PLG_CE_VARIANT: 0 one load in flight per thread (2 blocks / SM), 1 two loads
+  // (2 blocks / SM), 2 four loads (1 block / SM)
+  static const int variant = [] {
+    const char* e = std::getenv("PLG_CE_VARIANT");
+    const int v = e ? std::atoi(e) : 0;
+    return v >= 0 && v <= 2 ? v : 0;
+  }();
+  auto* kern = variant == 1 ? ce_rows_kernel<2, 2> : variant == 2 ? ce_rows_kernel<4, 1>
+                                                                  : ce_rows_kernel<1, 2>;
+  kern<<<rows, kCeThreads, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(logits), ld, labels, V,
+                                    ignore_index, grad_scale, softcap, lse_out, loss_sum, n_valid,
+                                    row_loss, stats_out, lse_in, label_offset);
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 
