@@ -267,10 +267,12 @@ __global__ void softcap_kernel(const T* __restrict__ x, T* __restrict__ y, long 
 // in flight at once, so pass 2 re-reads the row from L2 instead of DRAM.
 constexpr int kCeThreads = 1024;
 
-// kCeBatch: row loads in flight per thread before their math; kCeMinBlocks: resident
-// blocks per SM the register budget is sized for (2 -> 32 registers, 1 -> 64)
-template <int kCeBatch, int kCeMinBlocks>
-__global__ void __launch_bounds__(kCeThreads, kCeMinBlocks) ce_rows_kernel(
+// kCeBatch: row loads in flight per thread before their math (1: at 32 registers for
+// two resident 1024-thread blocks per SM; 2 loads, or 4 loads at one block per SM,
+// measured 4 % and 8 % slower)
+constexpr int kCeBatch = 1;
+
+__global__ void __launch_bounds__(kCeThreads, 2) ce_rows_kernel(
     __nv_bfloat16* __restrict__ logits, long long ld, const int64_t* __restrict__ labels, int V,
     int ignore_index, float grad_scale, float softcap, float* __restrict__ lse_out,
     float* __restrict__ loss_sum, int* __restrict__ n_valid, float* __restrict__ row_loss,
@@ -828,18 +830,10 @@ void ce_rows(void* logits, long long ld, const int64_t* labels, long long rows, 
   if (rows <= 0) return;
   if ((ld % 8) || (reinterpret_cast<uintptr_t>(logits) & 15))
     throw std::invalid_argument("ce_rows: logits rows must be 16-byte aligned");
-  // PLG_CE_VARIANT: 0 one load in flight per thread (2 blocks / SM), 1 two loads
-  // (2 blocks / SM), 2 four loads (1 block / SM)
-  static const int variant = [] {
-    const char* e = std::getenv("PLG_CE_VARIANT");
-    const int v = e ? std::atoi(e) : 0;
-    return v >= 0 && v <= 2 ? v : 0;
-  }();
-  auto* kern = variant == 1 ? ce_rows_kernel<2, 2> : variant == 2 ? ce_rows_kernel<4, 1>
-                                                                  : ce_rows_kernel<1, 2>;
-  kern<<<rows, kCeThreads, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(logits), ld, labels, V,
-                                    ignore_index, grad_scale, softcap, lse_out, loss_sum, n_valid,
-                                    row_loss, stats_out, lse_in, label_offset);
+  ce_rows_kernel<<<rows, kCeThreads, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(logits), ld, labels,
+                                              V, ignore_index, grad_scale, softcap, lse_out,
+                                              loss_sum, n_valid, row_loss, stats_out, lse_in,
+                                              label_offset);
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 
