@@ -56,6 +56,12 @@ def validate_config(cfg: dict) -> None:
         errs.append("mesh must map axis names (including 'dp') to positive sizes")
     if cfg.get("parallelism", "ddp") not in ("ddp", "fsdp2"):
         errs.append(f"parallelism must be 'ddp' or 'fsdp2', got {cfg.get('parallelism')!r}")
+    if "cuda_graph" in cfg and not isinstance(cfg["cuda_graph"], bool):
+        errs.append("cuda_graph must be true or false")
+    if cfg.get("cuda_graph") and (cfg.get("parallelism", "ddp") != "ddp"
+                                  or any(int(v) != 1 for v in mesh.values() if isinstance(mesh, dict))
+                                  or any(k in cfg for k in ("tp", "cp", "ep"))):
+        errs.append("cuda_graph runs one GPU with plain data parallelism (mesh of size 1, no tp/cp/ep)")
     o = cfg["optimizer"]
     if o.get("name") not in OPTIMIZER_REGISTRY:
         errs.append(f"optimizer.name {o.get('name')!r} not in {sorted(OPTIMIZER_REGISTRY)}")

@@ -27,3 +27,18 @@ def test_config_validates(path):
 
 def test_configs_present():
     assert len(CONFIGS) >= 6
+
+
+def test_cuda_graph_key_is_checked():
+    from pluggy_b200.train.validate import ConfigError, validate_config
+
+    with open(os.path.join(ROOT, "configs", "qwen3_0.6b_ddp_synthetic.json")) as f:
+        cfg = json.load(f)
+    cfg["mesh"] = {"dp": 1}
+    cfg["cuda_graph"] = True
+    validate_config(cfg)
+    for bad in ({"cuda_graph": "yes"}, {"cuda_graph": True, "mesh": {"dp": 2}},
+                {"cuda_graph": True, "parallelism": "fsdp2"}):
+        c = dict(cfg, **bad)
+        with pytest.raises(ConfigError, match="cuda_graph"):
+            validate_config(c)
