@@ -39,7 +39,8 @@ def _table(rows: list[list[int]], numels: list[int], device) -> tuple[torch.Tens
     # the pinned source stays referenced: a copy captured into a CUDA graph reads it
     # again on every replay
     _TABLES[key] = (host, dev)
-    if len(_TABLES) > _TABLES_MAX and not torch.cuda.is_current_stream_capturing():
+    capturing = dev.is_cuda and torch.cuda.is_current_stream_capturing()
+    if len(_TABLES) > _TABLES_MAX and not capturing:
         _TABLES.popitem(last=False)
     return dev, start
 
