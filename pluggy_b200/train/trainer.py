@@ -485,17 +485,17 @@ class Trainer:
             if why is not None:
                 raise ValueError(f"cuda_graph {why}")
             self._static_batch = {k: v.clone() for k, v in batch.items()}
-            self.optimizer.use_device_hyper(self.device)
             torch.cuda.synchronize(self.device)
             torch.cuda.empty_cache()  # the graph's pool takes the eager step's cached blocks
             from pluggy_b200.utils.launch_count import count_launches
 
             g = torch.cuda.CUDAGraph()
             try:
+                self.optimizer.use_device_hyper(self.device)
                 with count_launches() as cnt, torch.cuda.graph(g):
                     loss = self.micro_train_step(self._static_batch)
                     gnorm = self.optimizer_step(scheduler_step=False)
-            except RuntimeError as e:
+            except (RuntimeError, AssertionError) as e:
                 # nothing of the captured step ran: continue with eager steps
                 warnings.warn(f"cuda_graph: capture failed, running eager steps ({e})")
                 self.cuda_graph, self.optimizer._hyper = False, None
