@@ -221,13 +221,13 @@ void rope_apply(const at::Tensor& x, const at::Tensor& cos, const at::Tensor& si
   TORCH_CHECK(cos.size(1) == 1 && cos.size(2) == S && cos.size(3) == d &&
                   (cos.size(0) == 1 || cos.size(0) == B),
               "rope_apply: cos/sin shape does not match x");
-  TORCH_CHECK(y.is_contiguous() && y.sizes() == x.sizes() && y.scalar_type() == at::kBFloat16,
-              "rope_apply: y must be a contiguous bf16 tensor of x's shape");
+  TORCH_CHECK(y.sizes() == x.sizes() && y.scalar_type() == at::kBFloat16 && y.stride(3) == 1,
+              "rope_apply: y must be a bf16 tensor of x's shape with a contiguous last dim");
   const c10::cuda::CUDAGuard guard(x.device());
   const long long cs_b = cos.size(0) == 1 ? 0 : cos.stride(0);
   plg::rope_apply(x.data_ptr(), x.stride(0), x.stride(1), x.stride(2), cos.data_ptr<float>(),
-                  sin.data_ptr<float>(), cs_b, cos.stride(2), y.data_ptr(), B, H, S, d, backward,
-                  cur_stream());
+                  sin.data_ptr<float>(), cs_b, cos.stride(2), y.data_ptr(), y.stride(0), y.stride(1),
+                  y.stride(2), B, H, S, d, backward, cur_stream());
 }
 
 void qk_norm_rope_fwd(const at::Tensor& qkv, at::Tensor& q, at::Tensor& k, at::Tensor& rstd,

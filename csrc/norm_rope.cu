@@ -1039,6 +1039,8 @@ void qk_norm_rope_bwd(const QkRopeArgs& a, const void* dq, const void* dk, void*
 }
 
 // ------------------------------------------------------------ RoPE on [B, H, S, d]
+// (x and y with any B/H/S strides: a transposed view of a projection in, the same
+// layout out, so neither side needs a copy)
 // y = x * cos + rotate_half(x) * sin (rotate_half(x) = [-x2, x1] over the two halves of
 // d), the reference's apply_rotary, for x of any B/H/S strides and a cos/sin table
 // [Bc, S, d] (Bc = 1 broadcasts). Backward (the transpose): dx1 = dy1 cos1 + dy2 sin2,
@@ -1046,7 +1048,8 @@ void qk_norm_rope_bwd(const QkRopeArgs& a, const void* dq, const void* dk, void*
 __global__ void __launch_bounds__(256) rope_apply_kernel(
     const __nv_bfloat16* __restrict__ x, long long xs_b, long long xs_h, long long xs_s,
     const float* __restrict__ cs, const float* __restrict__ sn, long long cs_b, long long cs_s,
-    __nv_bfloat16* __restrict__ y, int B, int H, int S, int d, int backward) {
+    __nv_bfloat16* __restrict__ y, long long ys_b, long long ys_h, long long ys_s, int B, int H,
+    int S, int d, int backward) {
   const int hd = d / 2, q = d / 4;  // q: pairs of pairs per row
   const long long n = static_cast<long long>(B) * H * S * q;
   for (long long t = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; t < n;
@@ -1072,16 +1075,18 @@ __global__ void __launch_bounds__(256) rope_apply_kernel(
       y1 = make_float2(fmaf(x1.x, c1.x, -x2.x * s1.x), fmaf(x1.y, c1.y, -x2.y * s1.y));
       y2 = make_float2(fmaf(x2.x, c2.x, x1.x * s2.x), fmaf(x2.y, c2.y, x1.y * s2.y));
     }
-    __nv_bfloat16* yr = y + row * d;
+    __nv_bfloat16* yr = y + b * ys_b + h * ys_h + s * ys_s;
     *reinterpret_cast<uint32_t*>(yr + i) = pack_bf16x2(y1.x, y1.y);
     *reinterpret_cast<uint32_t*>(yr + hd + i) = pack_bf16x2(y2.x, y2.y);
   }
 }
 
 void rope_apply(const void* x, long long xs_b, long long xs_h, long long xs_s, const float* cos,
-                const float* sin, long long cs_b, long long cs_s, void* y, int B, int H, int S, int d,
-                bool backward, cudaStream_t st) {
+                const float* sin, long long cs_b, long long cs_s, void* y, long long ys_b,
+                long long ys_h, long long ys_s, int B, int H, int S, int d, bool backward,
+                cudaStream_t st) {
   if (d % 4 != 0 || (xs_b | xs_h | xs_s) % 2 != 0 || (cs_b | cs_s) % 2 != 0 ||
+      (ys_b | ys_h | ys_s) % 2 != 0 ||
       (reinterpret_cast<uintptr_t>(x) & 3) || (reinterpret_cast<uintptr_t>(cos) & 7) ||
       (reinterpret_cast<uintptr_t>(sin) & 7) || (reinterpret_cast<uintptr_t>(y) & 3))
     throw std::invalid_argument("rope_apply: head_dim % 4, even strides and aligned bases required");
@@ -1090,7 +1095,7 @@ void rope_apply(const void* x, long long xs_b, long long xs_h, long long xs_s, c
   const long long blocks = std::min<long long>((n + 255) / 256, 148LL * 16);
   rope_apply_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(
       static_cast<const __nv_bfloat16*>(x), xs_b, xs_h, xs_s, cos, sin, cs_b, cs_s,
-      static_cast<__nv_bfloat16*>(y), B, H, S, d, backward ? 1 : 0);
+      static_cast<__nv_bfloat16*>(y), ys_b, ys_h, ys_s, B, H, S, d, backward ? 1 : 0);
   PLG_CUDA_CHECK(cudaGetLastError());
 }
 

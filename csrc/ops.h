@@ -82,11 +82,12 @@ struct QkRopeArgs {
   int* status = nullptr;   // device status word (bounded waits of the TMA-fed kernels)
 };
 void qk_norm_rope_fwd(const QkRopeArgs& a, cudaStream_t stream);
-// y [B, H, S, d] contiguous = RoPE(x) (backward: its transpose); x with strides (b, h, s, 1),
+// y [B, H, S, d] = RoPE(x) (backward: its transpose); x and y with strides (b, h, s, 1),
 // cos/sin fp32 [Bc, S, d] with strides (b, s, 1) (b stride 0 broadcasts)
 void rope_apply(const void* x, long long xs_b, long long xs_h, long long xs_s, const float* cos,
-                const float* sin, long long cs_b, long long cs_s, void* y, int B, int H, int S, int d,
-                bool backward, cudaStream_t stream);
+                const float* sin, long long cs_b, long long cs_s, void* y, long long ys_b,
+                long long ys_h, long long ys_s, int B, int H, int S, int d, bool backward,
+                cudaStream_t stream);
 // backward: dq [T,Hq,d], dk [T,Hk,d] -> dqkv (q and k parts) ; dwq/dwk partials
 void qk_norm_rope_bwd(const QkRopeArgs& a, const void* dq, const void* dk, void* dqkv,
                       long long ld_dqkv, float* dwq_partial, float* dwk_partial, int dw_blocks,

@@ -94,7 +94,7 @@ class _Rope(torch.autograd.Function):
     def forward(ctx, x, cos, sin):
         from pluggy_b200.ops._ext import ext
 
-        y = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+        y = torch.empty_like(x)  # x's layout (a dense transposed view stays transposed)
         ext().rope_apply(x, cos, sin, y, False)
         ctx.save_for_backward(cos, sin)
         return y
@@ -104,8 +104,11 @@ class _Rope(torch.autograd.Function):
         from pluggy_b200.ops._ext import ext
 
         cos, sin = ctx.saved_tensors
-        dx = torch.empty(dy.shape, dtype=torch.bfloat16, device=dy.device)
-        ext().rope_apply(dy.contiguous() if dy.stride(-1) != 1 else dy, cos, sin, dx, True)
+        dy = dy.contiguous() if (dy.stride(-1) != 1 or any(s % 2 for s in dy.stride()[:3])) else dy
+        dx = torch.empty_like(dy)
+        if dx.stride(-1) != 1:
+            dx = torch.empty(dy.shape, dtype=dy.dtype, device=dy.device)
+        ext().rope_apply(dy, cos, sin, dx, True)
         return dx, None, None
 
 

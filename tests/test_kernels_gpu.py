@@ -702,6 +702,7 @@ def test_rope_kernel_fwd_bwd(B, H, S, d, bcast, transposed):
     x.requires_grad_(True)
     assert _rope_kernel_ok(x, cos, sin)
     y = apply_rotary(x, cos, sin)
+    assert y.stride() == x.stride()  # the input's layout: a transposed view needs no copy
     xf = x.detach().float().requires_grad_(True)
     yf = xf * cos + rotate_half(xf) * sin
     assert rel(y, yf) < 1e-2, rel(y, yf)
