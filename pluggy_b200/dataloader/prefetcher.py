@@ -9,16 +9,22 @@ prefetched batch on resume). On a CPU device the copy is synchronous.
 
 Addition: values that are the same host tensor object (``labels is
 input_ids``) are copied once and shared on the device; ``h2d_bytes`` counts
-what was actually copied for the last batch.
+what was actually copied for the last batch. ``background=True`` pulls batches
+from the loader on a worker thread (up to ``depth`` ahead, each with the state
+snapshot taken right before its pull), so host-side batch generation overlaps the
+device work instead of running at the step boundary.
 """
 
 from __future__ import annotations
+
+import queue
+import threading
 
 import torch
 
 
 class CUDAPrefetcher:
-    def __init__(self, loader, device: torch.device):
+    def __init__(self, loader, device: torch.device, background: bool = False, depth: int = 2):
         self.loader = loader
         self.loader_iter = iter(loader)
         self.device = torch.device(device)
@@ -26,7 +32,39 @@ class CUDAPrefetcher:
         self.next_batch = None
         self._loader_state = None
         self.h2d_bytes = 0
+        self._queue = None
+        if background:
+            self._queue = queue.Queue(maxsize=max(1, depth))
+            threading.Thread(target=self._produce, name="prefetch", daemon=True).start()
         self._preload()
+
+    def _produce(self) -> None:
+        # the only user of the loader once started: snapshot, pull, hand over
+        while True:
+            state = self.loader.state_dict()
+            try:
+                batch = next(self.loader_iter)
+            except StopIteration:
+                self._queue.put((state, None))
+                return
+            except BaseException as e:  # surfaced to the consumer
+                self._queue.put((state, e))
+                return
+            self._queue.put((state, batch))
+
+    def _pull(self):
+        if self._queue is None:
+            state = self.loader.state_dict()
+            try:
+                return state, next(self.loader_iter)
+            except StopIteration:
+                return state, None
+        state, batch = self._queue.get()
+        if isinstance(batch, BaseException):
+            raise batch
+        if batch is None:
+            self._queue.put((state, None))  # stays exhausted for later pulls
+        return state, batch
 
     def loader_state_dict(self) -> dict:
         return self._loader_state
@@ -47,10 +85,8 @@ class CUDAPrefetcher:
         return out
 
     def _preload(self) -> None:
-        self._loader_state = self.loader.state_dict()
-        try:
-            batch = next(self.loader_iter)
-        except StopIteration:
+        self._loader_state, batch = self._pull()
+        if batch is None:
             self.next_batch = None
             return
         if self.stream is None:

@@ -135,7 +135,9 @@ class Trainer:
         self._graph_eager_steps = 1
         self.start_step = self._resume()
         self._setup_wandb()
-        self.prefetcher = CUDAPrefetcher(self.dataloader, self.device)
+        # the synthetic source generates batches on the host: do it on a worker thread
+        background = self.device.type == "cuda" and bool(self.config["data"].get("synthetic"))
+        self.prefetcher = CUDAPrefetcher(self.dataloader, self.device, background=background)
 
     # ---------------------------------------------------------------- building
     def _build_model(self) -> nn.Module:

@@ -171,3 +171,43 @@ def test_fused_adamw_device_hyper_bookkeeping():
         assert torch.allclose(hyper, torch.tensor([5e-4, 1 - 0.9 ** 3, 1 - 0.95 ** 3]))
     sd = opt.state_dict()
     assert all(float(s["step"]) == 3.0 for s in sd["state"].values())
+
+
+def test_background_prefetcher_matches_inline():
+    """Pulling batches on a worker thread gives the same batches and the same
+    consumed-state snapshots as pulling them inline, and stops at the end."""
+    def run(background):
+        loader = SyntheticBatches(SyntheticZipfRows(500, 16, seed=3), 2)
+        pf = CUDAPrefetcher(loader, torch.device("cpu"), background=background, depth=3)
+        out = []
+        for _ in range(6):
+            b = next(pf)["input_ids"].clone()
+            out.append((b, dict(pf.loader_state_dict())))
+        return out
+
+    a, b = run(False), run(True)
+    for (x, sx), (y, sy) in zip(a, b, strict=True):
+        assert torch.equal(x, y) and sx == sy
+
+    class Short:
+        def __init__(self):
+            self.i = 0
+
+        def __iter__(self):
+            return self
+
+        def __next__(self):
+            if self.i == 2:
+                raise StopIteration
+            self.i += 1
+            return {"x": torch.full((2,), self.i)}
+
+        def state_dict(self):
+            return {"i": self.i}
+
+    pf = CUDAPrefetcher(Short(), torch.device("cpu"), background=True)
+    assert [int(next(pf)["x"][0]) for _ in range(2)] == [1, 2]
+    with pytest.raises(StopIteration):
+        next(pf)
+    with pytest.raises(StopIteration):
+        next(pf)
