@@ -306,6 +306,36 @@ def case_zero1(a, small):
     return fn, {"bytes": nbytes, "shape": {"elements": n, "kernel": "adamw_ag" if fn is ag else "rs"}}
 
 
+def case_rope(a, small):
+    """RoPE on a transposed [B, S, H, d] projection view (the OLMo-3 / Gemma-4 path)."""
+    from pluggy_b200.ops.elementwise import apply_rotary
+
+    T, H, d = _tokens(a, small), a.heads, a.head_dim
+    B = max(1, T // a.seq)
+    S = T // B
+    x = _bf16(B, S, H, d).transpose(1, 2)
+    inv = 1.0 / (1e6 ** (torch.arange(0, d, 2, device="cuda").float() / d))
+    f = torch.arange(S, device="cuda").float()[:, None] * inv
+    emb = torch.cat([f, f], -1)
+    cos, sin = emb.cos()[None, None], emb.sin()[None, None]
+    fn = lambda: apply_rotary(x, cos, sin)  # noqa: E731
+    return fn, {"bytes": B * S * H * d * 2 * 2 + S * d * 8, "shape": {"B": B, "S": S, "H": H, "d": d}}
+
+
+def case_router(a, small):
+    """MoE router: softmax + top-k + renormalisation + histogram over [T, E] logits."""
+    from pluggy_b200.ops._ext import ext
+
+    T, E, k = _tokens(a, small), a.experts, a.topk
+    logits = _bf16(T, E)
+    probs = torch.empty(T, E, device="cuda")
+    w = torch.empty(T, k, device="cuda")
+    idx = torch.empty(T, k, dtype=torch.int64, device="cuda")
+    counts = torch.zeros(E, dtype=torch.int32, device="cuda")
+    fn = lambda: ext().router_topk(logits, k, True, probs, w, idx, counts)  # noqa: E731
+    return fn, {"bytes": T * E * (2 + 4) + T * k * 12, "shape": {"T": T, "E": E, "k": k}}
+
+
 CASES = {
     "gemm": case_gemm, "attn_fwd": case_attn_fwd, "attn_bwd": case_attn_bwd,
     "qk_rope_fwd": case_qk_rope_fwd, "qk_rope_bwd": case_qk_rope_bwd,
@@ -313,6 +343,7 @@ CASES = {
     "glu_fwd": case_glu_fwd, "glu_bwd": case_glu_bwd,
     "ce_rows": case_ce_rows, "adamw": case_adamw, "sumsq": case_sumsq, "embedding": case_embedding,
     "embedding_bwd": case_embedding_bwd, "grouped_gemm": case_grouped_gemm, "zero1": case_zero1,
+    "rope": case_rope, "router": case_router,
 }
 
 
