@@ -1044,40 +1044,50 @@ void qk_norm_rope_bwd(const QkRopeArgs& a, const void* dq, const void* dk, void*
 // y = x * cos + rotate_half(x) * sin (rotate_half(x) = [-x2, x1] over the two halves of
 // d), the reference's apply_rotary, for x of any B/H/S strides and a cos/sin table
 // [Bc, S, d] (Bc = 1 broadcasts). Backward (the transpose): dx1 = dy1 cos1 + dy2 sin2,
-// dx2 = dy2 cos2 - dy1 sin1. fp32 math on bf16 data, two adjacent pairs per thread.
+// dx2 = dy2 cos2 - dy1 sin1. fp32 math on bf16 data.
 __global__ void __launch_bounds__(256) rope_apply_kernel(
     const __nv_bfloat16* __restrict__ x, long long xs_b, long long xs_h, long long xs_s,
     const float* __restrict__ cs, const float* __restrict__ sn, long long cs_b, long long cs_s,
     __nv_bfloat16* __restrict__ y, long long ys_b, long long ys_h, long long ys_s, int B, int H,
     int S, int d, int backward) {
-  const int hd = d / 2, q = d / 4;  // q: pairs of pairs per row
+  // four adjacent pairs per thread: 8-byte data accesses, 16-byte table reads
+  const int hd = d / 2, q = d / 8;
   const long long n = static_cast<long long>(B) * H * S * q;
   for (long long t = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; t < n;
        t += static_cast<long long>(gridDim.x) * blockDim.x) {
     const long long row = t / q;
-    const int i = static_cast<int>(t - row * q) * 2;
+    const int i = static_cast<int>(t - row * q) * 4;
     const int s = static_cast<int>(row % S);
     const long long bh = row / S;
     const int h = static_cast<int>(bh % H), b = static_cast<int>(bh / H);
     const __nv_bfloat16* xr = x + b * xs_b + h * xs_h + s * xs_s;
-    const float2 x1 = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(xr + i));
-    const float2 x2 = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(xr + hd + i));
+    const uint2 u1 = *reinterpret_cast<const uint2*>(xr + i);
+    const uint2 u2 = *reinterpret_cast<const uint2*>(xr + hd + i);
     const long long co = b * cs_b + s * cs_s;
-    const float2 c1 = *reinterpret_cast<const float2*>(cs + co + i);
-    const float2 c2 = *reinterpret_cast<const float2*>(cs + co + hd + i);
-    const float2 s1 = *reinterpret_cast<const float2*>(sn + co + i);
-    const float2 s2 = *reinterpret_cast<const float2*>(sn + co + hd + i);
-    float2 y1, y2;
-    if (backward) {
-      y1 = make_float2(fmaf(x1.x, c1.x, x2.x * s2.x), fmaf(x1.y, c1.y, x2.y * s2.y));
-      y2 = make_float2(fmaf(x2.x, c2.x, -x1.x * s1.x), fmaf(x2.y, c2.y, -x1.y * s1.y));
-    } else {
-      y1 = make_float2(fmaf(x1.x, c1.x, -x2.x * s1.x), fmaf(x1.y, c1.y, -x2.y * s1.y));
-      y2 = make_float2(fmaf(x2.x, c2.x, x1.x * s2.x), fmaf(x2.y, c2.y, x1.y * s2.y));
+    const float4 c1 = *reinterpret_cast<const float4*>(cs + co + i);
+    const float4 c2 = *reinterpret_cast<const float4*>(cs + co + hd + i);
+    const float4 s1 = *reinterpret_cast<const float4*>(sn + co + i);
+    const float4 s2 = *reinterpret_cast<const float4*>(sn + co + hd + i);
+    const float2 a0 = unpack_bf16x2(u1.x), a1 = unpack_bf16x2(u1.y);
+    const float2 b0 = unpack_bf16x2(u2.x), b1 = unpack_bf16x2(u2.y);
+    const float x1[4] = {a0.x, a0.y, a1.x, a1.y}, x2[4] = {b0.x, b0.y, b1.x, b1.y};
+    const float cc1[4] = {c1.x, c1.y, c1.z, c1.w}, cc2[4] = {c2.x, c2.y, c2.z, c2.w};
+    const float ss1[4] = {s1.x, s1.y, s1.z, s1.w}, ss2[4] = {s2.x, s2.y, s2.z, s2.w};
+    float y1[4], y2[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (backward) {
+        y1[e] = fmaf(x1[e], cc1[e], x2[e] * ss2[e]);
+        y2[e] = fmaf(x2[e], cc2[e], -x1[e] * ss1[e]);
+      } else {
+        y1[e] = fmaf(x1[e], cc1[e], -x2[e] * ss1[e]);
+        y2[e] = fmaf(x2[e], cc2[e], x1[e] * ss2[e]);
+      }
     }
     __nv_bfloat16* yr = y + b * ys_b + h * ys_h + s * ys_s;
-    *reinterpret_cast<uint32_t*>(yr + i) = pack_bf16x2(y1.x, y1.y);
-    *reinterpret_cast<uint32_t*>(yr + hd + i) = pack_bf16x2(y2.x, y2.y);
+    *reinterpret_cast<uint2*>(yr + i) = make_uint2(pack_bf16x2(y1[0], y1[1]), pack_bf16x2(y1[2], y1[3]));
+    *reinterpret_cast<uint2*>(yr + hd + i) =
+        make_uint2(pack_bf16x2(y2[0], y2[1]), pack_bf16x2(y2[2], y2[3]));
   }
 }
 
@@ -1085,12 +1095,13 @@ void rope_apply(const void* x, long long xs_b, long long xs_h, long long xs_s, c
                 const float* sin, long long cs_b, long long cs_s, void* y, long long ys_b,
                 long long ys_h, long long ys_s, int B, int H, int S, int d, bool backward,
                 cudaStream_t st) {
-  if (d % 4 != 0 || (xs_b | xs_h | xs_s) % 2 != 0 || (cs_b | cs_s) % 2 != 0 ||
-      (ys_b | ys_h | ys_s) % 2 != 0 ||
-      (reinterpret_cast<uintptr_t>(x) & 3) || (reinterpret_cast<uintptr_t>(cos) & 7) ||
-      (reinterpret_cast<uintptr_t>(sin) & 7) || (reinterpret_cast<uintptr_t>(y) & 3))
-    throw std::invalid_argument("rope_apply: head_dim % 4, even strides and aligned bases required");
-  const long long n = static_cast<long long>(B) * H * S * (d / 4);
+  if (d % 8 != 0 || (xs_b | xs_h | xs_s) % 4 != 0 || (cs_b | cs_s) % 4 != 0 ||
+      (ys_b | ys_h | ys_s) % 4 != 0 ||
+      (reinterpret_cast<uintptr_t>(x) & 7) || (reinterpret_cast<uintptr_t>(cos) & 15) ||
+      (reinterpret_cast<uintptr_t>(sin) & 15) || (reinterpret_cast<uintptr_t>(y) & 7))
+    throw std::invalid_argument(
+        "rope_apply: head_dim % 8, strides in multiples of 4 elements and 8/16-byte aligned bases");
+  const long long n = static_cast<long long>(B) * H * S * (d / 8);
   if (n == 0) return;
   const long long blocks = std::min<long long>((n + 255) / 256, 148LL * 16);
   rope_apply_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(

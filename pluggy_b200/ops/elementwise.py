@@ -104,7 +104,8 @@ class _Rope(torch.autograd.Function):
         from pluggy_b200.ops._ext import ext
 
         cos, sin = ctx.saved_tensors
-        dy = dy.contiguous() if (dy.stride(-1) != 1 or any(s % 2 for s in dy.stride()[:3])) else dy
+        dy = dy.contiguous() if (dy.stride(-1) != 1 or any(s % 4 for s in dy.stride()[:3])
+                                 or dy.data_ptr() % 8) else dy
         dx = torch.empty_like(dy)
         if dx.stride(-1) != 1:
             dx = torch.empty(dy.shape, dtype=dy.dtype, device=dy.device)
@@ -116,15 +117,15 @@ def _rope_kernel_ok(x, cos, sin) -> bool:
     if not (x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 4 and x.stride(-1) == 1):
         return False
     B, _, S, d = x.shape
-    if d % 4 or any(st % 2 for st in x.stride()[:3]) or x.data_ptr() % 4:
+    if d % 8 or any(st % 4 for st in x.stride()[:3]) or x.data_ptr() % 8:
         return False
     if cos.dim() != 4 or cos.dtype != torch.float32 or sin.shape != cos.shape:
         return False
     if cos.shape[1] != 1 or cos.shape[2] != S or cos.shape[3] != d or cos.shape[0] not in (1, B):
         return False
-    return (cos.stride() == sin.stride() and cos.stride(-1) == 1 and cos.stride(2) % 2 == 0
-            and (cos.shape[0] == 1 or cos.stride(0) % 2 == 0)
-            and cos.data_ptr() % 8 == 0 and sin.data_ptr() % 8 == 0)
+    return (cos.stride() == sin.stride() and cos.stride(-1) == 1 and cos.stride(2) % 4 == 0
+            and (cos.shape[0] == 1 or cos.stride(0) % 4 == 0)
+            and cos.data_ptr() % 16 == 0 and sin.data_ptr() % 16 == 0)
 
 
 def apply_rotary(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
