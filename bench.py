@@ -28,7 +28,6 @@ import statistics
 import subprocess
 import sys
 import threading
-import time
 from datetime import timedelta
 
 import torch

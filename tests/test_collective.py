@@ -2,7 +2,6 @@
 tests/collective.py): every op, src-as-coordinate, subgroup isolation, flatten."""
 
 import torch
-import torch.distributed as dist
 
 from tests._dist import run_ranks
 
