@@ -90,3 +90,27 @@ def test_jsonl_metrics_log(tmp_path):
     rows = [json.loads(x) for x in open(path)]
     assert [r["step"] for r in rows] == [1, 2, 3]
     assert {"train/loss", "train/grad_norm", "train/lr", "perf/tps"} <= set(rows[0])
+
+
+def _graph_on_cpu(rank, world, root, out):
+    cfg = json.loads(json.dumps(CFG))
+    cfg["mesh"] = {"dp": 1}
+    cfg["data"]["global_batch_size"] = 4
+    cfg["cuda_graph"] = True
+    tr = _trainer(cfg, rank, world, root)
+    tr._train_step()  # the eager first step runs
+    try:
+        tr._train_step()
+        msg = "no error"
+    except ValueError as e:
+        msg = str(e)
+    with open(out, "w") as f:
+        f.write(msg)
+
+
+def test_cuda_graph_refuses_a_cpu_device(tmp_path):
+    """``cuda_graph`` on a CPU device: the first (eager) step runs, the capture step stops
+    with a clear error instead of capturing nothing."""
+    out = str(tmp_path / "msg.txt")
+    run_ranks(_graph_on_cpu, 1, str(tmp_path / "ck"), out, timeout_s=120, join_s=600)
+    assert "cuda_graph needs a CUDA device" in open(out).read()
