@@ -38,6 +38,7 @@ import torch
 import torch.nn as nn
 
 from pluggy_b200.checkpoint.checkpointer import Checkpointer
+from pluggy_b200.train.failure import FailureNotice
 from pluggy_b200.core.collective import all_reduce, barrier
 from pluggy_b200.core.grad_helper import clip_grad_norm
 from pluggy_b200.core.mesh import Mesh
@@ -133,6 +134,9 @@ class Trainer:
         self.cuda_graph = bool(self.config.get("cuda_graph", False))
         self._graph = None
         self._graph_eager_steps = 1
+        # a rank that fails tells the others through the process group's store; each
+        # rank checks before every step ("failure_notice": false turns it off)
+        self.failure_notice = FailureNotice(rank, enabled=bool(self.config.get("failure_notice", True)))
         self.start_step = self._resume()
         self._setup_wandb()
         # the synthetic source generates batches on the host: do it on a worker thread
@@ -538,12 +542,17 @@ class Trainer:
     @debug_time
     def train_n_step_test(self, n_steps: int) -> None:
         tokens_per_step = self.config["data"]["seq_len"] * self.global_batch_size
-        for step in range(n_steps):
-            metrics, t = self.train_step()
-            if self.status_check_steps and (step + 1) % self.status_check_steps == 0:
-                self.check_device_status()
-            if self.rank == 0:
-                print(self._line(step, metrics, tokens_per_step, t))
+        try:
+            for step in range(n_steps):
+                self.failure_notice.check()
+                metrics, t = self.train_step()
+                if self.status_check_steps and (step + 1) % self.status_check_steps == 0:
+                    self.check_device_status()
+                if self.rank == 0:
+                    print(self._line(step, metrics, tokens_per_step, t))
+        except BaseException as e:
+            self.failure_notice.announce(e)
+            raise
         self._print_peak()
 
     def _print_peak(self) -> None:
@@ -554,6 +563,7 @@ class Trainer:
         tokens_per_step = self.config["data"]["seq_len"] * self.global_batch_size
         try:
             for step in range(self.start_step, self.num_train_steps):
+                self.failure_notice.check()
                 metrics, t = self.train_step()
                 if self.status_check_steps and (step + 1) % self.status_check_steps == 0:
                     self.check_device_status()
@@ -563,6 +573,9 @@ class Trainer:
                     self._log_metrics(metrics, step + 1, tokens_per_step, t)
                     print(self._line(step, metrics, tokens_per_step, t))
             self._print_peak()
+        except BaseException as e:
+            self.failure_notice.announce(e)
+            raise
         finally:
             if self.wandb_run is not None:
                 self.wandb_run.finish()
