@@ -1,6 +1,6 @@
 """The CPU/gloo plumbing config: world 2 DDP, 2-step accumulation, clip, chunked CE,
 AdamW + warmup-cosine, 10 steps; resume from a mid-run checkpoint reproduces the
-trajectory exactly; a mesh change on resume is refused."""
+trajectory exactly; a mesh or data-source change on resume is refused."""
 
 import json
 import os
@@ -55,9 +55,18 @@ def _run(rank, world, root, out):
         refused = False
     except AssertionError as e:
         refused = "mesh" in str(e)
+    # so must a change of the data source
+    bad = json.loads(json.dumps(cfg))
+    bad["data"]["synthetic"] = {"kind": "zipf", "s": 1.1}
+    try:
+        _trainer(bad, rank, world, root)
+        refused_data = False
+    except AssertionError as e:
+        refused_data = "data sources" in str(e)
     if rank == 0:
         with open(out, "w") as f:
-            json.dump({"losses": losses, "resumed": resumed, "refused": refused}, f)
+            json.dump({"losses": losses, "resumed": resumed, "refused": refused,
+                       "refused_data": refused_data}, f)
 
 
 def test_cpu_plumbing_config_and_resume(tmp_path):
@@ -69,7 +78,7 @@ def test_cpu_plumbing_config_and_resume(tmp_path):
     assert abs(L[0] - __import__("math").log(8192)) < 0.5  # fresh CE ~ ln V
     assert L[-1] < L[0]  # it learns (uniform ids: only the unigram entropy is learnable)
     assert r["resumed"] == L[5:], (r["resumed"], L[5:])  # exact replay after resume
-    assert r["refused"]
+    assert r["refused"] and r["refused_data"]
     assert os.path.exists(tmp_path / "ck" / "cpu_plumbing" / "5" / ".complete")
 
 
